@@ -1,0 +1,271 @@
+// Python bindings of the sm_100a kernels. Every entry point checks device, dtype,
+// contiguity and alignment and raises on anything its kernel does not handle, so a
+// kernel never receives arguments it was not written for.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common/tma.h"
+#include "gemm/gemm.h"
+#include "fused/fused.h"
+
+namespace {
+
+void check_cuda_tensor(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_bf16(const torch::Tensor& t, const char* name) {
+  check_cuda_tensor(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16");
+}
+void check_rows(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have unit stride in its last dimension");
+  TORCH_CHECK((t.stride(0) * t.element_size()) % 16 == 0, name,
+              " row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              " must be 16-byte aligned");
+}
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// D = A * B^T with the selected epilogue. `a_t`: A is stored [K, M]; `b_t`: B is [K, N].
+void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor D, int64_t epi, bool a_t, bool b_t,
+          c10::optional<torch::Tensor> C, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> D2, c10::optional<torch::Tensor> rope_tab,
+          int64_t rope_cols, int64_t rope_rows_per_seq, int64_t rope_pos_offset,
+          int64_t rope_head_dim, c10::optional<torch::Tensor> gate,
+          int64_t gate_rows_per_group, int64_t splits, int64_t bn) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_cuda_tensor(D, "D");
+  check_rows(A, "A");
+  check_rows(B, "B");
+  check_rows(D, "D");
+  const c10::cuda::CUDAGuard guard(A.device());
+  ddb::GemmArgs a;
+  a.a_mn_major = a_t;
+  a.b_mn_major = b_t;
+  a.M = a_t ? A.size(1) : A.size(0);
+  a.K = a_t ? A.size(0) : A.size(1);
+  a.N = b_t ? B.size(1) : B.size(0);
+  const int64_t kb = b_t ? B.size(0) : B.size(1);
+  TORCH_CHECK(kb == a.K, "gemm: inner dimensions differ (", a.K, " vs ", kb, ")");
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.D = D.data_ptr();
+  a.ldd = D.stride(0);
+  TORCH_CHECK(D.size(0) == a.M, "gemm: D has ", D.size(0), " rows, expected ", a.M);
+  const bool f32_out = (epi == ddb::kEpiF32 || epi == ddb::kEpiF32Atomic);
+  TORCH_CHECK(D.scalar_type() == (f32_out ? torch::kFloat32 : torch::kBFloat16),
+              "gemm: D dtype does not match the epilogue");
+  int64_t d_cols = a.N;
+  if (epi == ddb::kEpiDSwiGLU) d_cols = 2 * a.N;
+  TORCH_CHECK(D.size(1) >= d_cols, "gemm: D too narrow");
+  if (C) {
+    check_bf16(*C, "C");
+    check_rows(*C, "C");
+    TORCH_CHECK(C->size(0) == a.M, "gemm: C rows");
+    a.C = C->data_ptr();
+    a.ldc = C->stride(0);
+  }
+  if (epi == ddb::kEpiDSwiGLU) TORCH_CHECK(C.has_value(), "dswiglu epilogue needs C = gu");
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->is_contiguous() &&
+                    bias->numel() >= a.N,
+                "gemm: bias must be contiguous fp32 [N]");
+    a.bias = bias->data_ptr<float>();
+  }
+  if (epi == ddb::kEpiSwiGLU) {
+    TORCH_CHECK(D2.has_value(), "swiglu epilogue needs D2");
+    check_bf16(*D2, "D2");
+    check_rows(*D2, "D2");
+    TORCH_CHECK(D2->size(0) == a.M && D2->size(1) >= a.N / 2, "gemm: D2 shape");
+    a.D2 = D2->data_ptr();
+    a.ldd2 = D2->stride(0);
+  }
+  if (epi == ddb::kEpiRope) {
+    TORCH_CHECK(rope_tab.has_value() && rope_tab->scalar_type() == torch::kFloat32 &&
+                    rope_tab->is_contiguous(),
+                "rope epilogue needs a contiguous fp32 table [P, head_dim/2, 2]");
+    TORCH_CHECK(rope_head_dim % 32 == 0, "rope head_dim must be a multiple of 32");
+    TORCH_CHECK(rope_cols % rope_head_dim == 0, "rope_cols must be whole heads");
+    const int64_t max_pos = rope_tab->numel() / rope_head_dim;
+    TORCH_CHECK(rope_pos_offset + std::min<int64_t>(rope_rows_per_seq, a.M) <= max_pos,
+                "rope table too short for the requested positions");
+    a.rope_tab = reinterpret_cast<const float2*>(rope_tab->data_ptr<float>());
+    a.rope_cols = rope_cols;
+    a.rope_rows_per_seq = rope_rows_per_seq;
+    a.rope_pos_offset = rope_pos_offset;
+    a.rope_head_dim = rope_head_dim;
+  }
+  if (epi == ddb::kEpiGateResidual) {
+    TORCH_CHECK(gate.has_value(), "gated residual needs gate");
+    check_bf16(*gate, "gate");
+    check_rows(*gate, "gate");
+    a.gate = gate->data_ptr();
+    a.ldg = gate->stride(0);
+    a.gate_rows_per_group = gate_rows_per_group;
+    TORCH_CHECK((a.M + gate_rows_per_group - 1) / gate_rows_per_group <= gate->size(0),
+                "gate has too few rows");
+  }
+  a.splits = splits;
+  a.bn = bn;
+  ddb::gemm(a, static_cast<int>(epi), stream());
+}
+
+int64_t read_status() {
+  int dev = 0;
+  ddb::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  int v = 0;
+  ddb::check_cuda(cudaMemcpy(&v, ddb::device_status(dev), sizeof(int), cudaMemcpyDeviceToHost),
+                  "read status");
+  return v;
+}
+void reset_status() {
+  int dev = 0;
+  ddb::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  ddb::check_cuda(cudaMemset(ddb::device_status(dev), 0, sizeof(int)), "reset status");
+}
+
+// ------------------------------------------------------------------ fused norm
+std::vector<torch::Tensor> adaln_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor mod,
+                                     int64_t scale_off, int64_t shift_off,
+                                     int64_t rows_per_group, double eps) {
+  check_bf16(x, "x");
+  check_rows(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.numel() == x.size(1),
+              "w must be fp32 [D]");
+  TORCH_CHECK(mod.scalar_type() == torch::kFloat32 && mod.dim() == 2 && mod.stride(1) == 1,
+              "mod must be fp32 [groups, cols]");
+  TORCH_CHECK(mod.stride(0) % 4 == 0 && scale_off % 4 == 0 && shift_off % 4 == 0,
+              "mod columns must be 16-byte aligned");
+  const int64_t M = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 256 == 0 && D <= 2048, "adaln: D must be a multiple of 256, <= 2048");
+  TORCH_CHECK((M + rows_per_group - 1) / rows_per_group <= mod.size(0), "mod has too few rows");
+  TORCH_CHECK(std::max(scale_off, shift_off) + D <= mod.size(1), "mod too narrow");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto h = torch::empty_like(x);
+  auto rstd = torch::empty({M}, x.options().dtype(torch::kFloat32));
+  ddb::AdaLNArgs a;
+  a.M = M; a.D = D; a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.w = w.data_ptr<float>(); a.mod = mod.data_ptr<float>(); a.ld_mod = mod.stride(0);
+  a.scale_off = scale_off; a.shift_off = shift_off; a.rows_per_group = rows_per_group;
+  a.eps = static_cast<float>(eps);
+  a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr()); a.rstd = rstd.data_ptr<float>();
+  ddb::adaln_rmsnorm_fwd(a, stream());
+  return {h, rstd};
+}
+
+torch::Tensor adaln_bwd(torch::Tensor dh, torch::Tensor x, torch::Tensor rstd, torch::Tensor w,
+                        torch::Tensor mod, int64_t scale_off, int64_t shift_off,
+                        int64_t rows_per_group, c10::optional<torch::Tensor> dres,
+                        c10::optional<torch::Tensor> dw, torch::Tensor dmod) {
+  check_bf16(dh, "dh");
+  check_bf16(x, "x");
+  TORCH_CHECK(dh.is_contiguous() && x.is_contiguous() && dh.sizes() == x.sizes(), "dh/x shape");
+  const int64_t M = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % 256 == 0 && D <= 1024, "adaln bwd: D must be a multiple of 256, <= 1024");
+  TORCH_CHECK(rstd.scalar_type() == torch::kFloat32 && rstd.numel() == M, "rstd");
+  TORCH_CHECK(dmod.scalar_type() == torch::kFloat32 && dmod.dim() == 2 && dmod.stride(1) == 1 &&
+                  dmod.size(0) >= (M + rows_per_group - 1) / rows_per_group,
+              "dmod must be fp32 [groups, cols]");
+  TORCH_CHECK(mod.stride(0) % 4 == 0 && mod.scalar_type() == torch::kFloat32, "mod");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dx = torch::empty_like(x);
+  ddb::AdaLNArgs a;
+  a.M = M; a.D = D; a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.w = w.data_ptr<float>(); a.mod = mod.data_ptr<float>(); a.ld_mod = mod.stride(0);
+  a.scale_off = scale_off; a.shift_off = shift_off; a.rows_per_group = rows_per_group;
+  a.rstd = rstd.data_ptr<float>();
+  a.dh = reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr());
+  if (dres) {
+    check_bf16(*dres, "dres");
+    TORCH_CHECK(dres->is_contiguous() && dres->sizes() == x.sizes(), "dres shape");
+    a.dres = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+  }
+  a.dx = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  if (dw) {
+    TORCH_CHECK(dw->scalar_type() == torch::kFloat32 && dw->is_contiguous() && dw->numel() == D, "dw");
+    a.dw = dw->data_ptr<float>();
+  }
+  a.dmod = dmod.data_ptr<float>(); a.ld_dmod = dmod.stride(0);
+  ddb::adaln_rmsnorm_bwd(a, stream());
+  return dx;
+}
+
+// ------------------------------------------------------------------ optimizer / casts
+void adamw_flat(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v,
+                c10::optional<torch::Tensor> compute, torch::Tensor clip, double lr, double b1,
+                double b2, double eps, double wd, double bc1, double bc2, double grad_scale,
+                int64_t decay_end) {
+  for (auto* t : {&master, &grad, &m, &v}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous(),
+                "adamw buffers must be contiguous fp32 CUDA tensors");
+    TORCH_CHECK(t->numel() == master.numel(), "adamw buffers differ in length");
+  }
+  TORCH_CHECK(clip.scalar_type() == torch::kFloat32 && clip.numel() == 1 && clip.is_cuda(), "clip");
+  const c10::cuda::CUDAGuard guard(master.device());
+  ddb::AdamWArgs a;
+  a.master = master.data_ptr<float>(); a.grad = grad.data_ptr<float>();
+  a.m = m.data_ptr<float>(); a.v = v.data_ptr<float>();
+  if (compute) {
+    check_bf16(*compute, "compute");
+    TORCH_CHECK(compute->numel() == master.numel() && compute->is_contiguous(), "compute");
+    a.compute = reinterpret_cast<__nv_bfloat16*>(compute->data_ptr());
+  }
+  a.clip = clip.data_ptr<float>();
+  a.n = master.numel(); a.decay_end = decay_end;
+  a.lr = lr; a.b1 = b1; a.b2 = b2; a.eps = eps; a.wd = wd; a.bc1 = bc1; a.bc2 = bc2;
+  a.grad_scale = grad_scale;
+  ddb::adamw_flat(a, stream());
+}
+
+void cast_bf16(torch::Tensor src, torch::Tensor dst) {
+  TORCH_CHECK(src.scalar_type() == torch::kFloat32 && src.is_contiguous() && src.is_cuda(), "src");
+  check_bf16(dst, "dst");
+  TORCH_CHECK(dst.numel() == src.numel() && dst.is_contiguous(), "dst");
+  const c10::cuda::CUDAGuard guard(src.device());
+  ddb::cast_f32_bf16(src.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()),
+                     src.numel(), stream());
+}
+
+torch::Tensor sq_norm(torch::Tensor x) {
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.is_cuda(), "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto out = torch::zeros({}, x.options());
+  ddb::sq_norm_f32(x.data_ptr<float>(), x.numel(), out.data_ptr<float>(), stream());
+  return out;
+}
+
+void rope_rotate(torch::Tensor x, int64_t rot_cols, torch::Tensor tab, int64_t head_dim,
+                 int64_t rows_per_seq, int64_t pos_offset, bool inverse) {
+  check_bf16(x, "x");
+  check_rows(x, "x");
+  TORCH_CHECK(rot_cols % head_dim == 0 && head_dim % 8 == 0, "rope_rotate: columns");
+  TORCH_CHECK(tab.scalar_type() == torch::kFloat32 && tab.is_contiguous(), "tab");
+  TORCH_CHECK(pos_offset + std::min<int64_t>(rows_per_seq, x.size(0)) <= tab.numel() / head_dim,
+              "rope table too short");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ddb::rope_rotate_bf16(reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), x.size(0),
+                        rot_cols, reinterpret_cast<const float2*>(tab.data_ptr<float>()), head_dim,
+                        rows_per_seq, pos_offset, inverse, stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "drivedit_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
+  m.def("read_status", &read_status, "device status word (0 = ok)");
+  m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");
+  m.def("reset_status", &reset_status, "clear the device status word");
+  m.def("adaln_fwd", &adaln_fwd, "fused AdaLN-RMSNorm forward -> (h, rstd)");
+  m.def("adaln_bwd", &adaln_bwd, "fused AdaLN-RMSNorm backward -> dx (accumulates dw, dmod)");
+  m.def("adamw_flat", &adamw_flat, "flat AdamW + bf16 copy");
+  m.def("cast_bf16", &cast_bf16, "fp32 -> bf16 cast");
+  m.def("sq_norm", &sq_norm, "sum of squares (fp32)");
+  m.def("rope_rotate", &rope_rotate, "in-place rotary rotation of leading columns");
+}

@@ -1,0 +1,559 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[M,N] = A[M,K] * B[N,K]^T, bf16 operands, fp32 accumulation in TMEM.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: streams 128x64 A and BNx64 B tiles into a STAGES-deep
+//               shared-memory ring (128-byte swizzle), one mbarrier pair per slot.
+//   warp 1      owns TMEM (2 x BN fp32 columns, double-buffered accumulator) and issues
+//               tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees
+//               ring slots and hands finished accumulators to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fused elementwise op,
+//               16-byte global stores (or fp32 vector reductions for split-K).
+// Tiles are walked persistently (n fastest, so concurrent CTAs share the A panel in L2);
+// the epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Replaces every nn.Linear of the reference (layers/mha.py:307-308, layers/mlp.py:112-114,
+// layers/moe.py:54-56) and carries the SwiGLU (layers/mlp.py:131-155), rotary
+// (layers/rope_v2.py:95-148) and residual epilogues.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "../common/ptx.cuh"
+#include "../common/tma.h"
+#include "gemm.h"
+
+namespace ddb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+struct Sched {
+  int tiles_m, tiles_n, kblocks, kb_per_split, splits, total;
+  __device__ __forceinline__ void decode(int t, int& m0, int& n0, int& kb0, int& kb1) const {
+    int n_idx = t % tiles_n;
+    t /= tiles_n;
+    int m_idx = t % tiles_m;
+    int split = t / tiles_m;
+    m0 = m_idx * BM;
+    n0 = n_idx;  // scaled by BN by the caller
+    kb0 = split * kb_per_split;
+    kb1 = min(kblocks, kb0 + kb_per_split);
+  }
+};
+
+__device__ __forceinline__ void record_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// ---------------------------------------------------------------- epilogue ops
+template <int EPI>
+__device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0,
+                                            const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+
+  if constexpr (EPI == kEpiF32Atomic) {
+    float* d = reinterpret_cast<float*>(a.D) + static_cast<long>(row) * a.ldd + col0;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) red_add_v4_f32(d + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+    return;
+  } else {
+    if (a.bias != nullptr) {
+      const float4* b4 = reinterpret_cast<const float4*>(a.bias + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float4 b = __ldg(b4 + i);
+        v[4 * i] += b.x;
+        v[4 * i + 1] += b.y;
+        v[4 * i + 2] += b.z;
+        v[4 * i + 3] += b.w;
+      }
+    }
+    if constexpr (EPI == kEpiF32) {
+      float* d = reinterpret_cast<float*>(a.D) + static_cast<long>(row) * a.ldd + col0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        st_global_v4(d + i, __float_as_uint(v[i]), __float_as_uint(v[i + 1]),
+                     __float_as_uint(v[i + 2]), __float_as_uint(v[i + 3]));
+      return;
+    } else {
+      if constexpr (EPI == kEpiRope) {
+        if (col0 < a.rope_cols) {
+          const int pos = (row % a.rope_rows_per_seq) + a.rope_pos_offset;
+          const int half = a.rope_head_dim >> 1;
+          const int p0 = (col0 % a.rope_head_dim) >> 1;
+          const float2* tab = a.rope_tab + static_cast<long>(pos) * half + p0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float2 cs = __ldg(tab + i);
+            float x0 = v[2 * i], x1 = v[2 * i + 1];
+            v[2 * i] = x0 * cs.x - x1 * cs.y;
+            v[2 * i + 1] = x0 * cs.y + x1 * cs.x;
+          }
+        }
+      }
+      if constexpr (EPI == kEpiGateResidual) {
+        const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(a.gate) +
+                                 static_cast<long>(row / a.gate_rows_per_group) * a.ldg + col0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 gv = ld_global_v4(g + i);
+          uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 f = unpack_bf16(gw[j]);
+            v[i + 2 * j] *= f.x;
+            v[i + 2 * j + 1] *= f.y;
+          }
+        }
+      }
+      if (a.C != nullptr && (EPI == kEpiBf16 || EPI == kEpiGateResidual)) {
+        const __nv_bfloat16* c =
+            reinterpret_cast<const __nv_bfloat16*>(a.C) + static_cast<long>(row) * a.ldc + col0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 cv = ld_global_v4(c + i);
+          uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 f = unpack_bf16(cw[j]);
+            v[i + 2 * j] += f.x;
+            v[i + 2 * j + 1] += f.y;
+          }
+        }
+      }
+      __nv_bfloat16* d =
+          reinterpret_cast<__nv_bfloat16*>(a.D) + static_cast<long>(row) * a.ldd + col0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8)
+        st_global_v4(d + i, pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
+                     pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
+    }
+  }
+}
+
+// SwiGLU forward: accumulator columns come in groups of 64: 32 gate then 32 up.
+__device__ __forceinline__ void epi_swiglu(const GemmArgs& a, int row, int col0,
+                                           const uint32_t (&rg)[32], const uint32_t (&ru)[32]) {
+  __nv_bfloat16* gu =
+      reinterpret_cast<__nv_bfloat16*>(a.D) + static_cast<long>(row) * a.ldd + col0;
+  __nv_bfloat16* act =
+      reinterpret_cast<__nv_bfloat16*>(a.D2) + static_cast<long>(row) * a.ldd2 + (col0 >> 1);
+  float g[32], u[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    // round through bf16 so the saved pre-activation and the activation agree exactly
+    g[i] = __bfloat162float(__float2bfloat16(__uint_as_float(rg[i])));
+    u[i] = __bfloat162float(__float2bfloat16(__uint_as_float(ru[i])));
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    st_global_v4(gu + i, pack_bf16(g[i], g[i + 1]), pack_bf16(g[i + 2], g[i + 3]),
+                 pack_bf16(g[i + 4], g[i + 5]), pack_bf16(g[i + 6], g[i + 7]));
+    st_global_v4(gu + 32 + i, pack_bf16(u[i], u[i + 1]), pack_bf16(u[i + 2], u[i + 3]),
+                 pack_bf16(u[i + 4], u[i + 5]), pack_bf16(u[i + 6], u[i + 7]));
+  }
+  float h[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) h[i] = silu_f(g[i]) * u[i];
+#pragma unroll
+  for (int i = 0; i < 32; i += 8)
+    st_global_v4(act + i, pack_bf16(h[i], h[i + 1]), pack_bf16(h[i + 2], h[i + 3]),
+                 pack_bf16(h[i + 4], h[i + 5]), pack_bf16(h[i + 6], h[i + 7]));
+}
+
+// SwiGLU backward: acc = dA for activation columns [col0, col0+32), which map to the
+// gate columns 2*col0 + [0,32) and up columns 2*col0 + 32 + [0,32) of gu.
+__device__ __forceinline__ void epi_dswiglu(const GemmArgs& a, int row, int col0,
+                                            const uint32_t (&r)[32]) {
+  const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(a.C) +
+                            static_cast<long>(row) * a.ldc + 2 * col0;
+  __nv_bfloat16* dgu =
+      reinterpret_cast<__nv_bfloat16*>(a.D) + static_cast<long>(row) * a.ldd + 2 * col0;
+  float g[32], u[32];
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 gv = ld_global_v4(gu + i);
+    uint4 uv = ld_global_v4(gu + 32 + i);
+    uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 fg = unpack_bf16(gw[j]);
+      float2 fu = unpack_bf16(uw[j]);
+      g[i + 2 * j] = fg.x;
+      g[i + 2 * j + 1] = fg.y;
+      u[i + 2 * j] = fu.x;
+      u[i + 2 * j + 1] = fu.y;
+    }
+  }
+  float dg[32], du[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float da = __uint_as_float(r[i]);
+    float s = 1.f / (1.f + __expf(-g[i]));
+    float sl = g[i] * s;
+    du[i] = da * sl;
+    dg[i] = da * u[i] * s * (1.f + g[i] * (1.f - s));
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    st_global_v4(dgu + i, pack_bf16(dg[i], dg[i + 1]), pack_bf16(dg[i + 2], dg[i + 3]),
+                 pack_bf16(dg[i + 4], dg[i + 5]), pack_bf16(dg[i + 6], dg[i + 7]));
+    st_global_v4(dgu + 32 + i, pack_bf16(du[i], du[i + 1]), pack_bf16(du[i + 2], du[i + 3]),
+                 pack_bf16(du[i + 4], du[i + 5]), pack_bf16(du[i + 6], du[i + 7]));
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                   const __grid_constant__ CUtensorMap tmB, const GemmArgs args,
+                   const Sched sched, int* status) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = make_idesc_bf16(BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
+        int m0, nt, kb0, kb1;
+        sched.decode(t, m0, nt, kb0, kb1);
+        const int n0 = nt * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          if constexpr (A_MN) {
+            tma_load_2d(sa, &tmA, &full[stage], m0, kb * BK);
+            tma_load_2d(sa + 8192, &tmA, &full[stage], m0 + 64, kb * BK);
+          } else {
+            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(sb + c * 8192, &tmB, &full[stage], n0 + c * 64, kb * BK);
+          } else {
+            tma_load_2d(sb, &tmB, &full[stage], kb * BK, n0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        record_status(status, kStatusTimeoutProducer);
+        *abort_flag = 1;
+        // let copies already in flight land before the CTA exits (bounded)
+        int s = stage, ph = phase;
+        for (int i = 0; i < min(issued, STAGES); ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          long long t0 = clock64();
+          while (!mbar_try_wait(&full[s], ph) && clock64() - t0 < kSpinLimitCycles / 8) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int buf = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool any = false;
+      for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
+        int m0, nt, kb0, kb1;
+        sched.decode(t, m0, nt, kb0, kb1);
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t da = A_MN ? make_sw128_desc(sa + kk * 2048, 8192, 1024)
+                               : make_sw128_desc(sa + kk * 32, 16, 1024);
+            uint64_t db = B_MN ? make_sw128_desc(sb + kk * 2048, 8192, 1024)
+                               : make_sw128_desc(sb + kk * 32, 16, 1024);
+            mma_bf16_ss(d_tmem, da, db, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          any = true;
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[buf]);
+        if (++buf == 2) {
+          buf = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) {
+        record_status(status, kStatusTimeoutMma);
+        *abort_flag = 1;
+      }
+      if (any) {
+        // all MMAs of this thread complete before TMEM is released
+        mma_commit(drain_bar);
+        long long t0 = clock64();
+        while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
+      int m0, nt, kb0, kb1;
+      sched.decode(t, m0, nt, kb0, kb1);
+      const int n0 = nt * BN;
+      if (!mbar_wait(&acc_full[buf], acc_phase, abort_flag)) {
+        if (lane == 0) record_status(status, kStatusTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+      if constexpr (EPI == kEpiSwiGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tbase + c, rg);
+          tmem_ld32(tbase + c + 32, ru);
+          tmem_wait_ld();
+          if (row < args.M && n0 + c < args.N) epi_swiglu(args, row, n0 + c, rg, ru);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_wait_ld();
+          if (row < args.M && n0 + c < args.N) {
+            if constexpr (EPI == kEpiDSwiGLU)
+              epi_dswiglu(args, row, n0 + c, r);
+            else
+              epi_chunk32<EPI>(args, row, n0 + c, r);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (++buf == 2) {
+        buf = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host launch
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
+  using Cfg = GemmCfg<BN>;
+  static bool attr_set = false;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  if (!attr_set) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::SMEM_BYTES),
+               "cudaFuncSetAttribute(gemm smem)");
+    attr_set = true;
+  }
+  CUtensorMap tA, tB;
+  if (A_MN)
+    tA = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.lda * 2, 64, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    tA = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda * 2, 64, BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (B_MN)
+    tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb * 2, 64, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.ldb * 2, 64, BN,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status);
+  count_launch();
+  check_cuda(cudaGetLastError(), "gemm_tc_kernel launch");
+}
+
+template <int BN>
+void dispatch_bn(const GemmArgs& a, int epi, const Sched& s, int grid, cudaStream_t st,
+                 int* status) {
+  const int mode = (a.a_mn_major ? 2 : 0) | (a.b_mn_major ? 1 : 0);
+#define DDB_CASE(E)                                                             \
+  case E:                                                                       \
+    if (mode == 0) return launch<BN, false, false, E>(a, s, grid, st, status);  \
+    if (mode == 1) return launch<BN, false, true, E>(a, s, grid, st, status);   \
+    break;
+  switch (epi) {
+    DDB_CASE(kEpiBf16)
+    DDB_CASE(kEpiDSwiGLU)
+    case kEpiF32:
+      if (mode == 0) return launch<BN, false, false, kEpiF32>(a, s, grid, st, status);
+      if (mode == 3) return launch<BN, true, true, kEpiF32>(a, s, grid, st, status);
+      break;
+    case kEpiF32Atomic:
+      if (mode == 0) return launch<BN, false, false, kEpiF32Atomic>(a, s, grid, st, status);
+      if (mode == 3) return launch<BN, true, true, kEpiF32Atomic>(a, s, grid, st, status);
+      break;
+    case kEpiSwiGLU:
+      if (mode == 0) return launch<BN, false, false, kEpiSwiGLU>(a, s, grid, st, status);
+      break;
+    case kEpiRope:
+      if (mode == 0) return launch<BN, false, false, kEpiRope>(a, s, grid, st, status);
+      break;
+    case kEpiGateResidual:
+      if (mode == 0) return launch<BN, false, false, kEpiGateResidual>(a, s, grid, st, status);
+      break;
+    default:
+      break;
+  }
+#undef DDB_CASE
+  throw std::runtime_error("gemm: unsupported epilogue/major combination (epi=" +
+                           std::to_string(epi) + ", mode=" + std::to_string(mode) + ")");
+}
+
+}  // namespace
+
+void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
+  GemmArgs a = a_in;
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
+  if (a.N % 32 != 0) throw std::runtime_error("gemm: N must be a multiple of 32");
+  if (epi == kEpiSwiGLU && a.N % 64 != 0)
+    throw std::runtime_error("gemm: SwiGLU needs N % 64 == 0");
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  const int sms = num_sms(dev);
+  int bn = a.bn;
+  if (bn == 0) {
+    // 256-wide tiles unless that leaves most SMs idle on a small problem
+    const long tiles256 = static_cast<long>((a.M + BM - 1) / BM) * ((a.N + 255) / 256);
+    bn = (a.N >= 256 && tiles256 >= sms) ? 256 : 128;
+    if (a.N % 256 != 0 && a.N < 512) bn = 128;
+  }
+  Sched s;
+  s.tiles_m = (a.M + BM - 1) / BM;
+  s.tiles_n = (a.N + bn - 1) / bn;
+  s.kblocks = (a.K + BK - 1) / BK;
+  int splits = 1;
+  if (epi == kEpiF32Atomic) {
+    splits = a.splits;
+    if (splits <= 0) {
+      const int tiles = s.tiles_m * s.tiles_n;
+      splits = 1;
+      while (tiles * splits * 2 <= 2 * sms && s.kblocks / (splits * 2) >= 8) splits *= 2;
+    }
+  }
+  s.kb_per_split = (s.kblocks + splits - 1) / splits;
+  s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
+  s.total = s.tiles_m * s.tiles_n * s.splits;
+  int grid = s.total < sms ? s.total : sms;
+  if (a.max_ctas > 0 && grid > a.max_ctas) grid = a.max_ctas;
+  int* status = device_status(dev);
+  if (bn == 256)
+    dispatch_bn<256>(a, epi, s, grid, stream, status);
+  else
+    dispatch_bn<128>(a, epi, s, grid, stream, status);
+}
+
+}  // namespace ddb

@@ -1,0 +1,50 @@
+// Persistent tcgen05 GEMM for sm_100a: D[M,N] = A[M,K] * B[N,K]^T with fused epilogues.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ddb {
+
+enum GemmEpilogue : int {
+  kEpiBf16 = 0,        // D(bf16) = acc (+ bias[n]) (+ C[m,n])
+  kEpiF32 = 1,         // D(f32)  = acc (+ bias[n])
+  kEpiF32Atomic = 2,   // D(f32) += acc   (split-K capable)
+  kEpiSwiGLU = 3,      // D(bf16) = acc (gate/up interleaved by 32), D2(bf16) = silu(g)*u
+  kEpiDSwiGLU = 4,     // acc = dA; C = gu (bf16); D(bf16) = d(gu) in gu's layout
+  kEpiRope = 5,        // D(bf16) = acc with rotary pairs applied to columns < rope_cols
+  kEpiGateResidual = 6 // D(bf16) = C + gate[row_group, n] * acc (AdaLN-Zero residual)
+};
+
+struct GemmArgs {
+  int M = 0, N = 0, K = 0;
+  const void* A = nullptr;  // bf16
+  long lda = 0;             // elements between rows of A's storage
+  bool a_mn_major = false;  // storage is [K][M] instead of [M][K]
+  const void* B = nullptr;  // bf16
+  long ldb = 0;
+  bool b_mn_major = false;  // storage is [K][N] instead of [N][K]
+  void* D = nullptr;
+  long ldd = 0;
+  const void* C = nullptr;  // bf16 residual / gu for dswiglu (may alias D)
+  long ldc = 0;
+  const float* bias = nullptr;
+  void* D2 = nullptr;       // swiglu activation output
+  long ldd2 = 0;
+  // rotary table: float2 (cos, sin) [positions][pairs_per_head], row -> position
+  const float2* rope_tab = nullptr;
+  int rope_cols = 0;        // columns [0, rope_cols) are rotated (q and k)
+  int rope_rows_per_seq = 1;
+  int rope_pos_offset = 0;
+  int rope_head_dim = 64;
+  // gated residual: gate is bf16 [M / gate_rows_per_group][ldg]
+  const void* gate = nullptr;
+  long ldg = 0;
+  int gate_rows_per_group = 1;
+  int splits = 1;           // split-K factor (kEpiF32Atomic only)
+  int bn = 0;               // 0 = auto (128 or 256)
+  int max_ctas = 0;         // 0 = all SMs
+};
+
+void gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
+
+}  // namespace ddb

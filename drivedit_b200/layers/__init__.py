@@ -1,0 +1,10 @@
+"""PyTorch layer library (CPU path and numerical oracle for the sm_100a kernels)."""
+from .attention import (BidirectionalMultiHeadAttention, CausalMultiHeadAttention,
+                        CrossAttention, KVCache, MultiHeadAttention, attention_reference,
+                        create_block_causal_mask, create_causal_mask, frame_causal_mask, mha)
+from .mlp import GeGLU, MLP, ConditionalMLP, SwiGLU, create_mlp, pack_swiglu, unpack_swiglu
+from .moe import ExpertFFN, MoEFFN, MoEOutput, Router, aux_load_balance_loss
+from .norms import AdaLN, AdaLNZero, LayerNorm, RMSNorm
+from .rope import RoPE3D, RoPELayer, apply_rope, rope_angles_3d, rope_apply, rope_table
+from .sla import (CausalSparseLinearAttention, SLAConfig, SparseLinearAttention,
+                  create_sla_layer, sla_reference, sla_route)

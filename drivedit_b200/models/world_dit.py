@@ -1,0 +1,265 @@
+"""Action-conditioned latent-video flow-matching DiT (the flagship world model).
+
+Built from the reference's pieces, with the semantics decisions spelled out:
+  * tokens: latent frames ``[B, F, C, H, W]`` cut into ``p x p`` patches
+    (``C*p*p``-dim), projected by ``patch_embed``; ``unpatchify`` inverts it. (The
+    reference's ``WorldModel`` patches RGB at 16x16, models/world_model.py:113-134;
+    ``DiTStudent`` projects whole latent vectors, models/dit_student.py:42.)
+  * conditioning: per-frame ``c = silu(t_embed(t) + action_embed(a_f))`` where
+    ``t_embed`` is the reference's ``TimestepEmbedding`` (blocks/flow_matching.py:62-91,
+    256 Fourier features -> MLP; ``t`` is scaled by ``time_scale`` first) and the
+    action MLP maps each frame's action vector.
+  * blocks: the reference's ``DiTBlock`` (blocks/dit_block.py:21-140): pre-norm
+    AdaLN(RMSNorm) -> attention -> residual, AdaLN -> SwiGLU -> residual; the AdaLN
+    scale/shift come per frame from ``c`` (one ``ada`` projection per block), optional
+    adaLN-Zero gates (blocks/flow_matching.py:131-144).
+  * attention: 3-D RoPE with an explicit (16, 24, 24) channel split for d_head = 64,
+    frame-causal masking (every token of frame f sees frames <= f) or token-causal /
+    bidirectional, dense softmax or SLA (:mod:`drivedit_b200.layers.sla`).
+  * FFN: dense SwiGLU (gate/value rows interleaved by 32 for the fused epilogue) or the
+    DeepSeek MoE (:mod:`drivedit_b200.layers.moe`).
+  * head: AdaLN final norm + zero-initialised linear to patch space.
+
+On CUDA the blocks run through the fused sm_100a path (:mod:`drivedit_b200.ops.block`);
+on CPU the same math runs in PyTorch (the numerical oracle and the CPU baseline).
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..config import ModelConfig
+from ..layers.attention import attention_reference, frame_causal_mask
+from ..layers.mlp import split_gu
+from ..layers.moe import MoEFFN
+from ..layers.rope import RoPE3D, apply_rope
+from ..layers.sla import SLAConfig, sla_topk_reference
+
+
+def patchify(x: torch.Tensor, p: int) -> torch.Tensor:
+    """``[B, F, C, H, W]`` -> ``[B, F*(H/p)*(W/p), C*p*p]`` (channel-major patch vectors)."""
+    B, Fr, C, H, W = x.shape
+    x = x.reshape(B, Fr, C, H // p, p, W // p, p)
+    x = x.permute(0, 1, 3, 5, 2, 4, 6)
+    return x.reshape(B, Fr * (H // p) * (W // p), C * p * p)
+
+
+def unpatchify(t: torch.Tensor, frames: int, C: int, H: int, W: int, p: int) -> torch.Tensor:
+    B = t.shape[0]
+    t = t.reshape(B, frames, H // p, W // p, C, p, p)
+    t = t.permute(0, 1, 4, 2, 5, 3, 6)
+    return t.reshape(B, frames, C, H, W)
+
+
+class TimestepEmbedding(nn.Module):
+    """Sinusoidal features of ``t * time_scale`` -> Linear -> SiLU -> Linear
+    (reference names ``linear1`` / ``linear2``)."""
+
+    def __init__(self, dim: int, fourier_features: int = 256, time_scale: float = 1000.0):
+        super().__init__()
+        self.fourier_features = fourier_features
+        self.time_scale = time_scale
+        self.linear1 = nn.Linear(fourier_features, dim)
+        self.linear2 = nn.Linear(dim, dim)
+
+    def features(self, t: torch.Tensor) -> torch.Tensor:
+        half = self.fourier_features // 2
+        freq = torch.exp(-math.log(10000.0) * torch.arange(half, device=t.device, dtype=torch.float32)
+                         / (half - 1))
+        ang = t.float()[..., None] * self.time_scale * freq
+        return torch.cat([ang.sin(), ang.cos()], -1)
+
+    def forward(self, t: torch.Tensor) -> torch.Tensor:
+        return self.linear2(F.silu(self.linear1(self.features(t))))
+
+
+class ActionEmbedding(nn.Module):
+    def __init__(self, action_dim: int, dim: int):
+        super().__init__()
+        self.linear1 = nn.Linear(action_dim, dim)
+        self.linear2 = nn.Linear(dim, dim)
+
+    def forward(self, a: torch.Tensor) -> torch.Tensor:
+        return self.linear2(F.silu(self.linear1(a)))
+
+
+class _Lin(nn.Module):
+    """Bias-free weight holder with the reference's ``<name>.weight`` key."""
+
+    def __init__(self, out_f: int, in_f: int, std: float = 0.02):
+        super().__init__()
+        self.weight = nn.Parameter(torch.randn(out_f, in_f) * std)
+
+
+class _Norm(nn.Module):
+    def __init__(self, d: int):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+
+
+class WorldDiTBlock(nn.Module):
+    def __init__(self, cfg: ModelConfig, layer_idx: int):
+        super().__init__()
+        d, F_ = cfg.d_model, cfg.mlp_hidden
+        self.cfg = cfg
+        self.layer_idx = layer_idx
+        self.n_mod = 6 if cfg.adaln_zero else 4
+        self.norm1 = _Norm(d)
+        self.norm2 = _Norm(d)
+        self.attn = nn.Module()
+        self.attn.qkv = _Lin(3 * d, d, 0.02)
+        self.attn.proj = _Lin(d, d, 0.02 / math.sqrt(2 * cfg.n_layers))
+        if cfg.attention == "sla":
+            self.attn.proj_lin = _Lin(d, d, 0.0)
+        if cfg.moe is None:
+            self.mlp = nn.Module()
+            # gate/value rows interleaved by 32 (see layers/mlp.py: pack_swiglu)
+            self.mlp.w13 = _Lin(2 * F_, d, 0.02)
+            self.mlp.w3 = _Lin(d, F_, 0.02 / math.sqrt(2 * cfg.n_layers))
+            self.moe = None
+        else:
+            m = cfg.moe
+            self.moe = MoEFFN(d, m.num_experts, m.top_k, m.expert_dim, m.num_shared,
+                              bias_update_speed=m.bias_update_speed,
+                              aux_loss_weight=m.aux_loss_weight)
+        # per-frame modulation: (scale1, shift1, scale2, shift2[, gate1, gate2])
+        self.ada = nn.Linear(d, self.n_mod * d)
+        nn.init.zeros_(self.ada.weight)
+        nn.init.zeros_(self.ada.bias)
+
+    # ---------------------------------------------------------------- torch path
+    def forward_torch(self, x: torch.Tensor, mod: torch.Tensor, rope_tab: torch.Tensor,
+                      frames: int) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+        """``x [B, T, d]``, ``mod [B, F, n_mod*d]``; returns (x, aux_loss)."""
+        cfg = self.cfg
+        B, T, d = x.shape
+        H, Dh = cfg.n_heads, cfg.d_head
+        tpf = T // frames
+        m = mod.repeat_interleave(tpf, dim=1)
+        chunks = m.chunk(self.n_mod, -1)
+        s1, b1, s2, b2 = chunks[:4]
+        dt = x.dtype
+
+        def norm(v, w):
+            vf = v.float()
+            return (vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + cfg.norm_eps)).to(dt) * w.to(dt)
+
+        h = norm(x, self.norm1.weight) * (1 + s1) + b1
+        qkv = (h @ self.attn.qkv.weight.to(dt).t()).view(B, T, 3, H, Dh)
+        q, k, v = qkv.unbind(2)
+        q, k = apply_rope(q, rope_tab), apply_rope(k, rope_tab)
+        if cfg.attention == "sla":
+            scfg = SLAConfig(block_size=cfg.sla.block_size, topk_frac=cfg.sla.topk_frac,
+                             always_diag=cfg.sla.always_diag,
+                             tokens_per_frame=tpf if cfg.causal == "frame" else None,
+                             causal=cfg.causal == "token")
+            o_s, o_l, _ = sla_topk_reference(q, k, v, scfg)
+            a = o_s.to(dt).reshape(B, T, d) @ self.attn.proj.weight.to(dt).t() + \
+                o_l.to(dt).reshape(B, T, d) @ self.attn.proj_lin.weight.to(dt).t()
+        else:
+            if cfg.causal == "frame":
+                mask = frame_causal_mask(T, tpf, device=x.device)
+            elif cfg.causal == "token":
+                mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device=x.device))[None, None]
+            else:
+                mask = None
+            if x.dtype == torch.float32:
+                o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
+                                                   v.transpose(1, 2), attn_mask=mask).transpose(1, 2)
+            else:
+                o = attention_reference(q, k, v, mask).to(dt)
+            a = o.reshape(B, T, d) @ self.attn.proj.weight.to(dt).t()
+        if self.n_mod == 6:
+            a = a * chunks[4]
+        x = x + a
+        h2 = norm(x, self.norm2.weight) * (1 + s2) + b2
+        aux = None
+        if self.moe is None:
+            gu = h2 @ self.mlp.w13.weight.to(dt).t()
+            g, u = split_gu(gu)
+            f = (F.silu(g) * u) @ self.mlp.w3.weight.to(dt).t()
+        else:
+            out = self.moe(h2)
+            f, aux = out.output, out.aux_loss
+        if self.n_mod == 6:
+            f = f * chunks[5]
+        return x + f, aux
+
+
+class WorldDiT(nn.Module):
+    """Flow-matching latent-video DiT: predicts the velocity ``x1 - x0`` of ``x_t``."""
+
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        self.cfg = cfg
+        d = cfg.d_model
+        self.patch_embed = nn.Linear(cfg.patch_dim, d)
+        self.t_embed = TimestepEmbedding(d, 256, cfg.time_scale)
+        self.a_embed = ActionEmbedding(cfg.action_dim, d)
+        self.blocks = nn.ModuleList([WorldDiTBlock(cfg, i) for i in range(cfg.n_layers)])
+        self.final_norm = _Norm(d)
+        self.final_ada = nn.Linear(d, 2 * d)
+        nn.init.zeros_(self.final_ada.weight)
+        nn.init.zeros_(self.final_ada.bias)
+        self.out_proj = nn.Linear(d, cfg.patch_dim)
+        nn.init.zeros_(self.out_proj.weight)
+        nn.init.zeros_(self.out_proj.bias)
+        self.rope = RoPE3D(cfg.d_head, cfg.grid_h, cfg.grid_w, cfg.max_frames, cfg.rope_base,
+                           cfg.rope_temporal_factor, cfg.rope_split)
+        self.fused = None  # set by enable_fused() on CUDA
+
+    # ---------------------------------------------------------------- helpers
+    def condition(self, t: torch.Tensor, actions: torch.Tensor) -> torch.Tensor:
+        """Per-frame conditioning ``[B, F, d]`` from ``t [B]`` or ``[B, F]`` and actions."""
+        te = self.t_embed(t)
+        if te.dim() == 2:
+            te = te[:, None]
+        return F.silu(te + self.a_embed(actions.float()))
+
+    def no_decay_names(self) -> List[str]:
+        return [n for n, p in self.named_parameters()
+                if p.dim() < 2 or n.endswith(".bias") or "norm" in n.split(".")[-2]]
+
+    # ---------------------------------------------------------------- forward
+    def forward(self, x_t: torch.Tensor, t: torch.Tensor, actions: torch.Tensor,
+                frame_offset: int = 0, return_aux: bool = False, return_features: Optional[int] = None):
+        """``x_t [B, F, C, H, W]``, ``t [B]`` / ``[B, F]``, ``actions [B, F, A]``."""
+        cfg = self.cfg
+        B, Fr, C, H, W = x_t.shape
+        if self.fused is not None and x_t.is_cuda:
+            return self.fused.forward(self, x_t, t, actions, frame_offset, return_aux,
+                                      return_features)
+        dt = x_t.dtype
+        tok = patchify(x_t, cfg.patch)
+        x = self.patch_embed(tok.to(self.patch_embed.weight.dtype)).to(dt)
+        c = self.condition(t, actions)                       # [B, F, d] fp32
+        tab = self.rope.table(Fr, frame_offset).to(x.device)
+        aux_total = x.new_zeros((), dtype=torch.float32)
+        feats = None
+        for i, blk in enumerate(self.blocks):
+            mod = blk.ada(c).to(dt)
+            x, aux = blk.forward_torch(x, mod, tab, Fr)
+            if aux is not None:
+                aux_total = aux_total + aux
+            if return_features is not None and i + 1 == return_features:
+                feats = x
+        fm = self.final_ada(c).to(dt).repeat_interleave(x.shape[1] // Fr, 1)
+        sc, sh = fm.chunk(2, -1)
+        xf = x.float()
+        hn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg.norm_eps)).to(dt) * \
+            self.final_norm.weight.to(dt)
+        out = self.out_proj((hn * (1 + sc) + sh).to(self.out_proj.weight.dtype))
+        v = unpatchify(out.to(dt), Fr, C, H, W, cfg.patch)
+        if return_features is not None:
+            return v, aux_total, feats
+        return (v, aux_total) if return_aux else v
+
+    def enable_fused(self, **kw):
+        from ..ops.block import FusedWorldDiT
+
+        self.fused = FusedWorldDiT(self, **kw)
+        return self.fused

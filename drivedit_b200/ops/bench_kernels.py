@@ -1,0 +1,87 @@
+"""Kernel micro-benchmarks (CUDA-event timing after warm-up, L2 flushed between runs).
+
+``python -m drivedit_b200.ops.bench_kernels gemm`` times the tcgen05 GEMM at the DiT-B
+training shapes (8 x 8192 tokens, d=768) next to ``torch.matmul`` (cuBLAS) and prints
+one JSON line per shape with TFLOP/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _timeit(fn, iters=20, warmup=5, flush=True):
+    buf = torch.empty(L2_FLUSH_BYTES // 4, device="cuda", dtype=torch.float32)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush:
+            buf.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+GEMM_SHAPES = [
+    # (name, M, N, K, a_t, b_t, epi)
+    ("qkv_fwd", 65536, 2304, 768, False, False, "bf16"),
+    ("w13_fwd_swiglu", 65536, 6144, 768, False, False, "swiglu"),
+    ("w2_fwd", 65536, 768, 3072, False, False, "bf16"),
+    ("w2_dgrad_dswiglu", 65536, 3072, 768, False, True, "dswiglu"),
+    ("w13_dgrad", 65536, 768, 6144, False, True, "bf16"),
+    ("w13_wgrad", 6144, 768, 65536, True, True, "f32_acc"),
+    ("square_8192", 8192, 8192, 8192, False, False, "bf16"),
+]
+
+
+def bench_gemm(iters: int = 20):
+    from .gemm import gemm
+
+    for name, M, N, K, a_t, b_t, epi in GEMM_SHAPES:
+        a = torch.randn(*((K, M) if a_t else (M, K)), device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(*((K, N) if b_t else (N, K)), device="cuda", dtype=torch.bfloat16)
+        kw = {}
+        if epi == "dswiglu":
+            kw["residual"] = torch.randn(M, 2 * N, device="cuda", dtype=torch.bfloat16)
+        out = None
+        if epi == "f32_acc":
+            out = torch.zeros(M, N, device="cuda", dtype=torch.float32)
+        ms = _timeit(lambda: gemm(a, b, out, epi=epi, a_t=a_t, b_t=b_t, **kw), iters)
+        A = a.t() if a_t else a
+        B = b.t() if b_t else b
+        ms_ref = _timeit(lambda: torch.matmul(A, B.t()), iters)
+        flops = 2.0 * M * N * K
+        print(json.dumps({
+            "kernel": "gemm_tc", "shape": name, "M": M, "N": N, "K": K, "epi": epi,
+            "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+            "cublas_ms": round(ms_ref, 4), "cublas_tflops": round(flops / ms_ref / 1e9, 1),
+        }), flush=True)
+        del a, b, out, kw
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("what", nargs="*", default=["gemm"])
+    p.add_argument("--iters", type=int, default=20)
+    args = p.parse_args()
+    for w in args.what:
+        {"gemm": bench_gemm}[w](args.iters) if w == "gemm" else globals()[f"bench_{w}"](args.iters)
+    from ._ext import check_device_status
+
+    check_device_status()
+
+
+if __name__ == "__main__":
+    main()

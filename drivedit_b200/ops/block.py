@@ -1,0 +1,175 @@
+"""Fused sm_100a forward/backward of the world-model DiT blocks.
+
+Per block, with ``M = B*T`` token rows, ``d`` model width, ``F`` SwiGLU width:
+
+forward                                           kernels
+  h1, r1 = adaln_rmsnorm(x, w1, mod[s1, b1])        fused/norm.cu
+  qkv    = h1 Wqkv^T  (+ 3-D RoPE on q, k)          gemm.cu, rope epilogue
+  o, lse = attention(qkv)  (dense or SLA)           attn/*.cu
+  x1     = x + o Wo^T (+ o_lin Wlin^T)              gemm.cu, residual epilogue
+  h2, r2 = adaln_rmsnorm(x1, w2, mod[s2, b2])
+  gu, a  = h2 W13^T, silu(g) * u                    gemm.cu, SwiGLU epilogue
+  x2     = x1 + a W3^T                              gemm.cu, residual epilogue
+
+backward: the transposed products read operands in place (MN-major TMA tiles), weight
+gradients accumulate in fp32 straight into the flat gradient buffer, the SwiGLU
+derivative is the epilogue of the ``dA`` GEMM, and the norm backward adds the
+residual-stream gradient and reduces the norm-weight and modulation gradients.
+
+Non-block pieces (patch embedding, output head) use the same GEMM through
+:func:`drivedit_b200.ops.linear.linear`; the conditioning MLPs (``[B*F, d]``, a few
+hundred rows) stay in PyTorch.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ..parallel.flat import FlatParamGroup
+from .attention import attention_bwd, attention_fwd
+from .fused import adaln_rmsnorm, adaln_rmsnorm_bwd, rope_rotate_
+from .gemm import gemm
+from .linear import linear
+
+
+class BlockCtx:
+    """Static per-call data shared by all blocks of one forward."""
+
+    def __init__(self, B, T, frames, tpf, d, H, Dh, rope_tab, attn_mode, sla_cfg, causal,
+                 rope_pos_offset=0):
+        self.B, self.T, self.frames, self.tpf = B, T, frames, tpf
+        self.d, self.H, self.Dh = d, H, Dh
+        self.rope_tab = rope_tab
+        self.attn_mode = attn_mode
+        self.sla_cfg = sla_cfg
+        self.causal = causal
+        self.rope_pos_offset = rope_pos_offset
+
+
+class _BlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx):
+        d = bc.d
+        W = group.compute_view
+        w_qkv = W(blk.attn.qkv.weight)
+        w_o = W(blk.attn.proj.weight)
+        w_13 = W(blk.mlp.w13.weight)
+        w_3 = W(blk.mlp.w3.weight)
+        n1 = blk.norm1.weight
+        n2 = blk.norm2.weight
+        h1, r1 = adaln_rmsnorm(x, n1, mod, 0, d, bc.tpf)
+        qkv = gemm(h1, w_qkv, epi="rope", rope_tab=bc.rope_tab, rope_cols=2 * d,
+                   rope_rows_per_seq=bc.T, rope_pos_offset=bc.rope_pos_offset,
+                   rope_head_dim=bc.Dh)
+        o, o_lin, lse, aux = attention_fwd(qkv, bc)
+        x1 = gemm(o, w_o, residual=x)
+        if o_lin is not None:
+            gemm(o_lin, W(blk.attn.proj_lin.weight), x1, residual=x1)
+        h2, r2 = adaln_rmsnorm(x1, n2, mod, 2 * d, 3 * d, bc.tpf)
+        gu = torch.empty(x.shape[0], w_13.shape[0], device=x.device, dtype=torch.bfloat16)
+        a = torch.empty(x.shape[0], w_13.shape[0] // 2, device=x.device, dtype=torch.bfloat16)
+        gemm(h2, w_13, gu, epi="swiglu", out2=a)
+        x2 = gemm(a, w_3, residual=x1)
+        ctx.save_for_backward(x, mod, h1, r1, qkv, o, lse, x1, h2, r2, gu, a,
+                              *([o_lin] if o_lin is not None else []))
+        ctx.blk, ctx.group, ctx.bc, ctx.aux = blk, group, bc, aux
+        return x2
+
+    @staticmethod
+    def backward(ctx, dx2):
+        saved = ctx.saved_tensors
+        x, mod, h1, r1, qkv, o, lse, x1, h2, r2, gu, a = saved[:12]
+        o_lin = saved[12] if len(saved) > 12 else None
+        blk, group, bc = ctx.blk, ctx.group, ctx.bc
+        d = bc.d
+        W = group.compute_view
+        dx2 = dx2.contiguous()
+        # ---- MLP
+        dgu = gemm(dx2, W(blk.mlp.w3.weight), epi="dswiglu", b_t=True, residual=gu)
+        gemm(dx2, a, blk.mlp.w3.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+        dh2 = gemm(dgu, W(blk.mlp.w13.weight), b_t=True)
+        gemm(dgu, h2, blk.mlp.w13.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+        del dgu
+        dmod = torch.zeros(mod.shape, device=mod.device, dtype=torch.float32)
+        dx1 = adaln_rmsnorm_bwd(dh2, x1, r2, blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf,
+                                dmod, blk.norm2.weight.grad, dx2)
+        del dh2
+        # ---- attention output projection(s)
+        do = gemm(dx1, W(blk.attn.proj.weight), b_t=True)
+        gemm(dx1, o, blk.attn.proj.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+        do_lin = None
+        if o_lin is not None:
+            do_lin = gemm(dx1, W(blk.attn.proj_lin.weight), b_t=True)
+            gemm(dx1, o_lin, blk.attn.proj_lin.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+        dqkv = attention_bwd(qkv, o, lse, do, do_lin, ctx.aux, bc)
+        # q, k gradients back through the rotation
+        rope_rotate_(dqkv, 2 * d, bc.rope_tab, bc.Dh, bc.T, bc.rope_pos_offset, inverse=True)
+        dh1 = gemm(dqkv, W(blk.attn.qkv.weight), b_t=True)
+        gemm(dqkv, h1, blk.attn.qkv.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+        dx = adaln_rmsnorm_bwd(dh1, x, r1, blk.norm1.weight, mod, 0, d, bc.tpf, dmod,
+                               blk.norm1.weight.grad, dx1)
+        return dx, dmod, None, None, None
+
+
+class FusedWorldDiT:
+    """CUDA execution engine of :class:`~drivedit_b200.models.world_dit.WorldDiT`."""
+
+    def __init__(self, model, group: Optional[FlatParamGroup] = None):
+        self.model = model
+        self.group = group if group is not None else FlatParamGroup(model.named_parameters())
+        for blk in model.blocks:
+            if blk.moe is not None:
+                raise NotImplementedError("MoE blocks run through drivedit_b200.ops.moe_block")
+
+    def forward(self, model, x_t, t, actions, frame_offset=0, return_aux=False,
+                return_features=None):
+        from ..models.world_dit import patchify, unpatchify
+
+        cfg = model.cfg
+        g = self.group
+        B, Fr, C, H, W_ = x_t.shape
+        d = cfg.d_model
+        tok = patchify(x_t, cfg.patch).reshape(-1, cfg.patch_dim).to(torch.bfloat16).contiguous()
+        T = tok.shape[0] // B
+        x = linear(tok, g.compute_view(model.patch_embed.weight), model.patch_embed.bias,
+                   model.patch_embed.weight, model.patch_embed.bias)
+        c = model.condition(t, actions)                            # [B, F, d] fp32
+        c2 = c.reshape(B * Fr, d)
+        tab = model.rope.table(Fr, frame_offset).to(x.device)
+        bc = BlockCtx(B, T, Fr, T // Fr, d, cfg.n_heads, cfg.d_head, tab, cfg.attention,
+                      cfg.sla, cfg.causal)
+        feats = None
+        for i, blk in enumerate(model.blocks):
+            mod = blk.ada(c2)                                      # [B*F, 4d] fp32
+            x = _BlockFn.apply(x, mod, blk, g, bc)
+            if return_features is not None and i + 1 == return_features:
+                feats = x
+        fm = model.final_ada(c2)
+        h, _ = _FinalNorm.apply(x, fm, model.final_norm.weight, bc.tpf, cfg.norm_eps)
+        out = linear(h, g.compute_view(model.out_proj.weight), model.out_proj.bias,
+                     model.out_proj.weight, model.out_proj.bias)
+        v = unpatchify(out.view(B, T, cfg.patch_dim), Fr, C, H, W_, cfg.patch)
+        aux = torch.zeros((), device=x.device)
+        if return_features is not None:
+            return v, aux, feats
+        return (v, aux) if return_aux else v
+
+
+class _FinalNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, mod, w, tpf, eps):
+        d = x.shape[1]
+        h, r = adaln_rmsnorm(x, w, mod, 0, d, tpf, eps)
+        ctx.save_for_backward(x, mod, r)
+        ctx.w, ctx.tpf = w, tpf
+        return h, r
+
+    @staticmethod
+    def backward(ctx, dh, _dr):
+        x, mod, r = ctx.saved_tensors
+        d = x.shape[1]
+        dmod = torch.zeros(mod.shape, device=mod.device, dtype=torch.float32)
+        dx = adaln_rmsnorm_bwd(dh.contiguous(), x, r, ctx.w, mod, 0, d, ctx.tpf, dmod,
+                               ctx.w.grad, None)
+        return dx, dmod, None, None, None

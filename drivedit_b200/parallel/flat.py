@@ -1,0 +1,95 @@
+"""Flat parameter storage: one fp32 master buffer, one fp32 gradient buffer and one bf16
+compute copy for a group of parameters.
+
+Every ``nn.Parameter`` of the group is re-pointed at a view of the flat master buffer
+and its ``.grad`` at a view of the flat gradient buffer, so:
+  * autograd accumulates ordinary gradients in place into the flat buffer;
+  * fused kernels write weight gradients straight into ``p.grad`` (fp32 reductions);
+  * the fused AdamW kernel updates the whole group in one pass and writes the bf16
+    compute copy the next forward reads (no separate cast);
+  * FSDP shards exactly these buffers (``drivedit_b200.parallel.fsdp``).
+
+Segments are padded to 64 elements so every view starts 128-byte aligned in the bf16
+copy (TMA needs 16) and weight-decay / no-decay parameters are grouped so the update
+kernel receives one boundary instead of a mask.
+"""
+from __future__ import annotations
+
+from typing import Dict, Iterable, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+ALIGN = 64
+
+
+def _round(n: int, a: int) -> int:
+    return (n + a - 1) // a * a
+
+
+class FlatParamGroup:
+    def __init__(self, named_params: Iterable[Tuple[str, nn.Parameter]], device=None,
+                 no_decay: Optional[Iterable[str]] = None, pad_to: int = 1,
+                 compute_dtype: torch.dtype = torch.bfloat16):
+        named = list(named_params)
+        nd = set(no_decay or [])
+        decay = [(n, p) for n, p in named if n not in nd]
+        nodecay = [(n, p) for n, p in named if n in nd]
+        self.names: List[str] = []
+        self.params: List[nn.Parameter] = []
+        self.offsets: Dict[str, Tuple[int, int]] = {}
+        off = 0
+        self.decay_end = 0
+        for i, (n, p) in enumerate(decay + nodecay):
+            if i == len(decay):
+                self.decay_end = off
+            self.names.append(n)
+            self.params.append(p)
+            self.offsets[n] = (off, p.numel())
+            off = _round(off + p.numel(), ALIGN)
+        if not nodecay:
+            self.decay_end = off
+        self.numel = _round(off, ALIGN * max(pad_to, 1))
+        dev = device if device is not None else (self.params[0].device if self.params else "cpu")
+        self.device = torch.device(dev)
+        self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=self.device)
+        with torch.no_grad():
+            for n, p in zip(self.names, self.params):
+                o, k = self.offsets[n]
+                self.master[o:o + k].copy_(p.data.reshape(-1).float())
+                p.data = self.master[o:o + k].view(p.shape)
+                p.grad = self.grad[o:o + k].view(p.shape)
+        self.refresh_compute()
+
+    # ------------------------------------------------------------------ views
+    def view(self, buf: torch.Tensor, p: nn.Parameter) -> torch.Tensor:
+        n = self.names[self.index(p)]
+        o, k = self.offsets[n]
+        return buf[o:o + k].view(p.shape)
+
+    def index(self, p: nn.Parameter) -> int:
+        for i, q in enumerate(self.params):
+            if q is p:
+                return i
+        raise KeyError("parameter not in this group")
+
+    def compute_view(self, p: nn.Parameter) -> torch.Tensor:
+        return self.view(self.compute, p)
+
+    def grad_view(self, p: nn.Parameter) -> torch.Tensor:
+        return self.view(self.grad, p)
+
+    # ------------------------------------------------------------------ updates
+    def refresh_compute(self):
+        self.compute.copy_(self.master)
+
+    def zero_grad(self):
+        self.grad.zero_()
+        for n, p in zip(self.names, self.params):
+            if p.grad is None or p.grad.data_ptr() != self.grad_view(p).data_ptr():
+                p.grad = self.grad_view(p)
+
+    def state_dict(self) -> Dict[str, torch.Tensor]:
+        return {n: p.detach().clone() for n, p in zip(self.names, self.params)}

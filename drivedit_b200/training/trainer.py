@@ -1,0 +1,80 @@
+"""Flow-matching trainer for the world models (single device, DP, FSDP, FSDP + EP).
+
+One ``train_step(batch)`` = sample noise and flow time, build ``x_t``, predict the
+velocity, MSE (+ MoE aux loss, + REPA when configured), backward, AdamW. Mirrors the
+reference's ``FlowMatchingTrainer.train_step`` (blocks/flow_matching.py:424-491) and the
+``UnifiedTrainer`` step (training/unified_trainer.py:1095-1152) with bf16 compute on
+the sm_100a path instead of fp16 autocast + GradScaler.
+
+Parameters live in a :class:`FlatParamGroup`; on CUDA the forward/backward of every
+block runs through the fused kernels and the update is one fused AdamW pass that also
+writes the bf16 weights of the next step. Under ``parallel="fsdp"`` the
+:class:`~drivedit_b200.parallel.fsdp.FSDPEngine` owns the buffers instead.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.nn as nn
+
+from ..config import TrainConfig
+from ..data.synthetic import LatentBatch
+from ..parallel.flat import FlatParamGroup
+from .flow_matching import interpolate, sample_t
+from .optim import FlatAdamW
+
+
+class WorldModelTrainer:
+    def __init__(self, model: nn.Module, cfg: TrainConfig, device=None, fused: Optional[bool] = None,
+                 process_group=None):
+        self.model = model
+        self.cfg = cfg
+        self.device = torch.device(device) if device is not None else next(model.parameters()).device
+        self.model.to(self.device)
+        self.cuda = self.device.type == "cuda"
+        self.compute_dtype = torch.bfloat16 if (self.cuda and cfg.dtype == "bf16") else torch.float32
+        self.pg = process_group
+        self.group = FlatParamGroup(model.named_parameters(), self.device,
+                                    no_decay=model.no_decay_names())
+        self.opt = FlatAdamW(self.group, cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay, cfg.grad_clip)
+        self.fused = self.cuda if fused is None else fused
+        if self.fused:
+            model.enable_fused(group=self.group)
+        self.gen = torch.Generator(device=self.device)
+        self.gen.manual_seed(cfg.seed + 1)
+        self.step_idx = 0
+
+    def loss(self, batch: LatentBatch) -> torch.Tensor:
+        x1 = batch.latents.to(self.compute_dtype)
+        B = x1.shape[0]
+        x0 = torch.randn(x1.shape, device=x1.device, generator=self.gen, dtype=torch.float32)
+        t = sample_t(B, self.cfg.t_sampling, x1.device, self.gen)
+        x_t = interpolate(x0, x1.float(), t).to(self.compute_dtype)
+        v, aux = self.model(x_t, t, batch.actions, return_aux=True)
+        target = (x1.float() - x0)
+        loss = (v.float() - target).pow(2).mean()
+        return loss + aux
+
+    def train_step(self, batch: LatentBatch) -> torch.Tensor:
+        self.group.zero_grad()
+        loss = self.loss(batch)
+        loss.backward()
+        if self.pg is not None:
+            torch.distributed.all_reduce(self.group.grad, group=self.pg)
+            scale = 1.0 / torch.distributed.get_world_size(self.pg)
+        else:
+            scale = 1.0
+        self.opt.step(grad_scale=scale)
+        self.step_idx += 1
+        return loss.detach()
+
+    def state_dict(self) -> Dict:
+        return {"model": self.model.state_dict(), "optim": self.opt.state_dict(),
+                "step": self.step_idx}
+
+    def load_state_dict(self, sd: Dict):
+        self.model.load_state_dict(sd["model"])
+        self.group.refresh_compute()
+        self.opt.load_state_dict(sd["optim"])
+        self.step_idx = int(sd["step"])
