@@ -5,11 +5,17 @@ The model is assembled from the reference's public building blocks at the DiT-B 
 ``blocks.dit_block.DiTBlock`` (AdaLN conditioning, SwiGLU, 1-D RoPE) with its attention
 swapped for the reference's drop-in ``layers.sla.CausalSparseLinearAttention``
 (64-token blocks), ``blocks.flow_matching.TimestepEmbedding`` for the flow time and
-``layers.nn_helpers.RMSNorm`` for the head, trained by
-``training.cuda_optimized.OptimizedTrainer`` (bf16 autocast; FSDP over NCCL when more
-than one rank; its default activation checkpointing; no torch.compile, whose autotuning
-of the reference's Python block loop would not finish) with AdamW. The only glue code
-here is patchify/unpatchify, the action MLP and the loss closure.
+``layers.nn_helpers.RMSNorm`` for the head. Multi-GPU runs wrap the model with the
+reference's own FSDP wrapper (``OptimizedTrainer._wrap_fsdp``, training/cuda_optimized.py
+:571-615: FULL_SHARD, bf16 params / fp32 reduce, 1M-parameter auto-wrap) and the
+optimizer is the reference's ``create_optimized_optimizer`` (fused AdamW with decay /
+no-decay groups). The step is bf16 autocast forward, MSE, backward, clip 1.0, AdamW —
+the body of ``OptimizedTrainer.train_step``. ``OptimizedTrainer.__init__`` itself cannot
+run on this PyTorch: it calls ``torch.cuda.amp.autocast(device_type=...)``, which raises
+TypeError (training/cuda_optimized.py:19,518), so its step is reproduced here without
+torch.compile (whose autotuning of the reference's Python SLA block loop would not
+finish) and without activation checkpointing. The only glue code is patchify /
+unpatchify, the action MLP and the loss.
 """
 from __future__ import annotations
 
@@ -84,17 +90,36 @@ def run(args, ws, rank, local):
 
     cfg = get_config(args.config, args.override)
     sys.path.insert(0, REF)
+    import types
+
     import torch.distributed as dist
-    from training.cuda_optimized import CUDAOptimizedConfig, OptimizedTrainer
+    from training.cuda_optimized import (CUDAOptimizedConfig, OptimizedTrainer,
+                                         create_optimized_optimizer)
 
     dev = torch.device("cuda", local)
     torch.manual_seed(cfg.train.seed + rank)
     model = build(cfg, dev)
     ocfg = CUDAOptimizedConfig(compile_mode="default", amp_dtype=torch.bfloat16,
-                               grad_scaler_enabled=False, use_fsdp=ws > 1)
-    trainer = OptimizedTrainer(model, ocfg, dev)
-    opt = torch.optim.AdamW(trainer.model.parameters(), lr=cfg.train.lr,
-                            betas=tuple(cfg.train.betas), weight_decay=cfg.train.weight_decay)
+                               grad_scaler_enabled=False, use_fsdp=ws > 1,
+                               gradient_checkpointing=False)
+    if ws > 1:
+        holder = types.SimpleNamespace(config=ocfg, device=dev)
+        model = OptimizedTrainer._wrap_fsdp(holder, model)
+    opt = create_optimized_optimizer(model, lr=cfg.train.lr, weight_decay=cfg.train.weight_decay,
+                                     betas=tuple(cfg.train.betas))
+
+    class _Step:
+        def train_step(self, batch, optimizer, loss_fn):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = model(**batch)
+                loss = loss_fn(out, batch)["total"]
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(model.parameters(), ocfg.gradient_clip_norm)
+            optimizer.step()
+            optimizer.zero_grad(set_to_none=True)
+            return {"loss": loss.item()}
+
+    trainer = _Step()
     m = cfg.model
     B, Fr = cfg.train.batch_per_gpu, cfg.train.frames
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -144,6 +169,6 @@ def run(args, ws, rank, local):
         "config": {"model": cfg.model.name, "global_batch": B * ws,
                    "seq_len": Fr * m.tokens_per_frame, "attention": m.attention,
                    "parallelism": f"fsdp{ws}" if ws > 1 else "single",
-                   "stack": "reference DiTBlock + CausalSparseLinearAttention + OptimizedTrainer",
+                   "stack": "reference DiTBlock + CausalSparseLinearAttention + _wrap_fsdp + fused AdamW",
                    "l2": "256 MiB buffer overwritten before every timed step"},
     }

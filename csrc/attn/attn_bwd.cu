@@ -1,0 +1,544 @@
+// tcgen05 flash-attention backward, d_head = 64, for sm_100a (KV-stationary).
+//
+// One CTA = one (batch, head, 128-key tile = two adjacent 64-key blocks); it walks the
+// 128-query tiles that can see its keys (all later frames for frame-causal, or the SLA
+// transpose list). Per query tile, with the key tile's K and V resident in shared memory:
+//
+//   S^T  = K Q^T      (M=128 keys, N=128 queries, K=64)        TMEM cols [  0,128)
+//   dP^T = V dO^T     (M=128, N=128, K=64)                      TMEM cols [128,256)
+//   softmax warps (one thread per key row): P^T = exp2(S^T*scale*log2e - lse),
+//                 dS^T = scale * P^T (dP^T - delta); both to shared memory (bf16)
+//   dV  += P^T dO     (M=128, N=64, K=128 queries)              TMEM cols [256,320)
+//   dK  += dS^T Q     (M=128, N=64, K=128)                      TMEM cols [320,384)
+//   dQ   = dS K       (M=128 queries, N=64, K=128 keys; dS^T read MN-major)
+//                                                               TMEM cols [384,448)
+//   dQ warps: TMEM -> fp32 vector reductions into the dQ accumulator.
+// After the last query tile dK and dV go to global memory (bf16).
+//
+// Roles: warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 softmax/dS, warps 6-9 dQ reduction.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <stdexcept>
+
+#include "../common/ptx.cuh"
+#include "../common/tma.h"
+#include "attn.h"
+
+namespace ddb {
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int NS = 2;
+constexpr int TILE = 16384;
+constexpr int OFF_K = 0;
+constexpr int OFF_V = OFF_K + TILE;
+constexpr int OFF_Q = OFF_V + TILE;            // NS stages
+constexpr int OFF_DO = OFF_Q + NS * TILE;      // NS stages
+constexpr int OFF_PT = OFF_DO + NS * TILE;     // 2 chunks
+constexpr int OFF_DST = OFF_PT + 2 * TILE;     // 2 chunks
+constexpr int OFF_VEC = OFF_DST + 2 * TILE;    // lse[128], delta[128], lim[128]
+constexpr int OFF_BAR = OFF_VEC + 3 * 512;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+constexpr uint32_t IDESC_SS = make_idesc_bf16(128, 128, false, false);
+constexpr uint32_t IDESC_GRAD = make_idesc_bf16(128, 64, false, true);  // A K-major, B MN-major
+constexpr uint32_t IDESC_DQ = make_idesc_bf16(128, 64, true, true);     // both MN-major
+
+__device__ __forceinline__ int row_limit(const AttnArgs& a, int q_local) {
+  int lim = a.S;
+  const int qa = a.q_pos_offset + q_local;
+  if (a.causal == kCausalFrame) {
+    lim = min(lim, (qa / a.tpf + 1) * a.tpf - a.kv_pos_offset);
+  } else if (a.causal == kCausalToken) {
+    lim = min(lim, qa + 1 - a.kv_pos_offset);
+  }
+  return max(lim, 0);
+}
+
+// first query (within the sample) whose key limit exceeds key index k
+__device__ __forceinline__ int first_query_seeing(const AttnArgs& a, int k) {
+  if (a.causal == kCausalFrame) {
+    const int ka = k + a.kv_pos_offset;
+    return (ka / a.tpf) * a.tpf - a.q_pos_offset;
+  }
+  if (a.causal == kCausalToken) return k + a.kv_pos_offset - a.q_pos_offset;
+  return 0;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV,
+                    const __grid_constant__ CUtensorMap tmDO, const AttnBwdArgs g, int n_kvtiles,
+                    int n_qtiles, int* status) {
+  const AttnArgs& a = g.f;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;            // NS
+  uint64_t* qd_empty = bars + 1 + NS;      // NS
+  uint64_t* s_full = bars + 1 + 2 * NS;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* ds_full = s_full + 2;
+  uint64_t* ds_empty = s_full + 3;
+  uint64_t* dq_full = s_full + 4;
+  uint64_t* dq_free = s_full + 5;
+  uint64_t* drain = s_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_lse = reinterpret_cast<float*>(smem + OFF_VEC);
+  float* s_delta = s_lse + 128;
+  int* s_lim = reinterpret_cast<int*>(s_delta + 128);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int kt = blockIdx.x % n_kvtiles;
+  const int bh = blockIdx.x / n_kvtiles;
+  const int b = bh / a.H;
+  const int h = bh % a.H;
+  const int k0 = kt * 128;
+  const bool sparse = g.kv_count != nullptr;
+  const long list_idx = static_cast<long>(bh) * n_kvtiles + kt;
+  int nq, qt_first = 0;
+  if (sparse) {
+    nq = g.kv_count[list_idx];
+  } else {
+    const int fq = max(0, first_query_seeing(a, k0));
+    qt_first = fq / 128;
+    nq = fq < a.Tq ? n_qtiles - qt_first : 0;
+    if (k0 >= a.S) nq = 0;
+  }
+  auto qtile_of = [&](int j) -> int {
+    return sparse ? g.kv_qtiles[list_idx * g.max_q + j] : qt_first + j;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&qd_full[s], 1);
+      mbar_init(&qd_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(ds_full, 4);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      const int krow = static_cast<int>(b * a.kv_rows_per_b) + k0;
+      mbar_arrive_expect_tx(kv_full, 2 * TILE);
+      tma_load_2d(smem + OFF_K, &tmK, kv_full, a.k_col + h * 64, krow);
+      tma_load_2d(smem + OFF_K + 8192, &tmK, kv_full, a.k_col + h * 64, krow + 64);
+      tma_load_2d(smem + OFF_V, &tmV, kv_full, a.v_col + h * 64, krow);
+      tma_load_2d(smem + OFF_V + 8192, &tmV, kv_full, a.v_col + h * 64, krow + 64);
+      bool ok = true;
+      int issued = 0;
+      for (int j = 0; j < nq; ++j) {
+        const int s = j % NS;
+        if (!mbar_wait(&qd_empty[s], ((j / NS) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int qrow = static_cast<int>(b * a.q_rows_per_b) + qtile_of(j) * 128;
+        uint8_t* sq = smem + OFF_Q + s * TILE;
+        uint8_t* sd = smem + OFF_DO + s * TILE;
+        mbar_arrive_expect_tx(&qd_full[s], 2 * TILE);
+        tma_load_2d(sq, &tmQ, &qd_full[s], a.q_col + h * 64, qrow);
+        tma_load_2d(sq + 8192, &tmQ, &qd_full[s], a.q_col + h * 64, qrow + 64);
+        tma_load_2d(sd, &tmDO, &qd_full[s], g.do_col + h * 64, qrow);
+        tma_load_2d(sd + 8192, &tmDO, &qd_full[s], g.do_col + h * 64, qrow + 64);
+        ++issued;
+      }
+      if (!ok) {
+        if (status) atomicCAS(status, 0, kStatusTimeoutProducer);
+        *abort_flag = 1;
+      }
+      long long t0 = clock64();
+      while (!mbar_try_wait(kv_full, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
+      }
+      for (int j = max(0, issued - NS); j < issued; ++j) {
+        t0 = clock64();
+        while (!mbar_try_wait(&qd_full[j % NS], (j / NS) & 1) &&
+               clock64() - t0 < kSpinLimitCycles / 8) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(kv_full, 0, abort_flag);
+      const uint32_t aK = smem_u32(smem + OFF_K);
+      const uint32_t aV = smem_u32(smem + OFF_V);
+      const uint32_t aPT = smem_u32(smem + OFF_PT);
+      const uint32_t aDST = smem_u32(smem + OFF_DST);
+      auto issue_grads = [&](int i) -> bool {
+        if (!mbar_wait(ds_full, i & 1, abort_flag)) return false;
+        if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, abort_flag)) return false;
+        tc_fence_after();
+        const int s = i % NS;
+        const uint32_t aQ = smem_u32(smem + OFF_Q + s * TILE);
+        const uint32_t aDO = smem_u32(smem + OFF_DO + s * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // K = 128 queries
+          const uint32_t off = (kk >> 2) * TILE + (kk & 3) * 32;
+          // dV += P^T dO ; dK += dS^T Q   (B operands [queries][dh] read MN-major)
+          mma_bf16_ss(tmem + C_DV, make_sw128_desc(aPT + off, 16, 1024),
+                      make_sw128_desc(aDO + kk * 2048, 8192, 1024), IDESC_GRAD,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tmem + C_DK, make_sw128_desc(aDST + off, 16, 1024),
+                      make_sw128_desc(aQ + kk * 2048, 8192, 1024), IDESC_GRAD,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // K = 128 keys: dQ = dS K
+          // A = dS^T tile read MN-major: queries contiguous in 64-wide chunks (LBO =
+          // chunk distance), keys as rows; B = K [keys][dh] MN-major.
+          mma_bf16_ss(tmem + C_DQ, make_sw128_desc(aDST + kk * 2048, TILE, 1024),
+                      make_sw128_desc(aK + kk * 2048, 8192, 1024), IDESC_DQ, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&qd_empty[s]);
+        mma_commit(ds_empty);
+        mma_commit(dq_full);
+        return true;
+      };
+      for (int j = 0; j < nq && ok; ++j) {
+        const int s = j % NS;
+        if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
+            (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(smem + OFF_Q + s * TILE);
+        const uint32_t aDO = smem_u32(smem + OFF_DO + s * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16_ss(tmem + C_S, make_sw128_desc(aK + kk * 32, 16, 1024),
+                      make_sw128_desc(aQ + kk * 32, 16, 1024), IDESC_SS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tmem + C_DP, make_sw128_desc(aV + kk * 32, 16, 1024),
+                      make_sw128_desc(aDO + kk * 32, 16, 1024), IDESC_SS, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(s_full);
+        if (j > 0 && !issue_grads(j - 1)) ok = false;
+      }
+      if (ok && nq > 0) ok = issue_grads(nq - 1);
+      if (!ok) {
+        if (status) atomicCAS(status, 0, kStatusTimeoutMma);
+        *abort_flag = 1;
+      }
+      mma_commit(drain);
+      long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ softmax / dS warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;   // key row within the tile
+    const int t = (warp - 2) * 32 + lane;  // 0..127 for shared-vector loads
+    const int key = k0 + r;
+    const int khalf = r >> 6;
+    const float sl2 = a.scale * 1.4426950408889634f;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t swz = r & 7;
+    const uint32_t pt_base = smem_u32(smem + OFF_PT) + r * 128;
+    const uint32_t ds_base = smem_u32(smem + OFF_DST) + r * 128;
+    bool ok = true;
+    for (int j = 0; j < nq; ++j) {
+      const int qt = qtile_of(j);
+      const int q0 = qt * 128;
+      // per-query vectors for this tile
+      named_bar(1, 128);
+      {
+        const int q = q0 + t;
+        const bool valid = q < a.Tq;
+        const long vi = static_cast<long>(bh) * a.Tq + q;
+        s_lse[t] = valid ? a.lse[vi] : INFINITY;
+        s_delta[t] = valid ? g.delta[vi] : 0.f;
+        s_lim[t] = valid ? row_limit(a, q) : 0;
+      }
+      named_bar(1, 128);
+      const int bits = sparse ? g.kv_qmask[list_idx * g.max_q + j] : 0xF;
+      if (!mbar_wait(s_full, j & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j > 0 && !mbar_wait(ds_empty, (j - 1) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(trow + C_S + c0, rs);
+        tmem_ld32(trow + C_DP + c0, rp);
+        tmem_wait_ld();
+        const bool half_on = (bits >> ((c0 >> 6) * 2 + khalf)) & 1;
+        float p[32], ds[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int qi = c0 + c;
+          const bool vis = half_on && key < s_lim[qi];
+          const float pv = vis ? exp2f(__uint_as_float(rs[c]) * sl2 - s_lse[qi]) : 0.f;
+          p[c] = pv;
+          ds[c] = pv * (__uint_as_float(rp[c]) - s_delta[qi]) * a.scale;
+        }
+        const int ch = c0 >> 6;
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int u = ((c0 & 63) >> 3) + u4;
+          const int c = u4 * 8;
+          const uint32_t off = ch * TILE + ((u ^ swz) << 4);
+          st_shared_v4(pt_base + off, pack_bf16(p[c], p[c + 1]), pack_bf16(p[c + 2], p[c + 3]),
+                       pack_bf16(p[c + 4], p[c + 5]), pack_bf16(p[c + 6], p[c + 7]));
+          st_shared_v4(ds_base + off, pack_bf16(ds[c], ds[c + 1]),
+                       pack_bf16(ds[c + 2], ds[c + 3]), pack_bf16(ds[c + 4], ds[c + 5]),
+                       pack_bf16(ds[c + 6], ds[c + 7]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (!ok) {
+      if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+    // final dK, dV (bf16) once the last gradient MMAs are done
+    if (ok && nq > 0 && mbar_wait(ds_empty, (nq - 1) & 1, abort_flag)) {
+      tc_fence_after();
+      if (key < a.S) {
+        const long grow = b * a.kv_rows_per_b + key;
+        __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) + grow * g.lddk + g.dk_col + h * 64;
+        __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) + grow * g.lddv + g.dv_col + h * 64;
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 32) {
+          uint32_t rk[32], rv[32];
+          tmem_ld32(trow + C_DK + c0, rk);
+          tmem_ld32(trow + C_DV + c0, rv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            st_global_v4(dkr + c0 + c,
+                         pack_bf16(__uint_as_float(rk[c]), __uint_as_float(rk[c + 1])),
+                         pack_bf16(__uint_as_float(rk[c + 2]), __uint_as_float(rk[c + 3])),
+                         pack_bf16(__uint_as_float(rk[c + 4]), __uint_as_float(rk[c + 5])),
+                         pack_bf16(__uint_as_float(rk[c + 6]), __uint_as_float(rk[c + 7])));
+            st_global_v4(dvr + c0 + c,
+                         pack_bf16(__uint_as_float(rv[c]), __uint_as_float(rv[c + 1])),
+                         pack_bf16(__uint_as_float(rv[c + 2]), __uint_as_float(rv[c + 3])),
+                         pack_bf16(__uint_as_float(rv[c + 4]), __uint_as_float(rv[c + 5])),
+                         pack_bf16(__uint_as_float(rv[c + 6]), __uint_as_float(rv[c + 7])));
+          }
+        }
+      }
+    } else if (nq == 0 && key < a.S) {
+      // keys nobody attends to get zero gradients
+      const long grow = b * a.kv_rows_per_b + key;
+      __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) + grow * g.lddk + g.dk_col + h * 64;
+      __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) + grow * g.lddv + g.dv_col + h * 64;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        st_global_v4(dkr + c, 0, 0, 0, 0);
+        st_global_v4(dvr + c, 0, 0, 0, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ reduction warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row within the tile
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    bool ok = true;
+    for (int j = 0; j < nq; ++j) {
+      if (!mbar_wait(dq_full, j & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q = qtile_of(j) * 128 + r;
+      uint32_t v0[32], v1[32];
+      tmem_ld32(trow + C_DQ, v0);
+      tmem_ld32(trow + C_DQ + 32, v1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (q < a.Tq) {
+        float* dst = g.dq_acc + (b * a.q_rows_per_b + q) * g.ld_dqacc + h * 64;
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          red_add_v4_f32(dst + c, __uint_as_float(v0[c]), __uint_as_float(v0[c + 1]),
+                         __uint_as_float(v0[c + 2]), __uint_as_float(v0[c + 3]));
+          red_add_v4_f32(dst + 32 + c, __uint_as_float(v1[c]), __uint_as_float(v1[c + 1]),
+                         __uint_as_float(v1[c + 2]), __uint_as_float(v1[c + 3]));
+        }
+      }
+    }
+    if (!ok) {
+      if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// delta[b,h,t] = sum over the head's 64 columns of dO * O (one warp per row)
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, long ldo, int o_col,
+                             const __nv_bfloat16* __restrict__ dout, long lddo, int do_col,
+                             float* __restrict__ delta, int B, int H, int Tq, long rows_per_b) {
+  const int lane = threadIdx.x & 31;
+  const long row = blockIdx.x * 8L + (threadIdx.x >> 5);
+  if (row >= static_cast<long>(B) * Tq) return;
+  const int b = static_cast<int>(row / Tq);
+  const int t = static_cast<int>(row % Tq);
+  const long grow = b * rows_per_b + t;
+  const int chunks = H * 8;
+  for (int base = 0; base < chunks; base += 32) {
+    const int c = base + lane;
+    float s = 0.f;
+    if (c < chunks) {
+      uint4 ov = ld_global_v4(o + grow * ldo + o_col + c * 8);
+      uint4 dv = ld_global_v4(dout + grow * lddo + do_col + c * 8);
+      uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+      uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 a = unpack_bf16(ow[j]);
+        float2 d = unpack_bf16(dw[j]);
+        s += a.x * d.x + a.y * d.y;
+      }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if ((lane & 7) == 0 && c < chunks) {
+      const int hh = c / 8;
+      delta[(static_cast<long>(b) * H + hh) * Tq + t] = s;
+    }
+  }
+}
+
+// dq (bf16) = dq_acc, rotated back by the rotary table when given
+__global__ void dq_finalize_kernel(const float* __restrict__ acc, long ld_acc,
+                                   __nv_bfloat16* __restrict__ dq, long lddq, int dq_col, int rows,
+                                   int H, const float2* __restrict__ tab, int rows_per_seq,
+                                   int pos_offset) {
+  const long idx = blockIdx.x * 256L + threadIdx.x;
+  const int chunks = H * 8;
+  if (idx >= static_cast<long>(rows) * chunks) return;
+  const int row = static_cast<int>(idx / chunks);
+  const int c = static_cast<int>(idx % chunks) * 8;
+  const float* src = acc + row * ld_acc + c;
+  float4 x0 = *reinterpret_cast<const float4*>(src);
+  float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+  float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  if (tab) {
+    const int pos = row % rows_per_seq + pos_offset;
+    const float2* t = tab + static_cast<long>(pos) * 32 + (c % 64) / 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 cs = __ldg(t + j);
+      const float a0 = v[2 * j], a1 = v[2 * j + 1];
+      v[2 * j] = a0 * cs.x + a1 * cs.y;
+      v[2 * j + 1] = -a0 * cs.y + a1 * cs.x;
+    }
+  }
+  st_global_v4(dq + row * lddq + dq_col + c, pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
+               pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+}
+
+}  // namespace
+
+void attn_bwd(const AttnBwdArgs& g, cudaStream_t stream) {
+  const AttnArgs& a = g.f;
+  if (a.B <= 0 || a.H <= 0 || a.S <= 0) return;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES),
+               "cudaFuncSetAttribute(attn_bwd)");
+    attr = true;
+  }
+  const long q_rows = a.B * a.q_rows_per_b;
+  const long kv_rows = a.B * a.kv_rows_per_b;
+  CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
+                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,
+                                a.ldk * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
+                                a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tDO = make_tmap_2d(g.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.lddo, q_rows,
+                                 g.lddo * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int n_kvtiles = (a.S + 127) / 128;
+  const int n_qtiles = (a.Tq + 127) / 128;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  attn_bwd_kernel<<<a.B * a.H * n_kvtiles, kThreads, SMEM_BYTES, stream>>>(
+      tQ, tK, tV, tDO, g, n_kvtiles, n_qtiles, device_status(dev));
+  count_launch();
+  check_cuda(cudaGetLastError(), "attn_bwd_kernel launch");
+}
+
+void attn_bwd_delta(const void* o, long ldo, int o_col, const void* dout, long lddo, int do_col,
+                    float* delta, int B, int H, int Tq, long rows_per_b, cudaStream_t s) {
+  const long rows = static_cast<long>(B) * Tq;
+  delta_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), ldo, o_col,
+      reinterpret_cast<const __nv_bfloat16*>(dout), lddo, do_col, delta, B, H, Tq, rows_per_b);
+  count_launch();
+}
+
+void attn_dq_finalize(const float* dq_acc, long ld_acc, void* dq, long lddq, int dq_col, int rows,
+                      int H, const float2* rope_tab, int rows_per_seq, int pos_offset,
+                      cudaStream_t s) {
+  const long n = static_cast<long>(rows) * H * 8;
+  dq_finalize_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, s>>>(
+      dq_acc, ld_acc, reinterpret_cast<__nv_bfloat16*>(dq), lddq, dq_col, rows, H, rope_tab,
+      rows_per_seq, pos_offset);
+  count_launch();
+}
+
+}  // namespace ddb

@@ -1,0 +1,407 @@
+// tcgen05 flash-attention forward, d_head = 64, for sm_100a.
+//
+// One CTA = one (batch, head, 128-query tile). Roles (192 threads, 2 CTAs per SM):
+//   warp 0     TMA: Q tile once (two 64-row boxes), then K/V tiles of 128 keys made of
+//              two independent 64-key blocks (so SLA can pair any two selected blocks)
+//              into a 2-stage ring.
+//   warp 1     TMEM owner + MMA issuer: S = Q K^T (M=128, N=128, K=64) into TMEM
+//              columns [0,128), O += P V (M=128, N=64, K=128) into columns [128,192).
+//   warps 2-5  softmax: one thread per query row reads its S row from TMEM, applies the
+//              mask, keeps the running max / sum (log2 domain), rescales its O row in
+//              TMEM when the max moves, writes P (bf16) to shared memory in the 128-byte
+//              swizzled K-major layout the PV MMA reads, and finally normalises O.
+// The S MMA of tile j+1 overlaps the softmax of tile j; the second resident CTA of the
+// SM overlaps the rest.
+//
+// Masks: frame-causal (all keys of frames <= the query's frame), token-causal, none;
+// KV-cache attention via absolute query/key position offsets; block-sparse SLA via a
+// per-tile list of 64-key block pairs with a 4-bit (query half x key half) mask.
+// Semantics oracle: layers/attention.py attention_reference (reference layers/mha.py:88-116
+// with fp32 softmax), layers/sla.py sla_sparse_reference.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <stdexcept>
+
+#include "../common/ptx.cuh"
+#include "../common/tma.h"
+#include "attn.h"
+
+namespace ddb {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int NS = 2;
+constexpr int TILE_BYTES = 16384;  // 128 rows x 64 bf16
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TILE_BYTES;
+constexpr int OFF_V = OFF_K + NS * TILE_BYTES;
+constexpr int OFF_P = OFF_V + NS * TILE_BYTES;
+constexpr int OFF_BAR = OFF_P + 2 * TILE_BYTES;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t S_COL = 0;
+constexpr uint32_t O_COL = 128;
+constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, false, false);
+constexpr uint32_t IDESC_PV = make_idesc_bf16(128, 64, false, true);
+
+__device__ __forceinline__ int row_limit(const AttnArgs& a, int q_local) {
+  int lim = a.S;
+  const int qa = a.q_pos_offset + q_local;
+  if (a.causal == kCausalFrame) {
+    lim = min(lim, (qa / a.tpf + 1) * a.tpf - a.kv_pos_offset);
+  } else if (a.causal == kCausalToken) {
+    lim = min(lim, qa + 1 - a.kv_pos_offset);
+  }
+  return max(lim, 0);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnArgs a, int n_qtiles,
+                    int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;       // NS
+  uint64_t* kv_empty = bars + 1 + NS; // NS
+  uint64_t* s_full = bars + 1 + 2 * NS;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = s_full + 3;
+  uint64_t* drain = s_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int item = blockIdx.x;
+  const int qt = n_qtiles - 1 - (item % n_qtiles);  // heavy (late) tiles first
+  const int bh = item / n_qtiles;
+  const int b = bh / a.H;
+  const int h = bh % a.H;
+  const int q0 = qt * 128;
+  const bool sparse = a.pair_count != nullptr;
+  const long list_idx = static_cast<long>(bh) * n_qtiles + qt;
+  int ntiles;
+  if (sparse) {
+    ntiles = a.pair_count[list_idx];
+  } else {
+    const int lim = row_limit(a, min(q0 + 127, a.Tq - 1));
+    ntiles = (lim + 127) / 128;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  uint8_t* sQ = smem + OFF_Q;
+  uint8_t* sP = smem + OFF_P;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int qrow = static_cast<int>(b * a.q_rows_per_b) + q0;
+      const int qcol = a.q_col + h * 64;
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(sQ, &tmQ, q_full, qcol, qrow);
+      tma_load_2d(sQ + 8192, &tmQ, q_full, qcol, qrow + 64);
+      const int krow0 = static_cast<int>(b * a.kv_rows_per_b);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % NS;
+        const uint32_t ph = (j / NS) & 1;
+        if (!mbar_wait(&kv_empty[s], ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        int b0 = 2 * j, b1 = 2 * j + 1;
+        if (sparse) {
+          const int packed = a.pair_blocks[list_idx * a.max_pairs + j];
+          b0 = packed & 0xffff;
+          b1 = (packed >> 16) & 0xffff;
+        }
+        uint8_t* sK = smem + OFF_K + s * TILE_BYTES;
+        uint8_t* sV = smem + OFF_V + s * TILE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
+        tma_load_2d(sK, &tmK, &kv_full[s], a.k_col + h * 64, krow0 + b0 * 64);
+        tma_load_2d(sK + 8192, &tmK, &kv_full[s], a.k_col + h * 64, krow0 + b1 * 64);
+        tma_load_2d(sV, &tmV, &kv_full[s], a.v_col + h * 64, krow0 + b0 * 64);
+        tma_load_2d(sV + 8192, &tmV, &kv_full[s], a.v_col + h * 64, krow0 + b1 * 64);
+        ++issued;
+      }
+      if (!ok) {
+        if (status) atomicCAS(status, 0, kStatusTimeoutProducer);
+        *abort_flag = 1;
+      }
+      // loads still in flight land before the CTA can retire (bounded)
+      long long t0 = clock64();
+      while (!mbar_try_wait(q_full, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
+      }
+      for (int j = max(0, issued - NS); j < issued; ++j) {
+        t0 = clock64();
+        while (!mbar_try_wait(&kv_full[j % NS], (j / NS) & 1) &&
+               clock64() - t0 < kSpinLimitCycles / 8) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      const uint32_t aQ = smem_u32(sQ);
+      const uint32_t aP = smem_u32(sP);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(p_full, i & 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t aV = smem_u32(smem + OFF_V + (i % NS) * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t da = make_sw128_desc(aP + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = make_sw128_desc(aV + kk * 2048, 8192, 1024);
+          mma_bf16_ss(tmem + O_COL, da, db, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&kv_empty[i % NS]);
+        mma_commit(o_done);
+        return true;
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int s = j % NS;
+        if (!mbar_wait(&kv_full[s], (j / NS) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t aK = smem_u32(smem + OFF_K + s * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16_ss(tmem + S_COL, make_sw128_desc(aQ + kk * 32, 16, 1024),
+                      make_sw128_desc(aK + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(s_full);
+        if (j > 0 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok && ntiles > 0) ok = issue_pv(ntiles - 1);
+      if (!ok) {
+        if (status) atomicCAS(status, 0, kStatusTimeoutMma);
+        *abort_flag = 1;
+      }
+      mma_commit(drain);
+      long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int q_local = q0 + r;
+    const bool row_ok = q_local < a.Tq;
+    const int lim = row_ok ? row_limit(a, q_local) : 0;
+    const int qhalf = r >> 6;
+    const float sl2 = a.scale * 1.4426950408889634f;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t pbase = smem_u32(sP) + r * 128;
+    const uint32_t swz = r & 7;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait(s_full, j & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sf[128];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(trow + S_COL + 0, r0);
+        tmem_ld32(trow + S_COL + 32, r1);
+        tmem_ld32(trow + S_COL + 64, r2);
+        tmem_ld32(trow + S_COL + 96, r3);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          sf[c] = __uint_as_float(r0[c]);
+          sf[32 + c] = __uint_as_float(r1[c]);
+          sf[64 + c] = __uint_as_float(r2[c]);
+          sf[96 + c] = __uint_as_float(r3[c]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      if (sparse) {
+        const int bits = a.pair_mask[list_idx * a.max_pairs + j];
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {
+          if (!((bits >> (qhalf * 2 + kh)) & 1)) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) sf[kh * 64 + c] = -INFINITY;
+          }
+        }
+        if (!row_ok) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) sf[c] = -INFINITY;
+        }
+      } else if (j * 128 + 128 > lim) {
+        const int base = j * 128;
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (base + c >= lim) sf[c] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, sf[c]);
+      const float m_new = fmaxf(m, mx * sl2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = exp2f(m - m_use);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float p = exp2f(sf[c] * sl2 - m_use);
+        sf[c] = p;
+        sum += p;
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 16) {
+            uint32_t ov[16];
+            tmem_ld16(trow + O_COL + c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st16(trow + O_COL + c, ov);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P (bf16) -> shared memory, 128-byte swizzle, two 64-key chunks
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c0 = ch * 64 + u * 8;
+          st_shared_v4(pbase + ch * TILE_BYTES + ((u ^ swz) << 4), pack_bf16(sf[c0], sf[c0 + 1]),
+                       pack_bf16(sf[c0 + 2], sf[c0 + 3]), pack_bf16(sf[c0 + 4], sf[c0 + 5]),
+                       pack_bf16(sf[c0 + 6], sf[c0 + 7]));
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (!ok) {
+      if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+    float ov[64];
+    if (ok && ntiles > 0 && mbar_wait(o_done, (ntiles - 1) & 1, abort_flag)) {
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      tmem_ld32(trow + O_COL, o0);
+      tmem_ld32(trow + O_COL + 32, o1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        ov[c] = __uint_as_float(o0[c]);
+        ov[32 + c] = __uint_as_float(o1[c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 64; ++c) ov[c] = 0.f;
+    }
+    if (row_ok) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o) +
+                            (b * a.q_rows_per_b + q_local) * a.ldo + a.o_col + h * 64;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8)
+        st_global_v4(orow + c, pack_bf16(ov[c] * inv, ov[c + 1] * inv),
+                     pack_bf16(ov[c + 2] * inv, ov[c + 3] * inv),
+                     pack_bf16(ov[c + 4] * inv, ov[c + 5] * inv),
+                     pack_bf16(ov[c + 6] * inv, ov[c + 7] * inv));
+      if (a.lse) a.lse[static_cast<long>(bh) * a.Tq + q_local] = l > 0.f ? m + __log2f(l) : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
+  if (a.B <= 0 || a.H <= 0 || a.Tq <= 0) return;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES),
+               "cudaFuncSetAttribute(attn_fwd)");
+    attr = true;
+  }
+  const long q_rows = a.B * a.q_rows_per_b;
+  const long kv_rows = a.B * a.kv_rows_per_b;
+  CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
+                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,
+                                a.ldk * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
+                                a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int n_qtiles = (a.Tq + 127) / 128;
+  const int grid = a.B * a.H * n_qtiles;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  attn_fwd_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tQ, tK, tV, a, n_qtiles,
+                                                          device_status(dev));
+  count_launch();
+  check_cuda(cudaGetLastError(), "attn_fwd_kernel launch");
+}
+
+}  // namespace ddb

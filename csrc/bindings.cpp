@@ -8,6 +8,7 @@
 #include "common/tma.h"
 #include "gemm/gemm.h"
 #include "fused/fused.h"
+#include "attn/attn.h"
 
 namespace {
 
@@ -254,6 +255,154 @@ void rope_rotate(torch::Tensor x, int64_t rot_cols, torch::Tensor tab, int64_t h
                         rows_per_seq, pos_offset, inverse, stream());
 }
 
+// ------------------------------------------------------------------ attention
+ddb::AttnArgs make_attn_args(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                             int64_t q_col, int64_t k_col, int64_t v_col, int64_t B, int64_t H,
+                             int64_t Tq, int64_t S, int64_t q_rows_per_b, int64_t kv_rows_per_b,
+                             int64_t causal, int64_t tpf, int64_t q_pos_offset,
+                             int64_t kv_pos_offset, double scale) {
+  for (auto* t : {&q, &k, &v}) {
+    check_bf16(*t, "q/k/v");
+    check_rows(*t, "q/k/v");
+  }
+  TORCH_CHECK(q.size(0) >= B * q_rows_per_b && k.size(0) >= B * kv_rows_per_b &&
+                  v.size(0) >= B * kv_rows_per_b,
+              "attention: tensors have fewer rows than B * rows_per_b");
+  TORCH_CHECK(q_col + H * 64 <= q.size(1) && k_col + H * 64 <= k.size(1) &&
+                  v_col + H * 64 <= v.size(1),
+              "attention: head columns out of range");
+  TORCH_CHECK(q_col % 8 == 0 && k_col % 8 == 0 && v_col % 8 == 0, "attention: column offsets");
+  TORCH_CHECK(tpf >= 1, "tokens per frame");
+  ddb::AttnArgs a;
+  a.B = B; a.H = H; a.Tq = Tq; a.S = S; a.q_rows_per_b = q_rows_per_b;
+  a.kv_rows_per_b = kv_rows_per_b;
+  a.q = q.data_ptr(); a.ldq = q.stride(0); a.q_col = q_col;
+  a.k = k.data_ptr(); a.ldk = k.stride(0); a.k_col = k_col;
+  a.v = v.data_ptr(); a.ldv = v.stride(0); a.v_col = v_col;
+  a.causal = causal; a.tpf = tpf; a.q_pos_offset = q_pos_offset;
+  a.kv_pos_offset = kv_pos_offset; a.scale = static_cast<float>(scale);
+  return a;
+}
+
+void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+              c10::optional<torch::Tensor> lse, int64_t q_col, int64_t k_col, int64_t v_col,
+              int64_t o_col, int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t q_rows_per_b,
+              int64_t kv_rows_per_b, int64_t causal, int64_t tpf, int64_t q_pos_offset,
+              int64_t kv_pos_offset, double scale, c10::optional<torch::Tensor> pair_blocks,
+              c10::optional<torch::Tensor> pair_mask, c10::optional<torch::Tensor> pair_count) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto a = make_attn_args(q, k, v, q_col, k_col, v_col, B, H, Tq, S, q_rows_per_b, kv_rows_per_b,
+                          causal, tpf, q_pos_offset, kv_pos_offset, scale);
+  check_bf16(o, "o");
+  check_rows(o, "o");
+  TORCH_CHECK(o.size(0) >= B * q_rows_per_b && o_col + H * 64 <= o.size(1), "o shape");
+  a.o = o.data_ptr(); a.ldo = o.stride(0); a.o_col = o_col;
+  if (lse) {
+    TORCH_CHECK(lse->scalar_type() == torch::kFloat32 && lse->is_contiguous() &&
+                    lse->numel() >= B * H * Tq, "lse must be fp32 [B, H, Tq]");
+    a.lse = lse->data_ptr<float>();
+  }
+  if (pair_count) {
+    TORCH_CHECK(pair_blocks && pair_mask, "sparse attention needs blocks, mask and count");
+    const int64_t nqt = (Tq + 127) / 128;
+    TORCH_CHECK(pair_count->scalar_type() == torch::kInt32 && pair_count->numel() == B * H * nqt,
+                "pair_count must be int32 [B*H*n_qtiles]");
+    TORCH_CHECK(pair_blocks->scalar_type() == torch::kInt32 && pair_blocks->dim() == 2 &&
+                    pair_blocks->size(0) == B * H * nqt && pair_blocks->is_contiguous(),
+                "pair_blocks must be int32 [B*H*n_qtiles, max_pairs]");
+    TORCH_CHECK(pair_mask->scalar_type() == torch::kUInt8 && pair_mask->sizes() == pair_blocks->sizes() &&
+                    pair_mask->is_contiguous(), "pair_mask must be uint8 like pair_blocks");
+    a.pair_blocks = pair_blocks->data_ptr<int>();
+    a.pair_mask = pair_mask->data_ptr<uint8_t>();
+    a.pair_count = pair_count->data_ptr<int>();
+    a.max_pairs = pair_blocks->size(1);
+  }
+  ddb::attn_fwd(a, stream());
+}
+
+void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+              torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dq_acc,
+              torch::Tensor dk, torch::Tensor dv, int64_t q_col, int64_t k_col, int64_t v_col,
+              int64_t o_col, int64_t do_col, int64_t dk_col, int64_t dv_col, int64_t B, int64_t H,
+              int64_t Tq, int64_t S, int64_t q_rows_per_b, int64_t kv_rows_per_b, int64_t causal,
+              int64_t tpf, int64_t q_pos_offset, int64_t kv_pos_offset, double scale,
+              c10::optional<torch::Tensor> kv_qtiles, c10::optional<torch::Tensor> kv_qmask,
+              c10::optional<torch::Tensor> kv_count) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  ddb::AttnBwdArgs g;
+  g.f = make_attn_args(q, k, v, q_col, k_col, v_col, B, H, Tq, S, q_rows_per_b, kv_rows_per_b,
+                       causal, tpf, q_pos_offset, kv_pos_offset, scale);
+  check_bf16(dout, "dout");
+  check_rows(dout, "dout");
+  TORCH_CHECK(dout.size(0) >= B * q_rows_per_b && do_col + H * 64 <= dout.size(1), "dout shape");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.numel() >= B * H * Tq, "lse");
+  TORCH_CHECK(delta.scalar_type() == torch::kFloat32 && delta.numel() >= B * H * Tq, "delta");
+  TORCH_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.dim() == 2 &&
+                  dq_acc.stride(1) == 1 && dq_acc.stride(0) % 4 == 0 &&
+                  dq_acc.size(0) >= B * q_rows_per_b && dq_acc.size(1) >= H * 64,
+              "dq_acc must be fp32 [rows, >= H*64]");
+  for (auto* t : {&dk, &dv}) {
+    check_bf16(*t, "dk/dv");
+    check_rows(*t, "dk/dv");
+    TORCH_CHECK(t->size(0) >= B * kv_rows_per_b, "dk/dv rows");
+  }
+  TORCH_CHECK(dk_col + H * 64 <= dk.size(1) && dv_col + H * 64 <= dv.size(1), "dk/dv columns");
+  g.f.lse = lse.data_ptr<float>();
+  g.f.o = o.data_ptr(); g.f.ldo = o.stride(0); g.f.o_col = o_col;
+  g.dout = dout.data_ptr(); g.lddo = dout.stride(0); g.do_col = do_col;
+  g.delta = delta.data_ptr<float>();
+  g.dq_acc = dq_acc.data_ptr<float>(); g.ld_dqacc = dq_acc.stride(0);
+  g.dk = dk.data_ptr(); g.lddk = dk.stride(0); g.dk_col = dk_col;
+  g.dv = dv.data_ptr(); g.lddv = dv.stride(0); g.dv_col = dv_col;
+  if (kv_count) {
+    TORCH_CHECK(kv_qtiles && kv_qmask, "sparse backward needs q-tile lists, masks and counts");
+    const int64_t nkt = (S + 127) / 128;
+    TORCH_CHECK(kv_count->scalar_type() == torch::kInt32 && kv_count->numel() == B * H * nkt,
+                "kv_count must be int32 [B*H*n_kvtiles]");
+    TORCH_CHECK(kv_qtiles->scalar_type() == torch::kInt32 && kv_qtiles->dim() == 2 &&
+                    kv_qtiles->size(0) == B * H * nkt && kv_qtiles->is_contiguous(), "kv_qtiles");
+    TORCH_CHECK(kv_qmask->scalar_type() == torch::kUInt8 && kv_qmask->sizes() == kv_qtiles->sizes() &&
+                    kv_qmask->is_contiguous(), "kv_qmask");
+    g.kv_qtiles = kv_qtiles->data_ptr<int>();
+    g.kv_qmask = kv_qmask->data_ptr<uint8_t>();
+    g.kv_count = kv_count->data_ptr<int>();
+    g.max_q = kv_qtiles->size(1);
+  }
+  ddb::attn_bwd(g, stream());
+}
+
+void attn_delta(torch::Tensor o, torch::Tensor dout, torch::Tensor delta, int64_t o_col,
+                int64_t do_col, int64_t B, int64_t H, int64_t Tq, int64_t rows_per_b) {
+  check_bf16(o, "o");
+  check_bf16(dout, "dout");
+  check_rows(o, "o");
+  check_rows(dout, "dout");
+  TORCH_CHECK(delta.scalar_type() == torch::kFloat32 && delta.numel() >= B * H * Tq, "delta");
+  const c10::cuda::CUDAGuard guard(o.device());
+  ddb::attn_bwd_delta(o.data_ptr(), o.stride(0), o_col, dout.data_ptr(), dout.stride(0), do_col,
+                      delta.data_ptr<float>(), B, H, Tq, rows_per_b, stream());
+}
+
+void attn_dq_finalize(torch::Tensor dq_acc, torch::Tensor dq, int64_t dq_col, int64_t H,
+                      c10::optional<torch::Tensor> rope_tab, int64_t rows_per_seq,
+                      int64_t pos_offset) {
+  TORCH_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.stride(1) == 1 &&
+                  dq_acc.stride(0) % 4 == 0, "dq_acc");
+  check_bf16(dq, "dq");
+  check_rows(dq, "dq");
+  TORCH_CHECK(dq.size(0) == dq_acc.size(0) && dq_col + H * 64 <= dq.size(1), "dq shape");
+  const float2* tab = nullptr;
+  if (rope_tab) {
+    TORCH_CHECK(rope_tab->scalar_type() == torch::kFloat32 && rope_tab->is_contiguous() &&
+                    rope_tab->numel() >= (pos_offset + std::min<int64_t>(rows_per_seq, dq.size(0))) * 64,
+                "rope table");
+    tab = reinterpret_cast<const float2*>(rope_tab->data_ptr<float>());
+  }
+  const c10::cuda::CUDAGuard guard(dq.device());
+  ddb::attn_dq_finalize(dq_acc.data_ptr<float>(), dq_acc.stride(0), dq.data_ptr(), dq.stride(0),
+                        dq_col, dq.size(0), H, tab, rows_per_seq, pos_offset, stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -268,4 +417,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cast_bf16", &cast_bf16, "fp32 -> bf16 cast");
   m.def("sq_norm", &sq_norm, "sum of squares (fp32)");
   m.def("rope_rotate", &rope_rotate, "in-place rotary rotation of leading columns");
+  m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention forward (dense / frame-causal / sparse)");
+  m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)");
+  m.def("attn_delta", &attn_delta, "rowsum(dO * O) per head");
+  m.def("attn_dq_finalize", &attn_dq_finalize, "fp32 dq accumulator -> bf16 (+ inverse rope)");
 }
