@@ -64,6 +64,7 @@ struct AttnBwdArgs {
 };
 
 void attn_bwd(const AttnBwdArgs& a, cudaStream_t s);
+void attn_bwd_with_status(const AttnBwdArgs& a, int* status, cudaStream_t s);
 
 // delta[b,h,t] = sum_d dO * O over each head's 64 columns
 void attn_bwd_delta(const void* o, long ldo, int o_col, const void* dout, long lddo,

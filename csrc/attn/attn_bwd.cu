@@ -542,3 +542,33 @@ void attn_dq_finalize(const float* dq_acc, long ld_acc, void* dq, long lddq, int
 }
 
 }  // namespace ddb
+
+namespace ddb {
+
+// The attn_bwd launch with the bounded-wait status word supplied by the caller instead
+// of the per-device word (whose first use allocates it).
+void attn_bwd_with_status(const AttnBwdArgs& g, int* status, cudaStream_t stream) {
+  const AttnArgs& a = g.f;
+  if (a.B <= 0 || a.H <= 0 || a.S <= 0) return;
+  check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES),
+             "cudaFuncSetAttribute(attn_bwd)");
+  const long q_rows = a.B * a.q_rows_per_b;
+  const long kv_rows = a.B * a.kv_rows_per_b;
+  CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
+                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,
+                                a.ldk * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
+                                a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tDO = make_tmap_2d(g.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.lddo, q_rows,
+                                 g.lddo * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int n_kvtiles = (a.S + 127) / 128;
+  const int n_qtiles = (a.Tq + 127) / 128;
+  attn_bwd_kernel<<<a.B * a.H * n_kvtiles, kThreads, SMEM_BYTES, stream>>>(
+      tQ, tK, tV, tDO, g, n_kvtiles, n_qtiles, status);
+  count_launch();
+  check_cuda(cudaGetLastError(), "attn_bwd_kernel launch");
+}
+
+}  // namespace ddb
