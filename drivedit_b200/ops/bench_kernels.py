@@ -71,13 +71,58 @@ def bench_gemm(iters: int = 20):
         del a, b, out, kw
 
 
+def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512):
+    """Frame-causal flash attention fwd and bwd at the DiT-B training shape."""
+    import math
+
+    from ._ext import ext
+
+    d = H * 64
+    qkv = (torch.randn(B * T, 3 * d, device="cuda") * 0.5).bfloat16()
+    o = torch.empty(B * T, d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H * T, device="cuda")
+    do = torch.randn(B * T, d, device="cuda").bfloat16()
+    delta = torch.empty(B * H * T, device="cuda")
+    dq_acc = torch.zeros(B * T, d, device="cuda")
+    dqkv = torch.empty(B * T, 3 * d, device="cuda", dtype=torch.bfloat16)
+    sc = 1 / 8.0
+
+    def fwd():
+        ext().attn_fwd(qkv, qkv, qkv, o, lse, 0, d, 2 * d, 0, B, H, T, T, T, T, 1, tpf, 0, 0, sc,
+                       None, None, None)
+
+    def bwd():
+        ext().attn_delta(o, do, delta, 0, 0, B, H, T, T)
+        dq_acc.zero_()
+        ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d,
+                       2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, sc, None, None, None)
+        ext().attn_dq_finalize(dq_acc, dqkv, 0, H, None, T, 0)
+
+    fwd()
+    # visible (query, key) pairs under frame-causal masking
+    frames = T // tpf
+    pairs = B * H * tpf * tpf * frames * (frames + 1) / 2
+    f_fwd = 4.0 * pairs * 64
+    f_bwd = 10.0 * pairs * 64
+    ms_f = _timeit(fwd, iters)
+    ms_b = _timeit(bwd, iters)
+    print(json.dumps({"kernel": "attn_fwd", "B": B, "H": H, "T": T, "tpf": tpf, "ms": round(ms_f, 3),
+                      "tflops": round(f_fwd / ms_f / 1e9, 1)}), flush=True)
+    print(json.dumps({"kernel": "attn_bwd", "B": B, "H": H, "T": T, "tpf": tpf, "ms": round(ms_b, 3),
+                      "tflops": round(f_bwd / ms_b / 1e9, 1)}), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("what", nargs="*", default=["gemm"])
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--small", action="store_true", help="small attention case (for ncu)")
     args = p.parse_args()
     for w in args.what:
-        {"gemm": bench_gemm}[w](args.iters) if w == "gemm" else globals()[f"bench_{w}"](args.iters)
+        if w == "attn" and args.small:
+            bench_attn(args.iters, B=1, H=2, T=8192)
+        else:
+            globals()[f"bench_{w}"](args.iters)
     from ._ext import check_device_status
 
     check_device_status()
