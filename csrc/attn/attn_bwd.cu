@@ -35,11 +35,13 @@ constexpr int OFF_K = 0;
 constexpr int OFF_V = OFF_K + TILE;
 constexpr int OFF_Q = OFF_V + TILE;            // NS stages
 constexpr int OFF_DO = OFF_Q + NS * TILE;      // NS stages
-constexpr int OFF_PT = OFF_DO + NS * TILE;     // 2 chunks
-constexpr int OFF_DST = OFF_PT + 2 * TILE;     // 2 chunks
-constexpr int OFF_VEC = OFF_DST + 2 * TILE;    // lse[128], delta[128], lim[128]
-constexpr int OFF_BAR = OFF_VEC + 3 * 512;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int OFF_PT = OFF_DO + NS * TILE;     // 2 buffers x 2 chunks
+constexpr int OFF_DST = OFF_PT + 4 * TILE;     // 2 buffers x 2 chunks
+constexpr int OFF_VEC = OFF_DST + 4 * TILE;    // per stage: lse[128], delta[128]
+constexpr int OFF_BAR = OFF_VEC + NS * 1024;
+// no alignment slack: the dynamic shared window of a CTA without static shared memory
+// starts 1024-byte aligned; the kernel checks this and reports a status code otherwise.
+constexpr int SMEM_BYTES = OFF_BAR + 128;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
 constexpr uint32_t IDESC_SS = make_idesc_bf16(128, 128, false, false);
@@ -84,25 +86,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmDO, const AttnBwdArgs g, int n_kvtiles,
                     int n_qtiles, int* status) {
   const AttnArgs& a = g.f;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;            // NS
   uint64_t* qd_empty = bars + 1 + NS;      // NS
   uint64_t* s_full = bars + 1 + 2 * NS;
   uint64_t* s_free = s_full + 1;
-  uint64_t* ds_full = s_full + 2;
-  uint64_t* ds_empty = s_full + 3;
-  uint64_t* dq_full = s_full + 4;
-  uint64_t* dq_free = s_full + 5;
-  uint64_t* drain = s_full + 6;
+  uint64_t* ds_full = s_full + 2;   // 2 buffers
+  uint64_t* ds_empty = s_full + 4;  // 2 buffers
+  uint64_t* dq_full = s_full + 6;
+  uint64_t* dq_free = s_full + 7;
+  uint64_t* drain = s_full + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_lse = reinterpret_cast<float*>(smem + OFF_VEC);
-  float* s_delta = s_lse + 128;
-  int* s_lim = reinterpret_cast<int*>(s_delta + 128);
+  if ((smem_u32(smem_raw) & 1023) != 0) {
+    if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadArgument);
+    return;
+  }
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -134,8 +136,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 4);
-    mbar_init(ds_full, 4);
-    mbar_init(ds_empty, 1);
+    mbar_init(&ds_full[0], 4);
+    mbar_init(&ds_full[1], 4);
+    mbar_init(&ds_empty[0], 1);
+    mbar_init(&ds_empty[1], 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
     mbar_init(drain, 1);
@@ -172,14 +176,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const int qrow = static_cast<int>(b * a.q_rows_per_b) + qtile_of(j) * 128;
+        const int qt = qtile_of(j);
+        const int qrow = static_cast<int>(b * a.q_rows_per_b) + qt * 128;
         uint8_t* sq = smem + OFF_Q + s * TILE;
         uint8_t* sd = smem + OFF_DO + s * TILE;
-        mbar_arrive_expect_tx(&qd_full[s], 2 * TILE);
+        uint8_t* sv = smem + OFF_VEC + s * 1024;
+        const long vi = static_cast<long>(bh) * a.Tq + qt * 128;  // Tq % 128 == 0
+        mbar_arrive_expect_tx(&qd_full[s], 2 * TILE + 1024);
         tma_load_2d(sq, &tmQ, &qd_full[s], a.q_col + h * 64, qrow);
         tma_load_2d(sq + 8192, &tmQ, &qd_full[s], a.q_col + h * 64, qrow + 64);
         tma_load_2d(sd, &tmDO, &qd_full[s], g.do_col + h * 64, qrow);
         tma_load_2d(sd + 8192, &tmDO, &qd_full[s], g.do_col + h * 64, qrow + 64);
+        bulk_load(sv, a.lse + vi, 512, &qd_full[s]);
+        bulk_load(sv + 512, g.delta + vi, 512, &qd_full[s]);
         ++issued;
       }
       if (!ok) {
@@ -202,10 +211,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(kv_full, 0, abort_flag);
       const uint32_t aK = smem_u32(smem + OFF_K);
       const uint32_t aV = smem_u32(smem + OFF_V);
-      const uint32_t aPT = smem_u32(smem + OFF_PT);
-      const uint32_t aDST = smem_u32(smem + OFF_DST);
       auto issue_grads = [&](int i) -> bool {
-        if (!mbar_wait(ds_full, i & 1, abort_flag)) return false;
+        const int pb = i & 1;  // P^T / dS^T buffer
+        const uint32_t aPT = smem_u32(smem + OFF_PT + pb * 2 * TILE);
+        const uint32_t aDST = smem_u32(smem + OFF_DST + pb * 2 * TILE);
+        if (!mbar_wait(&ds_full[pb], (i >> 1) & 1, abort_flag)) return false;
         if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, abort_flag)) return false;
         tc_fence_after();
         const int s = i % NS;
@@ -230,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       make_sw128_desc(aK + kk * 2048, 8192, 1024), IDESC_DQ, kk > 0 ? 1u : 0u);
         }
         mma_commit(&qd_empty[s]);
-        mma_commit(ds_empty);
+        mma_commit(&ds_empty[pb]);
         mma_commit(dq_full);
         return true;
       };
@@ -268,39 +278,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ softmax / dS warps
     const int quad = warp & 3;
     const int r = quad * 32 + lane;   // key row within the tile
-    const int t = (warp - 2) * 32 + lane;  // 0..127 for shared-vector loads
     const int key = k0 + r;
     const int khalf = r >> 6;
     const float sl2 = a.scale * 1.4426950408889634f;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t swz = r & 7;
-    const uint32_t pt_base = smem_u32(smem + OFF_PT) + r * 128;
-    const uint32_t ds_base = smem_u32(smem + OFF_DST) + r * 128;
     bool ok = true;
     for (int j = 0; j < nq; ++j) {
-      const int qt = qtile_of(j);
-      const int q0 = qt * 128;
-      // per-query vectors for this tile
-      named_bar(1, 128);
-      {
-        const int q = q0 + t;
-        const bool valid = q < a.Tq;
-        const long vi = static_cast<long>(bh) * a.Tq + q;
-        s_lse[t] = valid ? a.lse[vi] : INFINITY;
-        s_delta[t] = valid ? g.delta[vi] : 0.f;
-        s_lim[t] = valid ? row_limit(a, q) : 0;
-      }
-      named_bar(1, 128);
+      const int s = j % NS;
+      const int pb = j & 1;
+      const int q0 = qtile_of(j) * 128;
+      const float* s_lse = reinterpret_cast<const float*>(smem + OFF_VEC + s * 1024);
+      const float* s_delta = s_lse + 128;
       const int bits = sparse ? g.kv_qmask[list_idx * g.max_q + j] : 0xF;
-      if (!mbar_wait(s_full, j & 1, abort_flag)) {
+      // element masks are needed only where some query of the tile cannot see some key
+      // of the tile (key limits are non-decreasing in the query index)
+      const bool need_mask = !sparse && row_limit(a, q0) < k0 + 128;
+      if (!mbar_wait(s_full, j & 1, abort_flag) ||
+          !mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
+          !mbar_wait(&ds_empty[pb], ((j >> 1) & 1) ^ 1, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (j > 0 && !mbar_wait(ds_empty, (j - 1) & 1, abort_flag)) {
-        ok = false;
-        break;
-      }
+      const uint32_t pt_base = smem_u32(smem + OFF_PT + pb * 2 * TILE) + r * 128;
+      const uint32_t ds_base = smem_u32(smem + OFF_DST + pb * 2 * TILE) + r * 128;
 #pragma unroll 1
       for (int c0 = 0; c0 < 128; c0 += 32) {
         uint32_t rs[32], rp[32];
@@ -312,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int qi = c0 + c;
-          const bool vis = half_on && key < s_lim[qi];
+          const bool vis = half_on && (!need_mask || key < row_limit(a, q0 + qi));
           const float pv = vis ? exp2f(__uint_as_float(rs[c]) * sl2 - s_lse[qi]) : 0.f;
           p[c] = pv;
           ds[c] = pv * (__uint_as_float(rp[c]) - s_delta[qi]) * a.scale;
@@ -335,14 +337,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(s_free);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_full);
+      if (lane == 0) mbar_arrive(&ds_full[pb]);
     }
     if (!ok) {
       if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
       *abort_flag = 1;
     }
     // final dK, dV (bf16) once the last gradient MMAs are done
-    if (ok && nq > 0 && mbar_wait(ds_empty, (nq - 1) & 1, abort_flag)) {
+    if (ok && nq > 0 && mbar_wait(&ds_empty[(nq - 1) & 1], ((nq - 1) >> 1) & 1, abort_flag)) {
       tc_fence_after();
       if (key < a.S) {
         const long grow = b * a.kv_rows_per_b + key;
@@ -495,6 +497,7 @@ __global__ void dq_finalize_kernel(const float* __restrict__ acc, long ld_acc,
 void attn_bwd(const AttnBwdArgs& g, cudaStream_t stream) {
   const AttnArgs& a = g.f;
   if (a.B <= 0 || a.H <= 0 || a.S <= 0) return;
+  if (a.Tq % 128 != 0) throw std::runtime_error("attn_bwd: queries per sample must be a multiple of 128");
   static bool attr = false;
   if (!attr) {
     check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -550,6 +553,7 @@ namespace ddb {
 void attn_bwd_with_status(const AttnBwdArgs& g, int* status, cudaStream_t stream) {
   const AttnArgs& a = g.f;
   if (a.B <= 0 || a.H <= 0 || a.S <= 0) return;
+  if (a.Tq % 128 != 0) throw std::runtime_error("attn_bwd: queries per sample must be a multiple of 128");
   check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES),
              "cudaFuncSetAttribute(attn_bwd)");

@@ -9,6 +9,7 @@
 #include "gemm/gemm.h"
 #include "fused/fused.h"
 #include "attn/attn.h"
+#include "attn/sla.h"
 
 namespace {
 
@@ -403,6 +404,131 @@ void attn_dq_finalize(torch::Tensor dq_acc, torch::Tensor dq, int64_t dq_col, in
                         dq_col, dq.size(0), H, tab, rows_per_seq, pos_offset, stream());
 }
 
+// ------------------------------------------------------------------ batched GEMM
+// D[b] = A[b] B[b]^T for 3-D bf16 A, B (row-major per batch); D is [batch * M, N].
+void gemm_batched(torch::Tensor A, torch::Tensor B, torch::Tensor D, int64_t epi, bool a_t,
+                  bool b_t) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3 && A.size(0) == B.size(0), "gemm_batched: 3-D A, B");
+  TORCH_CHECK(A.stride(2) == 1 && B.stride(2) == 1, "gemm_batched: unit inner stride");
+  TORCH_CHECK((A.stride(1) * 2) % 16 == 0 && (B.stride(1) * 2) % 16 == 0, "gemm_batched: row strides");
+  check_rows(D, "D");
+  const c10::cuda::CUDAGuard guard(A.device());
+  ddb::GemmArgs a;
+  a.batch = A.size(0);
+  a.a_mn_major = a_t;
+  a.b_mn_major = b_t;
+  a.M = a_t ? A.size(2) : A.size(1);
+  a.K = a_t ? A.size(1) : A.size(2);
+  a.N = b_t ? B.size(2) : B.size(1);
+  TORCH_CHECK((b_t ? B.size(1) : B.size(2)) == a.K, "gemm_batched: inner dimensions differ");
+  a.A = A.data_ptr(); a.lda = A.stride(1); a.stride_a = A.stride(0);
+  a.B = B.data_ptr(); a.ldb = B.stride(1); a.stride_b = B.stride(0);
+  a.D = D.data_ptr(); a.ldd = D.stride(0);
+  TORCH_CHECK(D.size(0) == static_cast<int64_t>(a.batch) * a.M && D.size(1) >= a.N, "gemm_batched: D shape");
+  const bool f32_out = (epi == ddb::kEpiF32 || epi == ddb::kEpiF32Atomic);
+  TORCH_CHECK(D.scalar_type() == (f32_out ? torch::kFloat32 : torch::kBFloat16), "gemm_batched: D dtype");
+  TORCH_CHECK(epi == ddb::kEpiF32 || epi == ddb::kEpiBf16, "gemm_batched: plain epilogues only");
+  ddb::gemm(a, static_cast<int>(epi), stream());
+}
+
+// ------------------------------------------------------------------ SLA
+void sla_pool(torch::Tensor qkv, torch::Tensor qm, torch::Tensor km, int64_t B, int64_t T, int64_t H) {
+  check_bf16(qkv, "qkv");
+  check_rows(qkv, "qkv");
+  TORCH_CHECK(T % 64 == 0 && qkv.size(0) == B * T && qkv.size(1) >= 3 * H * 64, "sla_pool: qkv shape");
+  TORCH_CHECK(qm.scalar_type() == torch::kFloat32 && qm.is_contiguous() && qm.numel() == B * H * T, "qm");
+  TORCH_CHECK(km.scalar_type() == torch::kFloat32 && km.is_contiguous() && km.numel() == B * H * T, "km");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  ddb::sla_pool(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), B, T, H,
+                qm.data_ptr<float>(), km.data_ptr<float>(), stream());
+}
+
+void sla_route(torch::Tensor qm, torch::Tensor km, int64_t BH, int64_t nb, int64_t topk,
+               int64_t causal, int64_t bpf, bool always_diag, torch::Tensor wlin,
+               torch::Tensor pair_blocks, torch::Tensor pair_mask, torch::Tensor pair_count,
+               torch::Tensor kv_qtiles, torch::Tensor kv_qmask, torch::Tensor kv_count,
+               c10::optional<torch::Tensor> sel_bits) {
+  TORCH_CHECK(nb % 2 == 0 && nb <= 256 && nb >= 2, "sla_route: even number of blocks <= 256");
+  TORCH_CHECK(qm.numel() == BH * nb * 64 && km.numel() == BH * nb * 64, "sla_route: qm/km");
+  check_bf16(wlin, "wlin");
+  TORCH_CHECK(wlin.numel() == BH * nb * nb && wlin.is_contiguous(), "wlin");
+  const int64_t nt = nb / 2;
+  TORCH_CHECK(pair_blocks.scalar_type() == torch::kInt32 && pair_blocks.size(0) == BH * nt &&
+                  pair_blocks.is_contiguous(), "pair_blocks");
+  TORCH_CHECK(pair_mask.scalar_type() == torch::kUInt8 && pair_mask.sizes() == pair_blocks.sizes(), "pair_mask");
+  TORCH_CHECK(pair_count.scalar_type() == torch::kInt32 && pair_count.numel() == BH * nt, "pair_count");
+  TORCH_CHECK(kv_qtiles.scalar_type() == torch::kInt32 && kv_qtiles.numel() == BH * nt * nt, "kv_qtiles");
+  TORCH_CHECK(kv_qmask.scalar_type() == torch::kUInt8 && kv_qmask.numel() == BH * nt * nt, "kv_qmask");
+  TORCH_CHECK(kv_count.scalar_type() == torch::kInt32 && kv_count.numel() == BH * nt, "kv_count");
+  const c10::cuda::CUDAGuard guard(qm.device());
+  ddb::SlaRouteArgs a;
+  a.qm = qm.data_ptr<float>(); a.km = km.data_ptr<float>();
+  a.nb = nb; a.topk = topk; a.causal = causal; a.bpf = bpf; a.always_diag = always_diag;
+  a.wlin = reinterpret_cast<__nv_bfloat16*>(wlin.data_ptr());
+  a.pair_blocks = pair_blocks.data_ptr<int>(); a.pair_mask = pair_mask.data_ptr<uint8_t>();
+  a.pair_count = pair_count.data_ptr<int>(); a.max_pairs = pair_blocks.size(1);
+  a.kv_qtiles = kv_qtiles.data_ptr<int>(); a.kv_qmask = kv_qmask.data_ptr<uint8_t>();
+  a.kv_count = kv_count.data_ptr<int>();
+  if (sel_bits) {
+    TORCH_CHECK(sel_bits->numel() == BH * nb * ((nb + 31) / 32), "sel_bits");
+    a.sel_bits = reinterpret_cast<uint32_t*>(sel_bits->data_ptr<int>());
+  }
+  ddb::sla_route(a, BH, stream());
+}
+
+void sla_kv_state(torch::Tensor qkv, torch::Tensor kvz, int64_t B, int64_t T, int64_t H) {
+  check_bf16(qkv, "qkv");
+  check_rows(qkv, "qkv");
+  check_bf16(kvz, "kvz");
+  TORCH_CHECK(kvz.is_contiguous() && kvz.numel() == B * H * (T / 64) * 4160, "kvz");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  ddb::sla_kv_state(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), B, T, H,
+                    reinterpret_cast<__nv_bfloat16*>(kvz.data_ptr()), stream());
+}
+
+void sla_lin_out(torch::Tensor qkv, torch::Tensor state, torch::Tensor o, torch::Tensor den,
+                 int64_t B, int64_t T, int64_t H, double eps) {
+  check_bf16(qkv, "qkv");
+  check_bf16(o, "o");
+  check_rows(o, "o");
+  TORCH_CHECK(state.scalar_type() == torch::kFloat32 && state.is_contiguous() &&
+                  state.numel() == B * H * (T / 64) * 4160, "state");
+  TORCH_CHECK(den.scalar_type() == torch::kFloat32 && den.numel() == B * H * T, "den");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  ddb::sla_lin_out(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), B, T, H,
+                   state.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), o.stride(0),
+                   den.data_ptr<float>(), static_cast<float>(eps), stream());
+}
+
+void sla_lin_bwd_q(torch::Tensor qkv, torch::Tensor state, torch::Tensor o, torch::Tensor dout,
+                   torch::Tensor den, torch::Tensor dsz, torch::Tensor dqkv, int64_t B, int64_t T,
+                   int64_t H) {
+  for (auto* t : {&qkv, &o, &dout, &dqkv}) check_bf16(*t, "bf16 operand");
+  check_bf16(dsz, "dsz");
+  TORCH_CHECK(dsz.is_contiguous() && dsz.numel() == B * H * (T / 64) * 4160, "dsz");
+  TORCH_CHECK(state.scalar_type() == torch::kFloat32 && state.numel() == B * H * (T / 64) * 4160, "state");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  ddb::sla_lin_bwd_q(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), B, T, H,
+                     state.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
+                     o.stride(0), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                     dout.stride(0), den.data_ptr<float>(),
+                     reinterpret_cast<__nv_bfloat16*>(dsz.data_ptr()),
+                     reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dqkv.stride(0), stream());
+}
+
+void sla_lin_bwd_kv(torch::Tensor qkv, torch::Tensor dkvz, torch::Tensor dqkv, int64_t B, int64_t T,
+                    int64_t H) {
+  check_bf16(qkv, "qkv");
+  check_bf16(dqkv, "dqkv");
+  TORCH_CHECK(dkvz.scalar_type() == torch::kFloat32 && dkvz.numel() == B * H * (T / 64) * 4160, "dkvz");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  ddb::sla_lin_bwd_kv(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), B, T, H,
+                      dkvz.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
+                      dqkv.stride(0), stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -420,5 +546,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention forward (dense / frame-causal / sparse)");
   m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)");
   m.def("attn_delta", &attn_delta, "rowsum(dO * O) per head");
+  m.def("gemm_batched", &gemm_batched, "strided-batched tcgen05 GEMM");
+  m.def("sla_pool", &sla_pool, "SLA block means of q, k");
+  m.def("sla_route", &sla_route, "SLA top-k routing + kernel lists");
+  m.def("sla_kv_state", &sla_kv_state, "SLA per-block linear states");
+  m.def("sla_lin_out", &sla_lin_out, "SLA linear-branch output");
+  m.def("sla_lin_bwd_q", &sla_lin_bwd_q, "SLA linear-branch backward (query side)");
+  m.def("sla_lin_bwd_kv", &sla_lin_bwd_kv, "SLA linear-branch backward (key side)");
   m.def("attn_dq_finalize", &attn_dq_finalize, "fp32 dq accumulator -> bf16 (+ inverse rope)");
 }

@@ -44,12 +44,16 @@ struct GemmCfg {
 };
 
 struct Sched {
-  int tiles_m, tiles_n, kblocks, kb_per_split, splits, total;
-  __device__ __forceinline__ void decode(int t, int& m0, int& n0, int& kb0, int& kb1) const {
+  int tiles_m, tiles_n, kblocks, kb_per_split, splits, total, M;
+  // tile t -> (batch bt, row m0, column tile n0, k-block range); n fastest
+  __device__ __forceinline__ void decode(int t, int& m0, int& n0, int& kb0, int& kb1,
+                                         int& bt) const {
     int n_idx = t % tiles_n;
     t /= tiles_n;
     int m_idx = t % tiles_m;
-    int split = t / tiles_m;
+    t /= tiles_m;
+    int split = t % splits;
+    bt = t / splits;
     m0 = m_idx * BM;
     n0 = n_idx;  // scaled by BN by the caller
     kb0 = split * kb_per_split;
@@ -280,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
-        int m0, nt, kb0, kb1;
-        sched.decode(t, m0, nt, kb0, kb1);
+        int m0, nt, kb0, kb1, bt;
+        sched.decode(t, m0, nt, kb0, kb1, bt);
         const int n0 = nt * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
@@ -292,17 +296,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           if constexpr (A_MN) {
-            tma_load_2d(sa, &tmA, &full[stage], m0, kb * BK);
-            tma_load_2d(sa + 8192, &tmA, &full[stage], m0 + 64, kb * BK);
+            tma_load_3d(sa, &tmA, &full[stage], m0, kb * BK, bt);
+            tma_load_3d(sa + 8192, &tmA, &full[stage], m0 + 64, kb * BK, bt);
           } else {
-            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+            tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, bt);
           }
           if constexpr (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_2d(sb + c * 8192, &tmB, &full[stage], n0 + c * 64, kb * BK);
+              tma_load_3d(sb + c * 8192, &tmB, &full[stage], n0 + c * 64, kb * BK, bt);
           } else {
-            tma_load_2d(sb, &tmB, &full[stage], kb * BK, n0);
+            tma_load_3d(sb, &tmB, &full[stage], kb * BK, n0, bt);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -337,8 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool any = false;
       for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
-        int m0, nt, kb0, kb1;
-        sched.decode(t, m0, nt, kb0, kb1);
+        int m0, nt, kb0, kb1, bt;
+        sched.decode(t, m0, nt, kb0, kb1, bt);
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort_flag)) {
           ok = false;
           break;
@@ -394,8 +398,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int buf = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
-      int m0, nt, kb0, kb1;
-      sched.decode(t, m0, nt, kb0, kb1);
+      int m0, nt, kb0, kb1, bt;
+      sched.decode(t, m0, nt, kb0, kb1, bt);
       const int n0 = nt * BN;
       if (!mbar_wait(&acc_full[buf], acc_phase, abort_flag)) {
         if (lane == 0) record_status(status, kStatusTimeoutEpilogue);
@@ -403,7 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int row = m0 + row_in_tile;
+      // batches are stacked row-wise in D (and C): global row = bt * M + row
+      const bool row_ok = m0 + row_in_tile < args.M;
+      const int row = bt * args.M + m0 + row_in_tile;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
       if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll 1
@@ -412,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tbase + c, rg);
           tmem_ld32(tbase + c + 32, ru);
           tmem_wait_ld();
-          if (row < args.M && n0 + c < args.N) epi_swiglu(args, row, n0 + c, rg, ru);
+          if (row_ok && n0 + c < args.N) epi_swiglu(args, row, n0 + c, rg, ru);
         }
       } else {
 #pragma unroll 1
@@ -420,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_wait_ld();
-          if (row < args.M && n0 + c < args.N) {
+          if (row_ok && n0 + c < args.N) {
             if constexpr (EPI == kEpiDSwiGLU)
               epi_dswiglu(args, row, n0 + c, r);
             else
@@ -459,18 +465,20 @@ void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, in
     attr_set = true;
   }
   CUtensorMap tA, tB;
+  const long sa = a.batch > 1 ? a.stride_a : (A_MN ? a.lda * a.K : a.lda * a.M);
+  const long sb = a.batch > 1 ? a.stride_b : (B_MN ? a.ldb * a.K : a.ldb * a.N);
   if (A_MN)
-    tA = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.lda * 2, 64, 64,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+    tA = make_tmap_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.batch, a.lda * 2,
+                      sa * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   else
-    tA = make_tmap_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda * 2, 64, BM,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+    tA = make_tmap_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.batch, a.lda * 2,
+                      sa * 2, 64, BM, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (B_MN)
-    tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb * 2, 64, 64,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+    tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.batch, a.ldb * 2,
+                      sb * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   else
-    tB = make_tmap_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.ldb * 2, 64, BN,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+    tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.batch, a.ldb * 2,
+                      sb * 2, 64, BN, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status);
   count_launch();
   check_cuda(cudaGetLastError(), "gemm_tc_kernel launch");
@@ -546,7 +554,10 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   }
   s.kb_per_split = (s.kblocks + splits - 1) / splits;
   s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
-  s.total = s.tiles_m * s.tiles_n * s.splits;
+  s.M = a.M;
+  s.total = s.tiles_m * s.tiles_n * s.splits * (a.batch > 1 ? a.batch : 1);
+  if (a.batch > 1 && (a.stride_a % 8 != 0 || a.stride_b % 8 != 0))
+    throw std::runtime_error("gemm: batch strides must be multiples of 8 elements");
   int grid = s.total < sms ? s.total : sms;
   if (a.max_ctas > 0 && grid > a.max_ctas) grid = a.max_ctas;
   int* status = device_status(dev);

@@ -40,6 +40,9 @@ struct GemmArgs {
   const void* gate = nullptr;
   long ldg = 0;
   int gate_rows_per_group = 1;
+  int batch = 1;            // strided batch: A, B advance by stride_a / stride_b elements,
+  long stride_a = 0;        // D (and C) by M rows (batches stacked row-wise)
+  long stride_b = 0;
   int splits = 1;           // split-K factor (kEpiF32Atomic only)
   int bn = 0;               // 0 = auto (128 or 256)
   int max_ctas = 0;         // 0 = all SMs

@@ -101,6 +101,72 @@ def sla_plan(q, k, B, T, H, cfg, tpf: Optional[int], causal: str) -> SLAPlan:
     return SLAPlan(sel, valid, pair_blocks, pair_mask, pair_count, kv_qtiles, kv_qmask, kv_count)
 
 
+class SLAKernelPlan:
+    """Routing outputs of the ``sla_route`` kernel plus the linear-branch state."""
+
+    def __init__(self, wlin, pair_blocks, pair_mask, pair_count, kv_qtiles, kv_qmask, kv_count):
+        self.wlin = wlin
+        self.pair_blocks, self.pair_mask, self.pair_count = pair_blocks, pair_mask, pair_count
+        self.kv_qtiles, self.kv_qmask, self.kv_count = kv_qtiles, kv_qmask, kv_count
+        self.state = None
+        self.den = None
+
+
+def sla_plan_kernel(qkv: torch.Tensor, B: int, T: int, H: int, cfg, tpf: int, causal: str,
+                    sel_bits: bool = False) -> SLAKernelPlan:
+    """Routing on the device: block means, scores, top-k, lists (``csrc/attn/sla.cu``)."""
+    assert cfg.block_size == 64 and T % 128 == 0
+    nb = T // 64
+    nt = nb // 2
+    dev = qkv.device
+    qm = torch.empty(B * H * T, device=dev, dtype=torch.float32)
+    km = torch.empty(B * H * T, device=dev, dtype=torch.float32)
+    ext().sla_pool(qkv, qm, km, B, T, H)
+    kk = min(n_selected(nb, cfg.topk_frac), nb)
+    max_pairs = max(1, kk)
+    BH = B * H
+    wlin = torch.empty(BH, nb, nb, device=dev, dtype=torch.bfloat16)
+    pb = torch.empty(BH * nt, max_pairs, device=dev, dtype=torch.int32)
+    pm = torch.empty(BH * nt, max_pairs, device=dev, dtype=torch.uint8)
+    pc = torch.empty(BH * nt, device=dev, dtype=torch.int32)
+    kq = torch.empty(BH * nt, nt, device=dev, dtype=torch.int32)
+    km_ = torch.empty(BH * nt, nt, device=dev, dtype=torch.uint8)
+    kc = torch.empty(BH * nt, device=dev, dtype=torch.int32)
+    code = {"none": 0, "frame": 1, "token": 2}[causal]
+    bpf = max(1, tpf // 64) if causal == "frame" else 1
+    sb = torch.empty(BH * nb * ((nb + 31) // 32), device=dev, dtype=torch.int32) if sel_bits else None
+    ext().sla_route(qm, km, BH, nb, kk, code, bpf, bool(cfg.always_diag), wlin, pb, pm, pc, kq,
+                    km_, kc, sb)
+    plan = SLAKernelPlan(wlin, pb, pm, pc, kq, km_, kc)
+    plan.sel_bits = sb
+    return plan
+
+
+def sla_linear_fwd_kernel(qkv, plan: SLAKernelPlan, B, T, H, eps=1e-6):
+    nb = T // 64
+    d = H * 64
+    dev = qkv.device
+    kvz = torch.empty(B * H, nb, 4160, device=dev, dtype=torch.bfloat16)
+    ext().sla_kv_state(qkv, kvz, B, T, H)
+    state = torch.empty(B * H * nb, 4160, device=dev, dtype=torch.float32)
+    ext().gemm_batched(plan.wlin, kvz, state, 1, False, True)
+    o_lin = torch.empty(B * T, d, device=dev, dtype=torch.bfloat16)
+    den = torch.empty(B * H * T, device=dev, dtype=torch.float32)
+    ext().sla_lin_out(qkv, state, o_lin, den, B, T, H, eps)
+    plan.state, plan.den = state, den
+    return o_lin
+
+
+def sla_linear_bwd_kernel(qkv, o_lin, do_lin, plan: SLAKernelPlan, dqkv, B, T, H):
+    nb = T // 64
+    dev = qkv.device
+    dsz = torch.empty(B * H, nb, 4160, device=dev, dtype=torch.bfloat16)
+    ext().sla_lin_bwd_q(qkv, plan.state, o_lin, do_lin, plan.den, dsz, dqkv, B, T, H)
+    dkvz = torch.empty(B * H * nb, 4160, device=dev, dtype=torch.float32)
+    ext().gemm_batched(plan.wlin, dsz, dkvz, 1, True, True)
+    ext().sla_lin_bwd_kv(qkv, dkvz, dqkv, B, T, H)
+
+
 def _heads(qkv, bc):
     B, T, H = bc.B, bc.T, bc.H
     v = qkv.view(B, T, 3, H, 64)
@@ -119,11 +185,10 @@ def attention_fwd_kernel(qkv: torch.Tensor, bc):
     o_lin = None
     lists = (None, None, None)
     if bc.attn_mode == "sla":
-        q, k, v = _heads(qkv, bc)
-        plan = sla_plan(q, k, B, T, H, bc.sla_cfg, bc.tpf, bc.causal)
+        plan = sla_plan_kernel(qkv, B, T, H, bc.sla_cfg, bc.tpf, bc.causal)
         lists = (plan.pair_blocks, plan.pair_mask, plan.pair_count)
-        lin = plan.valid[None, None] & ~plan.sel
-        o_lin = sla_linear_reference(q, k, v, lin, 64).to(torch.bfloat16).reshape(M, d)
+        o_lin = sla_linear_fwd_kernel(qkv, plan, B, T, H)
+        plan.o_lin = o_lin
     ext().attn_fwd(qkv, qkv, qkv, o, lse, 0, d, 2 * d, 0, B, H, T, T, T, T, causal, bc.tpf,
                    0, 0, scale, *lists)
     return o, o_lin, lse, plan
@@ -145,13 +210,7 @@ def attention_bwd_kernel(qkv, o, lse, do, do_lin, plan, bc):
                    1.0 / math.sqrt(bc.Dh), *lists)
     ext().attn_dq_finalize(dq_acc, dqkv, 0, H, None, T, 0)
     if plan is not None and do_lin is not None:
-        q, k, v = (t.detach().float().requires_grad_(True) for t in _heads(qkv, bc))
-        lin = plan.valid[None, None] & ~plan.sel
-        with torch.enable_grad():
-            ol = sla_linear_reference(q, k, v, lin, 64)
-            gq, gk, gv = torch.autograd.grad(ol, (q, k, v), do_lin.view(B, T, H, 64).float())
-        g = torch.stack([gq, gk, gv], 2).reshape(M, 3 * d)
-        dqkv = (dqkv.float() + g).to(torch.bfloat16)
+        sla_linear_bwd_kernel(qkv, plan.o_lin, do_lin, plan, dqkv, B, T, H)
     return dqkv
 
 
