@@ -61,6 +61,7 @@ struct AttnBwdArgs {
   const uint8_t* kv_qmask = nullptr; // 4 bits: (q half)*2 + (key half)
   const int* kv_count = nullptr;
   int max_q = 0;
+  int debug_flags = 0;        // bit 0: skip the dQ reductions (timing experiments only)
 };
 
 void attn_bwd(const AttnBwdArgs& a, cudaStream_t s);

@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      if (q < a.Tq) {
+      if (q < a.Tq && !(g.debug_flags & 1)) {
         float* dst = g.dq_acc + (b * a.q_rows_per_b + q) * g.ld_dqacc + h * 64;
 #pragma unroll
         for (int c = 0; c < 32; c += 4) {

@@ -10,6 +10,7 @@
 #include "fused/fused.h"
 #include "attn/attn.h"
 #include "attn/sla.h"
+#include "comm/comm.h"
 
 namespace {
 
@@ -328,9 +329,10 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
               int64_t Tq, int64_t S, int64_t q_rows_per_b, int64_t kv_rows_per_b, int64_t causal,
               int64_t tpf, int64_t q_pos_offset, int64_t kv_pos_offset, double scale,
               c10::optional<torch::Tensor> kv_qtiles, c10::optional<torch::Tensor> kv_qmask,
-              c10::optional<torch::Tensor> kv_count) {
+              c10::optional<torch::Tensor> kv_count, int64_t debug_flags) {
   const c10::cuda::CUDAGuard guard(q.device());
   ddb::AttnBwdArgs g;
+  g.debug_flags = debug_flags;
   g.f = make_attn_args(q, k, v, q_col, k_col, v_col, B, H, Tq, S, q_rows_per_b, kv_rows_per_b,
                        causal, tpf, q_pos_offset, kv_pos_offset, scale);
   check_bf16(dout, "dout");
@@ -529,6 +531,72 @@ void sla_lin_bwd_kv(torch::Tensor qkv, torch::Tensor dkvz, torch::Tensor dqkv, i
                       dqkv.stride(0), stream());
 }
 
+// ------------------------------------------------------------------ peer memory
+py::tuple ipc_alloc(int64_t bytes) {
+  auto a = ddb::ipc_alloc(static_cast<size_t>(bytes));
+  return py::make_tuple(reinterpret_cast<int64_t>(a.ptr), py::bytes(a.handle));
+}
+int64_t ipc_open(py::bytes handle) {
+  return reinterpret_cast<int64_t>(ddb::ipc_open(std::string(handle)));
+}
+void ipc_close(int64_t p) { ddb::ipc_close(reinterpret_cast<void*>(p)); }
+void ipc_free(int64_t p) { ddb::ipc_free(reinterpret_cast<void*>(p)); }
+
+// A tensor viewing `numel` elements at a device pointer this extension owns (no copy).
+torch::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, torch::Dtype dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel}, [](void*) {}, opts);
+}
+
+void xrank_barrier(torch::Tensor peer_table, int64_t local_ptr, int64_t rank, int64_t world,
+                   int64_t epoch, c10::optional<torch::Tensor> payload) {
+  TORCH_CHECK(peer_table.is_cuda() && peer_table.scalar_type() == torch::kInt64 &&
+                  peer_table.numel() == world, "peer table must be int64 [world] on the device");
+  const float* pay = nullptr;
+  if (payload) {
+    TORCH_CHECK(payload->scalar_type() == torch::kFloat32 && payload->is_cuda(), "payload");
+    pay = payload->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(peer_table.device());
+  int dev = peer_table.device().index();
+  ddb::xrank_barrier(reinterpret_cast<void* const*>(peer_table.data_ptr<int64_t>()),
+                     reinterpret_cast<void*>(local_ptr), rank, world, static_cast<uint32_t>(epoch),
+                     pay, ddb::device_status(dev), stream());
+}
+
+void rs_sum_sqnorm(torch::Tensor grad_table, int64_t world, int64_t off, int64_t len,
+                   torch::Tensor red, torch::Tensor sumsq) {
+  TORCH_CHECK(grad_table.scalar_type() == torch::kInt64 && grad_table.numel() == world, "grad table");
+  TORCH_CHECK(red.scalar_type() == torch::kFloat32 && red.numel() >= len && red.is_contiguous(), "red");
+  TORCH_CHECK(sumsq.scalar_type() == torch::kFloat32 && sumsq.numel() >= 1, "sumsq");
+  const c10::cuda::CUDAGuard guard(red.device());
+  ddb::rs_sum_sqnorm(reinterpret_cast<const float* const*>(grad_table.data_ptr<int64_t>()), world, off,
+                     len, red.data_ptr<float>(), sumsq.data_ptr<float>(), stream());
+}
+
+void shard_adamw_allgather(torch::Tensor red, torch::Tensor master_local, torch::Tensor m,
+                           torch::Tensor v, torch::Tensor master_table, torch::Tensor compute_table,
+                           int64_t world, int64_t off, int64_t len, int64_t decay_end,
+                           c10::optional<torch::Tensor> norm_payloads, double max_norm, double lr,
+                           double b1, double b2, double eps, double wd, double bc1, double bc2,
+                           double grad_scale) {
+  for (auto* t : {&red, &m, &v})
+    TORCH_CHECK(t->scalar_type() == torch::kFloat32 && t->numel() >= len && t->is_contiguous(), "shard buffers");
+  TORCH_CHECK(master_local.scalar_type() == torch::kFloat32 && master_local.numel() >= off + len, "master");
+  TORCH_CHECK(master_table.numel() == world && compute_table.numel() == world, "peer tables");
+  const c10::cuda::CUDAGuard guard(red.device());
+  ddb::ShardAdamWArgs a;
+  a.red = red.data_ptr<float>(); a.master_local = master_local.data_ptr<float>();
+  a.m = m.data_ptr<float>(); a.v = v.data_ptr<float>();
+  a.peer_master = reinterpret_cast<float* const*>(master_table.data_ptr<int64_t>());
+  a.peer_compute = reinterpret_cast<__nv_bfloat16* const*>(compute_table.data_ptr<int64_t>());
+  a.world = world; a.off = off; a.len = len; a.decay_end = decay_end;
+  if (norm_payloads) a.norm_payloads = norm_payloads->data_ptr<float>();
+  a.max_norm = max_norm; a.lr = lr; a.b1 = b1; a.b2 = b2; a.eps = eps; a.wd = wd;
+  a.bc1 = bc1; a.bc2 = bc2; a.grad_scale = grad_scale;
+  ddb::shard_adamw_allgather(a, stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -546,6 +614,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention forward (dense / frame-causal / sparse)");
   m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)");
   m.def("attn_delta", &attn_delta, "rowsum(dO * O) per head");
+  m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + IPC handle -> (ptr, handle)");
+  m.def("ipc_open", &ipc_open, "open a peer's IPC handle -> ptr");
+  m.def("ipc_close", &ipc_close, "close a peer mapping");
+  m.def("ipc_free", &ipc_free, "free a local IPC buffer");
+  m.def("tensor_from_ptr", &tensor_from_ptr, "tensor view of a device pointer");
+  m.def("xrank_barrier", &xrank_barrier, "bounded cross-rank flag barrier over peer memory");
+  m.def("rs_sum_sqnorm", &rs_sum_sqnorm, "reduce-scatter by peer loads + squared norm");
+  m.def("shard_adamw_allgather", &shard_adamw_allgather, "sharded AdamW + all-gather by peer stores");
   m.def("gemm_batched", &gemm_batched, "strided-batched tcgen05 GEMM");
   m.def("sla_pool", &sla_pool, "SLA block means of q, k");
   m.def("sla_route", &sla_route, "SLA top-k routing + kernel lists");

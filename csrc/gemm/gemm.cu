@@ -498,6 +498,7 @@ void dispatch_bn(const GemmArgs& a, int epi, const Sched& s, int grid, cudaStrea
     DDB_CASE(kEpiDSwiGLU)
     case kEpiF32:
       if (mode == 0) return launch<BN, false, false, kEpiF32>(a, s, grid, st, status);
+      if (mode == 1) return launch<BN, false, true, kEpiF32>(a, s, grid, st, status);
       if (mode == 3) return launch<BN, true, true, kEpiF32>(a, s, grid, st, status);
       break;
     case kEpiF32Atomic:

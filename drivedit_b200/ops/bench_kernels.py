@@ -71,7 +71,8 @@ def bench_gemm(iters: int = 20):
         del a, b, out, kw
 
 
-def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512):
+def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512,
+               dbg: int = 0):
     """Frame-causal flash attention fwd and bwd at the DiT-B training shape."""
     import math
 
@@ -95,7 +96,7 @@ def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int
         ext().attn_delta(o, do, delta, 0, 0, B, H, T, T)
         dq_acc.zero_()
         ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d,
-                       2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, sc, None, None, None)
+                       2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, sc, None, None, None, dbg)
         ext().attn_dq_finalize(dq_acc, dqkv, 0, H, None, T, 0)
 
     fwd()
@@ -109,7 +110,7 @@ def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int
     print(json.dumps({"kernel": "attn_fwd", "B": B, "H": H, "T": T, "tpf": tpf, "ms": round(ms_f, 3),
                       "tflops": round(f_fwd / ms_f / 1e9, 1)}), flush=True)
     print(json.dumps({"kernel": "attn_bwd", "B": B, "H": H, "T": T, "tpf": tpf, "ms": round(ms_b, 3),
-                      "tflops": round(f_bwd / ms_b / 1e9, 1)}), flush=True)
+                      "tflops": round(f_bwd / ms_b / 1e9, 1), "debug_flags": dbg}), flush=True)
 
 
 def main():
@@ -121,6 +122,8 @@ def main():
     for w in args.what:
         if w == "attn" and args.small:
             bench_attn(args.iters, B=1, H=2, T=8192)
+        elif w == "attn_nodq":  # timing experiment: backward without the dQ reductions
+            bench_attn(args.iters, dbg=1)
         else:
             globals()[f"bench_{w}"](args.iters)
     from ._ext import check_device_status

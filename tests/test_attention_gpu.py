@@ -55,7 +55,7 @@ def test_flash_fwd_bwd_dense(causal, T, tpf):
     dq_acc = torch.zeros(B * T, d, device="cuda")
     dqkv = torch.zeros(B * T, 3 * d, device="cuda", dtype=torch.bfloat16)
     ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d,
-                   2 * d, B, H, T, T, T, T, CAUSAL[causal], tpf, 0, 0, 1 / 8.0, None, None, None)
+                   2 * d, B, H, T, T, T, T, CAUSAL[causal], tpf, 0, 0, 1 / 8.0, None, None, None, 0)
     ext().attn_dq_finalize(dq_acc, dqkv, 0, H, None, T, 0)
     g = dqkv.view(B, T, 3, H, D)
     assert _rel(g[:, :, 0], q.grad) < 3e-2
@@ -102,7 +102,7 @@ def test_sla_sparse_fwd_bwd_matches_masked_reference():
     dqkv = torch.zeros(B * T, 3 * d, device="cuda", dtype=torch.bfloat16)
     ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d, 2 * d,
                    B, H, T, T, T, T, 1, tpf, 0, 0, 1 / 8.0, plan.kv_qtiles, plan.kv_qmask,
-                   plan.kv_count)
+                   plan.kv_count, 0)
     ext().attn_dq_finalize(dq_acc, dqkv, 0, H, None, T, 0)
     g = dqkv.view(B, T, 3, H, D)
     assert _rel(g[:, :, 0], q.grad) < 3e-2

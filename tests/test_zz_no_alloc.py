@@ -69,7 +69,7 @@ def test_noalloc_backward_matches_regular_entry_point_twice():
         dq_acc = torch.zeros(B * T, d, device="cuda")
         ref = torch.zeros(B * T, 3 * d, device="cuda", dtype=torch.bfloat16)
         ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, ref, ref, 0, d, 2 * d, 0, 0, d,
-                       2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, scale, None, None, None)
+                       2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, scale, None, None, None, 0)
         ext().attn_dq_finalize(dq_acc, ref, 0, H, None, T, 0)
         # allocation-free entry point
         out = torch.full((B * T, 3 * d), float("nan"), device="cuda", dtype=torch.bfloat16)
