@@ -62,6 +62,8 @@ struct AttnBwdArgs {
   const int* kv_count = nullptr;
   int max_q = 0;
   int debug_flags = 0;        // bit 0: skip the dQ reductions (timing experiments only)
+  long long* trace = nullptr; // optional per-role clock64 trace of CTA `trace_cta`
+  int trace_cta = 0;
 };
 
 void attn_bwd(const AttnBwdArgs& a, cudaStream_t s);

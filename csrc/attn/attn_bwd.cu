@@ -79,6 +79,13 @@ __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// trace slot: [role (0 producer, 1 mma, 2 softmax, 3 dq)][event < 8][pair < 64]
+#define DDB_TRACE(role, ev, j)                                                      \
+  do {                                                                              \
+    if (g.trace && blockIdx.x == g.trace_cta && (j) < 64)                           \
+      g.trace[((role) * 8 + (ev)) * 64 + (j)] = clock64();                          \
+  } while (0)
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
@@ -176,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        DDB_TRACE(0, 0, j);
         const int qt = qtile_of(j);
         const int qrow = static_cast<int>(b * a.q_rows_per_b) + qt * 128;
         uint8_t* sq = smem + OFF_Q + s * TILE;
@@ -216,7 +224,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t aPT = smem_u32(smem + OFF_PT + pb * 2 * TILE);
         const uint32_t aDST = smem_u32(smem + OFF_DST + pb * 2 * TILE);
         if (!mbar_wait(&ds_full[pb], (i >> 1) & 1, abort_flag)) return false;
+        DDB_TRACE(1, 3, i);
         if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, abort_flag)) return false;
+        DDB_TRACE(1, 4, i);
         tc_fence_after();
         const int s = i % NS;
         const uint32_t aQ = smem_u32(smem + OFF_Q + s * TILE);
@@ -242,15 +252,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&qd_empty[s]);
         mma_commit(&ds_empty[pb]);
         mma_commit(dq_full);
+        DDB_TRACE(1, 5, i);
         return true;
       };
       for (int j = 0; j < nq && ok; ++j) {
         const int s = j % NS;
-        if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
-            (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag))) {
+        if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag)) {
           ok = false;
           break;
         }
+        DDB_TRACE(1, 0, j);
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        DDB_TRACE(1, 1, j);
         tc_fence_after();
         const uint32_t aQ = smem_u32(smem + OFF_Q + s * TILE);
         const uint32_t aDO = smem_u32(smem + OFF_DO + s * TILE);
@@ -262,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       make_sw128_desc(aDO + kk * 32, 16, 1024), IDESC_SS, kk > 0 ? 1u : 0u);
         }
         mma_commit(s_full);
+        DDB_TRACE(1, 2, j);
         if (j > 0 && !issue_grads(j - 1)) ok = false;
       }
       if (ok && nq > 0) ok = issue_grads(nq - 1);
@@ -294,12 +311,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // element masks are needed only where some query of the tile cannot see some key
       // of the tile (key limits are non-decreasing in the query index)
       const bool need_mask = !sparse && row_limit(a, q0) < k0 + 128;
-      if (!mbar_wait(s_full, j & 1, abort_flag) ||
-          !mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
+      if (!mbar_wait(s_full, j & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (warp == 2 && lane == 0) DDB_TRACE(2, 0, j);
+      if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
           !mbar_wait(&ds_empty[pb], ((j >> 1) & 1) ^ 1, abort_flag)) {
         ok = false;
         break;
       }
+      if (warp == 2 && lane == 0) DDB_TRACE(2, 1, j);
       tc_fence_after();
       const uint32_t pt_base = smem_u32(smem + OFF_PT + pb * 2 * TILE) + r * 128;
       const uint32_t ds_base = smem_u32(smem + OFF_DST + pb * 2 * TILE) + r * 128;
@@ -332,6 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        pack_bf16(ds[c + 6], ds[c + 7]));
         }
       }
+      if (warp == 2 && lane == 0) DDB_TRACE(2, 2, j);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
@@ -393,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
+      if (warp == 6 && lane == 0) DDB_TRACE(3, 0, j);
       tc_fence_after();
       const int q = qtile_of(j) * 128 + r;
       uint32_t v0[32], v1[32];

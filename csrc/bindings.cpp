@@ -329,10 +329,16 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
               int64_t Tq, int64_t S, int64_t q_rows_per_b, int64_t kv_rows_per_b, int64_t causal,
               int64_t tpf, int64_t q_pos_offset, int64_t kv_pos_offset, double scale,
               c10::optional<torch::Tensor> kv_qtiles, c10::optional<torch::Tensor> kv_qmask,
-              c10::optional<torch::Tensor> kv_count, int64_t debug_flags) {
+              c10::optional<torch::Tensor> kv_count, int64_t debug_flags,
+              c10::optional<torch::Tensor> trace, int64_t trace_cta) {
   const c10::cuda::CUDAGuard guard(q.device());
   ddb::AttnBwdArgs g;
   g.debug_flags = debug_flags;
+  if (trace) {
+    TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->numel() >= 4 * 8 * 64, "trace");
+    g.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+    g.trace_cta = trace_cta;
+  }
   g.f = make_attn_args(q, k, v, q_col, k_col, v_col, B, H, Tq, S, q_rows_per_b, kv_rows_per_b,
                        causal, tpf, q_pos_offset, kv_pos_offset, scale);
   check_bf16(dout, "dout");
@@ -612,7 +618,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sq_norm", &sq_norm, "sum of squares (fp32)");
   m.def("rope_rotate", &rope_rotate, "in-place rotary rotation of leading columns");
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention forward (dense / frame-causal / sparse)");
-  m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)");
+  m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"), py::arg("lse"),
+        py::arg("delta"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("q_col"),
+        py::arg("k_col"), py::arg("v_col"), py::arg("o_col"), py::arg("do_col"), py::arg("dk_col"),
+        py::arg("dv_col"), py::arg("B"), py::arg("H"), py::arg("Tq"), py::arg("S"),
+        py::arg("q_rows_per_b"), py::arg("kv_rows_per_b"), py::arg("causal"), py::arg("tpf"),
+        py::arg("q_pos_offset"), py::arg("kv_pos_offset"), py::arg("scale"), py::arg("kv_qtiles"),
+        py::arg("kv_qmask"), py::arg("kv_count"), py::arg("debug_flags") = 0,
+        py::arg("trace") = py::none(), py::arg("trace_cta") = 0);
   m.def("attn_delta", &attn_delta, "rowsum(dO * O) per head");
   m.def("ipc_alloc", &ipc_alloc, "cudaMalloc + IPC handle -> (ptr, handle)");
   m.def("ipc_open", &ipc_open, "open a peer's IPC handle -> ptr");

@@ -204,7 +204,7 @@ def attention_bwd_kernel(qkv, o, lse, do, do_lin, plan, bc):
     dqkv = torch.empty(M, 3 * d, device=dev, dtype=torch.bfloat16)
     lists = (None, None, None)
     if plan is not None:
-        lists = (plan.kv_qtiles, plan.kv_qmask, plan.kv_count, 0)
+        lists = (plan.kv_qtiles, plan.kv_qmask, plan.kv_count)
     ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d,
                    2 * d, B, H, T, T, T, T, CAUSAL[bc.causal], bc.tpf, 0, 0,
                    1.0 / math.sqrt(bc.Dh), *lists, 0)

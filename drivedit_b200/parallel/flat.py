@@ -30,7 +30,9 @@ def _round(n: int, a: int) -> int:
 class FlatParamGroup:
     def __init__(self, named_params: Iterable[Tuple[str, nn.Parameter]], device=None,
                  no_decay: Optional[Iterable[str]] = None, pad_to: int = 1,
-                 compute_dtype: torch.dtype = torch.bfloat16):
+                 compute_dtype: torch.dtype = torch.bfloat16, allocator=None):
+        """``allocator(kind, numel, dtype)`` may supply the ``master`` / ``grad`` /
+        ``compute`` buffers (e.g. in peer-mapped memory); they must be zero-filled."""
         named = list(named_params)
         nd = set(no_decay or [])
         decay = [(n, p) for n, p in named if n not in nd]
@@ -52,9 +54,11 @@ class FlatParamGroup:
         self.numel = _round(off, ALIGN * max(pad_to, 1))
         dev = device if device is not None else (self.params[0].device if self.params else "cpu")
         self.device = torch.device(dev)
-        self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=self.device)
+        if allocator is None:
+            allocator = lambda kind, n, dt: torch.zeros(n, dtype=dt, device=self.device)
+        self.master = allocator("master", self.numel, torch.float32)
+        self.grad = allocator("grad", self.numel, torch.float32)
+        self.compute = allocator("compute", self.numel, compute_dtype)
         with torch.no_grad():
             for n, p in zip(self.names, self.params):
                 o, k = self.offsets[n]

@@ -1,0 +1,199 @@
+"""Sharded data parallelism for the world models (FSDP's communication pattern).
+
+Every rank holds the full bf16 compute weights (what the forward/backward kernels read),
+the full fp32 master copy (what the PyTorch-side conditioning modules read) and a full
+fp32 gradient buffer the backward accumulates into; the AdamW moments and the update
+itself are sharded ``1/world``. One optimizer step is
+
+    reduce-scatter(grad) -> clip by the global norm -> AdamW(shard) -> all-gather(weights)
+
+which is FSDP's SHARD_GRAD_OP schedule (reference ``training/cuda_optimized.py:571-615``)
+with weights kept gathered between steps, because HBM is not the constraint at these
+model sizes (DiT-B: 0.5 GB of fp32 master per rank).
+
+Two transports:
+
+``fused`` (default on CUDA)
+    The flat buffers live in CUDA-IPC memory mapped by every rank. The reduce-scatter is
+    the optimizer's own read of its shard from every peer's gradient buffer, and the
+    all-gather is the optimizer's store of the updated fp32/bf16 shard into every peer's
+    buffers (``csrc/comm/comm.cu``); bounded cross-rank flag barriers order the phases
+    and carry the squared-norm partials for clipping.
+``nccl``
+    ``reduce_scatter_tensor`` + local AdamW on the shard + ``all_gather_into_tensor``
+    (the baseline; on CPU the same calls run over gloo, which the multi-process tests use).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .flat import ALIGN, FlatParamGroup
+
+
+class SymmetricBuffer:
+    """An equally sized CUDA-IPC buffer on every rank with a device table of peer pointers."""
+
+    def __init__(self, nbytes: int, group, device: torch.device):
+        from ..ops._ext import ext
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.nbytes = nbytes
+        ptr, handle = ext().ipc_alloc(nbytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptr = ptr
+        self.peers = [ptr if r == self.rank else ext().ipc_open(handles[r])
+                      for r in range(self.world)]
+        self.table = torch.tensor(self.peers, dtype=torch.int64, device=device)
+        self.device = device
+
+    def tensor(self, numel: int, dtype: torch.dtype, byte_offset: int = 0) -> torch.Tensor:
+        from ..ops._ext import ext
+
+        return ext().tensor_from_ptr(self.ptr + byte_offset, numel, dtype, self.device.index)
+
+    def peer_table(self, byte_offset: int = 0) -> torch.Tensor:
+        return self.table + byte_offset
+
+    def close(self):
+        from ..ops._ext import ext
+
+        torch.cuda.synchronize(self.device)
+        for r, p in enumerate(self.peers):
+            if r != self.rank:
+                ext().ipc_close(p)
+        ext().ipc_free(self.ptr)
+        self.peers = []
+
+
+class ShardedDataParallel:
+    """Owns the flat buffers of a model and performs the sharded optimizer step."""
+
+    def __init__(self, model: nn.Module, group=None, device=None, transport: Optional[str] = None,
+                 lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, grad_clip=1.0):
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.device = torch.device(device) if device is not None else next(model.parameters()).device
+        self.transport = transport or ("fused" if self.device.type == "cuda" else "nccl")
+        self.lr, self.betas, self.eps, self.wd, self.grad_clip = lr, tuple(betas), eps, weight_decay, grad_clip
+        named = list(model.named_parameters())
+        no_decay = model.no_decay_names() if hasattr(model, "no_decay_names") else []
+        pad = ALIGN * self.world * 4
+        self.sym = {}
+        alloc = None
+        if self.transport == "fused":
+            numel = _padded_numel(named, no_decay, pad)
+            bufs = {}
+            for name, dt, es in (("master", torch.float32, 4), ("grad", torch.float32, 4),
+                                 ("compute", torch.bfloat16, 2)):
+                bufs[name] = SymmetricBuffer(numel * es, self.group, self.device)
+            self.sym = bufs
+            self.flags = SymmetricBuffer(8 * self.world + 64, self.group, self.device)
+
+            def alloc(name, n, dtype):
+                return bufs[name].tensor(n, dtype)
+        self.flat = FlatParamGroup(named, self.device, no_decay=no_decay, pad_to=self.world * 4,
+                                   allocator=alloc)
+        n = self.flat.numel
+        assert n % (self.world * 4) == 0
+        self.shard_len = n // self.world
+        self.shard_off = self.rank * self.shard_len
+        self.m = torch.zeros(self.shard_len, device=self.device)
+        self.v = torch.zeros(self.shard_len, device=self.device)
+        self.red = torch.zeros(self.shard_len, device=self.device)
+        self.sumsq = torch.zeros(1, device=self.device)
+        self.step_count = 0
+        self.epoch = 0
+        self.last_grad_norm: Optional[torch.Tensor] = None
+        # identical starting weights everywhere
+        dist.broadcast(self.flat.master, src=0, group=self.group)
+        self.flat.refresh_compute()
+        if self.transport == "fused":
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+
+    # ------------------------------------------------------------------ step
+    def zero_grad(self):
+        self.flat.zero_grad()
+
+    def step(self):
+        self.step_count += 1
+        b1, b2 = self.betas
+        bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
+        scale = 1.0 / self.world  # gradients are summed over ranks; the loss is a mean
+        if self.transport == "fused":
+            self._step_fused(bc1, bc2, scale)
+        else:
+            self._step_collective(bc1, bc2, scale)
+
+    def _barrier(self, payload=None):
+        from ..ops._ext import ext
+
+        self.epoch += 1
+        ext().xrank_barrier(self.flags.table, self.flags.ptr, self.rank, self.world, self.epoch,
+                            payload)
+
+    def _step_fused(self, bc1, bc2, scale):
+        from ..ops._ext import ext
+
+        self._barrier()                                   # every rank's gradients are final
+        self.sumsq.zero_()
+        ext().rs_sum_sqnorm(self.sym["grad"].table, self.world, self.shard_off, self.shard_len,
+                            self.red, self.sumsq)
+        self._barrier(self.sumsq)                         # squared-norm partials exchanged
+        pay = self.flags.tensor(self.world, torch.float32, 4 * self.world)
+        ext().shard_adamw_allgather(
+            self.red, self.flat.master, self.m, self.v, self.sym["master"].table,
+            self.sym["compute"].table, self.world, self.shard_off, self.shard_len,
+            self.flat.decay_end, pay if self.grad_clip > 0 else None, float(self.grad_clip),
+            self.lr, self.betas[0], self.betas[1], self.eps, self.wd, bc1, bc2, scale)
+        self._barrier()                                   # all peers' stores have landed
+
+    def _step_collective(self, bc1, bc2, scale):
+        g = self.flat.grad
+        dist.reduce_scatter_tensor(self.red, g, group=self.group)
+        clip = 1.0
+        if self.grad_clip > 0:
+            sq = self.red.double().pow(2).sum().float().reshape(1)
+            dist.all_reduce(sq, group=self.group)
+            norm = sq.sqrt() * scale
+            self.last_grad_norm = norm
+            clip = torch.clamp(self.grad_clip / (norm + 1e-6), max=1.0)
+        lo, hi = self.shard_off, self.shard_off + self.shard_len
+        master = self.flat.master[lo:hi]
+        gr = self.red * (scale * clip)
+        b1, b2 = self.betas
+        self.m.mul_(b1).add_(gr, alpha=1 - b1)
+        self.v.mul_(b2).addcmul_(gr, gr, value=1 - b2)
+        upd = (self.m / bc1) / ((self.v / bc2).sqrt() + self.eps)
+        if self.wd:
+            d_end = min(max(self.flat.decay_end - lo, 0), self.shard_len)
+            master[:d_end].mul_(1 - self.lr * self.wd)
+        master.add_(upd, alpha=-self.lr)
+        shard = master.clone()
+        dist.all_gather_into_tensor(self.flat.master, shard, group=self.group)
+        self.flat.refresh_compute()
+
+    def close(self):
+        for b in self.sym.values():
+            b.close()
+        if self.sym:
+            self.flags.close()
+        self.sym = {}
+
+
+def _padded_numel(named, no_decay, pad) -> int:
+    from .flat import _round
+
+    off = 0
+    for _, p in named:
+        off = _round(off + p.numel(), ALIGN)
+    return _round(off, pad)

@@ -35,9 +35,22 @@ class WorldModelTrainer:
         self.cuda = self.device.type == "cuda"
         self.compute_dtype = torch.bfloat16 if (self.cuda and cfg.dtype == "bf16") else torch.float32
         self.pg = process_group
-        self.group = FlatParamGroup(model.named_parameters(), self.device,
-                                    no_decay=model.no_decay_names())
-        self.opt = FlatAdamW(self.group, cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay, cfg.grad_clip)
+        self.engine = None
+        world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
+        if world > 1:
+            from ..parallel.sharded import ShardedDataParallel
+
+            transport = "fused" if (self.cuda and cfg.fused_collectives) else "nccl"
+            self.engine = ShardedDataParallel(model, process_group, self.device, transport,
+                                              cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
+                                              cfg.grad_clip)
+            self.group = self.engine.flat
+            self.opt = None
+        else:
+            self.group = FlatParamGroup(model.named_parameters(), self.device,
+                                        no_decay=model.no_decay_names())
+            self.opt = FlatAdamW(self.group, cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
+                                 cfg.grad_clip)
         self.fused = self.cuda if fused is None else fused
         if self.fused:
             model.enable_fused(group=self.group)
@@ -60,21 +73,25 @@ class WorldModelTrainer:
         self.group.zero_grad()
         loss = self.loss(batch)
         loss.backward()
-        if self.pg is not None:
-            torch.distributed.all_reduce(self.group.grad, group=self.pg)
-            scale = 1.0 / torch.distributed.get_world_size(self.pg)
+        if self.engine is not None:
+            self.engine.step()
         else:
-            scale = 1.0
-        self.opt.step(grad_scale=scale)
+            self.opt.step()
         self.step_idx += 1
         return loss.detach()
 
     def state_dict(self) -> Dict:
-        return {"model": self.model.state_dict(), "optim": self.opt.state_dict(),
-                "step": self.step_idx}
+        opt = self.opt.state_dict() if self.opt is not None else {
+            "m": self.engine.m, "v": self.engine.v, "step": self.engine.step_count}
+        return {"model": self.model.state_dict(), "optim": opt, "step": self.step_idx}
 
     def load_state_dict(self, sd: Dict):
         self.model.load_state_dict(sd["model"])
         self.group.refresh_compute()
-        self.opt.load_state_dict(sd["optim"])
+        if self.opt is not None:
+            self.opt.load_state_dict(sd["optim"])
+        else:
+            self.engine.m.copy_(sd["optim"]["m"])
+            self.engine.v.copy_(sd["optim"]["v"])
+            self.engine.step_count = int(sd["optim"]["step"])
         self.step_idx = int(sd["step"])
