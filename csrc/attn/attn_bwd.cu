@@ -231,6 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % NS;
         const uint32_t aQ = smem_u32(smem + OFF_Q + s * TILE);
         const uint32_t aDO = smem_u32(smem + OFF_DO + s * TILE);
+        if (!(g.debug_flags & 8))
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // K = 128 queries
           const uint32_t off = (kk >> 2) * TILE + (kk & 3) * 32;
@@ -242,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       make_sw128_desc(aQ + kk * 2048, 8192, 1024), IDESC_GRAD,
                       (i > 0 || kk > 0) ? 1u : 0u);
         }
+        if (!(g.debug_flags & 8))
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // K = 128 keys: dQ = dS K
           // A = dS^T tile read MN-major: queries contiguous in 64-wide chunks (LBO =
@@ -300,6 +302,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = a.scale * 1.4426950408889634f;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t swz = r & 7;
+    // this key is visible to every query q >= qmin (masks are monotone in the query);
+    // keys past the sequence end are visible to none
+    const int qmin = (key < a.S) ? (sparse ? 0 : first_query_seeing(a, key)) : (1 << 30);
     bool ok = true;
     for (int j = 0; j < nq; ++j) {
       const int s = j % NS;
@@ -308,9 +313,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* s_lse = reinterpret_cast<const float*>(smem + OFF_VEC + s * 1024);
       const float* s_delta = s_lse + 128;
       const int bits = sparse ? g.kv_qmask[list_idx * g.max_q + j] : 0xF;
-      // element masks are needed only where some query of the tile cannot see some key
-      // of the tile (key limits are non-decreasing in the query index)
-      const bool need_mask = !sparse && row_limit(a, q0) < k0 + 128;
       if (!mbar_wait(s_full, j & 1, abort_flag)) {
         ok = false;
         break;
@@ -331,17 +333,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(trow + C_S + c0, rs);
         tmem_ld32(trow + C_DP + c0, rp);
         tmem_wait_ld();
+        if (warp == 2 && lane == 0 && j < 8) DDB_TRACE(2, 3 + (c0 >> 5), j);
         const bool half_on = (bits >> ((c0 >> 6) * 2 + khalf)) & 1;
         float p[32], ds[32];
+        if (g.debug_flags & 2) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int qi = c0 + c;
-          const bool vis = half_on && (!need_mask || key < row_limit(a, q0 + qi));
-          const float pv = vis ? exp2f(__uint_as_float(rs[c]) * sl2 - s_lse[qi]) : 0.f;
-          p[c] = pv;
-          ds[c] = pv * (__uint_as_float(rp[c]) - s_delta[qi]) * a.scale;
+          for (int c = 0; c < 32; ++c) {
+            p[c] = __uint_as_float(rs[c]);
+            ds[c] = __uint_as_float(rp[c]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int qi = c0 + c;
+            const bool vis = half_on && (q0 + qi >= qmin);
+            const float pv = vis ? exp2f(__uint_as_float(rs[c]) * sl2 - s_lse[qi]) : 0.f;
+            p[c] = pv;
+            ds[c] = pv * (__uint_as_float(rp[c]) - s_delta[qi]) * a.scale;
+          }
         }
         const int ch = c0 >> 6;
+        if (!(g.debug_flags & 4))
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
           const int u = ((c0 & 63) >> 3) + u4;

@@ -82,10 +82,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
+  uint32_t backoff = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kSpinLimitCycles) return false;
+    // leave issue slots to the warps doing work while this one waits
+    if (backoff) __nanosleep(backoff);
+    backoff = backoff < 256 ? backoff + 32 : 256;
   }
 }
 
