@@ -15,6 +15,8 @@ struct AttnArgs {
   int S = 0;                  // keys per sample
   long q_rows_per_b = 0;      // row stride between samples in the q tensor (usually Tq)
   long kv_rows_per_b = 0;     // row stride between samples in the k/v tensors (usually S)
+  long q_rows_total = 0;      // rows addressable in q / k,v (0: B * rows_per_b)
+  long kv_rows_total = 0;
   const void* q = nullptr;    // bf16 rows; head h at column q_col + 64 h
   long ldq = 0;
   int q_col = 0;

@@ -386,8 +386,8 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
                "cudaFuncSetAttribute(attn_fwd)");
     attr = true;
   }
-  const long q_rows = a.B * a.q_rows_per_b;
-  const long kv_rows = a.B * a.kv_rows_per_b;
+  const long q_rows = a.q_rows_total > 0 ? a.q_rows_total : a.B * a.q_rows_per_b;
+  const long kv_rows = a.kv_rows_total > 0 ? a.kv_rows_total : a.B * a.kv_rows_per_b;
   CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
                                 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,

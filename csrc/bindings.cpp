@@ -267,9 +267,11 @@ ddb::AttnArgs make_attn_args(const torch::Tensor& q, const torch::Tensor& k, con
     check_bf16(*t, "q/k/v");
     check_rows(*t, "q/k/v");
   }
-  TORCH_CHECK(q.size(0) >= B * q_rows_per_b && k.size(0) >= B * kv_rows_per_b &&
-                  v.size(0) >= B * kv_rows_per_b,
-              "attention: tensors have fewer rows than B * rows_per_b");
+  TORCH_CHECK(q.size(0) >= (B - 1) * q_rows_per_b + Tq &&
+                  k.size(0) >= (B - 1) * kv_rows_per_b + S &&
+                  v.size(0) >= (B - 1) * kv_rows_per_b + S,
+              "attention: tensors have fewer rows than the samples need");
+  TORCH_CHECK(k.size(0) == v.size(0), "attention: k and v differ in rows");
   TORCH_CHECK(q_col + H * 64 <= q.size(1) && k_col + H * 64 <= k.size(1) &&
                   v_col + H * 64 <= v.size(1),
               "attention: head columns out of range");
@@ -283,6 +285,8 @@ ddb::AttnArgs make_attn_args(const torch::Tensor& q, const torch::Tensor& k, con
   a.v = v.data_ptr(); a.ldv = v.stride(0); a.v_col = v_col;
   a.causal = causal; a.tpf = tpf; a.q_pos_offset = q_pos_offset;
   a.kv_pos_offset = kv_pos_offset; a.scale = static_cast<float>(scale);
+  a.q_rows_total = q.size(0);
+  a.kv_rows_total = k.size(0);
   return a;
 }
 
@@ -297,7 +301,7 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
                           causal, tpf, q_pos_offset, kv_pos_offset, scale);
   check_bf16(o, "o");
   check_rows(o, "o");
-  TORCH_CHECK(o.size(0) >= B * q_rows_per_b && o_col + H * 64 <= o.size(1), "o shape");
+  TORCH_CHECK(o.size(0) >= (B - 1) * q_rows_per_b + Tq && o_col + H * 64 <= o.size(1), "o shape");
   a.o = o.data_ptr(); a.ldo = o.stride(0); a.o_col = o_col;
   if (lse) {
     TORCH_CHECK(lse->scalar_type() == torch::kFloat32 && lse->is_contiguous() &&

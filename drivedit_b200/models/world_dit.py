@@ -263,3 +263,124 @@ class WorldDiT(nn.Module):
 
         self.fused = FusedWorldDiT(self, **kw)
         return self.fused
+
+
+# ----------------------------------------------------------------------------- KV-cached
+class LayerKVCache:
+    """Per-layer key/value window for streaming generation.
+
+    ``k``/``v`` are ``[B, capacity, d]`` buffers holding consecutive tokens; ``start`` is
+    the buffer row of the first token inside the attention window, ``end`` one past the
+    last written token and ``pos0`` the absolute token position of buffer row 0. When a
+    new chunk would not fit, the last ``window`` tokens are moved to the front (amortised:
+    once every ``window / chunk`` chunks)."""
+
+    def __init__(self, B: int, capacity: int, d: int, window: int, device, dtype):
+        self.k = torch.zeros(B, capacity, d, device=device, dtype=dtype)
+        self.v = torch.zeros(B, capacity, d, device=device, dtype=dtype)
+        self.capacity, self.window = capacity, window
+        self.start = self.end = 0
+        self.pos0 = 0
+
+    def reserve(self, n: int) -> int:
+        """Make room for ``n`` new tokens after the window; returns their buffer row."""
+        keep_from = max(self.start, self.end - self.window)
+        if self.end + n > self.capacity:
+            keep = self.end - keep_from
+            self.k[:, :keep] = self.k[:, keep_from:self.end].clone()
+            self.v[:, :keep] = self.v[:, keep_from:self.end].clone()
+            self.pos0 += keep_from
+            self.end = keep
+            keep_from = 0
+        self.start = keep_from
+        return self.end
+
+    def commit(self, n: int):
+        self.end += n
+
+
+class KVCacheSet:
+    """One :class:`LayerKVCache` per block; ``frames`` counts committed frames."""
+
+    def __init__(self, model: "WorldDiT", B: int, window_frames: int, chunk_frames: int,
+                 device, dtype):
+        cfg = model.cfg
+        tpf = cfg.tokens_per_frame
+        cap = (2 * window_frames + chunk_frames) * tpf
+        self.layers = [LayerKVCache(B, cap, cfg.d_model, window_frames * tpf, device, dtype)
+                       for _ in model.blocks]
+        self.frames = 0
+        self.tpf = tpf
+
+    def reserve(self, n_tokens: int) -> int:
+        rows = [c.reserve(n_tokens) for c in self.layers]
+        return rows[0]
+
+    def commit(self, n_frames: int):
+        for c in self.layers:
+            c.commit(n_frames * self.tpf)
+        self.frames += n_frames
+
+
+def _block_cached_torch(blk: WorldDiTBlock, x, mod, tab_q, cache: LayerKVCache, row, frames):
+    """One block over a chunk ``x [B, T, d]`` attending to the cache window + itself;
+    writes the chunk's K/V into the cache rows ``[row, row + T)``."""
+    cfg = blk.cfg
+    B, T, d = x.shape
+    H, Dh = cfg.n_heads, cfg.d_head
+    dt = x.dtype
+    tpf = T // frames
+    m = mod.repeat_interleave(tpf, dim=1)
+    s1, b1, s2, b2 = m.chunk(blk.n_mod, -1)[:4]
+
+    def norm(v, w):
+        vf = v.float()
+        return (vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + cfg.norm_eps)).to(dt) * w.to(dt)
+
+    h = norm(x, blk.norm1.weight) * (1 + s1) + b1
+    qkv = (h @ blk.attn.qkv.weight.to(dt).t()).view(B, T, 3, H, Dh)
+    q, k, v = qkv.unbind(2)
+    q, k = apply_rope(q, tab_q), apply_rope(k, tab_q)
+    cache.k[:, row:row + T] = k.reshape(B, T, d)
+    cache.v[:, row:row + T] = v.reshape(B, T, d)
+    kk = cache.k[:, cache.start:row + T].view(B, -1, H, Dh)
+    vv = cache.v[:, cache.start:row + T].view(B, -1, H, Dh)
+    S = kk.shape[1]
+    mask = frame_causal_mask(T, tpf, S, x.device)
+    o = attention_reference(q, kk, vv, mask).to(dt)
+    x = x + o.reshape(B, T, d) @ blk.attn.proj.weight.to(dt).t()
+    h2 = norm(x, blk.norm2.weight) * (1 + s2) + b2
+    gu = h2 @ blk.mlp.w13.weight.to(dt).t()
+    g, u = split_gu(gu)
+    return x + (F.silu(g) * u) @ blk.mlp.w3.weight.to(dt).t()
+
+
+@torch.no_grad()
+def forward_cached(model: "WorldDiT", x_t: torch.Tensor, t: torch.Tensor, actions: torch.Tensor,
+                   cache: KVCacheSet, commit: bool = False) -> torch.Tensor:
+    """Velocity for a chunk of frames ``x_t [B, Fc, C, H, W]`` at absolute frame
+    ``cache.frames``, attending to the cached window. With ``commit`` the chunk's K/V stay
+    in the cache (call this on the clean chunk after sampling it)."""
+    if model.fused is not None and x_t.is_cuda:
+        return model.fused.forward_cached(model, x_t, t, actions, cache, commit)
+    cfg = model.cfg
+    B, Fc, C, H, W = x_t.shape
+    dt = x_t.dtype
+    tok = patchify(x_t, cfg.patch)
+    x = model.patch_embed(tok.to(model.patch_embed.weight.dtype)).to(dt)
+    c = model.condition(t, actions)
+    T = x.shape[1]
+    tab = model.rope.table(Fc, cache.frames).to(x.device)
+    row = cache.reserve(T)
+    for blk, lc in zip(model.blocks, cache.layers):
+        mod = blk.ada(c).to(dt)
+        x = _block_cached_torch(blk, x, mod, tab, lc, row, Fc)
+    if commit:
+        cache.commit(Fc)
+    fm = model.final_ada(c).to(dt).repeat_interleave(T // Fc, 1)
+    sc, sh = fm.chunk(2, -1)
+    xf = x.float()
+    hn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg.norm_eps)).to(dt) * \
+        model.final_norm.weight.to(dt)
+    out = model.out_proj((hn * (1 + sc) + sh).to(model.out_proj.weight.dtype))
+    return unpatchify(out.to(dt), Fc, C, H, W, cfg.patch)

@@ -22,6 +22,7 @@ hundred rows) stay in PyTorch.
 """
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import torch
@@ -173,3 +174,58 @@ class _FinalNorm(torch.autograd.Function):
         dx = adaln_rmsnorm_bwd(dh.contiguous(), x, r, ctx.w, mod, 0, d, ctx.tpf, dmod,
                                ctx.w.grad, None)
         return dx, dmod, None, None, None
+
+
+# ----------------------------------------------------------------------------- KV-cached
+def _forward_cached_fused(self, model, x_t, t, actions, cache, commit):
+    """Inference-only forward of a chunk over the cached K/V window (no autograd):
+    every block is AdaLN-RMSNorm -> QKV GEMM (rotary by absolute frame) -> K/V into the
+    cache window -> flash attention with absolute query/key offsets -> output GEMM with
+    residual -> AdaLN-RMSNorm -> SwiGLU GEMM -> down GEMM with residual."""
+    from ..models.world_dit import patchify, unpatchify
+    from ._ext import ext
+
+    cfg = model.cfg
+    g = self.group
+    W = g.compute_view
+    B, Fc, C, H, W_ = x_t.shape
+    d, Hh = cfg.d_model, cfg.n_heads
+    tok = patchify(x_t, cfg.patch).reshape(-1, cfg.patch_dim).to(torch.bfloat16).contiguous()
+    T = tok.shape[0] // B
+    tpf = T // Fc
+    x = gemm(tok, W(model.patch_embed.weight), bias=model.patch_embed.bias)
+    c2 = model.condition(t, actions).reshape(B * Fc, d)
+    tab = model.rope.table(Fc, cache.frames).to(x.device)
+    row = cache.reserve(T)
+    for blk, lc in zip(model.blocks, cache.layers):
+        mod = blk.ada(c2)
+        h1, _ = adaln_rmsnorm(x, blk.norm1.weight, mod, 0, d, tpf)
+        qkv = gemm(h1, W(blk.attn.qkv.weight), epi="rope", rope_tab=tab, rope_cols=2 * d,
+                   rope_rows_per_seq=T, rope_head_dim=cfg.d_head)
+        q3 = qkv.view(B, T, 3 * d)
+        lc.k[:, row:row + T].copy_(q3[:, :, d:2 * d])
+        lc.v[:, row:row + T].copy_(q3[:, :, 2 * d:])
+        cap = lc.k.shape[1]
+        k2 = lc.k.view(B * cap, d)[lc.start:]
+        v2 = lc.v.view(B * cap, d)[lc.start:]
+        S = row + T - lc.start
+        o = torch.empty(B * T, d, device=x.device, dtype=torch.bfloat16)
+        ext().attn_fwd(qkv, k2, v2, o, None, 0, 0, 0, 0, B, Hh, T, S, T, cap, 1, tpf,
+                       lc.pos0 + row, lc.pos0 + lc.start, 1.0 / math.sqrt(cfg.d_head),
+                       None, None, None)
+        x1 = gemm(o, W(blk.attn.proj.weight), residual=x)
+        h2, _ = adaln_rmsnorm(x1, blk.norm2.weight, mod, 2 * d, 3 * d, tpf)
+        w13 = W(blk.mlp.w13.weight)
+        gu = torch.empty(x.shape[0], w13.shape[0], device=x.device, dtype=torch.bfloat16)
+        a = torch.empty(x.shape[0], w13.shape[0] // 2, device=x.device, dtype=torch.bfloat16)
+        gemm(h2, w13, gu, epi="swiglu", out2=a)
+        x = gemm(a, W(blk.mlp.w3.weight), residual=x1)
+    if commit:
+        cache.commit(Fc)
+    fm = model.final_ada(c2)
+    h, _ = adaln_rmsnorm(x, model.final_norm.weight, fm, 0, d, tpf, cfg.norm_eps)
+    out = gemm(h, W(model.out_proj.weight), bias=model.out_proj.bias)
+    return unpatchify(out.view(B, T, cfg.patch_dim), Fc, C, H, W_, cfg.patch)
+
+
+FusedWorldDiT.forward_cached = _forward_cached_fused
