@@ -219,7 +219,9 @@ def run_ours(args, ws, rank, local):
             "global_batch": B * ws, "seq_len": Fr * cfg.model.tokens_per_frame,
             "frames": Fr, "latent": [cfg.model.latent_channels, cfg.model.latent_h,
                                      cfg.model.latent_w],
-            "parallelism": f"dp{ws}" if ws > 1 else "single",
+            "parallelism": f"fsdp{ws}" if ws > 1 else "single",
+            "sharding": ("gradients reduce-scattered and weights all-gathered by the fused "
+                         "NVLink optimizer kernel; AdamW state sharded") if ws > 1 else None,
             "l2": "256 MiB buffer overwritten before every timed step",
         },
         "clocks": clk.summary(),
