@@ -11,6 +11,7 @@
 #include "attn/attn.h"
 #include "attn/sla.h"
 #include "comm/comm.h"
+#include "moe/moe.h"
 
 namespace {
 
@@ -607,6 +608,177 @@ void shard_adamw_allgather(torch::Tensor red, torch::Tensor master_local, torch:
   ddb::shard_adamw_allgather(a, stream());
 }
 
+// ------------------------------------------------------------------ MoE
+// mode 1: D[rows] = A[rows] B[e]^T per expert row-tile (A: [rows, K]; B: [E, N, K] or, b_t,
+//         [E, K, N]); mode 2: D[e] (+)= A[seg e]^T B[seg e] (A: [rows, M], B: [rows, N]).
+void gemm_grouped(torch::Tensor A, torch::Tensor B, torch::Tensor D, int64_t epi, bool b_t,
+                  int64_t mode, torch::Tensor tile_expert, torch::Tensor tile_row,
+                  torch::Tensor total_mtiles, torch::Tensor kstart, torch::Tensor kend,
+                  int64_t max_mtiles, c10::optional<torch::Tensor> C,
+                  c10::optional<torch::Tensor> D2) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_rows(A, "A");
+  check_rows(D, "D");
+  for (auto* t : {&tile_expert, &tile_row, &total_mtiles, &kstart, &kend})
+    TORCH_CHECK(t->scalar_type() == torch::kInt32 && t->is_cuda(), "grouped tables must be int32 CUDA");
+  const c10::cuda::CUDAGuard guard(A.device());
+  ddb::GemmArgs a;
+  a.grouped = mode;
+  a.grp_tile_expert = tile_expert.data_ptr<int>();
+  a.grp_tile_row = tile_row.data_ptr<int>();
+  a.grp_total_mtiles = total_mtiles.data_ptr<int>();
+  a.grp_kstart = kstart.data_ptr<int>();
+  a.grp_kend = kend.data_ptr<int>();
+  a.grp_max_mtiles = max_mtiles;
+  if (mode == 1) {
+    TORCH_CHECK(B.dim() == 3 && B.stride(2) == 1, "grouped mode 1: B [E, rows, cols]");
+    a.a_mn_major = false;
+    a.b_mn_major = b_t;
+    a.M = A.size(0);
+    a.K = A.size(1);
+    a.N = b_t ? B.size(2) : B.size(1);
+    TORCH_CHECK((b_t ? B.size(1) : B.size(2)) == a.K, "grouped: inner dimensions differ");
+    a.batch = B.size(0);
+    a.stride_b = B.stride(0);
+    a.ldb = B.stride(1);
+  } else {
+    TORCH_CHECK(mode == 2 && B.dim() == 2, "grouped mode 2: B [rows, N]");
+    check_rows(B, "B");
+    a.a_mn_major = true;
+    a.b_mn_major = true;
+    a.M = A.size(1);
+    a.K = A.size(0);
+    a.N = B.size(1);
+    TORCH_CHECK(B.size(0) == a.K, "grouped mode 2: A and B rows differ");
+    a.batch = kstart.numel();
+    a.ldb = B.stride(0);
+    TORCH_CHECK(D.size(0) == static_cast<int64_t>(a.batch) * a.M, "grouped mode 2: D rows");
+  }
+  a.A = A.data_ptr(); a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.D = D.data_ptr(); a.ldd = D.stride(0);
+  if (C) {
+    check_bf16(*C, "C");
+    check_rows(*C, "C");
+    a.C = C->data_ptr(); a.ldc = C->stride(0);
+  }
+  if (D2) {
+    check_bf16(*D2, "D2");
+    check_rows(*D2, "D2");
+    a.D2 = D2->data_ptr(); a.ldd2 = D2->stride(0);
+  }
+  ddb::gemm(a, static_cast<int>(epi), stream());
+}
+
+std::vector<torch::Tensor> moe_route(torch::Tensor logits, c10::optional<torch::Tensor> bias,
+                                     int64_t E, int64_t k, int64_t ns, bool want_probs) {
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2 && logits.stride(1) == 1,
+              "logits must be fp32 [N, cols]");
+  TORCH_CHECK(logits.size(1) >= E + ns, "logits too narrow");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0);
+  auto opt = logits.options();
+  auto idx = torch::empty({N, k}, opt.dtype(torch::kInt32));
+  auto w = torch::empty({N, k}, opt);
+  auto sw = torch::empty({N, std::max<int64_t>(ns, 1)}, opt);
+  auto probs = want_probs ? torch::empty({N, E}, opt) : torch::empty({0}, opt);
+  auto counts = torch::zeros({E}, opt.dtype(torch::kInt32));
+  auto psum = torch::zeros({E}, opt);
+  ddb::MoeRouteArgs a;
+  a.logits = logits.data_ptr<float>(); a.ld_logits = logits.stride(0);
+  if (bias) a.bias = bias->data_ptr<float>();
+  a.N = N; a.E = E; a.k = k; a.ns = ns;
+  a.topk_idx = idx.data_ptr<int>(); a.topk_w = w.data_ptr<float>(); a.shared_w = sw.data_ptr<float>();
+  a.probs = want_probs ? probs.data_ptr<float>() : nullptr;
+  a.counts = counts.data_ptr<int>(); a.psum = psum.data_ptr<float>();
+  ddb::moe_route(a, stream());
+  return {idx, w, sw, probs, counts, psum};
+}
+
+std::vector<torch::Tensor> moe_plan(torch::Tensor counts, int64_t E, int64_t ns, int64_t N,
+                                    int64_t max_mtiles) {
+  const c10::cuda::CUDAGuard guard(counts.device());
+  auto opt = counts.options().dtype(torch::kInt32);
+  const int64_t Ep = E + ns;
+  auto seg_start = torch::empty({Ep}, opt), seg_count = torch::empty({Ep}, opt);
+  auto tile_expert = torch::empty({max_mtiles}, opt), tile_row = torch::empty({max_mtiles}, opt);
+  auto total = torch::empty({1}, opt), kstart = torch::empty({Ep}, opt), kend = torch::empty({Ep}, opt);
+  auto cursor = torch::empty({Ep}, opt);
+  ddb::moe_plan(counts.data_ptr<int>(), E, ns, N, seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
+                tile_expert.data_ptr<int>(), tile_row.data_ptr<int>(), total.data_ptr<int>(),
+                kstart.data_ptr<int>(), kend.data_ptr<int>(), cursor.data_ptr<int>(), max_mtiles,
+                stream());
+  return {seg_start, seg_count, tile_expert, tile_row, total, kstart, kend, cursor};
+}
+
+torch::Tensor moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor seg_start,
+                           torch::Tensor seg_count, torch::Tensor cursor, torch::Tensor xp,
+                           int64_t E, int64_t ns) {
+  check_bf16(x, "x");
+  check_bf16(xp, "xp");
+  check_rows(x, "x");
+  check_rows(xp, "xp");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), k = topk_idx.size(1);
+  auto slot_of = torch::empty({N, k + ns}, x.options().dtype(torch::kInt32));
+  ddb::moe_dispatch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), N, x.size(1), k,
+                    ns, E, topk_idx.data_ptr<int>(), seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
+                    cursor.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()),
+                    xp.stride(0), slot_of.data_ptr<int>(), stream());
+  return slot_of;
+}
+
+ddb::MoeCombineArgs combine_args(torch::Tensor topk_w, torch::Tensor shared_w, torch::Tensor slot_of,
+                                 torch::Tensor y, int64_t ns) {
+  check_bf16(y, "y");
+  check_rows(y, "y");
+  ddb::MoeCombineArgs a;
+  a.N = topk_w.size(0); a.k = topk_w.size(1); a.ns = ns; a.d = y.size(1);
+  a.topk_w = topk_w.data_ptr<float>(); a.shared_w = shared_w.data_ptr<float>();
+  a.slot_of = slot_of.data_ptr<int>();
+  a.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()); a.ld_y = y.stride(0);
+  return a;
+}
+
+torch::Tensor moe_combine(torch::Tensor topk_w, torch::Tensor shared_w, torch::Tensor slot_of,
+                          torch::Tensor y, c10::optional<torch::Tensor> residual, int64_t ns) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  auto a = combine_args(topk_w, shared_w, slot_of, y, ns);
+  auto out = torch::empty({a.N, a.d}, y.options());
+  if (residual) {
+    check_bf16(*residual, "residual");
+    a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    a.ld_res = residual->stride(0);
+  }
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr()); a.ld_out = out.stride(0);
+  ddb::moe_combine(a, stream());
+  return out;
+}
+
+std::vector<torch::Tensor> moe_combine_bwd(torch::Tensor topk_w, torch::Tensor shared_w,
+                                           torch::Tensor slot_of, torch::Tensor y, torch::Tensor dout,
+                                           int64_t ns) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  auto a = combine_args(topk_w, shared_w, slot_of, y, ns);
+  check_bf16(dout, "dout");
+  auto dy = torch::zeros_like(y);
+  auto dw = torch::empty({a.N, a.k + ns}, topk_w.options());
+  ddb::moe_combine_bwd(a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+                       reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dw.data_ptr<float>(), stream());
+  return {dy, dw};
+}
+
+torch::Tensor moe_unpermute(torch::Tensor dxp, torch::Tensor slot_of, int64_t N) {
+  check_bf16(dxp, "dxp");
+  const c10::cuda::CUDAGuard guard(dxp.device());
+  auto dx = torch::empty({N, dxp.size(1)}, dxp.options());
+  ddb::moe_unpermute(reinterpret_cast<const __nv_bfloat16*>(dxp.data_ptr()), dxp.stride(0),
+                     slot_of.data_ptr<int>(), N, slot_of.size(1), dxp.size(1),
+                     reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), stream());
+  return dx;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -640,6 +812,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("xrank_barrier", &xrank_barrier, "bounded cross-rank flag barrier over peer memory");
   m.def("rs_sum_sqnorm", &rs_sum_sqnorm, "reduce-scatter by peer loads + squared norm");
   m.def("shard_adamw_allgather", &shard_adamw_allgather, "sharded AdamW + all-gather by peer stores");
+  m.def("gemm_grouped", &gemm_grouped, "grouped (MoE) tcgen05 GEMM with device tile tables");
+  m.def("moe_route", &moe_route, "MoE top-k routing (+ shared gates, counts, prob sums)");
+  m.def("moe_plan", &moe_plan, "MoE segment layout and grouped-GEMM tables");
+  m.def("moe_dispatch", &moe_dispatch, "MoE token permutation into expert segments");
+  m.def("moe_combine", &moe_combine, "MoE weighted combine (+ residual)");
+  m.def("moe_combine_bwd", &moe_combine_bwd, "MoE combine backward");
+  m.def("moe_unpermute", &moe_unpermute, "MoE gather-sum of permuted gradients");
   m.def("gemm_batched", &gemm_batched, "strided-batched tcgen05 GEMM");
   m.def("sla_pool", &sla_pool, "SLA block means of q, k");
   m.def("sla_route", &sla_route, "SLA top-k routing + kernel lists");

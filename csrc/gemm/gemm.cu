@@ -45,19 +45,40 @@ struct GemmCfg {
 
 struct Sched {
   int tiles_m, tiles_n, kblocks, kb_per_split, splits, total, M;
-  // tile t -> (batch bt, row m0, column tile n0, k-block range); n fastest
-  __device__ __forceinline__ void decode(int t, int& m0, int& n0, int& kb0, int& kb1,
+  int grouped;
+  const int* g_tile_expert;
+  const int* g_tile_row;
+  const int* g_total_mtiles;
+  const int* g_kstart;
+  const int* g_kend;
+  // tile t -> (batch bt, row m0, column tile n0, k-block range); n fastest.
+  // Returns false for tiles that carry no work (grouped tables).
+  __device__ __forceinline__ bool decode(int t, int& m0, int& n0, int& kb0, int& kb1,
                                          int& bt) const {
     int n_idx = t % tiles_n;
     t /= tiles_n;
+    n0 = n_idx;  // scaled by BN by the caller
+    if (grouped == 1) {
+      if (t >= __ldg(g_total_mtiles)) return false;
+      bt = __ldg(g_tile_expert + t);
+      m0 = __ldg(g_tile_row + t);
+      kb0 = 0;
+      kb1 = kblocks;
+      return true;
+    }
     int m_idx = t % tiles_m;
     t /= tiles_m;
     int split = t % splits;
     bt = t / splits;
     m0 = m_idx * BM;
-    n0 = n_idx;  // scaled by BN by the caller
+    if (grouped == 2) {
+      kb0 = __ldg(g_kstart + bt);
+      kb1 = __ldg(g_kend + bt);
+      return kb1 > kb0;
+    }
     kb0 = split * kb_per_split;
     kb1 = min(kblocks, kb0 + kb_per_split);
+    return true;
   }
 };
 
@@ -285,8 +306,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
         int m0, nt, kb0, kb1, bt;
-        sched.decode(t, m0, nt, kb0, kb1, bt);
+        if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
         const int n0 = nt * BN;
+        const int ab = sched.grouped ? 0 : bt;        // A batch coordinate
+        const int bb = sched.grouped == 2 ? 0 : bt;   // B batch coordinate
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
@@ -296,17 +319,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           if constexpr (A_MN) {
-            tma_load_3d(sa, &tmA, &full[stage], m0, kb * BK, bt);
-            tma_load_3d(sa + 8192, &tmA, &full[stage], m0 + 64, kb * BK, bt);
+            tma_load_3d(sa, &tmA, &full[stage], m0, kb * BK, ab);
+            tma_load_3d(sa + 8192, &tmA, &full[stage], m0 + 64, kb * BK, ab);
           } else {
-            tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, bt);
+            tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, ab);
           }
           if constexpr (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_3d(sb + c * 8192, &tmB, &full[stage], n0 + c * 64, kb * BK, bt);
+              tma_load_3d(sb + c * 8192, &tmB, &full[stage], n0 + c * 64, kb * BK, bb);
           } else {
-            tma_load_3d(sb, &tmB, &full[stage], kb * BK, n0, bt);
+            tma_load_3d(sb, &tmB, &full[stage], kb * BK, n0, bb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -342,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool any = false;
       for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
         int m0, nt, kb0, kb1, bt;
-        sched.decode(t, m0, nt, kb0, kb1, bt);
+        if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort_flag)) {
           ok = false;
           break;
@@ -399,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
       int m0, nt, kb0, kb1, bt;
-      sched.decode(t, m0, nt, kb0, kb1, bt);
+      if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
       const int n0 = nt * BN;
       if (!mbar_wait(&acc_full[buf], acc_phase, abort_flag)) {
         if (lane == 0) record_status(status, kStatusTimeoutEpilogue);
@@ -407,9 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // batches are stacked row-wise in D (and C): global row = bt * M + row
+      // batches are stacked row-wise in D (and C): global row = bt * M + row; grouped
+      // row tiles address the permuted buffer directly
       const bool row_ok = m0 + row_in_tile < args.M;
-      const int row = bt * args.M + m0 + row_in_tile;
+      const int row = (sched.grouped == 1 ? 0 : bt * args.M) + m0 + row_in_tile;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
       if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll 1
@@ -465,19 +489,23 @@ void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, in
     attr_set = true;
   }
   CUtensorMap tA, tB;
-  const long sa = a.batch > 1 ? a.stride_a : (A_MN ? a.lda * a.K : a.lda * a.M);
-  const long sb = a.batch > 1 ? a.stride_b : (B_MN ? a.ldb * a.K : a.ldb * a.N);
+  // batch extents of the operand maps (grouped: A is one permuted buffer; in the
+  // weight-gradient form neither operand is batched, only D is)
+  const int nba = a.grouped ? 1 : a.batch;
+  const int nbb = a.grouped == 2 ? 1 : a.batch;
+  const long sa = nba > 1 ? a.stride_a : (A_MN ? a.lda * a.K : a.lda * a.M);
+  const long sb = nbb > 1 ? a.stride_b : (B_MN ? a.ldb * a.K : a.ldb * a.N);
   if (A_MN)
-    tA = make_tmap_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.batch, a.lda * 2,
+    tA = make_tmap_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, nba, a.lda * 2,
                       sa * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   else
-    tA = make_tmap_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.batch, a.lda * 2,
+    tA = make_tmap_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, nba, a.lda * 2,
                       sa * 2, 64, BM, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (B_MN)
-    tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.batch, a.ldb * 2,
+    tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, nbb, a.ldb * 2,
                       sb * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   else
-    tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.batch, a.ldb * 2,
+    tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, nbb, a.ldb * 2,
                       sb * 2, 64, BN, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status);
   count_launch();
@@ -556,8 +584,23 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   s.kb_per_split = (s.kblocks + splits - 1) / splits;
   s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
   s.M = a.M;
-  s.total = s.tiles_m * s.tiles_n * s.splits * (a.batch > 1 ? a.batch : 1);
-  if (a.batch > 1 && (a.stride_a % 8 != 0 || a.stride_b % 8 != 0))
+  s.grouped = a.grouped;
+  s.g_tile_expert = a.grp_tile_expert;
+  s.g_tile_row = a.grp_tile_row;
+  s.g_total_mtiles = a.grp_total_mtiles;
+  s.g_kstart = a.grp_kstart;
+  s.g_kend = a.grp_kend;
+  if (a.grouped == 1) {
+    s.splits = 1;
+    s.total = a.grp_max_mtiles * s.tiles_n;
+  } else if (a.grouped == 2) {
+    s.splits = 1;
+    s.total = s.tiles_m * s.tiles_n * a.batch;
+  } else {
+    s.total = s.tiles_m * s.tiles_n * s.splits * (a.batch > 1 ? a.batch : 1);
+  }
+  if (a.batch > 1 && ((a.grouped == 0 && a.stride_a % 8 != 0) ||
+                      (a.grouped != 2 && a.stride_b % 8 != 0)))
     throw std::runtime_error("gemm: batch strides must be multiples of 8 elements");
   int grid = s.total < sms ? s.total : sms;
   if (a.max_ctas > 0 && grid > a.max_ctas) grid = a.max_ctas;

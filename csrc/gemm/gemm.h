@@ -43,6 +43,19 @@ struct GemmArgs {
   int batch = 1;            // strided batch: A, B advance by stride_a / stride_b elements,
   long stride_a = 0;        // D (and C) by M rows (batches stacked row-wise)
   long stride_b = 0;
+  // grouped (MoE) scheduling with device-side tables:
+  //  1: A rows are expert segments of a permuted buffer; m-tile i covers rows
+  //     [grp_tile_row[i], +128) of expert grp_tile_expert[i] (B batch = expert);
+  //     *grp_total_mtiles tiles are valid (launched for an upper bound)
+  //  2: reduction over expert segments (weight gradients): expert e reduces k-blocks
+  //     [grp_kstart[e], grp_kend[e]) of A/B and writes D batch e
+  int grouped = 0;
+  const int* grp_tile_expert = nullptr;
+  const int* grp_tile_row = nullptr;
+  const int* grp_total_mtiles = nullptr;
+  const int* grp_kstart = nullptr;
+  const int* grp_kend = nullptr;
+  int grp_max_mtiles = 0;
   int splits = 1;           // split-K factor (kEpiF32Atomic only)
   int bn = 0;               // 0 = auto (128 or 256)
   int max_ctas = 0;         // 0 = all SMs

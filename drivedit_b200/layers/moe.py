@@ -11,15 +11,18 @@ Semantics follow the reference's ``layers/moe.py``:
   * ``MoEDiTBlock`` (:427-547): pre-norm attention + MoE FFN.
 
 Differences:
-  * routed-expert weights are stacked (``w_gate/w_value [E, F, d]``, ``w_out [E, d, F]``)
-    so the grouped GEMM reads one tensor per projection; ``load_state_dict`` accepts the
-    reference's per-expert keys ``experts.N.{w_gate,w_value,w_out}.weight`` and
+  * expert weights are stacked in the kernel layout (``w13 [E + ns, 2F, d]`` with gate and
+    value rows interleaved by 32, ``w2 [E + ns, d, F]``, shared experts last) so the
+    grouped GEMMs read one tensor per projection; ``load_state_dict`` accepts the
+    reference's per-expert keys ``experts.N.{w_gate,w_value,w_out}.weight``,
+    ``shared_experts.N.*``, ``router.gate.weight``, ``shared_gate.weight`` and
     :meth:`MoEFFN.reference_state_dict` writes them back.
   * the aux load-balance loss ``E * sum_e f_e P_e`` (f = share of the N*k assignments,
     P = mean router probability) is returned for the objective (weight configurable);
     the reference only logs it.
-  * with ``ep_group`` set, only this rank's ``E / ep`` experts live here and tokens are
-    exchanged by the expert-parallel dispatch/combine in ``drivedit_b200.parallel.ep``.
+  * on CUDA the whole FFN runs as routing / dispatch / grouped-GEMM / combine kernels
+    (:mod:`drivedit_b200.ops.moe`); shared experts are routed to every token with their
+    softmax gate and share that path.
 """
 from __future__ import annotations
 
@@ -100,6 +103,7 @@ def aux_load_balance_loss(probs: torch.Tensor, experts: torch.Tensor, num_expert
 
 
 def routing_metrics(probs, weights, experts, counts, num_experts) -> MoEMetrics:
+    probs, weights = probs.detach(), weights.detach()
     mean = counts.float().mean()
     lb = num_experts * ((counts.float() / max(experts.shape[0], 1)) * probs.mean(0)).sum()
     return MoEMetrics(
@@ -131,108 +135,155 @@ class ExpertFFN(nn.Module):
 
 
 class MoEFFN(nn.Module):
+    """Routed + shared SwiGLU experts in the kernel layout.
+
+    Parameters: ``router_weight [Epad, d]`` — rows ``[0, E)`` are the router gate, rows
+    ``[E, E + ns)`` the shared-expert gate, the rest zero padding to a multiple of 32;
+    ``w13 [E + ns, 2F, d]`` — each expert's gate and value rows interleaved in groups of
+    32 (``layers/mlp.py: pack_swiglu``), shared experts last; ``w2 [E + ns, d, F]``.
+    """
+
     def __init__(self, d_model: int, num_experts: int = 8, top_k: int = 2,
                  expert_dim: Optional[int] = None, num_shared_experts: int = 0,
                  dropout: float = 0.0, bias: bool = False, jitter_noise: float = 0.0,
-                 bias_update_speed: float = 0.001, aux_loss_weight: float = 0.0,
-                 expert_range: Optional[Tuple[int, int]] = None):
+                 bias_update_speed: float = 0.001, aux_loss_weight: float = 0.0):
         super().__init__()
-        assert not bias, "routed experts are bias-free"
+        assert not bias, "experts are bias-free"
+        from .mlp import pack_swiglu
+
         self.d_model, self.num_experts, self.top_k = d_model, num_experts, top_k
         self.expert_dim = expert_dim or default_expert_dim(d_model, top_k)
         self.num_shared_experts = num_shared_experts
         self.aux_loss_weight = aux_loss_weight
-        self.expert_range = expert_range or (0, num_experts)
-        e_local = self.expert_range[1] - self.expert_range[0]
-        Fh = self.expert_dim
-        self.router = Router(d_model, num_experts, top_k, jitter_noise, bias_update_speed)
-        self.w_gate = nn.Parameter(torch.randn(e_local, Fh, d_model) * 0.02)
-        self.w_value = nn.Parameter(torch.randn(e_local, Fh, d_model) * 0.02)
-        self.w_out = nn.Parameter(torch.randn(e_local, d_model, Fh) * (0.02 / math.sqrt(2)))
-        if num_shared_experts > 0:
-            self.shared_experts = nn.ModuleList(
-                [ExpertFFN(d_model, Fh) for _ in range(num_shared_experts)])
-            self.shared_gate = nn.Linear(d_model, num_shared_experts, bias=False)
-        else:
-            self.shared_experts = None
-            self.shared_gate = None
+        self.jitter_noise, self.bias_update_speed = jitter_noise, bias_update_speed
+        E, ns, Fh = num_experts, num_shared_experts, self.expert_dim
+        self.n_total = E + ns
+        self.e_pad = ((E + ns + 31) // 32) * 32
+        rw = torch.zeros(self.e_pad, d_model)
+        rw[:E + ns].normal_(0, 0.02)
+        self.router_weight = nn.Parameter(rw)
+        self.register_buffer("expert_bias", torch.zeros(E))
+        self.register_buffer("expert_load_ema", torch.ones(E) / E)
+        wg = torch.randn(E + ns, Fh, d_model) * 0.02
+        wv = torch.randn(E + ns, Fh, d_model) * 0.02
+        self.w13 = nn.Parameter(torch.stack([pack_swiglu(wg[i], wv[i]) for i in range(E + ns)]))
+        self.w2 = nn.Parameter(torch.randn(E + ns, d_model, Fh) * (0.02 / math.sqrt(2)))
         self._register_load_state_dict_pre_hook(self._load_reference_keys)
 
     # -------------------------------------------------------------- checkpoint compat
     def _load_reference_keys(self, state_dict, prefix, *args):
-        key0 = prefix + "experts.0.w_gate.weight"
-        if key0 not in state_dict:
+        from .mlp import pack_swiglu
+
+        if prefix + "experts.0.w_gate.weight" not in state_dict:
             return
-        lo, hi = self.expert_range
-        for name in ("w_gate", "w_value", "w_out"):
-            ws = [state_dict.pop(f"{prefix}experts.{e}.{name}.weight")
-                  for e in range(self.num_experts)
-                  if f"{prefix}experts.{e}.{name}.weight" in state_dict]
-            state_dict[prefix + name] = torch.stack(ws[lo:hi]) if len(ws) == self.num_experts else torch.stack(ws)
+        E, ns = self.num_experts, self.num_shared_experts
+        rw = self.router_weight.detach().clone()
+        rw[:E] = state_dict.pop(prefix + "router.gate.weight")
+        if ns:
+            rw[E:E + ns] = state_dict.pop(prefix + "shared_gate.weight")
+        state_dict[prefix + "router_weight"] = rw
+        for b in ("expert_bias", "expert_load_ema"):
+            if prefix + "router." + b in state_dict:
+                state_dict[prefix + b] = state_dict.pop(prefix + "router." + b)
+        w13, w2 = [], []
+        for i in range(E + ns):
+            base = f"{prefix}experts.{i}." if i < E else f"{prefix}shared_experts.{i - E}."
+            g = state_dict.pop(base + "w_gate.weight")
+            v = state_dict.pop(base + "w_value.weight")
+            w13.append(pack_swiglu(g, v))
+            w2.append(state_dict.pop(base + "w_out.weight"))
+        state_dict[prefix + "w13"] = torch.stack(w13)
+        state_dict[prefix + "w2"] = torch.stack(w2)
 
     def reference_state_dict(self, prefix: str = "") -> Dict[str, torch.Tensor]:
         """Per-expert keys in the reference's layout (``experts.N.w_gate.weight`` ...)."""
-        out = {}
-        lo, _ = self.expert_range
-        for name in ("w_gate", "w_value", "w_out"):
-            w = getattr(self, name).detach()
-            for i in range(w.shape[0]):
-                out[f"{prefix}experts.{lo + i}.{name}.weight"] = w[i].clone()
-        for k, v in self.state_dict().items():
-            if k.split(".")[0] not in ("w_gate", "w_value", "w_out"):
-                out[prefix + k] = v
+        from .mlp import unpack_swiglu
+
+        E, ns = self.num_experts, self.num_shared_experts
+        out = {prefix + "router.gate.weight": self.router_weight[:E].detach().clone(),
+               prefix + "router.expert_bias": self.expert_bias.clone(),
+               prefix + "router.expert_load_ema": self.expert_load_ema.clone()}
+        if ns:
+            out[prefix + "shared_gate.weight"] = self.router_weight[E:E + ns].detach().clone()
+        for i in range(E + ns):
+            base = f"{prefix}experts.{i}." if i < E else f"{prefix}shared_experts.{i - E}."
+            g, v = unpack_swiglu(self.w13[i].detach())
+            out[base + "w_gate.weight"] = g.clone()
+            out[base + "w_value.weight"] = v.clone()
+            out[base + "w_out.weight"] = self.w2[i].detach().clone()
         return out
 
-    # -------------------------------------------------------------- compute
-    def experts_forward(self, x: torch.Tensor, weights: torch.Tensor, experts: torch.Tensor):
-        """Reference-math routed output (stable sort by expert, loop over experts)."""
+    # -------------------------------------------------------------- routing
+    def route(self, x: torch.Tensor):
+        """(weights [N,k], experts [N,k], probs [N,E], shared gates [N,ns])."""
+        E, ns = self.num_experts, self.num_shared_experts
+        logits = (x @ self.router_weight[:E + ns].to(x.dtype).t()).float()
+        rl = logits[:, :E]
+        if self.training and self.jitter_noise > 0:
+            rl = rl + torch.randn_like(rl) * self.jitter_noise
+        p = F.softmax(rl + self.expert_bias, dim=-1)
+        w, e = torch.topk(p, self.top_k, dim=-1)
+        w = w / (w.sum(-1, keepdim=True) + 1e-8)
+        g = F.softmax(logits[:, E:E + ns], -1) if ns else None
+        return w, e, p, g
+
+    @torch.no_grad()
+    def update_bias(self, counts: torch.Tensor, n_tokens: int):
+        """Aux-loss-free balancing (reference layers/moe.py:164-181)."""
+        if not self.training:
+            return
+        s = self.bias_update_speed
+        load = counts.float() / (n_tokens * self.top_k + 1e-8)
+        self.expert_load_ema.mul_(1 - s).add_(load, alpha=s)
+        self.expert_bias.add_(-s * (self.expert_load_ema - 1.0 / self.num_experts))
+
+    def _expert(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        from .mlp import split_gu
+
+        gu = x @ self.w13[i].to(x.dtype).t()
+        g, u = split_gu(gu)
+        return (F.silu(g) * u) @ self.w2[i].to(x.dtype).t()
+
+    def experts_forward(self, x, weights, experts):
         N, D = x.shape
         out = torch.zeros(N, D, dtype=torch.float32, device=x.device)
         flat_e = experts.reshape(-1)
         order = torch.argsort(flat_e, stable=True)
-        tok = order // self.top_k
         counts = torch.bincount(flat_e, minlength=self.num_experts)
-        lo, hi = self.expert_range
         starts = torch.cumsum(counts, 0) - counts
-        for e in range(lo, hi):
+        for e in range(self.num_experts):
             c = int(counts[e])
             if c == 0:
                 continue
             idx = order[int(starts[e]):int(starts[e]) + c]
-            t = tok[int(starts[e]):int(starts[e]) + c]
-            xe = x[t]
-            i = e - lo
-            h = F.silu(xe @ self.w_gate[i].t()) * (xe @ self.w_value[i].t())
-            ye = (h @ self.w_out[i].t()).float()
-            out.index_add_(0, t, ye * weights.reshape(-1)[idx, None].float())
+            t = idx // self.top_k
+            out.index_add_(0, t, self._expert(e, x[t]).float() * weights.reshape(-1)[idx, None].float())
         return out
 
-    def shared_forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self.shared_experts is None:
-            return torch.zeros_like(x, dtype=torch.float32)
-        g = F.softmax(self.shared_gate(x).float(), -1)
-        out = 0
-        for i, ex in enumerate(self.shared_experts):
-            out = out + g[:, i:i + 1] * ex(x).float()
+    def shared_forward(self, x, gates):
+        out = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
+        for s in range(self.num_shared_experts):
+            out = out + gates[:, s:s + 1] * self._expert(self.num_experts + s, x).float()
         return out
 
     def forward(self, x: torch.Tensor, return_metrics: bool = False) -> MoEOutput:
         shape = x.shape
         xf = x.reshape(-1, shape[-1])
-        w, e, p = self.router(xf)
+        w, e, p, g = self.route(xf)
         aux, counts = aux_load_balance_loss(p, e, self.num_experts)
-        self.router.update_bias(counts, xf.shape[0])
-        y = self.experts_forward(xf, w, e) + self.shared_forward(xf)
+        self.update_bias(counts, xf.shape[0])
+        y = self.experts_forward(xf, w, e)
+        if self.num_shared_experts:
+            y = y + self.shared_forward(xf, g)
         metrics = routing_metrics(p, w, e, counts, self.num_experts) if return_metrics else None
         return MoEOutput(y.to(x.dtype).view(shape), aux * self.aux_loss_weight, metrics)
 
     def get_load_balance_stats(self) -> Dict[str, float]:
-        r = self.router
         return {
-            "load_ema_std": float(r.expert_load_ema.std()),
-            "load_ema_max": float(r.expert_load_ema.max()),
-            "load_ema_min": float(r.expert_load_ema.min()),
-            "bias_std": float(r.expert_bias.std()),
-            "bias_max": float(r.expert_bias.max()),
-            "bias_min": float(r.expert_bias.min()),
+            "load_ema_std": float(self.expert_load_ema.std()),
+            "load_ema_max": float(self.expert_load_ema.max()),
+            "load_ema_min": float(self.expert_load_ema.min()),
+            "bias_std": float(self.expert_bias.std()),
+            "bias_max": float(self.expert_bias.max()),
+            "bias_min": float(self.expert_bias.min()),
         }

@@ -48,68 +48,107 @@ class BlockCtx:
         self.rope_pos_offset = rope_pos_offset
 
 
+def _attn_forward(x, mod, blk, W, bc):
+    d = bc.d
+    h1, r1 = adaln_rmsnorm(x, blk.norm1.weight, mod, 0, d, bc.tpf)
+    qkv = gemm(h1, W(blk.attn.qkv.weight), epi="rope", rope_tab=bc.rope_tab, rope_cols=2 * d,
+               rope_rows_per_seq=bc.T, rope_pos_offset=bc.rope_pos_offset, rope_head_dim=bc.Dh)
+    o, o_lin, lse, aux = attention_fwd(qkv, bc)
+    x1 = gemm(o, W(blk.attn.proj.weight), residual=x)
+    if o_lin is not None:
+        gemm(o_lin, W(blk.attn.proj_lin.weight), x1, residual=x1)
+    return x1, dict(x=x, h1=h1, r1=r1, qkv=qkv, o=o, o_lin=o_lin, lse=lse, aux=aux)
+
+
+def _attn_backward(dx1, sa, blk, W, bc, mod, dmod):
+    """Gradient of the block input given the gradient of the attention-residual output."""
+    d = bc.d
+    do = gemm(dx1, W(blk.attn.proj.weight), b_t=True)
+    gemm(dx1, sa["o"], blk.attn.proj.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+    do_lin = None
+    if sa["o_lin"] is not None:
+        do_lin = gemm(dx1, W(blk.attn.proj_lin.weight), b_t=True)
+        gemm(dx1, sa["o_lin"], blk.attn.proj_lin.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+    dqkv = attention_bwd(sa["qkv"], sa["o"], sa["lse"], do, do_lin, sa["aux"], bc)
+    # q, k gradients back through the rotation
+    rope_rotate_(dqkv, 2 * d, bc.rope_tab, bc.Dh, bc.T, bc.rope_pos_offset, inverse=True)
+    dh1 = gemm(dqkv, W(blk.attn.qkv.weight), b_t=True)
+    gemm(dqkv, sa["h1"], blk.attn.qkv.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+    return adaln_rmsnorm_bwd(dh1, sa["x"], sa["r1"], blk.norm1.weight, mod, 0, d, bc.tpf, dmod,
+                             blk.norm1.weight.grad, dx1)
+
+
+def _mlp_forward(x1, mod, blk, W, bc):
+    d = bc.d
+    h2, r2 = adaln_rmsnorm(x1, blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf)
+    w13 = W(blk.mlp.w13.weight)
+    gu = torch.empty(x1.shape[0], w13.shape[0], device=x1.device, dtype=torch.bfloat16)
+    a = torch.empty(x1.shape[0], w13.shape[0] // 2, device=x1.device, dtype=torch.bfloat16)
+    gemm(h2, w13, gu, epi="swiglu", out2=a)
+    x2 = gemm(a, W(blk.mlp.w3.weight), residual=x1)
+    return x2, dict(x1=x1, h2=h2, r2=r2, gu=gu, a=a)
+
+
+def _mlp_backward(dx2, sm, blk, W, bc, mod, dmod):
+    d = bc.d
+    dgu = gemm(dx2, W(blk.mlp.w3.weight), epi="dswiglu", b_t=True, residual=sm["gu"])
+    gemm(dx2, sm["a"], blk.mlp.w3.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+    dh2 = gemm(dgu, W(blk.mlp.w13.weight), b_t=True)
+    gemm(dgu, sm["h2"], blk.mlp.w13.weight.grad, epi="f32_acc", a_t=True, b_t=True)
+    del dgu
+    return adaln_rmsnorm_bwd(dh2, sm["x1"], sm["r2"], blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf,
+                             dmod, blk.norm2.weight.grad, dx2)
+
+
+def _moe_forward(x1, mod, blk, W, bc):
+    from .moe import moe_ffn_forward
+
+    d = bc.d
+    h2, r2 = adaln_rmsnorm(x1, blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf)
+    x2, aux, sv = moe_ffn_forward(h2, x1, blk.moe, W)
+    sv.update(x1=x1, r2=r2)
+    return x2, aux, sv
+
+
+def _moe_backward(dx2, d_aux, sv, blk, W, bc, mod, dmod):
+    from .moe import moe_ffn_backward
+
+    d = bc.d
+    dh2 = moe_ffn_backward(dx2, d_aux, blk.moe, W, sv)
+    return adaln_rmsnorm_bwd(dh2, sv["x1"], sv["r2"], blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf,
+                             dmod, blk.norm2.weight.grad, dx2)
+
+
 class _BlockFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx):
-        d = bc.d
-        W = group.compute_view
-        w_qkv = W(blk.attn.qkv.weight)
-        w_o = W(blk.attn.proj.weight)
-        w_13 = W(blk.mlp.w13.weight)
-        w_3 = W(blk.mlp.w3.weight)
-        n1 = blk.norm1.weight
-        n2 = blk.norm2.weight
-        h1, r1 = adaln_rmsnorm(x, n1, mod, 0, d, bc.tpf)
-        qkv = gemm(h1, w_qkv, epi="rope", rope_tab=bc.rope_tab, rope_cols=2 * d,
-                   rope_rows_per_seq=bc.T, rope_pos_offset=bc.rope_pos_offset,
-                   rope_head_dim=bc.Dh)
-        o, o_lin, lse, aux = attention_fwd(qkv, bc)
-        x1 = gemm(o, w_o, residual=x)
-        if o_lin is not None:
-            gemm(o_lin, W(blk.attn.proj_lin.weight), x1, residual=x1)
-        h2, r2 = adaln_rmsnorm(x1, n2, mod, 2 * d, 3 * d, bc.tpf)
-        gu = torch.empty(x.shape[0], w_13.shape[0], device=x.device, dtype=torch.bfloat16)
-        a = torch.empty(x.shape[0], w_13.shape[0] // 2, device=x.device, dtype=torch.bfloat16)
-        gemm(h2, w_13, gu, epi="swiglu", out2=a)
-        x2 = gemm(a, w_3, residual=x1)
-        ctx.save_for_backward(x, mod, h1, r1, qkv, o, lse, x1, h2, r2, gu, a,
-                              *([o_lin] if o_lin is not None else []))
-        ctx.blk, ctx.group, ctx.bc, ctx.aux = blk, group, bc, aux
-        return x2
+    """One dense (attention + SwiGLU) or MoE (attention + experts) block; returns
+    ``(x_out, aux_loss)`` where ``aux_loss`` is the unweighted MoE load-balance term."""
 
     @staticmethod
-    def backward(ctx, dx2):
-        saved = ctx.saved_tensors
-        x, mod, h1, r1, qkv, o, lse, x1, h2, r2, gu, a = saved[:12]
-        o_lin = saved[12] if len(saved) > 12 else None
-        blk, group, bc = ctx.blk, ctx.group, ctx.bc
-        d = bc.d
+    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx):
         W = group.compute_view
+        x1, sa = _attn_forward(x, mod, blk, W, bc)
+        if blk.moe is None:
+            x2, sm = _mlp_forward(x1, mod, blk, W, bc)
+            aux = torch.zeros((), device=x.device)
+        else:
+            x2, aux, sm = _moe_forward(x1, mod, blk, W, bc)
+        ctx.sa, ctx.sm, ctx.mod = sa, sm, mod
+        ctx.blk, ctx.group, ctx.bc = blk, group, bc
+        return x2, aux
+
+    @staticmethod
+    def backward(ctx, dx2, d_aux):
+        blk, bc, mod = ctx.blk, ctx.bc, ctx.mod
+        W = ctx.group.compute_view
         dx2 = dx2.contiguous()
-        # ---- MLP
-        dgu = gemm(dx2, W(blk.mlp.w3.weight), epi="dswiglu", b_t=True, residual=gu)
-        gemm(dx2, a, blk.mlp.w3.weight.grad, epi="f32_acc", a_t=True, b_t=True)
-        dh2 = gemm(dgu, W(blk.mlp.w13.weight), b_t=True)
-        gemm(dgu, h2, blk.mlp.w13.weight.grad, epi="f32_acc", a_t=True, b_t=True)
-        del dgu
         dmod = torch.zeros(mod.shape, device=mod.device, dtype=torch.float32)
-        dx1 = adaln_rmsnorm_bwd(dh2, x1, r2, blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf,
-                                dmod, blk.norm2.weight.grad, dx2)
-        del dh2
-        # ---- attention output projection(s)
-        do = gemm(dx1, W(blk.attn.proj.weight), b_t=True)
-        gemm(dx1, o, blk.attn.proj.weight.grad, epi="f32_acc", a_t=True, b_t=True)
-        do_lin = None
-        if o_lin is not None:
-            do_lin = gemm(dx1, W(blk.attn.proj_lin.weight), b_t=True)
-            gemm(dx1, o_lin, blk.attn.proj_lin.weight.grad, epi="f32_acc", a_t=True, b_t=True)
-        dqkv = attention_bwd(qkv, o, lse, do, do_lin, ctx.aux, bc)
-        # q, k gradients back through the rotation
-        rope_rotate_(dqkv, 2 * d, bc.rope_tab, bc.Dh, bc.T, bc.rope_pos_offset, inverse=True)
-        dh1 = gemm(dqkv, W(blk.attn.qkv.weight), b_t=True)
-        gemm(dqkv, h1, blk.attn.qkv.weight.grad, epi="f32_acc", a_t=True, b_t=True)
-        dx = adaln_rmsnorm_bwd(dh1, x, r1, blk.norm1.weight, mod, 0, d, bc.tpf, dmod,
-                               blk.norm1.weight.grad, dx1)
+        if blk.moe is None:
+            dx1 = _mlp_backward(dx2, ctx.sm, blk, W, bc, mod, dmod)
+        else:
+            # d_aux already carries the aux-loss weight (the caller scales the output)
+            dx1 = _moe_backward(dx2, d_aux, ctx.sm, blk, W, bc, mod, dmod)
+        dx = _attn_backward(dx1, ctx.sa, blk, W, bc, mod, dmod)
+        ctx.sa = ctx.sm = None
         return dx, dmod, None, None, None
 
 
@@ -119,9 +158,6 @@ class FusedWorldDiT:
     def __init__(self, model, group: Optional[FlatParamGroup] = None):
         self.model = model
         self.group = group if group is not None else FlatParamGroup(model.named_parameters())
-        for blk in model.blocks:
-            if blk.moe is not None:
-                raise NotImplementedError("MoE blocks run through drivedit_b200.ops.moe_block")
 
     def forward(self, model, x_t, t, actions, frame_offset=0, return_aux=False,
                 return_features=None):
@@ -141,9 +177,12 @@ class FusedWorldDiT:
         bc = BlockCtx(B, T, Fr, T // Fr, d, cfg.n_heads, cfg.d_head, tab, cfg.attention,
                       cfg.sla, cfg.causal)
         feats = None
+        aux = torch.zeros((), device=x.device)
         for i, blk in enumerate(model.blocks):
             mod = blk.ada(c2)                                      # [B*F, 4d] fp32
-            x = _BlockFn.apply(x, mod, blk, g, bc)
+            x, a = _BlockFn.apply(x, mod, blk, g, bc)
+            if blk.moe is not None:
+                aux = aux + a * blk.moe.aux_loss_weight
             if return_features is not None and i + 1 == return_features:
                 feats = x
         fm = model.final_ada(c2)
@@ -151,7 +190,6 @@ class FusedWorldDiT:
         out = linear(h, g.compute_view(model.out_proj.weight), model.out_proj.bias,
                      model.out_proj.weight, model.out_proj.bias)
         v = unpatchify(out.view(B, T, cfg.patch_dim), Fr, C, H, W_, cfg.patch)
-        aux = torch.zeros((), device=x.device)
         if return_features is not None:
             return v, aux, feats
         return (v, aux) if return_aux else v
