@@ -85,23 +85,36 @@ def moe_ffn_backward(dout: torch.Tensor, d_aux, moe, W, sv) -> torch.Tensor:
     g_w13 = moe.w13.grad.view(Ep * 2 * Fh, d)
     ext().gemm_grouped(dgu, sv["xp"], g_w13, EPI["f32_acc"], True, 2, *tables, None, None)
     dh = ext().moe_unpermute(dxp, sv["slot_of"], N)
-    # router: renormalised top-k softmax (+ aux loss), shared-gate softmax
-    p, idx, w = sv["probs"], sv["idx"].long(), sv["w"]
-    dwr = dw[:, :k]
-    ptop = torch.gather(p, 1, idx)
-    stop = ptop.sum(-1, keepdim=True)
-    dptop = (dwr - (dwr * w).sum(-1, keepdim=True)) / (stop + 1e-8)
-    dp = torch.zeros_like(p).scatter_(1, idx, dptop)
-    if d_aux is not None:  # a 0-dim device tensor: no host synchronisation
-        dp = dp + d_aux.float() * (E / N) * sv["f"][None, :]
-    dz = p * (dp - (p * dp).sum(-1, keepdim=True))
-    dlog = torch.zeros(N, moe.e_pad, device=h.device, dtype=torch.float32)
-    dlog[:, :E] = dz
-    if ns:
-        g = sv["sw"][:, :ns]
-        dws = dw[:, k:]
-        dlog[:, E:E + ns] = g * (dws - (g * dws).sum(-1, keepdim=True))
+    dlog = router_dlogits(sv["probs"], sv["idx"], sv["w"], sv["sw"], dw, d_aux, sv["f"],
+                          E, k, ns, moe.e_pad)
     dlog = dlog.to(torch.bfloat16)
     gemm(dlog, h, moe.router_weight.grad, epi="f32_acc", a_t=True, b_t=True)
     gemm(dlog, W(moe.router_weight), dh, b_t=True, residual=dh)
     return dh
+
+
+def router_dlogits(p, idx, w, sw, dw, d_aux, f, E: int, k: int, ns: int, e_pad: int):
+    """Gradient of the loss w.r.t. the router logits ``[N, e_pad]`` (fp32).
+
+    ``dw [N, k+ns]`` is the gradient w.r.t. the combine weights (renormalised top-k
+    gates, then shared gates). The routed part goes back through the top-k
+    renormalisation ``w_j = p_j / sum_top p`` and ``p = softmax(logits + bias)``; the aux
+    load-balance loss ``E * sum_e f_e mean_n p_ne`` adds ``d_aux * E/N * f`` to ``dp``
+    (``f`` is a count share, not differentiated); shared gates are a plain softmax.
+    """
+    N = p.shape[0]
+    idx = idx.long()
+    dwr = dw[:, :k].float()
+    stop = torch.gather(p, 1, idx).sum(-1, keepdim=True)
+    dptop = (dwr - (dwr * w).sum(-1, keepdim=True)) / (stop + 1e-8)
+    dp = torch.zeros_like(p).scatter_(1, idx, dptop)
+    if d_aux is not None:  # a 0-dim device tensor: no host synchronisation
+        dp = dp + d_aux.float() * (E / N) * f[None, :]
+    dz = p * (dp - (p * dp).sum(-1, keepdim=True))
+    dlog = torch.zeros(N, e_pad, device=p.device, dtype=torch.float32)
+    dlog[:, :E] = dz
+    if ns:
+        g = sw[:, :ns].float()
+        dws = dw[:, k:].float()
+        dlog[:, E:E + ns] = g * (dws - (g * dws).sum(-1, keepdim=True))
+    return dlog

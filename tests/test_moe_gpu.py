@@ -9,6 +9,10 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
 
 
+def _frob(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
 def test_grouped_gemm_matches_per_expert():
     from drivedit_b200.ops._ext import ext
     from drivedit_b200.ops.gemm import EPI
@@ -54,8 +58,8 @@ def test_moe_world_model_fused_matches_torch():
         for n, p in m_ref.named_parameters():
             if p.abs().sum() == 0 and "router_weight" not in n:
                 p.normal_(0, 0.02)
-            if "router_weight" in n:  # well-separated routing: no top-k ties between paths
-                p.mul_(50.0)
+            if "router_weight" in n:  # wider logits: few near-ties between the two paths
+                p.mul_(10.0)
     m = WorldDiT(cfg.model).cuda()
     m.load_state_dict(m_ref.state_dict())
     group = FlatParamGroup(m.named_parameters(), "cuda")
@@ -66,7 +70,7 @@ def test_moe_world_model_fused_matches_torch():
     m_ref.train(); m.train()
     v_ref, aux_ref = m_ref(x, t, a, return_aux=True)
     v, aux = m(x.bfloat16(), t, a, return_aux=True)
-    assert _rel(v, v_ref) < 5e-2
+    assert _frob(v, v_ref) < 3e-2
     assert abs(float(aux) - float(aux_ref)) < 1e-3 * max(1.0, abs(float(aux_ref)))
     dv = torch.randn_like(v_ref)
     (v_ref.float() * dv).sum().add(aux_ref).backward()
@@ -79,7 +83,9 @@ def test_moe_world_model_fused_matches_torch():
         g = ref[n].grad
         if g is None or g.abs().max() == 0:
             continue
-        r = _rel(p.grad, g)
-        if r > 8e-2:
+        # Frobenius-relative: a bf16 rounding that flips one token's k-th expert moves
+        # that token's gradients only
+        r = _frob(p.grad, g)
+        if r > 5e-2:
             bad[n] = r
     assert not bad, bad
