@@ -12,6 +12,8 @@
 #include "attn/sla.h"
 #include "comm/comm.h"
 #include "moe/moe.h"
+#include "vae/conv3d.h"
+#include "vae/groupnorm.h"
 
 namespace {
 
@@ -779,10 +781,119 @@ torch::Tensor moe_unpermute(torch::Tensor dxp, torch::Tensor slot_of, int64_t N)
   return dx;
 }
 
+
+// ---------------------------------------------------------------- video VAE
+void check_cl5(const torch::Tensor& t, const char* name) {
+  check_bf16(t, name);
+  TORCH_CHECK(t.dim() == 5 && t.is_contiguous(), name, " must be a contiguous [B,T,H,W,C] tensor");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+// y[B,To,Ho,Wo,Cout] = conv(x[B,T,H,W,Cin], w[Cout, kt*kh*kw*Cin]) (+bias) (+residual)
+void conv3d_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y, int64_t kt, int64_t kh,
+                int64_t kw, int64_t pt, int64_t ph, int64_t pw,
+                c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual) {
+  check_cl5(x, "x");
+  check_cl5(y, "y");
+  check_bf16(w, "w");
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "w must be contiguous [Cout, K]");
+  const int64_t Cin = x.size(4), Cout = y.size(4);
+  TORCH_CHECK(w.size(0) == Cout && w.size(1) == kt * kh * kw * Cin, "w shape");
+  TORCH_CHECK(y.size(0) == x.size(0), "batch");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ddb::Conv3dArgs a;
+  a.x = x.data_ptr(); a.B = x.size(0); a.T = x.size(1); a.H = x.size(2); a.W = x.size(3);
+  a.Cin = Cin; a.To = y.size(1); a.Ho = y.size(2); a.Wo = y.size(3); a.Cout = Cout;
+  a.kt = kt; a.kh = kh; a.kw = kw; a.pt = pt; a.ph = ph; a.pw = pw;
+  a.w = w.data_ptr(); a.y = y.data_ptr();
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() == Cout &&
+                bias->is_contiguous(), "bias must be fp32 [Cout]");
+    a.bias = bias->data_ptr<float>();
+  }
+  if (residual) {
+    check_cl5(*residual, "residual");
+    TORCH_CHECK(residual->sizes() == y.sizes(), "residual shape");
+    a.residual = residual->data_ptr();
+  }
+  ddb::conv3d_fwd(a, stream());
+}
+
+// dw[Cout, kt*kh*kw*Cin] (fp32) += weight gradient of conv(x) given dy
+void conv3d_wgrad(torch::Tensor x, torch::Tensor dy, torch::Tensor dw, int64_t kt, int64_t kh,
+                  int64_t kw, int64_t pt, int64_t ph, int64_t pw, int64_t splits) {
+  check_cl5(x, "x");
+  check_cl5(dy, "dy");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous() && dw.dim() == 2,
+              "dw must be contiguous fp32 [Cout, K]");
+  const int64_t Cin = x.size(4), Cout = dy.size(4);
+  TORCH_CHECK(dw.size(0) == Cout && dw.size(1) == kt * kh * kw * Cin, "dw shape");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ddb::Conv3dArgs a;
+  a.x = x.data_ptr(); a.B = x.size(0); a.T = x.size(1); a.H = x.size(2); a.W = x.size(3);
+  a.Cin = Cin; a.To = dy.size(1); a.Ho = dy.size(2); a.Wo = dy.size(3); a.Cout = Cout;
+  a.kt = kt; a.kh = kh; a.kw = kw; a.pt = pt; a.ph = ph; a.pw = pw;
+  a.dy = dy.data_ptr(); a.dw = dw.data_ptr<float>(); a.splits = splits;
+  ddb::conv3d_wgrad(a, stream());
+}
+
+// GroupNorm(+SiLU) over x[B, P, C] -> (y, stats[B,G,2])
+std::vector<torch::Tensor> groupnorm_fwd(torch::Tensor x, torch::Tensor w,
+                                         c10::optional<torch::Tensor> b, int64_t G, double eps,
+                                         bool silu) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x must be contiguous [B, P, C]");
+  const int64_t B = x.size(0), P = x.size(1), C = x.size(2);
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.numel() == C && w.is_contiguous(), "w");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  auto stats = torch::empty({B, G, 2}, x.options().dtype(torch::kFloat32));
+  auto acc = torch::empty({B, C, 2}, x.options().dtype(torch::kFloat64));
+  ddb::GroupNormArgs a;
+  a.B = B; a.P = P; a.C = C; a.G = G; a.eps = static_cast<float>(eps); a.silu = silu;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()); a.w = w.data_ptr<float>();
+  if (b) {
+    TORCH_CHECK(b->scalar_type() == torch::kFloat32 && b->numel() == C && b->is_contiguous(), "b");
+    a.b = b->data_ptr<float>();
+  }
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.stats = stats.data_ptr<float>(); a.acc = acc.data_ptr<double>();
+  ddb::groupnorm_fwd(a, stream());
+  return {y, stats};
+}
+
+// -> (dx, per-sample channel sums [B, C, 2] = (sum dpre, sum dpre*xhat)) in fp64
+std::vector<torch::Tensor> groupnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w,
+                                         c10::optional<torch::Tensor> b, torch::Tensor stats,
+                                         bool silu) {
+  check_bf16(x, "x");
+  check_bf16(dy, "dy");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous() && dy.is_contiguous() && dy.sizes() == x.sizes(),
+              "x/dy must be contiguous [B, P, C]");
+  const int64_t B = x.size(0), P = x.size(1), C = x.size(2), G = stats.size(1);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dx = torch::empty_like(x);
+  auto acc = torch::empty({B, C, 2}, x.options().dtype(torch::kFloat64));
+  auto coef = torch::empty({B, G, 2}, x.options().dtype(torch::kFloat32));
+  ddb::GroupNormArgs a;
+  a.B = B; a.P = P; a.C = C; a.G = G; a.silu = silu;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()); a.w = w.data_ptr<float>();
+  if (b) a.b = b->data_ptr<float>();
+  a.stats = stats.data_ptr<float>(); a.acc = acc.data_ptr<double>(); a.coef = coef.data_ptr<float>();
+  a.dy = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  a.dx = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  ddb::groupnorm_bwd(a, stream());
+  return {dx, acc};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "drivedit_b200 sm_100a kernels";
+  m.def("conv3d_fwd", &conv3d_fwd, "causal 3-D conv (channels-last implicit GEMM, tcgen05)");
+  m.def("conv3d_wgrad", &conv3d_wgrad, "causal 3-D conv weight gradient (fp32 accumulate)");
+  m.def("groupnorm_fwd", &groupnorm_fwd, "GroupNorm(+SiLU) forward -> (y, stats)");
+  m.def("groupnorm_bwd", &groupnorm_bwd, "GroupNorm(+SiLU) backward -> (dx, channel sums)");
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
   m.def("read_status", &read_status, "device status word (0 = ok)");
   m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");

@@ -76,6 +76,38 @@ CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int elem_b
   return m;
 }
 
+CUtensorMap make_tmap_nd(const void* base, CUtensorMapDataType dtype, int elem_bytes, int rank,
+                         const uint64_t* dims, const uint64_t* strides_bytes,
+                         const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  if (rank < 1 || rank > 5) throw std::runtime_error("TMA rank must be 1..5");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    throw std::runtime_error("TMA base address must be 16-byte aligned");
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides_bytes[i] % 16 != 0)
+      throw std::runtime_error("TMA strides must be multiples of 16 bytes");
+  if ((box[0] * elem_bytes) % 16 != 0)
+    throw std::runtime_error("TMA box inner extent must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t b[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    estr[i] = 1;
+    if (box[i] < 1 || box[i] > 256) throw std::runtime_error("TMA box dims must be 1..256");
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+  CUresult r = encode_fn()(&m, dtype, rank, const_cast<void*>(base), d, st, b, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled (rank " + std::to_string(rank) +
+                             ") failed with code " + std::to_string(static_cast<int>(r)));
+  return m;
+}
+
 namespace {
 std::atomic<long> g_launches{0};
 }

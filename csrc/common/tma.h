@@ -22,6 +22,12 @@ CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int elem_b
                          uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2,
                          CUtensorMapSwizzle swizzle);
 
+// Tensor map of rank 1..5: dims[0] contiguous, strides_bytes[i] is the byte stride of
+// dims[i+1]. Out-of-range box elements read as zero.
+CUtensorMap make_tmap_nd(const void* base, CUtensorMapDataType dtype, int elem_bytes, int rank,
+                         const uint64_t* dims, const uint64_t* strides_bytes,
+                         const uint32_t* box, CUtensorMapSwizzle swizzle);
+
 int num_sms(int device);
 
 // Number of kernels this extension has launched in the process (for launch accounting).

@@ -46,10 +46,12 @@ GEMM_SHAPES = [
 ]
 
 
-def bench_gemm(iters: int = 20):
+def bench_gemm(iters: int = 20, shapes=None):
     from .gemm import gemm
 
     for name, M, N, K, a_t, b_t, epi in GEMM_SHAPES:
+        if shapes and name not in shapes:
+            continue
         a = torch.randn(*((K, M) if a_t else (M, K)), device="cuda", dtype=torch.bfloat16)
         b = torch.randn(*((K, N) if b_t else (N, K)), device="cuda", dtype=torch.bfloat16)
         kw = {}
@@ -113,17 +115,49 @@ def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int
                       "tflops": round(f_bwd / ms_b / 1e9, 1), "debug_flags": dbg}), flush=True)
 
 
+def bench_conv3d(iters: int = 10):
+    """VAE causal 3x3x3 convolutions at 8 frames of 256x512 RGB (encoder level 0,
+    128 ch, and level 2, 512 ch at 65x129), stride-2 downsample, vs cuDNN."""
+    import torch.nn.functional as F
+
+    from .conv3d import causal_conv3d
+
+    shapes = [("enc_l0_res", 1, 128, 128, 8, 256, 512, (3, 3, 3), (1, 1, 1)),
+              ("enc_l2_res", 1, 512, 512, 2, 65, 129, (3, 3, 3), (1, 1, 1)),
+              ("enc_down0", 1, 128, 128, 8, 256, 512, (4, 4, 4), (2, 2, 2))]
+    for name, B, Cin, Cout, T, H, W, k, st in shapes:
+        x = torch.randn(B, Cin, T, H, W, device="cuda").bfloat16()
+        x = x.contiguous(memory_format=torch.channels_last_3d)
+        w = torch.randn(Cout, Cin, *k, device="cuda") * 0.02
+        b = torch.zeros(Cout, device="cuda")
+        y = causal_conv3d(x, w, b, st)
+        ms = _timeit(lambda: causal_conv3d(x, w, b, st), iters)
+        wb = w.bfloat16().contiguous(memory_format=torch.channels_last_3d)
+        xp = F.pad(x, (0, 0, 0, 0, k[0] - 1, 0))
+        ms_ref = _timeit(lambda: F.conv3d(xp, wb, None, st, (0, k[1] // 2, k[2] // 2)), iters)
+        flops = 2.0 * y.numel() * Cin * k[0] * k[1] * k[2]
+        print(json.dumps({"kernel": "conv3d_tc", "shape": name, "ms": round(ms, 4),
+                          "tflops": round(flops / ms / 1e9, 1), "cudnn_ms": round(ms_ref, 4),
+                          "cudnn_tflops": round(flops / ms_ref / 1e9, 1)}), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("what", nargs="*", default=["gemm"])
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--small", action="store_true", help="small attention case (for ncu)")
+    p.add_argument("--B", type=int, default=8, help="attention batch")
+    p.add_argument("--shape", nargs="*", help="gemm shapes to run (names in GEMM_SHAPES)")
     args = p.parse_args()
     for w in args.what:
         if w == "attn" and args.small:
             bench_attn(args.iters, B=1, H=2, T=8192)
+        elif w == "attn":
+            bench_attn(args.iters, B=args.B)
         elif w == "attn_nodq":  # timing experiment: backward without the dQ reductions
             bench_attn(args.iters, dbg=1)
+        elif w == "gemm":
+            bench_gemm(args.iters, args.shape)
         else:
             globals()[f"bench_{w}"](args.iters)
     from ._ext import check_device_status

