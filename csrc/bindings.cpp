@@ -886,6 +886,64 @@ std::vector<torch::Tensor> groupnorm_bwd(torch::Tensor dy, torch::Tensor x, torc
   return {dx, acc};
 }
 
+
+// LayerNorm over rows: -> (y, mean, rstd)
+std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w,
+                                         c10::optional<torch::Tensor> b, double eps) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous(), "x must be contiguous [M, D]");
+  const int64_t M = x.size(0), D = x.size(1);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  auto mean = torch::empty({M}, x.options().dtype(torch::kFloat32));
+  auto rstd = torch::empty({M}, x.options().dtype(torch::kFloat32));
+  ddb::LayerNormArgs a;
+  a.M = M; a.D = D; a.eps = static_cast<float>(eps);
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  if (w) {
+    TORCH_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == D && w->is_contiguous(), "w");
+    a.w = w->data_ptr<float>();
+  }
+  if (b) {
+    TORCH_CHECK(b->scalar_type() == torch::kFloat32 && b->numel() == D && b->is_contiguous(), "b");
+    a.b = b->data_ptr<float>();
+  }
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.mean = mean.data_ptr<float>(); a.rstd = rstd.data_ptr<float>();
+  ddb::layernorm_fwd(a, stream());
+  return {y, mean, rstd};
+}
+
+// -> dx; accumulates dw / db (fp32, optional)
+torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor mean,
+                            torch::Tensor rstd, c10::optional<torch::Tensor> w,
+                            c10::optional<torch::Tensor> dw, c10::optional<torch::Tensor> db) {
+  check_bf16(dy, "dy");
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && dy.is_contiguous() && dy.sizes() == x.sizes(),
+              "x / dy must be contiguous [M, D]");
+  const int64_t M = x.size(0), D = x.size(1);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dx = torch::empty_like(x);
+  ddb::LayerNormArgs a;
+  a.M = M; a.D = D;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.dy = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  a.dx = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  a.mean = mean.data_ptr<float>(); a.rstd = rstd.data_ptr<float>();
+  if (w) a.w = w->data_ptr<float>();
+  if (dw) {
+    TORCH_CHECK(dw->scalar_type() == torch::kFloat32 && dw->numel() == D && dw->is_contiguous(), "dw");
+    a.dw = dw->data_ptr<float>();
+  }
+  if (db) {
+    TORCH_CHECK(db->scalar_type() == torch::kFloat32 && db->numel() == D && db->is_contiguous(), "db");
+    a.db = db->data_ptr<float>();
+  }
+  ddb::layernorm_bwd(a, stream());
+  return dx;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -894,6 +952,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv3d_wgrad", &conv3d_wgrad, "causal 3-D conv weight gradient (fp32 accumulate)");
   m.def("groupnorm_fwd", &groupnorm_fwd, "GroupNorm(+SiLU) forward -> (y, stats)");
   m.def("groupnorm_bwd", &groupnorm_bwd, "GroupNorm(+SiLU) backward -> (dx, channel sums)");
+  m.def("layernorm_fwd", &layernorm_fwd, "LayerNorm forward -> (y, mean, rstd)");
+  m.def("layernorm_bwd", &layernorm_bwd, "LayerNorm backward -> dx (accumulates dw, db)");
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
   m.def("read_status", &read_status, "device status word (0 = ok)");
   m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");

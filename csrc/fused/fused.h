@@ -25,6 +25,24 @@ struct AdaLNArgs {
   long ld_dmod = 0;
 };
 
+struct LayerNormArgs {
+  long M = 0;
+  int D = 0;
+  float eps = 1e-5f;
+  const __nv_bfloat16* x = nullptr;
+  const float* w = nullptr;  // [D] or null
+  const float* b = nullptr;  // [D] or null
+  __nv_bfloat16* y = nullptr;
+  float* mean = nullptr;     // [M] fwd output / bwd input
+  float* rstd = nullptr;     // [M]
+  const __nv_bfloat16* dy = nullptr;
+  __nv_bfloat16* dx = nullptr;
+  float* dw = nullptr;       // += sum dy * xhat (may be null)
+  float* db = nullptr;       // += sum dy (may be null)
+};
+void layernorm_fwd(const LayerNormArgs& a, cudaStream_t s);
+void layernorm_bwd(const LayerNormArgs& a, cudaStream_t s);
+
 void adaln_rmsnorm_fwd(const AdaLNArgs& a, cudaStream_t s);
 void adaln_rmsnorm_bwd(const AdaLNArgs& a, cudaStream_t s);
 

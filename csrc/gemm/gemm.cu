@@ -151,6 +151,10 @@ __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0
           }
         }
       }
+      if constexpr (EPI == kEpiGelu) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.5f * v[i] * (1.f + erff(v[i] * 0.70710678118654752f));
+      }
       if (a.C != nullptr && (EPI == kEpiBf16 || EPI == kEpiGateResidual)) {
         const __nv_bfloat16* c =
             reinterpret_cast<const __nv_bfloat16*>(a.C) + static_cast<long>(row) * a.ldc + col0;
@@ -541,6 +545,9 @@ void dispatch_bn(const GemmArgs& a, int epi, const Sched& s, int grid, cudaStrea
       break;
     case kEpiGateResidual:
       if (mode == 0) return launch<BN, false, false, kEpiGateResidual>(a, s, grid, st, status);
+      break;
+    case kEpiGelu:
+      if (mode == 0) return launch<BN, false, false, kEpiGelu>(a, s, grid, st, status);
       break;
     default:
       break;

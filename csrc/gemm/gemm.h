@@ -12,7 +12,8 @@ enum GemmEpilogue : int {
   kEpiSwiGLU = 3,      // D(bf16) = acc (gate/up interleaved by 32), D2(bf16) = silu(g)*u
   kEpiDSwiGLU = 4,     // acc = dA; C = gu (bf16); D(bf16) = d(gu) in gu's layout
   kEpiRope = 5,        // D(bf16) = acc with rotary pairs applied to columns < rope_cols
-  kEpiGateResidual = 6 // D(bf16) = C + gate[row_group, n] * acc (AdaLN-Zero residual)
+  kEpiGateResidual = 6, // D(bf16) = C + gate[row_group, n] * acc (AdaLN-Zero residual)
+  kEpiGelu = 7          // D(bf16) = gelu(acc + bias[n]) (erf form)
 };
 
 struct GemmArgs {

@@ -36,16 +36,23 @@
 namespace ddb {
 namespace {
 
-constexpr int BM = 128;
+constexpr int BM = 128;  // rows of one MMA (one M sub-tile)
 constexpr int BN = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
-constexpr int STAGES = 6;
-constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+// MT M sub-tiles (128 rows each) share every B tile: MT = 2 halves the shared-memory
+// fill traffic per FLOP (48 KB per 2 x 128x128x64 MMAs instead of 32 KB per one), which
+// is what keeps the tensor pipe fed from L2 at 128-wide N.
+template <int MT>
+struct ConvCfg {
+  static constexpr int A_BYTES = MT * BM * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = MT == 2 ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * MT * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
 
 struct ConvSched {
   int tiles_n, tiles_m, total;
@@ -81,13 +88,18 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
-template <bool WG>
+template <bool WG, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const Conv3dArgs args,
                      const ConvSched sched, int* status) {
   // forward: A = input patch (K-major), B = weights (K-major)
   // wgrad:   A = dy patch (MN-major over cout), B = input patch (MN-major over cin)
+  using Cfg = ConvCfg<MT>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int A_BYTES = Cfg::A_BYTES;
+  constexpr int STAGE_BYTES = Cfg::STAGE_BYTES;
+  constexpr int TMEM_COLS = Cfg::TMEM_COLS;
   constexpr uint32_t IDESC = make_idesc_bf16(BM, BN, WG, WG);
 
   extern __shared__ uint8_t smem_raw[];
@@ -167,9 +179,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sb, &tmB, &full[stage], kb * BK, ni * BN);
           } else {
             sched.pos(kb, b, to, h0, w0);
-            const int m0 = mi * BM;
-            tma_load_5d(sa, &tmA, &full[stage], m0, w0, h0, to, b);
-            tma_load_5d(sa + 8192, &tmA, &full[stage], m0 + 64, w0, h0, to, b);
+            const int m0 = mi * BM * MT;
+#pragma unroll
+            for (int c = 0; c < 2 * MT; ++c)
+              tma_load_5d(sa + c * 8192, &tmA, &full[stage], m0 + 64 * c, w0, h0, to, b);
             tma_load_5d(sb, &tmB, &full[stage], c0, w0 + dw - args.pw, h0 + dh - args.ph,
                         to + dt - args.pt, b);
             tma_load_5d(sb + 8192, &tmB, &full[stage], c0 + 64, w0 + dw - args.pw,
@@ -214,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * MT * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
@@ -225,11 +238,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            uint64_t da = WG ? make_sw128_desc(sa + kk * 2048, 8192, 1024)
-                             : make_sw128_desc(sa + kk * 32, 16, 1024);
             uint64_t db = WG ? make_sw128_desc(sb + kk * 2048, 8192, 1024)
                              : make_sw128_desc(sb + kk * 32, 16, 1024);
-            mma_bf16_ss(d_tmem, da, db, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              // sub-tile mt: rows [128 mt, 128 mt + 128) of the A tile (16 KB apart)
+              const uint32_t am = sa + mt * (BM * BK * 2);
+              uint64_t da = WG ? make_sw128_desc(am + kk * 2048, 8192, 1024)
+                               : make_sw128_desc(am + kk * 32, 16, 1024);
+              mma_bf16_ss(d_tmem + mt * BN, da, db, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
           }
           any = true;
           mma_commit(&empty[stage]);
@@ -271,77 +289,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
-      if constexpr (!WG) {
-        int b, to, h0, w0;
-        sched.pos(mi, b, to, h0, w0);
-        const int h = h0 + r / sched.wbox;
-        const int w = w0 + r % sched.wbox;
-        const bool row_ok = h < args.Ho && w < args.Wo;
-        const long orow = ((static_cast<long>(b) * args.To + to) * args.Ho + h) * args.Wo + w;
-        const int n0 = ni * BN;
-        const bool vec_ok = (args.Cout & 7) == 0;
+      const uint32_t tlane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * MT * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t rr[32];
-          tmem_ld32(tbase + c, rr);
-          tmem_wait_ld();
-          const int col0 = n0 + c;
-          if (!row_ok || col0 >= args.Cout) continue;
-          float v[32];
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint32_t tbase = tlane + mt * BN;
+        const int rr_row = mt * BM + r;  // row within the MT*128-row tile
+        if constexpr (!WG) {
+          int b, to, h0, w0;
+          sched.pos(mi, b, to, h0, w0);
+          const int h = h0 + rr_row / sched.wbox;
+          const int w = w0 + rr_row % sched.wbox;
+          const bool row_ok = h < args.Ho && w < args.Wo;
+          const long orow = ((static_cast<long>(b) * args.To + to) * args.Ho + h) * args.Wo + w;
+          const int n0 = ni * BN;
+          const bool vec_ok = (args.Cout & 7) == 0;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t rr[32];
+            tmem_ld32(tbase + c, rr);
+            tmem_wait_ld();
+            const int col0 = n0 + c;
+            if (!row_ok || col0 >= args.Cout) continue;
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rr[i]);
-          const int ncol = min(32, args.Cout - col0);
-          if (args.bias != nullptr)
-            for (int i = 0; i < ncol; ++i) v[i] += __ldg(args.bias + col0 + i);
-          __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.y) + orow * args.Cout + col0;
-          const __nv_bfloat16* res =
-              args.residual == nullptr
-                  ? nullptr
-                  : reinterpret_cast<const __nv_bfloat16*>(args.residual) + orow * args.Cout + col0;
-          if (vec_ok && ncol == 32) {
-            if (res != nullptr) {
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rr[i]);
+            const int ncol = min(32, args.Cout - col0);
+            if (args.bias != nullptr)
+              for (int i = 0; i < ncol; ++i) v[i] += __ldg(args.bias + col0 + i);
+            __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.y) + orow * args.Cout + col0;
+            const __nv_bfloat16* res =
+                args.residual == nullptr
+                    ? nullptr
+                    : reinterpret_cast<const __nv_bfloat16*>(args.residual) + orow * args.Cout + col0;
+            if (vec_ok && ncol == 32) {
+              if (res != nullptr) {
 #pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 cv = ld_global_v4(res + i);
-                uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+                for (int i = 0; i < 32; i += 8) {
+                  uint4 cv = ld_global_v4(res + i);
+                  uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  float2 f = unpack_bf16(cw[j]);
-                  v[i + 2 * j] += f.x;
-                  v[i + 2 * j + 1] += f.y;
+                  for (int j = 0; j < 4; ++j) {
+                    float2 f = unpack_bf16(cw[j]);
+                    v[i + 2 * j] += f.x;
+                    v[i + 2 * j + 1] += f.y;
+                  }
                 }
               }
-            }
 #pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              st_global_v4(y + i, pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
-                           pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
-          } else {
-            for (int i = 0; i < ncol; ++i) {
-              float o = v[i];
-              if (res != nullptr) o += __bfloat162float(res[i]);
-              y[i] = __float2bfloat16(o);
+              for (int i = 0; i < 32; i += 8)
+                st_global_v4(y + i, pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
+                             pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
+            } else {
+              for (int i = 0; i < ncol; ++i) {
+                float o = v[i];
+                if (res != nullptr) o += __bfloat162float(res[i]);
+                y[i] = __float2bfloat16(o);
+              }
             }
           }
-        }
-      } else {
-        // dw[cout = m0 + r, tap * Cin + c0 + col]
-        const int tap = ni / sched.cchunks;
-        const int c0 = (ni % sched.cchunks) * 128;
-        const int row = mi * BM + r;
-        const int K = sched.kw * sched.kh * (args.kt) * args.Cin;
+        } else {
+          // dw[cout = m0 + row, tap * Cin + c0 + col]
+          const int tap = ni / sched.cchunks;
+          const int c0 = (ni % sched.cchunks) * 128;
+          const int row = mi * BM * MT + rr_row;
+          const long K = static_cast<long>(sched.kw) * sched.kh * args.kt * args.Cin;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t rr[32];
-          tmem_ld32(tbase + c, rr);
-          tmem_wait_ld();
-          if (row >= args.Cout || c0 + c >= args.Cin) continue;
-          float* d = args.dw + static_cast<long>(row) * K + static_cast<long>(tap) * args.Cin + c0 + c;
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t rr[32];
+            tmem_ld32(tbase + c, rr);
+            tmem_wait_ld();
+            if (row >= args.Cout || c0 + c >= args.Cin) continue;
+            float* d = args.dw + row * K + static_cast<long>(tap) * args.Cin + c0 + c;
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            red_add_v4_f32(d + i, __uint_as_float(rr[i]), __uint_as_float(rr[i + 1]),
-                           __uint_as_float(rr[i + 2]), __uint_as_float(rr[i + 3]));
+            for (int i = 0; i < 32; i += 4)
+              red_add_v4_f32(d + i, __uint_as_float(rr[i]), __uint_as_float(rr[i + 1]),
+                             __uint_as_float(rr[i + 2]), __uint_as_float(rr[i + 3]));
+          }
         }
       }
       tc_fence_before();
@@ -362,12 +385,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// patch geometry: wbox * hbox = positions per tile, wbox a power of two covering as much
-// of a row as possible
-void patch_dims(int Wo, int positions, int& wbox, int& hbox) {
-  wbox = positions;
-  while (wbox > 8 && wbox / 2 >= Wo) wbox /= 2;
-  hbox = positions / wbox;
+// patch geometry: wbox * hbox = positions per tile (wbox a power of two, 8..256, hbox
+// <= 256), chosen to minimise the padded output area ceil(Wo/wbox)*wbox *
+// ceil(Ho/hbox)*hbox; ties go to the wider patch (longer contiguous TMA rows)
+void patch_dims(int Wo, int Ho, int positions, int& wbox, int& hbox) {
+  long best = -1;
+  for (int wb = std::min(positions, 256); wb >= 8; wb /= 2) {
+    const int hb = positions / wb;
+    if (hb > 256) break;
+    const long area = static_cast<long>((Wo + wb - 1) / wb) * wb * ((Ho + hb - 1) / hb) * hb;
+    if (best < 0 || area < best) {
+      best = area;
+      wbox = wb;
+      hbox = hb;
+    }
+  }
 }
 
 CUtensorMap act_map(const void* base, int B, int T, int H, int W, int C, int wbox, int hbox) {
@@ -383,11 +415,12 @@ CUtensorMap act_map(const void* base, int B, int T, int H, int W, int C, int wbo
                       CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <bool WG>
+template <bool WG, int MT>
 void launch(const CUtensorMap& tA, const CUtensorMap& tB, const Conv3dArgs& a,
             const ConvSched& s, cudaStream_t stream) {
   static bool attr_set = false;
-  auto kern = conv3d_tc_kernel<WG>;
+  constexpr int SMEM_BYTES = ConvCfg<MT>::SMEM_BYTES;
+  auto kern = conv3d_tc_kernel<WG, MT>;
   if (!attr_set) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     SMEM_BYTES),
@@ -418,7 +451,8 @@ void conv3d_fwd(const Conv3dArgs& a, cudaStream_t stream) {
   if (a.x == nullptr || a.w == nullptr || a.y == nullptr)
     throw std::runtime_error("conv3d_fwd: null operand");
   ConvSched s{};
-  patch_dims(a.Wo, BM, s.wbox, s.hbox);
+  constexpr int MT = 2;
+  patch_dims(a.Wo, a.Ho, BM * MT, s.wbox, s.hbox);
   s.tiles_w = (a.Wo + s.wbox - 1) / s.wbox;
   s.tiles_h = (a.Ho + s.hbox - 1) / s.hbox;
   s.To = a.To;
@@ -435,7 +469,7 @@ void conv3d_fwd(const Conv3dArgs& a, cudaStream_t stream) {
   const long K = static_cast<long>(a.kt) * a.kh * a.kw * a.Cin;
   const CUtensorMap tB = make_tmap_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, a.Cout,
                                       K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
-  launch<false>(tA, tB, a, s, stream);
+  launch<false, MT>(tA, tB, a, s, stream);
 }
 
 void conv3d_wgrad(const Conv3dArgs& a, cudaStream_t stream) {
@@ -445,11 +479,12 @@ void conv3d_wgrad(const Conv3dArgs& a, cudaStream_t stream) {
   if (a.Cin % 128 != 0 || a.Cout % 64 != 0)
     throw std::runtime_error("conv3d_wgrad: needs Cin % 128 == 0 and Cout % 64 == 0");
   ConvSched s{};
-  patch_dims(a.Wo, BK, s.wbox, s.hbox);
+  patch_dims(a.Wo, a.Ho, BK, s.wbox, s.hbox);
+  const int MT = a.Cout >= 256 ? 2 : 1;
   s.tiles_w = (a.Wo + s.wbox - 1) / s.wbox;
   s.tiles_h = (a.Ho + s.hbox - 1) / s.hbox;
   s.To = a.To;
-  s.tiles_m = (a.Cout + BM - 1) / BM;
+  s.tiles_m = (a.Cout + BM * MT - 1) / (BM * MT);
   s.cchunks = a.Cin / 128;
   s.tiles_n = a.kt * a.kh * a.kw * s.cchunks;
   s.kw = a.kw;
@@ -469,7 +504,10 @@ void conv3d_wgrad(const Conv3dArgs& a, cudaStream_t stream) {
   s.total = s.tiles_m * s.tiles_n * s.splits;
   const CUtensorMap tA = act_map(a.dy, a.B, a.To, a.Ho, a.Wo, a.Cout, s.wbox, s.hbox);
   const CUtensorMap tB = act_map(a.x, a.B, a.T, a.H, a.W, a.Cin, s.wbox, s.hbox);
-  launch<true>(tA, tB, a, s, stream);
+  if (MT == 2)
+    launch<true, 2>(tA, tB, a, s, stream);
+  else
+    launch<true, 1>(tA, tB, a, s, stream);
 }
 
 }  // namespace ddb

@@ -231,3 +231,17 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: s
                    tokens_per_frame, q_pos_offset, kv_pos_offset,
                    scale if scale is not None else 1.0 / math.sqrt(D), None, None, None)
     return o.view(B, T, H, D), lse.view(B, H, T)
+
+
+def packed_self_attention(qkv: torch.Tensor, B: int, T: int, H: int, causal: str = "none",
+                          tokens_per_frame: int = 1, scale: Optional[float] = None) -> torch.Tensor:
+    """Forward-only attention over a packed ``qkv [B*T, 3*H*64]`` bf16 projection (q, k, v
+    column blocks, heads contiguous within each); any ``T`` (the last tile is masked).
+    Returns ``o [B*T, H*64]``."""
+    d = H * 64
+    assert qkv.shape == (B * T, 3 * d) and qkv.is_contiguous()
+    o = torch.empty(B * T, d, device=qkv.device, dtype=torch.bfloat16)
+    lse = torch.empty(B * H * T, device=qkv.device, dtype=torch.float32)
+    ext().attn_fwd(qkv, qkv, qkv, o, lse, 0, d, 2 * d, 0, B, H, T, T, T, T, CAUSAL[causal],
+                   tokens_per_frame, 0, 0, scale if scale is not None else 0.125, None, None, None)
+    return o

@@ -45,3 +45,36 @@ def rope_rotate_(x: torch.Tensor, rot_cols: int, tab: torch.Tensor, head_dim: in
                  rows_per_seq: int = 1 << 30, pos_offset: int = 0, inverse: bool = False):
     ext().rope_rotate(x, rot_cols, tab, head_dim, rows_per_seq, pos_offset, inverse)
     return x
+
+
+class _LayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1]).to(torch.bfloat16).contiguous()
+        w = None if weight is None else weight.detach().float().contiguous()
+        b = None if bias is None else bias.detach().float().contiguous()
+        y, mean, rstd = ext().layernorm_fwd(x2, w, b, eps)
+        ctx.save_for_backward(x2, mean, rstd)
+        ctx.w, ctx.params = w, (weight, bias)
+        ctx.shp = shp
+        return y.view(shp)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, mean, rstd = ctx.saved_tensors
+        weight, bias = ctx.params
+        D = x2.shape[1]
+        dw = torch.zeros(D, device=x2.device) if weight is not None and weight.requires_grad else None
+        db = torch.zeros(D, device=x2.device) if bias is not None and bias.requires_grad else None
+        dx = ext().layernorm_bwd(dy.reshape(-1, D).to(torch.bfloat16).contiguous(), x2, mean, rstd,
+                                 ctx.w, dw, db)
+        return (dx.view(ctx.shp), None if dw is None else dw.to(weight.dtype),
+                None if db is None else db.to(bias.dtype), None)
+
+
+def layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None,
+               bias: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
+    """LayerNorm over the last dim on ``csrc/fused/layernorm.cu`` (bf16 out, fp32 stats),
+    differentiable in ``x``, ``weight`` and ``bias``; ``D`` a multiple of 256."""
+    return _LayerNormFn.apply(x, weight, bias, eps)

@@ -31,6 +31,7 @@ EPI = {
     "dswiglu": 4,
     "rope": 5,
     "gate_res": 6,
+    "gelu": 7,
 }
 
 
