@@ -150,7 +150,8 @@ def run_ours(args, ws, rank, local):
     B, Fr = cfg.train.batch_per_gpu, cfg.train.frames
     tokens_per_step = B * Fr * cfg.model.tokens_per_frame
     gen = torch.Generator().manual_seed(1234 + rank)
-    dev_batch = make_batch(cfg, device=dev, generator=gen)
+    rgb = Fr if cfg.model.repa is not None else 0  # REPA teacher frames (RGB ~U[0,1])
+    dev_batch = make_batch(cfg, device=dev, generator=gen, rgb_frames=rgb)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
 
     for _ in range(args.warmup):
@@ -178,7 +179,7 @@ def run_ours(args, ws, rank, local):
     check_device_status()
 
     # ---- end to end through the public API: pinned host inputs in, loss out
-    host = [make_batch(cfg, generator=gen, pin=True) for _ in range(2)]
+    host = [make_batch(cfg, generator=gen, pin=True, rgb_frames=rgb) for _ in range(2)]
     h2d = host[0].nbytes()
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     barrier()
@@ -210,7 +211,9 @@ def run_ours(args, ws, rank, local):
         "scaling": "weak",
         "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 4),
         "dtype": "bf16",
-        "data": "synthetic latents/actions/flow-time, random-init weights",
+        "data": "synthetic latents/actions/flow-time, random-init weights" + (
+            ", RGB frames ~U[0,1] for the random-init frozen ViT-L REPA teacher"
+            if cfg.model.repa is not None else ""),
         "config": {
             "model": cfg.model.name,
             "layers": cfg.model.n_layers, "d_model": cfg.model.d_model,

@@ -59,7 +59,7 @@ class REPAParams:
     teacher_patch: int = 16
     image_h: int = 256
     image_w: int = 512
-    proj_hidden: int = 2048
+    proj_hidden: Optional[int] = None  # None: (d_model + teacher_dim) // 2
     feature_layer: int = -1  # teacher layer whose output is aligned to (-1 = last)
 
 

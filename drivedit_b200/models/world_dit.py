@@ -210,6 +210,15 @@ class WorldDiT(nn.Module):
         nn.init.zeros_(self.out_proj.bias)
         self.rope = RoPE3D(cfg.d_head, cfg.grid_h, cfg.grid_w, cfg.max_frames, cfg.rope_base,
                            cfg.rope_temporal_factor, cfg.rope_split)
+        self.repa_head = None
+        if cfg.repa is not None:
+            # REPA projection of the layer-`cfg.repa.layer` hidden states onto the frozen
+            # teacher's feature space; trained with the model (same optimizer / shards)
+            from ..training.repa import ProjectionMLP
+
+            rp = cfg.repa
+            hid = rp.proj_hidden or (d + rp.teacher_dim) // 2
+            self.repa_head = ProjectionMLP(d, hid, rp.teacher_dim)
         self.fused = None  # set by enable_fused() on CUDA
 
     # ---------------------------------------------------------------- helpers

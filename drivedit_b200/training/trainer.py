@@ -57,6 +57,28 @@ class WorldModelTrainer:
         self.gen = torch.Generator(device=self.device)
         self.gen.manual_seed(cfg.seed + 1)
         self.step_idx = 0
+        self.teacher = None
+        rp = getattr(getattr(model, "cfg", None), "repa", None)
+        if rp is not None:
+            self._build_teacher(rp)
+        self.last_losses: Dict[str, torch.Tensor] = {}
+
+    def _build_teacher(self, rp):
+        """Frozen ViT/V-JEPA teacher whose layer ``rp.feature_layer`` (-1: last) features
+        the DiT's layer-``rp.layer`` hidden states are aligned to (cosine, weight
+        ``rp.weight``). Random-init unless weights are loaded into ``self.teacher``."""
+        from ..models.vjepa import VJEPABackbone, VJEPAConfig
+
+        tl = rp.feature_layer if rp.feature_layer >= 0 else rp.teacher_layers - 1
+        self.teacher_layer = tl
+        vcfg = VJEPAConfig(embed_dim=rp.teacher_dim, num_layers=rp.teacher_layers,
+                           num_heads=rp.teacher_heads, patch_size=rp.teacher_patch,
+                           tubelet_size=2, num_frames=self.cfg.frames,
+                           image_size=(rp.image_h, rp.image_w), extract_layers=[tl])
+        g = torch.random.get_rng_state()
+        torch.manual_seed(self.cfg.seed + 7)
+        self.teacher = VJEPABackbone(vcfg).to(self.device)
+        torch.random.set_rng_state(g)
 
     def loss(self, batch: LatentBatch) -> torch.Tensor:
         x1 = batch.latents.to(self.compute_dtype)
@@ -64,10 +86,25 @@ class WorldModelTrainer:
         x0 = torch.randn(x1.shape, device=x1.device, generator=self.gen, dtype=torch.float32)
         t = sample_t(B, self.cfg.t_sampling, x1.device, self.gen)
         x_t = interpolate(x0, x1.float(), t).to(self.compute_dtype)
-        v, aux = self.model(x_t, t, batch.actions, return_aux=True)
         target = (x1.float() - x0)
-        loss = (v.float() - target).pow(2).mean()
-        return loss + aux
+        if self.teacher is None:
+            v, aux = self.model(x_t, t, batch.actions, return_aux=True)
+            mse = (v.float() - target).pow(2).mean()
+            self.last_losses = {"mse": mse.detach(), "aux": aux.detach()}
+            return mse + aux
+        rp = self.model.cfg.repa
+        v, aux, feats = self.model(x_t, t, batch.actions, return_aux=True,
+                                   return_features=rp.layer)
+        mse = (v.float() - target).pow(2).mean()
+        with torch.no_grad():
+            tf = self.teacher(batch.rgb, max_layer=self.teacher_layer)["intermediate"]
+            tfeat = tf[f"layer_{self.teacher_layer}"]
+        from .repa import alignment_loss
+
+        proj = self.model.repa_head(feats.reshape(B, -1, feats.shape[-1]))
+        repa = alignment_loss(proj, tfeat, "cosine")
+        self.last_losses = {"mse": mse.detach(), "aux": aux.detach(), "repa": repa.detach()}
+        return mse + aux + rp.weight * repa
 
     def train_step(self, batch: LatentBatch) -> torch.Tensor:
         self.group.zero_grad()
