@@ -63,9 +63,15 @@ class StreamingRollout:
 
     @torch.no_grad()
     def run(self, context: torch.Tensor, actions: torch.Tensor, total_frames: Optional[int] = None,
-            generator: Optional[torch.Generator] = None) -> RolloutResult:
+            generator: Optional[torch.Generator] = None, extra_cond: Optional[torch.Tensor] = None,
+            replace=None) -> RolloutResult:
         """``context [B, Fc, C, H, W]`` clean latent frames, ``actions [B, F_total, A]``
-        for every frame (context included); returns context + generated frames."""
+        for every frame (context included); returns context + generated frames.
+
+        ``extra_cond [B, F_total, d]`` is added to each frame's conditioning. ``replace``
+        (a callable ``(f0, n) -> chunk or None``) may supply the chunk of frames
+        ``[f0, f0 + n)`` instead of generating it (e.g. the ground-truth frames in
+        self-forcing training for chunks that are not self-generated)."""
         cfg = self.cfg
         m = self.model
         B, Fc = context.shape[:2]
@@ -78,7 +84,7 @@ class StreamingRollout:
         for f0 in range(0, Fc, chunk):
             f1 = min(Fc, f0 + chunk)
             forward_cached(m, context[:, f0:f1].to(self.dtype), ones, actions[:, f0:f1], cache,
-                           commit=True)
+                           commit=True, extra_cond=None if extra_cond is None else extra_cond[:, f0:f1])
         ts = torch.linspace(0.0, 1.0, cfg.flow_steps + 1, device=self.device)
         chunk_ms: List[float] = []
         t_all0 = time.perf_counter()
@@ -87,17 +93,22 @@ class StreamingRollout:
         while f < total:
             n = min(chunk, total - f)
             a = actions[:, f:f + n]
+            ec = None if extra_cond is None else extra_cond[:, f:f + n]
             s_ev, e_ev = self._timer()
             t0 = time.perf_counter()
             if s_ev is not None:
                 s_ev.record()
-            x = torch.randn(shape[:1] + (n,) + shape[2:], device=self.device, generator=generator,
-                            dtype=torch.float32).to(self.dtype)
-            for i in range(cfg.flow_steps):
-                t = ts[i].expand(B)
-                v = forward_cached(m, x, t, a, cache, commit=False)
-                x = (x.float() + (ts[i + 1] - ts[i]) * v.float()).to(self.dtype)
-            forward_cached(m, x, ones, a, cache, commit=True)
+            given = replace(f, n) if replace is not None else None
+            if given is not None:
+                x = given.to(self.dtype)
+            else:
+                x = torch.randn(shape[:1] + (n,) + shape[2:], device=self.device,
+                                generator=generator, dtype=torch.float32).to(self.dtype)
+                for i in range(cfg.flow_steps):
+                    t = ts[i].expand(B)
+                    v = forward_cached(m, x, t, a, cache, commit=False, extra_cond=ec)
+                    x = (x.float() + (ts[i + 1] - ts[i]) * v.float()).to(self.dtype)
+            forward_cached(m, x, ones, a, cache, commit=True, extra_cond=ec)
             if e_ev is not None:
                 e_ev.record()
                 e_ev.synchronize()

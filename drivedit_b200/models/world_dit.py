@@ -222,12 +222,18 @@ class WorldDiT(nn.Module):
         self.fused = None  # set by enable_fused() on CUDA
 
     # ---------------------------------------------------------------- helpers
-    def condition(self, t: torch.Tensor, actions: torch.Tensor) -> torch.Tensor:
-        """Per-frame conditioning ``[B, F, d]`` from ``t [B]`` or ``[B, F]`` and actions."""
+    def condition(self, t: torch.Tensor, actions: torch.Tensor,
+                  extra: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Per-frame conditioning ``[B, F, d]`` from ``t [B]`` or ``[B, F]`` and actions;
+        ``extra`` (``[B, d]`` or ``[B, F, d]``, e.g. control / future-anchor embeddings)
+        is added before the activation."""
         te = self.t_embed(t)
         if te.dim() == 2:
             te = te[:, None]
-        return F.silu(te + self.a_embed(actions.float()))
+        h = te + self.a_embed(actions.float())
+        if extra is not None:
+            h = h + (extra[:, None] if extra.dim() == 2 else extra).float()
+        return F.silu(h)
 
     def no_decay_names(self) -> List[str]:
         return [n for n, p in self.named_parameters()
@@ -235,17 +241,19 @@ class WorldDiT(nn.Module):
 
     # ---------------------------------------------------------------- forward
     def forward(self, x_t: torch.Tensor, t: torch.Tensor, actions: torch.Tensor,
-                frame_offset: int = 0, return_aux: bool = False, return_features: Optional[int] = None):
-        """``x_t [B, F, C, H, W]``, ``t [B]`` / ``[B, F]``, ``actions [B, F, A]``."""
+                frame_offset: int = 0, return_aux: bool = False, return_features: Optional[int] = None,
+                extra_cond: Optional[torch.Tensor] = None):
+        """``x_t [B, F, C, H, W]``, ``t [B]`` / ``[B, F]``, ``actions [B, F, A]``,
+        optional ``extra_cond`` added to the per-frame conditioning."""
         cfg = self.cfg
         B, Fr, C, H, W = x_t.shape
         if self.fused is not None and x_t.is_cuda:
             return self.fused.forward(self, x_t, t, actions, frame_offset, return_aux,
-                                      return_features)
+                                      return_features, extra_cond)
         dt = x_t.dtype
         tok = patchify(x_t, cfg.patch)
         x = self.patch_embed(tok.to(self.patch_embed.weight.dtype)).to(dt)
-        c = self.condition(t, actions)                       # [B, F, d] fp32
+        c = self.condition(t, actions, extra_cond)           # [B, F, d] fp32
         tab = self.rope.table(Fr, frame_offset).to(x.device)
         aux_total = x.new_zeros((), dtype=torch.float32)
         feats = None
@@ -366,18 +374,19 @@ def _block_cached_torch(blk: WorldDiTBlock, x, mod, tab_q, cache: LayerKVCache, 
 
 @torch.no_grad()
 def forward_cached(model: "WorldDiT", x_t: torch.Tensor, t: torch.Tensor, actions: torch.Tensor,
-                   cache: KVCacheSet, commit: bool = False) -> torch.Tensor:
+                   cache: KVCacheSet, commit: bool = False,
+                   extra_cond: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Velocity for a chunk of frames ``x_t [B, Fc, C, H, W]`` at absolute frame
     ``cache.frames``, attending to the cached window. With ``commit`` the chunk's K/V stay
     in the cache (call this on the clean chunk after sampling it)."""
     if model.fused is not None and x_t.is_cuda:
-        return model.fused.forward_cached(model, x_t, t, actions, cache, commit)
+        return model.fused.forward_cached(model, x_t, t, actions, cache, commit, extra_cond)
     cfg = model.cfg
     B, Fc, C, H, W = x_t.shape
     dt = x_t.dtype
     tok = patchify(x_t, cfg.patch)
     x = model.patch_embed(tok.to(model.patch_embed.weight.dtype)).to(dt)
-    c = model.condition(t, actions)
+    c = model.condition(t, actions, extra_cond)
     T = x.shape[1]
     tab = model.rope.table(Fc, cache.frames).to(x.device)
     row = cache.reserve(T)

@@ -160,7 +160,7 @@ class FusedWorldDiT:
         self.group = group if group is not None else FlatParamGroup(model.named_parameters())
 
     def forward(self, model, x_t, t, actions, frame_offset=0, return_aux=False,
-                return_features=None):
+                return_features=None, extra_cond=None):
         from ..models.world_dit import patchify, unpatchify
 
         cfg = model.cfg
@@ -171,7 +171,7 @@ class FusedWorldDiT:
         T = tok.shape[0] // B
         x = linear(tok, g.compute_view(model.patch_embed.weight), model.patch_embed.bias,
                    model.patch_embed.weight, model.patch_embed.bias)
-        c = model.condition(t, actions)                            # [B, F, d] fp32
+        c = model.condition(t, actions, extra_cond)                # [B, F, d] fp32
         c2 = c.reshape(B * Fr, d)
         tab = model.rope.table(Fr, frame_offset).to(x.device)
         bc = BlockCtx(B, T, Fr, T // Fr, d, cfg.n_heads, cfg.d_head, tab, cfg.attention,
@@ -215,7 +215,7 @@ class _FinalNorm(torch.autograd.Function):
 
 
 # ----------------------------------------------------------------------------- KV-cached
-def _forward_cached_fused(self, model, x_t, t, actions, cache, commit):
+def _forward_cached_fused(self, model, x_t, t, actions, cache, commit, extra_cond=None):
     """Inference-only forward of a chunk over the cached K/V window (no autograd):
     every block is AdaLN-RMSNorm -> QKV GEMM (rotary by absolute frame) -> K/V into the
     cache window -> flash attention with absolute query/key offsets -> output GEMM with
@@ -232,7 +232,7 @@ def _forward_cached_fused(self, model, x_t, t, actions, cache, commit):
     T = tok.shape[0] // B
     tpf = T // Fc
     x = gemm(tok, W(model.patch_embed.weight), bias=model.patch_embed.bias)
-    c2 = model.condition(t, actions).reshape(B * Fc, d)
+    c2 = model.condition(t, actions, extra_cond).reshape(B * Fc, d)
     tab = model.rope.table(Fc, cache.frames).to(x.device)
     row = cache.reserve(T)
     for blk, lc in zip(model.blocks, cache.layers):

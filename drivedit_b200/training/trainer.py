@@ -64,16 +64,18 @@ class WorldModelTrainer:
         self.last_losses: Dict[str, torch.Tensor] = {}
 
     def _build_teacher(self, rp):
-        """Frozen ViT/V-JEPA teacher whose layer ``rp.feature_layer`` (-1: last) features
-        the DiT's layer-``rp.layer`` hidden states are aligned to (cosine, weight
-        ``rp.weight``). Random-init unless weights are loaded into ``self.teacher``."""
+        """Frozen ViT teacher (the V-JEPA encoder with 2-D patches: tubelet 1, one frame
+        per image) applied to every RGB frame; its layer ``rp.feature_layer`` (-1: last)
+        patch features, frame-major like the DiT tokens, are what the DiT's
+        layer-``rp.layer`` hidden states are aligned to (cosine, weight ``rp.weight``).
+        Random-init unless weights are loaded into ``self.teacher``."""
         from ..models.vjepa import VJEPABackbone, VJEPAConfig
 
         tl = rp.feature_layer if rp.feature_layer >= 0 else rp.teacher_layers - 1
         self.teacher_layer = tl
         vcfg = VJEPAConfig(embed_dim=rp.teacher_dim, num_layers=rp.teacher_layers,
                            num_heads=rp.teacher_heads, patch_size=rp.teacher_patch,
-                           tubelet_size=2, num_frames=self.cfg.frames,
+                           tubelet_size=1, num_frames=1,
                            image_size=(rp.image_h, rp.image_w), extract_layers=[tl])
         g = torch.random.get_rng_state()
         torch.manual_seed(self.cfg.seed + 7)
@@ -97,8 +99,10 @@ class WorldModelTrainer:
                                    return_features=rp.layer)
         mse = (v.float() - target).pow(2).mean()
         with torch.no_grad():
-            tf = self.teacher(batch.rgb, max_layer=self.teacher_layer)["intermediate"]
-            tfeat = tf[f"layer_{self.teacher_layer}"]
+            rgb = batch.rgb  # [B, F, 3, Hi, Wi] -> B*F single-frame clips [B*F, 3, 1, Hi, Wi]
+            clips = rgb.reshape(-1, *rgb.shape[2:]).unsqueeze(2)
+            tf = self.teacher(clips, max_layer=self.teacher_layer)["intermediate"]
+            tfeat = tf[f"layer_{self.teacher_layer}"].reshape(B, -1, self.teacher.config.embed_dim)
         from .repa import alignment_loss
 
         proj = self.model.repa_head(feats.reshape(B, -1, feats.shape[-1]))
