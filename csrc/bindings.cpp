@@ -944,6 +944,43 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor mea
   return dx;
 }
 
+
+// fused flip / brightness / contrast / normalise (+ HWC uint8 -> CHW) over a clip batch
+torch::Tensor video_augment(torch::Tensor x, bool input_u8_hwc, bool out_bf16,
+                            c10::optional<torch::Tensor> flip, c10::optional<torch::Tensor> brightness,
+                            c10::optional<torch::Tensor> contrast, c10::optional<torch::Tensor> mean,
+                            c10::optional<torch::Tensor> std_) {
+  check_cuda_tensor(x, "x");
+  TORCH_CHECK(x.dim() == 5 && x.is_contiguous(), "x must be a contiguous 5-D clip batch");
+  if (input_u8_hwc) TORCH_CHECK(x.scalar_type() == torch::kUInt8, "uint8 HWC input expected");
+  else TORCH_CHECK(x.scalar_type() == torch::kFloat32, "float32 CHW input expected");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ddb::AugmentArgs a;
+  a.B = x.size(0); a.T = x.size(1);
+  if (input_u8_hwc) { a.H = x.size(2); a.W = x.size(3); a.C = x.size(4); }
+  else { a.C = x.size(2); a.H = x.size(3); a.W = x.size(4); }
+  a.x = x.data_ptr(); a.input_u8_hwc = input_u8_hwc; a.out_bf16 = out_bf16;
+  auto y = torch::empty({a.B, a.T, a.C, a.H, a.W},
+                        x.options().dtype(out_bf16 ? torch::kBFloat16 : torch::kFloat32));
+  a.y = y.data_ptr();
+  auto f32 = [&](const c10::optional<torch::Tensor>& t, int64_t n, const char* nm) -> const float* {
+    if (!t) return nullptr;
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->numel() == n && t->is_contiguous(), nm);
+    return t->data_ptr<float>();
+  };
+  if (flip) {
+    TORCH_CHECK(flip->is_cuda() && flip->scalar_type() == torch::kInt32 && flip->numel() == a.B, "flip");
+    a.flip = flip->data_ptr<int>();
+  }
+  a.brightness = f32(brightness, a.B, "brightness");
+  a.contrast = f32(contrast, a.B, "contrast");
+  a.mean = f32(mean, a.C, "mean");
+  a.std = f32(std_, a.C, "std");
+  TORCH_CHECK((a.mean == nullptr) == (a.std == nullptr), "mean and std go together");
+  ddb::video_augment(a, stream());
+  return y;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -954,6 +991,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("groupnorm_bwd", &groupnorm_bwd, "GroupNorm(+SiLU) backward -> (dx, channel sums)");
   m.def("layernorm_fwd", &layernorm_fwd, "LayerNorm forward -> (y, mean, rstd)");
   m.def("layernorm_bwd", &layernorm_bwd, "LayerNorm backward -> dx (accumulates dw, db)");
+  m.def("video_augment", &video_augment, "fused flip/brightness/contrast/normalise of clips");
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
   m.def("read_status", &read_status, "device status word (0 = ok)");
   m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");

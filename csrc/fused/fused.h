@@ -43,6 +43,20 @@ struct LayerNormArgs {
 void layernorm_fwd(const LayerNormArgs& a, cudaStream_t s);
 void layernorm_bwd(const LayerNormArgs& a, cudaStream_t s);
 
+struct AugmentArgs {
+  int B = 0, T = 0, C = 0, H = 0, W = 0;
+  const void* x = nullptr;          // uint8 [B,T,H,W,C] or float [B,T,C,H,W]
+  bool input_u8_hwc = false;
+  void* y = nullptr;                // [B,T,C,H,W] float32 or bf16
+  bool out_bf16 = false;
+  const int* flip = nullptr;        // [B] or null
+  const float* brightness = nullptr;  // [B] additive, or null
+  const float* contrast = nullptr;    // [B] multiplicative, or null
+  const float* mean = nullptr;      // [C] or null (no normalisation)
+  const float* std = nullptr;       // [C]
+};
+void video_augment(const AugmentArgs& a, cudaStream_t s);
+
 void adaln_rmsnorm_fwd(const AdaLNArgs& a, cudaStream_t s);
 void adaln_rmsnorm_bwd(const AdaLNArgs& a, cudaStream_t s);
 

@@ -48,6 +48,8 @@ if data_sources:
             sources=[os.path.relpath(s, ROOT) for s in data_sources],
             include_dirs=[CSRC],
             extra_compile_args=["-O3", "-std=c++17", "-pthread"],
+            libraries=["z"],
+            extra_link_args=["-pthread"],
         )
     )
 

@@ -111,3 +111,20 @@ def test_fused_model_matches_torch_path():
         worst[n] = _rel(p.grad, g_ref)
     bad = {k: v for k, v in worst.items() if v > 6e-2}
     assert not bad, bad
+
+
+def test_video_augment_kernel():
+    from drivedit_b200.data.transforms import AugmentationPipeline, clip_augment_reference
+    torch.manual_seed(0)
+    x = torch.rand(3, 4, 3, 17, 33, device="cuda")
+    flip = torch.tensor([1, 0, 1], device="cuda")
+    br = torch.tensor([0.1, -0.2, 0.0], device="cuda")
+    ct = torch.tensor([1.2, 0.8, 1.0], device="cuda")
+    mean, std = [0.5, 0.4, 0.3], [0.2, 0.25, 0.3]
+    y = AugmentationPipeline.fused_clip_augment(x, flip, br, ct, mean, std)
+    ref = clip_augment_reference(x, flip, br, ct, mean, std)
+    assert (y - ref).abs().max() < 1e-5
+    u8 = (x.permute(0, 1, 3, 4, 2) * 255).round().to(torch.uint8).contiguous()
+    y2 = AugmentationPipeline.fused_clip_augment(u8, flip, br, ct, mean, std, out_bf16=True, input_u8_hwc=True)
+    ref2 = clip_augment_reference(u8.permute(0, 1, 4, 2, 3).float() / 255, flip, br, ct, mean, std)
+    assert (y2.float() - ref2).abs().max() < 3e-2
