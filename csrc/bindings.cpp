@@ -952,8 +952,11 @@ torch::Tensor video_augment(torch::Tensor x, bool input_u8_hwc, bool out_bf16,
                             c10::optional<torch::Tensor> std_) {
   check_cuda_tensor(x, "x");
   TORCH_CHECK(x.dim() == 5 && x.is_contiguous(), "x must be a contiguous 5-D clip batch");
-  if (input_u8_hwc) TORCH_CHECK(x.scalar_type() == torch::kUInt8, "uint8 HWC input expected");
-  else TORCH_CHECK(x.scalar_type() == torch::kFloat32, "float32 CHW input expected");
+  if (input_u8_hwc) {
+    TORCH_CHECK(x.scalar_type() == torch::kUInt8, "uint8 HWC input expected");
+  } else {
+    TORCH_CHECK(x.scalar_type() == torch::kFloat32, "float32 CHW input expected");
+  }
   const c10::cuda::CUDAGuard guard(x.device());
   ddb::AugmentArgs a;
   a.B = x.size(0); a.T = x.size(1);
