@@ -497,11 +497,17 @@ class Decoder3D(nn.Module):
             skips = list(reversed(skips))
         for i, blk in enumerate(self.up_blocks):
             h = blk["upsample"](h, target_size=targets[i])
-            if skips is not None and self.skip_weights is not None:
-                s = skips[i]
-                if s.shape[2:] != h.shape[2:]:
-                    s = F.interpolate(s, size=h.shape[2:], mode="trilinear", align_corners=False)
-                h = torch.cat([h, (s * self.skip_weights[i]).to(h.dtype)], dim=1)
+            if self.skip_weights is not None:
+                if skips is not None:
+                    s = skips[i]
+                    if s.shape[2:] != h.shape[2:]:
+                        s = F.interpolate(s, size=h.shape[2:], mode="trilinear", align_corners=False)
+                    h = torch.cat([h, (s * self.skip_weights[i]).to(h.dtype)], dim=1)
+                else:
+                    # decoding latents alone (sampling, streaming): the skip half of the
+                    # fused input is zero, so the same weights apply (the reference
+                    # concatenates nothing here and its res-blocks then see too few channels)
+                    h = torch.cat([h, torch.zeros_like(h)], dim=1)
             for rb in blk["res_blocks"]:
                 h = rb(h)
             h = blk["attn"](h)
