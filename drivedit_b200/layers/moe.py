@@ -229,7 +229,9 @@ class MoEFFN(nn.Module):
 
     @torch.no_grad()
     def update_bias(self, counts: torch.Tensor, n_tokens: int):
-        """Aux-loss-free balancing (reference layers/moe.py:164-181)."""
+        """Aux-loss-free balancing (reference layers/moe.py:164-181). The step's
+        per-expert counts stay on the device in ``last_counts`` for monitoring."""
+        self.last_counts = counts.detach()
         if not self.training:
             return
         s = self.bias_update_speed
