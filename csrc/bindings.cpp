@@ -716,23 +716,42 @@ std::vector<torch::Tensor> moe_plan(torch::Tensor counts, int64_t E, int64_t ns,
 
 torch::Tensor moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tensor seg_start,
                            torch::Tensor seg_count, torch::Tensor cursor, torch::Tensor xp,
-                           int64_t E, int64_t ns) {
+                           int64_t E, int64_t ns, c10::optional<torch::Tensor> xp2,
+                           bool zero_routed_pad) {
   check_bf16(x, "x");
   check_bf16(xp, "xp");
   check_rows(x, "x");
   check_rows(xp, "xp");
+  __nv_bfloat16* p2 = nullptr;
+  int64_t ld2 = 0;
+  if (xp2) {
+    check_bf16(*xp2, "xp2");
+    check_rows(*xp2, "xp2");
+    p2 = reinterpret_cast<__nv_bfloat16*>(xp2->data_ptr());
+    ld2 = xp2->stride(0);
+  }
   const c10::cuda::CUDAGuard guard(x.device());
   const int64_t N = x.size(0), k = topk_idx.size(1);
   auto slot_of = torch::empty({N, k + ns}, x.options().dtype(torch::kInt32));
   ddb::moe_dispatch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), N, x.size(1), k,
                     ns, E, topk_idx.data_ptr<int>(), seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
                     cursor.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()),
-                    xp.stride(0), slot_of.data_ptr<int>(), stream());
+                    xp.stride(0), slot_of.data_ptr<int>(), stream(), p2, ld2, zero_routed_pad);
   return slot_of;
 }
 
+void moe_zero_pad(torch::Tensor seg_start, torch::Tensor seg_count, torch::Tensor xp) {
+  check_bf16(xp, "xp");
+  check_rows(xp, "xp");
+  TORCH_CHECK(seg_start.scalar_type() == torch::kInt32 && seg_count.scalar_type() == torch::kInt32 &&
+                  seg_start.is_cuda() && seg_count.numel() == seg_start.numel(), "segment tables");
+  const c10::cuda::CUDAGuard guard(xp.device());
+  ddb::moe_zero_pad(seg_start.data_ptr<int>(), seg_count.data_ptr<int>(), seg_start.numel(),
+                    reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()), xp.stride(0), xp.size(1), stream());
+}
+
 ddb::MoeCombineArgs combine_args(torch::Tensor topk_w, torch::Tensor shared_w, torch::Tensor slot_of,
-                                 torch::Tensor y, int64_t ns) {
+                                 torch::Tensor y, int64_t ns, const c10::optional<torch::Tensor>& y2) {
   check_bf16(y, "y");
   check_rows(y, "y");
   ddb::MoeCombineArgs a;
@@ -740,13 +759,21 @@ ddb::MoeCombineArgs combine_args(torch::Tensor topk_w, torch::Tensor shared_w, t
   a.topk_w = topk_w.data_ptr<float>(); a.shared_w = shared_w.data_ptr<float>();
   a.slot_of = slot_of.data_ptr<int>();
   a.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()); a.ld_y = y.stride(0);
+  if (y2) {
+    check_bf16(*y2, "y2");
+    check_rows(*y2, "y2");
+    TORCH_CHECK(y2->size(1) == y.size(1), "y2 width");
+    a.y2 = reinterpret_cast<const __nv_bfloat16*>(y2->data_ptr());
+    a.ld_y2 = y2->stride(0);
+  }
   return a;
 }
 
 torch::Tensor moe_combine(torch::Tensor topk_w, torch::Tensor shared_w, torch::Tensor slot_of,
-                          torch::Tensor y, c10::optional<torch::Tensor> residual, int64_t ns) {
+                          torch::Tensor y, c10::optional<torch::Tensor> residual, int64_t ns,
+                          c10::optional<torch::Tensor> y2) {
   const c10::cuda::CUDAGuard guard(y.device());
-  auto a = combine_args(topk_w, shared_w, slot_of, y, ns);
+  auto a = combine_args(topk_w, shared_w, slot_of, y, ns, y2);
   auto out = torch::empty({a.N, a.d}, y.options());
   if (residual) {
     check_bf16(*residual, "residual");
@@ -758,29 +785,51 @@ torch::Tensor moe_combine(torch::Tensor topk_w, torch::Tensor shared_w, torch::T
   return out;
 }
 
+// dy (and dy2 for the shared rows when y2 is given) may be supplied as outputs; rows no
+// route writes keep their contents (a fresh dy is zero-filled).
 std::vector<torch::Tensor> moe_combine_bwd(torch::Tensor topk_w, torch::Tensor shared_w,
                                            torch::Tensor slot_of, torch::Tensor y, torch::Tensor dout,
-                                           int64_t ns) {
+                                           int64_t ns, c10::optional<torch::Tensor> y2,
+                                           c10::optional<torch::Tensor> dy_out,
+                                           c10::optional<torch::Tensor> dy2_out) {
   const c10::cuda::CUDAGuard guard(y.device());
-  auto a = combine_args(topk_w, shared_w, slot_of, y, ns);
+  auto a = combine_args(topk_w, shared_w, slot_of, y, ns, y2);
   check_bf16(dout, "dout");
-  auto dy = torch::zeros_like(y);
+  torch::Tensor dy = dy_out ? *dy_out : torch::zeros_like(y);
+  check_bf16(dy, "dy");
+  TORCH_CHECK(dy.stride(0) == a.ld_y && dy.size(0) >= y.size(0), "dy must match y's layout");
+  torch::Tensor dy2;
+  if (y2) {
+    dy2 = dy2_out ? *dy2_out : torch::zeros_like(*y2);
+    check_bf16(dy2, "dy2");
+    TORCH_CHECK(dy2.stride(0) == a.ld_y2 && dy2.size(0) >= y2->size(0), "dy2 must match y2's layout");
+  }
   auto dw = torch::empty({a.N, a.k + ns}, topk_w.options());
   ddb::moe_combine_bwd(a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
-                       reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dw.data_ptr<float>(), stream());
+                       reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dw.data_ptr<float>(), stream(),
+                       y2 ? reinterpret_cast<__nv_bfloat16*>(dy2.data_ptr()) : nullptr);
+  if (y2) return {dy, dw, dy2};
   return {dy, dw};
 }
 
-torch::Tensor moe_unpermute(torch::Tensor dxp, torch::Tensor slot_of, int64_t N) {
+torch::Tensor moe_unpermute(torch::Tensor dxp, torch::Tensor slot_of, int64_t N,
+                            c10::optional<torch::Tensor> dxp2, int64_t k) {
   check_bf16(dxp, "dxp");
+  const __nv_bfloat16* p2 = nullptr;
+  int64_t ld2 = 0;
+  if (dxp2) {
+    check_bf16(*dxp2, "dxp2");
+    TORCH_CHECK(dxp2->size(1) == dxp.size(1), "dxp2 width");
+    p2 = reinterpret_cast<const __nv_bfloat16*>(dxp2->data_ptr());
+    ld2 = dxp2->stride(0);
+  }
   const c10::cuda::CUDAGuard guard(dxp.device());
   auto dx = torch::empty({N, dxp.size(1)}, dxp.options());
   ddb::moe_unpermute(reinterpret_cast<const __nv_bfloat16*>(dxp.data_ptr()), dxp.stride(0),
                      slot_of.data_ptr<int>(), N, slot_of.size(1), dxp.size(1),
-                     reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), stream());
+                     reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), stream(), k, p2, ld2);
   return dx;
 }
-
 
 // ---------------------------------------------------------------- video VAE
 void check_cl5(const torch::Tensor& t, const char* name) {
@@ -984,6 +1033,38 @@ torch::Tensor video_augment(torch::Tensor x, bool input_u8_hwc, bool out_bf16,
   return y;
 }
 
+
+// Row-block copies for expert parallelism: blocks [n, 4] int32 (src_rank, src_row, dst_rank,
+// dst_row), row_prefix [n] int32 (first flat row of each block). A side is either a table of
+// per-rank base pointers (int64 device array) or one local base pointer.
+void ep_copy_rows(c10::optional<torch::Tensor> src_table, int64_t src_ptr,
+                  c10::optional<torch::Tensor> dst_table, int64_t dst_ptr, torch::Tensor blocks,
+                  torch::Tensor row_prefix, int64_t total_rows, int64_t row_bytes, int64_t src_ld,
+                  int64_t dst_ld) {
+  for (auto* t : {&src_table, &dst_table})
+    if (*t) TORCH_CHECK((*t)->is_cuda() && (*t)->scalar_type() == torch::kInt64 && (*t)->is_contiguous(),
+                        "pointer tables must be int64 device arrays");
+  TORCH_CHECK(src_table || src_ptr, "ep_copy_rows: no source");
+  TORCH_CHECK(dst_table || dst_ptr, "ep_copy_rows: no destination");
+  for (auto* t : {&blocks, &row_prefix})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->is_contiguous(), "int32 device block list");
+  TORCH_CHECK(blocks.dim() == 2 && blocks.size(1) == 4 && row_prefix.numel() == blocks.size(0), "block list");
+  const c10::cuda::CUDAGuard guard(blocks.device());
+  ddb::EpCopyArgs a;
+  if (src_table) a.src_table = reinterpret_cast<const void* const*>(src_table->data_ptr<int64_t>());
+  if (dst_table) a.dst_table = reinterpret_cast<void* const*>(dst_table->data_ptr<int64_t>());
+  a.src_local = reinterpret_cast<const void*>(src_ptr);
+  a.dst_local = reinterpret_cast<void*>(dst_ptr);
+  a.blocks = blocks.data_ptr<int>();
+  a.row_prefix = row_prefix.data_ptr<int>();
+  a.nblocks = blocks.size(0);
+  a.total_rows = total_rows;
+  a.row_bytes = row_bytes;
+  a.src_ld = src_ld;
+  a.dst_ld = dst_ld;
+  ddb::ep_copy_rows(a, stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -995,6 +1076,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_fwd", &layernorm_fwd, "LayerNorm forward -> (y, mean, rstd)");
   m.def("layernorm_bwd", &layernorm_bwd, "LayerNorm backward -> dx (accumulates dw, db)");
   m.def("video_augment", &video_augment, "fused flip/brightness/contrast/normalise of clips");
+  m.def("ep_copy_rows", &ep_copy_rows, "row-block copies between local and peer buffers (EP)");
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
   m.def("read_status", &read_status, "device status word (0 = ok)");
   m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");
@@ -1027,10 +1109,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped, "grouped (MoE) tcgen05 GEMM with device tile tables");
   m.def("moe_route", &moe_route, "MoE top-k routing (+ shared gates, counts, prob sums)");
   m.def("moe_plan", &moe_plan, "MoE segment layout and grouped-GEMM tables");
-  m.def("moe_dispatch", &moe_dispatch, "MoE token permutation into expert segments");
-  m.def("moe_combine", &moe_combine, "MoE weighted combine (+ residual)");
-  m.def("moe_combine_bwd", &moe_combine_bwd, "MoE combine backward");
-  m.def("moe_unpermute", &moe_unpermute, "MoE gather-sum of permuted gradients");
+  m.def("moe_dispatch", &moe_dispatch, "MoE token permutation into expert segments",
+        py::arg("x"), py::arg("topk_idx"), py::arg("seg_start"), py::arg("seg_count"), py::arg("cursor"),
+        py::arg("xp"), py::arg("E"), py::arg("ns"), py::arg("xp2") = py::none(),
+        py::arg("zero_routed_pad") = true);
+  m.def("moe_zero_pad", &moe_zero_pad, "zero the padding rows of 128-row expert segments");
+  m.def("moe_combine", &moe_combine, "MoE weighted combine (+ residual)", py::arg("topk_w"),
+        py::arg("shared_w"), py::arg("slot_of"), py::arg("y"), py::arg("residual"), py::arg("ns"),
+        py::arg("y2") = py::none());
+  m.def("moe_combine_bwd", &moe_combine_bwd, "MoE combine backward", py::arg("topk_w"),
+        py::arg("shared_w"), py::arg("slot_of"), py::arg("y"), py::arg("dout"), py::arg("ns"),
+        py::arg("y2") = py::none(), py::arg("dy") = py::none(), py::arg("dy2") = py::none());
+  m.def("moe_unpermute", &moe_unpermute, "MoE gather-sum of permuted gradients", py::arg("dxp"),
+        py::arg("slot_of"), py::arg("N"), py::arg("dxp2") = py::none(), py::arg("k") = 0);
   m.def("gemm_batched", &gemm_batched, "strided-batched tcgen05 GEMM");
   m.def("sla_pool", &sla_pool, "SLA block means of q, k");
   m.def("sla_route", &sla_route, "SLA top-k routing + kernel lists");

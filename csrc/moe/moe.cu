@@ -14,6 +14,9 @@
 //   moe_combine   out[t] = residual[t] + sum_j w[t,j] * y[slot(t,j)]
 //   moe_combine_bwd  dy[slot(t,j)] = w[t,j] dout[t];  dw[t,j] = dout[t] . y[slot(t,j)]
 //   moe_unpermute dx[t] = sum_j dx_perm[slot(t,j)]
+// Under expert parallelism the routed rows (j < k) and the shared-expert rows (j >= k) live
+// in different buffers (a compact send / return buffer in peer-mapped memory, and the
+// local shared-expert segments); every kernel then takes the second buffer for j >= k.
 // Semantics: reference layers/moe.py:73-228 (Router), :231-424 (MoEFFN).
 #include <cuda_bf16.h>
 
@@ -151,7 +154,8 @@ __global__ void moe_plan_kernel(const int* __restrict__ counts, int E, int ns, i
 __global__ void __launch_bounds__(256) moe_dispatch_kernel(
     const __nv_bfloat16* __restrict__ x, long ldx, int N, int d, int k, int ns, int E,
     const int* __restrict__ topk_idx, const int* __restrict__ seg_start, int* __restrict__ cursor,
-    __nv_bfloat16* __restrict__ xp, long ldp, int* __restrict__ slot_of) {
+    __nv_bfloat16* __restrict__ xp, long ldp, int* __restrict__ slot_of, __nv_bfloat16* __restrict__ xp2,
+    long ldp2) {
   const int lane = threadIdx.x & 31;
   const long wi = blockIdx.x * 8L + (threadIdx.x >> 5);
   const int R = k + ns;
@@ -169,7 +173,8 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(
   }
   slot = __shfl_sync(0xffffffffu, slot, 0);
   const __nv_bfloat16* src = x + static_cast<long>(t) * ldx;
-  __nv_bfloat16* dst = xp + static_cast<long>(slot) * ldp;
+  __nv_bfloat16* dst = (xp2 != nullptr && j >= k) ? xp2 + static_cast<long>(slot) * ldp2
+                                                  : xp + static_cast<long>(slot) * ldp;
   for (int c = lane * 8; c < d; c += 256) {
     const uint4 v = ld_global_v4(src + c);
     st_global_v4(dst + c, v.x, v.y, v.z, v.w);
@@ -192,6 +197,11 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ seg_start,
 __device__ __forceinline__ float route_w(const MoeCombineArgs& a, int t, int j) {
   return j < a.k ? a.topk_w[static_cast<long>(t) * a.k + j]
                  : a.shared_w[static_cast<long>(t) * a.ns + (j - a.k)];
+}
+
+__device__ __forceinline__ const __nv_bfloat16* y_row(const MoeCombineArgs& a, int j, int slot) {
+  return (a.y2 != nullptr && j >= a.k) ? a.y2 + static_cast<long>(slot) * a.ld_y2
+                                       : a.y + static_cast<long>(slot) * a.ld_y;
 }
 
 // one warp per token; d <= 2048
@@ -218,7 +228,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
     for (int j = 0; j < R; ++j) {
       const float w = route_w(a, t, j);
       const int slot = a.slot_of[static_cast<long>(t) * R + j];
-      const uint4 y = ld_global_v4(a.y + static_cast<long>(slot) * a.ld_y + c);
+      const uint4 y = ld_global_v4(y_row(a, j, slot) + c);
       const uint32_t yw[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -237,7 +247,8 @@ __global__ void __launch_bounds__(256) moe_combine_bwd_kernel(MoeCombineArgs a,
                                                               const __nv_bfloat16* __restrict__ dout,
                                                               long ld_dout,
                                                               __nv_bfloat16* __restrict__ dy,
-                                                              float* __restrict__ dw) {
+                                                              float* __restrict__ dw,
+                                                              __nv_bfloat16* __restrict__ dy2) {
   const int lane = threadIdx.x & 31;
   const long wi = blockIdx.x * 8L + (threadIdx.x >> 5);
   const int R = a.k + a.ns;
@@ -245,10 +256,13 @@ __global__ void __launch_bounds__(256) moe_combine_bwd_kernel(MoeCombineArgs a,
   const int t = static_cast<int>(wi / R), j = static_cast<int>(wi % R);
   const float w = route_w(a, t, j);
   const int slot = a.slot_of[wi];
+  const bool second = a.y2 != nullptr && j >= a.k;
+  __nv_bfloat16* dst = second ? dy2 + static_cast<long>(slot) * a.ld_y2 : dy + static_cast<long>(slot) * a.ld_y;
+  const __nv_bfloat16* yr = y_row(a, j, slot);
   float dot = 0.f;
   for (int c = lane * 8; c < a.d; c += 256) {
     const uint4 g = ld_global_v4(dout + static_cast<long>(t) * ld_dout + c);
-    const uint4 y = ld_global_v4(a.y + static_cast<long>(slot) * a.ld_y + c);
+    const uint4 y = ld_global_v4(yr + c);
     const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, yw[4] = {y.x, y.y, y.z, y.w};
     uint32_t o[4];
 #pragma unroll
@@ -257,7 +271,7 @@ __global__ void __launch_bounds__(256) moe_combine_bwd_kernel(MoeCombineArgs a,
       dot += fg.x * fy.x + fg.y * fy.y;
       o[q] = pack_bf16(w * fg.x, w * fg.y);
     }
-    st_global_v4(dy + static_cast<long>(slot) * a.ld_y + c, o[0], o[1], o[2], o[3]);
+    st_global_v4(dst + c, o[0], o[1], o[2], o[3]);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
@@ -268,7 +282,9 @@ __global__ void __launch_bounds__(256) moe_combine_bwd_kernel(MoeCombineArgs a,
 __global__ void __launch_bounds__(256) moe_unpermute_kernel(const __nv_bfloat16* __restrict__ dxp,
                                                             long ldp, const int* __restrict__ slot_of,
                                                             int N, int R, int d,
-                                                            __nv_bfloat16* __restrict__ dx, long ldx) {
+                                                            __nv_bfloat16* __restrict__ dx, long ldx,
+                                                            int k, const __nv_bfloat16* __restrict__ dxp2,
+                                                            long ldp2) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= N) return;
@@ -276,7 +292,9 @@ __global__ void __launch_bounds__(256) moe_unpermute_kernel(const __nv_bfloat16*
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = 0; j < R; ++j) {
       const int slot = slot_of[static_cast<long>(t) * R + j];
-      const uint4 v = ld_global_v4(dxp + static_cast<long>(slot) * ldp + c);
+      const __nv_bfloat16* row = (dxp2 != nullptr && j >= k) ? dxp2 + static_cast<long>(slot) * ldp2
+                                                             : dxp + static_cast<long>(slot) * ldp;
+      const uint4 v = ld_global_v4(row + c);
       const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -308,13 +326,27 @@ void moe_plan(const int* counts, int E, int ns, int N, int* seg_start, int* seg_
 
 void moe_dispatch(const __nv_bfloat16* x, long ldx, int N, int d, int k, int ns, int E,
                   const int* topk_idx, const int* seg_start, const int* seg_count, int* cursor,
-                  __nv_bfloat16* xp, long ldp, int* slot_of, cudaStream_t s) {
+                  __nv_bfloat16* xp, long ldp, int* slot_of, cudaStream_t s, __nv_bfloat16* xp2,
+                  long ldp2, bool zero_routed_pad) {
   if (d % 8 != 0) throw std::runtime_error("moe_dispatch: d % 8");
   const long rows = static_cast<long>(N) * (k + ns);
   moe_dispatch_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, s>>>(
-      x, ldx, N, d, k, ns, E, topk_idx, seg_start, cursor, xp, ldp, slot_of);
-  moe_zero_pad_kernel<<<E + ns, 128, 0, s>>>(seg_start, seg_count, xp, ldp, d);
-  count_launch(2);
+      x, ldx, N, d, k, ns, E, topk_idx, seg_start, cursor, xp, ldp, slot_of, xp2, ldp2);
+  count_launch();
+  if (xp2 == nullptr && zero_routed_pad) {
+    moe_zero_pad(seg_start, seg_count, E + ns, xp, ldp, d, s);
+  } else {
+    // compact routed rows (zero_routed_pad false) have no padding to clear
+    if (zero_routed_pad) moe_zero_pad(seg_start, seg_count, E, xp, ldp, d, s);
+    if (ns) moe_zero_pad(seg_start + E, seg_count + E, ns, xp2 ? xp2 : xp, xp2 ? ldp2 : ldp, d, s);
+  }
+}
+
+void moe_zero_pad(const int* seg_start, const int* seg_count, int nseg, __nv_bfloat16* xp, long ldp,
+                  int d, cudaStream_t s) {
+  if (nseg <= 0) return;
+  moe_zero_pad_kernel<<<nseg, 128, 0, s>>>(seg_start, seg_count, xp, ldp, d);
+  count_launch();
 }
 
 void moe_combine(const MoeCombineArgs& a, cudaStream_t s) {
@@ -323,15 +355,17 @@ void moe_combine(const MoeCombineArgs& a, cudaStream_t s) {
 }
 
 void moe_combine_bwd(const MoeCombineArgs& a, const __nv_bfloat16* dout, long ld_dout,
-                     __nv_bfloat16* dy, float* dw, cudaStream_t s) {
+                     __nv_bfloat16* dy, float* dw, cudaStream_t s, __nv_bfloat16* dy2) {
   const long rows = static_cast<long>(a.N) * (a.k + a.ns);
-  moe_combine_bwd_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, s>>>(a, dout, ld_dout, dy, dw);
+  if ((a.y2 == nullptr) != (dy2 == nullptr)) throw std::runtime_error("moe_combine_bwd: y2 / dy2");
+  moe_combine_bwd_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, s>>>(a, dout, ld_dout, dy, dw, dy2);
   count_launch();
 }
 
 void moe_unpermute(const __nv_bfloat16* dxp, long ldp, const int* slot_of, int N, int R, int d,
-                   __nv_bfloat16* dx, long ldx, cudaStream_t s) {
-  moe_unpermute_kernel<<<(N + 7) / 8, 256, 0, s>>>(dxp, ldp, slot_of, N, R, d, dx, ldx);
+                   __nv_bfloat16* dx, long ldx, cudaStream_t s, int k, const __nv_bfloat16* dxp2,
+                   long ldp2) {
+  moe_unpermute_kernel<<<(N + 7) / 8, 256, 0, s>>>(dxp, ldp, slot_of, N, R, d, dx, ldx, k, dxp2, ldp2);
   count_launch();
 }
 

@@ -23,6 +23,10 @@ Differences:
   * on CUDA the whole FFN runs as routing / dispatch / grouped-GEMM / combine kernels
     (:mod:`drivedit_b200.ops.moe`); shared experts are routed to every token with their
     softmax gate and share that path.
+  * expert parallelism (:meth:`MoEFFN.shard_experts`, :mod:`drivedit_b200.parallel.expert`):
+    each rank keeps its ``E / world`` routed experts in ``w13 / w2`` and the replicated
+    shared experts in ``w13_shared / w2_shared``; tokens travel to their expert's rank
+    and back. The reference has no expert parallelism.
 """
 from __future__ import annotations
 
@@ -168,7 +172,32 @@ class MoEFFN(nn.Module):
         wv = torch.randn(E + ns, Fh, d_model) * 0.02
         self.w13 = nn.Parameter(torch.stack([pack_swiglu(wg[i], wv[i]) for i in range(E + ns)]))
         self.w2 = nn.Parameter(torch.randn(E + ns, d_model, Fh) * (0.02 / math.sqrt(2)))
+        self.ep = None          # ExpertParallel context once the experts are sharded
+        self.ep_slot = -1       # this layer's index among the EP layers (return-buffer slot)
         self._register_load_state_dict_pre_hook(self._load_reference_keys)
+
+    # -------------------------------------------------------------- expert parallelism
+    def shard_experts(self, ep) -> None:
+        """Keep only this rank's routed experts (``ep.local_range()``) in ``w13 / w2``
+        and move the shared experts to ``w13_shared / w2_shared``. Every rank must hold
+        identical full weights when this is called (same seed or a loaded checkpoint)."""
+        assert self.ep is None, "experts already sharded"
+        assert ep.num_experts == self.num_experts
+        lo, hi = ep.local_range()
+        E, ns = self.num_experts, self.num_shared_experts
+        with torch.no_grad():
+            w13, w2 = self.w13.detach(), self.w2.detach()
+            self.w13 = nn.Parameter(w13[lo:hi].clone())
+            self.w2 = nn.Parameter(w2[lo:hi].clone())
+            if ns:
+                self.w13_shared = nn.Parameter(w13[E:E + ns].clone())
+                self.w2_shared = nn.Parameter(w2[E:E + ns].clone())
+        self.ep = ep
+        self.ep_slot = ep.register(self)
+
+    def expert_parameter_names(self, prefix: str = ""):
+        """Names of the rank-local (not replicated) parameters under expert parallelism."""
+        return [prefix + "w13", prefix + "w2"] if self.ep is not None else []
 
     # -------------------------------------------------------------- checkpoint compat
     def _load_reference_keys(self, state_dict, prefix, *args):
@@ -176,6 +205,7 @@ class MoEFFN(nn.Module):
 
         if prefix + "experts.0.w_gate.weight" not in state_dict:
             return
+        assert self.ep is None, "load reference checkpoints before sharding the experts"
         E, ns = self.num_experts, self.num_shared_experts
         rw = self.router_weight.detach().clone()
         rw[:E] = state_dict.pop(prefix + "router.gate.weight")
@@ -199,6 +229,7 @@ class MoEFFN(nn.Module):
         """Per-expert keys in the reference's layout (``experts.N.w_gate.weight`` ...)."""
         from .mlp import unpack_swiglu
 
+        assert self.ep is None, "reference export needs the full expert set (gather the shards first)"
         E, ns = self.num_experts, self.num_shared_experts
         out = {prefix + "router.gate.weight": self.router_weight[:E].detach().clone(),
                prefix + "router.expert_bias": self.expert_bias.clone(),
@@ -240,11 +271,20 @@ class MoEFFN(nn.Module):
         self.expert_bias.add_(-s * (self.expert_load_ema - 1.0 / self.num_experts))
 
     def _expert(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        """Expert ``i`` of ``w13 / w2`` (under expert parallelism: local index)."""
+        return self._swiglu(self.w13[i], self.w2[i], x)
+
+    def _shared_expert(self, s: int, x: torch.Tensor) -> torch.Tensor:
+        if self.ep is not None:
+            return self._swiglu(self.w13_shared[s], self.w2_shared[s], x)
+        return self._expert(self.num_experts + s, x)
+
+    @staticmethod
+    def _swiglu(w13, w2, x):
         from .mlp import split_gu
 
-        gu = x @ self.w13[i].to(x.dtype).t()
-        g, u = split_gu(gu)
-        return (F.silu(g) * u) @ self.w2[i].to(x.dtype).t()
+        g, u = split_gu(x @ w13.to(x.dtype).t())
+        return (F.silu(g) * u) @ w2.to(x.dtype).t()
 
     def experts_forward(self, x, weights, experts):
         N, D = x.shape
@@ -265,7 +305,7 @@ class MoEFFN(nn.Module):
     def shared_forward(self, x, gates):
         out = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
         for s in range(self.num_shared_experts):
-            out = out + gates[:, s:s + 1] * self._expert(self.num_experts + s, x).float()
+            out = out + gates[:, s:s + 1] * self._shared_expert(s, x).float()
         return out
 
     def forward(self, x: torch.Tensor, return_metrics: bool = False) -> MoEOutput:
@@ -273,8 +313,16 @@ class MoEFFN(nn.Module):
         xf = x.reshape(-1, shape[-1])
         w, e, p, g = self.route(xf)
         aux, counts = aux_load_balance_loss(p, e, self.num_experts)
-        self.update_bias(counts, xf.shape[0])
-        y = self.experts_forward(xf, w, e)
+        if self.ep is None:
+            self.update_bias(counts, xf.shape[0])
+            y = self.experts_forward(xf, w, e)
+        else:
+            from ..parallel.expert import ep_experts_forward_torch
+
+            y, table = ep_experts_forward_torch(self, xf, w, e)
+            # every rank applies the same bias update from the global counts
+            gcounts = torch.as_tensor(table.sum(0), device=xf.device)
+            self.update_bias(gcounts, xf.shape[0] * self.ep.world)
         if self.num_shared_experts:
             y = y + self.shared_forward(xf, g)
         metrics = routing_metrics(p, w, e, counts, self.num_experts) if return_metrics else None

@@ -275,6 +275,19 @@ class WorldDiT(nn.Module):
             return v, aux_total, feats
         return (v, aux_total) if return_aux else v
 
+    def enable_expert_parallel(self, ep) -> List[str]:
+        """Shard every MoE layer's routed experts over the EP group ``ep``
+        (:class:`~drivedit_b200.parallel.expert.ExpertParallel`); returns the names of the
+        now rank-local parameters. Call before any flat parameter group is built."""
+        for blk in self.blocks:
+            if blk.moe is not None:
+                blk.moe.shard_experts(ep)
+        return self.expert_parameter_names()
+
+    def expert_parameter_names(self) -> List[str]:
+        return [n for i, blk in enumerate(self.blocks) if blk.moe is not None
+                for n in blk.moe.expert_parameter_names(f"blocks.{i}.moe.")]
+
     def enable_fused(self, **kw):
         from ..ops.block import FusedWorldDiT
 

@@ -101,20 +101,22 @@ def _mlp_backward(dx2, sm, blk, W, bc, mod, dmod):
 
 
 def _moe_forward(x1, mod, blk, W, bc):
-    from .moe import moe_ffn_forward
+    from .moe import moe_ffn_forward, moe_ffn_forward_ep
 
     d = bc.d
     h2, r2 = adaln_rmsnorm(x1, blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf)
-    x2, aux, sv = moe_ffn_forward(h2, x1, blk.moe, W)
+    fwd = moe_ffn_forward if blk.moe.ep is None else moe_ffn_forward_ep
+    x2, aux, sv = fwd(h2, x1, blk.moe, W)
     sv.update(x1=x1, r2=r2)
     return x2, aux, sv
 
 
 def _moe_backward(dx2, d_aux, sv, blk, W, bc, mod, dmod):
-    from .moe import moe_ffn_backward
+    from .moe import moe_ffn_backward, moe_ffn_backward_ep
 
     d = bc.d
-    dh2 = moe_ffn_backward(dx2, d_aux, blk.moe, W, sv)
+    bwd = moe_ffn_backward if blk.moe.ep is None else moe_ffn_backward_ep
+    dh2 = bwd(dx2, d_aux, blk.moe, W, sv)
     return adaln_rmsnorm_bwd(dh2, sv["x1"], sv["r2"], blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf,
                              dmod, blk.norm2.weight.grad, dx2)
 

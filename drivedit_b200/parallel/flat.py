@@ -59,6 +59,10 @@ class FlatParamGroup:
         self.master = allocator("master", self.numel, torch.float32)
         self.grad = allocator("grad", self.numel, torch.float32)
         self.compute = allocator("compute", self.numel, compute_dtype)
+        # groups whose parameters this one resolves views for too (rank-local expert
+        # parameters under expert parallelism live in their own group)
+        self.linked: List["FlatParamGroup"] = []
+        self._pos = {id(p): i for i, p in enumerate(self.params)}
         with torch.no_grad():
             for n, p in zip(self.names, self.params):
                 o, k = self.offsets[n]
@@ -74,12 +78,20 @@ class FlatParamGroup:
         return buf[o:o + k].view(p.shape)
 
     def index(self, p: nn.Parameter) -> int:
-        for i, q in enumerate(self.params):
-            if q is p:
-                return i
-        raise KeyError("parameter not in this group")
+        i = self._pos.get(id(p))
+        if i is None or self.params[i] is not p:
+            raise KeyError("parameter not in this group")
+        return i
+
+    def owns(self, p: nn.Parameter) -> bool:
+        i = self._pos.get(id(p))
+        return i is not None and self.params[i] is p
 
     def compute_view(self, p: nn.Parameter) -> torch.Tensor:
+        if not self.owns(p):
+            for g in self.linked:
+                if g.owns(p):
+                    return g.compute_view(p)
         return self.view(self.compute, p)
 
     def grad_view(self, p: nn.Parameter) -> torch.Tensor:
@@ -88,8 +100,12 @@ class FlatParamGroup:
     # ------------------------------------------------------------------ updates
     def refresh_compute(self):
         self.compute.copy_(self.master)
+        for g in self.linked:
+            g.refresh_compute()
 
     def zero_grad(self):
+        for g in self.linked:
+            g.zero_grad()
         self.grad.zero_()
         for n, p in zip(self.names, self.params):
             if p.grad is None or p.grad.data_ptr() != self.grad_view(p).data_ptr():

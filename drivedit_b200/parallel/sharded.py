@@ -26,7 +26,7 @@ Two transports:
 from __future__ import annotations
 
 import math
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -77,14 +77,21 @@ class ShardedDataParallel:
     """Owns the flat buffers of a model and performs the sharded optimizer step."""
 
     def __init__(self, model: nn.Module, group=None, device=None, transport: Optional[str] = None,
-                 lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, grad_clip=1.0):
+                 lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, grad_clip=1.0,
+                 local_params: Optional[Sequence[str]] = None):
+        """``local_params``: names of rank-local parameters (expert-parallel experts).
+        They are neither reduced nor sharded: a local flat group with a full AdamW holds
+        them, their squared gradient norm joins the global clipping norm, and the main
+        group resolves their compute views (``FlatParamGroup.linked``)."""
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
         self.transport = transport or ("fused" if self.device.type == "cuda" else "nccl")
         self.lr, self.betas, self.eps, self.wd, self.grad_clip = lr, tuple(betas), eps, weight_decay, grad_clip
-        named = list(model.named_parameters())
+        named_all = list(model.named_parameters())
+        local = set(local_params or [])
+        named = [(n, p) for n, p in named_all if n not in local]
         no_decay = model.no_decay_names() if hasattr(model, "no_decay_names") else []
         pad = ALIGN * self.world * 4
         self.sym = {}
@@ -102,6 +109,14 @@ class ShardedDataParallel:
                 return bufs[name].tensor(n, dtype)
         self.flat = FlatParamGroup(named, self.device, no_decay=no_decay, pad_to=self.world * 4,
                                    allocator=alloc)
+        self.local_opt = None
+        if local:
+            from ..training.optim import FlatAdamW
+
+            lg = FlatParamGroup([(n, p) for n, p in named_all if n in local], self.device,
+                                no_decay=no_decay)
+            self.local_opt = FlatAdamW(lg, lr, betas, eps, weight_decay, grad_clip)
+            self.flat.linked.append(lg)
         n = self.flat.numel
         assert n % (self.world * 4) == 0
         self.shard_len = n // self.world
@@ -148,6 +163,8 @@ class ShardedDataParallel:
         self.sumsq.zero_()
         ext().rs_sum_sqnorm(self.sym["grad"].table, self.world, self.shard_off, self.shard_len,
                             self.red, self.sumsq)
+        if self.local_opt is not None and self.grad_clip > 0:
+            self.sumsq += self.local_opt.grad_sq_norm()
         self._barrier(self.sumsq)                         # squared-norm partials exchanged
         pay = self.flags.tensor(self.world, torch.float32, 4 * self.world)
         ext().shard_adamw_allgather(
@@ -155,14 +172,19 @@ class ShardedDataParallel:
             self.sym["compute"].table, self.world, self.shard_off, self.shard_len,
             self.flat.decay_end, pay if self.grad_clip > 0 else None, float(self.grad_clip),
             self.lr, self.betas[0], self.betas[1], self.eps, self.wd, bc1, bc2, scale)
+        if self.local_opt is not None:
+            self._local_step(scale, pay.sum() if self.grad_clip > 0 else None)
         self._barrier()                                   # all peers' stores have landed
 
     def _step_collective(self, bc1, bc2, scale):
         g = self.flat.grad
         dist.reduce_scatter_tensor(self.red, g, group=self.group)
         clip = 1.0
+        sq = None
         if self.grad_clip > 0:
             sq = self.red.double().pow(2).sum().float().reshape(1)
+            if self.local_opt is not None:
+                sq = sq + self.local_opt.grad_sq_norm().reshape(1)
             dist.all_reduce(sq, group=self.group)
             norm = sq.sqrt() * scale
             self.last_grad_norm = norm
@@ -181,6 +203,14 @@ class ShardedDataParallel:
         shard = master.clone()
         dist.all_gather_into_tensor(self.flat.master, shard, group=self.group)
         self.flat.refresh_compute()
+        if self.local_opt is not None:
+            self._local_step(scale, sq.reshape(()) if sq is not None else None)
+
+    def _local_step(self, scale, sq_norm):
+        """AdamW on the rank-local parameters with the same step count, gradient scale
+        and global clipping norm as the sharded update."""
+        self.local_opt.step_count = self.step_count - 1
+        self.local_opt.step(grad_scale=scale, sq_norm=sq_norm)
 
     def close(self):
         for b in self.sym.values():

@@ -36,14 +36,23 @@ class WorldModelTrainer:
         self.compute_dtype = torch.bfloat16 if (self.cuda and cfg.dtype == "bf16") else torch.float32
         self.pg = process_group
         self.engine = None
+        self.ep = None
         world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
         if world > 1:
             from ..parallel.sharded import ShardedDataParallel
 
             transport = "fused" if (self.cuda and cfg.fused_collectives) else "nccl"
+            local = None
+            moe_cfg = getattr(getattr(model, "cfg", None), "moe", None)
+            if cfg.parallel == "fsdp_ep" and moe_cfg is not None:
+                from ..parallel.expert import ExpertParallel
+
+                # expert parallelism over the whole data-parallel group
+                self.ep = ExpertParallel(process_group, moe_cfg.num_experts, transport, self.device)
+                local = model.enable_expert_parallel(self.ep)
             self.engine = ShardedDataParallel(model, process_group, self.device, transport,
                                               cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
-                                              cfg.grad_clip)
+                                              cfg.grad_clip, local_params=local)
             self.group = self.engine.flat
             self.opt = None
         else:
@@ -124,6 +133,8 @@ class WorldModelTrainer:
     def state_dict(self) -> Dict:
         opt = self.opt.state_dict() if self.opt is not None else {
             "m": self.engine.m, "v": self.engine.v, "step": self.engine.step_count}
+        if self.engine is not None and self.engine.local_opt is not None:
+            opt["local"] = self.engine.local_opt.state_dict()   # this rank's experts
         return {"model": self.model.state_dict(), "optim": opt, "step": self.step_idx}
 
     def load_state_dict(self, sd: Dict):
@@ -135,4 +146,6 @@ class WorldModelTrainer:
             self.engine.m.copy_(sd["optim"]["m"])
             self.engine.v.copy_(sd["optim"]["v"])
             self.engine.step_count = int(sd["optim"]["step"])
+            if self.engine.local_opt is not None and "local" in sd["optim"]:
+                self.engine.local_opt.load_state_dict(sd["optim"]["local"])
         self.step_idx = int(sd["step"])

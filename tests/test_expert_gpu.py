@@ -1,0 +1,183 @@
+"""Expert-parallel MoE on the GPU kernels.
+
+* one rank (one GPU): the expert-parallel kernel path (compact dispatch, owner layout,
+  peer-copy pull/push through the rank's own symmetric buffers, shared experts apart)
+  reproduces the single-device MoE kernel path exactly on the same weights;
+* two ranks (two GPUs): one fsdp_ep training step with the peer-memory transport matches
+  the NCCL all-to-all transport and plain fsdp (every expert on every rank).
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _np(obj):
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().float().cpu().numpy().copy()
+    if isinstance(obj, dict):
+        return {k: _np(v) for k, v in obj.items()}
+    return obj
+
+
+def _init(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+
+
+def _cfg(parallel, fused=True):
+    from drivedit_b200.config.presets import Config, ModelConfig, MoEParams, TrainConfig
+
+    m = ModelConfig(n_layers=2, d_model=256, n_heads=4, mlp_hidden=512, latent_channels=16,
+                    latent_h=16, latent_w=32, moe=MoEParams(num_experts=8, top_k=2, expert_dim=256,
+                                                            num_shared=1, aux_loss_weight=0.01))
+    return Config(model=m, train=TrainConfig(batch_per_gpu=2, frames=4, lr=1e-3, dtype="bf16",
+                                             parallel=parallel, fused_collectives=fused))
+
+
+# ----------------------------------------------------------------------------- one GPU
+def _one_rank_worker(rank, world, port, q):
+    _init(rank, world, port)
+    from drivedit_b200.layers.moe import MoEFFN
+    from drivedit_b200.ops._ext import check_device_status
+    from drivedit_b200.ops.moe import moe_ffn_backward, moe_ffn_backward_ep, moe_ffn_forward, moe_ffn_forward_ep
+    from drivedit_b200.parallel.expert import ExpertParallel
+    from drivedit_b200.parallel.flat import FlatParamGroup
+
+    d, E, k, F, ns, N = 256, 8, 2, 256, 2, 1000
+    res = {}
+    for mode in ("local", "ep"):
+        torch.manual_seed(0)
+        moe = MoEFFN(d, E, k, F, ns).cuda()
+        if mode == "ep":
+            ep = ExpertParallel(num_experts=E, transport="fused", device="cuda")
+            moe.shard_experts(ep)
+            main = FlatParamGroup([(n, p) for n, p in moe.named_parameters() if n not in ("w13", "w2")])
+            main.linked.append(FlatParamGroup([("w13", moe.w13), ("w2", moe.w2)]))
+            grp = main
+        else:
+            grp = FlatParamGroup(moe.named_parameters())
+        grp.zero_grad()
+        g = torch.Generator(device="cuda").manual_seed(1)
+        h = torch.randn(N, d, device="cuda", generator=g).to(torch.bfloat16)
+        r = torch.randn(N, d, device="cuda", generator=g).to(torch.bfloat16)
+        dout = torch.randn(N, d, device="cuda", generator=g).to(torch.bfloat16)
+        fwd, bwd = (moe_ffn_forward, moe_ffn_backward) if mode == "local" else (moe_ffn_forward_ep,
+                                                                                moe_ffn_backward_ep)
+        out, aux, sv = fwd(h, r, moe, grp.compute_view)
+        dh = bwd(dout, torch.ones((), device="cuda"), moe, grp.compute_view, sv)
+        torch.cuda.synchronize()
+        w13g = moe.w13.grad if mode == "local" else torch.cat([moe.w13.grad, moe.w13_shared.grad])
+        w2g = moe.w2.grad if mode == "local" else torch.cat([moe.w2.grad, moe.w2_shared.grad])
+        res[mode] = dict(out=out, dh=dh, w13=w13g, w2=w2g, router=moe.router_weight.grad)
+        if mode == "ep":
+            ep.close()
+    check_device_status()
+    q.put((rank, _np(res)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_kernel_path_matches_local_one_gpu():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_one_rank_worker, args=(0, 1, _port(), q))
+    p.start()
+    _, res = q.get(timeout=300)
+    p.join(timeout=60)
+    assert p.exitcode == 0
+    a, b = res["local"], res["ep"]
+    for key in ("out", "dh", "w13", "w2", "router"):
+        x, y = a[key], b[key]
+        err = np.linalg.norm(x - y) / (np.linalg.norm(x) + 1e-12)
+        assert err < 2e-3, (key, err)
+
+
+# ----------------------------------------------------------------------------- two GPUs
+def _two_rank_worker(rank, world, port, q):
+    _init(rank, world, port)
+    from drivedit_b200.data import make_batch
+    from drivedit_b200.models.world_dit import WorldDiT
+    from drivedit_b200.ops._ext import check_device_status
+    from drivedit_b200.training.trainer import WorldModelTrainer
+
+    out = {}
+    for name, parallel, fused in (("ep_fused", "fsdp_ep", True), ("ep_nccl", "fsdp_ep", False),
+                                  ("fsdp", "fsdp", True)):
+        cfg = _cfg(parallel, fused)
+        torch.manual_seed(0)
+        model = WorldDiT(cfg.model)
+        tr = WorldModelTrainer(model, cfg.train, f"cuda:{rank}", process_group=dist.group.WORLD)
+        batch = make_batch(cfg, generator=torch.Generator().manual_seed(100 + rank),
+                           device=f"cuda:{rank}")
+        losses = [float(tr.train_step(batch))]
+        sd1 = _np(model.state_dict())
+        losses.append(float(tr.train_step(batch)))   # second step reuses every EP buffer
+        torch.cuda.synchronize()
+        out[name] = {"loss": losses, "lo": tr.ep.local_range()[0] if tr.ep is not None else 0,
+                     "sd1": sd1, "sd2": _np(model.state_dict())}
+        tr.engine.close()
+        if tr.ep is not None:
+            tr.ep.close()
+    check_device_status()
+    q.put((rank, out))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fsdp_ep_two_gpus_matches_nccl_and_fsdp():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_two_rank_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    E = 8
+    for r in range(world):
+        a, b, c = res[r]["ep_fused"], res[r]["ep_nccl"], res[r]["fsdp"]
+        # same kernels, different transport: the same numbers up to the optimizer's
+        # clipping-norm arithmetic
+        assert a["loss"][0] == b["loss"][0], (a["loss"], b["loss"])
+        assert abs(a["loss"][1] - b["loss"][1]) < 1e-4 * abs(b["loss"][1])
+        for n in a["sd2"]:
+            err = np.linalg.norm(a["sd2"][n] - b["sd2"][n]) / (np.linalg.norm(b["sd2"][n]) + 1e-12)
+            assert err < 1e-4, (n, err)
+        # against every expert on every rank (first step): equal up to bf16 rounding
+        assert abs(a["loss"][0] - c["loss"][0]) < 2e-3 * abs(c["loss"][0])
+        lo = a["lo"]
+        for n, v in a["sd1"].items():
+            if n.endswith("moe.w13") or n.endswith("moe.w2"):
+                want = c["sd1"][n][lo:lo + E // world]
+            elif n.endswith("_shared"):
+                base = n.replace("w13_shared", "w13").replace("w2_shared", "w2")
+                want = c["sd1"][base][E:]
+            elif "expert_bias" in n or "expert_load_ema" in n:
+                continue
+            else:
+                want = c["sd1"][n]
+            err = np.linalg.norm(v - want) / (np.linalg.norm(want) + 1e-12)
+            assert err < 5e-3, (n, err)
