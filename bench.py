@@ -222,9 +222,16 @@ def run_ours(args, ws, rank, local):
             "global_batch": B * ws, "seq_len": Fr * cfg.model.tokens_per_frame,
             "frames": Fr, "latent": [cfg.model.latent_channels, cfg.model.latent_h,
                                      cfg.model.latent_w],
-            "parallelism": f"fsdp{ws}" if ws > 1 else "single",
-            "sharding": ("gradients reduce-scattered and weights all-gathered by the fused "
-                         "NVLink optimizer kernel; AdamW state sharded") if ws > 1 else None,
+            "parallelism": (f"fsdp{ws}+ep{ws}" if trainer.ep is not None else f"fsdp{ws}")
+                           if ws > 1 else "single",
+            "sharding": (("gradients reduce-scattered and weights all-gathered by the fused "
+                          "NVLink optimizer kernel" if trainer.engine.transport == "fused" else
+                          "NCCL reduce_scatter / all_gather around a local AdamW")
+                         + "; AdamW state sharded") if ws > 1 else None,
+            "expert_parallel": None if trainer.ep is None else (
+                f"{cfg.model.moe.num_experts // ws} routed experts per rank; token rows "
+                + ("pulled/pushed over NVLink peer memory by the EP copy kernel"
+                   if trainer.ep.transport == "fused" else "exchanged by NCCL all_to_all")),
             "l2": "256 MiB buffer overwritten before every timed step",
         },
         "clocks": clk.summary(),

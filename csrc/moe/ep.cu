@@ -8,7 +8,7 @@
 // the combine push (P2P stores of expert outputs back to the token's rank). Rows are
 // moved as 16-byte vectors, a warp per row stripe, all blocks of all peers in one grid
 // (block list prefix-summed on the host), so the copies to / from every peer overlap.
-// No TMA and no multicast: plain vector loads and stores through the NVLink mapping.
+// Plain 16-byte vector loads and stores through the NVLink mapping (no TMA).
 //
 // Replaces the reference's single-device token scatter / gather (layers/kernels/
 // moe_kernels.py:45-148, never distributed) with the cross-GPU form of the same step.
@@ -40,11 +40,11 @@ __global__ void __launch_bounds__(256) ep_copy_rows_kernel(EpCopyArgs a) {
     const int c = static_cast<int>(i % lanes_per_row);
     const int b = find_block(a.row_prefix, a.nblocks, r);
     const long k = r - a.row_prefix[b];
-    const int4 blk = reinterpret_cast<const int4*>(a.blocks)[b];
-    const void* sb = a.src_table != nullptr ? a.src_table[blk.x] : a.src_local;
-    void* db = a.dst_table != nullptr ? a.dst_table[blk.z] : a.dst_local;
-    const char* src = reinterpret_cast<const char*>(sb) + (blk.y + k) * a.src_ld + c * 16;
-    char* dst = reinterpret_cast<char*>(db) + (blk.w + k) * a.dst_ld + c * 16;
+    const int* blk = a.blocks + 4 * b;   // 4-byte aligned only: plain loads
+    const void* sb = a.src_table != nullptr ? a.src_table[blk[0]] : a.src_local;
+    void* db = a.dst_table != nullptr ? a.dst_table[blk[2]] : a.dst_local;
+    const char* src = reinterpret_cast<const char*>(sb) + (blk[1] + k) * a.src_ld + c * 16;
+    char* dst = reinterpret_cast<char*>(db) + (blk[3] + k) * a.dst_ld + c * 16;
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
   }
 }

@@ -51,7 +51,10 @@ class ExpertParallel:
         assert num_experts % self.world == 0, "experts must divide evenly over the EP ranks"
         self.num_experts = num_experts
         self.local_experts = num_experts // self.world
-        self.device = torch.device(device) if device is not None else torch.device("cpu")
+        dev = torch.device(device) if device is not None else torch.device("cpu")
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
         self.transport = transport or ("fused" if self.device.type == "cuda" else "nccl")
         self.n_layers = 0
         self._sym = {}

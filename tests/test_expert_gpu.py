@@ -35,6 +35,22 @@ def _np(obj):
     return obj
 
 
+def _collect(q, procs, n, timeout):
+    """``n`` results from ``q``; fails fast when a worker died instead of waiting."""
+    import queue
+    import time
+
+    out, t0 = [], time.monotonic()
+    while len(out) < n:
+        try:
+            out.append(q.get(timeout=5))
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead, f"worker exited with {dead}"
+            assert time.monotonic() - t0 < timeout, "workers timed out"
+    return out
+
+
 def _init(rank, world, port):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -101,7 +117,7 @@ def test_expert_parallel_kernel_path_matches_local_one_gpu():
     q = ctx.Queue()
     p = ctx.Process(target=_one_rank_worker, args=(0, 1, _port(), q))
     p.start()
-    _, res = q.get(timeout=300)
+    _, res = _collect(q, [p], 1, 300)[0]
     p.join(timeout=60)
     assert p.exitcode == 0
     a, b = res["local"], res["ep"]
@@ -152,7 +168,7 @@ def test_fsdp_ep_two_gpus_matches_nccl_and_fsdp():
     procs = [ctx.Process(target=_two_rank_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in range(world))
+    res = dict(_collect(q, procs, world, 600))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -163,9 +179,10 @@ def test_fsdp_ep_two_gpus_matches_nccl_and_fsdp():
         # clipping-norm arithmetic
         assert a["loss"][0] == b["loss"][0], (a["loss"], b["loss"])
         assert abs(a["loss"][1] - b["loss"][1]) < 1e-4 * abs(b["loss"][1])
-        for n in a["sd2"]:
-            err = np.linalg.norm(a["sd2"][n] - b["sd2"][n]) / (np.linalg.norm(b["sd2"][n]) + 1e-12)
-            assert err < 1e-4, (n, err)
+        for key, tol in (("sd1", 1e-4), ("sd2", 2e-3)):   # step 2 runs on re-rounded bf16 weights
+            for n in a[key]:
+                err = np.linalg.norm(a[key][n] - b[key][n]) / (np.linalg.norm(b[key][n]) + 1e-12)
+                assert err < tol, (key, n, err)
         # against every expert on every rank (first step): equal up to bf16 rounding
         assert abs(a["loss"][0] - c["loss"][0]) < 2e-3 * abs(c["loss"][0])
         lo = a["lo"]
