@@ -1034,6 +1034,119 @@ torch::Tensor video_augment(torch::Tensor x, bool input_u8_hwc, bool out_bf16,
 }
 
 
+// Owner-driven expert parallelism. Tables are int64 device arrays of per-rank base
+// pointers (routing ids, routing weights, rows, return / dw buffers).
+ddb::EpOwnerArgs ep_owner_args(torch::Tensor peer_idx, torch::Tensor peer_w, torch::Tensor peer_rows,
+                               int64_t world, int64_t rank, int64_t N, int64_t k, int64_t d, int64_t lo,
+                               int64_t El, torch::Tensor seg_start, torch::Tensor cursor,
+                               torch::Tensor meta, torch::Tensor meta_w, torch::Tensor n_uniq) {
+  for (auto* t : {&peer_idx, &peer_w, &peer_rows})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt64 && t->numel() == world, "peer tables");
+  for (auto* t : {&seg_start, &cursor, &meta, &n_uniq})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->is_contiguous(), "int32 EP state");
+  TORCH_CHECK(meta_w.scalar_type() == torch::kFloat32 && meta_w.is_contiguous(), "meta_w");
+  TORCH_CHECK(meta.dim() == 2 && meta.size(1) == 2 + k && meta_w.size(0) == meta.size(0), "meta shape");
+  ddb::EpOwnerArgs a;
+  a.world = world; a.rank = rank; a.N = N; a.k = k; a.d = d; a.lo = lo; a.El = El;
+  a.peer_idx = reinterpret_cast<const int* const*>(peer_idx.data_ptr<int64_t>());
+  a.peer_w = reinterpret_cast<const float* const*>(peer_w.data_ptr<int64_t>());
+  a.peer_rows = reinterpret_cast<const __nv_bfloat16* const*>(peer_rows.data_ptr<int64_t>());
+  a.seg_start = seg_start.data_ptr<int>();
+  a.cursor = cursor.data_ptr<int>();
+  a.meta = meta.data_ptr<int>();
+  a.meta_w = meta_w.data_ptr<float>();
+  a.n_uniq = n_uniq.data_ptr<int>();
+  a.cap = meta.size(0);
+  return a;
+}
+
+void ep_owner_gather(torch::Tensor peer_idx, torch::Tensor peer_w, torch::Tensor peer_rows, int64_t world,
+                     int64_t rank, int64_t N, int64_t k, int64_t d, int64_t lo, int64_t El,
+                     torch::Tensor seg_start, torch::Tensor cursor, torch::Tensor meta, torch::Tensor meta_w,
+                     torch::Tensor n_uniq, torch::Tensor xr) {
+  check_bf16(xr, "xr");
+  check_rows(xr, "xr");
+  TORCH_CHECK(xr.size(1) == d, "xr width");
+  const c10::cuda::CUDAGuard guard(xr.device());
+  auto a = ep_owner_args(peer_idx, peer_w, peer_rows, world, rank, N, k, d, lo, El, seg_start, cursor, meta,
+                         meta_w, n_uniq);
+  TORCH_CHECK(a.cap >= world * N, "meta capacity below world * N");
+  a.xr = reinterpret_cast<__nv_bfloat16*>(xr.data_ptr());
+  a.ld_xr = xr.stride(0);
+  ddb::ep_owner_gather(a, stream());
+}
+
+void ep_owner_grad_gather(torch::Tensor peer_idx, torch::Tensor peer_w, torch::Tensor peer_rows,
+                          int64_t world, int64_t rank, int64_t N, int64_t k, int64_t d, int64_t lo, int64_t El,
+                          torch::Tensor seg_start, torch::Tensor cursor, torch::Tensor meta,
+                          torch::Tensor meta_w, torch::Tensor n_uniq, torch::Tensor y, torch::Tensor dy,
+                          torch::Tensor peer_dw) {
+  check_bf16(y, "y");
+  check_bf16(dy, "dy");
+  check_rows(y, "y");
+  check_rows(dy, "dy");
+  TORCH_CHECK(peer_dw.scalar_type() == torch::kInt64 && peer_dw.numel() == world, "dw table");
+  const c10::cuda::CUDAGuard guard(y.device());
+  auto a = ep_owner_args(peer_idx, peer_w, peer_rows, world, rank, N, k, d, lo, El, seg_start, cursor, meta,
+                         meta_w, n_uniq);
+  ddb::ep_owner_grad_gather(a, reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+                            reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0),
+                            reinterpret_cast<float* const*>(peer_dw.data_ptr<int64_t>()), stream());
+}
+
+void ep_owner_scatter_sum(torch::Tensor peer_idx, torch::Tensor peer_w, torch::Tensor peer_rows,
+                          int64_t world, int64_t rank, int64_t N, int64_t k, int64_t d, int64_t lo, int64_t El,
+                          torch::Tensor seg_start, torch::Tensor cursor, torch::Tensor meta,
+                          torch::Tensor meta_w, torch::Tensor n_uniq, torch::Tensor src, bool weighted,
+                          torch::Tensor peer_ret) {
+  check_bf16(src, "src");
+  check_rows(src, "src");
+  TORCH_CHECK(peer_ret.scalar_type() == torch::kInt64 && peer_ret.numel() == world, "return table");
+  const c10::cuda::CUDAGuard guard(src.device());
+  auto a = ep_owner_args(peer_idx, peer_w, peer_rows, world, rank, N, k, d, lo, El, seg_start, cursor, meta,
+                         meta_w, n_uniq);
+  ddb::ep_owner_scatter_sum(a, reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0), weighted,
+                            reinterpret_cast<__nv_bfloat16* const*>(peer_ret.data_ptr<int64_t>()), stream());
+}
+
+torch::Tensor ep_source_reduce(torch::Tensor idx, torch::Tensor ret, int64_t El,
+                               c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> shared_w,
+                               c10::optional<torch::Tensor> slot_s, c10::optional<torch::Tensor> ys) {
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.dim() == 2 && idx.is_contiguous(), "idx [N, k] int32");
+  check_bf16(ret, "ret");
+  TORCH_CHECK(ret.is_contiguous() && ret.dim() == 2, "ret [world * N, d] contiguous");
+  const c10::cuda::CUDAGuard guard(ret.device());
+  ddb::EpSourceArgs a;
+  a.N = idx.size(0); a.k = idx.size(1); a.d = ret.size(1); a.El = El;
+  a.idx = idx.data_ptr<int>();
+  a.ret = reinterpret_cast<const __nv_bfloat16*>(ret.data_ptr());
+  if (residual) {
+    check_bf16(*residual, "residual");
+    check_rows(*residual, "residual");
+    a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    a.ld_res = residual->stride(0);
+  }
+  if (slot_s) {
+    TORCH_CHECK(ys.has_value(), "shared rows");
+    TORCH_CHECK(slot_s->scalar_type() == torch::kInt32 && slot_s->is_contiguous(), "slot_s int32");
+    check_bf16(*ys, "ys");
+    check_rows(*ys, "ys");
+    a.ns = slot_s->size(1);
+    a.slot_s = slot_s->data_ptr<int>();
+    a.ys = reinterpret_cast<const __nv_bfloat16*>(ys->data_ptr());
+    a.ld_ys = ys->stride(0);
+    if (shared_w) {
+      TORCH_CHECK(shared_w->scalar_type() == torch::kFloat32 && shared_w->is_contiguous(), "shared_w");
+      a.shared_w = shared_w->data_ptr<float>();
+    }
+  }
+  auto out = torch::empty({a.N, a.d}, ret.options());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ld_out = out.stride(0);
+  ddb::ep_source_reduce(a, stream());
+  return out;
+}
+
 // Row-block copies for expert parallelism: blocks [n, 4] int32 (src_rank, src_row, dst_rank,
 // dst_row), row_prefix [n] int32 (first flat row of each block). A side is either a table of
 // per-rank base pointers (int64 device array) or one local base pointer.
@@ -1077,6 +1190,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_bwd", &layernorm_bwd, "LayerNorm backward -> dx (accumulates dw, db)");
   m.def("video_augment", &video_augment, "fused flip/brightness/contrast/normalise of clips");
   m.def("ep_copy_rows", &ep_copy_rows, "row-block copies between local and peer buffers (EP)");
+  m.def("ep_owner_gather", &ep_owner_gather, "EP dispatch: owner pulls each routed token row once");
+  m.def("ep_owner_grad_gather", &ep_owner_grad_gather, "EP backward dispatch: dy rows and routing-weight grads");
+  m.def("ep_owner_scatter_sum", &ep_owner_scatter_sum, "EP combine: owner-side partial sums pushed to sources");
+  m.def("ep_source_reduce", &ep_source_reduce, "EP source-side sum of owner partials (+ shared, residual)",
+        py::arg("idx"), py::arg("ret"), py::arg("El"), py::arg("residual") = py::none(),
+        py::arg("shared_w") = py::none(), py::arg("slot_s") = py::none(), py::arg("ys") = py::none());
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
   m.def("read_status", &read_status, "device status word (0 = ok)");
   m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");

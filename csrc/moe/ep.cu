@@ -17,6 +17,7 @@
 #include <algorithm>
 #include <stdexcept>
 
+#include "../common/ptx.cuh"
 #include "../common/tma.h"
 #include "moe.h"
 
@@ -49,6 +50,214 @@ __global__ void __launch_bounds__(256) ep_copy_rows_kernel(EpCopyArgs a) {
   }
 }
 
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kMaxChunks = 8;  // rows of up to 8 x 256 bf16 = 2048 columns
+
+// Load one bf16 row (d columns, d % 8 == 0, d <= 2048) into registers: lane holds chunks
+// i * 256 + lane * 8 .. + 8.
+__device__ __forceinline__ void load_row(const __nv_bfloat16* row, int d, int lane, uint4 (&v)[kMaxChunks]) {
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = i * 256 + lane * 8;
+    if (c < d) v[i] = ld_global_v4(row + c);
+  }
+}
+
+__device__ __forceinline__ void store_row(__nv_bfloat16* row, int d, int lane, const uint4 (&v)[kMaxChunks]) {
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = i * 256 + lane * 8;
+    if (c < d) st_global_v4(row + c, v[i].x, v[i].y, v[i].z, v[i].w);
+  }
+}
+
+__device__ __forceinline__ void axpy_row(float (&acc)[kMaxChunks][8], float w, const __nv_bfloat16* row, int d,
+                                         int lane) {
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = i * 256 + lane * 8;
+    if (c < d) {
+      const uint4 y = ld_global_v4(row + c);
+      const uint32_t yw[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16(yw[q]);
+        acc[i][2 * q] += w * f.x;
+        acc[i][2 * q + 1] += w * f.y;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_acc(__nv_bfloat16* row, int d, int lane, const float (&acc)[kMaxChunks][8]) {
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = i * 256 + lane * 8;
+    if (c < d)
+      st_global_v4(row + c, pack_bf16(acc[i][0], acc[i][1]), pack_bf16(acc[i][2], acc[i][3]),
+                   pack_bf16(acc[i][4], acc[i][5]), pack_bf16(acc[i][6], acc[i][7]));
+  }
+}
+
+// One warp per (source, token): does the token route to one of my experts? Then pull its
+// row once (P2P loads) and write it into each of my expert segments it routes to.
+__global__ void __launch_bounds__(256) ep_owner_gather_kernel(EpOwnerArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long wi = blockIdx.x * 8L + (threadIdx.x >> 5);
+  if (wi >= static_cast<long>(a.world) * a.N) return;
+  const int s = static_cast<int>(wi / a.N), t = static_cast<int>(wi % a.N);
+  int e = -1;
+  float w = 0.f;
+  if (lane < a.k) {
+    e = a.peer_idx[s][static_cast<long>(t) * a.k + lane];
+    w = a.peer_w[s][static_cast<long>(t) * a.k + lane];
+  }
+  const bool mine = lane < a.k && e >= a.lo && e < a.lo + a.El;
+  const unsigned mask = __ballot_sync(kFull, mine);
+  if (mask == 0) return;
+  int slot = -1;
+  if (mine) slot = a.seg_start[e - a.lo] + atomicAdd(a.cursor + (e - a.lo), 1);
+  int u = 0;
+  if (lane == 0) u = atomicAdd(a.n_uniq, 1);
+  u = __shfl_sync(kFull, u, 0);
+  if (u >= a.cap) return;  // cap = world * N bounds every possible row
+  int* m = a.meta + static_cast<long>(u) * (2 + a.k);
+  if (lane == 0) {
+    m[0] = s;
+    m[1] = t;
+  }
+  if (lane < a.k) {
+    m[2 + lane] = slot;
+    a.meta_w[static_cast<long>(u) * a.k + lane] = mine ? w : 0.f;
+  }
+  uint4 v[kMaxChunks];
+  load_row(a.peer_rows[s] + static_cast<long>(t) * a.d, a.d, lane, v);
+  for (unsigned mm = mask; mm; mm &= mm - 1) {
+    const int j = __ffs(mm) - 1;
+    const int sl = __shfl_sync(kFull, slot, j);
+    store_row(a.xr + static_cast<long>(sl) * a.ld_xr, a.d, lane, v);
+  }
+}
+
+// One warp per unique row: z = sum_j w_j src[slot_j] -> the source's return buffer.
+__global__ void __launch_bounds__(256) ep_owner_scatter_sum_kernel(EpOwnerArgs a, const __nv_bfloat16* src,
+                                                                   long ld_src, bool weighted,
+                                                                   __nv_bfloat16* const* peer_ret) {
+  const int lane = threadIdx.x & 31;
+  const long u = blockIdx.x * 8L + (threadIdx.x >> 5);
+  if (u >= *a.n_uniq) return;
+  const int* m = a.meta + u * (2 + a.k);
+  const int s = m[0], t = m[1];
+  int sl = -1;
+  float wj = 0.f;
+  if (lane < a.k) {
+    sl = m[2 + lane];
+    wj = weighted ? a.meta_w[u * a.k + lane] : 1.f;
+  }
+  const unsigned mask = __ballot_sync(kFull, lane < a.k && sl >= 0);
+  float acc[kMaxChunks][8];
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i)
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
+  for (unsigned mm = mask; mm; mm &= mm - 1) {
+    const int j = __ffs(mm) - 1;
+    const int slj = __shfl_sync(kFull, sl, j);
+    const float w = __shfl_sync(kFull, wj, j);
+    axpy_row(acc, w, src + static_cast<long>(slj) * ld_src, a.d, lane);
+  }
+  store_acc(peer_ret[s] + (static_cast<long>(a.rank) * a.N + t) * a.d, a.d, lane, acc);
+}
+
+// One warp per unique row: pull dout once; dy[slot_j] = w_j dout; dw_j = dout . y[slot_j]
+// stored into the source's dw buffer.
+__global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a, const __nv_bfloat16* y,
+                                                                   long ld_y, __nv_bfloat16* dy, long ld_dy,
+                                                                   float* const* peer_dw) {
+  const int lane = threadIdx.x & 31;
+  const long u = blockIdx.x * 8L + (threadIdx.x >> 5);
+  if (u >= *a.n_uniq) return;
+  const int* m = a.meta + u * (2 + a.k);
+  const int s = m[0], t = m[1];
+  int sl = -1;
+  float wj = 0.f;
+  if (lane < a.k) {
+    sl = m[2 + lane];
+    wj = a.meta_w[u * a.k + lane];
+  }
+  const unsigned mask = __ballot_sync(kFull, lane < a.k && sl >= 0);
+  uint4 g[kMaxChunks];
+  load_row(a.peer_rows[s] + static_cast<long>(t) * a.d, a.d, lane, g);
+  for (unsigned mm = mask; mm; mm &= mm - 1) {
+    const int j = __ffs(mm) - 1;
+    const int slj = __shfl_sync(kFull, sl, j);
+    const float w = __shfl_sync(kFull, wj, j);
+    const __nv_bfloat16* yr = y + static_cast<long>(slj) * ld_y;
+    __nv_bfloat16* dr = dy + static_cast<long>(slj) * ld_dy;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = i * 256 + lane * 8;
+      if (c < a.d) {
+        const uint4 yv = ld_global_v4(yr + c);
+        const uint32_t gw[4] = {g[i].x, g[i].y, g[i].z, g[i].w}, yw[4] = {yv.x, yv.y, yv.z, yv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 fg = unpack_bf16(gw[q]), fy = unpack_bf16(yw[q]);
+          dot += fg.x * fy.x + fg.y * fy.y;
+          o[q] = pack_bf16(w * fg.x, w * fg.y);
+        }
+        st_global_v4(dr + c, o[0], o[1], o[2], o[3]);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(kFull, dot, off);
+    if (lane == 0) peer_dw[s][static_cast<long>(t) * a.k + j] = dot;
+  }
+}
+
+// One warp per local token: residual + the partial rows of every owner it routed to
+// (+ gated shared-expert rows).
+__global__ void __launch_bounds__(256) ep_source_reduce_kernel(EpSourceArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= a.N) return;
+  unsigned bits = 0;
+  if (lane < a.k) bits = 1u << (a.idx[static_cast<long>(t) * a.k + lane] / a.El);
+  const unsigned owners = __reduce_or_sync(kFull, bits);
+  float acc[kMaxChunks][8];
+  if (a.residual) {
+    uint4 r[kMaxChunks];
+    load_row(a.residual + static_cast<long>(t) * a.ld_res, a.d, lane, r);
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const uint32_t rw[4] = {r[i].x, r[i].y, r[i].z, r[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16(rw[q]);
+        acc[i][2 * q] = f.x;
+        acc[i][2 * q + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
+  }
+  for (unsigned mm = owners; mm; mm &= mm - 1) {
+    const int o = __ffs(mm) - 1;
+    axpy_row(acc, 1.f, a.ret + (static_cast<long>(o) * a.N + t) * a.d, a.d, lane);
+  }
+  for (int sh = 0; sh < a.ns; ++sh) {
+    const float gsh = a.shared_w ? a.shared_w[static_cast<long>(t) * a.ns + sh] : 1.f;
+    const int sl = a.slot_s[static_cast<long>(t) * a.ns + sh];
+    axpy_row(acc, gsh, a.ys + static_cast<long>(sl) * a.ld_ys, a.d, lane);
+  }
+  store_acc(a.out + static_cast<long>(t) * a.ld_out, a.d, lane, acc);
+}
+
 }  // namespace
 
 void ep_copy_rows(const EpCopyArgs& a, cudaStream_t stream) {
@@ -62,6 +271,52 @@ void ep_copy_rows(const EpCopyArgs& a, cudaStream_t stream) {
   ep_copy_rows_kernel<<<std::max(grid, 1), 256, 0, stream>>>(a);
   count_launch();
   check_cuda(cudaGetLastError(), "ep_copy_rows_kernel launch");
+}
+
+}  // namespace ddb
+
+namespace ddb {
+namespace {
+void check_owner(const EpOwnerArgs& a) {
+  if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
+  if (a.k > 32 || a.k < 1) throw std::runtime_error("ep: 1 <= k <= 32");
+  if (a.world > 32) throw std::runtime_error("ep: at most 32 ranks");
+}
+}  // namespace
+
+void ep_owner_gather(const EpOwnerArgs& a, cudaStream_t s) {
+  check_owner(a);
+  const long warps = static_cast<long>(a.world) * a.N;
+  if (warps == 0) return;
+  ep_owner_gather_kernel<<<static_cast<int>((warps + 7) / 8), 256, 0, s>>>(a);
+  count_launch();
+  check_cuda(cudaGetLastError(), "ep_owner_gather launch");
+}
+
+void ep_owner_grad_gather(const EpOwnerArgs& a, const __nv_bfloat16* y, long ld_y, __nv_bfloat16* dy,
+                          long ld_dy, float* const* peer_dw, cudaStream_t s) {
+  check_owner(a);
+  if (a.cap == 0) return;
+  ep_owner_grad_gather_kernel<<<(a.cap + 7) / 8, 256, 0, s>>>(a, y, ld_y, dy, ld_dy, peer_dw);
+  count_launch();
+  check_cuda(cudaGetLastError(), "ep_owner_grad_gather launch");
+}
+
+void ep_owner_scatter_sum(const EpOwnerArgs& a, const __nv_bfloat16* src, long ld_src, bool weighted,
+                          __nv_bfloat16* const* peer_ret, cudaStream_t s) {
+  check_owner(a);
+  if (a.cap == 0) return;
+  ep_owner_scatter_sum_kernel<<<(a.cap + 7) / 8, 256, 0, s>>>(a, src, ld_src, weighted, peer_ret);
+  count_launch();
+  check_cuda(cudaGetLastError(), "ep_owner_scatter_sum launch");
+}
+
+void ep_source_reduce(const EpSourceArgs& a, cudaStream_t s) {
+  if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
+  if (a.N == 0) return;
+  ep_source_reduce_kernel<<<(a.N + 7) / 8, 256, 0, s>>>(a);
+  count_launch();
+  check_cuda(cudaGetLastError(), "ep_source_reduce launch");
 }
 
 }  // namespace ddb

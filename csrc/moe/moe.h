@@ -66,4 +66,54 @@ struct EpCopyArgs {
 };
 void ep_copy_rows(const EpCopyArgs& a, cudaStream_t stream);
 
+// ---- expert parallelism, owner-driven with one row per (token, owner rank)
+// Every rank exposes its routing (topk idx / weights), its FFN input rows h and, in
+// backward, its output gradient rows in peer-mapped buffers. The owner of experts
+// [lo, lo + El) reads every source's routing, pulls each source token that routes to
+// one of its experts ONCE and writes it to each of its local expert segments; after the
+// expert GEMMs it sums the token's local expert outputs (weighted) and stores that one
+// row into the source's return buffer. Sources add the rows of the owners they used.
+struct EpOwnerArgs {
+  int world = 0, rank = 0, N = 0, k = 0, d = 0, lo = 0, El = 0;
+  const int* const* peer_idx = nullptr;              // [world] -> [N, k] int32 routed expert ids
+  const float* const* peer_w = nullptr;              // [world] -> [N, k] fp32 routed weights
+  const __nv_bfloat16* const* peer_rows = nullptr;   // [world] -> [N, d] rows (h, or dout)
+  const int* seg_start = nullptr;                    // [El] owner-layout segment starts
+  int* cursor = nullptr;                             // [El] zeroed
+  __nv_bfloat16* xr = nullptr;                       // owner layout rows
+  long ld_xr = 0;
+  // unique (source, token) rows that route here: [cap] x (2 + k) int32 = (s, t, slot per route
+  // or -1) and [cap] x k fp32 weights; count in *n_uniq
+  int* meta = nullptr;
+  float* meta_w = nullptr;
+  int* n_uniq = nullptr;
+  int cap = 0;
+};
+// forward dispatch: fills xr (owner layout), meta, meta_w, n_uniq
+void ep_owner_gather(const EpOwnerArgs& a, cudaStream_t s);
+// backward dispatch: per unique row pulls dout (peer_rows) once, writes dy[slot] = w dout and
+// stores dw = dout . y[slot] into the source's dw buffer (peer_dw[s][t * k + j])
+void ep_owner_grad_gather(const EpOwnerArgs& a, const __nv_bfloat16* y, long ld_y, __nv_bfloat16* dy,
+                          long ld_dy, float* const* peer_dw, cudaStream_t s);
+// owner combine: per unique row z = sum_j (weighted ? w_j : 1) src[slot_j]; stored (bf16) into
+// peer_ret[s] + ((rank * N) + t) * d
+void ep_owner_scatter_sum(const EpOwnerArgs& a, const __nv_bfloat16* src, long ld_src, bool weighted,
+                          __nv_bfloat16* const* peer_ret, cudaStream_t s);
+// source combine: out[t] = residual[t] + sum_{owners o of t's experts} ret[o * N + t]
+//                          + sum_s g[t, s] shared[slot_of_s[t, s]]   (g = 1 when shared_w null)
+struct EpSourceArgs {
+  int N = 0, k = 0, d = 0, El = 0, ns = 0;
+  const int* idx = nullptr;                 // [N, k]
+  const __nv_bfloat16* ret = nullptr;       // [world * N, d]
+  const __nv_bfloat16* residual = nullptr;  // [N, d] or null
+  long ld_res = 0;
+  const float* shared_w = nullptr;          // [N, ns] or null (unit gates)
+  const int* slot_s = nullptr;              // [N, ns]
+  const __nv_bfloat16* ys = nullptr;        // shared-expert rows
+  long ld_ys = 0;
+  __nv_bfloat16* out = nullptr;
+  long ld_out = 0;
+};
+void ep_source_reduce(const EpSourceArgs& a, cudaStream_t s);
+
 }  // namespace ddb

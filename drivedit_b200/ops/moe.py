@@ -143,14 +143,189 @@ def _grouped_ffn_bwd(dy, x, gu, act, w13, w2, g13, g2, tables, Fh):
     return dx
 
 
-def moe_ffn_forward_ep(h: torch.Tensor, residual: torch.Tensor, moe, W):
-    """Expert-parallel form of :func:`moe_ffn_forward` (``moe.ep`` set).
+def _route(h, moe, W):
+    E, k, ns = moe.num_experts, moe.top_k, moe.num_shared_experts
+    logits = gemm(h, W(moe.router_weight), epi="f32")
+    return ext().moe_route(logits, moe.expert_bias, E, k, ns, True)
 
-    route (local) -> count table exchange -> compact dispatch of the routed rows into the
-    send buffer (shared-expert rows into the local shared layout) -> owner pull into the
-    grouped-GEMM layout -> local experts' grouped GEMMs -> push of the outputs into the
-    sources' return buffers (the shared experts' GEMMs run meanwhile) -> combine.
-    """
+
+def _shared_forward(h, moe, W, ep):
+    """Shared experts on the local tokens: dispatch into their 128-row segments and the
+    grouped SwiGLU FFN. Returns (slot_of [N, ns], xs, gu, act, y, tables) or Nones."""
+    ns = moe.num_shared_experts
+    if not ns:
+        return None, None, None, None, None, None
+    N, d = h.shape
+    sp, mt_s = ep.shared_plan(N, ns)
+    xs = torch.empty(mt_s * 128, d, device=h.device, dtype=torch.bfloat16)
+    none = torch.empty(N, 0, device=h.device, dtype=torch.int32)
+    slot_s = ext().moe_dispatch(h, none, sp[0], sp[1], sp[7], xs, 0, ns)
+    tables = (sp[2], sp[3], sp[4], sp[5], sp[6], mt_s)
+    gu, act, y = _grouped_ffn(xs, W(moe.w13_shared), W(moe.w2_shared), tables, moe.expert_dim)
+    return slot_s, xs, gu, act, y, tables
+
+
+def _shared_backward(dout, moe, W, sv):
+    """(dw_shared [N, ns], dx rows of the shared segments) for the local tokens."""
+    ns = moe.num_shared_experts
+    N, d = dout.shape
+    if not ns:
+        return torch.empty(N, 0, device=dout.device), None
+    w0 = torch.empty(N, 0, device=dout.device, dtype=torch.float32)
+    dys, dws = ext().moe_combine_bwd(w0, sv["sw"], sv["slot_s"], sv["y_s"], dout, ns)
+    Fh = moe.expert_dim
+    dxs = _grouped_ffn_bwd(dys, sv["xs"], sv["gu_s"], sv["act_s"], W(moe.w13_shared), W(moe.w2_shared),
+                           moe.w13_shared.grad.view(ns * 2 * Fh, d), moe.w2_shared.grad.view(ns * d, Fh),
+                           sv["tables_s"], Fh)
+    return dws, dxs
+
+
+def _router_backward(h, dw, d_aux, dh, moe, W, sv):
+    E, k, ns = moe.num_experts, moe.top_k, moe.num_shared_experts
+    dlog = router_dlogits(sv["probs"], sv["idx"], sv["w"], sv["sw"], dw, d_aux, sv["f"],
+                          E, k, ns, moe.e_pad)
+    dlog = dlog.to(torch.bfloat16)
+    gemm(dlog, h, moe.router_weight.grad, epi="f32_acc", a_t=True, b_t=True)
+    gemm(dlog, W(moe.router_weight), dh, b_t=True, residual=dh)
+    return dh
+
+
+def _finish_forward(moe, ep, counts, psum, table, N):
+    E, k = moe.num_experts, moe.top_k
+    f = counts.float() / (N * k)
+    aux = E * (f * (psum / N)).sum()
+    gcounts = torch.from_numpy(table.sum(0)).to(counts.device, non_blocking=True)
+    moe.update_bias(gcounts, N * ep.world)
+    return f, aux
+
+
+def _owner_plan(ep, plan, N, device):
+    """Owner-layout tables of this rank's local experts (counts from the table)."""
+    lcounts = torch.from_numpy(plan.local_counts.astype("int32")).to(device, non_blocking=True)
+    rp = ext().moe_plan(lcounts, ep.local_experts, 0, N, max(plan.owner_mtiles, 1))
+    return rp, (rp[2], rp[3], rp[4], rp[5], rp[6], plan.owner_mtiles)
+
+
+def moe_ffn_forward_ep(h: torch.Tensor, residual: torch.Tensor, moe, W):
+    """Expert-parallel form of :func:`moe_ffn_forward` (``moe.ep`` set): the
+    ``fused`` transport moves rows over NVLink peer memory, ``nccl`` with all-to-all."""
+    if moe.ep.transport == "fused":
+        return _ep_forward_fused(h, residual, moe, W)
+    return _ep_forward_nccl(h, residual, moe, W)
+
+
+def moe_ffn_backward_ep(dout: torch.Tensor, d_aux, moe, W, sv) -> torch.Tensor:
+    if moe.ep.transport == "fused":
+        return _ep_backward_fused(dout, d_aux, moe, W, sv)
+    return _ep_backward_nccl(dout, d_aux, moe, W, sv)
+
+
+# ---- fused transport: owner-driven, one row per (token, owner rank) each way
+def _expose(ep, idx, w, h) -> bool:
+    """Copy this rank's routing and rows into its peer-readable buffers when they are
+    large enough (every rank decides alike: equal token counts, buffers grown together)."""
+    N, k = idx.shape
+    d = h.shape[1]
+    rb, hb = ep._sym.get("route"), ep._sym.get("rows")
+    if rb is None or hb is None or rb.nbytes < N * k * 8 or hb.nbytes < N * d * 2:
+        return False
+    rb.tensor(N * k, torch.int32).view(N, k).copy_(idx)
+    rb.tensor(N * k, torch.float32, N * k * 4).view(N, k).copy_(w)
+    hb.tensor(N * d, torch.bfloat16).view(N, d).copy_(h)
+    return True
+
+
+def _ep_forward_fused(h, residual, moe, W):
+    """route -> routing and rows exposed in peer memory -> count table (one host sync) ->
+    every owner pulls each source token routed to its experts once, fanned out into its
+    expert segments (``ep_owner_gather``) -> local experts' grouped GEMMs -> per-token
+    partial sums over the owner's experts stored into the sources' return buffers
+    (``ep_owner_scatter_sum``; the shared experts' GEMMs run meanwhile) -> barrier ->
+    ``ep_source_reduce``: residual + the owners' partials + gated shared experts."""
+    from ..parallel.expert import EpPlan
+
+    ep = moe.ep
+    N, d = h.shape
+    E, k, ns, Fh = moe.num_experts, moe.top_k, moe.num_shared_experts, moe.expert_dim
+    El = ep.local_experts
+    lo = ep.rank * El
+    idx, w, sw, probs, counts, psum = _route(h, moe, W)
+    fast = _expose(ep, idx, w, h)
+    table = ep.exchange_counts(counts)            # barrier: counts, routing and rows visible
+    if not (table.sum(1) == N * k).all():
+        raise RuntimeError("expert parallelism needs the same number of tokens on every rank")
+    if not fast:                                  # first use / growth: every rank alike
+        ep.sym("route", N * k * 8)
+        ep.sym("rows", N * d * 2)
+        _expose(ep, idx, w, h)
+        ep.barrier()
+    plan = EpPlan(ep, table)
+    rp, tables_r = _owner_plan(ep, plan, N, h.device)
+    cap = ep.world * N
+    meta = torch.empty(cap, 2 + k, device=h.device, dtype=torch.int32)
+    meta_w = torch.empty(cap, k, device=h.device, dtype=torch.float32)
+    n_uniq = torch.zeros(1, device=h.device, dtype=torch.int32)
+    xr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
+    rt, ht = ep._sym["route"], ep._sym["rows"]
+    base = (rt.table, ep.slot_table("route", 1, N * k * 4), ht.table, ep.world, ep.rank, N, k, d, lo, El,
+            rp[0], rp[7], meta, meta_w, n_uniq)
+    ext().ep_owner_gather(*base, xr)
+    gu_r = act_r = None
+    y_r = xr
+    if plan.owner_rows:
+        ext().moe_zero_pad(rp[0], rp[1], xr)
+        gu_r, act_r, y_r = _grouped_ffn(xr, W(moe.w13), W(moe.w2), tables_r, Fh)
+    ret = ep.sym("ret", cap * d * 2)
+    ext().ep_owner_scatter_sum(*base, y_r, True, ret.table)
+    slot_s, xs, gu_s, act_s, y_s, tables_s = _shared_forward(h, moe, W, ep)
+    ep.barrier()                                  # every owner's partial rows have landed
+    out = ext().ep_source_reduce(idx, ret.tensor(cap * d, torch.bfloat16).view(cap, d), El, residual,
+                                 sw if ns else None, slot_s, y_s)
+    f, aux = _finish_forward(moe, ep, counts, psum, table, N)
+    saved = dict(h=h, idx=idx, w=w, sw=sw, probs=probs, f=f, plan=plan, owner=base[3:], rp=rp,
+                 tables_r=tables_r, xr=xr, gu_r=gu_r, act_r=act_r, y_r=y_r, slot_s=slot_s, xs=xs,
+                 gu_s=gu_s, act_s=act_s, y_s=y_s, tables_s=tables_s)
+    return out, aux, saved
+
+
+def _ep_backward_fused(dout, d_aux, moe, W, sv):
+    """dout exposed in peer memory -> barrier -> owners pull each (token, owner) dout row
+    once, write ``dy = w dout`` into their segments and store ``dw = dout . y`` into the
+    source (``ep_owner_grad_gather``) -> local experts' backward GEMMs -> per-token sums
+    of ``dx`` over the owner's experts pushed back -> barrier -> sources add them up."""
+    ep = moe.ep
+    h = sv["h"]
+    N, d = h.shape
+    k, ns, Fh = moe.top_k, moe.num_shared_experts, moe.expert_dim
+    El = ep.local_experts
+    plan = sv["plan"]
+    cap = ep.world * N
+    drows = ep.sym("drows", N * d * 2)
+    drows.tensor(N * d, torch.bfloat16).view(N, d).copy_(dout)
+    dwb = ep.sym("dw", N * k * 4)
+    dws, dxs = _shared_backward(dout, moe, W, sv)
+    ep.barrier()                                  # every rank's dout rows are visible
+    rt = ep._sym["route"]
+    owner = (rt.table, ep.slot_table("route", 1, N * k * 4), drows.table) + sv["owner"]
+    dyr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
+    ext().ep_owner_grad_gather(*owner, sv["y_r"], dyr, dwb.table)
+    dxr = dyr
+    if plan.owner_rows:
+        ext().moe_zero_pad(sv["rp"][0], sv["rp"][1], dyr)
+        dxr = _grouped_ffn_bwd(dyr, sv["xr"], sv["gu_r"], sv["act_r"], W(moe.w13), W(moe.w2),
+                               moe.w13.grad.view(El * 2 * Fh, d), moe.w2.grad.view(El * d, Fh),
+                               sv["tables_r"], Fh)
+    dret = ep.sym("dret", cap * d * 2)
+    ext().ep_owner_scatter_sum(*owner, dxr, False, dret.table)
+    ep.barrier()                                  # every dx partial and dw value has landed
+    dh = ext().ep_source_reduce(sv["idx"], dret.tensor(cap * d, torch.bfloat16).view(cap, d), El,
+                                None, None, sv["slot_s"], dxs)
+    dw = torch.cat([dwb.tensor(N * k, torch.float32).view(N, k), dws], 1)
+    return _router_backward(h, dw, d_aux, dh, moe, W, sv)
+
+
+# ---- nccl transport: compact rows sorted by expert, all_to_all, local re-layout
+def _ep_forward_nccl(h, residual, moe, W):
     import torch.distributed as dist
 
     from ..parallel.expert import EpPlan, ep_move, upload_packet
@@ -159,79 +334,47 @@ def moe_ffn_forward_ep(h: torch.Tensor, residual: torch.Tensor, moe, W):
     N, d = h.shape
     E, k, ns, Fh = moe.num_experts, moe.top_k, moe.num_shared_experts, moe.expert_dim
     El = ep.local_experts
-    fused = ep.transport == "fused"
-    logits = gemm(h, W(moe.router_weight), epi="f32")
-    idx, w, sw, probs, counts, psum = ext().moe_route(logits, moe.expert_bias, E, k, ns, True)
-    table = ep.exchange_counts(counts)                       # host: [W, E]
+    idx, w, sw, probs, counts, psum = _route(h, moe, W)
+    table = ep.exchange_counts(counts)
     plan = EpPlan(ep, table)
     arr, sizes, nb = plan.packet(ep, N, ns, k)
     pull_b, pull_p, push_b, push_p, lcounts, seg_start, seg_count, cursor = upload_packet(
         arr, sizes, h.device)
     rb = 2 * d
-    cap = int(table.sum(1).max())                            # same on every rank
-    assert plan.n_routed == N * k
-    xs = None
-    if ns:
-        sp, mt_s = ep.shared_plan(N, ns)
-        xs = torch.empty(mt_s * 128, d, device=h.device, dtype=torch.bfloat16)
-    if fused:
-        sbuf = ep.sym("send", cap * rb)
-        send = sbuf.tensor(cap * d, torch.bfloat16).view(cap, d)
-    else:
-        send = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
-    slot_of = ext().moe_dispatch(h, idx, seg_start, seg_count, cursor, send, E, ns, xs, False)
-    # ---- dispatch: the owner gathers its experts' rows from every source
+    send = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
+    # routed rows only (compact, sorted by expert); shared experts go their own way
+    slot_of = ext().moe_dispatch(h, idx, seg_start[:E], seg_count[:E], cursor[:E], send, E, 0, None, False)
+    recv = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
+    dist.all_to_all_single(recv[:plan.n_recv], send[:N * k], plan.recv_splits, plan.send_splits,
+                           group=ep.group)
     xr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
-    if fused:
-        ep.barrier()                                         # every send buffer is complete
-        ep_move(pull_b, pull_p, plan.n_recv, rb, src_table=sbuf.table, dst=xr)
-    else:
-        recv = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
-        dist.all_to_all_single(recv[:plan.n_recv], send[:N * k], plan.recv_splits, plan.send_splits,
-                               group=ep.group)
-        ep_move(pull_b, pull_p, plan.n_recv, rb, src=recv, dst=xr)
-    rp = ext().moe_plan(lcounts, El, 0, N, max(plan.owner_mtiles, 1))
-    seg_r = (rp[0], rp[1])
-    tables_r = (rp[2], rp[3], rp[4], rp[5], rp[6], plan.owner_mtiles)
-    w13, w2 = W(moe.w13), W(moe.w2)
+    ep_move(pull_b, pull_p, plan.n_recv, rb, src=recv, dst=xr)
+    rp, tables_r = _owner_plan(ep, plan, N, h.device)
     gu_r = act_r = None
     y_r = xr
     if plan.owner_rows:
-        ext().moe_zero_pad(seg_r[0], seg_r[1], xr)
-        gu_r, act_r, y_r = _grouped_ffn(xr, w13, w2, tables_r, Fh)
-    # ---- combine side: outputs back to the sources' compact return buffers
-    if fused:
-        rbuf = ep.sym("ret", ep.n_layers * cap * rb)
-        ret_tab = ep.slot_table("ret", moe.ep_slot, cap * rb)
-        ep_move(push_b, push_p, plan.n_recv, rb, src=y_r, dst_table=ret_tab)
-        yret = rbuf.tensor(cap * d, torch.bfloat16, moe.ep_slot * cap * rb).view(cap, d)
+        ext().moe_zero_pad(rp[0], rp[1], xr)
+        gu_r, act_r, y_r = _grouped_ffn(xr, W(moe.w13), W(moe.w2), tables_r, Fh)
+    stage = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
+    ep_move(push_b, push_p, plan.n_recv, rb, src=y_r, dst=stage)
+    yret = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
+    dist.all_to_all_single(yret[:N * k], stage[:plan.n_recv], plan.send_splits, plan.recv_splits,
+                           group=ep.group)
+    slot_s, xs, gu_s, act_s, y_s, tables_s = _shared_forward(h, moe, W, ep)
+    if ns:   # routed slots index yret, shared slots index y_s
+        slot_all = torch.cat([slot_of, slot_s], 1).contiguous()
+        out = ext().moe_combine(w, sw, slot_all, yret, residual, ns, y_s)
     else:
-        stage = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
-        ep_move(push_b, push_p, plan.n_recv, rb, src=y_r, dst=stage)
-        yret = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
-        dist.all_to_all_single(yret[:N * k], stage[:plan.n_recv], plan.send_splits, plan.recv_splits,
-                               group=ep.group)
-    gu_s = act_s = y_s = None
-    if ns:   # shared experts on the local tokens while the peers finish
-        tables_s = (sp[2], sp[3], sp[4], sp[5], sp[6], mt_s)
-        gu_s, act_s, y_s = _grouped_ffn(xs, W(moe.w13_shared), W(moe.w2_shared), tables_s, Fh)
-    if fused:
-        ep.barrier()                                         # every return row has landed
-    out = ext().moe_combine(w, sw, slot_of, yret, residual, ns, y_s)
-    f = counts.float() / (N * k)
-    aux = E * (f * (psum / N)).sum()
-    gcounts = torch.from_numpy(table.sum(0)).to(h.device, non_blocking=True)
-    moe.update_bias(gcounts, N * ep.world)
+        out = ext().moe_combine(w, sw, slot_of, yret, residual, 0)
+    f, aux = _finish_forward(moe, ep, counts, psum, table, N)
     saved = dict(h=h, idx=idx, w=w, sw=sw, probs=probs, f=f, slot_of=slot_of, plan=plan,
-                 pull=(pull_b, pull_p), push=(push_b, push_p), cap=cap, xr=xr, gu_r=gu_r,
-                 act_r=act_r, seg_r=seg_r, tables_r=tables_r, yret=yret, xs=xs, gu_s=gu_s,
-                 act_s=act_s, y_s=y_s, tables_s=tables_s if ns else None)
+                 pull=(pull_b, pull_p), push=(push_b, push_p), xr=xr, gu_r=gu_r, act_r=act_r,
+                 rp=rp, tables_r=tables_r, yret=yret, slot_s=slot_s, xs=xs, gu_s=gu_s, act_s=act_s,
+                 y_s=y_s, tables_s=tables_s)
     return out, aux, saved
 
 
-def moe_ffn_backward_ep(dout: torch.Tensor, d_aux, moe, W, sv) -> torch.Tensor:
-    """Backward of :func:`moe_ffn_forward_ep`: ``dy`` rows travel to the experts' owners
-    (pull), the local experts' backward GEMMs run there, ``dx`` rows travel back (push)."""
+def _ep_backward_nccl(dout, d_aux, moe, W, sv):
     import torch.distributed as dist
 
     from ..parallel.expert import ep_move
@@ -241,55 +384,28 @@ def moe_ffn_backward_ep(dout: torch.Tensor, d_aux, moe, W, sv) -> torch.Tensor:
     N, d = h.shape
     E, k, ns, Fh = moe.num_experts, moe.top_k, moe.num_shared_experts, moe.expert_dim
     El = ep.local_experts
-    fused = ep.transport == "fused"
-    plan, cap, rb = sv["plan"], sv["cap"], 2 * d
-    if fused:
-        dsb = ep.sym("dsend", cap * rb)
-        dsend = dsb.tensor(cap * d, torch.bfloat16).view(cap, d)
-    else:
-        dsend = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
-    res = ext().moe_combine_bwd(sv["w"], sv["sw"], sv["slot_of"], sv["yret"], dout, ns, sv["y_s"],
-                                dsend, None)
-    dw = res[1]
-    dys = res[2] if ns else None
+    plan, rb = sv["plan"], 2 * d
+    dy_c, dw_r = ext().moe_combine_bwd(sv["w"], sv["sw"], sv["slot_of"], sv["yret"], dout, 0)
+    recv = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
+    dist.all_to_all_single(recv[:plan.n_recv], dy_c[:N * k], plan.recv_splits, plan.send_splits,
+                           group=ep.group)
     dyr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
-    pull_b, pull_p = sv["pull"]
-    if fused:
-        ep.barrier()                                         # every dy row is written
-        ep_move(pull_b, pull_p, plan.n_recv, rb, src_table=dsb.table, dst=dyr)
-    else:
-        recv = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
-        dist.all_to_all_single(recv[:plan.n_recv], dsend[:N * k], plan.recv_splits, plan.send_splits,
-                               group=ep.group)
-        ep_move(pull_b, pull_p, plan.n_recv, rb, src=recv, dst=dyr)
+    ep_move(*sv["pull"], plan.n_recv, rb, src=recv, dst=dyr)
     dxr = dyr
     if plan.owner_rows:
-        ext().moe_zero_pad(sv["seg_r"][0], sv["seg_r"][1], dyr)
+        ext().moe_zero_pad(sv["rp"][0], sv["rp"][1], dyr)
         dxr = _grouped_ffn_bwd(dyr, sv["xr"], sv["gu_r"], sv["act_r"], W(moe.w13), W(moe.w2),
                                moe.w13.grad.view(El * 2 * Fh, d), moe.w2.grad.view(El * d, Fh),
                                sv["tables_r"], Fh)
-    push_b, push_p = sv["push"]
-    if fused:
-        drb = ep.sym("dret", cap * rb)
-        ep_move(push_b, push_p, plan.n_recv, rb, src=dxr, dst_table=drb.table)
-        dret = drb.tensor(cap * d, torch.bfloat16).view(cap, d)
+    stage = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
+    ep_move(*sv["push"], plan.n_recv, rb, src=dxr, dst=stage)
+    dret = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
+    dist.all_to_all_single(dret[:N * k], stage[:plan.n_recv], plan.send_splits, plan.recv_splits,
+                           group=ep.group)
+    dws, dxs = _shared_backward(dout, moe, W, sv)
+    if ns:   # routed slots index dret, shared slots index dxs
+        dh = ext().moe_unpermute(dret, torch.cat([sv["slot_of"], sv["slot_s"]], 1).contiguous(), N, dxs, k)
     else:
-        stage = torch.empty(max(plan.n_recv, 1), d, device=h.device, dtype=torch.bfloat16)
-        ep_move(push_b, push_p, plan.n_recv, rb, src=dxr, dst=stage)
-        dret = torch.empty(max(N * k, 1), d, device=h.device, dtype=torch.bfloat16)
-        dist.all_to_all_single(dret[:N * k], stage[:plan.n_recv], plan.send_splits, plan.recv_splits,
-                               group=ep.group)
-    dxs = None
-    if ns:
-        dxs = _grouped_ffn_bwd(dys, sv["xs"], sv["gu_s"], sv["act_s"], W(moe.w13_shared),
-                               W(moe.w2_shared), moe.w13_shared.grad.view(ns * 2 * Fh, d),
-                               moe.w2_shared.grad.view(ns * d, Fh), sv["tables_s"], Fh)
-    if fused:
-        ep.barrier()                                         # every dx row has landed
-    dh = ext().moe_unpermute(dret, sv["slot_of"], N, dxs, k)
-    dlog = router_dlogits(sv["probs"], sv["idx"], sv["w"], sv["sw"], dw, d_aux, sv["f"],
-                          E, k, ns, moe.e_pad)
-    dlog = dlog.to(torch.bfloat16)
-    gemm(dlog, h, moe.router_weight.grad, epi="f32_acc", a_t=True, b_t=True)
-    gemm(dlog, W(moe.router_weight), dh, b_t=True, residual=dh)
-    return dh
+        dh = ext().moe_unpermute(dret, sv["slot_of"], N)
+    dw = torch.cat([dw_r, dws], 1)
+    return _router_backward(h, dw, d_aux, dh, moe, W, sv)

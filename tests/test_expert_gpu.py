@@ -1,8 +1,8 @@
 """Expert-parallel MoE on the GPU kernels.
 
-* one rank (one GPU): the expert-parallel kernel path (compact dispatch, owner layout,
-  peer-copy pull/push through the rank's own symmetric buffers, shared experts apart)
-  reproduces the single-device MoE kernel path exactly on the same weights;
+* one rank (one GPU): the expert-parallel kernel path (owner gather of token rows from
+  the peer-mapped buffers, owner-side partial sums, shared experts apart) reproduces the
+  single-device MoE kernel path on the same weights;
 * two ranks (two GPUs): one fsdp_ep training step with the peer-memory transport matches
   the NCCL all-to-all transport and plain fsdp (every expert on every rank).
 """
@@ -124,7 +124,7 @@ def test_expert_parallel_kernel_path_matches_local_one_gpu():
     for key in ("out", "dh", "w13", "w2", "router"):
         x, y = a[key], b[key]
         err = np.linalg.norm(x - y) / (np.linalg.norm(x) + 1e-12)
-        assert err < 2e-3, (key, err)
+        assert err < 5e-3, (key, err)   # owner partial sums are rounded to bf16 once more
 
 
 # ----------------------------------------------------------------------------- two GPUs
@@ -175,11 +175,10 @@ def test_fsdp_ep_two_gpus_matches_nccl_and_fsdp():
     E = 8
     for r in range(world):
         a, b, c = res[r]["ep_fused"], res[r]["ep_nccl"], res[r]["fsdp"]
-        # same kernels, different transport: the same numbers up to the optimizer's
-        # clipping-norm arithmetic
-        assert a["loss"][0] == b["loss"][0], (a["loss"], b["loss"])
-        assert abs(a["loss"][1] - b["loss"][1]) < 1e-4 * abs(b["loss"][1])
-        for key, tol in (("sd1", 1e-4), ("sd2", 2e-3)):   # step 2 runs on re-rounded bf16 weights
+        # peer-memory transport (per-owner partial sums) against the all-to-all transport
+        assert abs(a["loss"][0] - b["loss"][0]) < 1e-3 * abs(b["loss"][0]), (a["loss"], b["loss"])
+        assert abs(a["loss"][1] - b["loss"][1]) < 1e-3 * abs(b["loss"][1])
+        for key, tol in (("sd1", 2e-3), ("sd2", 5e-3)):   # step 2 runs on re-rounded bf16 weights
             for n in a[key]:
                 err = np.linalg.norm(a[key][n] - b[key][n]) / (np.linalg.norm(b[key][n]) + 1e-12)
                 assert err < tol, (key, n, err)
