@@ -9,6 +9,7 @@
   *self*-attention and never projects ``context``; here the cross-attention attends to the
   projected context.
 * :class:`MemoryEfficientDiTBlock` (:249-307): activation checkpointing wrapper.
+* :class:`MoEDiTBlock` (``layers/moe.py:427-547``): the same block with the MoE FFN.
 * :class:`FlowMatchingBlock` / :class:`FlowPredictor` (flow_matching.py:94-218): 6-way
   AdaLN-Zero modulation from the time embedding, zero-initialised output.
 """
@@ -90,9 +91,61 @@ class MemoryEfficientDiTBlock(DiTBlock):
         return super().forward(x, kv_cache, pos, cond, causal_mask, start_pos)
 
 
+class MoEDiTBlock(DiTBlock):
+    """DiT block whose FFN is the DeepSeek-style MoE (reference ``layers/moe.py:427-547``):
+    returns ``(x, kv_cache)`` like :class:`DiTBlock`; the last load-balance loss and
+    (when asked for) routing metrics stay on the block."""
+
+    def __init__(self, d_model: int, n_heads: int, num_experts: int = 8, top_k: int = 2,
+                 expert_dim: Optional[int] = None, num_shared_experts: int = 0, dropout: float = 0.0,
+                 causal: bool = True, use_rope: bool = True, max_seq_len: int = 2048,
+                 cond_dim: Optional[int] = None, bias: bool = False, jitter_noise: float = 0.0,
+                 bias_update_speed: float = 0.001, aux_loss_weight: float = 0.0,
+                 tokens_per_frame: Optional[int] = None):
+        from ..layers.moe import MoEFFN
+
+        super().__init__(d_model, n_heads, d_ff=None, dropout=dropout, causal=causal, use_rope=use_rope,
+                         max_seq_len=max_seq_len, cond_dim=cond_dim, bias=bias,
+                         tokens_per_frame=tokens_per_frame)
+        del self.mlp
+        self.moe_ffn = MoEFFN(d_model, num_experts, top_k, expert_dim, num_shared_experts, dropout,
+                              jitter_noise=jitter_noise, bias_update_speed=bias_update_speed,
+                              aux_loss_weight=aux_loss_weight)
+        self._last_moe_metrics = None
+        self._last_aux_loss = None
+
+    def forward(self, x, kv_cache=None, pos=None, cond=None, causal_mask=None, start_pos=None,
+                return_moe_metrics: bool = False):
+        h = self._norm(self.norm_attn, x, cond)
+        if causal_mask is not None:
+            a, new_cache = MultiHeadAttention.forward(self.attn, h, kv_cache, causal_mask, start_pos)
+        else:
+            a, new_cache = self.attn(h, kv_cache=kv_cache, start_pos=start_pos)
+        x = x + a
+        out = self.moe_ffn(self._norm(self.norm_mlp, x, cond), return_metrics=return_moe_metrics)
+        self._last_aux_loss = out.aux_loss
+        if return_moe_metrics:
+            self._last_moe_metrics = out.metrics
+        return x + out.output, new_cache
+
+    def get_aux_loss(self):
+        return self._last_aux_loss
+
+    def get_moe_metrics(self):
+        return self._last_moe_metrics
+
+    def get_load_balance_stats(self):
+        return self.moe_ffn.get_load_balance_stats()
+
+
+def create_moe_dit_block(d_model: int, n_heads: int, num_experts: int = 8, top_k: int = 2,
+                         **kw) -> MoEDiTBlock:
+    return MoEDiTBlock(d_model, n_heads, num_experts=num_experts, top_k=top_k, **kw)
+
+
 def create_dit_block(block_type: str = "standard", **kw) -> nn.Module:
     return {"standard": DiTBlock, "cross_attention": DiTBlockWithCrossAttention,
-            "memory_efficient": MemoryEfficientDiTBlock}[block_type](**kw)
+            "memory_efficient": MemoryEfficientDiTBlock, "moe": MoEDiTBlock}[block_type](**kw)
 
 
 # ----------------------------------------------------------------------------- flow matching
