@@ -626,3 +626,7 @@ def get_minimal_config() -> SelfForcingPlusConfig:
                                  kv_cache_max_length=128, kv_cache_truncate_to=64,
                                  curriculum_warmup_steps=1000, sequence_curriculum_steps=2000,
                                  self_forcing_warmup_steps=2000)
+
+
+# first-generation self-forcing trainer (frame -> frame models), kept under the same module
+from .self_forcing_v1 import SelfForcingTrainer, create_dummy_dataloader, create_simple_model  # noqa: E402,F401
