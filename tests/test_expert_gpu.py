@@ -144,12 +144,13 @@ def _two_rank_worker(rank, world, port, q):
         tr = WorldModelTrainer(model, cfg.train, f"cuda:{rank}", process_group=dist.group.WORLD)
         batch = make_batch(cfg, generator=torch.Generator().manual_seed(100 + rank),
                            device=f"cuda:{rank}")
+        sd0 = _np(model.state_dict())
         losses = [float(tr.train_step(batch))]
         sd1 = _np(model.state_dict())
         losses.append(float(tr.train_step(batch)))   # second step reuses every EP buffer
         torch.cuda.synchronize()
         out[name] = {"loss": losses, "lo": tr.ep.local_range()[0] if tr.ep is not None else 0,
-                     "sd1": sd1, "sd2": _np(model.state_dict())}
+                     "sd0": sd0, "sd1": sd1, "sd2": _np(model.state_dict())}
         tr.engine.close()
         if tr.ep is not None:
             tr.ep.close()
@@ -178,24 +179,28 @@ def test_fsdp_ep_two_gpus_matches_nccl_and_fsdp():
         # peer-memory transport (per-owner partial sums) against the all-to-all transport
         assert abs(a["loss"][0] - b["loss"][0]) < 1e-3 * abs(b["loss"][0]), (a["loss"], b["loss"])
         assert abs(a["loss"][1] - b["loss"][1]) < 1e-3 * abs(b["loss"][1])
-        # parameters: Adam's first steps move every weight by about +-lr whatever the gradient's
-        # size, so sign noise in tiny bf16 gradients shows up at the 1e-2 level
-        for key, tol in (("sd1", 1.5e-2), ("sd2", 1.5e-2)):
-            for n in a[key]:
-                err = np.linalg.norm(a[key][n] - b[key][n]) / (np.linalg.norm(b[key][n]) + 1e-12)
-                assert err < tol, (key, n, err)
+        # parameter updates (Adam moves every weight by about +-lr whatever its gradient's size,
+        # so updates are compared by direction over each whole tensor)
+        def cos(u, v):
+            u, v = u.ravel(), v.ravel()
+            return float(u @ v / (np.linalg.norm(u) * np.linalg.norm(v) + 1e-20))
+
+        for n in a["sd1"]:
+            if "expert_bias" in n or "expert_load_ema" in n:
+                continue
+            assert cos(a["sd1"][n] - a["sd0"][n], b["sd1"][n] - b["sd0"][n]) > 0.97, n
         # against every expert on every rank (first step): equal up to bf16 rounding
         assert abs(a["loss"][0] - c["loss"][0]) < 2e-3 * abs(c["loss"][0])
         lo = a["lo"]
-        for n, v in a["sd1"].items():
+
+        def ref(sd, n):
             if n.endswith("moe.w13") or n.endswith("moe.w2"):
-                want = c["sd1"][n][lo:lo + E // world]
-            elif n.endswith("_shared"):
-                base = n.replace("w13_shared", "w13").replace("w2_shared", "w2")
-                want = c["sd1"][base][E:]
-            elif "expert_bias" in n or "expert_load_ema" in n:
+                return sd[n][lo:lo + E // world]
+            if n.endswith("_shared"):
+                return sd[n.replace("w13_shared", "w13").replace("w2_shared", "w2")][E:]
+            return sd[n]
+
+        for n in a["sd1"]:
+            if "expert_bias" in n or "expert_load_ema" in n:
                 continue
-            else:
-                want = c["sd1"][n]
-            err = np.linalg.norm(v - want) / (np.linalg.norm(want) + 1e-12)
-            assert err < 1.5e-2, (n, err)
+            assert cos(a["sd1"][n] - a["sd0"][n], ref(c["sd1"], n) - ref(c["sd0"], n)) > 0.95, n
