@@ -182,8 +182,11 @@ def test_fsdp_ep_two_gpus_matches_nccl_and_fsdp():
         # parameter updates (Adam moves every weight by about +-lr whatever its gradient's size,
         # so updates are compared by direction over each whole tensor)
         def cos(u, v):
-            u, v = u.ravel(), v.ravel()
-            return float(u @ v / (np.linalg.norm(u) * np.linalg.norm(v) + 1e-20))
+            u, v = u.ravel().astype(np.float64), v.ravel().astype(np.float64)
+            nu, nv = np.linalg.norm(u), np.linalg.norm(v)
+            if nu < 1e-12 and nv < 1e-12:      # neither run moved this tensor
+                return 1.0
+            return float(u @ v / (nu * nv + 1e-30))
 
         for n in a["sd1"]:
             if "expert_bias" in n or "expert_load_ema" in n:
