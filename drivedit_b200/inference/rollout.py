@@ -16,10 +16,12 @@ sampler (blocks/flow_matching.py:228-281), the rolling KV window
 from __future__ import annotations
 
 import time
+from collections import defaultdict, deque
 from dataclasses import dataclass
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 import torch
+import torch.nn.functional as F
 
 from ..config import RolloutConfig
 from ..models.world_dit import KVCacheSet, WorldDiT, forward_cached
@@ -46,8 +48,105 @@ class RolloutResult:
         return xs[i]
 
 
+class MemoryBank:
+    """Long-horizon memory of pooled frame features (reference ``inference/rollout.py:26-129``).
+
+    ``update`` stores an 8x8 average-pooled summary of each frame, scored by its variance,
+    and a 4x4 summary of frames with strong edges as object memory; ``get_memory_tokens``
+    returns the ``top_k`` best-scored summaries (recency-weighted, temporal order kept)
+    projected to ``d_model``. The projection is drawn once per feature width from a fixed
+    seed; the reference draws a new random matrix on every call, so its tokens change
+    between identical calls."""
+
+    def __init__(self, d_model: int = 1024, max_spatial_memory: int = 2048, max_object_memory: int = 512,
+                 decay_rate: float = 0.95, seed: int = 0):
+        self.d_model, self.decay_rate, self.seed = d_model, decay_rate, seed
+        self.max_spatial_memory, self.max_object_memory = max_spatial_memory, max_object_memory
+        self.spatial_memory = deque(maxlen=max_spatial_memory)
+        self.object_memory = deque(maxlen=max_object_memory)
+        self.memory_scores = deque(maxlen=max_spatial_memory)
+        self.frame_count = 0
+        self._proj: Dict[int, torch.Tensor] = {}
+
+    def update(self, frame: torch.Tensor, frame_idx: int = 0):
+        self.spatial_memory.append(F.adaptive_avg_pool2d(frame, (8, 8)).flatten(1).detach())
+        self.memory_scores.append(float(frame.float().var(dim=(2, 3)).mean()))
+        edges = (frame[..., 1:] - frame[..., :-1]).abs().mean() + (frame[..., 1:, :] - frame[..., :-1, :]).abs().mean()
+        if float(edges) > 0.1:
+            self.object_memory.append(F.adaptive_avg_pool2d(frame, (4, 4)).flatten(1).detach())
+        self.frame_count += 1
+
+    def _projection(self, width: int, device) -> torch.Tensor:
+        if width not in self._proj:
+            g = torch.Generator().manual_seed(self.seed + width)
+            self._proj[width] = torch.randn(self.d_model, width, generator=g) * 0.02
+        return self._proj[width].to(device)
+
+    def get_memory_tokens(self, top_k: int = 64) -> torch.Tensor:
+        if not self.spatial_memory:
+            return torch.zeros(1, 0, self.d_model)
+        mem = torch.stack(list(self.spatial_memory), 0)              # [T, B, f]
+        scores = torch.tensor(list(self.memory_scores))
+        w = scores * torch.exp(-0.1 * torch.arange(len(scores), 0, -1, dtype=torch.float32))
+        if len(w) > top_k:
+            mem = mem[torch.sort(torch.topk(w, top_k).indices).values.to(mem.device)]
+        flat = mem.reshape(-1, mem.shape[-1]).float()
+        return F.linear(flat, self._projection(flat.shape[-1], flat.device)).unsqueeze(0)
+
+    def clear(self):
+        self.spatial_memory.clear()
+        self.object_memory.clear()
+        self.memory_scores.clear()
+        self.frame_count = 0
+
+
+class InferenceConfig:
+    """Streaming-inference settings (reference ``inference/rollout.py:132-155``); maps onto
+    :class:`~drivedit_b200.config.RolloutConfig` (``chunk_size`` -> chunk frames,
+    ``context_window`` -> KV window frames, ``max_sequence_length`` -> total frames)."""
+
+    def __init__(self, max_sequence_length: int = 300, context_window: int = 8, memory_limit: int = 2048,
+                 temperature: float = 1.0, top_p: float = 0.9, use_kv_cache: bool = True,
+                 mixed_precision: bool = True, chunk_size: int = 4, memory_offload_freq: int = 20,
+                 flow_steps: int = 4):
+        self.max_sequence_length, self.context_window, self.memory_limit = max_sequence_length, context_window, memory_limit
+        self.temperature, self.top_p, self.use_kv_cache = temperature, top_p, use_kv_cache
+        self.mixed_precision, self.chunk_size, self.memory_offload_freq = mixed_precision, chunk_size, memory_offload_freq
+        self.flow_steps = flow_steps
+
+    def to_rollout_config(self) -> RolloutConfig:
+        return RolloutConfig(total_frames=self.max_sequence_length, chunk_frames=self.chunk_size,
+                             flow_steps=self.flow_steps, window_frames=max(self.context_window, self.chunk_size))
+
+
+class RolloutEvaluator:
+    """Generated vs ground-truth frames: MSE, an edge-gradient L1 (perceptual proxy) and
+    temporal-difference consistency (reference ``inference/rollout.py:495-546``)."""
+
+    def __init__(self):
+        self.metrics = defaultdict(list)
+
+    @staticmethod
+    def _compute_gradients(frames: torch.Tensor) -> torch.Tensor:
+        gx = F.pad(frames[..., 1:] - frames[..., :-1], (0, 1))
+        gy = F.pad(frames[..., 1:, :] - frames[..., :-1, :], (0, 0, 0, 1))
+        return gx + gy
+
+    def evaluate_sequence(self, generated_frames: torch.Tensor, ground_truth_frames: torch.Tensor) -> Dict[str, float]:
+        g, t = generated_frames.float(), ground_truth_frames.float()
+        m = {"mse": float(F.mse_loss(g, t)),
+             "lpips_proxy": float(F.l1_loss(self._compute_gradients(g), self._compute_gradients(t)))}
+        if g.shape[1] > 1:
+            m["temporal_consistency"] = float(F.mse_loss(g[:, 1:] - g[:, :-1], t[:, 1:] - t[:, :-1]))
+        for k, v in m.items():
+            self.metrics[k].append(v)
+        return m
+
+
 class StreamingRollout:
-    def __init__(self, model: WorldDiT, cfg: RolloutConfig, dtype: Optional[torch.dtype] = None):
+    def __init__(self, model: WorldDiT, cfg, dtype: Optional[torch.dtype] = None):
+        if isinstance(cfg, InferenceConfig):
+            cfg = cfg.to_rollout_config()
         self.model = model
         self.cfg = cfg
         dev = next(model.parameters()).device
@@ -119,3 +218,21 @@ class StreamingRollout:
             f += n
         total_ms = (time.perf_counter() - t_all0) * 1000.0
         return RolloutResult(torch.cat(out, 1), chunk_ms, total_ms)
+
+    # ---------------------------------------------------------------- reference-style API
+    def reset_state(self):
+        """Rollouts keep no state between ``run`` calls (each builds its own KV window)."""
+
+    def generate_sequence(self, context_frames: torch.Tensor, controls: Optional[torch.Tensor] = None,
+                          num_frames: Optional[int] = None, return_intermediates: bool = False):
+        """``context_frames [B, Fc, C, H, W]`` latents, ``controls [B, F_total, A]`` ->
+        ``{"frames": generated frames only, "chunk_ms": [...]}``."""
+        B, Fc = context_frames.shape[:2]
+        total = Fc + (num_frames if num_frames is not None else self.cfg.total_frames - Fc)
+        if controls is None:
+            controls = torch.zeros(B, total, self.model.cfg.action_dim, device=self.device)
+        res = self.run(context_frames, controls, total)
+        out = {"frames": res.frames[:, Fc:], "chunk_ms": res.chunk_ms, "total_ms": res.total_ms}
+        if return_intermediates:
+            out["all_frames"] = res.frames
+        return out
