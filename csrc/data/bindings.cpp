@@ -6,7 +6,9 @@
 #include <memory>
 
 #include "enfcap.h"
+#include "depth.h"
 #include "frames.h"
+#include "service.h"
 #include "telemetry.h"
 
 namespace py = pybind11;
@@ -203,4 +205,61 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           return out;
         },
         py::arg("paths"), py::arg("height"), py::arg("width"), py::arg("threads") = 0);
+
+  // ---- depth maps
+  auto depth_cfg = [](int tw, int th, float mn, float mx, bool clip, bool inv, const std::string& name) {
+    ddd::DepthLoaderConfig c;
+    c.target_width = tw; c.target_height = th; c.min_depth = mn; c.max_depth = mx;
+    c.clip_depth = clip; c.invert_depth = inv; c.npz_array_name = name;
+    return c;
+  };
+  m.def("load_depth",
+        [depth_cfg](const std::string& path, int tw, int th, float mn, float mx, bool clip, bool inv,
+                    const std::string& name) {
+          ddd::DepthMap dm;
+          {
+            py::gil_scoped_release nogil;
+            dm = ddd::load_depth(path, depth_cfg(tw, th, mn, mx, clip, inv, name));
+          }
+          return py::make_tuple(to_tensor(dm.data, torch::kFloat32, {dm.height, dm.width}), dm.original_min,
+                                dm.original_max);
+        },
+        py::arg("path"), py::arg("target_width") = 640, py::arg("target_height") = 360, py::arg("min_depth") = 0.f,
+        py::arg("max_depth") = 0.f, py::arg("clip_depth") = true, py::arg("invert_depth") = false,
+        py::arg("npz_array_name") = "depth");
+  m.def("load_depth_batch",
+        [depth_cfg](const std::vector<std::string>& paths, int tw, int th, float mn, float mx, bool clip, bool inv,
+                    const std::string& name, int threads) {
+          auto out = torch::empty({static_cast<int64_t>(paths.size()), th, tw}, torch::kFloat32);
+          float* p = out.data_ptr<float>();
+          {
+            py::gil_scoped_release nogil;
+            ddd::load_depth_batch(paths, depth_cfg(tw, th, mn, mx, clip, inv, name), threads, p);
+          }
+          return out;
+        },
+        py::arg("paths"), py::arg("target_width") = 640, py::arg("target_height") = 360, py::arg("min_depth") = 0.f,
+        py::arg("max_depth") = 0.f, py::arg("clip_depth") = true, py::arg("invert_depth") = false,
+        py::arg("npz_array_name") = "depth", py::arg("threads") = 0);
+
+  // ---- background frame loading
+  py::class_<ddd::FrameLoaderService, std::shared_ptr<ddd::FrameLoaderService>>(m, "FrameLoaderService")
+      .def(py::init<int, size_t>(), py::arg("threads") = 0, py::arg("cache_frames") = 256)
+      .def("submit",
+           [](ddd::FrameLoaderService& s, const std::vector<std::string>& paths, int H, int W) {
+             auto out = torch::empty({static_cast<int64_t>(paths.size()), H, W, 3}, torch::kUInt8);
+             const int64_t id = s.submit(paths, H, W, out.data_ptr<uint8_t>());
+             return py::make_tuple(id, out);
+           })
+      .def("wait", [](ddd::FrameLoaderService& s, int64_t id) {
+             py::gil_scoped_release nogil;
+             s.wait(id);
+           })
+      .def("done", &ddd::FrameLoaderService::done)
+      .def("pending", &ddd::FrameLoaderService::pending)
+      .def("cache_stats", [](ddd::FrameLoaderService& s) {
+             return py::dict(py::arg("size") = s.cache().size(), py::arg("hits") = s.cache().hits(),
+                             py::arg("misses") = s.cache().misses());
+           })
+      .def("clear_cache", [](ddd::FrameLoaderService& s) { s.cache().clear(); });
 }

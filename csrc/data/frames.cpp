@@ -42,7 +42,7 @@ std::vector<uint8_t> read_file(const std::string& path) {
 
 }  // namespace
 
-Image decode_png(const uint8_t* data, size_t size) {
+PngPixels decode_png_pixels(const uint8_t* data, size_t size) {
   static const uint8_t sig[8] = {0x89, 'P', 'N', 'G', '\r', '\n', 0x1a, '\n'};
   if (size < 8 || std::memcmp(data, sig, 8) != 0) throw std::runtime_error("PNG: bad signature");
   size_t o = 8;
@@ -106,6 +106,21 @@ Image decode_png(const uint8_t* data, size_t size) {
       dst[x] = static_cast<uint8_t>(v);
     }
   }
+  PngPixels out;
+  out.w = static_cast<int>(w);
+  out.h = static_cast<int>(h);
+  out.channels = ch;
+  out.depth = depth;
+  out.px = std::move(px);
+  return out;
+}
+
+Image decode_png(const uint8_t* data, size_t size) {
+  const PngPixels pp = decode_png_pixels(data, size);
+  const uint32_t w = pp.w, h = pp.h;
+  const int ch = pp.channels, depth = pp.depth;
+  const size_t bpp = static_cast<size_t>(ch) * (depth / 8);
+  const std::vector<uint8_t>& px = pp.px;
   Image img;
   img.w = static_cast<int>(w);
   img.h = static_cast<int>(h);

@@ -98,7 +98,7 @@ class EnfusionSession:
             raise FileNotFoundError(f"Frames directory not found: {self.session_dir / 'frames'}")
         self.metadata = self._load_metadata()
         self.frame_paths = self._glob("frames", ("*.png", "*.jpg", "*.jpeg"))
-        self.depth_paths = self._glob("depth", ("*.npz", "*.npy")) if config.load_depth else []
+        self.depth_paths = self._glob("depth", ("*.npz", "*.npy", "*.png")) if config.load_depth else []
         self.scene_paths = self._glob("scene", ("*.json",)) if config.load_scene else []
         self.parser = TelemetryParser(config.telemetry_config)
         self.normalizer = ControlNormalizer(config.telemetry_config)
@@ -207,16 +207,26 @@ class EnfusionSession:
         return u8.permute(0, 3, 1, 2).float().div_(255.0)
 
     def load_depth(self, idx: List[int]) -> Optional[torch.Tensor]:
+        """``[T, 1, H, W]`` depth clipped to ``[0, max_depth]`` and scaled to [0, 1]; decoded
+        and resized by the native depth loader when it is built."""
         if not self.depth_paths:
             return None
         H, W = self.config.image_size
+        paths = [self.depth_paths[min(i, len(self.depth_paths) - 1)] for i in idx]
+        from .native import available
+
+        if available():
+            from .depth import DepthLoader, DepthLoaderConfig
+
+            cfg = DepthLoaderConfig(target_width=W, target_height=H, min_depth=0.0,
+                                    max_depth=self.config.max_depth, npz_array_name="")
+            return DepthLoader(cfg).load_batch_contiguous(paths, self.config.loader_threads)[:, None]
         out = []
-        for i in idx:
-            p = self.depth_paths[min(i, len(self.depth_paths) - 1)]
+        for p in paths:
             d = np.load(p)
             d = d[d.files[0]] if hasattr(d, "files") else d
             t = torch.from_numpy(np.asarray(d, np.float32))[None, None]
-            t = F.interpolate(t, size=(H, W), mode="nearest")[0]
+            t = F.interpolate(t, size=(H, W), mode="bilinear", align_corners=False)[0]
             out.append(t.clamp(0, self.config.max_depth) / self.config.max_depth)
         return torch.stack(out)
 
