@@ -141,6 +141,98 @@ def bench_conv3d(iters: int = 10):
                           "cudnn_tflops": round(flops / ms_ref / 1e9, 1)}), flush=True)
 
 
+def bench_ep(iters: int = 5, d: int = 1024, E: int = 64, k: int = 6, F: int = 512, ns: int = 2,
+             N: int = 32768, transport: str = "fused"):
+    """Expert-parallel MoE layer on all ranks of a torchrun job (one per GPU): device time
+    of each stage of the forward and backward (max over ranks), and the NVLink bytes of
+    the row movement next to the 770 GB/s per-direction peer-copy reference.
+    Defaults: the MoE-DiT-L layer (d 1024, 64 experts of width 512, top-6, 2 shared) on
+    4 x 8192 tokens per rank."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from . import moe as moe_ops
+    from ..layers.moe import MoEFFN
+    from ..parallel.expert import ExpertParallel
+    from ..parallel.flat import FlatParamGroup
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    rank, W = dist.get_rank(), dist.get_world_size()
+    torch.manual_seed(0)
+    moe = MoEFFN(d, E, k, F, ns).cuda()
+    ep = ExpertParallel(num_experts=E, transport=transport, device="cuda")
+    moe.shard_experts(ep)
+    main_g = FlatParamGroup([(n, p) for n, p in moe.named_parameters() if n not in ("w13", "w2")])
+    main_g.linked.append(FlatParamGroup([("w13", moe.w13), ("w2", moe.w2)]))
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    h = torch.randn(N, d, device="cuda", generator=g).to(torch.bfloat16)
+    r = torch.randn(N, d, device="cuda", generator=g).to(torch.bfloat16)
+    dout = torch.randn(N, d, device="cuda", generator=g).to(torch.bfloat16)
+    one = torch.ones((), device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+
+    def step():
+        out, aux, sv = moe_ops.moe_ffn_forward_ep(h, r, moe, main_g.compute_view)
+        moe_ops.moe_ffn_backward_ep(dout, one, moe, main_g.compute_view, sv)
+        return sv
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    stages = {}
+    totals = []
+    for _ in range(iters):
+        flush.zero_()
+        dist.barrier()
+        moe_ops.EP_TRACE = []
+        s0 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        sv = step()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.cuda.synchronize()
+        tr, moe_ops.EP_TRACE = moe_ops.EP_TRACE, None
+        totals.append(s0.elapsed_time(e0))
+        for (a, ea), (b, eb) in zip(tr[:-1], tr[1:]):
+            if a.split(".")[0] == b.split(".")[0]:
+                stages.setdefault(b, []).append(ea.elapsed_time(eb))
+    # rows this rank pulled from peers in the last forward (NVLink inbound), and pushed out
+    meta = sv.get("owner")[9] if transport == "fused" else None
+    remote_rows = 0
+    if meta is not None:
+        nu = int(sv["owner"][11].item())
+        remote_rows = int((meta[:nu, 0] != rank).sum())
+    med = {kk: sorted(v)[len(v) // 2] for kk, v in stages.items()}
+    t = torch.tensor([sorted(totals)[len(totals) // 2]] + [med[kk] for kk in sorted(med)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    rr = torch.tensor([float(remote_rows)], device="cuda")
+    dist.all_reduce(rr, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        keys = sorted(med)
+        res = {"what": "ep_layer", "transport": transport, "world": W, "N_per_rank": N, "d": d, "experts": E,
+               "top_k": k, "ms_fwd_bwd": round(float(t[0]), 3),
+               "stage_ms_max_over_ranks": {kk: round(float(v), 3) for kk, v in zip(keys, t[1:].tolist())},
+               "remote_rows_per_direction_max": int(rr.item())}
+        if transport == "fused":
+            mb = rr.item() * d * 2 / 1e6
+            res["nvlink_mb_per_phase"] = round(mb, 1)
+            for st in ("fwd.gather", "fwd.scatter", "bwd.gather", "bwd.scatter"):
+                ms = res["stage_ms_max_over_ranks"].get(st)
+                if ms:
+                    gbs = mb / ms
+                    res[f"{st}_GBps"] = round(gbs, 1)
+                    res[f"{st}_frac_of_770"] = round(gbs / 770.0, 3)
+        print(json.dumps(res), flush=True)
+    ep.close()
+    dist.barrier()
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("what", nargs="*", default=["gemm"])
@@ -148,6 +240,7 @@ def main():
     p.add_argument("--small", action="store_true", help="small attention case (for ncu)")
     p.add_argument("--B", type=int, default=8, help="attention batch")
     p.add_argument("--shape", nargs="*", help="gemm shapes to run (names in GEMM_SHAPES)")
+    p.add_argument("--transport", default="fused", help="ep: fused | nccl")
     args = p.parse_args()
     for w in args.what:
         if w == "attn" and args.small:
@@ -158,6 +251,8 @@ def main():
             bench_attn(args.iters, dbg=1)
         elif w == "gemm":
             bench_gemm(args.iters, args.shape)
+        elif w == "ep":
+            bench_ep(args.iters, transport=args.transport)
         else:
             globals()[f"bench_{w}"](args.iters)
     from ._ext import check_device_status

@@ -221,6 +221,18 @@ def moe_ffn_backward_ep(dout: torch.Tensor, d_aux, moe, W, sv) -> torch.Tensor:
 
 
 # ---- fused transport: owner-driven, one row per (token, owner rank) each way
+# Optional stage timing for benchmarks: when EP_TRACE is a list, CUDA events are appended
+# as (stage, event) at the stage boundaries of the fused forward / backward.
+EP_TRACE = None
+
+
+def _mark(stage: str):
+    if EP_TRACE is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        EP_TRACE.append((stage, ev))
+
+
 def _expose(ep, idx, w, h) -> bool:
     """Copy this rank's routing and rows into its peer-readable buffers when they are
     large enough (every rank decides alike: equal token counts, buffers grown together)."""
@@ -249,9 +261,12 @@ def _ep_forward_fused(h, residual, moe, W):
     E, k, ns, Fh = moe.num_experts, moe.top_k, moe.num_shared_experts, moe.expert_dim
     El = ep.local_experts
     lo = ep.rank * El
+    _mark("fwd.start")
     idx, w, sw, probs, counts, psum = _route(h, moe, W)
+    _mark("fwd.route")
     fast = _expose(ep, idx, w, h)
     table = ep.exchange_counts(counts)            # barrier: counts, routing and rows visible
+    _mark("fwd.counts")
     if not (table.sum(1) == N * k).all():
         raise RuntimeError("expert parallelism needs the same number of tokens on every rank")
     if not fast:                                  # first use / growth: every rank alike
@@ -269,18 +284,25 @@ def _ep_forward_fused(h, residual, moe, W):
     rt, ht = ep._sym["route"], ep._sym["rows"]
     base = (rt.table, ep.slot_table("route", 1, N * k * 4), ht.table, ep.world, ep.rank, N, k, d, lo, El,
             rp[0], rp[7], meta, meta_w, n_uniq)
+    _mark("fwd.plan")
     ext().ep_owner_gather(*base, xr)
+    _mark("fwd.gather")
     gu_r = act_r = None
     y_r = xr
     if plan.owner_rows:
         ext().moe_zero_pad(rp[0], rp[1], xr)
         gu_r, act_r, y_r = _grouped_ffn(xr, W(moe.w13), W(moe.w2), tables_r, Fh)
+    _mark("fwd.experts")
     ret = ep.sym("ret", cap * d * 2)
     ext().ep_owner_scatter_sum(*base, y_r, True, ret.table)
+    _mark("fwd.scatter")
     slot_s, xs, gu_s, act_s, y_s, tables_s = _shared_forward(h, moe, W, ep)
+    _mark("fwd.shared")
     ep.barrier()                                  # every owner's partial rows have landed
+    _mark("fwd.barrier")
     out = ext().ep_source_reduce(idx, ret.tensor(cap * d, torch.bfloat16).view(cap, d), El, residual,
                                  sw if ns else None, slot_s, y_s)
+    _mark("fwd.reduce")
     f, aux = _finish_forward(moe, ep, counts, psum, table, N)
     saved = dict(h=h, idx=idx, w=w, sw=sw, probs=probs, f=f, plan=plan, owner=base[3:], rp=rp,
                  tables_r=tables_r, xr=xr, gu_r=gu_r, act_r=act_r, y_r=y_r, slot_s=slot_s, xs=xs,
@@ -300,26 +322,34 @@ def _ep_backward_fused(dout, d_aux, moe, W, sv):
     El = ep.local_experts
     plan = sv["plan"]
     cap = ep.world * N
+    _mark("bwd.start")
     drows = ep.sym("drows", N * d * 2)
     drows.tensor(N * d, torch.bfloat16).view(N, d).copy_(dout)
     dwb = ep.sym("dw", N * k * 4)
     dws, dxs = _shared_backward(dout, moe, W, sv)
+    _mark("bwd.shared")
     ep.barrier()                                  # every rank's dout rows are visible
+    _mark("bwd.barrier1")
     rt = ep._sym["route"]
     owner = (rt.table, ep.slot_table("route", 1, N * k * 4), drows.table) + sv["owner"]
     dyr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
     ext().ep_owner_grad_gather(*owner, sv["y_r"], dyr, dwb.table)
+    _mark("bwd.gather")
     dxr = dyr
     if plan.owner_rows:
         ext().moe_zero_pad(sv["rp"][0], sv["rp"][1], dyr)
         dxr = _grouped_ffn_bwd(dyr, sv["xr"], sv["gu_r"], sv["act_r"], W(moe.w13), W(moe.w2),
                                moe.w13.grad.view(El * 2 * Fh, d), moe.w2.grad.view(El * d, Fh),
                                sv["tables_r"], Fh)
+    _mark("bwd.experts")
     dret = ep.sym("dret", cap * d * 2)
     ext().ep_owner_scatter_sum(*owner, dxr, False, dret.table)
+    _mark("bwd.scatter")
     ep.barrier()                                  # every dx partial and dw value has landed
+    _mark("bwd.barrier2")
     dh = ext().ep_source_reduce(sv["idx"], dret.tensor(cap * d, torch.bfloat16).view(cap, d), El,
                                 None, None, sv["slot_s"], dxs)
+    _mark("bwd.reduce")
     dw = torch.cat([dwb.tensor(N * k, torch.float32).view(N, k), dws], 1)
     return _router_backward(h, dw, d_aux, dh, moe, W, sv)
 
