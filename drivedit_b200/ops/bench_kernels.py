@@ -233,6 +233,59 @@ def bench_ep(iters: int = 5, d: int = 1024, E: int = 64, k: int = 6, F: int = 51
     dist.barrier()
 
 
+def bench_optim(iters: int = 10, numel: int = 130_000_000, transport: str = "fused"):
+    """Sharded optimizer step on every rank of a torchrun job (reduce-scatter of the fp32
+    gradients + global-norm clip + AdamW on the shard + all-gather of fp32 and bf16
+    weights) for a flat buffer of ``numel`` parameters (DiT-B has ~130M); device time max
+    over ranks and the bytes that cross NVLink per rank next to the 770 GB/s reference."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+    import torch.nn as nn
+
+    from ..parallel.sharded import ShardedDataParallel
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    rank, W = dist.get_rank(), dist.get_world_size()
+    rows = numel // 4096
+    net = nn.Module()
+    net.w = nn.Parameter(torch.randn(rows, 4096, device="cuda") * 0.02)
+    eng = ShardedDataParallel(net, transport=transport, lr=1e-4, weight_decay=0.01, grad_clip=1.0)
+    eng.flat.grad.normal_()
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        dist.barrier()
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        eng.step()
+        e0.record()
+        torch.cuda.synchronize()
+        ts.append(s0.elapsed_time(e0))
+    t = torch.tensor([sorted(ts)[len(ts) // 2]], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    n = eng.flat.numel
+    # per rank: read (W-1)/W of the fp32 gradient from peers, write (W-1)/W of fp32 master
+    # + bf16 compute into peers
+    mb_in = n * 4 * (W - 1) / W / 1e6
+    mb_out = n * 6 * (W - 1) / W / 1e6
+    if rank == 0:
+        ms = float(t.item())
+        print(json.dumps({"what": "sharded_optimizer_step", "transport": transport, "world": W, "numel": n,
+                          "ms": round(ms, 3), "nvlink_in_mb": round(mb_in, 1), "nvlink_out_mb": round(mb_out, 1),
+                          "roofline_ms_at_770": round(max(mb_in, mb_out) / 770.0, 3),
+                          "frac_of_roofline": round(max(mb_in, mb_out) / 770.0 / ms, 3)}), flush=True)
+    eng.close()
+    dist.barrier()
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("what", nargs="*", default=["gemm"])
@@ -253,6 +306,8 @@ def main():
             bench_gemm(args.iters, args.shape)
         elif w == "ep":
             bench_ep(args.iters, transport=args.transport)
+        elif w == "optim":
+            bench_optim(args.iters, transport=args.transport)
         else:
             globals()[f"bench_{w}"](args.iters)
     from ._ext import check_device_status
