@@ -421,6 +421,87 @@ void attn_dq_finalize(torch::Tensor dq_acc, torch::Tensor dq, int64_t dq_col, in
 
 // ------------------------------------------------------------------ batched GEMM
 // D[b] = A[b] B[b]^T for 3-D bf16 A, B (row-major per batch); D is [batch * M, N].
+// Tensor-parallel forms of the GEMM: the all-gather of A fused into its TMA loads (rows of
+// peer p read from a_peers[p]) and/or the reduce-scatter fused into the bf16 store (row r
+// stored into rank r / d_rows_per_peer's buffer through the device pointer table d_peers).
+void gemm_tp(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> D, int64_t epi, int64_t M,
+             std::vector<int64_t> a_peers, int64_t a_rows_per_peer, c10::optional<torch::Tensor> d_peers,
+             int64_t d_rows_per_peer, int64_t d_slot, int64_t ldd, c10::optional<torch::Tensor> D2,
+             c10::optional<torch::Tensor> rope_tab, int64_t rope_cols, int64_t rope_rows_per_seq,
+             int64_t rope_pos_offset, int64_t rope_head_dim) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_rows(A, "A");
+  check_rows(B, "B");
+  const c10::cuda::CUDAGuard guard(A.device());
+  ddb::GemmArgs a;
+  a.M = M;
+  a.K = A.size(1);
+  a.N = B.size(0);
+  TORCH_CHECK(B.size(1) == a.K, "gemm_tp: inner dimensions differ");
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  if (!a_peers.empty()) {
+    TORCH_CHECK(static_cast<int>(a_peers.size()) <= ddb::kMaxGemmPeers, "gemm_tp: too many peers");
+    a.a_npeers = static_cast<int>(a_peers.size());
+    a.a_rows_per_peer = a_rows_per_peer;
+    for (size_t p = 0; p < a_peers.size(); ++p) a.a_peer_ptrs[p] = reinterpret_cast<const void*>(a_peers[p]);
+  } else {
+    TORCH_CHECK(A.size(0) == M, "gemm_tp: A rows");
+  }
+  if (d_peers) {
+    TORCH_CHECK(d_peers->is_cuda() && d_peers->scalar_type() == torch::kInt64, "gemm_tp: d_peers table");
+    TORCH_CHECK(epi == ddb::kEpiBf16, "gemm_tp: the reduce-scatter store is bf16 only");
+    a.d_peers = reinterpret_cast<void* const*>(d_peers->data_ptr<int64_t>());
+    a.d_rows_per_peer = d_rows_per_peer;
+    a.d_slot = d_slot;
+    a.ldd = ldd;
+    a.D = reinterpret_cast<void*>(1);  // never written through: rows go to the peers
+  } else {
+    TORCH_CHECK(D.has_value(), "gemm_tp: D or d_peers");
+    check_bf16(*D, "D");
+    check_rows(*D, "D");
+    TORCH_CHECK(D->size(0) == M, "gemm_tp: D rows");
+    a.D = D->data_ptr();
+    a.ldd = D->stride(0);
+  }
+  if (epi == ddb::kEpiSwiGLU) {
+    TORCH_CHECK(D2.has_value(), "swiglu epilogue needs D2");
+    check_bf16(*D2, "D2");
+    a.D2 = D2->data_ptr();
+    a.ldd2 = D2->stride(0);
+  }
+  if (epi == ddb::kEpiRope) {
+    TORCH_CHECK(rope_tab.has_value() && rope_tab->scalar_type() == torch::kFloat32, "rope table");
+    a.rope_tab = reinterpret_cast<const float2*>(rope_tab->data_ptr<float>());
+    a.rope_cols = rope_cols;
+    a.rope_rows_per_seq = rope_rows_per_seq;
+    a.rope_pos_offset = rope_pos_offset;
+    a.rope_head_dim = rope_head_dim;
+  }
+  ddb::gemm(a, static_cast<int>(epi), stream());
+}
+
+// out[r] = residual[r] + sum_s recv[s * rows + r] (bf16, fp32 accumulation)
+torch::Tensor tp_sum_rows(torch::Tensor recv, int64_t world, int64_t rows, c10::optional<torch::Tensor> residual) {
+  check_bf16(recv, "recv");
+  TORCH_CHECK(recv.is_contiguous() && recv.size(0) >= world * rows, "recv [world * rows, d]");
+  const c10::cuda::CUDAGuard guard(recv.device());
+  const int64_t d = recv.size(1);
+  auto out = torch::empty({rows, d}, recv.options());
+  const __nv_bfloat16* res = nullptr;
+  if (residual) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->is_contiguous() && residual->size(0) == rows && residual->size(1) == d, "residual");
+    res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  ddb::tp_sum_rows(reinterpret_cast<const __nv_bfloat16*>(recv.data_ptr()), world, rows, d, res,
+                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), stream());
+  return out;
+}
+
 void gemm_batched(torch::Tensor A, torch::Tensor B, torch::Tensor D, int64_t epi, bool a_t,
                   bool b_t) {
   check_bf16(A, "A");
@@ -1223,6 +1304,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_free", &ipc_free, "free a local IPC buffer");
   m.def("tensor_from_ptr", &tensor_from_ptr, "tensor view of a device pointer");
   m.def("xrank_barrier", &xrank_barrier, "bounded cross-rank flag barrier over peer memory");
+  m.def("gemm_tp", &gemm_tp, "tcgen05 GEMM with the all-gather of A and/or the reduce-scatter of D fused");
+  m.def("tp_sum_rows", &tp_sum_rows, "sum of the per-rank partial rows (+ residual)");
   m.def("rs_sum_sqnorm", &rs_sum_sqnorm, "reduce-scatter by peer loads + squared norm");
   m.def("shard_adamw_allgather", &shard_adamw_allgather, "sharded AdamW + all-gather by peer stores");
   m.def("gemm_grouped", &gemm_grouped, "grouped (MoE) tcgen05 GEMM with device tile tables");

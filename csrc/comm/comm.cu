@@ -16,6 +16,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <stdexcept>
 
 #include "../common/ptx.cuh"
@@ -175,6 +176,49 @@ void rs_sum_sqnorm(const float* const* peer_grads, int world, long off, long len
 void shard_adamw_allgather(const ShardAdamWArgs& a, cudaStream_t s) {
   if (a.len % 4 != 0 || a.off % 4 != 0) throw std::runtime_error("shard_adamw: 16-byte granularity");
   shard_adamw_kernel<<<grid_for(a.len / 4), 256, 0, s>>>(a);
+  count_launch();
+}
+
+
+namespace {
+__global__ void __launch_bounds__(256) tp_sum_rows_kernel(const __nv_bfloat16* __restrict__ recv, long world,
+                                                          long rows, long d, const __nv_bfloat16* __restrict__ res,
+                                                          __nv_bfloat16* __restrict__ out) {
+  const long n8 = rows * d / 8;
+  for (long i = blockIdx.x * 256L + threadIdx.x; i < n8; i += static_cast<long>(gridDim.x) * 256) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    auto add = [&](const __nv_bfloat16* p) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p + i * 8);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[q]));
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    };
+    if (res) add(res);
+    for (long s = 0; s < world; ++s) add(recv + s * rows * d);
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+      o[q] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(out + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+}  // namespace
+
+void tp_sum_rows(const __nv_bfloat16* recv, long world, long rows, long d, const __nv_bfloat16* residual,
+                 __nv_bfloat16* out, cudaStream_t s) {
+  if (d % 8 != 0) throw std::runtime_error("tp_sum_rows: d % 8");
+  const long n8 = rows * d / 8;
+  if (n8 == 0) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = static_cast<int>(std::min<long>((n8 + 255) / 256, 4L * num_sms(dev)));
+  tp_sum_rows_kernel<<<grid, 256, 0, s>>>(recv, world, rows, d, residual, out);
   count_launch();
 }
 

@@ -23,6 +23,9 @@ void ipc_free(void* ptr);
 // Cross-rank barrier on `epoch`: rank r writes epoch (and an optional float payload) into
 // slot r of every peer's flag array, then waits (bounded) until every slot of its own array
 // holds >= epoch. flags layout per rank: [world] uint32 flags, then [world] float payloads.
+// out[r] = residual[r] + sum_s recv[s * rows + r] over d bf16 columns (d % 8 == 0).
+void tp_sum_rows(const __nv_bfloat16* recv, long world, long rows, long d, const __nv_bfloat16* residual,
+                 __nv_bfloat16* out, cudaStream_t s);
 void xrank_barrier(void* const* peer_flag_bufs, void* local_flag_buf, int rank, int world,
                    uint32_t epoch, const float* payload, int* status, cudaStream_t s);
 

@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cstring>
 #include <stdexcept>
 #include <string>
 
@@ -170,8 +171,14 @@ __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0
           }
         }
       }
-      __nv_bfloat16* d =
-          reinterpret_cast<__nv_bfloat16*>(a.D) + static_cast<long>(row) * a.ldd + col0;
+      __nv_bfloat16* d;
+      if (EPI == kEpiBf16 && a.d_peers != nullptr) {  // reduce-scatter: P2P store to the row's owner
+        const int owner = row / a.d_rows_per_peer;
+        const long lrow = static_cast<long>(a.d_slot) * a.d_rows_per_peer + row % a.d_rows_per_peer;
+        d = reinterpret_cast<__nv_bfloat16*>(a.d_peers[owner]) + lrow * a.ldd + col0;
+      } else {
+        d = reinterpret_cast<__nv_bfloat16*>(a.D) + static_cast<long>(row) * a.ldd + col0;
+      }
 #pragma unroll
       for (int i = 0; i < 32; i += 8)
         st_global_v4(d + i, pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
@@ -253,12 +260,17 @@ __device__ __forceinline__ void epi_dswiglu(const GemmArgs& a, int row, int col0
   }
 }
 
+// Per-peer A maps of the all-gather-fused form (unused entries are never read).
+struct PeerMaps {
+  CUtensorMap m[kMaxGemmPeers];
+};
+
 // ---------------------------------------------------------------- kernel
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args,
-                   const Sched sched, int* status) {
+                   const Sched sched, int* status, const __grid_constant__ PeerMaps pmA) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = make_idesc_bf16(BM, BN, A_MN, B_MN);
@@ -291,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    for (int p = 0; p < args.a_npeers; ++p) tma_prefetch_desc(&pmA.m[p]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -325,6 +338,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (A_MN) {
             tma_load_3d(sa, &tmA, &full[stage], m0, kb * BK, ab);
             tma_load_3d(sa + 8192, &tmA, &full[stage], m0 + 64, kb * BK, ab);
+          } else if (args.a_npeers > 0) {  // all-gather fused: rows of peer m0 / rows_per_peer
+            tma_load_3d(sa, &pmA.m[m0 / args.a_rows_per_peer], &full[stage], kb * BK,
+                        m0 % args.a_rows_per_peer, 0);
           } else {
             tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, ab);
           }
@@ -511,7 +527,20 @@ void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, in
   else
     tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, nbb, a.ldb * 2,
                       sb * 2, 64, BN, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status);
+  PeerMaps pm;
+  std::memset(&pm, 0, sizeof(pm));
+  if (a.a_npeers > 0) {
+    if (A_MN || a.batch > 1 || a.grouped) throw std::runtime_error("gemm: peer A needs K-major, unbatched A");
+    if (a.a_npeers > kMaxGemmPeers || a.a_rows_per_peer % BM != 0 ||
+        static_cast<long>(a.a_rows_per_peer) * a.a_npeers != a.M)
+      throw std::runtime_error("gemm: peer A rows must be a multiple of 128 per peer and cover M");
+    for (int p = 0; p < a.a_npeers; ++p)
+      pm.m[p] = make_tmap_3d(a.a_peer_ptrs[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.a_rows_per_peer, 1,
+                             a.lda * 2, a.lda * 2 * a.a_rows_per_peer, 64, BM, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (a.d_peers != nullptr && (EPI != kEpiBf16 || a.C != nullptr || a.bias != nullptr || a.d_rows_per_peer <= 0))
+    throw std::runtime_error("gemm: the reduce-scatter store needs the plain bf16 epilogue");
+  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status, pm);
   count_launch();
   check_cuda(cudaGetLastError(), "gemm_tc_kernel launch");
 }

@@ -16,6 +16,8 @@ enum GemmEpilogue : int {
   kEpiGelu = 7          // D(bf16) = gelu(acc + bias[n]) (erf form)
 };
 
+constexpr int kMaxGemmPeers = 8;
+
 struct GemmArgs {
   int M = 0, N = 0, K = 0;
   const void* A = nullptr;  // bf16
@@ -57,6 +59,18 @@ struct GemmArgs {
   const int* grp_kstart = nullptr;
   const int* grp_kend = nullptr;
   int grp_max_mtiles = 0;
+  // Tensor parallelism, all-gather fused into the A loads (K-major A, no batch): A rows
+  // [p * a_rows_per_peer, (p + 1) * a_rows_per_peer) are read by TMA straight from rank p's
+  // buffer a_peer_ptrs[p] (a CUDA-IPC mapping; plain loads, no multicast), row-major with lda.
+  int a_npeers = 0;
+  int a_rows_per_peer = 0;
+  const void* a_peer_ptrs[kMaxGemmPeers] = {};
+  // Reduce-scatter fused into the bf16 store (epilogue kEpiBf16 without residual): output row
+  // r is stored into rank (r / d_rows_per_peer)'s buffer d_peers[...] at row
+  // d_slot * d_rows_per_peer + r % d_rows_per_peer (d_peers: device array of base pointers).
+  void* const* d_peers = nullptr;
+  int d_rows_per_peer = 0;
+  int d_slot = 0;
   int splits = 1;           // split-K factor (kEpiF32Atomic only)
   int bn = 0;               // 0 = auto (128 or 256)
   int max_ctas = 0;         // 0 = all SMs

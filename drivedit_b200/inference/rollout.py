@@ -24,7 +24,8 @@ import torch
 import torch.nn.functional as F
 
 from ..config import RolloutConfig
-from ..models.world_dit import KVCacheSet, WorldDiT, forward_cached
+from ..models.world_dit import KVCacheSet, WorldDiT
+from ..models.world_dit import forward_cached as _forward_cached
 
 
 @dataclass
@@ -176,7 +177,16 @@ class StreamingRollout:
         B, Fc = context.shape[:2]
         total = total_frames or cfg.total_frames
         chunk = cfg.chunk_frames
-        cache = KVCacheSet(m, B, cfg.window_frames, chunk, self.device, self.dtype)
+        make_cache = getattr(m, "make_kv_cache", None)     # e.g. a tensor-parallel model
+        fwd_chunk = getattr(m, "forward_cached_chunk", None)
+        cache = (make_cache(B, cfg.window_frames, chunk, self.device, self.dtype) if make_cache is not None
+                 else KVCacheSet(m, B, cfg.window_frames, chunk, self.device, self.dtype))
+
+        def forward_cached(m_, x_, t_, a_, cache_, commit=False, extra_cond=None):
+            if fwd_chunk is not None:
+                return fwd_chunk(x_, t_, a_, cache_, commit, extra_cond)
+            return _forward_cached(m_, x_, t_, a_, cache_, commit=commit, extra_cond=extra_cond)
+
         out = [context.to(self.dtype)]
         ones = torch.ones(B, device=self.device)
         # context frames -> cache (clean, t = 1)
