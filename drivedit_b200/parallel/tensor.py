@@ -17,9 +17,12 @@ ranks); the KV cache holds only the rank's heads. Per block::
 Transports:
 
 ``fused``
-    The all-gather happens inside the GEMM: its TMA producer loads the A rows of peer p
-    straight out of p's row shard in peer memory (``csrc/gemm/gemm.cu``, per-peer tensor
-    maps, no multicast). The reduce-scatter happens inside the GEMM too: its epilogue
+    The all-gather reads the peers' row shards in peer memory: for narrow GEMMs (one
+    column tile per rank) inside the GEMM, whose TMA producer loads the A rows of peer p
+    straight out of p's shard (``csrc/gemm/gemm.cu``, per-peer tensor maps, no multicast);
+    for wider ones a P2P-load kernel pulls each peer's rows across NVLink once on a side
+    stream while the GEMM runs on the rank's own rows (a remote A tile re-read by several
+    column tiles would cross NVLink each time). The reduce-scatter happens inside the GEMM: its epilogue
     stores every output tile into the owning rank's receive slot (P2P stores), so the
     transfer overlaps the remaining tiles; the owner then sums its ``W`` slots with the
     residual (``tp_sum_rows``). Bounded cross-rank flag barriers order the phases.
@@ -101,7 +104,10 @@ class TensorParallelWorldDiT:
     rank before sharding). Plugs into :class:`~drivedit_b200.inference.rollout.StreamingRollout`
     through ``make_kv_cache`` / ``forward_cached_chunk``."""
 
-    def __init__(self, model, group=None, transport: Optional[str] = None, dtype=torch.bfloat16):
+    def __init__(self, model, group=None, transport: Optional[str] = None, dtype=torch.bfloat16,
+                 ag_tma_max_n: int = 256):
+        """``ag_tma_max_n``: widest per-rank GEMM (columns) whose all-gather runs inside the
+        GEMM as peer TMA loads; wider ones pull the rows once and overlap."""
         self.model = model
         self.cfg = model.cfg
         self.group = group if group is not None else dist.group.WORLD
@@ -110,6 +116,7 @@ class TensorParallelWorldDiT:
         self.device = next(model.parameters()).device
         self.transport = transport or ("fused" if self.device.type == "cuda" else "nccl")
         self.dtype = dtype
+        self.ag_tma_max_n = ag_tma_max_n
         self.layers = [TPLayerWeights(b, self.rank, self.world, self.cfg, dtype) for b in model.blocks]
         self.heads_local = self.layers[0].heads
         self.d_local = self.heads_local * self.cfg.d_head
@@ -161,28 +168,90 @@ class TensorParallelWorldDiT:
 
     # ---------------------------------------------------------------- collectives
     def _gather_gemm(self, h_shard, h_sym, w, rows, M, epi="bf16", **kw):
-        """``all_gather(h) @ w^T`` (the fused form reads the peers' rows inside the GEMM)."""
+        """``all_gather(h) @ w^T``. Fused transport: with at most one 256-column tile per
+        rank the GEMM reads the peers' rows itself (TMA loads of peer memory); otherwise a
+        copy kernel on a side stream pulls every peer's rows across NVLink once while the
+        GEMM runs on this rank's own rows, and the GEMMs over the peers' rows follow (a
+        tile of A read by several column tiles would otherwise cross NVLink several times,
+        since peer reads are not cached in this GPU's L2)."""
         from ..ops._ext import ext
         from ..ops.gemm import EPI, gemm
 
         N = w.shape[0]
+        sw = epi == "swiglu"
         if self.transport == "fused":
             out = torch.empty(M, N, device=self.device, dtype=torch.bfloat16)
-            out2 = None
-            if epi == "swiglu":
-                out2 = torch.empty(M, N // 2, device=self.device, dtype=torch.bfloat16)
-            ext().gemm_tp(h_sym, w, out, EPI[epi], M, list(self._h_peers), rows, None, 0, 0, 0, out2,
-                          kw.get("rope_tab"), kw.get("rope_cols", 0), kw.get("rope_rows_per_seq", 1),
-                          kw.get("rope_pos_offset", 0), kw.get("rope_head_dim", 64))
-            return (out, out2) if epi == "swiglu" else out
+            out2 = torch.empty(M, N // 2, device=self.device, dtype=torch.bfloat16) if sw else None
+            T = kw.get("rope_rows_per_seq", 1)
+            if N <= self.ag_tma_max_n or self.world == 1:
+                ext().gemm_tp(h_sym, w, out, EPI[epi], M, list(self._h_peers), rows, None, 0, 0, 0, out2,
+                              kw.get("rope_tab"), kw.get("rope_cols", 0), T, 0, kw.get("rope_head_dim", 64))
+                return (out, out2) if sw else out
+            W, r = self.world, self.rank
+            K = h_sym.shape[1]
+            full = self._local("hfull", M, K)
+            main = torch.cuda.current_stream()
+            side = self._side_stream()
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                self._pull_rows(full, K, rows)
+                ev = torch.cuda.Event()
+                ev.record(side)
+            r0 = r * rows
+
+            def part(a, lo, hi):
+                if hi <= lo:
+                    return
+                kw2 = {}
+                if epi == "rope":
+                    kw2 = dict(rope_tab=kw["rope_tab"], rope_cols=kw["rope_cols"], rope_rows_per_seq=T,
+                               rope_pos_offset=lo % T, rope_head_dim=kw.get("rope_head_dim", 64))
+                if sw:
+                    gemm(a, w, out[lo:hi], epi="swiglu", out2=out2[lo:hi])
+                else:
+                    gemm(a, w, out[lo:hi], epi=epi, **kw2)
+
+            part(h_sym, r0, r0 + rows)                   # own rows while the peers' rows arrive
+            main.wait_event(ev)
+            part(full[:r0], 0, r0)
+            part(full[r0 + rows:], r0 + rows, M)
+            full.record_stream(main)
+            return (out, out2) if sw else out
         full = torch.empty(M, h_shard.shape[1], device=self.device, dtype=torch.bfloat16)
         dist.all_gather_into_tensor(full, h_shard.contiguous(), group=self.group)
-        if epi == "swiglu":
+        if sw:
             out = torch.empty(M, N, device=self.device, dtype=torch.bfloat16)
             a = torch.empty(M, N // 2, device=self.device, dtype=torch.bfloat16)
             gemm(full, w, out, epi="swiglu", out2=a)
             return out, a
         return gemm(full, w, epi=epi, **kw)
+
+    def _local(self, name, rows, cols):
+        t = getattr(self, "_locals", {}).get(name)
+        if t is None or t.shape != (rows, cols):
+            t = torch.empty(rows, cols, device=self.device, dtype=torch.bfloat16)
+            self._locals = {**getattr(self, "_locals", {}), name: t}
+        return t
+
+    def _side_stream(self):
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        return self._side
+
+    def _pull_rows(self, full, K, rows):
+        """Every peer's row shard -> its rows of ``full`` (one P2P-load kernel)."""
+        from ..ops._ext import ext
+
+        key = (rows, K)
+        if getattr(self, "_pull_key", None) != key:
+            peers = [p for p in range(self.world) if p != self.rank]
+            self._pull_blocks = torch.tensor([[p, 0, 0, p * rows] for p in peers], dtype=torch.int32,
+                                             device=self.device)
+            self._pull_prefix = torch.arange(0, len(peers) * rows, rows, dtype=torch.int32, device=self.device)
+            self._pull_key = key
+        hb = self._sym["h"]
+        ext().ep_copy_rows(hb.table, 0, None, full.data_ptr(), self._pull_blocks, self._pull_prefix,
+                           (self.world - 1) * rows, K * 2, K * 2, K * 2)
 
     def _gemm_scatter(self, a, w, rows, residual):
         """``residual + reduce_scatter(a @ w^T)`` for this rank's rows."""

@@ -28,7 +28,7 @@ def _port():
     return p
 
 
-def _rollout(model, tp_transport=None):
+def _rollout(model, tp_transport=None, ag_tma_max_n=256):
     from drivedit_b200.config import RolloutConfig
     from drivedit_b200.inference.rollout import StreamingRollout
 
@@ -42,7 +42,7 @@ def _rollout(model, tp_transport=None):
     if tp_transport is not None:
         from drivedit_b200.parallel.tensor import TensorParallelWorldDiT
 
-        tp = TensorParallelWorldDiT(model, transport=tp_transport)
+        tp = TensorParallelWorldDiT(model, transport=tp_transport, ag_tma_max_n=ag_tma_max_n)
         target = tp
     res = StreamingRollout(target, cfg).run(ctx, act, 8, generator=g)
     torch.cuda.synchronize()
@@ -77,6 +77,8 @@ def _worker(rank, world, port, q, transports):
     out = {"single": _rollout(model)}
     for t in transports:
         out[t] = _rollout(model, t)
+    if "fused" in transports:      # every all-gather inside the GEMM as peer TMA loads
+        out["fused_tma"] = _rollout(model, "fused", ag_tma_max_n=1 << 20)
     check_device_status()
     q.put((rank, out))
     dist.barrier()
@@ -125,4 +127,5 @@ def test_tensor_parallel_rollout_two_ranks():
     for r in range(2):
         _close(res[r]["fused"], res[r]["single"], 2e-2)
         _close(res[r]["nccl"], res[r]["single"], 2e-2)
+        _close(res[r]["fused_tma"], res[r]["single"], 2e-2)
     np.testing.assert_array_equal(res[0]["fused"], res[1]["fused"])
