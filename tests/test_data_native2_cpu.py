@@ -130,3 +130,49 @@ def test_sessions_and_presets(tmp_path):
     md = SessionMetadata.from_dir(tmp_path / "s1")
     assert (md.num_frames, md.width, md.height, md.has_telemetry) == (2, 10, 6, True)
     assert DatasetConfig.minimal().image_width == 128 and DatasetConfig.production().load_flow
+
+
+def test_native_batch_loader_matches_dataset(tmp_path):
+    import numpy as np
+    import torch
+    from PIL import Image
+
+    from drivedit_b200.data import native_loader as nl
+
+    if not nl.check_native_available():
+        pytest.skip("data runtime not built")
+    rng = np.random.default_rng(0)
+    for s in range(3):
+        d = tmp_path / f"session_{s:04d}"
+        (d / "frames").mkdir(parents=True)
+        for i in range(8):
+            Image.fromarray(rng.integers(0, 256, (20, 36, 3), dtype=np.uint8)).save(d / "frames" / f"frame_{i:06d}.png")
+        rows = ["timestamp_ms,steering,throttle,brake,speed_kmh"]
+        rows += [f"{i * 100},{np.sin(i):.3f},0.5,0.0,{30 + i}" for i in range(8)]
+        (d / "telemetry.csv").write_text("\n".join(rows) + "\n")
+    cfg = nl.RustDatasetConfig(sequence_length=3, frame_skip=2, image_height=16, image_width=24, load_depth=False,
+                               num_workers=2)
+    ds = nl.RustEnfusionDataset(tmp_path, cfg)
+    assert len(ds) == 3 * 4
+    loader = nl.RustBatchLoader(ds, batch_size=5, shuffle=False, drop_last=False)
+    batches = list(loader)
+    assert len(batches) == len(loader) == 3
+    assert [b["frames"].shape[0] for b in batches] == [5, 5, 2]
+    b0 = batches[0]
+    assert b0["frames"].shape == (5, 3, 3, 16, 24) and b0["controls"].shape == (5, 3, 6)
+    for j in range(5):
+        ref = ds[j]
+        torch.testing.assert_close(b0["frames"][j], ref["frames"], atol=0, rtol=0)
+        torch.testing.assert_close(b0["controls"][j], ref["controls"])
+        assert b0["anchor_mask"][j].tolist() == ref["anchor_mask"].tolist()
+    tr, va = nl.create_rust_dataloaders(tmp_path, cfg, batch_size=2, val_fraction=0.34)
+    assert len(tr.dataset) + len(va.dataset) == len(ds)
+    hy = nl.get_best_loader(tmp_path, cfg, batch_size=2)
+    assert hy.source == "native"
+    n = sum(1 for _ in hy)
+    assert n == len(hy) and hy.get_performance_stats()["native"]["batches"] == n
+    py = nl.HybridDataLoader(tmp_path, cfg, nl.HybridLoaderConfig(prefer_native=False, batch_size=2))
+    assert py.source == "python" and next(iter(py))["frames"].shape == (2, 3, 3, 16, 24)
+    r = nl.benchmark_rust_vs_python(tmp_path, cfg, batch_size=2, num_batches=2)
+    assert r["native_batches_per_s"] > 0 and r["python_batches_per_s"] > 0
+    assert nl.get_rust_version()
