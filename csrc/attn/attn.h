@@ -43,6 +43,8 @@ struct AttnArgs {
 };
 
 void attn_fwd(const AttnArgs& a, cudaStream_t s);
+// pipeline-study hook: record clock64 events of CTA `cta` into buf[3 * 8 * 64] (nullptr: off)
+void attn_fwd_set_trace(long long* buf, int cta);
 
 struct AttnBwdArgs {
   AttnArgs f;                 // forward description (q/k/v/o/lse, masks)

@@ -12,10 +12,14 @@
 //   dK  += dS^T Q     (M=128, N=64, K=128)                      TMEM cols [320,384)
 //   dQ   = dS K       (M=128 queries, N=64, K=128 keys; dS^T read MN-major)
 //                                                               TMEM cols [384,448)
-//   dQ warps: TMEM -> fp32 vector reductions into the dQ accumulator.
+//   dQ warps: TMEM -> the tile's P^T buffer (free once dQ is computed; fp32, two 128-byte
+//             swizzled boxes) -> one TMA reduce-add into the fp32 dQ accumulator, so the
+//             accumulation bypasses the load/store pipe the softmax warps use.
 // After the last query tile dK and dV go to global memory (bf16).
 //
-// Roles: warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 softmax/dS, warps 6-9 dQ reduction.
+// Roles: warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 softmax/dS (two warps per TMEM lane
+// quarter: warps 2-5 take queries 0-63 of the tile, warps 6-9 queries 64-127, so two
+// softmax warps share each SM sub-partition), warps 10-13 dQ.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -28,7 +32,7 @@
 namespace ddb {
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 constexpr int NS = 2;
 constexpr int TILE = 16384;
 constexpr int OFF_K = 0;
@@ -41,7 +45,8 @@ constexpr int OFF_VEC = OFF_DST + 4 * TILE;    // per stage: lse[128], delta[128
 constexpr int OFF_BAR = OFF_VEC + NS * 1024;
 // no alignment slack: the dynamic shared window of a CTA without static shared memory
 // starts 1024-byte aligned; the kernel checks this and reports a status code otherwise.
-constexpr int SMEM_BYTES = OFF_BAR + 128;
+constexpr int SMEM_BYTES = OFF_BAR + 256;
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
 constexpr uint32_t IDESC_SS = make_idesc_bf16(128, 128, false, false);
@@ -75,9 +80,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                "r"(d)
                : "memory");
 }
-__device__ __forceinline__ void named_bar(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 // trace slot: [role (0 producer, 1 mma, 2 softmax, 3 dq)][event < 8][pair < 64]
 #define DDB_TRACE(role, ev, j)                                                      \
@@ -90,7 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
-                    const __grid_constant__ CUtensorMap tmDO, const AttnBwdArgs g, int n_kvtiles,
+                    const __grid_constant__ CUtensorMap tmDO,
+                    const __grid_constant__ CUtensorMap tmDQ, const AttnBwdArgs g, int n_kvtiles,
                     int n_qtiles, int* status) {
   const AttnArgs& a = g.f;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -106,7 +109,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_full = s_full + 6;
   uint64_t* dq_free = s_full + 7;
   uint64_t* drain = s_full + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* pt_free = s_full + 9;   // 2 buffers: P^T buffer free again (dQ staging read)
+  uint64_t* dq_staged = s_full + 11;  // the 4 dQ warps' rows are in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_staged + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if ((smem_u32(smem_raw) & 1023) != 0) {
     if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadArgument);
@@ -142,9 +147,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qd_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(&ds_full[0], 4);
-    mbar_init(&ds_full[1], 4);
+    mbar_init(s_free, 8);
+    mbar_init(&ds_full[0], 8);
+    mbar_init(&ds_full[1], 8);
+    mbar_init(&pt_free[0], 1);
+    mbar_init(&pt_free[1], 1);
+    mbar_init(dq_staged, 4);
     mbar_init(&ds_empty[0], 1);
     mbar_init(&ds_empty[1], 1);
     mbar_init(dq_full, 1);
@@ -293,10 +301,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (!mbar_try_wait(drain, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ softmax / dS warps
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;   // key row within the tile
+    const int half = (warp - 2) >> 2;  // this warp's 64 query columns of the tile
+    const int r = quad * 32 + lane;    // key row within the tile
     const int key = k0 + r;
     const int khalf = r >> 6;
     const float sl2 = a.scale * 1.4426950408889634f;
@@ -318,8 +327,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       if (warp == 2 && lane == 0) DDB_TRACE(2, 0, j);
+      const uint32_t ph_free = ((j >> 1) & 1) ^ 1;
       if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
-          !mbar_wait(&ds_empty[pb], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          !mbar_wait(&ds_empty[pb], ph_free, abort_flag) ||
+          !mbar_wait(&pt_free[pb], ph_free, abort_flag)) {
         ok = false;
         break;
       }
@@ -328,12 +339,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t pt_base = smem_u32(smem + OFF_PT + pb * 2 * TILE) + r * 128;
       const uint32_t ds_base = smem_u32(smem + OFF_DST + pb * 2 * TILE) + r * 128;
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
         uint32_t rs[32], rp[32];
         tmem_ld32(trow + C_S + c0, rs);
         tmem_ld32(trow + C_DP + c0, rp);
         tmem_wait_ld();
-        if (warp == 2 && lane == 0 && j < 8) DDB_TRACE(2, 3 + (c0 >> 5), j);
+        if (warp == 2 && lane == 0 && j < 8) DDB_TRACE(2, 3 + ((c0 & 63) >> 5), j);
         const bool half_on = (bits >> ((c0 >> 6) * 2 + khalf)) & 1;
         float p[32], ds[32];
         if (g.debug_flags & 2) {
@@ -378,77 +389,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
       *abort_flag = 1;
     }
-    // final dK, dV (bf16) once the last gradient MMAs are done
+    // final dK (warps of half 0) and dV (half 1), bf16, once the last gradient MMAs are done
+    const uint32_t c_src = half == 0 ? C_DK : C_DV;
+    const long grow = b * a.kv_rows_per_b + key;
+    __nv_bfloat16* drow = half == 0
+                              ? reinterpret_cast<__nv_bfloat16*>(g.dk) + grow * g.lddk + g.dk_col + h * 64
+                              : reinterpret_cast<__nv_bfloat16*>(g.dv) + grow * g.lddv + g.dv_col + h * 64;
     if (ok && nq > 0 && mbar_wait(&ds_empty[(nq - 1) & 1], ((nq - 1) >> 1) & 1, abort_flag)) {
       tc_fence_after();
+      uint32_t rv[2][32];
+      tmem_ld32(trow + c_src, rv[0]);
+      tmem_ld32(trow + c_src + 32, rv[1]);
+      tmem_wait_ld();
       if (key < a.S) {
-        const long grow = b * a.kv_rows_per_b + key;
-        __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) + grow * g.lddk + g.dk_col + h * 64;
-        __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) + grow * g.lddv + g.dv_col + h * 64;
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          uint32_t rk[32], rv[32];
-          tmem_ld32(trow + C_DK + c0, rk);
-          tmem_ld32(trow + C_DV + c0, rv);
-          tmem_wait_ld();
+        for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            st_global_v4(dkr + c0 + c,
-                         pack_bf16(__uint_as_float(rk[c]), __uint_as_float(rk[c + 1])),
-                         pack_bf16(__uint_as_float(rk[c + 2]), __uint_as_float(rk[c + 3])),
-                         pack_bf16(__uint_as_float(rk[c + 4]), __uint_as_float(rk[c + 5])),
-                         pack_bf16(__uint_as_float(rk[c + 6]), __uint_as_float(rk[c + 7])));
-            st_global_v4(dvr + c0 + c,
-                         pack_bf16(__uint_as_float(rv[c]), __uint_as_float(rv[c + 1])),
-                         pack_bf16(__uint_as_float(rv[c + 2]), __uint_as_float(rv[c + 3])),
-                         pack_bf16(__uint_as_float(rv[c + 4]), __uint_as_float(rv[c + 5])),
-                         pack_bf16(__uint_as_float(rv[c + 6]), __uint_as_float(rv[c + 7])));
-          }
-        }
+          for (int c = 0; c < 32; c += 8)
+            st_global_v4(drow + hh * 32 + c,
+                         pack_bf16(__uint_as_float(rv[hh][c]), __uint_as_float(rv[hh][c + 1])),
+                         pack_bf16(__uint_as_float(rv[hh][c + 2]), __uint_as_float(rv[hh][c + 3])),
+                         pack_bf16(__uint_as_float(rv[hh][c + 4]), __uint_as_float(rv[hh][c + 5])),
+                         pack_bf16(__uint_as_float(rv[hh][c + 6]), __uint_as_float(rv[hh][c + 7])));
       }
     } else if (nq == 0 && key < a.S) {
       // keys nobody attends to get zero gradients
-      const long grow = b * a.kv_rows_per_b + key;
-      __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) + grow * g.lddk + g.dk_col + h * 64;
-      __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) + grow * g.lddv + g.dv_col + h * 64;
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        st_global_v4(dkr + c, 0, 0, 0, 0);
-        st_global_v4(dvr + c, 0, 0, 0, 0);
-      }
+      for (int c = 0; c < 64; c += 8) st_global_v4(drow + c, 0, 0, 0, 0);
     }
   } else {
-    // ------------------------------------------------------------ dQ reduction warps
+    // ------------------------------------------------------------ dQ warps
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row within the tile
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const bool issuer = warp == 10 && lane == 0;
     bool ok = true;
     for (int j = 0; j < nq; ++j) {
+      const int pb = j & 1;
       if (!mbar_wait(dq_full, j & 1, abort_flag)) {
         ok = false;
         break;
       }
-      if (warp == 6 && lane == 0) DDB_TRACE(3, 0, j);
+      if (issuer) DDB_TRACE(3, 0, j);
       tc_fence_after();
-      const int q = qtile_of(j) * 128 + r;
-      uint32_t v0[32], v1[32];
-      tmem_ld32(trow + C_DQ, v0);
-      tmem_ld32(trow + C_DQ + 32, v1);
+      uint32_t v[2][32];
+      tmem_ld32(trow + C_DQ, v[0]);
+      tmem_ld32(trow + C_DQ + 32, v[1]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      if (q < a.Tq && !(g.debug_flags & 1)) {
-        float* dst = g.dq_acc + (b * a.q_rows_per_b + q) * g.ld_dqacc + h * 64;
+      // The tile's P^T buffer is free: every MMA that read it completed before dq_full.
+      // Stage dQ there as two [128 rows][32 fp32] boxes, 128-byte swizzled (16-byte chunk
+      // c of row r at chunk c ^ (r & 7)), then one thread adds both boxes into the
+      // accumulator with TMA and frees the buffer once the reads are done.
+      uint8_t* stage = smem + OFF_PT + pb * 2 * TILE;
+      if (!(g.debug_flags & 1)) {
+        const uint32_t sbase = smem_u32(stage) + r * 128;
 #pragma unroll
-        for (int c = 0; c < 32; c += 4) {
-          red_add_v4_f32(dst + c, __uint_as_float(v0[c]), __uint_as_float(v0[c + 1]),
-                         __uint_as_float(v0[c + 2]), __uint_as_float(v0[c + 3]));
-          red_add_v4_f32(dst + 32 + c, __uint_as_float(v1[c]), __uint_as_float(v1[c + 1]),
-                         __uint_as_float(v1[c + 2]), __uint_as_float(v1[c + 3]));
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            st_shared_v4(sbase + hh * TILE + ((c ^ (r & 7)) << 4), v[hh][4 * c], v[hh][4 * c + 1],
+                         v[hh][4 * c + 2], v[hh][4 * c + 3]);
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_staged);
+      bool staged = true;
+      if (issuer) {
+        staged = mbar_wait(dq_staged, j & 1, abort_flag);
+        if (staged && !(g.debug_flags & 1)) {
+          const int row0 = static_cast<int>(b * a.q_rows_per_b) + qtile_of(j) * 128;
+          tma_reduce_add_2d(&tmDQ, stage, h * 64, row0);
+          tma_reduce_add_2d(&tmDQ, stage + TILE, h * 64 + 32, row0);
+          tma_store_commit();
+          tma_store_wait_read();
         }
+        mbar_arrive(&pt_free[pb]);
+      }
+      // warp-uniform exit (the next iteration's TMEM loads are warp-collective)
+      if (warp == 10 && !__shfl_sync(0xffffffffu, staged, 0)) {
+        ok = false;
+        break;
       }
     }
+    if (issuer) tma_store_wait_all();
     if (!ok) {
       if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
       *abort_flag = 1;
@@ -530,6 +556,32 @@ __global__ void dq_finalize_kernel(const float* __restrict__ acc, long ld_acc,
 
 }  // namespace
 
+namespace {
+void launch_bwd(const AttnBwdArgs& g, int* status, cudaStream_t stream) {
+  const AttnArgs& a = g.f;
+  const long q_rows = a.q_rows_total > 0 ? a.q_rows_total : a.B * a.q_rows_per_b;
+  const long kv_rows = a.kv_rows_total > 0 ? a.kv_rows_total : a.B * a.kv_rows_per_b;
+  if (g.ld_dqacc % 4 != 0 || (reinterpret_cast<uintptr_t>(g.dq_acc) & 15) != 0)
+    throw std::runtime_error("attn_bwd: the dQ accumulator needs 16-byte aligned rows");
+  CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
+                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,
+                                a.ldk * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
+                                a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tDO = make_tmap_2d(g.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.lddo, q_rows,
+                                 g.lddo * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tDQ = make_tmap_2d(g.dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.ld_dqacc, a.B * a.q_rows_per_b,
+                                 g.ld_dqacc * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int n_kvtiles = (a.S + 127) / 128;
+  const int n_qtiles = (a.Tq + 127) / 128;
+  attn_bwd_kernel<<<a.B * a.H * n_kvtiles, kThreads, SMEM_BYTES, stream>>>(
+      tQ, tK, tV, tDO, tDQ, g, n_kvtiles, n_qtiles, status);
+  count_launch();
+  check_cuda(cudaGetLastError(), "attn_bwd_kernel launch");
+}
+}  // namespace
+
 void attn_bwd(const AttnBwdArgs& g, cudaStream_t stream) {
   const AttnArgs& a = g.f;
   if (a.B <= 0 || a.H <= 0 || a.S <= 0) return;
@@ -541,24 +593,9 @@ void attn_bwd(const AttnBwdArgs& g, cudaStream_t stream) {
                "cudaFuncSetAttribute(attn_bwd)");
     attr = true;
   }
-  const long q_rows = a.q_rows_total > 0 ? a.q_rows_total : a.B * a.q_rows_per_b;
-  const long kv_rows = a.kv_rows_total > 0 ? a.kv_rows_total : a.B * a.kv_rows_per_b;
-  CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
-                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,
-                                a.ldk * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
-                                a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tDO = make_tmap_2d(g.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.lddo, q_rows,
-                                 g.lddo * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  const int n_kvtiles = (a.S + 127) / 128;
-  const int n_qtiles = (a.Tq + 127) / 128;
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  attn_bwd_kernel<<<a.B * a.H * n_kvtiles, kThreads, SMEM_BYTES, stream>>>(
-      tQ, tK, tV, tDO, g, n_kvtiles, n_qtiles, device_status(dev));
-  count_launch();
-  check_cuda(cudaGetLastError(), "attn_bwd_kernel launch");
+  launch_bwd(g, device_status(dev), stream);
 }
 
 void attn_bwd_delta(const void* o, long ldo, int o_col, const void* dout, long lddo, int do_col,
@@ -593,22 +630,7 @@ void attn_bwd_with_status(const AttnBwdArgs& g, int* status, cudaStream_t stream
   check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES),
              "cudaFuncSetAttribute(attn_bwd)");
-  const long q_rows = a.q_rows_total > 0 ? a.q_rows_total : a.B * a.q_rows_per_b;
-  const long kv_rows = a.kv_rows_total > 0 ? a.kv_rows_total : a.B * a.kv_rows_per_b;
-  CUtensorMap tQ = make_tmap_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldq, q_rows, a.ldq * 2,
-                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tK = make_tmap_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldk, kv_rows,
-                                a.ldk * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
-                                a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tDO = make_tmap_2d(g.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.lddo, q_rows,
-                                 g.lddo * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  const int n_kvtiles = (a.S + 127) / 128;
-  const int n_qtiles = (a.Tq + 127) / 128;
-  attn_bwd_kernel<<<a.B * a.H * n_kvtiles, kThreads, SMEM_BYTES, stream>>>(
-      tQ, tK, tV, tDO, g, n_kvtiles, n_qtiles, status);
-  count_launch();
-  check_cuda(cudaGetLastError(), "attn_bwd_kernel launch");
+  launch_bwd(g, status, stream);
 }
 
 }  // namespace ddb

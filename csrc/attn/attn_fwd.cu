@@ -1,17 +1,17 @@
 // tcgen05 flash-attention forward, d_head = 64, for sm_100a.
 //
 // One CTA = one (batch, head, 128-query tile). Roles (192 threads, 2 CTAs per SM):
-//   warp 0     TMA: Q tile once (two 64-row boxes), then K/V tiles of 128 keys made of
+//   warp 0     TMA: Q tile once (two 64-row boxes), then K and V tiles of 128 keys made of
 //              two independent 64-key blocks (so SLA can pair any two selected blocks)
-//              into a 2-stage ring.
+//              into 2-stage rings, K one tile ahead of V.
 //   warp 1     TMEM owner + MMA issuer: S = Q K^T (M=128, N=128, K=64) into TMEM
 //              columns [0,128), O += P V (M=128, N=64, K=128) into columns [128,192).
 //   warps 2-5  softmax: one thread per query row reads its S row from TMEM, applies the
 //              mask, keeps the running max / sum (log2 domain), rescales its O row in
-//              TMEM when the max moves, writes P (bf16) to shared memory in the 128-byte
+//              TMEM when the max moves by more than 2^8, writes P (bf16) to shared memory in the 128-byte
 //              swizzled K-major layout the PV MMA reads, and finally normalises O.
 // The S MMA of tile j+1 overlaps the softmax of tile j; the second resident CTA of the
-// SM overlaps the rest.
+// SM (113 KB of shared memory each) overlaps the rest.
 //
 // Masks: frame-causal (all keys of frames <= the query's frame), token-causal, none;
 // KV-cache attention via absolute query/key position offsets; block-sparse SLA via a
@@ -31,6 +31,7 @@ namespace ddb {
 namespace {
 
 constexpr int kThreads = 192;
+constexpr float kRescaleLog2 = 8.f;
 constexpr int NS = 2;
 constexpr int TILE_BYTES = 16384;  // 128 rows x 64 bf16
 constexpr int OFF_Q = 0;
@@ -38,12 +39,27 @@ constexpr int OFF_K = OFF_Q + TILE_BYTES;
 constexpr int OFF_V = OFF_K + NS * TILE_BYTES;
 constexpr int OFF_P = OFF_V + NS * TILE_BYTES;
 constexpr int OFF_BAR = OFF_P + 2 * TILE_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+// No alignment slack: the dynamic shared window of a CTA without static shared memory
+// starts 1024-byte aligned (checked below). With the slack two CTAs (2 x (113 KB + 1 KB
+// reserved)) would not fit the SM's 228 KB and only one would be resident.
+constexpr int SMEM_BYTES = OFF_BAR + 256;
+static_assert(2 * (SMEM_BYTES + 1024) <= 233472, "two CTAs per SM");
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t S_COL = 0;
 constexpr uint32_t O_COL = 128;
 constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_PV = make_idesc_bf16(128, 64, false, true);
+
+// Optional clock64 trace of one CTA for pipeline studies: slot [role][event < 8][tile < 64]
+// (role 0 producer, 1 MMA issuer, 2 softmax warp 2). Off unless attn_fwd_set_trace was given
+// a buffer of 3 * 8 * 64 int64.
+struct FwdTrace {
+  long long* buf;
+  int cta;
+};
+__device__ __forceinline__ void fwd_trace(const FwdTrace& t, int role, int ev, int j) {
+  if (t.buf && blockIdx.x == t.cta && j < 64) t.buf[(role * 8 + ev) * 64 + j] = clock64();
+}
 
 __device__ __forceinline__ int row_limit(const AttnArgs& a, int q_local) {
   int lim = a.S;
@@ -67,15 +83,22 @@ __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs a, int n_qtiles,
-                    int* status) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+                    int* status, const FwdTrace tr) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem_raw) & 1023) != 0) {
+    if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadArgument);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;       // NS
-  uint64_t* kv_empty = bars + 1 + NS; // NS
-  uint64_t* s_full = bars + 1 + 2 * NS;
+  // K and V stages are released separately: K_j as soon as S_j is computed, V_j after PV_j,
+  // so the K load of a later tile does not wait for the previous P V product.
+  uint64_t* k_full = bars + 1;            // NS
+  uint64_t* k_empty = bars + 1 + NS;      // NS
+  uint64_t* v_full = bars + 1 + 2 * NS;   // NS
+  uint64_t* v_empty = bars + 1 + 3 * NS;  // NS
+  uint64_t* s_full = bars + 1 + 4 * NS;
   uint64_t* s_free = s_full + 1;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_done = s_full + 3;
@@ -104,8 +127,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 4);
@@ -137,29 +162,34 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_load_2d(sQ, &tmQ, q_full, qcol, qrow);
       tma_load_2d(sQ + 8192, &tmQ, q_full, qcol, qrow + 64);
       const int krow0 = static_cast<int>(b * a.kv_rows_per_b);
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < ntiles; ++j) {
+      int issued_k = 0, issued_v = 0;
+      // one 128-key tile of K (is_v false) or V into its stage, once the stage is free
+      auto load_tile = [&](int j, bool is_v) -> bool {
         const int s = j % NS;
-        const uint32_t ph = (j / NS) & 1;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
+        uint64_t* empty = is_v ? &v_empty[s] : &k_empty[s];
+        uint64_t* full = is_v ? &v_full[s] : &k_full[s];
+        if (!mbar_wait(empty, ((j / NS) & 1) ^ 1, abort_flag)) return false;
+        fwd_trace(tr, 0, is_v ? 1 : 0, j);
         int b0 = 2 * j, b1 = 2 * j + 1;
         if (sparse) {
           const int packed = a.pair_blocks[list_idx * a.max_pairs + j];
           b0 = packed & 0xffff;
           b1 = (packed >> 16) & 0xffff;
         }
-        uint8_t* sK = smem + OFF_K + s * TILE_BYTES;
-        uint8_t* sV = smem + OFF_V + s * TILE_BYTES;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        tma_load_2d(sK, &tmK, &kv_full[s], a.k_col + h * 64, krow0 + b0 * 64);
-        tma_load_2d(sK + 8192, &tmK, &kv_full[s], a.k_col + h * 64, krow0 + b1 * 64);
-        tma_load_2d(sV, &tmV, &kv_full[s], a.v_col + h * 64, krow0 + b0 * 64);
-        tma_load_2d(sV + 8192, &tmV, &kv_full[s], a.v_col + h * 64, krow0 + b1 * 64);
-        ++issued;
+        uint8_t* dst = smem + (is_v ? OFF_V : OFF_K) + s * TILE_BYTES;
+        const CUtensorMap* tm = is_v ? &tmV : &tmK;
+        const int col = (is_v ? a.v_col : a.k_col) + h * 64;
+        mbar_arrive_expect_tx(full, TILE_BYTES);
+        tma_load_2d(dst, tm, full, col, krow0 + b0 * 64);
+        tma_load_2d(dst + 8192, tm, full, col, krow0 + b1 * 64);
+        if (is_v) ++issued_v; else ++issued_k;
+        return true;
+      };
+      // K runs one tile ahead of V: K_{j+1} needs only S_{j-1} done, V_j needs PV_{j-2}
+      bool ok = ntiles == 0 || load_tile(0, false);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (j + 1 < ntiles) ok = load_tile(j + 1, false);
+        if (ok) ok = load_tile(j, true);
       }
       if (!ok) {
         if (status) atomicCAS(status, 0, kStatusTimeoutProducer);
@@ -169,9 +199,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       long long t0 = clock64();
       while (!mbar_try_wait(q_full, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
       }
-      for (int j = max(0, issued - NS); j < issued; ++j) {
+      for (int j = max(0, issued_k - NS); j < issued_k; ++j) {
         t0 = clock64();
-        while (!mbar_try_wait(&kv_full[j % NS], (j / NS) & 1) &&
+        while (!mbar_try_wait(&k_full[j % NS], (j / NS) & 1) &&
+               clock64() - t0 < kSpinLimitCycles / 8) {
+        }
+      }
+      for (int j = max(0, issued_v - NS); j < issued_v; ++j) {
+        t0 = clock64();
+        while (!mbar_try_wait(&v_full[j % NS], (j / NS) & 1) &&
                clock64() - t0 < kSpinLimitCycles / 8) {
         }
       }
@@ -183,6 +219,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t aP = smem_u32(sP);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait(p_full, i & 1, abort_flag)) return false;
+        if (!mbar_wait(&v_full[i % NS], (i / NS) & 1, abort_flag)) return false;
+        fwd_trace(tr, 1, 2, i);
         tc_fence_after();
         const uint32_t aV = smem_u32(smem + OFF_V + (i % NS) * TILE_BYTES);
 #pragma unroll
@@ -191,20 +229,22 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t db = make_sw128_desc(aV + kk * 2048, 8192, 1024);
           mma_bf16_ss(tmem + O_COL, da, db, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&kv_empty[i % NS]);
+        mma_commit(&v_empty[i % NS]);
         mma_commit(o_done);
         return true;
       };
       for (int j = 0; j < ntiles && ok; ++j) {
         const int s = j % NS;
-        if (!mbar_wait(&kv_full[s], (j / NS) & 1, abort_flag)) {
+        if (!mbar_wait(&k_full[s], (j / NS) & 1, abort_flag)) {
           ok = false;
           break;
         }
+        fwd_trace(tr, 1, 0, j);
         if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
+        fwd_trace(tr, 1, 1, j);
         tc_fence_after();
         const uint32_t aK = smem_u32(smem + OFF_K + s * TILE_BYTES);
 #pragma unroll
@@ -212,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           mma_bf16_ss(tmem + S_COL, make_sw128_desc(aQ + kk * 32, 16, 1024),
                       make_sw128_desc(aK + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
         }
+        mma_commit(&k_empty[s]);
         mma_commit(s_full);
         if (j > 0 && !issue_pv(j - 1)) ok = false;
       }
@@ -244,6 +285,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         ok = false;
         break;
       }
+      const bool tw = warp == 2 && lane == 0;
+      if (tw) fwd_trace(tr, 2, 0, j);
       tc_fence_after();
       float sf[128];
       {
@@ -264,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
+      if (tw) fwd_trace(tr, 2, 1, j);
       if (sparse) {
         const int bits = a.pair_mask[list_idx * a.max_pairs + j];
 #pragma unroll
@@ -283,26 +327,40 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < 128; ++c)
           if (base + c >= lim) sf[c] = -INFINITY;
       }
-      float mx = -INFINITY;
+      // row max and row sum as 8 independent chains (a single 128-long chain of dependent
+      // max/add instructions would be latency-bound with two softmax warps per SMSP)
+      float mp[8];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, sf[c]);
-      const float m_new = fmaxf(m, mx * sl2);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = exp2f(m - m_use);
-      float sum = 0.f;
+      for (int i = 0; i < 8; ++i) mp[i] = sf[i];
+#pragma unroll
+      for (int c = 8; c < 128; ++c) mp[c & 7] = fmaxf(mp[c & 7], sf[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      // The running max moves only when a score exceeds it by more than 2^8 (log2 units):
+      // exponentials stay <= 256, and most tiles skip the O rescale in TMEM.
+      const float mx2 = mx * sl2;
+      float alpha = 1.f;
+      if (mx2 > m + kRescaleLog2) {
+        alpha = exp2f(m - mx2);
+        m = mx2;
+      }
+      const float m_use = (m == -INFINITY) ? 0.f : m;
+      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 128; ++c) {
         const float p = exp2f(sf[c] * sl2 - m_use);
         sf[c] = p;
-        sum += p;
+        sp[c & 7] += p;
       }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
-      m = m_new;
+      if (tw) fwd_trace(tr, 2, 2, j);
       if (j > 0) {
         if (!mbar_wait(o_done, (j - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
+        if (tw) fwd_trace(tr, 2, 3, j);
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -332,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (tw) fwd_trace(tr, 2, 4, j);
     }
     if (!ok) {
       if (lane == 0 && status) atomicCAS(status, 0, kStatusTimeoutEpilogue);
@@ -375,7 +434,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+FwdTrace g_fwd_trace{nullptr, 0};
+
 }  // namespace
+
+void attn_fwd_set_trace(long long* buf, int cta) { g_fwd_trace = FwdTrace{buf, cta}; }
 
 void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0) return;
@@ -399,7 +462,7 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   attn_fwd_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tQ, tK, tV, a, n_qtiles,
-                                                          device_status(dev));
+                                                          device_status(dev), g_fwd_trace);
   count_launch();
   check_cuda(cudaGetLastError(), "attn_fwd_kernel launch");
 }

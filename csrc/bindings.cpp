@@ -329,6 +329,16 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   ddb::attn_fwd(a, stream());
 }
 
+void attn_fwd_set_trace(c10::optional<torch::Tensor> trace, int64_t cta) {
+  if (trace) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == torch::kInt64 && trace->numel() >= 3 * 8 * 64,
+                "trace must be int64 CUDA [3 * 8 * 64]");
+    ddb::attn_fwd_set_trace(reinterpret_cast<long long*>(trace->data_ptr<int64_t>()), cta);
+  } else {
+    ddb::attn_fwd_set_trace(nullptr, 0);
+  }
+}
+
 void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dq_acc,
               torch::Tensor dk, torch::Tensor dv, int64_t q_col, int64_t k_col, int64_t v_col,
@@ -1288,6 +1298,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sq_norm", &sq_norm, "sum of squares (fp32)");
   m.def("rope_rotate", &rope_rotate, "in-place rotary rotation of leading columns");
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention forward (dense / frame-causal / sparse)");
+  m.def("attn_fwd_set_trace", &attn_fwd_set_trace, "clock64 trace of one forward CTA (None: off)");
   m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"), py::arg("lse"),
         py::arg("delta"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("q_col"),

@@ -74,7 +74,7 @@ def bench_gemm(iters: int = 20, shapes=None):
 
 
 def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512,
-               dbg: int = 0):
+               dbg: int = 0, trace: bool = False):
     """Frame-causal flash attention fwd and bwd at the DiT-B training shape."""
     import math
 
@@ -113,6 +113,44 @@ def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int
                       "tflops": round(f_fwd / ms_f / 1e9, 1)}), flush=True)
     print(json.dumps({"kernel": "attn_bwd", "B": B, "H": H, "T": T, "tpf": tpf, "ms": round(ms_b, 3),
                       "tflops": round(f_bwd / ms_b / 1e9, 1), "debug_flags": dbg}), flush=True)
+    if trace:
+        _attn_trace(fwd, qkv, o, do, lse, delta, dq_acc, dqkv, B, H, T, tpf, sc)
+
+
+def _attn_trace(fwd, qkv, o, do, lse, delta, dq_acc, dqkv, B, H, T, tpf, sc):
+    """clock64 events of one heavy CTA per kernel (cycles from the CTA's first event):
+    forward roles producer / MMA / softmax, backward producer / MMA / softmax / dQ."""
+    from ._ext import ext
+
+    d = H * 64
+    buf = torch.zeros(3 * 8 * 64, dtype=torch.int64, device="cuda")
+    ext().attn_fwd_set_trace(buf, 0)
+    fwd()
+    torch.cuda.synchronize()
+    ext().attn_fwd_set_trace(None, 0)
+    _print_trace("attn_fwd", buf.view(3, 8, 64).cpu(), ["producer", "mma", "softmax"])
+    tb = torch.zeros(4 * 8 * 64, dtype=torch.int64, device="cuda")
+    ext().attn_delta(o, do, delta, 0, 0, B, H, T, T)
+    dq_acc.zero_()
+    ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d,
+                   2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, sc, None, None, None, 0, trace=tb, trace_cta=0)
+    torch.cuda.synchronize()
+    _print_trace("attn_bwd", tb.view(4, 8, 64).cpu(), ["producer", "mma", "softmax", "dq"])
+
+
+def _print_trace(name, t, roles):
+    nz = t[t != 0]
+    if nz.numel() == 0:
+        print(json.dumps({"trace": name, "empty": True}), flush=True)
+        return
+    t0 = int(nz.min())
+    out = {}
+    for r, role in enumerate(roles):
+        for ev in range(8):
+            row = t[r, ev]
+            if (row != 0).any():
+                out[f"{role}.{ev}"] = [int(x) - t0 if int(x) else None for x in row[:24]]
+    print(json.dumps({"trace": name, "cycles_from_first_event": out}), flush=True)
 
 
 def bench_conv3d(iters: int = 10):
@@ -292,6 +330,7 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--small", action="store_true", help="small attention case (for ncu)")
     p.add_argument("--B", type=int, default=8, help="attention batch")
+    p.add_argument("--trace", action="store_true", help="attention: clock64 trace of one CTA per kernel")
     p.add_argument("--shape", nargs="*", help="gemm shapes to run (names in GEMM_SHAPES)")
     p.add_argument("--transport", default="fused", help="ep: fused | nccl")
     args = p.parse_args()
@@ -299,7 +338,7 @@ def main():
         if w == "attn" and args.small:
             bench_attn(args.iters, B=1, H=2, T=8192)
         elif w == "attn":
-            bench_attn(args.iters, B=args.B)
+            bench_attn(args.iters, B=args.B, trace=args.trace)
         elif w == "attn_nodq":  # timing experiment: backward without the dQ reductions
             bench_attn(args.iters, dbg=1)
         elif w == "gemm":
