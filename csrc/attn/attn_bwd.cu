@@ -6,15 +6,19 @@
 //
 //   S^T  = K Q^T      (M=128 keys, N=128 queries, K=64)        TMEM cols [  0,128)
 //   dP^T = V dO^T     (M=128, N=128, K=64)                      TMEM cols [128,256)
-//   softmax warps (one thread per key row): P^T = exp2(S^T*scale*log2e - lse),
-//                 dS^T = scale * P^T (dP^T - delta); both to shared memory (bf16)
-//   dV  += P^T dO     (M=128, N=64, K=128 queries)              TMEM cols [256,320)
+//   softmax warps (one thread per key row): P^T = exp2(S^T*scale*log2e - lse) -> TMEM
+//                 cols [448,512) as bf16 pairs; dS^T = scale * P^T (dP^T - delta) ->
+//                 shared memory (bf16, 128-byte swizzle)
+//   dV  += P^T dO     (M=128, N=64, K=128 queries; A read from TMEM) TMEM cols [256,320)
 //   dK  += dS^T Q     (M=128, N=64, K=128)                      TMEM cols [320,384)
 //   dQ   = dS K       (M=128 queries, N=64, K=128 keys; dS^T read MN-major)
 //                                                               TMEM cols [384,448)
-//   dQ warps: TMEM -> the tile's P^T buffer (free once dQ is computed; fp32, two 128-byte
-//             swizzled boxes) -> one TMA reduce-add into the fp32 dQ accumulator, so the
-//             accumulation bypasses the load/store pipe the softmax warps use.
+//   dQ warps: TMEM -> the tile's dS^T buffer (free once dQ is computed; fp32, two
+//             128-byte swizzled boxes) -> one TMA reduce-add into the fp32 dQ
+//             accumulator, so the accumulation bypasses the load/store pipe the softmax
+//             warps use.
+// Q / dO (+ lse / delta) stream through 3 stages; keeping P^T out of shared memory pays
+// for the third stage and halves the shared-memory reads of the dV MMA.
 // After the last query tile dK and dV go to global memory (bf16).
 //
 // Roles: warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 softmax/dS (two warps per TMEM lane
@@ -33,14 +37,13 @@ namespace ddb {
 namespace {
 
 constexpr int kThreads = 448;
-constexpr int NS = 2;
+constexpr int NS = 3;                          // Q / dO stages
 constexpr int TILE = 16384;
 constexpr int OFF_K = 0;
 constexpr int OFF_V = OFF_K + TILE;
 constexpr int OFF_Q = OFF_V + TILE;            // NS stages
 constexpr int OFF_DO = OFF_Q + NS * TILE;      // NS stages
-constexpr int OFF_PT = OFF_DO + NS * TILE;     // 2 buffers x 2 chunks
-constexpr int OFF_DST = OFF_PT + 4 * TILE;     // 2 buffers x 2 chunks
+constexpr int OFF_DST = OFF_DO + NS * TILE;    // 2 buffers x 2 chunks (dS^T, then dQ staging)
 constexpr int OFF_VEC = OFF_DST + 4 * TILE;    // per stage: lse[128], delta[128]
 constexpr int OFF_BAR = OFF_VEC + NS * 1024;
 // no alignment slack: the dynamic shared window of a CTA without static shared memory
@@ -48,7 +51,7 @@ constexpr int OFF_BAR = OFF_VEC + NS * 1024;
 constexpr int SMEM_BYTES = OFF_BAR + 256;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384, C_PT = 448;
 constexpr uint32_t IDESC_SS = make_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_GRAD = make_idesc_bf16(128, 64, false, true);  // A K-major, B MN-major
 constexpr uint32_t IDESC_DQ = make_idesc_bf16(128, 64, true, true);     // both MN-major
@@ -104,13 +107,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* qd_empty = bars + 1 + NS;      // NS
   uint64_t* s_full = bars + 1 + 2 * NS;
   uint64_t* s_free = s_full + 1;
-  uint64_t* ds_full = s_full + 2;   // 2 buffers
-  uint64_t* ds_empty = s_full + 4;  // 2 buffers
+  uint64_t* ds_full = s_full + 2;   // 2 buffers: P^T (TMEM) and dS^T (smem) of the tile written
+  uint64_t* ds_empty = s_full + 4;  // 2 buffers: all gradient MMAs of the tile done
   uint64_t* dq_full = s_full + 6;
   uint64_t* dq_free = s_full + 7;
   uint64_t* drain = s_full + 8;
-  uint64_t* pt_free = s_full + 9;   // 2 buffers: P^T buffer free again (dQ staging read)
+  uint64_t* ds_free = s_full + 9;   // 2 buffers: dS^T buffer free again (dQ staging read)
   uint64_t* dq_staged = s_full + 11;  // the 4 dQ warps' rows are in shared memory
+  uint64_t* pt_tfree = s_full + 12;   // P^T in TMEM consumed by the dV MMAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_staged + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if ((smem_u32(smem_raw) & 1023) != 0) {
@@ -150,9 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(s_free, 8);
     mbar_init(&ds_full[0], 8);
     mbar_init(&ds_full[1], 8);
-    mbar_init(&pt_free[0], 1);
-    mbar_init(&pt_free[1], 1);
+    mbar_init(&ds_free[0], 1);
+    mbar_init(&ds_free[1], 1);
     mbar_init(dq_staged, 4);
+    mbar_init(pt_tfree, 1);
     mbar_init(&ds_empty[0], 1);
     mbar_init(&ds_empty[1], 1);
     mbar_init(dq_full, 1);
@@ -228,8 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t aK = smem_u32(smem + OFF_K);
       const uint32_t aV = smem_u32(smem + OFF_V);
       auto issue_grads = [&](int i) -> bool {
-        const int pb = i & 1;  // P^T / dS^T buffer
-        const uint32_t aPT = smem_u32(smem + OFF_PT + pb * 2 * TILE);
+        const int pb = i & 1;  // dS^T buffer
         const uint32_t aDST = smem_u32(smem + OFF_DST + pb * 2 * TILE);
         if (!mbar_wait(&ds_full[pb], (i >> 1) & 1, abort_flag)) return false;
         DDB_TRACE(1, 3, i);
@@ -239,18 +243,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % NS;
         const uint32_t aQ = smem_u32(smem + OFF_Q + s * TILE);
         const uint32_t aDO = smem_u32(smem + OFF_DO + s * TILE);
-        if (!(g.debug_flags & 8))
+        if (!(g.debug_flags & 8)) {
+          // dV += P^T dO: A = P^T straight from TMEM (keys = lanes, 16 queries per 8
+          // columns), B = dO [queries][dh] read MN-major
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // K = 128 queries
-          const uint32_t off = (kk >> 2) * TILE + (kk & 3) * 32;
-          // dV += P^T dO ; dK += dS^T Q   (B operands [queries][dh] read MN-major)
-          mma_bf16_ss(tmem + C_DV, make_sw128_desc(aPT + off, 16, 1024),
-                      make_sw128_desc(aDO + kk * 2048, 8192, 1024), IDESC_GRAD,
-                      (i > 0 || kk > 0) ? 1u : 0u);
-          mma_bf16_ss(tmem + C_DK, make_sw128_desc(aDST + off, 16, 1024),
-                      make_sw128_desc(aQ + kk * 2048, 8192, 1024), IDESC_GRAD,
-                      (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16_ts(tmem + C_DV, tmem + C_PT + kk * 8, make_sw128_desc(aDO + kk * 2048, 8192, 1024),
+                        IDESC_GRAD, (i > 0 || kk > 0) ? 1u : 0u);
         }
+        mma_commit(pt_tfree);
+        if (!(g.debug_flags & 8)) {
+          // dK += dS^T Q
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * TILE + (kk & 3) * 32;
+            mma_bf16_ss(tmem + C_DK, make_sw128_desc(aDST + off, 16, 1024),
+                        make_sw128_desc(aQ + kk * 2048, 8192, 1024), IDESC_GRAD,
+                        (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(&qd_empty[s]);  // Q and dO of this stage are no longer read
         if (!(g.debug_flags & 8))
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // K = 128 keys: dQ = dS K
@@ -259,7 +271,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_bf16_ss(tmem + C_DQ, make_sw128_desc(aDST + kk * 2048, TILE, 1024),
                       make_sw128_desc(aK + kk * 2048, 8192, 1024), IDESC_DQ, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&qd_empty[s]);
         mma_commit(&ds_empty[pb]);
         mma_commit(dq_full);
         DDB_TRACE(1, 5, i);
@@ -329,14 +340,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp == 2 && lane == 0) DDB_TRACE(2, 0, j);
       const uint32_t ph_free = ((j >> 1) & 1) ^ 1;
       if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
-          !mbar_wait(&ds_empty[pb], ph_free, abort_flag) ||
-          !mbar_wait(&pt_free[pb], ph_free, abort_flag)) {
+          !mbar_wait(&ds_free[pb], ph_free, abort_flag)) {
         ok = false;
         break;
       }
       if (warp == 2 && lane == 0) DDB_TRACE(2, 1, j);
       tc_fence_after();
-      const uint32_t pt_base = smem_u32(smem + OFF_PT + pb * 2 * TILE) + r * 128;
       const uint32_t ds_base = smem_u32(smem + OFF_DST + pb * 2 * TILE) + r * 128;
 #pragma unroll 1
       for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
@@ -345,6 +354,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(trow + C_DP + c0, rp);
         tmem_wait_ld();
         if (warp == 2 && lane == 0 && j < 8) DDB_TRACE(2, 3 + ((c0 & 63) >> 5), j);
+        if ((c0 & 63) == 32) {  // this warp's S^T / dP^T columns are all read
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_free);
+        }
         const bool half_on = (bits >> ((c0 >> 6) * 2 + khalf)) & 1;
         float p[32], ds[32];
         if (g.debug_flags & 2) {
@@ -355,14 +369,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int qi = c0 + c;
-            const bool vis = half_on && (q0 + qi >= qmin);
-            const float pv = vis ? exp2f(__uint_as_float(rs[c]) * sl2 - s_lse[qi]) : 0.f;
-            p[c] = pv;
-            ds[c] = pv * (__uint_as_float(rp[c]) - s_delta[qi]) * a.scale;
+          for (int c4 = 0; c4 < 32; c4 += 4) {
+            // lse / delta of 4 queries as broadcast 16-byte loads
+            const float4 l4 = *reinterpret_cast<const float4*>(s_lse + c0 + c4);
+            const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c0 + c4);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = c4 + e;
+              const bool vis = half_on && (q0 + c0 + c >= qmin);
+              const float pv = vis ? exp2f(__uint_as_float(rs[c]) * sl2 - lv[e]) : 0.f;
+              p[c] = pv;
+              ds[c] = pv * (__uint_as_float(rp[c]) - dv[e]) * a.scale;
+            }
           }
         }
+        // P^T (bf16 pairs) -> TMEM for the dV MMA, once the previous tile's dV is done
+        if ((c0 & 63) == 0 && j > 0) {
+          if (!mbar_wait(pt_tfree, (j - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(p[2 * i], p[2 * i + 1]);
+          tmem_st16(trow + C_PT + (c0 >> 1), pk);
+        }
+        // dS^T (bf16) -> shared memory for the dK and dQ MMAs
         const int ch = c0 >> 6;
         if (!(g.debug_flags & 4))
 #pragma unroll
@@ -370,17 +406,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int u = ((c0 & 63) >> 3) + u4;
           const int c = u4 * 8;
           const uint32_t off = ch * TILE + ((u ^ swz) << 4);
-          st_shared_v4(pt_base + off, pack_bf16(p[c], p[c + 1]), pack_bf16(p[c + 2], p[c + 3]),
-                       pack_bf16(p[c + 4], p[c + 5]), pack_bf16(p[c + 6], p[c + 7]));
           st_shared_v4(ds_base + off, pack_bf16(ds[c], ds[c + 1]),
                        pack_bf16(ds[c + 2], ds[c + 3]), pack_bf16(ds[c + 4], ds[c + 5]),
                        pack_bf16(ds[c + 6], ds[c + 7]));
         }
       }
+      if (!ok) break;
       if (warp == 2 && lane == 0) DDB_TRACE(2, 2, j);
+      tmem_wait_st();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[pb]);
@@ -439,11 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      // The tile's P^T buffer is free: every MMA that read it completed before dq_full.
+      // The tile's dS^T buffer is free: every MMA that read it completed before dq_full.
       // Stage dQ there as two [128 rows][32 fp32] boxes, 128-byte swizzled (16-byte chunk
       // c of row r at chunk c ^ (r & 7)), then one thread adds both boxes into the
       // accumulator with TMA and frees the buffer once the reads are done.
-      uint8_t* stage = smem + OFF_PT + pb * 2 * TILE;
+      uint8_t* stage = smem + OFF_DST + pb * 2 * TILE;
       if (!(g.debug_flags & 1)) {
         const uint32_t sbase = smem_u32(stage) + r * 128;
 #pragma unroll
@@ -466,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_store_commit();
           tma_store_wait_read();
         }
-        mbar_arrive(&pt_free[pb]);
+        mbar_arrive(&ds_free[pb]);
       }
       // warp-uniform exit (the next iteration's TMEM loads are warp-collective)
       if (warp == 10 && !__shfl_sync(0xffffffffu, staged, 0)) {
