@@ -338,9 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       if (warp == 2 && lane == 0) DDB_TRACE(2, 0, j);
-      const uint32_t ph_free = ((j >> 1) & 1) ^ 1;
-      if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag) ||
-          !mbar_wait(&ds_free[pb], ph_free, abort_flag)) {
+      if (!mbar_wait(&qd_full[s], (j / NS) & 1, abort_flag)) {
         ok = false;
         break;
       }
@@ -398,7 +396,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(p[2 * i], p[2 * i + 1]);
           tmem_st16(trow + C_PT + (c0 >> 1), pk);
         }
-        // dS^T (bf16) -> shared memory for the dK and dQ MMAs
+        // dS^T (bf16) -> shared memory for the dK and dQ MMAs, once the buffer's previous
+        // contents (tile j - 2's dS^T, then its dQ staging) have been read
+        if ((c0 & 63) == 0 && !mbar_wait(&ds_free[pb], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
         const int ch = c0 >> 6;
         if (!(g.debug_flags & 4))
 #pragma unroll
