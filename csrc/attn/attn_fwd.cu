@@ -3,15 +3,16 @@
 // One CTA = one (batch, head, 128-query tile). Roles (192 threads, 2 CTAs per SM):
 //   warp 0     TMA: Q tile once (two 64-row boxes), then K and V tiles of 128 keys made of
 //              two independent 64-key blocks (so SLA can pair any two selected blocks)
-//              into 2-stage rings, K one tile ahead of V.
+//              into 3-stage rings, K one tile ahead of V.
 //   warp 1     TMEM owner + MMA issuer: S = Q K^T (M=128, N=128, K=64) into TMEM
-//              columns [0,128), O += P V (M=128, N=64, K=128) into columns [128,192).
+//              columns [0,128), O += P V (M=128, N=64, K=128; A = P read from TMEM
+//              columns [192,256)) into columns [128,192).
 //   warps 2-5  softmax: one thread per query row reads its S row from TMEM, applies the
 //              mask, keeps the running max / sum (log2 domain), rescales its O row in
-//              TMEM when the max moves by more than 2^8, writes P (bf16) to shared memory in the 128-byte
-//              swizzled K-major layout the PV MMA reads, and finally normalises O.
+//              TMEM when the max moves by more than 2^8, writes P (bf16 pairs) to TMEM,
+//              and finally normalises O.
 // The S MMA of tile j+1 overlaps the softmax of tile j; the second resident CTA of the
-// SM (113 KB of shared memory each) overlaps the rest.
+// SM (112 KB of shared memory each) overlaps the rest.
 //
 // Masks: frame-causal (all keys of frames <= the query's frame), token-causal, none;
 // KV-cache attention via absolute query/key position offsets; block-sparse SLA via a
@@ -32,13 +33,12 @@ namespace {
 
 constexpr int kThreads = 192;
 constexpr float kRescaleLog2 = 8.f;
-constexpr int NS = 2;
+constexpr int NS = 3;
 constexpr int TILE_BYTES = 16384;  // 128 rows x 64 bf16
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + TILE_BYTES;
 constexpr int OFF_V = OFF_K + NS * TILE_BYTES;
-constexpr int OFF_P = OFF_V + NS * TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * TILE_BYTES;
+constexpr int OFF_BAR = OFF_V + NS * TILE_BYTES;
 // No alignment slack: the dynamic shared window of a CTA without static shared memory
 // starts 1024-byte aligned (checked below). With the slack two CTAs (2 x (113 KB + 1 KB
 // reserved)) would not fit the SM's 228 KB and only one would be resident.
@@ -47,6 +47,7 @@ static_assert(2 * (SMEM_BYTES + 1024) <= 233472, "two CTAs per SM");
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t S_COL = 0;
 constexpr uint32_t O_COL = 128;
+constexpr uint32_t P_COL = 192;  // P as bf16 pairs: 128 keys in 64 columns
 constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_PV = make_idesc_bf16(128, 64, false, true);
 
@@ -72,12 +73,6 @@ __device__ __forceinline__ int row_limit(const AttnArgs& a, int q_local) {
   return max(lim, 0);
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
-}
 
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -149,7 +144,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   uint8_t* sQ = smem + OFF_Q;
-  uint8_t* sP = smem + OFF_P;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -216,7 +210,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, abort_flag);
       const uint32_t aQ = smem_u32(sQ);
-      const uint32_t aP = smem_u32(sP);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait(p_full, i & 1, abort_flag)) return false;
         if (!mbar_wait(&v_full[i % NS], (i / NS) & 1, abort_flag)) return false;
@@ -224,10 +217,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
         const uint32_t aV = smem_u32(smem + OFF_V + (i % NS) * TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t da = make_sw128_desc(aP + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024);
+        for (int kk = 0; kk < 8; ++kk) {  // A = P from TMEM: 16 keys per 8 columns
           const uint64_t db = make_sw128_desc(aV + kk * 2048, 8192, 1024);
-          mma_bf16_ss(tmem + O_COL, da, db, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tmem + O_COL, tmem + P_COL + kk * 8, db, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&v_empty[i % NS]);
         mma_commit(o_done);
@@ -276,8 +268,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int qhalf = r >> 6;
     const float sl2 = a.scale * 1.4426950408889634f;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const uint32_t pbase = smem_u32(sP) + r * 128;
-    const uint32_t swz = r & 7;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
@@ -345,12 +335,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         m = mx2;
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
+      // exponentials packed to bf16 pairs as they are made (P lives in 64 registers)
       float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float p = exp2f(sf[c] * sl2 - m_use);
-        sf[c] = p;
-        sp[c & 7] += p;
+      for (int c = 0; c < 128; c += 2) {
+        const float p0 = exp2f(sf[c] * sl2 - m_use);
+        const float p1 = exp2f(sf[c + 1] * sl2 - m_use);
+        sp[c & 7] += p0;
+        sp[(c + 1) & 7] += p1;
+        pk[c >> 1] = pack_bf16(p0, p1);
       }
       const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
@@ -375,18 +369,15 @@ __global__ void __launch_bounds__(kThreads, 2)
           tmem_wait_st();
         }
       }
-      // P (bf16) -> shared memory, 128-byte swizzle, two 64-key chunks
+      // P (bf16 pairs) -> TMEM columns [P_COL, P_COL + 64), the A operand of the PV MMA
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t q[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int c0 = ch * 64 + u * 8;
-          st_shared_v4(pbase + ch * TILE_BYTES + ((u ^ swz) << 4), pack_bf16(sf[c0], sf[c0 + 1]),
-                       pack_bf16(sf[c0 + 2], sf[c0 + 3]), pack_bf16(sf[c0 + 4], sf[c0 + 5]),
-                       pack_bf16(sf[c0 + 6], sf[c0 + 7]));
-        }
+        for (int i = 0; i < 16; ++i) q[i] = pk[ch * 16 + i];
+        tmem_st16(trow + P_COL + ch * 16, q);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
