@@ -77,12 +77,6 @@ __device__ __forceinline__ int first_query_seeing(const AttnArgs& a, int k) {
   return 0;
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
-}
 
 // trace slot: [role (0 producer, 1 mma, 2 softmax, 3 dq)][event < 8][pair < 64]
 #define DDB_TRACE(role, ev, j)                                                      \

@@ -8,8 +8,11 @@
 //   warp 1      owns TMEM (2 x BN fp32 columns, double-buffered accumulator) and issues
 //               tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees
 //               ring slots and hands finished accumulators to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fused elementwise op,
-//               16-byte global stores (or fp32 vector reductions for split-K).
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fused elementwise op; bf16
+//               outputs go through a per-warp [32 rows x 64 cols] shared-memory box
+//               (128-byte swizzle) and a TMA store, so every row segment leaves as full
+//               lines instead of 32 scattered 16-byte stores per instruction; fp32
+//               outputs use 16-byte stores or vector reductions (split-K).
 // Tiles are walked persistently (n fastest, so concurrent CTAs share the A panel in L2);
 // the epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -34,6 +37,12 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
+// per epilogue warp: one [32 x 64] bf16 box for D (128-byte swizzle) and one [32 x 32]
+// bf16 box for D2 (SwiGLU activation, unswizzled 64-byte rows)
+constexpr int kOutBoxD = 32 * 128;
+constexpr int kOutBoxD2 = 32 * 64;
+constexpr int kOutStage = 4 * (kOutBoxD + kOutBoxD2);
+
 template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -41,9 +50,54 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int OFF_OUT = STAGES * STAGE_BYTES;   // epilogue output boxes
+  static constexpr int OFF_BAR = OFF_OUT + kOutStage;     // mbarriers, TMEM slot, abort flag
+  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
+// TMA store maps of the bf16 outputs: D as {cols, rows, batch} with [64 x 32] boxes,
+// D2 as {cols, rows, batch} with [32 x 32] boxes. use == 0: plain global stores.
+struct OutMaps {
+  CUtensorMap d;
+  CUtensorMap d2;
+  int use;
+};
+
+// Per-warp output staging. Rows are the warp's 32 TMEM lanes (row `lane` of the box).
+struct OutStage {
+  uint32_t box_d;   // shared address of this warp's D box
+  uint32_t box_d2;  // and D2 box
+  // wait until the previous stores of this warp have read their boxes
+  __device__ __forceinline__ void acquire(int lane) const {
+    if (lane == 0) tma_store_wait_read();
+    __syncwarp();
+  }
+  // 32 bf16 columns (16 packed pairs) into half `h` of the 64-column D box
+  __device__ __forceinline__ void put_d(int lane, int h, const uint32_t (&p)[16]) const {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      st_shared_v4(box_d + lane * 128 + (((h * 4 + i) ^ (lane & 7)) << 4), p[4 * i], p[4 * i + 1],
+                   p[4 * i + 2], p[4 * i + 3]);
+  }
+  __device__ __forceinline__ void put_d2(int lane, const uint32_t (&p)[16]) const {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      st_shared_v4(box_d2 + lane * 64 + i * 16, p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+  }
+  // hand the filled D box (and the D2 box when `d2`) to TMA; rows / columns past the
+  // tensor's extent are clipped by the copy
+  __device__ __forceinline__ void flush(int lane, const OutMaps& om, int col, int row0, int bt, bool d2,
+                                        int col2) const {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(&om.d, box_d, col, row0, bt);
+      if (d2) tma_store_3d(&om.d2, box_d2, col2, row0, bt);
+      tma_store_commit();
+    }
+  }
+};
 struct Sched {
   int tiles_m, tiles_n, kblocks, kb_per_split, splits, total, M;
   int grouped;
@@ -92,7 +146,8 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x))
 // ---------------------------------------------------------------- epilogue ops
 template <int EPI>
 __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0,
-                                            const uint32_t (&r)[32]) {
+                                            const uint32_t (&r)[32], const OutStage* st = nullptr,
+                                            int lane = 0, int h = 0) {
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
@@ -171,6 +226,13 @@ __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0
           }
         }
       }
+      if (st != nullptr) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+        st->put_d(lane, h, pk);
+        return;
+      }
       __nv_bfloat16* d;
       if (EPI == kEpiBf16 && a.d_peers != nullptr) {  // reduce-scatter: P2P store to the row's owner
         const int owner = row / a.d_rows_per_peer;
@@ -189,7 +251,8 @@ __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0
 
 // SwiGLU forward: accumulator columns come in groups of 64: 32 gate then 32 up.
 __device__ __forceinline__ void epi_swiglu(const GemmArgs& a, int row, int col0,
-                                           const uint32_t (&rg)[32], const uint32_t (&ru)[32]) {
+                                           const uint32_t (&rg)[32], const uint32_t (&ru)[32],
+                                           const OutStage* st = nullptr, int lane = 0) {
   __nv_bfloat16* gu =
       reinterpret_cast<__nv_bfloat16*>(a.D) + static_cast<long>(row) * a.ldd + col0;
   __nv_bfloat16* act =
@@ -200,6 +263,19 @@ __device__ __forceinline__ void epi_swiglu(const GemmArgs& a, int row, int col0,
     // round through bf16 so the saved pre-activation and the activation agree exactly
     g[i] = __bfloat162float(__float2bfloat16(__uint_as_float(rg[i])));
     u[i] = __bfloat162float(__float2bfloat16(__uint_as_float(ru[i])));
+  }
+  if (st != nullptr) {
+    uint32_t pg[16], pu[16], ph[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      pg[i] = pack_bf16(g[2 * i], g[2 * i + 1]);
+      pu[i] = pack_bf16(u[2 * i], u[2 * i + 1]);
+      ph[i] = pack_bf16(silu_f(g[2 * i]) * u[2 * i], silu_f(g[2 * i + 1]) * u[2 * i + 1]);
+    }
+    st->put_d(lane, 0, pg);
+    st->put_d(lane, 1, pu);
+    st->put_d2(lane, ph);
+    return;
   }
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
@@ -220,7 +296,8 @@ __device__ __forceinline__ void epi_swiglu(const GemmArgs& a, int row, int col0,
 // SwiGLU backward: acc = dA for activation columns [col0, col0+32), which map to the
 // gate columns 2*col0 + [0,32) and up columns 2*col0 + 32 + [0,32) of gu.
 __device__ __forceinline__ void epi_dswiglu(const GemmArgs& a, int row, int col0,
-                                            const uint32_t (&r)[32]) {
+                                            const uint32_t (&r)[32], const OutStage* st = nullptr,
+                                            int lane = 0) {
   const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(a.C) +
                             static_cast<long>(row) * a.ldc + 2 * col0;
   __nv_bfloat16* dgu =
@@ -251,6 +328,17 @@ __device__ __forceinline__ void epi_dswiglu(const GemmArgs& a, int row, int col0
     du[i] = da * sl;
     dg[i] = da * u[i] * s * (1.f + g[i] * (1.f - s));
   }
+  if (st != nullptr) {
+    uint32_t pg[16], pu[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      pg[i] = pack_bf16(dg[2 * i], dg[2 * i + 1]);
+      pu[i] = pack_bf16(du[2 * i], du[2 * i + 1]);
+    }
+    st->put_d(lane, 0, pg);
+    st->put_d(lane, 1, pu);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
     st_global_v4(dgu + i, pack_bf16(dg[i], dg[i + 1]), pack_bf16(dg[i + 2], dg[i + 3]),
@@ -270,7 +358,8 @@ template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args,
-                   const Sched sched, int* status, const __grid_constant__ PeerMaps pmA) {
+                   const Sched sched, int* status, const __grid_constant__ PeerMaps pmA,
+                   const __grid_constant__ OutMaps om) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = make_idesc_bf16(BM, BN, A_MN, B_MN);
@@ -278,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -438,6 +527,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    constexpr bool kBf16Out = EPI != kEpiF32 && EPI != kEpiF32Atomic;
+    const bool tma_out = kBf16Out && om.use != 0;
+    const OutStage ost{smem_u32(smem + Cfg::OFF_OUT + (warp - 2) * kOutBoxD),
+                       smem_u32(smem + Cfg::OFF_OUT + 4 * kOutBoxD + (warp - 2) * kOutBoxD2)};
     int buf = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
@@ -455,6 +548,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = m0 + row_in_tile < args.M;
       const int row = (sched.grouped == 1 ? 0 : bt * args.M) + m0 + row_in_tile;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+      // TMA box coordinates: rows within the batch, batch index (grouped: one buffer)
+      const int box_row = m0 + quad * 32;
+      const int box_bt = sched.grouped == 1 ? 0 : bt;
       if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 64) {
@@ -462,7 +558,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tbase + c, rg);
           tmem_ld32(tbase + c + 32, ru);
           tmem_wait_ld();
-          if (row_ok && n0 + c < args.N) epi_swiglu(args, row, n0 + c, rg, ru);
+          if (n0 + c >= args.N) continue;
+          if (tma_out) {
+            ost.acquire(lane);  // rows past M: nothing read, the store clips them
+            if (row_ok) epi_swiglu(args, row, n0 + c, rg, ru, &ost, lane);
+            ost.flush(lane, om, n0 + c, box_row, box_bt, true, (n0 + c) >> 1);
+          } else if (row_ok) {
+            epi_swiglu(args, row, n0 + c, rg, ru);
+          }
         }
       } else {
 #pragma unroll 1
@@ -470,11 +573,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_wait_ld();
-          if (row_ok && n0 + c < args.N) {
-            if constexpr (EPI == kEpiDSwiGLU)
+          if (n0 + c >= args.N) continue;
+          if constexpr (EPI == kEpiDSwiGLU) {
+            if (tma_out) {  // 32 activation-gradient columns -> one 64-column box of dgu
+              ost.acquire(lane);
+              if (row_ok) epi_dswiglu(args, row, n0 + c, r, &ost, lane);
+              ost.flush(lane, om, 2 * (n0 + c), box_row, box_bt, false, 0);
+            } else if (row_ok) {
               epi_dswiglu(args, row, n0 + c, r);
-            else
-              epi_chunk32<EPI>(args, row, n0 + c, r);
+            }
+          } else if (tma_out) {  // two 32-column chunks fill one 64-column box
+            const int h = (c >> 5) & 1;
+            if (h == 0) ost.acquire(lane);
+            if (row_ok) epi_chunk32<EPI>(args, row, n0 + c, r, &ost, lane, h);
+            if (h == 1 || n0 + c + 32 >= args.N) ost.flush(lane, om, n0 + c - 32 * h, box_row, box_bt, false, 0);
+          } else if (row_ok) {
+            epi_chunk32<EPI>(args, row, n0 + c, r);
           }
         }
       }
@@ -486,6 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (tma_out && lane == 0) tma_store_wait_all();  // boxes read and stores complete
   }
 
   tc_fence_before();
@@ -540,7 +655,24 @@ void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, in
   }
   if (a.d_peers != nullptr && (EPI != kEpiBf16 || a.C != nullptr || a.bias != nullptr || a.d_rows_per_peer <= 0))
     throw std::runtime_error("gemm: the reduce-scatter store needs the plain bf16 epilogue");
-  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status, pm);
+  OutMaps om;
+  std::memset(&om, 0, sizeof(om));
+  constexpr bool kBf16Out = EPI != kEpiF32 && EPI != kEpiF32Atomic;
+  auto aligned = [](const void* p, long ld) {
+    return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ld % 8 == 0;
+  };
+  if (kBf16Out && a.d_peers == nullptr && a.grouped != 2 && aligned(a.D, a.ldd) &&
+      (EPI != kEpiSwiGLU || aligned(a.D2, a.ldd2))) {
+    const int nbd = a.grouped == 1 ? 1 : a.batch;
+    const long dcols = EPI == kEpiDSwiGLU ? 2L * a.N : a.N;
+    om.d = make_tmap_3d(a.D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dcols, a.M, nbd, a.ldd * 2,
+                        static_cast<uint64_t>(a.M) * a.ldd * 2, 64, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (EPI == kEpiSwiGLU)
+      om.d2 = make_tmap_3d(a.D2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N / 2, a.M, nbd, a.ldd2 * 2,
+                           static_cast<uint64_t>(a.M) * a.ldd2 * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    om.use = 1;
+  }
+  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status, pm, om);
   count_launch();
   check_cuda(cudaGetLastError(), "gemm_tc_kernel launch");
 }
@@ -597,24 +729,33 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   const int sms = num_sms(dev);
+  const int kblocks = (a.K + BK - 1) / BK;
+  const long tiles_m = (a.M + BM - 1) / BM;
+  const long nbatch = (a.grouped == 0 && a.batch > 1) ? a.batch : 1;
+  // Estimated time of a (BN, split-K) choice: waves of persistent tiles x tile work. A
+  // 128-wide tile re-reads its A tile from shared memory twice as often per FLOP and runs
+  // at ~0.8 of a 256-wide one.
+  auto est = [&](int bn_c, int sp) -> double {
+    const long items = tiles_m * ((a.N + bn_c - 1) / bn_c) * sp * nbatch;
+    const long waves = (items + sms - 1) / sms;
+    const long kb = (kblocks + sp - 1) / sp;
+    return static_cast<double>(waves) * bn_c * kb / (bn_c == 256 ? 1.0 : 0.8);
+  };
   int bn = a.bn;
   if (bn == 0) {
-    // 256-wide tiles unless that leaves most SMs idle on a small problem
-    const long tiles256 = static_cast<long>((a.M + BM - 1) / BM) * ((a.N + 255) / 256);
-    bn = (a.N >= 256 && tiles256 >= sms) ? 256 : 128;
-    if (a.N % 256 != 0 && a.N < 512) bn = 128;
+    bn = 128;
+    if (a.N >= 256 && !(a.N % 256 != 0 && a.N < 512) && est(256, 1) <= est(128, 1)) bn = 256;
   }
   Sched s;
-  s.tiles_m = (a.M + BM - 1) / BM;
+  s.tiles_m = static_cast<int>(tiles_m);
   s.tiles_n = (a.N + bn - 1) / bn;
-  s.kblocks = (a.K + BK - 1) / BK;
+  s.kblocks = kblocks;
   int splits = 1;
   if (epi == kEpiF32Atomic) {
     splits = a.splits;
-    if (splits <= 0) {
-      const int tiles = s.tiles_m * s.tiles_n;
+    if (splits <= 0) {  // split K only while it strictly shortens the estimate
       splits = 1;
-      while (tiles * splits * 2 <= 2 * sms && s.kblocks / (splits * 2) >= 8) splits *= 2;
+      while (s.kblocks / (splits * 2) >= 8 && est(bn, splits * 2) < est(bn, splits)) splits *= 2;
     }
   }
   s.kb_per_split = (s.kblocks + splits - 1) / splits;
