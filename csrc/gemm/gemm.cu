@@ -37,67 +37,112 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
-// per epilogue warp: one [32 x 64] bf16 box for D (128-byte swizzle) and one [32 x 32]
-// bf16 box for D2 (SwiGLU activation, unswizzled 64-byte rows)
+// Epilogue staging per epilogue warp (bf16-output kernels only), each double-buffered:
+//   D  box [32 rows x 64 cols] bf16, 128-byte swizzle       (TMA store)
+//   D2 box [32 rows x 32 cols] bf16, unswizzled 64-byte rows (TMA store, SwiGLU activation)
+//   C  box [32 rows x 64 cols] bf16, 128-byte swizzle       (TMA load of the residual / gu)
 constexpr int kOutBoxD = 32 * 128;
 constexpr int kOutBoxD2 = 32 * 64;
-constexpr int kOutStage = 4 * (kOutBoxD + kOutBoxD2);
+constexpr int kOffD2 = 4 * 2 * kOutBoxD;
+constexpr int kOffC = kOffD2 + 4 * 2 * kOutBoxD2;
+constexpr int kOutStage = kOffC + 4 * 2 * kOutBoxD;
 
-template <int BN>
+// Shared-memory layouts: fp32 outputs (no boxes), bf16 outputs (D boxes only), and
+// bf16 outputs with a second output or a C operand (all boxes, one operand stage fewer).
+enum GemmLayout : int { kLayF32 = 0, kLayOut = 1, kLayOutC = 2 };
+
+template <int BN, int LAY>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = LAY == kLayOutC ? ((BN == 256) ? 3 : 4) : ((BN == 256) ? 4 : 6);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int OFF_OUT = STAGES * STAGE_BYTES;   // epilogue output boxes
-  static constexpr int OFF_BAR = OFF_OUT + kOutStage;     // mbarriers, TMEM slot, abort flag
+  static constexpr int OFF_OUT = STAGES * STAGE_BYTES;   // epilogue boxes
+  static constexpr int OUT_BYTES = LAY == kLayOutC ? kOutStage : (LAY == kLayOut ? kOffD2 : 0);
+  static constexpr int OFF_BAR = OFF_OUT + OUT_BYTES;    // mbarriers, TMEM slot, abort flag
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
-// TMA store maps of the bf16 outputs: D as {cols, rows, batch} with [64 x 32] boxes,
-// D2 as {cols, rows, batch} with [32 x 32] boxes. use == 0: plain global stores.
+// TMA maps of the bf16 epilogue: D {cols, rows, batch} with [64 x 32] boxes, D2 with
+// [32 x 32] boxes, C (residual / gu) with [64 x 32] boxes. use == 0: plain global stores;
+// use_c == 0: C read with plain loads.
 struct OutMaps {
   CUtensorMap d;
   CUtensorMap d2;
+  CUtensorMap c;
   int use;
+  int use_c;
 };
 
-// Per-warp output staging. Rows are the warp's 32 TMEM lanes (row `lane` of the box).
+// Per-warp output staging; rows are the warp's 32 TMEM lanes (row `lane` of each box).
+// Box k of the warp uses buffer k & 1.
 struct OutStage {
-  uint32_t box_d;   // shared address of this warp's D box
-  uint32_t box_d2;  // and D2 box
-  // wait until the previous stores of this warp have read their boxes
+  uint32_t base_d, base_d2, base_c;  // shared addresses of this warp's buffer 0
+  uint64_t* cbar;                    // 2 mbarriers: C box loaded
+  int k = 0;                         // output boxes flushed so far
+  int kc = 0;                        // C boxes requested so far
+  __device__ __forceinline__ uint32_t box_d() const { return base_d + (k & 1) * kOutBoxD; }
+  __device__ __forceinline__ uint32_t box_d2() const { return base_d2 + (k & 1) * kOutBoxD2; }
+  // wait until the store that last used this buffer (two boxes ago) has read it
   __device__ __forceinline__ void acquire(int lane) const {
-    if (lane == 0) tma_store_wait_read();
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
     __syncwarp();
   }
   // 32 bf16 columns (16 packed pairs) into half `h` of the 64-column D box
   __device__ __forceinline__ void put_d(int lane, int h, const uint32_t (&p)[16]) const {
+    const uint32_t b = box_d() + lane * 128;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      st_shared_v4(box_d + lane * 128 + (((h * 4 + i) ^ (lane & 7)) << 4), p[4 * i], p[4 * i + 1],
-                   p[4 * i + 2], p[4 * i + 3]);
+      st_shared_v4(b + (((h * 4 + i) ^ (lane & 7)) << 4), p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
   }
   __device__ __forceinline__ void put_d2(int lane, const uint32_t (&p)[16]) const {
+    const uint32_t b = box_d2() + lane * 64;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      st_shared_v4(box_d2 + lane * 64 + i * 16, p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+    for (int i = 0; i < 4; ++i) st_shared_v4(b + i * 16, p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
   }
-  // hand the filled D box (and the D2 box when `d2`) to TMA; rows / columns past the
-  // tensor's extent are clipped by the copy
+  // hand the filled D box (and the D2 box when `d2`) to TMA as one bulk group; rows /
+  // columns past the tensor's extent are clipped by the copy
   __device__ __forceinline__ void flush(int lane, const OutMaps& om, int col, int row0, int bt, bool d2,
-                                        int col2) const {
+                                        int col2) {
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_3d(&om.d, box_d, col, row0, bt);
-      if (d2) tma_store_3d(&om.d2, box_d2, col2, row0, bt);
+      tma_store_3d(&om.d, box_d(), col, row0, bt);
+      if (d2) tma_store_3d(&om.d2, box_d2(), col2, row0, bt);
       tma_store_commit();
     }
+    ++k;
+  }
+  // request C box kc (columns col.., rows row0.., batch bt) into buffer kc & 1; the buffer's
+  // previous box was consumed by this warp before (program order + __syncwarp)
+  __device__ __forceinline__ void load_c(int lane, const OutMaps& om, int col, int row0, int bt) {
+    fence_proxy_async_smem();  // this warp's reads of the buffer precede the TMA write
+    __syncwarp();
+    if (lane == 0) {
+      uint64_t* bar = &cbar[kc & 1];
+      mbar_arrive_expect_tx(bar, kOutBoxD);
+      tma_load_3d_s(base_c + (kc & 1) * kOutBoxD, &om.c, bar, col, row0, bt);
+    }
+    ++kc;
+  }
+  // wait for C box `idx` (bounded) and return its shared address
+  __device__ __forceinline__ bool wait_c(int idx, volatile int* abort_flag, uint32_t& addr) const {
+    addr = base_c + (idx & 1) * kOutBoxD;
+    return mbar_wait(&cbar[idx & 1], (idx >> 1) & 1, abort_flag);
   }
 };
+
+// 8 bf16 of row `lane`, 16-byte chunk `chunk` of a 128-byte-swizzled [32 x 64] box
+__device__ __forceinline__ uint4 box_chunk(uint32_t box, int lane, int chunk) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(box + lane * 128 + ((chunk ^ (lane & 7)) << 4)));
+  return v;
+}
+
 struct Sched {
   int tiles_m, tiles_n, kblocks, kb_per_split, splits, total, M;
   int grouped;
@@ -147,7 +192,7 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x))
 template <int EPI>
 __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0,
                                             const uint32_t (&r)[32], const OutStage* st = nullptr,
-                                            int lane = 0, int h = 0) {
+                                            int lane = 0, int h = 0, uint32_t cbox = 0) {
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
@@ -216,7 +261,8 @@ __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0
             reinterpret_cast<const __nv_bfloat16*>(a.C) + static_cast<long>(row) * a.ldc + col0;
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
-          uint4 cv = ld_global_v4(c + i);
+          // C from the TMA-loaded box (columns h*32.. of it) or straight from global memory
+          uint4 cv = cbox ? box_chunk(cbox, lane, h * 4 + i / 8) : ld_global_v4(c + i);
           uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -297,7 +343,7 @@ __device__ __forceinline__ void epi_swiglu(const GemmArgs& a, int row, int col0,
 // gate columns 2*col0 + [0,32) and up columns 2*col0 + 32 + [0,32) of gu.
 __device__ __forceinline__ void epi_dswiglu(const GemmArgs& a, int row, int col0,
                                             const uint32_t (&r)[32], const OutStage* st = nullptr,
-                                            int lane = 0) {
+                                            int lane = 0, uint32_t cbox = 0) {
   const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(a.C) +
                             static_cast<long>(row) * a.ldc + 2 * col0;
   __nv_bfloat16* dgu =
@@ -305,8 +351,9 @@ __device__ __forceinline__ void epi_dswiglu(const GemmArgs& a, int row, int col0
   float g[32], u[32];
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
-    uint4 gv = ld_global_v4(gu + i);
-    uint4 uv = ld_global_v4(gu + 32 + i);
+    // gate columns are chunks 0-3 of the C box, up columns chunks 4-7
+    uint4 gv = cbox ? box_chunk(cbox, lane, i / 8) : ld_global_v4(gu + i);
+    uint4 uv = cbox ? box_chunk(cbox, lane, 4 + i / 8) : ld_global_v4(gu + 32 + i);
     uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
     uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
 #pragma unroll
@@ -354,13 +401,14 @@ struct PeerMaps {
 };
 
 // ---------------------------------------------------------------- kernel
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int LAY>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args,
                    const Sched sched, int* status, const __grid_constant__ PeerMaps pmA,
                    const __grid_constant__ OutMaps om) {
-  using Cfg = GemmCfg<BN>;
+  constexpr bool kBf16Out = LAY != kLayF32;
+  using Cfg = GemmCfg<BN, LAY>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = make_idesc_bf16(BM, BN, A_MN, B_MN);
 
@@ -372,7 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* cin_bar = drain_bar + 1;  // 4 epilogue warps x 2 C buffers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cin_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -388,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&cin_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -527,16 +577,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    constexpr bool kBf16Out = EPI != kEpiF32 && EPI != kEpiF32Atomic;
     const bool tma_out = kBf16Out && om.use != 0;
-    const OutStage ost{smem_u32(smem + Cfg::OFF_OUT + (warp - 2) * kOutBoxD),
-                       smem_u32(smem + Cfg::OFF_OUT + 4 * kOutBoxD + (warp - 2) * kOutBoxD2)};
+    const bool tma_c = LAY == kLayOutC && tma_out && om.use_c != 0;
+    const int ew = warp - 2;
+    OutStage ost;
+    ost.base_d = smem_u32(smem + Cfg::OFF_OUT + ew * 2 * kOutBoxD);
+    ost.base_d2 = smem_u32(smem + Cfg::OFF_OUT + kOffD2 + ew * 2 * kOutBoxD2);
+    ost.base_c = smem_u32(smem + Cfg::OFF_OUT + kOffC + ew * 2 * kOutBoxD);
+    ost.cbar = cin_bar + 2 * ew;
+    int c_done = 0;  // C boxes consumed
     int buf = 0;
     uint32_t acc_phase = 0;
+    // Epilogues that read a bf16 operand C (residual, or gu for dSwiGLU) pull this thread's
+    // C row segment of a tile into L2 one tile ahead, while the MMAs of that tile run, so
+    // the row-per-thread reads of C hit L2 instead of waiting on DRAM.
+    auto prefetch_c = [&](int tp) {
+      if constexpr (EPI == kEpiDSwiGLU || EPI == kEpiBf16 || EPI == kEpiGateResidual) {
+        if (args.C == nullptr || tp >= sched.total) return;
+        int pm0, pnt, pk0, pk1, pbt;
+        if (!sched.decode(tp, pm0, pnt, pk0, pk1, pbt)) return;
+        if (pm0 + row_in_tile >= args.M) return;
+        const long prow = (sched.grouped == 1 ? 0 : static_cast<long>(pbt) * args.M) + pm0 + row_in_tile;
+        const int c0 = (EPI == kEpiDSwiGLU ? 2 : 1) * pnt * BN;
+        const int ncols = min((EPI == kEpiDSwiGLU ? 2 : 1) * BN,
+                              (EPI == kEpiDSwiGLU ? 2 * args.N : args.N) - c0);
+        const char* base = reinterpret_cast<const char*>(args.C) + (prow * args.ldc + c0) * 2;
+        for (int off = 0; off < ncols * 2; off += 128)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+      }
+    };
+    prefetch_c(blockIdx.x);
     for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
       int m0, nt, kb0, kb1, bt;
       if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
       const int n0 = nt * BN;
+      prefetch_c(t + gridDim.x);
+      // TMA loads of this tile's C boxes (two in flight), issued before the accumulator
+      // is ready: DSwiGLU reads one 64-column gu box per 32 accumulator columns, the
+      // residual epilogues one box per 64 columns
+      const int box_row_c = m0 + quad * 32;
+      const int box_bt_c = sched.grouped == 1 ? 0 : bt;
+      constexpr int kCStep = EPI == kEpiDSwiGLU ? 32 : 64;  // accumulator columns per C box
+      const int n_cbox = tma_c ? (min(BN, args.N - n0) + kCStep - 1) / kCStep : 0;
+      const int c_first = ost.kc;
+      auto c_col = [&](int i) { return (EPI == kEpiDSwiGLU ? 2 : 1) * (n0 + i * kCStep); };
+      for (int i = 0; i < min(2, n_cbox); ++i) ost.load_c(lane, om, c_col(i), box_row_c, box_bt_c);
+      bool c_ok = true;
+      // wait for C box i of this tile; request box i + 2 once box i has been read
+      auto c_box = [&](int i, uint32_t& addr) {
+        if (!ost.wait_c(c_first + i, abort_flag, addr)) {
+          if (lane == 0) record_status(status, kStatusTimeoutEpilogue);
+          *abort_flag = 1;
+          c_ok = false;
+        }
+      };
+      auto c_release = [&](int i) {
+        ++c_done;
+        if (i + 2 < n_cbox) ost.load_c(lane, om, c_col(i + 2), box_row_c, box_bt_c);
+      };
       if (!mbar_wait(&acc_full[buf], acc_phase, abort_flag)) {
         if (lane == 0) record_status(status, kStatusTimeoutEpilogue);
         *abort_flag = 1;
@@ -576,22 +674,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n0 + c >= args.N) continue;
           if constexpr (EPI == kEpiDSwiGLU) {
             if (tma_out) {  // 32 activation-gradient columns -> one 64-column box of dgu
+              uint32_t cb = 0;
+              if (tma_c) c_box(c >> 5, cb);
+              if (!c_ok) break;
               ost.acquire(lane);
-              if (row_ok) epi_dswiglu(args, row, n0 + c, r, &ost, lane);
+              if (row_ok) epi_dswiglu(args, row, n0 + c, r, &ost, lane, cb);
+              if (tma_c) {
+                __syncwarp();
+                c_release(c >> 5);
+              }
               ost.flush(lane, om, 2 * (n0 + c), box_row, box_bt, false, 0);
             } else if (row_ok) {
               epi_dswiglu(args, row, n0 + c, r);
             }
           } else if (tma_out) {  // two 32-column chunks fill one 64-column box
             const int h = (c >> 5) & 1;
+            uint32_t cb = 0;
+            if (tma_c) {
+              c_box(c >> 6, cb);
+              if (!c_ok) break;
+            }
             if (h == 0) ost.acquire(lane);
-            if (row_ok) epi_chunk32<EPI>(args, row, n0 + c, r, &ost, lane, h);
-            if (h == 1 || n0 + c + 32 >= args.N) ost.flush(lane, om, n0 + c - 32 * h, box_row, box_bt, false, 0);
+            if (row_ok) epi_chunk32<EPI>(args, row, n0 + c, r, &ost, lane, h, cb);
+            const bool last = h == 1 || n0 + c + 32 >= args.N;
+            if (tma_c && last) {
+              __syncwarp();
+              c_release(c >> 6);
+            }
+            if (last) ost.flush(lane, om, n0 + c - 32 * h, box_row, box_bt, false, 0);
           } else if (row_ok) {
             epi_chunk32<EPI>(args, row, n0 + c, r);
           }
         }
       }
+      if (!c_ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -601,6 +717,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (tma_out && lane == 0) tma_store_wait_all();  // boxes read and stores complete
+    // C boxes requested but not consumed (an aborted tile) land before the CTA exits
+    for (int i = c_done; i < ost.kc; ++i) {
+      long long t0 = clock64();
+      while (!mbar_try_wait(&ost.cbar[i & 1], (i >> 1) & 1) && clock64() - t0 < kSpinLimitCycles / 8) {
+      }
+    }
   }
 
   tc_fence_before();
@@ -612,11 +734,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- host launch
-template <int BN, bool A_MN, bool B_MN, int EPI>
-void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
-  using Cfg = GemmCfg<BN>;
+template <int BN, bool A_MN, bool B_MN, int EPI, int LAY>
+void launch_lay(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
+  using Cfg = GemmCfg<BN, LAY>;
   static bool attr_set = false;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, LAY>;
   if (!attr_set) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     Cfg::SMEM_BYTES),
@@ -657,7 +779,7 @@ void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, in
     throw std::runtime_error("gemm: the reduce-scatter store needs the plain bf16 epilogue");
   OutMaps om;
   std::memset(&om, 0, sizeof(om));
-  constexpr bool kBf16Out = EPI != kEpiF32 && EPI != kEpiF32Atomic;
+  constexpr bool kBf16Out = LAY != kLayF32;
   auto aligned = [](const void* p, long ld) {
     return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ld % 8 == 0;
   };
@@ -671,10 +793,34 @@ void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, in
       om.d2 = make_tmap_3d(a.D2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N / 2, a.M, nbd, a.ldd2 * 2,
                            static_cast<uint64_t>(a.M) * a.ldd2 * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
     om.use = 1;
+    if (LAY == kLayOutC && (EPI == kEpiDSwiGLU || EPI == kEpiBf16 || EPI == kEpiGateResidual) &&
+        aligned(a.C, a.ldc)) {
+      om.c = make_tmap_3d(a.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dcols, a.M, nbd, a.ldc * 2,
+                          static_cast<uint64_t>(a.M) * a.ldc * 2, 64, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+      om.use_c = 1;
+    }
   }
   kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status, pm, om);
   count_launch();
   check_cuda(cudaGetLastError(), "gemm_tc_kernel launch");
+}
+
+// layout by epilogue: fp32 outputs need no boxes; SwiGLU (second output), dSwiGLU and
+// residual epilogues with a C operand take all boxes; other bf16 outputs the D boxes only
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
+  if constexpr (EPI == kEpiF32 || EPI == kEpiF32Atomic) {
+    launch_lay<BN, A_MN, B_MN, EPI, kLayF32>(a, s, grid, stream, status);
+  } else if constexpr (EPI == kEpiSwiGLU || EPI == kEpiDSwiGLU) {
+    launch_lay<BN, A_MN, B_MN, EPI, kLayOutC>(a, s, grid, stream, status);
+  } else if constexpr (EPI == kEpiBf16 || EPI == kEpiGateResidual) {
+    if (a.C != nullptr)
+      launch_lay<BN, A_MN, B_MN, EPI, kLayOutC>(a, s, grid, stream, status);
+    else
+      launch_lay<BN, A_MN, B_MN, EPI, kLayOut>(a, s, grid, stream, status);
+  } else {
+    launch_lay<BN, A_MN, B_MN, EPI, kLayOut>(a, s, grid, stream, status);
+  }
 }
 
 template <int BN>
