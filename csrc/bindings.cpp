@@ -1151,27 +1151,73 @@ ddb::EpOwnerArgs ep_owner_args(torch::Tensor peer_idx, torch::Tensor peer_w, tor
   return a;
 }
 
-void ep_owner_gather(torch::Tensor peer_idx, torch::Tensor peer_w, torch::Tensor peer_rows, int64_t world,
-                     int64_t rank, int64_t N, int64_t k, int64_t d, int64_t lo, int64_t El,
-                     torch::Tensor seg_start, torch::Tensor cursor, torch::Tensor meta, torch::Tensor meta_w,
-                     torch::Tensor n_uniq, torch::Tensor xr) {
+// Source push of token rows (h, or dout in gradient mode) into the owners' staging rows.
+void ep_push_rows(torch::Tensor idx, c10::optional<torch::Tensor> w, torch::Tensor rows,
+                  torch::Tensor stage_table, c10::optional<torch::Tensor> smeta_table,
+                  c10::optional<torch::Tensor> cnt, torch::Tensor pos, int64_t world, int64_t rank,
+                  int64_t El) {
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == torch::kInt32 && idx.dim() == 2 && idx.is_contiguous(), "idx");
+  check_bf16(rows, "rows");
+  check_rows(rows, "rows");
+  const int64_t N = idx.size(0), k = idx.size(1);
+  TORCH_CHECK(rows.size(0) == N, "rows / idx");
+  TORCH_CHECK(stage_table.scalar_type() == torch::kInt64 && stage_table.numel() == world, "stage table");
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && pos.is_contiguous() && pos.numel() == N * world, "pos [N, world]");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  ddb::EpPushArgs a;
+  a.world = world; a.rank = rank; a.N = N; a.k = k; a.d = rows.size(1); a.El = El;
+  a.idx = idx.data_ptr<int>();
+  a.rows = reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr());
+  a.ld_rows = rows.stride(0);
+  a.stage = reinterpret_cast<__nv_bfloat16* const*>(stage_table.data_ptr<int64_t>());
+  a.pos = pos.data_ptr<int>();
+  if (smeta_table) {
+    TORCH_CHECK(w && cnt, "forward push needs weights and the owner counters");
+    TORCH_CHECK(w->scalar_type() == torch::kFloat32 && w->is_contiguous() && w->numel() == N * k, "w");
+    TORCH_CHECK(cnt->scalar_type() == torch::kInt32 && cnt->numel() == world, "cnt");
+    TORCH_CHECK(smeta_table->scalar_type() == torch::kInt64 && smeta_table->numel() == world, "smeta table");
+    a.w = w->data_ptr<float>();
+    a.cnt = cnt->data_ptr<int>();
+    a.smeta = reinterpret_cast<int* const*>(smeta_table->data_ptr<int64_t>());
+  }
+  ddb::ep_push_rows(a, stream());
+}
+
+// Owner fan-out of the staged rows into the local expert segments.
+void ep_owner_fanout(int64_t stage_ptr, int64_t smeta_ptr, torch::Tensor prefix, int64_t total, int64_t world,
+                     int64_t N, int64_t k, int64_t d, int64_t lo, int64_t El, torch::Tensor seg_start,
+                     torch::Tensor cursor, torch::Tensor xr, torch::Tensor meta, torch::Tensor meta_w,
+                     torch::Tensor urow, torch::Tensor n_uniq) {
   check_bf16(xr, "xr");
   check_rows(xr, "xr");
   TORCH_CHECK(xr.size(1) == d, "xr width");
+  for (auto* t : {&prefix, &seg_start, &cursor, &meta, &urow, &n_uniq})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->is_contiguous(), "int32 EP state");
+  TORCH_CHECK(prefix.numel() == world + 1, "prefix [world + 1]");
+  TORCH_CHECK(meta.dim() == 2 && meta.size(1) == 2 + k && meta.size(0) >= total && meta_w.size(0) >= total &&
+                  urow.numel() >= total, "meta capacity");
   const c10::cuda::CUDAGuard guard(xr.device());
-  auto a = ep_owner_args(peer_idx, peer_w, peer_rows, world, rank, N, k, d, lo, El, seg_start, cursor, meta,
-                         meta_w, n_uniq);
-  TORCH_CHECK(a.cap >= world * N, "meta capacity below world * N");
+  ddb::EpFanoutArgs a;
+  a.world = world; a.N = N; a.k = k; a.d = d; a.lo = lo; a.El = El; a.total = total;
+  a.stage = reinterpret_cast<const __nv_bfloat16*>(stage_ptr);
+  a.smeta = reinterpret_cast<const int*>(smeta_ptr);
+  a.prefix = prefix.data_ptr<int>();
+  a.seg_start = seg_start.data_ptr<int>();
+  a.cursor = cursor.data_ptr<int>();
   a.xr = reinterpret_cast<__nv_bfloat16*>(xr.data_ptr());
   a.ld_xr = xr.stride(0);
-  ddb::ep_owner_gather(a, stream());
+  a.meta = meta.data_ptr<int>();
+  a.meta_w = meta_w.data_ptr<float>();
+  a.urow = urow.data_ptr<int>();
+  a.n_uniq = n_uniq.data_ptr<int>();
+  ddb::ep_owner_fanout(a, stream());
 }
 
 void ep_owner_grad_gather(torch::Tensor peer_idx, torch::Tensor peer_w, torch::Tensor peer_rows,
                           int64_t world, int64_t rank, int64_t N, int64_t k, int64_t d, int64_t lo, int64_t El,
                           torch::Tensor seg_start, torch::Tensor cursor, torch::Tensor meta,
                           torch::Tensor meta_w, torch::Tensor n_uniq, torch::Tensor y, torch::Tensor dy,
-                          torch::Tensor peer_dw) {
+                          torch::Tensor peer_dw, int64_t local_rows, c10::optional<torch::Tensor> urow) {
   check_bf16(y, "y");
   check_bf16(dy, "dy");
   check_rows(y, "y");
@@ -1180,6 +1226,11 @@ void ep_owner_grad_gather(torch::Tensor peer_idx, torch::Tensor peer_w, torch::T
   const c10::cuda::CUDAGuard guard(y.device());
   auto a = ep_owner_args(peer_idx, peer_w, peer_rows, world, rank, N, k, d, lo, El, seg_start, cursor, meta,
                          meta_w, n_uniq);
+  if (local_rows != 0) {  // dout rows pushed into this rank's staging buffer
+    TORCH_CHECK(urow && urow->scalar_type() == torch::kInt32 && urow->numel() >= meta.size(0), "urow");
+    a.local_rows = reinterpret_cast<const __nv_bfloat16*>(local_rows);
+    a.urow = urow->data_ptr<int>();
+  }
   ddb::ep_owner_grad_gather(a, reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
                             reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0),
                             reinterpret_cast<float* const*>(peer_dw.data_ptr<int64_t>()), stream());
@@ -1281,8 +1332,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_bwd", &layernorm_bwd, "LayerNorm backward -> dx (accumulates dw, db)");
   m.def("video_augment", &video_augment, "fused flip/brightness/contrast/normalise of clips");
   m.def("ep_copy_rows", &ep_copy_rows, "row-block copies between local and peer buffers (EP)");
-  m.def("ep_owner_gather", &ep_owner_gather, "EP dispatch: owner pulls each routed token row once");
-  m.def("ep_owner_grad_gather", &ep_owner_grad_gather, "EP backward dispatch: dy rows and routing-weight grads");
+  m.def("ep_owner_grad_gather", &ep_owner_grad_gather, "EP backward dispatch: dy rows and routing-weight grads",
+        py::arg("peer_idx"), py::arg("peer_w"), py::arg("peer_rows"), py::arg("world"), py::arg("rank"),
+        py::arg("N"), py::arg("k"), py::arg("d"), py::arg("lo"), py::arg("El"), py::arg("seg_start"),
+        py::arg("cursor"), py::arg("meta"), py::arg("meta_w"), py::arg("n_uniq"), py::arg("y"), py::arg("dy"),
+        py::arg("peer_dw"), py::arg("local_rows") = 0, py::arg("urow") = py::none());
+  m.def("ep_push_rows", &ep_push_rows, "EP dispatch: source pushes token rows to their owners' staging",
+        py::arg("idx"), py::arg("w"), py::arg("rows"), py::arg("stage_table"), py::arg("smeta_table"),
+        py::arg("cnt"), py::arg("pos"), py::arg("world"), py::arg("rank"), py::arg("El"));
+  m.def("ep_owner_fanout", &ep_owner_fanout, "EP dispatch: owner fans staged rows out to expert segments");
   m.def("ep_owner_scatter_sum", &ep_owner_scatter_sum, "EP combine: owner-side partial sums pushed to sources");
   m.def("ep_source_reduce", &ep_source_reduce, "EP source-side sum of owner partials (+ shared, residual)",
         py::arg("idx"), py::arg("ret"), py::arg("El"), py::arg("residual") = py::none(),

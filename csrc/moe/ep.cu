@@ -99,46 +99,6 @@ __device__ __forceinline__ void store_acc(__nv_bfloat16* row, int d, int lane, c
   }
 }
 
-// One warp per (source, token): does the token route to one of my experts? Then pull its
-// row once (P2P loads) and write it into each of my expert segments it routes to.
-__global__ void __launch_bounds__(256) ep_owner_gather_kernel(EpOwnerArgs a) {
-  const int lane = threadIdx.x & 31;
-  const long wi = blockIdx.x * 8L + (threadIdx.x >> 5);
-  if (wi >= static_cast<long>(a.world) * a.N) return;
-  const int s = static_cast<int>(wi / a.N), t = static_cast<int>(wi % a.N);
-  int e = -1;
-  float w = 0.f;
-  if (lane < a.k) {
-    e = a.peer_idx[s][static_cast<long>(t) * a.k + lane];
-    w = a.peer_w[s][static_cast<long>(t) * a.k + lane];
-  }
-  const bool mine = lane < a.k && e >= a.lo && e < a.lo + a.El;
-  const unsigned mask = __ballot_sync(kFull, mine);
-  if (mask == 0) return;
-  int slot = -1;
-  if (mine) slot = a.seg_start[e - a.lo] + atomicAdd(a.cursor + (e - a.lo), 1);
-  int u = 0;
-  if (lane == 0) u = atomicAdd(a.n_uniq, 1);
-  u = __shfl_sync(kFull, u, 0);
-  if (u >= a.cap) return;  // cap = world * N bounds every possible row
-  int* m = a.meta + static_cast<long>(u) * (2 + a.k);
-  if (lane == 0) {
-    m[0] = s;
-    m[1] = t;
-  }
-  if (lane < a.k) {
-    m[2 + lane] = slot;
-    a.meta_w[static_cast<long>(u) * a.k + lane] = mine ? w : 0.f;
-  }
-  uint4 v[kMaxChunks];
-  load_row(a.peer_rows[s] + static_cast<long>(t) * a.d, a.d, lane, v);
-  for (unsigned mm = mask; mm; mm &= mm - 1) {
-    const int j = __ffs(mm) - 1;
-    const int sl = __shfl_sync(kFull, slot, j);
-    store_row(a.xr + static_cast<long>(sl) * a.ld_xr, a.d, lane, v);
-  }
-}
-
 // One warp per unique row: z = sum_j w_j src[slot_j] -> the source's return buffer.
 __global__ void __launch_bounds__(256) ep_owner_scatter_sum_kernel(EpOwnerArgs a, const __nv_bfloat16* src,
                                                                    long ld_src, bool weighted,
@@ -169,7 +129,104 @@ __global__ void __launch_bounds__(256) ep_owner_scatter_sum_kernel(EpOwnerArgs a
   store_acc(peer_ret[s] + (static_cast<long>(a.rank) * a.N + t) * a.d, a.d, lane, acc);
 }
 
-// One warp per unique row: pull dout once; dy[slot_j] = w_j dout; dw_j = dout . y[slot_j]
+// Source push. One warp per token; owners of the token's experts found by lanes < k. Block
+// counters aggregate the positions so each owner counter takes one atomic per block.
+__global__ void __launch_bounds__(256) ep_push_rows_kernel(EpPushArgs a) {
+  __shared__ int s_cnt[32], s_base[32];
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const bool fwd = a.smeta != nullptr;
+  const bool live = t < a.N;
+  int e = -1, o = -1;
+  float w = 0.f;
+  if (live && lane < a.k) {
+    e = a.idx[static_cast<long>(t) * a.k + lane];
+    w = a.w ? a.w[static_cast<long>(t) * a.k + lane] : 0.f;
+    o = e / a.El;
+  }
+  // owner set of the token as a bitmask over ranks (every lane reaches the same collective)
+  bool routed = false;  // gradient mode: lane o's owner received this token
+  if (!fwd && live && lane < a.world) routed = a.pos[static_cast<long>(t) * a.world + lane] >= 0;
+  const unsigned owners = fwd ? __reduce_or_sync(kFull, o >= 0 ? (1u << o) : 0u) : __ballot_sync(kFull, routed);
+  int myp = -1;  // lane o: this token's position at owner o
+  if (fwd) {
+    if (threadIdx.x < 32) s_cnt[threadIdx.x] = 0;
+    __syncthreads();
+    if (live && lane < a.world && ((owners >> lane) & 1)) myp = atomicAdd(&s_cnt[lane], 1);
+    __syncthreads();
+    if (threadIdx.x < a.world) s_base[threadIdx.x] = s_cnt[threadIdx.x] ? atomicAdd(&a.cnt[threadIdx.x], s_cnt[threadIdx.x]) : 0;
+    __syncthreads();
+    if (myp >= 0) myp += s_base[lane];
+    if (live && lane < a.world) a.pos[static_cast<long>(t) * a.world + lane] = myp;
+  } else if (live && lane < a.world) {
+    myp = a.pos[static_cast<long>(t) * a.world + lane];
+  }
+  if (!live) return;
+  uint4 v[kMaxChunks];
+  load_row(a.rows + static_cast<long>(t) * a.ld_rows, a.d, lane, v);
+  for (unsigned mm = owners; mm; mm &= mm - 1) {
+    const int ow = __ffs(mm) - 1;
+    const long r = static_cast<long>(a.rank) * a.N + __shfl_sync(kFull, myp, ow);
+    store_row(a.stage[ow] + r * a.d, a.d, lane, v);
+    if (fwd) {
+      int* m = a.smeta[ow] + r * (1 + 2 * a.k);
+      if (lane == 0) m[0] = t;
+      if (lane < a.k) {
+        const bool here = o == ow;
+        m[1 + lane] = here ? e : -1;
+        m[1 + a.k + lane] = __float_as_int(here ? w : 0.f);
+      }
+    }
+  }
+}
+
+// Owner fan-out of the staged rows into the local experts' segments (local copies).
+__global__ void __launch_bounds__(256) ep_owner_fanout_kernel(EpFanoutArgs a) {
+  __shared__ int s_cnt[256], s_base[256];
+  const int lane = threadIdx.x & 31;
+  const int u = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const bool live = u < a.total;
+  for (int i = threadIdx.x; i < a.El; i += 256) s_cnt[i] = 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *a.n_uniq = a.total;
+  __syncthreads();
+  // source of u: the last s with prefix[s] <= u (prefix[0] = 0)
+  const bool le = live && lane < a.world && a.prefix[lane] <= u;
+  const unsigned lemask = __ballot_sync(kFull, le);
+  const int s = lemask ? 31 - __clz(lemask) : 0;
+  const long R = static_cast<long>(s) * a.N + (live ? u - a.prefix[s] : 0);
+  const int* rec = a.smeta + R * (1 + 2 * a.k);
+  int e = -1, loc = -1;
+  float w = 0.f;
+  if (live && lane < a.k) {
+    e = rec[1 + lane];
+    w = __int_as_float(rec[1 + a.k + lane]);
+    if (e >= 0) loc = atomicAdd(&s_cnt[e - a.lo], 1);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.El; i += 256)
+    s_base[i] = s_cnt[i] ? atomicAdd(&a.cursor[i], s_cnt[i]) : 0;
+  __syncthreads();
+  if (!live) return;
+  const int slot = e >= 0 ? a.seg_start[e - a.lo] + s_base[e - a.lo] + loc : -1;
+  int* m = a.meta + static_cast<long>(u) * (2 + a.k);
+  if (lane == 0) {
+    m[0] = s;
+    m[1] = rec[0];
+    a.urow[u] = static_cast<int>(R);
+  }
+  if (lane < a.k) {
+    m[2 + lane] = slot;
+    a.meta_w[static_cast<long>(u) * a.k + lane] = e >= 0 ? w : 0.f;
+  }
+  uint4 v[kMaxChunks];
+  load_row(a.stage + R * a.d, a.d, lane, v);
+  for (unsigned mm = __ballot_sync(kFull, slot >= 0); mm; mm &= mm - 1) {
+    const int j = __ffs(mm) - 1;
+    store_row(a.xr + static_cast<long>(__shfl_sync(kFull, slot, j)) * a.ld_xr, a.d, lane, v);
+  }
+}
+
+// One warp per unique row: read dout once; dy[slot_j] = w_j dout; dw_j = dout . y[slot_j]
 // stored into the source's dw buffer.
 __global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a, const __nv_bfloat16* y,
                                                                    long ld_y, __nv_bfloat16* dy, long ld_dy,
@@ -187,7 +244,9 @@ __global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a
   }
   const unsigned mask = __ballot_sync(kFull, lane < a.k && sl >= 0);
   uint4 g[kMaxChunks];
-  load_row(a.peer_rows[s] + static_cast<long>(t) * a.d, a.d, lane, g);
+  load_row(a.local_rows ? a.local_rows + static_cast<long>(a.urow[u]) * a.d
+                        : a.peer_rows[s] + static_cast<long>(t) * a.d,
+           a.d, lane, g);
   for (unsigned mm = mask; mm; mm &= mm - 1) {
     const int j = __ffs(mm) - 1;
     const int slj = __shfl_sync(kFull, sl, j);
@@ -284,13 +343,25 @@ void check_owner(const EpOwnerArgs& a) {
 }
 }  // namespace
 
-void ep_owner_gather(const EpOwnerArgs& a, cudaStream_t s) {
-  check_owner(a);
-  const long warps = static_cast<long>(a.world) * a.N;
-  if (warps == 0) return;
-  ep_owner_gather_kernel<<<static_cast<int>((warps + 7) / 8), 256, 0, s>>>(a);
+void ep_push_rows(const EpPushArgs& a, cudaStream_t s) {
+  if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
+  if (a.k > 32 || a.k < 1 || a.world > 32 || a.world < 1) throw std::runtime_error("ep: k <= 32, world <= 32");
+  if (a.N == 0) return;
+  ep_push_rows_kernel<<<(a.N + 7) / 8, 256, 0, s>>>(a);
   count_launch();
-  check_cuda(cudaGetLastError(), "ep_owner_gather launch");
+  check_cuda(cudaGetLastError(), "ep_push_rows launch");
+}
+
+void ep_owner_fanout(const EpFanoutArgs& a, cudaStream_t s) {
+  if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
+  if (a.k > 32 || a.world > 32 || a.El > 256) throw std::runtime_error("ep: k <= 32, world <= 32, El <= 256");
+  if (a.total <= 0) {
+    check_cuda(cudaMemsetAsync(a.n_uniq, 0, sizeof(int), s), "ep fanout n_uniq");
+    return;
+  }
+  ep_owner_fanout_kernel<<<(a.total + 7) / 8, 256, 0, s>>>(a);
+  count_launch();
+  check_cuda(cudaGetLastError(), "ep_owner_fanout launch");
 }
 
 void ep_owner_grad_gather(const EpOwnerArgs& a, const __nv_bfloat16* y, long ld_y, __nv_bfloat16* dy,

@@ -66,13 +66,13 @@ struct EpCopyArgs {
 };
 void ep_copy_rows(const EpCopyArgs& a, cudaStream_t stream);
 
-// ---- expert parallelism, owner-driven with one row per (token, owner rank)
-// Every rank exposes its routing (topk idx / weights), its FFN input rows h and, in
-// backward, its output gradient rows in peer-mapped buffers. The owner of experts
-// [lo, lo + El) reads every source's routing, pulls each source token that routes to
-// one of its experts ONCE and writes it to each of its local expert segments; after the
-// expert GEMMs it sums the token's local expert outputs (weighted) and stores that one
-// row into the source's return buffer. Sources add the rows of the owners they used.
+// ---- expert parallelism, one row per (token, owner rank) each way
+// Every source pushes each token row ONCE to every rank owning one of its experts
+// (ep_push_rows, P2P stores into the owner's staging rows); the owner of experts
+// [lo, lo + El) fans its staged rows out into its local expert segments (ep_owner_fanout);
+// after the expert GEMMs it sums the token's local expert outputs (weighted) and stores
+// that one row into the source's return buffer. Sources add the rows of the owners they
+// used. Backward pushes the output-gradient rows to the same staging positions.
 struct EpOwnerArgs {
   int world = 0, rank = 0, N = 0, k = 0, d = 0, lo = 0, El = 0;
   const int* const* peer_idx = nullptr;              // [world] -> [N, k] int32 routed expert ids
@@ -88,10 +88,52 @@ struct EpOwnerArgs {
   float* meta_w = nullptr;
   int* n_uniq = nullptr;
   int cap = 0;
+  // gradient gather from local staging rows (pushed by the sources) instead of peer rows:
+  // the dout row of unique row u is local_rows[urow[u]]
+  const __nv_bfloat16* local_rows = nullptr;
+  const int* urow = nullptr;
 };
-// forward dispatch: fills xr (owner layout), meta, meta_w, n_uniq
-void ep_owner_gather(const EpOwnerArgs& a, cudaStream_t s);
-// backward dispatch: per unique row pulls dout (peer_rows) once, writes dy[slot] = w dout and
+
+// Source-side push of token rows to their expert owners (P2P stores). Forward mode
+// (smeta != nullptr): each token's row goes once to every rank owning one of its experts,
+// into that owner's staging rows [rank * N + p] (p = the token's position among this
+// rank's tokens for that owner, from cnt[o]), with a record (t, expert ids on that owner or
+// -1, weights) in the owner's staging metadata; pos[t * world + o] = p or -1. Gradient
+// mode (smeta == nullptr): the rows go to the same staging positions, read from pos.
+struct EpPushArgs {
+  int world = 0, rank = 0, N = 0, k = 0, d = 0, El = 0;
+  const int* idx = nullptr;            // [N, k]
+  const float* w = nullptr;            // [N, k]
+  const __nv_bfloat16* rows = nullptr; // [N, d] (h, or dout)
+  long ld_rows = 0;
+  __nv_bfloat16* const* stage = nullptr;  // [world] -> [world * N, d] staging rows
+  int* const* smeta = nullptr;            // [world] -> [world * N, 1 + 2k] records
+  int* cnt = nullptr;                     // [world] zeroed: rows pushed to each owner
+  int* pos = nullptr;                     // [N, world]
+};
+void ep_push_rows(const EpPushArgs& a, cudaStream_t s);
+
+// Owner side after the pushes landed: staged rows u in [0, total) (sources in order, row
+// u of source s at stage[s * N + u - prefix[s]]) fan out into the local experts' segments
+// of xr; meta [total, 2 + k] = (source, token, slot per route or -1), meta_w [total, k],
+// *n_uniq = total, urow[u] = staging row.
+struct EpFanoutArgs {
+  int world = 0, N = 0, k = 0, d = 0, lo = 0, El = 0, total = 0;
+  const __nv_bfloat16* stage = nullptr;
+  const int* smeta = nullptr;
+  const int* prefix = nullptr;  // [world + 1]
+  const int* seg_start = nullptr;
+  int* cursor = nullptr;
+  __nv_bfloat16* xr = nullptr;
+  long ld_xr = 0;
+  int* meta = nullptr;
+  float* meta_w = nullptr;
+  int* urow = nullptr;
+  int* n_uniq = nullptr;
+};
+void ep_owner_fanout(const EpFanoutArgs& a, cudaStream_t s);
+// backward dispatch: per unique row reads dout once (local staging row urow[u], or the
+// source's peer_rows), writes dy[slot] = w dout and
 // stores dw = dout . y[slot] into the source's dw buffer (peer_dw[s][t * k + j])
 void ep_owner_grad_gather(const EpOwnerArgs& a, const __nv_bfloat16* y, long ld_y, __nv_bfloat16* dy,
                           long ld_dy, float* const* peer_dw, cudaStream_t s);
