@@ -240,7 +240,7 @@ def bench_ep(iters: int = 5, d: int = 1024, E: int = 64, k: int = 6, F: int = 51
         for (a, ea), (b, eb) in zip(tr[:-1], tr[1:]):
             if a.split(".")[0] == b.split(".")[0]:
                 stages.setdefault(b, []).append(ea.elapsed_time(eb))
-    # rows this rank pulled from peers in the last forward (NVLink inbound), and pushed out
+    # rows peers pushed to this rank in the last forward (NVLink inbound); as many go back
     meta = sv.get("owner")[9] if transport == "fused" else None
     remote_rows = 0
     if meta is not None:
@@ -260,7 +260,8 @@ def bench_ep(iters: int = 5, d: int = 1024, E: int = 64, k: int = 6, F: int = 51
         if transport == "fused":
             mb = rr.item() * d * 2 / 1e6
             res["nvlink_mb_per_phase"] = round(mb, 1)
-            for st in ("fwd.gather", "fwd.scatter", "bwd.gather", "bwd.scatter"):
+            # P2P-store phases: row pushes to the owners, partial sums back to the sources
+            for st in ("fwd.push", "fwd.scatter", "bwd.push", "bwd.scatter"):
                 ms = res["stage_ms_max_over_ranks"].get(st)
                 if ms:
                     gbs = mb / ms

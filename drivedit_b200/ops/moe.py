@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
 import torch
 
 from ._ext import ext
@@ -233,24 +234,12 @@ def _mark(stage: str):
         EP_TRACE.append((stage, ev))
 
 
-def _expose(ep, idx, w, h) -> bool:
-    """Copy this rank's routing and rows into its peer-readable buffers when they are
-    large enough (every rank decides alike: equal token counts, buffers grown together)."""
-    N, k = idx.shape
-    d = h.shape[1]
-    rb, hb = ep._sym.get("route"), ep._sym.get("rows")
-    if rb is None or hb is None or rb.nbytes < N * k * 8 or hb.nbytes < N * d * 2:
-        return False
-    rb.tensor(N * k, torch.int32).view(N, k).copy_(idx)
-    rb.tensor(N * k, torch.float32, N * k * 4).view(N, k).copy_(w)
-    hb.tensor(N * d, torch.bfloat16).view(N, d).copy_(h)
-    return True
-
-
 def _ep_forward_fused(h, residual, moe, W):
-    """route -> routing and rows exposed in peer memory -> count table (one host sync) ->
-    every owner pulls each source token routed to its experts once, fanned out into its
-    expert segments (``ep_owner_gather``) -> local experts' grouped GEMMs -> per-token
+    """route -> every source pushes each token row once to every rank owning one of its
+    experts (``ep_push_rows``: P2P stores into the owner's staging rows, with the token's
+    routing for that owner) -> count table (one barrier and host sync; the pushes have
+    landed) -> each owner fans its staged rows out into its expert segments
+    (``ep_owner_fanout``, local copies) -> local experts' grouped GEMMs -> per-token
     partial sums over the owner's experts stored into the sources' return buffers
     (``ep_owner_scatter_sum``; the shared experts' GEMMs run meanwhile) -> barrier ->
     ``ep_source_reduce``: residual + the owners' partials + gated shared experts."""
@@ -259,33 +248,38 @@ def _ep_forward_fused(h, residual, moe, W):
     ep = moe.ep
     N, d = h.shape
     E, k, ns, Fh = moe.num_experts, moe.top_k, moe.num_shared_experts, moe.expert_dim
+    Wd = ep.world
     El = ep.local_experts
     lo = ep.rank * El
+    cap = Wd * N
     _mark("fwd.start")
     idx, w, sw, probs, counts, psum = _route(h, moe, W)
     _mark("fwd.route")
-    fast = _expose(ep, idx, w, h)
-    table = ep.exchange_counts(counts)            # barrier: counts, routing and rows visible
+    stage = ep.sym("stage", cap * d * 2)
+    smeta = ep.sym("smeta", cap * (1 + 2 * k) * 4)
+    ocnt = torch.zeros(Wd, device=h.device, dtype=torch.int32)
+    pos = torch.empty(N, Wd, device=h.device, dtype=torch.int32)
+    ext().ep_push_rows(idx, w, h, stage.table, smeta.table, ocnt, pos, Wd, ep.rank, El)
+    _mark("fwd.push")
+    full = ep.exchange_counts(torch.cat([counts.to(torch.int32), ocnt]))  # barrier: pushes landed
+    table = full[:, :E]
     _mark("fwd.counts")
     if not (table.sum(1) == N * k).all():
         raise RuntimeError("expert parallelism needs the same number of tokens on every rank")
-    if not fast:                                  # first use / growth: every rank alike
-        ep.sym("route", N * k * 8)
-        ep.sym("rows", N * d * 2)
-        _expose(ep, idx, w, h)
-        ep.barrier()
     plan = EpPlan(ep, table)
     rp, tables_r = _owner_plan(ep, plan, N, h.device)
-    cap = ep.world * N
-    meta = torch.empty(cap, 2 + k, device=h.device, dtype=torch.int32)
-    meta_w = torch.empty(cap, k, device=h.device, dtype=torch.float32)
+    uniq = full[:, E + ep.rank]                   # rows each source pushed to me
+    prefix_h = np.concatenate([[0], np.cumsum(uniq)]).astype(np.int32)
+    total = int(prefix_h[-1])
+    prefix = torch.from_numpy(prefix_h).to(h.device, non_blocking=True)
+    meta = torch.empty(max(total, 1), 2 + k, device=h.device, dtype=torch.int32)
+    meta_w = torch.empty(max(total, 1), k, device=h.device, dtype=torch.float32)
+    urow = torch.empty(max(total, 1), device=h.device, dtype=torch.int32)
     n_uniq = torch.zeros(1, device=h.device, dtype=torch.int32)
     xr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
-    rt, ht = ep._sym["route"], ep._sym["rows"]
-    base = (rt.table, ep.slot_table("route", 1, N * k * 4), ht.table, ep.world, ep.rank, N, k, d, lo, El,
-            rp[0], rp[7], meta, meta_w, n_uniq)
     _mark("fwd.plan")
-    ext().ep_owner_gather(*base, xr)
+    ext().ep_owner_fanout(stage.ptr, smeta.ptr, prefix, total, Wd, N, k, d, lo, El, rp[0], rp[7], xr, meta,
+                          meta_w, urow, n_uniq)
     _mark("fwd.gather")
     gu_r = act_r = None
     y_r = xr
@@ -294,6 +288,9 @@ def _ep_forward_fused(h, residual, moe, W):
         gu_r, act_r, y_r = _grouped_ffn(xr, W(moe.w13), W(moe.w2), tables_r, Fh)
     _mark("fwd.experts")
     ret = ep.sym("ret", cap * d * 2)
+    # owner-side arguments (the three peer tables are unused by these kernels)
+    base = (stage.table, stage.table, stage.table, Wd, ep.rank, N, k, d, lo, El, rp[0], rp[7], meta, meta_w,
+            n_uniq)
     ext().ep_owner_scatter_sum(*base, y_r, True, ret.table)
     _mark("fwd.scatter")
     slot_s, xs, gu_s, act_s, y_s, tables_s = _shared_forward(h, moe, W, ep)
@@ -306,34 +303,36 @@ def _ep_forward_fused(h, residual, moe, W):
     f, aux = _finish_forward(moe, ep, counts, psum, table, N)
     saved = dict(h=h, idx=idx, w=w, sw=sw, probs=probs, f=f, plan=plan, owner=base[3:], rp=rp,
                  tables_r=tables_r, xr=xr, gu_r=gu_r, act_r=act_r, y_r=y_r, slot_s=slot_s, xs=xs,
-                 gu_s=gu_s, act_s=act_s, y_s=y_s, tables_s=tables_s)
+                 gu_s=gu_s, act_s=act_s, y_s=y_s, tables_s=tables_s, pos=pos, urow=urow)
     return out, aux, saved
 
 
 def _ep_backward_fused(dout, d_aux, moe, W, sv):
-    """dout exposed in peer memory -> barrier -> owners pull each (token, owner) dout row
-    once, write ``dy = w dout`` into their segments and store ``dw = dout . y`` into the
-    source (``ep_owner_grad_gather``) -> local experts' backward GEMMs -> per-token sums
-    of ``dx`` over the owner's experts pushed back -> barrier -> sources add them up."""
+    """every source pushes its dout rows to the owners' staging rows of the forward
+    (``ep_push_rows`` in gradient mode) -> barrier -> each owner reads them locally, writes
+    ``dy = w dout`` into its segments and stores ``dw = dout . y`` into the source
+    (``ep_owner_grad_gather``) -> local experts' backward GEMMs -> per-token sums of ``dx``
+    over the owner's experts pushed back -> barrier -> sources add them up."""
     ep = moe.ep
     h = sv["h"]
     N, d = h.shape
     k, ns, Fh = moe.top_k, moe.num_shared_experts, moe.expert_dim
     El = ep.local_experts
     plan = sv["plan"]
-    cap = ep.world * N
+    Wd = ep.world
+    cap = Wd * N
     _mark("bwd.start")
-    drows = ep.sym("drows", N * d * 2)
-    drows.tensor(N * d, torch.bfloat16).view(N, d).copy_(dout)
+    dstage = ep.sym("dstage", cap * d * 2)
+    ext().ep_push_rows(sv["idx"], None, dout, dstage.table, None, None, sv["pos"], Wd, ep.rank, El)
+    _mark("bwd.push")
     dwb = ep.sym("dw", N * k * 4)
     dws, dxs = _shared_backward(dout, moe, W, sv)
     _mark("bwd.shared")
-    ep.barrier()                                  # every rank's dout rows are visible
+    ep.barrier()                                  # every rank's dout rows have landed
     _mark("bwd.barrier1")
-    rt = ep._sym["route"]
-    owner = (rt.table, ep.slot_table("route", 1, N * k * 4), drows.table) + sv["owner"]
+    owner = (dstage.table, dstage.table, dstage.table) + sv["owner"]
     dyr = torch.empty(max(plan.owner_rows, 1), d, device=h.device, dtype=torch.bfloat16)
-    ext().ep_owner_grad_gather(*owner, sv["y_r"], dyr, dwb.table)
+    ext().ep_owner_grad_gather(*owner, sv["y_r"], dyr, dwb.table, local_rows=dstage.ptr, urow=sv["urow"])
     _mark("bwd.gather")
     dxr = dyr
     if plan.owner_rows:

@@ -14,13 +14,14 @@ moves.
 Transports:
 
 ``fused`` (CUDA)
-    Rows move through NVLink peer memory with ``ep_copy_rows`` (``csrc/moe/ep.cu``): the
-    owner *pulls* the rows routed to its experts out of every source's symmetric send
-    buffer (P2P loads) straight into its grouped-GEMM layout, and *pushes* the expert
-    outputs into each source's symmetric return buffer (P2P stores); backward pulls
-    ``dy`` the same way and pushes ``dx``. Bounded cross-rank flag barriers order the
-    phases; the count table itself travels by P2P stores. No NCCL call carries token
-    payload.
+    Rows move through NVLink peer memory from inside our kernels (``csrc/moe/ep.cu``): each
+    source *pushes* every token row once to every rank owning one of its experts (P2P
+    stores into the owner's symmetric staging rows, with the token's routing for that
+    owner), the owner fans the staged rows out into its grouped-GEMM layout with local
+    copies, and *pushes* per-token partial sums of its expert outputs into each source's
+    symmetric return buffer (P2P stores); backward pushes ``dout`` to the same staging rows
+    and ``dx`` partial sums back. Bounded cross-rank flag barriers order the phases; the
+    count table itself travels by P2P stores. No NCCL call carries token payload.
 ``nccl``
     ``all_to_all_single`` of the compact rows plus a local ``ep_copy_rows`` into the
     grouped-GEMM layout (the baseline); on CPU the PyTorch path below runs over gloo.
@@ -114,8 +115,9 @@ class ExpertParallel:
 
     # ------------------------------------------------------------------ count table
     def exchange_counts(self, counts: torch.Tensor) -> np.ndarray:
-        """``counts [E]`` of this rank -> the ``[W, E]`` table of all ranks, on the host."""
-        E = self.num_experts
+        """``counts [n]`` of this rank (per-expert counts, optionally followed by more
+        per-rank integers) -> the ``[W, n]`` table of all ranks, on the host."""
+        E = counts.numel()
         if self.transport == "fused":
             from ..ops._ext import ext
 
