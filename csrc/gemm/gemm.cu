@@ -887,23 +887,27 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
     const long kb = (kblocks + sp - 1) / sp;
     return static_cast<double>(waves) * bn_c * kb / (bn_c == 256 ? 1.0 : 0.8);
   };
+  // split K (fp32-accumulating epilogue only) while it strictly shortens the estimate
+  auto best_splits = [&](int bn_c) {
+    int sp = 1;
+    if (epi == kEpiF32Atomic) {
+      if (a.splits > 0) return a.splits;
+      while (kblocks / (sp * 2) >= 8 && est(bn_c, sp * 2) < est(bn_c, sp)) sp *= 2;
+    }
+    return sp;
+  };
   int bn = a.bn;
-  if (bn == 0) {
+  if (bn == 0) {  // tile width and split-K chosen together
     bn = 128;
-    if (a.N >= 256 && !(a.N % 256 != 0 && a.N < 512) && est(256, 1) <= est(128, 1)) bn = 256;
+    if (a.N >= 256 && !(a.N % 256 != 0 && a.N < 512) &&
+        est(256, best_splits(256)) <= est(128, best_splits(128)))
+      bn = 256;
   }
   Sched s;
   s.tiles_m = static_cast<int>(tiles_m);
   s.tiles_n = (a.N + bn - 1) / bn;
   s.kblocks = kblocks;
-  int splits = 1;
-  if (epi == kEpiF32Atomic) {
-    splits = a.splits;
-    if (splits <= 0) {  // split K only while it strictly shortens the estimate
-      splits = 1;
-      while (s.kblocks / (splits * 2) >= 8 && est(bn, splits * 2) < est(bn, splits)) splits *= 2;
-    }
-  }
+  const int splits = best_splits(bn);
   s.kb_per_split = (s.kblocks + splits - 1) / splits;
   s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
   s.M = a.M;
