@@ -359,10 +359,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             p[c] = __uint_as_float(rs[c]);
             ds[c] = __uint_as_float(rp[c]);
           }
-        } else {
+        } else if (__all_sync(0xffffffffu, half_on && q0 + c0 >= qmin)) {
+          // every query of the chunk sees every key of the warp: no per-element mask;
+          // dS = P * (scale * dP - scale * delta) as one FFMA and one FMUL
 #pragma unroll
           for (int c4 = 0; c4 < 32; c4 += 4) {
             // lse / delta of 4 queries as broadcast 16-byte loads
+            const float4 l4 = *reinterpret_cast<const float4*>(s_lse + c0 + c4);
+            const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c0 + c4);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+            const float nsd[4] = {-a.scale * d4.x, -a.scale * d4.y, -a.scale * d4.z, -a.scale * d4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = c4 + e;
+              const float pv = exp2f(__uint_as_float(rs[c]) * sl2 - lv[e]);
+              p[c] = pv;
+              ds[c] = pv * fmaf(a.scale, __uint_as_float(rp[c]), nsd[e]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c4 = 0; c4 < 32; c4 += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(s_lse + c0 + c4);
             const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c0 + c4);
             const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};

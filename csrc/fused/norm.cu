@@ -95,6 +95,11 @@ __global__ void __launch_bounds__(256) adaln_bwd_kernel(
     const __nv_bfloat16* gr = dh + static_cast<long>(row) * D;
     float n[VEC][8], dn[VEC][8];
     float dot = 0.f;
+    // the residual gradient is loaded with x and dh so a row costs one memory round trip
+    const __nv_bfloat16* rr = dres ? dres + static_cast<long>(row) * D : nullptr;
+    uint4 ures[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) ures[i] = rr ? ld_global_v4(rr + (i * 32 + lane) * 8) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 8;
@@ -138,7 +143,6 @@ __global__ void __launch_bounds__(256) adaln_bwd_kernel(
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
     dot /= D;
     __nv_bfloat16* dxr = dx + static_cast<long>(row) * D;
-    const __nv_bfloat16* rr = dres ? dres + static_cast<long>(row) * D : nullptr;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 8;
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__(256) adaln_bwd_kernel(
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = r * (dn[i][j] - n[i][j] * dot);
       if (rr) {
-        uint4 u = ld_global_v4(rr + c);
+        const uint4 u = ures[i];
         uint32_t wr[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
