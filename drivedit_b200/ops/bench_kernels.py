@@ -153,6 +153,34 @@ def _print_trace(name, t, roles):
     print(json.dumps({"trace": name, "cycles_from_first_event": out}), flush=True)
 
 
+def bench_sla_linear(iters: int = 10, B: int = 4, H: int = 12, T: int = 8192):
+    """The four per-block kernels of the SLA linear branch at the DiT-B shape (state and
+    state gradients random; the batched GEMM between them is not timed here)."""
+    from ._ext import ext
+
+    d = H * 64
+    nb = T // 64
+    qkv = (torch.randn(B * T, 3 * d, device="cuda") * 0.5).bfloat16()
+    kvz = torch.empty(B * H * nb * 4160, device="cuda", dtype=torch.bfloat16)
+    state = torch.rand(B * H * nb, 4160, device="cuda") + 0.1
+    o = torch.empty(B * T, d, device="cuda", dtype=torch.bfloat16)
+    den = torch.empty(B * H * T, device="cuda")
+    do = torch.randn(B * T, d, device="cuda").bfloat16()
+    dsz = torch.empty(B * H * nb * 4160, device="cuda", dtype=torch.bfloat16)
+    dqkv = torch.zeros(B * T, 3 * d, device="cuda", dtype=torch.bfloat16)
+    dkvz = torch.randn(B * H * nb, 4160, device="cuda") * 0.01
+    runs = {
+        "sla_kv_state": lambda: ext().sla_kv_state(qkv, kvz, B, T, H),
+        "sla_lin_out": lambda: ext().sla_lin_out(qkv, state, o, den, B, T, H, 1e-6),
+        "sla_lin_bwd_q": lambda: ext().sla_lin_bwd_q(qkv, state, o, do, den, dsz, dqkv, B, T, H),
+        "sla_lin_bwd_kv": lambda: ext().sla_lin_bwd_kv(qkv, dkvz, dqkv, B, T, H),
+    }
+    for name, fn in runs.items():
+        fn()
+        ms = _timeit(fn, iters)
+        print(json.dumps({"kernel": name, "B": B, "H": H, "T": T, "ms": round(ms, 4)}), flush=True)
+
+
 def bench_conv3d(iters: int = 10):
     """VAE causal 3x3x3 convolutions at 8 frames of 256x512 RGB (encoder level 0,
     128 ch, and level 2, 512 ch at 65x129), stride-2 downsample, vs cuDNN."""
@@ -342,6 +370,8 @@ def main():
             bench_attn(args.iters, B=args.B, trace=args.trace)
         elif w == "attn_nodq":  # timing experiment: backward without the dQ reductions
             bench_attn(args.iters, dbg=1)
+        elif w == "sla":
+            bench_sla_linear(args.iters, B=args.B if args.B != 8 else 4)
         elif w == "gemm":
             bench_gemm(args.iters, args.shape)
         elif w == "ep":
