@@ -404,22 +404,25 @@ __global__ void __launch_bounds__(kThreads) sla_lin_bwd_q_tc(
   }
   const int r = threadIdx.x, blk = r >> 6, dd = r & 63;
   // dz_j[d] = sum_t phi(q)[t][d] dden[t] for block blk, feature dd (fp32 over bf16 phi)
-  float dz = 0.f;
+  // this token's q and dq rows for the epilogue, in flight while the MMAs run
+  __nv_bfloat16* qrow = dqkv + (row0 + r) * lddq + h * D;
+  uint4 qall[8], call[8];
+  load_row64(qall, qkv + (row0 + r) * ld + h * D);
+  load_row64(call, qrow);
+  float dzp[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains over t
+#pragma unroll 8
   for (int t = 0; t < 64; ++t) {
     const uint4 u = tile_get(tQ + blk * TILE, t, dd >> 3);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
     const float2 f = unpack_bf16(w[(dd & 7) >> 1]);
-    dz += ((dd & 1) ? f.y : f.x) * dds[blk * 64 + t];
+    dzp[t & 3] += ((dd & 1) ? f.y : f.x) * dds[blk * 64 + t];
   }
+  const float dz = (dzp[0] + dzp[1]) + (dzp[2] + dzp[3]);
   if (wait_mma(c, status)) {
     uint32_t v[64];
     tmem_row64(c.tmem, v);  // (a): row r = token r, column d
     {
-      __nv_bfloat16* qrow = dqkv + (row0 + r) * lddq + h * D;
       const float ddn = dds[r];
-      uint4 qall[8], call[8];
-      load_row64(qall, qkv + (row0 + r) * ld + h * D);
-      load_row64(call, qrow);
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         const uint4 qv = qall[c8], cv = call[c8];
@@ -506,13 +509,14 @@ __global__ void __launch_bounds__(kThreads) sla_lin_bwd_kv_tc(const __nv_bfloat1
     mma_commit(c.bar);
   }
   const int r = threadIdx.x, blk = r >> 6;
+  // this token's k and dk rows for the epilogue, in flight while the MMAs run
+  __nv_bfloat16* krow = dqkv + (row0 + r) * lddq + dm + h * D;
+  uint4 kall[8], call[8];
+  load_row64(kall, qkv + (row0 + r) * ld + dm + h * D);
+  load_row64(call, krow);
   if (wait_mma(c, status)) {
     uint32_t v[64];
     tmem_row64(c.tmem, v);
-    __nv_bfloat16* krow = dqkv + (row0 + r) * lddq + dm + h * D;
-    uint4 kall[8], call[8];
-    load_row64(kall, qkv + (row0 + r) * ld + dm + h * D);
-    load_row64(call, krow);
 #pragma unroll
     for (int c8 = 0; c8 < 8; ++c8) {
       const uint4 kv = kall[c8], cv = call[c8];
