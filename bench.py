@@ -230,7 +230,7 @@ def run_ours(args, ws, rank, local):
                          + "; AdamW state sharded") if ws > 1 else None,
             "expert_parallel": None if trainer.ep is None else (
                 f"{cfg.model.moe.num_experts // ws} routed experts per rank; token rows "
-                + ("pulled/pushed over NVLink peer memory by the EP copy kernel"
+                + ("pushed once per owner over NVLink peer memory (P2P stores) by the EP kernels"
                    if trainer.ep.transport == "fused" else "exchanged by NCCL all_to_all")),
             "l2": "256 MiB buffer overwritten before every timed step",
         },
