@@ -16,6 +16,7 @@
 
 #include <algorithm>
 #include <stdexcept>
+#include <type_traits>
 
 #include "../common/ptx.cuh"
 #include "../common/tma.h"
@@ -53,28 +54,34 @@ __global__ void __launch_bounds__(256) ep_copy_rows_kernel(EpCopyArgs a) {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMaxChunks = 8;  // rows of up to 8 x 256 bf16 = 2048 columns
 
+// Row helpers and kernels are instantiated for C 256-column chunks per row (C = 4 for
+// d <= 1024, else 8): the per-lane row buffers and fp32 accumulators take C x 8 registers,
+// so narrow rows keep more warps resident.
 // Load one bf16 row (d columns, d % 8 == 0, d <= 2048) into registers: lane holds chunks
 // i * 256 + lane * 8 .. + 8.
-__device__ __forceinline__ void load_row(const __nv_bfloat16* row, int d, int lane, uint4 (&v)[kMaxChunks]) {
+template <int C>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* row, int d, int lane, uint4 (&v)[C]) {
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
+  for (int i = 0; i < C; ++i) {
     const int c = i * 256 + lane * 8;
     if (c < d) v[i] = ld_global_v4(row + c);
   }
 }
 
-__device__ __forceinline__ void store_row(__nv_bfloat16* row, int d, int lane, const uint4 (&v)[kMaxChunks]) {
+template <int C>
+__device__ __forceinline__ void store_row(__nv_bfloat16* row, int d, int lane, const uint4 (&v)[C]) {
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
+  for (int i = 0; i < C; ++i) {
     const int c = i * 256 + lane * 8;
     if (c < d) st_global_v4(row + c, v[i].x, v[i].y, v[i].z, v[i].w);
   }
 }
 
-__device__ __forceinline__ void axpy_row(float (&acc)[kMaxChunks][8], float w, const __nv_bfloat16* row, int d,
+template <int C>
+__device__ __forceinline__ void axpy_row(float (&acc)[C][8], float w, const __nv_bfloat16* row, int d,
                                          int lane) {
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
+  for (int i = 0; i < C; ++i) {
     const int c = i * 256 + lane * 8;
     if (c < d) {
       const uint4 y = ld_global_v4(row + c);
@@ -89,9 +96,10 @@ __device__ __forceinline__ void axpy_row(float (&acc)[kMaxChunks][8], float w, c
   }
 }
 
-__device__ __forceinline__ void store_acc(__nv_bfloat16* row, int d, int lane, const float (&acc)[kMaxChunks][8]) {
+template <int C>
+__device__ __forceinline__ void store_acc(__nv_bfloat16* row, int d, int lane, const float (&acc)[C][8]) {
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
+  for (int i = 0; i < C; ++i) {
     const int c = i * 256 + lane * 8;
     if (c < d)
       st_global_v4(row + c, pack_bf16(acc[i][0], acc[i][1]), pack_bf16(acc[i][2], acc[i][3]),
@@ -100,6 +108,7 @@ __device__ __forceinline__ void store_acc(__nv_bfloat16* row, int d, int lane, c
 }
 
 // One warp per unique row: z = sum_j w_j src[slot_j] -> the source's return buffer.
+template <int C>
 __global__ void __launch_bounds__(256) ep_owner_scatter_sum_kernel(EpOwnerArgs a, const __nv_bfloat16* src,
                                                                    long ld_src, bool weighted,
                                                                    __nv_bfloat16* const* peer_ret) {
@@ -115,9 +124,9 @@ __global__ void __launch_bounds__(256) ep_owner_scatter_sum_kernel(EpOwnerArgs a
     wj = weighted ? a.meta_w[u * a.k + lane] : 1.f;
   }
   const unsigned mask = __ballot_sync(kFull, lane < a.k && sl >= 0);
-  float acc[kMaxChunks][8];
+  float acc[C][8];
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i)
+  for (int i = 0; i < C; ++i)
 #pragma unroll
     for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
   for (unsigned mm = mask; mm; mm &= mm - 1) {
@@ -131,6 +140,7 @@ __global__ void __launch_bounds__(256) ep_owner_scatter_sum_kernel(EpOwnerArgs a
 
 // Source push. One warp per token; owners of the token's experts found by lanes < k. Block
 // counters aggregate the positions so each owner counter takes one atomic per block.
+template <int C>
 __global__ void __launch_bounds__(256) ep_push_rows_kernel(EpPushArgs a) {
   __shared__ int s_cnt[32], s_base[32];
   const int lane = threadIdx.x & 31;
@@ -162,7 +172,7 @@ __global__ void __launch_bounds__(256) ep_push_rows_kernel(EpPushArgs a) {
     myp = a.pos[static_cast<long>(t) * a.world + lane];
   }
   if (!live) return;
-  uint4 v[kMaxChunks];
+  uint4 v[C];
   load_row(a.rows + static_cast<long>(t) * a.ld_rows, a.d, lane, v);
   for (unsigned mm = owners; mm; mm &= mm - 1) {
     const int ow = __ffs(mm) - 1;
@@ -181,6 +191,7 @@ __global__ void __launch_bounds__(256) ep_push_rows_kernel(EpPushArgs a) {
 }
 
 // Owner fan-out of the staged rows into the local experts' segments (local copies).
+template <int C>
 __global__ void __launch_bounds__(256) ep_owner_fanout_kernel(EpFanoutArgs a) {
   __shared__ int s_cnt[256], s_base[256];
   const int lane = threadIdx.x & 31;
@@ -218,7 +229,7 @@ __global__ void __launch_bounds__(256) ep_owner_fanout_kernel(EpFanoutArgs a) {
     m[2 + lane] = slot;
     a.meta_w[static_cast<long>(u) * a.k + lane] = e >= 0 ? w : 0.f;
   }
-  uint4 v[kMaxChunks];
+  uint4 v[C];
   load_row(a.stage + R * a.d, a.d, lane, v);
   for (unsigned mm = __ballot_sync(kFull, slot >= 0); mm; mm &= mm - 1) {
     const int j = __ffs(mm) - 1;
@@ -228,6 +239,7 @@ __global__ void __launch_bounds__(256) ep_owner_fanout_kernel(EpFanoutArgs a) {
 
 // One warp per unique row: read dout once; dy[slot_j] = w_j dout; dw_j = dout . y[slot_j]
 // stored into the source's dw buffer.
+template <int C>
 __global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a, const __nv_bfloat16* y,
                                                                    long ld_y, __nv_bfloat16* dy, long ld_dy,
                                                                    float* const* peer_dw) {
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a
     wj = a.meta_w[u * a.k + lane];
   }
   const unsigned mask = __ballot_sync(kFull, lane < a.k && sl >= 0);
-  uint4 g[kMaxChunks];
+  uint4 g[C];
   load_row(a.local_rows ? a.local_rows + static_cast<long>(a.urow[u]) * a.d
                         : a.peer_rows[s] + static_cast<long>(t) * a.d,
            a.d, lane, g);
@@ -255,7 +267,7 @@ __global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a
     __nv_bfloat16* dr = dy + static_cast<long>(slj) * ld_dy;
     float dot = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
+    for (int i = 0; i < C; ++i) {
       const int c = i * 256 + lane * 8;
       if (c < a.d) {
         const uint4 yv = ld_global_v4(yr + c);
@@ -278,6 +290,7 @@ __global__ void __launch_bounds__(256) ep_owner_grad_gather_kernel(EpOwnerArgs a
 
 // One warp per local token: residual + the partial rows of every owner it routed to
 // (+ gated shared-expert rows).
+template <int C>
 __global__ void __launch_bounds__(256) ep_source_reduce_kernel(EpSourceArgs a) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -285,12 +298,12 @@ __global__ void __launch_bounds__(256) ep_source_reduce_kernel(EpSourceArgs a) {
   unsigned bits = 0;
   if (lane < a.k) bits = 1u << (a.idx[static_cast<long>(t) * a.k + lane] / a.El);
   const unsigned owners = __reduce_or_sync(kFull, bits);
-  float acc[kMaxChunks][8];
+  float acc[C][8];
   if (a.residual) {
-    uint4 r[kMaxChunks];
+    uint4 r[C];
     load_row(a.residual + static_cast<long>(t) * a.ld_res, a.d, lane, r);
 #pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
+    for (int i = 0; i < C; ++i) {
       const uint32_t rw[4] = {r[i].x, r[i].y, r[i].z, r[i].w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -301,7 +314,7 @@ __global__ void __launch_bounds__(256) ep_source_reduce_kernel(EpSourceArgs a) {
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i)
+    for (int i = 0; i < C; ++i)
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
   }
@@ -336,6 +349,14 @@ void ep_copy_rows(const EpCopyArgs& a, cudaStream_t stream) {
 
 namespace ddb {
 namespace {
+// run f with the chunk count for rows of d columns as a compile-time constant
+template <typename F>
+void launch_c(int d, F f) {
+  if (d <= 1024)
+    f(std::integral_constant<int, 4>{});
+  else
+    f(std::integral_constant<int, 8>{});
+}
 void check_owner(const EpOwnerArgs& a) {
   if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
   if (a.k > 32 || a.k < 1) throw std::runtime_error("ep: 1 <= k <= 32");
@@ -347,7 +368,7 @@ void ep_push_rows(const EpPushArgs& a, cudaStream_t s) {
   if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
   if (a.k > 32 || a.k < 1 || a.world > 32 || a.world < 1) throw std::runtime_error("ep: k <= 32, world <= 32");
   if (a.N == 0) return;
-  ep_push_rows_kernel<<<(a.N + 7) / 8, 256, 0, s>>>(a);
+  launch_c(a.d, [&](auto c) { ep_push_rows_kernel<decltype(c)::value><<<(a.N + 7) / 8, 256, 0, s>>>(a); });
   count_launch();
   check_cuda(cudaGetLastError(), "ep_push_rows launch");
 }
@@ -359,7 +380,7 @@ void ep_owner_fanout(const EpFanoutArgs& a, cudaStream_t s) {
     check_cuda(cudaMemsetAsync(a.n_uniq, 0, sizeof(int), s), "ep fanout n_uniq");
     return;
   }
-  ep_owner_fanout_kernel<<<(a.total + 7) / 8, 256, 0, s>>>(a);
+  launch_c(a.d, [&](auto c) { ep_owner_fanout_kernel<decltype(c)::value><<<(a.total + 7) / 8, 256, 0, s>>>(a); });
   count_launch();
   check_cuda(cudaGetLastError(), "ep_owner_fanout launch");
 }
@@ -368,7 +389,9 @@ void ep_owner_grad_gather(const EpOwnerArgs& a, const __nv_bfloat16* y, long ld_
                           long ld_dy, float* const* peer_dw, cudaStream_t s) {
   check_owner(a);
   if (a.cap == 0) return;
-  ep_owner_grad_gather_kernel<<<(a.cap + 7) / 8, 256, 0, s>>>(a, y, ld_y, dy, ld_dy, peer_dw);
+  launch_c(a.d, [&](auto c) {
+    ep_owner_grad_gather_kernel<decltype(c)::value><<<(a.cap + 7) / 8, 256, 0, s>>>(a, y, ld_y, dy, ld_dy, peer_dw);
+  });
   count_launch();
   check_cuda(cudaGetLastError(), "ep_owner_grad_gather launch");
 }
@@ -377,7 +400,9 @@ void ep_owner_scatter_sum(const EpOwnerArgs& a, const __nv_bfloat16* src, long l
                           __nv_bfloat16* const* peer_ret, cudaStream_t s) {
   check_owner(a);
   if (a.cap == 0) return;
-  ep_owner_scatter_sum_kernel<<<(a.cap + 7) / 8, 256, 0, s>>>(a, src, ld_src, weighted, peer_ret);
+  launch_c(a.d, [&](auto c) {
+    ep_owner_scatter_sum_kernel<decltype(c)::value><<<(a.cap + 7) / 8, 256, 0, s>>>(a, src, ld_src, weighted, peer_ret);
+  });
   count_launch();
   check_cuda(cudaGetLastError(), "ep_owner_scatter_sum launch");
 }
@@ -385,7 +410,7 @@ void ep_owner_scatter_sum(const EpOwnerArgs& a, const __nv_bfloat16* src, long l
 void ep_source_reduce(const EpSourceArgs& a, cudaStream_t s) {
   if (a.d % 8 != 0 || a.d > 256 * kMaxChunks) throw std::runtime_error("ep: d % 8 == 0 and d <= 2048");
   if (a.N == 0) return;
-  ep_source_reduce_kernel<<<(a.N + 7) / 8, 256, 0, s>>>(a);
+  launch_c(a.d, [&](auto c) { ep_source_reduce_kernel<decltype(c)::value><<<(a.N + 7) / 8, 256, 0, s>>>(a); });
   count_launch();
   check_cuda(cudaGetLastError(), "ep_source_reduce launch");
 }
