@@ -66,8 +66,10 @@ __device__ __forceinline__ bool block_valid(int i, int j, int causal, int bpf) {
   return true;
 }
 
-// one CTA per (b, h); nb <= 256 (multiple of 32)
-__global__ void __launch_bounds__(256) sla_route_kernel(SlaRouteArgs a) {
+// one CTA per (b, h); nb <= 256 (multiple of 32). 32 warps per CTA: there are only B*H
+// CTAs, so each one's query-block rows are spread over as many warps as a CTA holds.
+constexpr int kRouteThreads = 1024;
+__global__ void __launch_bounds__(kRouteThreads) sla_route_kernel(SlaRouteArgs a) {
   extern __shared__ float sm[];
   const int nb = a.nb;
   const int words = (nb + 31) / 32;
@@ -77,7 +79,7 @@ __global__ void __launch_bounds__(256) sla_route_kernel(SlaRouteArgs a) {
   const int bh = blockIdx.x;
   const float* qm = a.qm + static_cast<long>(bh) * nb * D;
   const float* km = a.km + static_cast<long>(bh) * nb * D;
-  for (int i = threadIdx.x; i < nb * D; i += 256) {
+  for (int i = threadIdx.x; i < nb * D; i += kRouteThreads) {
     sq[i] = qm[i];
     sk[(i / D) * (D + 1) + i % D] = km[i];
   }
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(256) sla_route_kernel(SlaRouteArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float scale = rsqrtf(static_cast<float>(D));
   constexpr int MAXS = 8;  // nb / 32 <= 8
-  for (int i = warp; i < nb; i += 8) {
+  for (int i = warp; i < nb; i += kRouteThreads / 32) {
     float sc[MAXS];
 #pragma unroll
     for (int s = 0; s < MAXS; ++s) {
@@ -140,12 +142,12 @@ __global__ void __launch_bounds__(256) sla_route_kernel(SlaRouteArgs a) {
   }
   __syncthreads();
   if (a.sel_bits)
-    for (int i = threadIdx.x; i < nb * words; i += 256)
+    for (int i = threadIdx.x; i < nb * words; i += kRouteThreads)
       a.sel_bits[static_cast<long>(bh) * nb * words + i] = sel[i];
   const int nt = nb / 2;
   auto bit = [&](int row, int col) -> uint32_t { return (sel[row * words + (col >> 5)] >> (col & 31)) & 1u; };
   // forward lists: per query tile t, its union of selected key blocks, paired
-  for (int t = threadIdx.x; t < nt; t += 256) {
+  for (int t = threadIdx.x; t < nt; t += kRouteThreads) {
     const long li = static_cast<long>(bh) * nt + t;
     int n = 0, pending = -1;
     for (int j = 0; j < nb; ++j) {
@@ -174,7 +176,7 @@ __global__ void __launch_bounds__(256) sla_route_kernel(SlaRouteArgs a) {
     a.pair_count[li] = min(n, a.max_pairs);
   }
   // backward lists: per key tile t (blocks 2t, 2t+1), the query tiles that selected it
-  for (int t = threadIdx.x; t < nt; t += 256) {
+  for (int t = threadIdx.x; t < nt; t += kRouteThreads) {
     const long li = static_cast<long>(bh) * nt + t;
     int n = 0;
     for (int i = 0; i < nt; ++i) {
@@ -210,7 +212,7 @@ void sla_route(const SlaRouteArgs& a, int BH, cudaStream_t s) {
                "cudaFuncSetAttribute(sla_route)");
     attr = true;
   }
-  sla_route_kernel<<<BH, 256, smem, s>>>(a);
+  sla_route_kernel<<<BH, kRouteThreads, smem, s>>>(a);
   count_launch();
 }
 
