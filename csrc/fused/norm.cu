@@ -204,10 +204,10 @@ void adaln_rmsnorm_fwd(const AdaLNArgs& a, cudaStream_t s) {
 
 void adaln_rmsnorm_bwd(const AdaLNArgs& a, cudaStream_t s) {
   count_launch();
-  // rows per CTA: a divisor of rows_per_group so a CTA never straddles two groups
-  int rpc = 64;
-  while (a.rows_per_group % rpc) rpc >>= 1;
-  if (rpc < 8) rpc = a.rows_per_group < 8 ? a.rows_per_group : 8;
+  // rows per CTA: the largest divisor of rows_per_group up to 64, so a CTA never
+  // straddles two groups
+  int rpc = a.rows_per_group < 64 ? a.rows_per_group : 64;
+  while (a.rows_per_group % rpc) --rpc;
   const int grid = (a.M + rpc - 1) / rpc;
   switch (a.D) {
 #define CASE(V)                                                                                   \

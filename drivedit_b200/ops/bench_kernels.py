@@ -181,6 +181,30 @@ def bench_sla_linear(iters: int = 10, B: int = 4, H: int = 12, T: int = 8192):
         print(json.dumps({"kernel": name, "B": B, "H": H, "T": T, "ms": round(ms, 4)}), flush=True)
 
 
+def bench_norm(iters: int = 20, M: int = 65536, D: int = 768, tpf: int = 512):
+    """AdaLN-RMSNorm forward and backward at the DiT-B shape (8 x 8192 tokens, d=768,
+    512 tokens per frame), with achieved DRAM bandwidth over the bytes each must move."""
+    from .fused import adaln_rmsnorm, adaln_rmsnorm_bwd
+
+    G = M // tpf
+    x = torch.randn(M, D, device="cuda").bfloat16()
+    w = 1 + 0.1 * torch.randn(D, device="cuda")
+    mod = 0.2 * torch.randn(G, 6 * D, device="cuda")
+    dh = torch.randn(M, D, device="cuda").bfloat16()
+    dres = torch.randn(M, D, device="cuda").bfloat16()
+    dmod = torch.zeros_like(mod)
+    dw = torch.zeros_like(w)
+    h, r = adaln_rmsnorm(x, w, mod, 0, D, tpf)
+    row = M * D * 2
+    for name, fn, nbytes in (
+            ("adaln_fwd", lambda: adaln_rmsnorm(x, w, mod, 0, D, tpf), 2 * row),
+            ("adaln_bwd", lambda: adaln_rmsnorm_bwd(dh, x, r, w, mod, 0, D, tpf, dmod, dw, dres),
+             4 * row)):
+        ms = _timeit(fn, iters)
+        print(json.dumps({"kernel": name, "M": M, "D": D, "ms": round(ms, 4),
+                          "GB_s": round(nbytes / ms / 1e6, 1)}), flush=True)
+
+
 def bench_conv3d(iters: int = 10):
     """VAE causal 3x3x3 convolutions at 8 frames of 256x512 RGB (encoder level 0,
     128 ch, and level 2, 512 ch at 65x129), stride-2 downsample, vs cuDNN."""

@@ -36,6 +36,29 @@ def test_adaln_fwd_bwd(D):
     assert _rel(dmod, mf.grad) < 1e-2
 
 
+def test_adaln_bwd_odd_groups_no_dw_no_residual():
+    """Groups of 100 rows (not a multiple of 8: CTAs of 50 rows), no norm-weight gradient,
+    no residual."""
+    from drivedit_b200.ops.fused import adaln_rmsnorm, adaln_rmsnorm_bwd
+    M, D, tpf = 1000, 768, 100
+    G = M // tpf
+    x = torch.randn(M, D, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(D, device="cuda"))
+    mod = 0.2 * torch.randn(G, 2 * D, device="cuda")
+    h, r = adaln_rmsnorm(x, w, mod, 0, D, tpf)
+    xf = x.float().requires_grad_(True)
+    mf = mod.clone().requires_grad_(True)
+    sc = mf[:, :D].repeat_interleave(tpf, 0)
+    sh = mf[:, D:].repeat_interleave(tpf, 0)
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w * (1 + sc) + sh
+    dh = torch.randn(M, D, device="cuda").bfloat16()
+    ref.backward(dh.float())
+    dmod = torch.zeros_like(mod)
+    dx = adaln_rmsnorm_bwd(dh, x, r, w, mod, 0, D, tpf, dmod)
+    assert _rel(dx, xf.grad) < 2e-2
+    assert _rel(dmod, mf.grad) < 1e-2
+
+
 def test_adamw_matches_reference():
     from drivedit_b200.ops.fused import adamw_flat
     n = 4096
