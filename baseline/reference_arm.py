@@ -136,9 +136,16 @@ def run(args, ws, rank, local):
         return {"total": F.mse_loss(out.float(), batch["target"])}
 
     batch = make()
-    for _ in range(args.warmup):
-        trainer.train_step(batch, opt, loss_fn)
-    torch.cuda.synchronize()
+    try:
+        for _ in range(args.warmup):
+            trainer.train_step(batch, opt, loss_fn)
+        torch.cuda.synchronize()
+    except torch.OutOfMemoryError as exc:
+        # the unmodified reference does not fit this config (eager SLA block loop, no
+        # activation checkpointing): report it instead of a number
+        return _unavailable(f"out of memory on one GPU in the reference's training step at "
+                            f"{B} x {Fr * m.tokens_per_frame} tokens per GPU "
+                            f"({str(exc).splitlines()[0][:160]})")
     if dist.is_initialized():
         dist.barrier()
     torch.cuda.synchronize()
