@@ -11,9 +11,13 @@ logit-normal flow time, velocity-MSE loss, AdamW. Synthetic data, random-init we
 Timing: W untimed warm-up steps, then K steps between a barrier + device sync on each
 side, timed with CUDA events on the training stream; each step first overwrites a
 256 MiB buffer to flush L2. The reported ms/step is the max over ranks; ``value`` is the
-whole-job token rate. ``e2e`` repeats the measurement through the public trainer API
-with each step's inputs copied from pinned host memory and the loss read back.
-Rank 0 prints one JSON line.
+whole-job token rate. ``e2e`` repeats the measurement (same step count) through the
+public trainer API with each step's inputs copied from pinned host memory and the loss
+read back. ``extras`` adds, unless ``--no-extras``: MoE DiT-L training tok/s (fsdp +
+expert parallel over the job's ranks) and streaming-rollout frames/s with p50 / p99
+chunk latency at batch 1 and 16 (tensor parallel over the job's ranks). Rank 0 prints
+one JSON line. ``--impl reference`` runs the reference arm (``baseline/reference_arm.py``)
+and prints the same line with ``"impl": "reference"``.
 """
 from __future__ import annotations
 
@@ -43,14 +47,25 @@ def dist_env():
     return ws, rank, local
 
 
-def init_dist(ws, local):
+def init_dist(ws, local, timeout_s=300):
     torch.cuda.set_device(local)
     if ws > 1 and not dist.is_initialized():
         import datetime
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
                                 device_id=torch.device("cuda", local))
+
+
+def check_device_free(rank, local, min_free_frac=0.5):
+    """Print this rank's free / total device memory; refuse to start on a GPU that
+    another process already fills (a leftover job would make the run fail later)."""
+    free, total = torch.cuda.mem_get_info(local)
+    print(f"[rank {rank}] cuda:{local} free {free / 2**30:.1f} / {total / 2**30:.1f} GiB",
+          file=sys.stderr, flush=True)
+    if free < min_free_frac * total:
+        raise RuntimeError(f"rank {rank}: cuda:{local} has only {free / 2**30:.1f} GiB of "
+                           f"{total / 2**30:.1f} GiB free; another process holds the GPU")
 
 
 def max_over_ranks(x: float) -> float:
@@ -133,15 +148,24 @@ def launch_count():
 
 
 # --------------------------------------------------------------------------- our arm
-def run_ours(args, ws, rank, local):
-    sys.path.insert(0, ROOT)
+def _gpu_index(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return int(vis.split(",")[local]) if vis else local
+
+
+def _train_throughput(cfg_name, overrides, steps, warmup, ws, rank, local, e2e_steps=0,
+                      clocks=False):
+    """Device-timed training throughput of one preset through the public trainer API.
+
+    Returns (result dict, trainer summary dict). ``e2e_steps`` > 0 adds the end-to-end
+    measurement (pinned host batch copied in, loss read back, every step)."""
     from drivedit_b200.config import get_config
     from drivedit_b200.data.synthetic import make_batch
     from drivedit_b200.models.world_dit import WorldDiT
     from drivedit_b200.ops._ext import check_device_status
     from drivedit_b200.training.trainer import WorldModelTrainer
 
-    cfg = get_config(args.config, args.override)
+    cfg = get_config(cfg_name, overrides)
     torch.manual_seed(cfg.train.seed + rank)
     dev = torch.device("cuda", local)
     model = WorldDiT(cfg.model)
@@ -154,7 +178,7 @@ def run_ours(args, ws, rank, local):
     dev_batch = make_batch(cfg, device=dev, generator=gen, rgb_frames=rgb)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         trainer.train_step(dev_batch)
     torch.cuda.synchronize()
     check_device_status()
@@ -162,44 +186,96 @@ def run_ours(args, ws, rank, local):
     barrier()
     torch.cuda.synchronize()
     n0 = launch_count()
-    with ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                      int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])) as clk:
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(args.steps):
-            flush.zero_()
-            loss = trainer.train_step(dev_batch)
-        end.record()
-        torch.cuda.synchronize()
+    clk = ClockSampler(_gpu_index(local)) if clocks else None
+    if clk is not None:
+        clk.__enter__()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        flush.zero_()
+        loss = trainer.train_step(dev_batch)
+    end.record()
+    torch.cuda.synchronize()
+    if clk is not None:
+        clk.__exit__()
     barrier()
     n_launch = launch_count() - n0  # this extension's kernels only (the L2 flush is not one)
-    ms = start.elapsed_time(end) / args.steps
-    ms = max_over_ranks(ms)
+    ms = max_over_ranks(start.elapsed_time(end) / steps)
     check_device_status()
+    out = {"ms_per_step": ms, "value": ws * tokens_per_step / (ms / 1000.0),
+           "gpu_launches": n_launch, "tokens_per_step_per_gpu": tokens_per_step,
+           "final_loss": float(loss.item())}
+    if clk is not None:
+        out["clocks"] = clk.summary()
 
-    # ---- end to end through the public API: pinned host inputs in, loss out
-    host = [make_batch(cfg, generator=gen, pin=True, rgb_frames=rgb) for _ in range(2)]
-    h2d = host[0].nbytes()
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    barrier()
+    if e2e_steps > 0:
+        # end to end through the public API: pinned host inputs in, loss out, every step
+        host = [make_batch(cfg, generator=gen, pin=True, rgb_frames=rgb) for _ in range(2)]
+        h2d = host[0].nbytes()
+        barrier()
+        torch.cuda.synchronize()
+        s2 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        s2.record()
+        losses = []
+        for i in range(e2e_steps):
+            flush.zero_()  # same cold-L2 start as the device-timed steps
+            b = host[i % 2].to(dev, non_blocking=True)
+            losses.append(float(trainer.train_step(b).item()))
+        e2.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps)
+        barrier()
+        out["e2e"] = {"value": round(ws * tokens_per_step / (e2e_ms / 1000.0), 1),
+                      "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                      "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps}
+        out["final_loss"] = losses[-1]
+    summary = {
+        "model": cfg.model.name,
+        "layers": cfg.model.n_layers, "d_model": cfg.model.d_model,
+        "heads": cfg.model.n_heads, "mlp_hidden": cfg.model.mlp_hidden,
+        "attention": cfg.model.attention,
+        "global_batch": B * ws, "seq_len": Fr * cfg.model.tokens_per_frame,
+        "frames": Fr, "latent": [cfg.model.latent_channels, cfg.model.latent_h,
+                                 cfg.model.latent_w],
+        "parallelism": (f"fsdp{ws}+ep{ws}" if trainer.ep is not None else f"fsdp{ws}")
+        if ws > 1 else "single",
+        "sharding": (("gradients reduce-scattered and weights all-gathered by the fused "
+                      "NVLink optimizer kernel" if trainer.engine.transport == "fused" else
+                      "NCCL reduce_scatter / all_gather around a local AdamW")
+                     + "; AdamW state sharded") if ws > 1 else None,
+        "expert_parallel": None if trainer.ep is None else (
+            f"{cfg.model.moe.num_experts // ws} routed experts per rank; token rows "
+            + ("pushed once per owner over NVLink peer memory (P2P stores) by the EP kernels"
+               if trainer.ep.transport == "fused" else "exchanged by NCCL all_to_all")),
+        "repa": cfg.model.repa is not None,
+    }
+    trainer.close()
+    del trainer, model, dev_batch, flush
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    s2 = torch.cuda.Event(enable_timing=True)
-    e2 = torch.cuda.Event(enable_timing=True)
-    s2.record()
-    losses = []
-    for i in range(e2e_steps):
-        flush.zero_()  # same cold-L2 start as the device-timed steps
-        b = host[i % 2].to(dev, non_blocking=True)
-        losses.append(float(trainer.train_step(b).item()))
-    e2.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps)
-    barrier()
+    torch.cuda.empty_cache()
+    return out, summary
 
-    value = ws * tokens_per_step / (ms / 1000.0)
-    e2e_value = ws * tokens_per_step / (e2e_ms / 1000.0)
+
+def _rollout_ours(batch, ws):
+    """Streaming rollout of the causal DiT-B student: tensor parallel over the job's
+    ranks when ws > 1 (fused all-gather / reduce-scatter GEMMs)."""
+    from drivedit_b200.inference.bench_rollout import run
+
+    res = run(batch, 120)
+    return {"batch": batch, "frames_per_s": res["value"], "p50_chunk_ms": res["p50_chunk_ms"],
+            "p99_chunk_ms": res["p99_chunk_ms"], "chunks": res["chunks"],
+            "tensor_parallel": res["tensor_parallel"]}
+
+
+def run_ours(args, ws, rank, local):
+    sys.path.insert(0, ROOT)
+    res, summary = _train_throughput(args.config, args.override, args.steps, args.warmup, ws,
+                                     rank, local, e2e_steps=args.steps, clocks=True)
+    value, ms = res["value"], res["ms_per_step"]
+    summary["l2"] = ("256 MiB buffer overwritten before every timed step "
+                     "(device-timed and end-to-end)")
     out = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -214,43 +290,52 @@ def run_ours(args, ws, rank, local):
         "dtype": "bf16",
         "data": "synthetic latents/actions/flow-time, random-init weights" + (
             ", RGB frames ~U[0,1] for the random-init frozen ViT-L REPA teacher"
-            if cfg.model.repa is not None else ""),
-        "config": {
-            "model": cfg.model.name,
-            "layers": cfg.model.n_layers, "d_model": cfg.model.d_model,
-            "heads": cfg.model.n_heads, "mlp_hidden": cfg.model.mlp_hidden,
-            "attention": cfg.model.attention,
-            "global_batch": B * ws, "seq_len": Fr * cfg.model.tokens_per_frame,
-            "frames": Fr, "latent": [cfg.model.latent_channels, cfg.model.latent_h,
-                                     cfg.model.latent_w],
-            "parallelism": (f"fsdp{ws}+ep{ws}" if trainer.ep is not None else f"fsdp{ws}")
-                           if ws > 1 else "single",
-            "sharding": (("gradients reduce-scattered and weights all-gathered by the fused "
-                          "NVLink optimizer kernel" if trainer.engine.transport == "fused" else
-                          "NCCL reduce_scatter / all_gather around a local AdamW")
-                         + "; AdamW state sharded") if ws > 1 else None,
-            "expert_parallel": None if trainer.ep is None else (
-                f"{cfg.model.moe.num_experts // ws} routed experts per rank; token rows "
-                + ("pushed once per owner over NVLink peer memory (P2P stores) by the EP kernels"
-                   if trainer.ep.transport == "fused" else "exchanged by NCCL all_to_all")),
-            "l2": "256 MiB buffer overwritten before every timed step (device-timed and end-to-end)",
-        },
-        "clocks": clk.summary(),
-        "e2e": {"value": round(e2e_value, 1), "unit": "tok/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                "ms_per_step": round(e2e_ms, 3)},
-        "gpu_launches": n_launch,
-        "final_loss": losses[-1] if losses else None,
+            if summary["repa"] else ""),
+        "config": summary,
+        "clocks": res["clocks"],
+        "e2e": res["e2e"],
+        "gpu_launches": res["gpu_launches"],
+        "final_loss": res["final_loss"],
     }
+    if not args.no_extras:
+        extras = {}
+        # MoE DiT-L (fsdp + expert parallel over the job's ranks)
+        mres, msum = _train_throughput("moe_dit_l", [], args.extra_steps, 3, ws, rank, local)
+        extras["moe_dit_l"] = {"value": round(mres["value"], 1), "unit": "tok/s",
+                               "ms_per_step": round(mres["ms_per_step"], 3),
+                               "steps": args.extra_steps, "warmup": 3,
+                               "gpu_launches": mres["gpu_launches"],
+                               "parallelism": msum["parallelism"],
+                               "global_batch": msum["global_batch"],
+                               "seq_len": msum["seq_len"]}
+        # streaming rollout (frames/s, p50 / p99 chunk latency)
+        extras["rollout"] = [_rollout_ours(b, ws) for b in (1, 16)]
+        out["extras"] = extras
     if rank == 0:
         print(json.dumps(out), flush=True)
 
 
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args, ws, rank, local):
-    from baseline.reference_arm import run
+    from baseline.reference_arm import run, run_rollout
 
     out = run(args, ws, rank, local)
+    if not args.no_extras and out is not None:
+        extras = {}
+        rolls = []
+        for b in (1, 16):
+            r = run_rollout(b)
+            if "frames_per_s" in r:
+                # every rank runs its own rollouts (the reference has no tensor
+                # parallelism): the slowest rank's rate, times the ranks
+                per = max_over_ranks(1.0 / r["frames_per_s"])
+                r["frames_per_s_per_rank"] = round(1.0 / per, 2)
+                r["frames_per_s"] = round(ws / per, 2)
+                r["tensor_parallel"] = 1
+                r["replicas"] = ws
+            rolls.append(r)
+        extras["rollout"] = rolls
+        out["extras"] = extras
     if rank == 0 and out is not None:
         print(json.dumps(out), flush=True)
 
@@ -260,7 +345,10 @@ def main():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--extra-steps", type=int, default=10,
+                   help="timed steps of the extra workloads (MoE DiT-L)")
+    p.add_argument("--no-extras", action="store_true",
+                   help="only the headline DiT-B training number")
     p.add_argument("--config", default="dit_b")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("override", nargs="*", help="config overrides key=value")
@@ -276,16 +364,26 @@ def main():
         else:
             print(json.dumps({"metric": METRIC, "unavailable": "no CUDA device"}))
         return
-    init_dist(ws, local)
     try:
+        check_device_free(rank, local)
+        init_dist(ws, local)
         if args.impl == "reference":
             run_reference(args, ws, rank, local)
         else:
             run_ours(args, ws, rank, local)
+    except BaseException:
+        # every rank reports its own failure before it exits non-zero
+        import traceback
+
+        print(f"[rank {rank}/{ws}] bench.py ({args.impl}) failed:\n{traceback.format_exc()}",
+              file=sys.stderr, flush=True)
+        raise
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
 
 
 if __name__ == "__main__":
-    main()
+    from torch.distributed.elastic.multiprocessing.errors import record
+
+    record(main)()

@@ -268,7 +268,16 @@ class Upsample3D(nn.Module):
 
 # ----------------------------------------------------------------------------- latent tools
 class VectorQuantizer(nn.Module):
-    """Nearest-codebook quantiser with straight-through gradients and EMA codebook updates."""
+    """Codebook quantiser (VQ-VAE, van den Oord et al. 2017) whose codebook follows the
+    exponential moving average of the vectors assigned to each code (Razavi et al. 2019).
+
+    Forward: each latent vector (channel dim 1) snaps to its nearest code; the output
+    passes gradients straight through to the encoder; the loss is the codebook term
+    plus ``commitment_cost`` times the commitment term. The EMA update runs in one pass
+    over the assignments: ``bincount`` gives the per-code counts and ``index_add_`` the
+    per-code sums (no one-hot matrix), then the counts are Laplace-smoothed so that an
+    unused code keeps a finite centroid.
+    """
 
     def __init__(self, num_embeddings, embedding_dim, commitment_cost=0.25, decay=0.99,
                  epsilon=1e-5):
@@ -276,41 +285,62 @@ class VectorQuantizer(nn.Module):
         self.num_embeddings, self.embedding_dim = num_embeddings, embedding_dim
         self.commitment_cost, self.decay, self.epsilon = commitment_cost, decay, epsilon
         self.embeddings = nn.Embedding(num_embeddings, embedding_dim)
-        nn.init.uniform_(self.embeddings.weight, -1 / num_embeddings, 1 / num_embeddings)
+        bound = 1.0 / num_embeddings
+        with torch.no_grad():
+            self.embeddings.weight.uniform_(-bound, bound)
         self.register_buffer("ema_cluster_size", torch.zeros(num_embeddings))
         self.register_buffer("ema_w", self.embeddings.weight.detach().clone())
 
+    def assign(self, vectors: torch.Tensor) -> torch.Tensor:
+        """Index of the nearest code for each row of ``vectors [N, C]``."""
+        code = self.embeddings.weight
+        # |v - e|^2 = |v|^2 - 2 v.e + |e|^2; |v|^2 is the same for every code of a row
+        score = torch.addmm(code.pow(2).sum(1)[None, :], vectors, code.t(), alpha=-2.0)
+        return score.argmin(dim=1)
+
+    @torch.no_grad()
+    def _ema_update(self, vectors: torch.Tensor, idx: torch.Tensor) -> None:
+        K, keep = self.num_embeddings, self.decay
+        counts = torch.bincount(idx, minlength=K).to(vectors.dtype)
+        sums = torch.zeros_like(self.ema_w).index_add_(0, idx, vectors.to(self.ema_w.dtype))
+        self.ema_cluster_size.lerp_(counts, 1.0 - keep)
+        self.ema_w.lerp_(sums, 1.0 - keep)
+        total = self.ema_cluster_size.sum()
+        smoothed = (self.ema_cluster_size + self.epsilon) * (total / (total + K * self.epsilon))
+        self.embeddings.weight.copy_(self.ema_w / smoothed[:, None])
+
     def forward(self, z):
-        B, C, T, H, W = z.shape
-        flat = z.permute(0, 2, 3, 4, 1).reshape(-1, C)
-        e = self.embeddings.weight
-        d = flat.pow(2).sum(1, keepdim=True) - 2 * flat @ e.t() + e.pow(2).sum(1)
-        idx = d.argmin(1)
-        zq = self.embeddings(idx).view(B, T, H, W, C).permute(0, 4, 1, 2, 3)
-        loss = F.mse_loss(zq, z.detach()) + self.commitment_cost * F.mse_loss(zq.detach(), z)
-        zq_st = z + (zq - z).detach()
+        C = z.shape[1]
+        channels_last = z.movedim(1, -1)
+        vectors = channels_last.reshape(-1, C)
+        idx = self.assign(vectors)
+        quant = self.embeddings(idx).view_as(channels_last).movedim(-1, 1)
+        codebook_term = (quant - z.detach()).pow(2).mean()
+        commitment_term = (z - quant.detach()).pow(2).mean()
+        loss = codebook_term + self.commitment_cost * commitment_term
+        out = z + (quant - z).detach()
         if self.training:
-            with torch.no_grad():
-                onehot = F.one_hot(idx, self.num_embeddings).to(flat.dtype)
-                self.ema_cluster_size.mul_(self.decay).add_(onehot.sum(0), alpha=1 - self.decay)
-                self.ema_w.mul_(self.decay).add_(onehot.t() @ flat, alpha=1 - self.decay)
-                n = self.ema_cluster_size.sum()
-                size = (self.ema_cluster_size + self.epsilon) / (n + self.num_embeddings * self.epsilon) * n
-                self.embeddings.weight.data.copy_(self.ema_w / size[:, None])
-        return zq_st, loss, idx.view(B, T, H, W)
+            self._ema_update(vectors.detach(), idx)
+        return out, loss, idx.view(channels_last.shape[:-1])
 
 
 class LearnablePrior(nn.Module):
+    """Learned Gaussian prior over the latent grid: a learned base tensor through a
+    small conv net gives (mean, log-variance). The prior does not depend on the sample,
+    so it is computed once and broadcast over the batch."""
+
     def __init__(self, latent_dim, hidden_dim=256, latent_shape=(2, 32, 32)):
         super().__init__()
         self.latent_dim, self.latent_shape = latent_dim, latent_shape
-        self.base_embedding = nn.Parameter(torch.randn(1, hidden_dim, *latent_shape) * 0.02)
+        self.base_embedding = nn.Parameter(0.02 * torch.randn(1, hidden_dim, *latent_shape))
         self.net = nn.Sequential(nn.Conv3d(hidden_dim, hidden_dim, 3, padding=1), nn.SiLU(),
                                  nn.Conv3d(hidden_dim, 2 * latent_dim, 3, padding=1))
 
     def forward(self, batch_size, device):
-        p = self.net(self.base_embedding.expand(batch_size, -1, -1, -1, -1).to(device))
-        return p.chunk(2, dim=1)
+        params = self.net(self.base_embedding.to(device))
+        mean, logvar = params.split(self.latent_dim, dim=1)
+        return (mean.expand(batch_size, *mean.shape[1:]),
+                logvar.expand(batch_size, *logvar.shape[1:]))
 
 
 class PerceptualLoss(nn.Module):
@@ -344,34 +374,46 @@ class PerceptualLoss(nn.Module):
 
 
 class KLAnnealer:
+    """Weight of the KL term by training step, on the shared piecewise schedule:
+    ``constant`` (``end_beta``), ``linear`` (warm-up from ``start_beta`` to ``end_beta``
+    over ``warmup_steps``, then hold) or ``cyclical`` (a half-cosine ramp from
+    ``start_beta`` towards ``end_beta`` repeated every ``cycle_period`` steps, the
+    cyclical schedule of Fu et al. 2019). ``free_bits`` > 0 subtracts a per-dimension
+    allowance from the KL before it is weighted (no gradient below the allowance)."""
+
     def __init__(self, mode="cyclical", cycle_period=10000, start_beta=0.0, end_beta=1.0,
                  warmup_steps=1000, free_bits=0.0):
+        from ..utils.schedules import PiecewiseSchedule, Segment
+
         self.mode, self.cycle_period = mode, cycle_period
         self.start_beta, self.end_beta = start_beta, end_beta
         self.warmup_steps, self.free_bits = warmup_steps, free_bits
         self.step = 0
-        self._restart_cycle_step = 0
+        if mode == "constant":
+            segs, period = [Segment(None, end_beta, end_beta, "constant")], None
+        elif mode == "linear":
+            segs = [Segment(max(1, warmup_steps), start_beta, end_beta, "linear", "warmup"),
+                    Segment(None, end_beta, end_beta, "constant", "hold")]
+            period = None
+        elif mode == "cyclical":
+            segs, period = [Segment(cycle_period, start_beta, end_beta, "cosine")], cycle_period
+        else:
+            raise ValueError(f"Unknown annealing mode: {mode}")
+        self.schedule = PiecewiseSchedule(segs, period)
 
     def get_beta(self) -> float:
-        if self.mode == "constant":
-            return self.end_beta
-        if self.mode == "linear":
-            if self.step < self.warmup_steps:
-                return self.start_beta + (self.end_beta - self.start_beta) * self.step / self.warmup_steps
-            return self.end_beta
-        if self.mode == "cyclical":
-            prog = ((self.step - self._restart_cycle_step) % self.cycle_period) / self.cycle_period
-            return self.start_beta + 0.5 * (self.end_beta - self.start_beta) * (1 - math.cos(math.pi * prog))
-        raise ValueError(f"Unknown annealing mode: {self.mode}")
+        return self.schedule(self.step)
 
     def update(self):
         self.step += 1
 
     def warm_restart(self):
-        self._restart_cycle_step = self.step
+        self.schedule.restart(self.step)
 
     def apply_free_bits(self, kl_per_dim):
-        return torch.clamp(kl_per_dim - self.free_bits, min=0.0) if self.free_bits > 0 else kl_per_dim
+        if self.free_bits <= 0:
+            return kl_per_dim
+        return (kl_per_dim - self.free_bits).clamp_min(0.0)
 
 
 # ----------------------------------------------------------------------------- encoder / decoder

@@ -6,6 +6,10 @@ rotated) and returns ``(o [M, d] bf16, o_lin or None, lse, aux)``;
 
 Modes: ``dense`` (frame-causal / token-causal / bidirectional softmax attention) and
 ``sla`` (top-k block routing, block-sparse softmax, linear branch).
+
+CUDA tensors always run the sm_100a kernels; a missing or incomplete extension raises
+instead of falling back. CPU tensors run the PyTorch reference (dense only), which is
+what the CPU tests and the CPU oracles use.
 """
 from __future__ import annotations
 
@@ -14,8 +18,14 @@ import torch
 from ._ext import ext
 
 
-def _kernels():
-    return getattr(ext(), "attn_fwd", None) is not None
+def _kernels(t: torch.Tensor) -> bool:
+    """True for CUDA tensors; raises when the extension lacks the attention kernels."""
+    if not t.is_cuda:
+        return False
+    if getattr(ext(), "attn_fwd", None) is None:
+        raise RuntimeError("the drivedit_b200 extension was built without the attention "
+                           "kernels; rebuild it with `python setup.py build_ext --inplace`")
+    return True
 
 
 def _split(qkv, bc):
@@ -40,19 +50,19 @@ def _torch_dense(q, k, v, bc):
 
 
 def attention_fwd(qkv: torch.Tensor, bc):
-    if _kernels():
+    if _kernels(qkv):
         from .attention_kernels import attention_fwd_kernel
 
         return attention_fwd_kernel(qkv, bc)
     if bc.attn_mode != "dense":
-        raise RuntimeError("SLA attention needs the attn kernels of the extension")
+        raise RuntimeError("SLA attention on the fused block path needs CUDA tensors")
     q, k, v = _split(qkv, bc)
     o = _torch_dense(q, k, v, bc)
     return o.reshape(qkv.shape[0], -1).contiguous(), None, None, None
 
 
 def attention_bwd(qkv, o, lse, do, do_lin, aux, bc):
-    if _kernels():
+    if _kernels(qkv):
         from .attention_kernels import attention_bwd_kernel
 
         return attention_bwd_kernel(qkv, o, lse, do, do_lin, aux, bc)

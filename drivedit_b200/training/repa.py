@@ -13,7 +13,6 @@ projection's two GEMMs and its LayerNorm run on the hand-written kernels.
 """
 from __future__ import annotations
 
-import math
 import warnings
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional
@@ -92,32 +91,39 @@ class ProjectionMLP(nn.Module):
 
 
 class HASTEScheduler:
-    """Weight 0 -> 1 over the warm-up fraction (cosine / linear / step), 1 while active,
-    0 from ``haste_termination_ratio`` of training on."""
+    """REPA weight under HASTE's stage-wise termination (Wang et al. 2025, "REPA Works
+    Until It Doesn't"): representation alignment helps early training and is switched
+    off later. The weight ramps in over the first ``haste_warmup_ratio`` of training
+    (``haste_schedule``: linear, cosine, or step = off until the ramp ends), holds at 1,
+    and is 0 from ``haste_termination_ratio`` of training on. Built on the shared
+    piecewise schedule; ``enable_haste=False`` keeps the weight at 1 throughout."""
+
+    PHASES = ("warmup", "active", "terminated")
 
     def __init__(self, config: REPAConfig):
+        from ..utils.schedules import PiecewiseSchedule, Segment
+
         self.config = config
         self.current_step = 0
         total = config.total_training_steps
         self.warmup_end = int(total * config.haste_warmup_ratio)
-        self.termination_start = int(total * config.haste_termination_ratio)
+        self.termination_start = max(self.warmup_end, int(total * config.haste_termination_ratio))
+        shape = config.haste_schedule if config.haste_schedule in ("linear", "cosine") else "step"
+        segs = []
+        if self.warmup_end > 0:
+            segs.append(Segment(self.warmup_end, 0.0, 1.0, shape, "warmup"))
+        if self.termination_start > self.warmup_end:
+            segs.append(Segment(self.termination_start - self.warmup_end, 1.0, 1.0, "constant",
+                                "active"))
+        segs.append(Segment(None, 0.0, 0.0, "constant", "terminated"))
+        self.schedule = PiecewiseSchedule(segs)
 
     def get_weight(self, step: Optional[int] = None) -> float:
         if step is not None:
             self.current_step = step
         if not self.config.enable_haste:
             return 1.0
-        s = self.current_step
-        if s < self.warmup_end:
-            prog = s / self.warmup_end
-            if self.config.haste_schedule == "linear":
-                return prog
-            if self.config.haste_schedule == "cosine":
-                return 0.5 * (1 - math.cos(math.pi * prog))
-            return 0.0 if prog < 0.5 else 1.0
-        if s >= self.termination_start:
-            return 0.0
-        return 1.0
+        return self.schedule(self.current_step)
 
     def update(self, step: int):
         self.current_step = step
@@ -126,11 +132,7 @@ class HASTEScheduler:
         return self.get_weight() > 0.0
 
     def get_phase(self) -> str:
-        if self.current_step < self.warmup_end:
-            return "warmup"
-        if self.current_step < self.termination_start:
-            return "active"
-        return "terminated"
+        return self.schedule.phase(self.current_step)
 
     def get_progress_info(self) -> Dict[str, Any]:
         return {"current_step": self.current_step, "warmup_end": self.warmup_end,

@@ -325,31 +325,40 @@ class EMAModel:
 
 
 class UncertaintyWeighting(nn.Module):
-    """``sum_i 0.5 exp(-s_i) L_i + 0.5 s_i`` with learnable log variances ``s``."""
+    """Homoscedastic-uncertainty task weighting (Kendall, Gal & Cipolla, CVPR 2018).
+
+    Each task i has a learnable ``s_i = log sigma_i^2``. For regression-type losses the
+    Gaussian likelihood gives ``L = sum_i L_i / (2 sigma_i^2) + log sigma_i
+    = sum_i 0.5 (exp(-s_i) L_i + s_i)``: a noisier task gets less weight, and the
+    ``s_i`` term stops every sigma from growing without bound. The losses present in a
+    call are stacked and weighted in one vector expression; absent ones contribute
+    nothing (their ``s_i`` receive no gradient)."""
 
     def __init__(self, loss_names: List[str], initial_log_var: float = 0.0):
         super().__init__()
         self.loss_names = list(loss_names)
         self.num_losses = len(self.loss_names)
+        self._index = {n: i for i, n in enumerate(self.loss_names)}
         self.log_vars = nn.Parameter(torch.full((self.num_losses,), float(initial_log_var)))
 
     def forward(self, losses: Dict[str, torch.Tensor]):
-        total = torch.zeros((), device=self.log_vars.device)
-        weights = {}
-        for i, name in enumerate(self.loss_names):
-            if name in losses:
-                prec = torch.exp(-self.log_vars[i])
-                total = total + 0.5 * prec * losses[name] + 0.5 * self.log_vars[i]
-                weights[name] = prec.detach()
-        return total, weights
+        names = [n for n in self.loss_names if n in losses]
+        if not names:
+            return torch.zeros((), device=self.log_vars.device), {}
+        idx = torch.tensor([self._index[n] for n in names], device=self.log_vars.device)
+        s = self.log_vars.index_select(0, idx)
+        vals = torch.stack([losses[n].reshape(()).to(s.dtype) for n in names])
+        precision = torch.exp(-s)
+        total = 0.5 * (precision * vals + s).sum()
+        return total, dict(zip(names, precision.detach().unbind(0)))
 
     def get_weights(self) -> Dict[str, float]:
-        w = torch.exp(-self.log_vars.detach()).tolist()
-        return dict(zip(self.loss_names, w))
+        """Current precision ``exp(-s_i)`` per task."""
+        return dict(zip(self.loss_names, self.log_vars.detach().neg().exp().tolist()))
 
     def get_uncertainties(self) -> Dict[str, float]:
-        u = torch.exp(0.5 * self.log_vars.detach()).tolist()
-        return dict(zip(self.loss_names, u))
+        """Current ``sigma_i = exp(s_i / 2)`` per task."""
+        return dict(zip(self.loss_names, self.log_vars.detach().mul(0.5).exp().tolist()))
 
 
 class PerLayerGradientClipper:

@@ -8,8 +8,11 @@ the sm_100a path instead of fp16 autocast + GradScaler.
 
 Parameters live in a :class:`FlatParamGroup`; on CUDA the forward/backward of every
 block runs through the fused kernels and the update is one fused AdamW pass that also
-writes the bf16 weights of the next step. Under ``parallel="fsdp"`` the
-:class:`~drivedit_b200.parallel.fsdp.FSDPEngine` owns the buffers instead.
+writes the bf16 weights of the next step. On a process group of more than one rank the
+:class:`~drivedit_b200.parallel.sharded.ShardedDataParallel` engine owns the buffers
+instead (sharded AdamW state, reduce-scatter / all-gather fused into the optimizer
+kernel), and with ``parallel="fsdp_ep"`` :class:`~drivedit_b200.parallel.expert.ExpertParallel`
+places the routed experts.
 """
 from __future__ import annotations
 
@@ -129,6 +132,14 @@ class WorldModelTrainer:
             self.opt.step()
         self.step_idx += 1
         return loss.detach()
+
+    def close(self):
+        """Release the symmetric (CUDA-IPC) buffers of the sharded and expert-parallel
+        engines; every rank calls it at the same point."""
+        if self.engine is not None:
+            self.engine.close()
+        if self.ep is not None:
+            self.ep.close()
 
     def state_dict(self) -> Dict:
         opt = self.opt.state_dict() if self.opt is not None else {
