@@ -1,36 +1,14 @@
-// Allocation-free attention backward: one extern "C" entry point.
+// Allocation-free attention backward: the implementation of the extern "C" interface
+// declared in attn_noalloc.h (which states who it is for, its limits and its rules).
 //
 // This entry point has no counterpart in the reference (DriveDiT has no CUDA code at
 // all); it is an addition of this library.
 //
-// Who needs it: code that cannot call cudaMalloc while it runs. Examples are a host
-// runtime that pre-plans every byte of device memory (a static memory planner or an
-// embedded/serving executor that forbids allocation after start-up), a caller that
-// holds a non-CUDA allocator and must not let a library grow its own pool, and code
-// running in a context where allocation would stall or is not permitted. The regular
-// backward (``attn_bwd`` through the Python extension) needs two scratch buffers — the
-// fp32 dQ accumulator and the per-row ``delta`` vector — which its caller allocates;
-// here they live in fixed device arrays instead.
-//
 // Scratch: two file-scope ``static __device__`` arrays, 16 MiB for the dQ accumulator
-// (``kNoAllocMaxDqFloats`` floats, i.e. rows * heads * 64 <= 4,194,304) and 1 MiB for
-// ``delta`` (``kNoAllocMaxDeltaFloats`` floats, i.e. batch * heads * queries <= 262,144),
-// plus an int status word. Every GPU that loads this library holds these 17 MiB until
-// the process exits.
-//
-// Use:
-//  * The caller passes inputs (q, k, v, o, dO, lse) and outputs (dq, dk, dv) as device
-//    pointers with row strides and column offsets, exactly like the regular backward.
-//  * The first call on a device (with that device current) looks up the device address
-//    of the arrays once with cudaGetSymbolAddress; make that first call before any
-//    stream capture on that device.
-//  * Every call shares the same arrays and each call overwrites them (the dQ
-//    accumulator is cleared with cudaMemsetAsync at the start of each call). Calls
-//    that overlap on the GPU — on different streams, or from different threads without
-//    ordering — race on the scratch and give wrong results; serialise them.
-//  * Sizes beyond the maxima are rejected (return code kNoAllocTooLarge, message on
-//    stderr); nothing is launched then.
-//  * No cudaMalloc, cudaFree or allocating library routine is called.
+// and 1 MiB for ``delta``, plus an int status word. Host code never passes the
+// arrays' names to a kernel (in host code they are host-side stand-ins, not device
+// addresses): the first call on a device looks up their device addresses with
+// cudaGetSymbolAddress, with that device current, and every launch gets those.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -39,11 +17,12 @@
 
 #include "../common/tma.h"
 #include "attn.h"
+#include "attn_noalloc.h"
 
 namespace {
 
-constexpr long kNoAllocMaxDqFloats = 4L << 20;     // 16 MiB
-constexpr long kNoAllocMaxDeltaFloats = 256L << 10;  // 1 MiB
+constexpr long kNoAllocMaxDqFloats = DDB_NOALLOC_MAX_DQ_FLOATS;        // 16 MiB
+constexpr long kNoAllocMaxDeltaFloats = DDB_NOALLOC_MAX_DELTA_FLOATS;  // 1 MiB
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_dq_acc[kNoAllocMaxDqFloats];
@@ -88,60 +67,42 @@ int scratch_for_current_device(ScratchPtrs* out) {
 
 extern "C" {
 
-// Arguments of ddb_attn_bwd_noalloc. Row strides and column offsets are in elements;
-// head h of q/k/v/o/dO/dq/dk/dv occupies columns [col + 64 h, col + 64 h + 64).
-typedef struct {
-  int B, H, Tq, S;                 // batch, heads (d_head = 64), queries, keys per sample
-  long long q_rows_per_b, kv_rows_per_b;  // rows between samples in q/o/dO/dq and in k/v/dk/dv
-  const void* q; long long ldq; int q_col;
-  const void* k; long long ldk; int k_col;
-  const void* v; long long ldv; int v_col;
-  const void* o; long long ldo; int o_col;
-  const void* dout; long long lddo; int do_col;
-  const float* lse;                // [B, H, Tq] from the forward (log2 domain)
-  void* dq; long long lddq; int dq_col;
-  void* dk; long long lddk; int dk_col;
-  void* dv; long long lddv; int dv_col;
-  int causal;                      // 0 none, 1 frame-causal, 2 token-causal
-  int tokens_per_frame;
-  int q_pos_offset, kv_pos_offset;
-  float scale;                     // softmax scale (1/sqrt(64) normally)
-} ddb_attn_bwd_noalloc_args;
+__attribute__((visibility("default"))) unsigned long long ddb_attn_bwd_noalloc_args_size(void) {
+  return sizeof(ddb_attn_bwd_noalloc_args);
+}
 
-enum {
-  kNoAllocOk = 0,
-  kNoAllocBadArgument = 1,
-  kNoAllocTooLarge = 2,
-  kNoAllocSetupFailed = 3,
-  kNoAllocLaunchFailed = 4,
-};
-
-// Backward of flash attention (bf16, d_head = 64) writing dq, dk, dv without allocating.
-// Returns 0 on success or one of the codes above; `stream` may be 0 (legacy stream).
 __attribute__((visibility("default"))) int ddb_attn_bwd_noalloc(
     const ddb_attn_bwd_noalloc_args* args, cudaStream_t stream) {
-  if (args == nullptr) return kNoAllocBadArgument;
+  if (args == nullptr) return DDB_NOALLOC_BAD_ARGUMENT;
   const ddb_attn_bwd_noalloc_args& x = *args;
   if (x.B <= 0 || x.H <= 0 || x.Tq <= 0 || x.S <= 0 || !x.q || !x.k || !x.v || !x.o ||
       !x.dout || !x.lse || !x.dq || !x.dk || !x.dv || x.tokens_per_frame < 1 ||
       x.q_rows_per_b < x.Tq || x.kv_rows_per_b < x.S) {
     fprintf(stderr, "ddb_attn_bwd_noalloc: invalid argument (null pointer or bad shape)\n");
-    return kNoAllocBadArgument;
+    return DDB_NOALLOC_BAD_ARGUMENT;
+  }
+  if (x.Tq % 128 != 0) {
+    fprintf(stderr, "ddb_attn_bwd_noalloc: queries per sample (%d) must be a multiple of 128\n",
+            x.Tq);
+    return DDB_NOALLOC_BAD_ARGUMENT;
+  }
+  // bound each factor by division first, so the products below cannot overflow
+  const long per_row = static_cast<long>(x.H) * 64;
+  if (x.q_rows_per_b > kNoAllocMaxDqFloats / per_row / x.B ||
+      x.Tq > kNoAllocMaxDeltaFloats / x.H / x.B) {
+    fprintf(stderr,
+            "ddb_attn_bwd_noalloc: problem too large for the static scratch: needs "
+            "batch*rows*heads*64 <= %ld and batch*heads*queries <= %ld (batch %d, heads %d, "
+            "rows per sample %lld, queries %d)\n",
+            kNoAllocMaxDqFloats, kNoAllocMaxDeltaFloats, x.B, x.H, x.q_rows_per_b, x.Tq);
+    return DDB_NOALLOC_TOO_LARGE;
   }
   const long q_rows = static_cast<long>(x.B) * x.q_rows_per_b;
-  const long dq_floats = q_rows * x.H * 64;
-  const long delta_floats = static_cast<long>(x.B) * x.H * x.Tq;
-  if (dq_floats > kNoAllocMaxDqFloats || delta_floats > kNoAllocMaxDeltaFloats) {
-    fprintf(stderr,
-            "ddb_attn_bwd_noalloc: problem too large for the static scratch: rows*heads*64 = "
-            "%ld (max %ld), batch*heads*queries = %ld (max %ld)\n",
-            dq_floats, kNoAllocMaxDqFloats, delta_floats, kNoAllocMaxDeltaFloats);
-    return kNoAllocTooLarge;
-  }
+  const long dq_floats = q_rows * per_row;
   ScratchPtrs sp;
   if (scratch_for_current_device(&sp) != 0) {
     fprintf(stderr, "ddb_attn_bwd_noalloc: cudaGetSymbolAddress failed on this device\n");
-    return kNoAllocSetupFailed;
+    return DDB_NOALLOC_SETUP_FAILED;
   }
   try {
     ddb::AttnBwdArgs g;
@@ -158,22 +119,43 @@ __attribute__((visibility("default"))) int ddb_attn_bwd_noalloc(
     a.scale = x.scale;
     g.dout = x.dout; g.lddo = x.lddo; g.do_col = x.do_col;
     g.delta = sp.delta;
-    g.dq_acc = sp.dq_acc; g.ld_dqacc = static_cast<long>(x.H) * 64;
+    g.dq_acc = sp.dq_acc; g.ld_dqacc = per_row;
     g.dk = x.dk; g.lddk = x.lddk; g.dk_col = x.dk_col;
     g.dv = x.dv; g.lddv = x.lddv; g.dv_col = x.dv_col;
-    if (cudaMemsetAsync(sp.dq_acc, 0, dq_floats * sizeof(float), stream) != cudaSuccess)
-      return kNoAllocLaunchFailed;
+    // the status word keeps the first error of a launch: clear what the last call left
+    if (cudaMemsetAsync(sp.status, 0, 8 * sizeof(int), stream) != cudaSuccess ||
+        cudaMemsetAsync(sp.dq_acc, 0, dq_floats * sizeof(float), stream) != cudaSuccess)
+      return DDB_NOALLOC_LAUNCH_FAILED;
     ddb::attn_bwd_delta(x.o, x.ldo, x.o_col, x.dout, x.lddo, x.do_col, sp.delta, x.B, x.H,
                         x.Tq, x.q_rows_per_b, stream);
     ddb::attn_bwd_with_status(g, sp.status, stream);
-    ddb::attn_dq_finalize(sp.dq_acc, g.ld_dqacc, x.dq, x.lddq, x.dq_col,
-                          static_cast<int>(q_rows), x.H, nullptr, 1, 0, stream);
-    if (cudaGetLastError() != cudaSuccess) return kNoAllocLaunchFailed;
+    // finalize each sample's Tq rows only: rows between samples belong to the caller
+    for (int b = 0; b < x.B; ++b) {
+      const long row0 = static_cast<long>(b) * x.q_rows_per_b;
+      ddb::attn_dq_finalize(sp.dq_acc + row0 * per_row, per_row,
+                            static_cast<__nv_bfloat16*>(x.dq) + row0 * x.lddq, x.lddq, x.dq_col,
+                            x.Tq, x.H, nullptr, 1, 0, stream);
+    }
+    if (cudaGetLastError() != cudaSuccess) return DDB_NOALLOC_LAUNCH_FAILED;
   } catch (const std::exception& e) {
     fprintf(stderr, "ddb_attn_bwd_noalloc: %s\n", e.what());
-    return kNoAllocLaunchFailed;
+    return DDB_NOALLOC_LAUNCH_FAILED;
   }
-  return kNoAllocOk;
+  return DDB_NOALLOC_OK;
+}
+
+__attribute__((visibility("default"))) int ddb_attn_bwd_noalloc_status(cudaStream_t stream,
+                                                                       int* device_status) {
+  if (device_status == nullptr) return DDB_NOALLOC_BAD_ARGUMENT;
+  ScratchPtrs sp;
+  if (scratch_for_current_device(&sp) != 0) return DDB_NOALLOC_SETUP_FAILED;
+  int v = 0;
+  if (cudaMemcpyAsync(&v, sp.status, sizeof(int), cudaMemcpyDeviceToHost, stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return DDB_NOALLOC_LAUNCH_FAILED;
+  *device_status = v;
+  return v == 0 ? DDB_NOALLOC_OK : DDB_NOALLOC_DEVICE_ERROR;
 }
 
 }  // extern "C"
