@@ -66,6 +66,35 @@ class RectifiedFlowSampler:
             x = x + dt * v
         return x
 
+    @torch.no_grad()
+    def ddim_sample(self, velocity_fn: Callable, z_init: torch.Tensor,
+                    num_steps: Optional[int] = None, eta: float = 0.0,
+                    t_start: float = 1.0, t_end: float = 0.0,
+                    generator: Optional[torch.Generator] = None) -> torch.Tensor:
+        """DDIM-style sampler in the flow-matching parameterisation (reference
+        ``RectifiedFlowSampler.ddim_sample``, blocks/flow_matching.py:283-314, whose
+        schedule runs t from 1 to 0 by default).
+
+        At each step the velocity gives both endpoint estimates, ``x1 = x + (1 - t) v``
+        (data) and ``x0 = x - t v`` (noise), and the state moves to the next time on the
+        straight path between them. With ``eta = 0`` that equals an Euler step of the
+        ODE. With ``eta > 0`` the noise estimate is partly replaced by fresh Gaussian
+        noise, ``x0 <- sqrt(1 - eta^2) x0 + eta * eps``, which keeps its variance (the
+        stochastic DDIM family of Song et al. 2021)."""
+        n = num_steps or self.num_steps
+        ts = torch.linspace(t_start, t_end, n + 1, device=z_init.device, dtype=torch.float64)
+        x = z_init
+        for i in range(n):
+            t, t_next = float(ts[i]), float(ts[i + 1])
+            v = velocity_fn(x, ts[i].to(z_init.dtype))
+            x1_hat = x + (1.0 - t) * v
+            x0_hat = x - t * v
+            if eta > 0.0:
+                eps = torch.randn(x.shape, device=x.device, dtype=x.dtype, generator=generator)
+                x0_hat = (1.0 - eta * eta) ** 0.5 * x0_hat + eta * eps
+            x = (1.0 - t_next) * x0_hat + t_next * x1_hat
+        return x
+
 
 class FlowMatchingLoss(torch.nn.Module):
     """Velocity MSE plus the reference's distillation target ``(z_{t+dt} - z_t)/dt``
