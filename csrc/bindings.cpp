@@ -40,7 +40,9 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor D, int64_t epi, bool a
           c10::optional<torch::Tensor> D2, c10::optional<torch::Tensor> rope_tab,
           int64_t rope_cols, int64_t rope_rows_per_seq, int64_t rope_pos_offset,
           int64_t rope_head_dim, c10::optional<torch::Tensor> gate,
-          int64_t gate_rows_per_group, int64_t splits, int64_t bn) {
+          int64_t gate_rows_per_group, int64_t splits, int64_t bn,
+          c10::optional<torch::Tensor> gb_counters, std::vector<int64_t> gb_peers,
+          int64_t gb_rank, int64_t gb_elem0, int64_t gb_shard, int64_t gb_epoch) {
   check_bf16(A, "A");
   check_bf16(B, "B");
   check_cuda_tensor(D, "D");
@@ -118,6 +120,22 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor D, int64_t epi, bool a
   }
   a.splits = splits;
   a.bn = bn;
+  if (gb_counters) {  // FSDP weight all-gather fused into the B loads
+    TORCH_CHECK(!b_t, "gemm: the fused weight gather reads a K-major B");
+    TORCH_CHECK(gb_counters->is_cuda() && gb_counters->scalar_type() == torch::kInt32 &&
+                    gb_counters->is_contiguous() && gb_counters->numel() >= (a.N + 127) / 128,
+                "gemm: gather counters must be int32 CUDA [ceil(N / 128)]");
+    TORCH_CHECK(!gb_peers.empty() && static_cast<int>(gb_peers.size()) <= ddb::kMaxGemmPeers,
+                "gemm: gather peer table");
+    a.gb_world = static_cast<int>(gb_peers.size());
+    a.gb_rank = static_cast<int>(gb_rank);
+    a.gb_elem0 = gb_elem0;
+    a.gb_shard = gb_shard;
+    a.gb_epoch = static_cast<unsigned>(gb_epoch);
+    a.gb_counters = reinterpret_cast<unsigned*>(gb_counters->data_ptr<int>());
+    for (size_t r = 0; r < gb_peers.size(); ++r)
+      a.gb_peers[r] = reinterpret_cast<const void*>(gb_peers[r]);
+  }
   ddb::gemm(a, static_cast<int>(epi), stream());
 }
 
@@ -683,7 +701,7 @@ void shard_adamw_allgather(torch::Tensor red, torch::Tensor master_local, torch:
                            int64_t world, int64_t off, int64_t len, int64_t decay_end,
                            c10::optional<torch::Tensor> norm_payloads, double max_norm, double lr,
                            double b1, double b2, double eps, double wd, double bc1, double bc2,
-                           double grad_scale) {
+                           double grad_scale, int64_t rank, int64_t local_end) {
   for (auto* t : {&red, &m, &v})
     TORCH_CHECK(t->scalar_type() == torch::kFloat32 && t->numel() >= len && t->is_contiguous(), "shard buffers");
   TORCH_CHECK(master_local.scalar_type() == torch::kFloat32 && master_local.numel() >= off + len, "master");
@@ -698,6 +716,7 @@ void shard_adamw_allgather(torch::Tensor red, torch::Tensor master_local, torch:
   if (norm_payloads) a.norm_payloads = norm_payloads->data_ptr<float>();
   a.max_norm = max_norm; a.lr = lr; a.b1 = b1; a.b2 = b2; a.eps = eps; a.wd = wd;
   a.bc1 = bc1; a.bc2 = bc2; a.grad_scale = grad_scale;
+  a.rank = static_cast<int>(rank); a.local_end = local_end;
   ddb::shard_adamw_allgather(a, stream());
 }
 

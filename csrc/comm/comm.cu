@@ -143,9 +143,14 @@ __global__ void __launch_bounds__(256) shard_adamw_kernel(ShardAdamWArgs a) {
     reinterpret_cast<float4*>(a.v)[i] = make_float4(va[0], va[1], va[2], va[3]);
     const float4 np = make_float4(pa[0], pa[1], pa[2], pa[3]);
     const uint2 nb = make_uint2(pack_bf16(pa[0], pa[1]), pack_bf16(pa[2], pa[3]));
-    for (int r = 0; r < a.world; ++r) {
-      *reinterpret_cast<float4*>(a.peer_master[r] + gi) = np;
-      *reinterpret_cast<uint2*>(a.peer_compute[r] + gi) = nb;
+    if (gi < a.local_end) {  // gathered by the consuming GEMM: own buffers only
+      *reinterpret_cast<float4*>(a.peer_master[a.rank] + gi) = np;
+      *reinterpret_cast<uint2*>(a.peer_compute[a.rank] + gi) = nb;
+    } else {
+      for (int r = 0; r < a.world; ++r) {
+        *reinterpret_cast<float4*>(a.peer_master[r] + gi) = np;
+        *reinterpret_cast<uint2*>(a.peer_compute[r] + gi) = nb;
+      }
     }
   }
   __threadfence_system();
@@ -174,7 +179,9 @@ void rs_sum_sqnorm(const float* const* peer_grads, int world, long off, long len
 }
 
 void shard_adamw_allgather(const ShardAdamWArgs& a, cudaStream_t s) {
-  if (a.len % 4 != 0 || a.off % 4 != 0) throw std::runtime_error("shard_adamw: 16-byte granularity");
+  if (a.len % 4 != 0 || a.off % 4 != 0 || a.local_end % 4 != 0)
+    throw std::runtime_error("shard_adamw: 16-byte granularity");
+  if (a.rank < 0 || a.rank >= a.world) throw std::runtime_error("shard_adamw: bad rank");
   shard_adamw_kernel<<<grid_for(a.len / 4), 256, 0, s>>>(a);
   count_launch();
 }

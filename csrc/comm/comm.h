@@ -41,13 +41,18 @@ struct ShardAdamWArgs {
   float* const* peer_master = nullptr; // device array [world] of full fp32 master buffers
   __nv_bfloat16* const* peer_compute = nullptr;  // device array [world] of bf16 copies
   int world = 1;
+  int rank = 0;
   long off = 0, len = 0, decay_end = 0;  // decay_end is a global element index
+  // elements below local_end (global index) are weights that their consuming GEMM
+  // all-gathers itself (weight-sharded mode): stored into this rank's buffers only
+  long local_end = 0;
   const float* norm_payloads = nullptr;  // [world] squared-norm partials (clipping), or null
   float max_norm = 0.f;
   float lr = 0, b1 = 0, b2 = 0, eps = 0, wd = 0, bc1 = 1, bc2 = 1, grad_scale = 1;
 };
 // AdamW on the shard; the updated fp32 and bf16 values are stored into every rank's
-// buffers at [off, off + len) (peer stores = the all-gather).
+// buffers at [off, off + len) (peer stores = the all-gather), except elements below
+// local_end, which go to this rank's buffers only.
 void shard_adamw_allgather(const ShardAdamWArgs& a, cudaStream_t s);
 
 }  // namespace ddb

@@ -188,6 +188,58 @@ __device__ __forceinline__ void record_status(int* status, int code) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
+// ---------------------------------------------------------------- fused weight all-gather
+constexpr long kGatherPieceElems = 8192;  // 16 KB of bf16 per gather work item
+constexpr int kGatherRows = 128;          // rows of B per readiness counter
+
+__device__ __forceinline__ int gather_pieces(const GemmArgs& a, int g) {
+  const long rows = min(kGatherRows, a.N - g * kGatherRows);
+  return static_cast<int>((rows * a.K + kGatherPieceElems - 1) / kGatherPieceElems);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Epilogue warps (128 threads, named barrier 1): copy the peer-owned pieces of this CTA's
+// gather items into the local copy of B, then count each finished item on its row group.
+__device__ void gather_weight_pieces(const GemmArgs& a, int tid) {
+  const int groups = (a.N + kGatherRows - 1) / kGatherRows;
+  const int ppg = static_cast<int>((static_cast<long>(kGatherRows) * a.K + kGatherPieceElems - 1) /
+                                   kGatherPieceElems);
+  const long total = static_cast<long>(groups) * ppg;
+  const long n_elems = static_cast<long>(a.N) * a.K;
+  uint4* local = reinterpret_cast<uint4*>(const_cast<void*>(a.B));
+  for (long item = blockIdx.x; item < total; item += gridDim.x) {
+    const int g = static_cast<int>(item / ppg);
+    const int q = static_cast<int>(item % ppg);
+    // the last row group may hold fewer pieces; the same for all 128 threads, so the
+    // named barrier below stays uniform, and only real pieces are counted
+    if (q >= gather_pieces(a, g)) continue;
+    const long group_end = min(n_elems, static_cast<long>(g + 1) * kGatherRows * a.K);
+    long e = static_cast<long>(g) * kGatherRows * a.K + q * kGatherPieceElems;
+    const long e_end = min(group_end, e + kGatherPieceElems);
+    while (e < e_end) {  // split the piece at shard (owner) boundaries
+      const long flat = a.gb_elem0 + e;
+      const int owner = static_cast<int>(flat / a.gb_shard);
+      const long seg_end = min(e_end, (owner + 1) * a.gb_shard - a.gb_elem0);
+      if (owner != a.gb_rank) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.gb_peers[owner]);
+        for (long v = e / 8 + tid; v < seg_end / 8; v += 128) local[v] = src[v];
+      }
+      e = seg_end;
+    }
+    __threadfence();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (tid == 0) {
+      fence_proxy_async_global();
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.gb_counters + g) : "memory");
+    }
+  }
+}
+
 // ---------------------------------------------------------------- epilogue ops
 template <int EPI>
 __device__ __forceinline__ void epi_chunk32(const GemmArgs& a, int row, int col0,
@@ -460,10 +512,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
+      uint64_t ready = 0;  // row groups (< 64) whose gathered B this CTA has acquired
       for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
         int m0, nt, kb0, kb1, bt;
         if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
         const int n0 = nt * BN;
+        if (args.gb_world > 1) {  // this tile's B rows must have landed locally
+          const int g_end = min((n0 + BN + kGatherRows - 1) / kGatherRows,
+                                (args.N + kGatherRows - 1) / kGatherRows);
+          for (int g = n0 / kGatherRows; g < g_end && ok; ++g) {
+            if (g < 64 && ((ready >> g) & 1)) continue;
+            const unsigned target = args.gb_epoch * static_cast<unsigned>(gather_pieces(args, g));
+            const long long t0 = clock64();
+            while (static_cast<int>(ld_acquire_gpu_u32(args.gb_counters + g) - target) < 0) {
+              if (*abort_flag || clock64() - t0 > kSpinLimitCycles) {
+                ok = false;
+                break;
+              }
+              __nanosleep(64);
+            }
+            if (g < 64) ready |= 1ull << g;
+          }
+          fence_proxy_async_global();  // generic-proxy stores of the gather -> TMA reads
+          if (!ok) break;
+        }
         const int ab = sched.grouped ? 0 : bt;        // A batch coordinate
         const int bb = sched.grouped == 2 ? 0 : bt;   // B batch coordinate
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -606,6 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
       }
     };
+    if (args.gb_world > 1) gather_weight_pieces(args, threadIdx.x - 64);
     prefetch_c(blockIdx.x);
     for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
       int m0, nt, kb0, kb1, bt;
@@ -925,6 +998,18 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
     s.total = s.tiles_m * s.tiles_n * a.batch;
   } else {
     s.total = s.tiles_m * s.tiles_n * s.splits * (a.batch > 1 ? a.batch : 1);
+  }
+  if (a.gb_world > 1) {
+    if (a.b_mn_major || a.batch > 1 || a.grouped || a.ldb != a.K || a.K % 8 != 0)
+      throw std::runtime_error("gemm: the fused weight gather needs an unbatched K-major B with ldb == K");
+    if (a.gb_world > kMaxGemmPeers || a.gb_rank < 0 || a.gb_rank >= a.gb_world ||
+        a.gb_peers[a.gb_rank] != a.B || a.gb_counters == nullptr || a.gb_epoch == 0 ||
+        a.gb_shard <= 0 || a.gb_shard % 8 != 0 || a.gb_elem0 % 8 != 0 ||
+        a.gb_elem0 + static_cast<long>(a.N) * a.K > a.gb_shard * a.gb_world)
+      throw std::runtime_error("gemm: bad fused weight-gather arguments");
+    for (int r = 0; r < a.gb_world; ++r)
+      if (a.gb_peers[r] == nullptr || (reinterpret_cast<uintptr_t>(a.gb_peers[r]) & 15) != 0)
+        throw std::runtime_error("gemm: weight-gather peer pointers must be 16-byte aligned");
   }
   if (a.batch > 1 && ((a.grouped == 0 && a.stride_a % 8 != 0) ||
                       (a.grouped != 2 && a.stride_b % 8 != 0)))

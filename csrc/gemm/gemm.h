@@ -71,6 +71,24 @@ struct GemmArgs {
   void* const* d_peers = nullptr;
   int d_rows_per_peer = 0;
   int d_slot = 0;
+  // FSDP parameter all-gather fused into the B (weight) loads. B is a K-major [N][K]
+  // weight (ldb == K) inside a flat parameter buffer that is sharded over gb_world ranks
+  // in contiguous ranges of gb_shard elements; B[0][0] is flat element gb_elem0, and
+  // gb_peers[r] is B's address in rank r's copy of the buffer (gb_peers[gb_rank] == B,
+  // a CUDA-IPC mapping for the others). Before its first tile, every CTA's epilogue warps
+  // copy their share of B's peer-owned pieces into this rank's copy (plain 16-byte P2P
+  // loads, local stores) and publish one counter per 128-row group of B
+  // (red.release.gpu); the TMA producer acquires the counters of a tile's row groups
+  // (bounded wait) before it loads that tile's B. gb_counters [ceil(N / 128)] start at
+  // zero and are never reset: launch number gb_epoch (1, 2, ...) waits for gb_epoch x the
+  // pieces of a group. No TMA ever reads peer memory here.
+  int gb_world = 0;
+  int gb_rank = 0;
+  long gb_elem0 = 0;
+  long gb_shard = 0;
+  const void* gb_peers[kMaxGemmPeers] = {};
+  unsigned* gb_counters = nullptr;
+  unsigned gb_epoch = 0;
   int splits = 1;           // split-K factor (kEpiF32Atomic only)
   int bn = 0;               // 0 = auto (128 or 256)
   int max_ctas = 0;         // 0 = all SMs

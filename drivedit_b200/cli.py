@@ -35,7 +35,8 @@ def _train(a) -> int:
     from .config import get_config
     from .data.synthetic import make_batch
     from .models.world_dit import WorldDiT
-    from .training.distributed import CheckpointManager
+    from .config import to_dict
+    from .training.checkpoint import load_distributed, save_distributed
     from .training.trainer import WorldModelTrainer
     from .utils.observability import MetricsLogger
 
@@ -56,21 +57,18 @@ def _train(a) -> int:
     torch.manual_seed(cfg.train.seed)
     model = WorldDiT(cfg.model)
     tr = WorldModelTrainer(model, cfg.train, dev, process_group=dist.group.WORLD if ws > 1 else None)
-    ckpt = CheckpointManager(a.out, keep_checkpoints=3, rank=rank, world_size=ws)
+    ckdir = str(Path(a.out) / "checkpoints")
     start = 0
-    if a.resume:
-        p = ckpt._get_latest_checkpoint()
-        if p:
-            ck = torch.load(p, map_location="cpu", weights_only=False)
-            tr.load_state_dict(ck["config"]["trainer_state"]) if ck.get("config") and "trainer_state" in ck["config"] \
-                else model.load_state_dict(ck["model_state_dict"])
-            start = int(ck["step"])
+    if a.resume:  # per-rank files: sharded optimizer state, each rank's experts, RNG
+        start = load_distributed(tr, ckdir) or 0
     log = MetricsLogger(a.out, rank, ws, config={"preset": a.config, "overrides": a.override})
-    gen = torch.Generator().manual_seed(1000 + rank)
     rgb = cfg.train.frames if cfg.model.repa is not None else 0
     tokens = cfg.train.batch_per_gpu * cfg.train.frames * cfg.model.tokens_per_frame
     t0 = time.perf_counter()
     for step in range(start, a.steps):
+        # the synthetic stream is a function of (step, rank), so a resumed run sees the
+        # same batches as an uninterrupted one
+        gen = torch.Generator().manual_seed(1000 + 7919 * step + rank)
         batch = make_batch(cfg, generator=gen, pin=cuda, rgb_frames=rgb).to(dev, non_blocking=True)
         loss = tr.train_step(batch)
         if (step + 1) % a.log_every == 0:
@@ -81,8 +79,7 @@ def _train(a) -> int:
             log.log(step + 1, {"loss": float(loss), "tok_per_s": ws * tokens * a.log_every / dt,
                                **{k: float(v) for k, v in tr.last_losses.items()}})
         if a.ckpt_every and (step + 1) % a.ckpt_every == 0:
-            ckpt.save_checkpoint(model, None, None, 0, step + 1, float(loss),
-                                 config={"trainer_state": tr.state_dict()} if ws == 1 else None)
+            save_distributed(tr, ckdir, step + 1, config=to_dict(cfg))
     if ws > 1:
         dist.barrier()
         if tr.engine is not None:

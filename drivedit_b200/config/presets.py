@@ -123,6 +123,9 @@ class TrainConfig:
     t_sampling: str = "logit_normal"  # "logit_normal" | "uniform"
     parallel: str = "dp"            # "dp" | "fsdp" | "fsdp_ep"
     fused_collectives: bool = True
+    # FULL_SHARD for the block GEMM weights: each forward GEMM all-gathers its weight's
+    # peer-owned pieces itself (fused transport); the optimizer keeps them rank-local
+    shard_weights: bool = False
 
 
 @dataclass

@@ -48,15 +48,24 @@ class BlockCtx:
         self.rope_pos_offset = rope_pos_offset
 
 
+def _gather_of(W):
+    """The fused weight all-gather handle lookup of a weight-sharded group (or none)."""
+    fn = getattr(getattr(W, "__self__", None), "gather_for", None)
+    return fn if fn is not None else (lambda p: None)
+
+
 def _attn_forward(x, mod, blk, W, bc):
     d = bc.d
+    G = _gather_of(W)
     h1, r1 = adaln_rmsnorm(x, blk.norm1.weight, mod, 0, d, bc.tpf)
     qkv = gemm(h1, W(blk.attn.qkv.weight), epi="rope", rope_tab=bc.rope_tab, rope_cols=2 * d,
-               rope_rows_per_seq=bc.T, rope_pos_offset=bc.rope_pos_offset, rope_head_dim=bc.Dh)
+               rope_rows_per_seq=bc.T, rope_pos_offset=bc.rope_pos_offset, rope_head_dim=bc.Dh,
+               gather=G(blk.attn.qkv.weight))
     o, o_lin, lse, aux = attention_fwd(qkv, bc)
-    x1 = gemm(o, W(blk.attn.proj.weight), residual=x)
+    x1 = gemm(o, W(blk.attn.proj.weight), residual=x, gather=G(blk.attn.proj.weight))
     if o_lin is not None:
-        gemm(o_lin, W(blk.attn.proj_lin.weight), x1, residual=x1)
+        gemm(o_lin, W(blk.attn.proj_lin.weight), x1, residual=x1,
+             gather=G(blk.attn.proj_lin.weight))
     return x1, dict(x=x, h1=h1, r1=r1, qkv=qkv, o=o, o_lin=o_lin, lse=lse, aux=aux)
 
 
@@ -80,12 +89,13 @@ def _attn_backward(dx1, sa, blk, W, bc, mod, dmod):
 
 def _mlp_forward(x1, mod, blk, W, bc):
     d = bc.d
+    G = _gather_of(W)
     h2, r2 = adaln_rmsnorm(x1, blk.norm2.weight, mod, 2 * d, 3 * d, bc.tpf)
     w13 = W(blk.mlp.w13.weight)
     gu = torch.empty(x1.shape[0], w13.shape[0], device=x1.device, dtype=torch.bfloat16)
     a = torch.empty(x1.shape[0], w13.shape[0] // 2, device=x1.device, dtype=torch.bfloat16)
-    gemm(h2, w13, gu, epi="swiglu", out2=a)
-    x2 = gemm(a, W(blk.mlp.w3.weight), residual=x1)
+    gemm(h2, w13, gu, epi="swiglu", out2=a, gather=G(blk.mlp.w13.weight))
+    x2 = gemm(a, W(blk.mlp.w3.weight), residual=x1, gather=G(blk.mlp.w3.weight))
     return x2, dict(x1=x1, h2=h2, r2=r2, gu=gu, a=a)
 
 

@@ -55,7 +55,11 @@ def gemm(
     gate_rows_per_group: int = 1,
     splits: int = 0,
     bn: int = 0,
+    gather=None,
 ) -> torch.Tensor:
+    """``gather``: a :class:`WeightGather` handle when ``b`` is a sharded weight whose
+    peer-owned pieces this GEMM all-gathers into the local buffer before using them
+    (FSDP all-gather fused with the consuming GEMM)."""
     M = a.shape[1] if a_t else a.shape[0]
     N = b.shape[1] if b_t else b.shape[0]
     if out is None:
@@ -69,9 +73,13 @@ def gemm(
             out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
     if epi == "swiglu" and out2 is None:
         out2 = torch.empty(M, N // 2, device=a.device, dtype=torch.bfloat16)
+    if gather is not None:
+        g = gather.launch_args(b)
+    else:
+        g = (None, [], 0, 0, 0, 0)
     ext().gemm(
         a, b, out, EPI[epi], a_t, b_t, residual, bias, out2, rope_tab, rope_cols,
         rope_rows_per_seq, rope_pos_offset, rope_head_dim, gate, gate_rows_per_group,
-        splits, bn,
+        splits, bn, *g,
     )
     return out

@@ -11,6 +11,17 @@ which is FSDP's SHARD_GRAD_OP schedule (reference ``training/cuda_optimized.py:5
 with weights kept gathered between steps, because HBM is not the constraint at these
 model sizes (DiT-B: 0.5 GB of fp32 master per rank).
 
+``weight_gather=True`` (fused transport) switches the block GEMM weights (attention
+QKV / output / linear-branch projections, SwiGLU W13 / W3) to FULL_SHARD's schedule: the
+optimizer stores their updated shard only into its own rank's buffers, and each
+forward GEMM that consumes one of these weights first all-gathers the peer-owned pieces
+into the local buffer from inside the GEMM kernel (``GemmArgs.gb_*`` in
+``csrc/gemm/gemm.cu``): the parameter all-gather fused with the first GEMM that reads
+it, tile by tile, with no separate collective launch. The backward GEMMs read the
+gathered copy. These weights form a contiguous prefix of the flat buffer, so the
+optimizer needs one boundary (``local_end``). :meth:`ShardedDataParallel.gather_weights`
+materialises the full weights (fp32 and bf16) for checkpointing or inference.
+
 Two transports:
 
 ``fused`` (default on CUDA)
@@ -26,7 +37,8 @@ Two transports:
 from __future__ import annotations
 
 import math
-from typing import Optional, Sequence
+import re
+from typing import Dict, Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -73,12 +85,37 @@ class SymmetricBuffer:
         self.peers = []
 
 
+GATHERED_WEIGHT = re.compile(r"^blocks\.\d+\.(attn\.(qkv|proj|proj_lin)|mlp\.(w13|w3))\.weight$")
+
+
+class WeightGather:
+    """Launch state of one weight's fused all-gather: its flat offset, its address in
+    every rank's bf16 buffer, the per-128-row readiness counters and the launch epoch."""
+
+    def __init__(self, engine: "ShardedDataParallel", name: str, param: nn.Parameter):
+        off, numel = engine.flat.offsets[name]
+        self.name = name
+        self.elem0 = off
+        self.numel = numel
+        self.rank, self.shard = engine.rank, engine.shard_len
+        self.peers = [int(p) + 2 * off for p in engine.sym["compute"].peers]
+        rows = param.shape[0]
+        self.counters = torch.zeros((rows + 127) // 128, dtype=torch.int32, device=engine.device)
+        self.epoch = 0
+
+    def launch_args(self, b: torch.Tensor):
+        if b.data_ptr() != self.peers[self.rank] or b.numel() != self.numel:
+            raise RuntimeError(f"fused weight gather: {self.name} is not the registered view")
+        self.epoch += 1
+        return self.counters, self.peers, self.rank, self.elem0, self.shard, self.epoch
+
+
 class ShardedDataParallel:
     """Owns the flat buffers of a model and performs the sharded optimizer step."""
 
     def __init__(self, model: nn.Module, group=None, device=None, transport: Optional[str] = None,
                  lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, grad_clip=1.0,
-                 local_params: Optional[Sequence[str]] = None):
+                 local_params: Optional[Sequence[str]] = None, weight_gather: bool = False):
         """``local_params``: names of rank-local parameters (expert-parallel experts).
         They are neither reduced nor sharded: a local flat group with a full AdamW holds
         them, their squared gradient norm joins the global clipping norm, and the main
@@ -92,6 +129,10 @@ class ShardedDataParallel:
         named_all = list(model.named_parameters())
         local = set(local_params or [])
         named = [(n, p) for n, p in named_all if n not in local]
+        self.weight_gather = bool(weight_gather) and self.transport == "fused" and self.world > 1
+        if self.weight_gather:  # gathered weights first: a contiguous prefix of the flat buffer
+            named = ([(n, p) for n, p in named if GATHERED_WEIGHT.match(n)]
+                     + [(n, p) for n, p in named if not GATHERED_WEIGHT.match(n)])
         no_decay = model.no_decay_names() if hasattr(model, "no_decay_names") else []
         pad = ALIGN * self.world * 4
         self.sym = {}
@@ -109,6 +150,8 @@ class ShardedDataParallel:
                 return bufs[name].tensor(n, dtype)
         self.flat = FlatParamGroup(named, self.device, no_decay=no_decay, pad_to=self.world * 4,
                                    allocator=alloc)
+        self.local_end = 0
+        self.gathers: Dict[int, WeightGather] = {}
         self.local_opt = None
         if local:
             from ..training.optim import FlatAdamW
@@ -121,6 +164,14 @@ class ShardedDataParallel:
         assert n % (self.world * 4) == 0
         self.shard_len = n // self.world
         self.shard_off = self.rank * self.shard_len
+        if self.weight_gather:
+            for n, p in named:
+                if GATHERED_WEIGHT.match(n):
+                    o, k = self.flat.offsets[n]
+                    self.local_end = max(self.local_end, o + k)
+                    self.gathers[id(p)] = WeightGather(self, n, p)
+            self.local_end = (self.local_end + 3) // 4 * 4
+            self.flat.gather_for = lambda p: self.gathers.get(id(p))
         self.m = torch.zeros(self.shard_len, device=self.device)
         self.v = torch.zeros(self.shard_len, device=self.device)
         self.red = torch.zeros(self.shard_len, device=self.device)
@@ -171,7 +222,8 @@ class ShardedDataParallel:
             self.red, self.flat.master, self.m, self.v, self.sym["master"].table,
             self.sym["compute"].table, self.world, self.shard_off, self.shard_len,
             self.flat.decay_end, pay if self.grad_clip > 0 else None, float(self.grad_clip),
-            self.lr, self.betas[0], self.betas[1], self.eps, self.wd, bc1, bc2, scale)
+            self.lr, self.betas[0], self.betas[1], self.eps, self.wd, bc1, bc2, scale,
+            self.rank, self.local_end)
         if self.local_opt is not None:
             self._local_step(scale, pay.sum() if self.grad_clip > 0 else None)
         self._barrier()                                   # all peers' stores have landed
@@ -211,6 +263,29 @@ class ShardedDataParallel:
         and global clipping norm as the sharded update."""
         self.local_opt.step_count = self.step_count - 1
         self.local_opt.step(grad_scale=scale, sq_norm=sq_norm)
+
+    def gather_weights(self):
+        """Weight-sharded mode: copy every rank's shard of the GEMM-gathered weights
+        (fp32 master and bf16) into all buffers, so the full weights are resident (before
+        ``state_dict`` / checkpointing / inference). Collective: every rank calls it."""
+        if not self.weight_gather or self.local_end == 0:
+            return
+        from ..ops._ext import ext
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        S = self.shard_len
+        for r in range(self.world):
+            lo, hi = r * S, min((r + 1) * S, self.local_end)
+            if r == self.rank or hi <= lo:
+                continue
+            for kind, es in (("master", 4), ("compute", 2)):
+                src = ext().tensor_from_ptr(self.sym[kind].peers[r] + lo * es, hi - lo,
+                                            torch.float32 if es == 4 else torch.bfloat16,
+                                            self.device.index)
+                (self.flat.master if es == 4 else self.flat.compute)[lo:hi].copy_(src)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
     def close(self):
         for b in self.sym.values():

@@ -55,7 +55,8 @@ class WorldModelTrainer:
                 local = model.enable_expert_parallel(self.ep)
             self.engine = ShardedDataParallel(model, process_group, self.device, transport,
                                               cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
-                                              cfg.grad_clip, local_params=local)
+                                              cfg.grad_clip, local_params=local,
+                                              weight_gather=getattr(cfg, "shard_weights", False))
             self.group = self.engine.flat
             self.opt = None
         else:
@@ -142,6 +143,8 @@ class WorldModelTrainer:
             self.ep.close()
 
     def state_dict(self) -> Dict:
+        if self.engine is not None:
+            self.engine.gather_weights()   # weight-sharded mode: materialise full weights
         opt = self.opt.state_dict() if self.opt is not None else {
             "m": self.engine.m, "v": self.engine.v, "step": self.engine.step_count}
         if self.engine is not None and self.engine.local_opt is not None:

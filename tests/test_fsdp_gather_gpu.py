@@ -1,0 +1,86 @@
+"""FULL_SHARD for the block GEMM weights on 2 GPUs: each forward GEMM all-gathers its
+weight's peer-owned pieces itself (the all-gather fused with the consuming GEMM). Three
+training steps (no clipping, so every reduction is elementwise) must give bit-identical
+losses and weights to the weight-replicated
+fused engine, and every rank must end with the full weights after ``gather_weights``."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    from drivedit_b200.config import get_config
+    from drivedit_b200.data.synthetic import make_batch
+    from drivedit_b200.models.world_dit import WorldDiT
+    from drivedit_b200.ops._ext import check_device_status
+    from drivedit_b200.training.trainer import WorldModelTrainer
+
+    out = {}
+    for shard in (False, True):
+        cfg = get_config("tiny", ["train.dtype=bf16", "model.attention=sla", "model.latent_h=32",
+                                  "model.latent_w=32", "train.grad_clip=0",
+                                  f"train.shard_weights={shard}"])
+        torch.manual_seed(0)
+        model = WorldDiT(cfg.model)
+        tr = WorldModelTrainer(model, cfg.train, torch.device("cuda", rank),
+                               process_group=dist.group.WORLD)
+        assert tr.engine.weight_gather == shard
+        if shard:
+            assert tr.engine.local_end > tr.engine.shard_len  # the gathered prefix spans ranks
+        gen = torch.Generator().manual_seed(7 + rank)
+        losses = []
+        for _ in range(3):
+            b = make_batch(cfg, device=torch.device("cuda", rank), generator=gen)
+            losses.append(float(tr.train_step(b)))
+        sd = tr.state_dict()["model"]
+        torch.cuda.synchronize()
+        check_device_status()
+        out[shard] = (losses, {k: v.detach().cpu().clone() for k, v in sd.items()},
+                      tr.engine.flat.compute.float().cpu().clone())
+        tr.close()
+    q.put((rank, out))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_weight_gather_training_matches_replicated_weights():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert res[r][True][0] == res[r][False][0], (r, res[r][True][0], res[r][False][0])
+        for k, v in res[r][False][1].items():
+            assert torch.equal(res[r][True][1][k], v), (r, k)
+    for k in res[0][True][1]:
+        assert torch.equal(res[0][True][1][k], res[1][True][1][k]), k
+    # after gather_weights both ranks hold the same full bf16 weights
+    assert torch.equal(res[0][True][2], res[1][True][2])

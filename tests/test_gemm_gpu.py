@@ -117,3 +117,69 @@ def test_status_clean():
     from drivedit_b200.ops._ext import device_status
     torch.cuda.synchronize()
     assert device_status() == 0
+
+
+class _Gather:
+    """Launch arguments of the fused weight gather for a B emulated as sharded over
+    ``world`` ranks whose buffers all live on this GPU."""
+
+    def __init__(self, bufs, rank, elem0, shard, rows):
+        self.bufs, self.rank, self.elem0, self.shard = bufs, rank, elem0, shard
+        self.counters = torch.zeros((rows + 127) // 128, dtype=torch.int32, device="cuda")
+        self.epoch = 0
+
+    def launch_args(self, b):
+        self.epoch += 1
+        peers = [buf.data_ptr() + 2 * self.elem0 for buf in self.bufs]
+        assert peers[self.rank] == b.data_ptr()
+        return self.counters, peers, self.rank, self.elem0, self.shard, self.epoch
+
+
+@pytest.mark.parametrize("world,rank,N,K,epi", [(2, 0, 768, 256, "bf16"), (4, 2, 2304, 768, "rope"),
+                                                 (8, 5, 1536, 512, "swiglu"), (3, 1, 640, 3072, "bf16")])
+def test_gemm_fused_weight_gather(world, rank, N, K, epi):
+    """B lives at flat offset elem0 of a buffer sharded over `world` ranks; the local
+    copy holds garbage outside this rank's shard, the other ranks' copies hold the
+    truth for their shards. The GEMM must gather B (restoring the local copy exactly)
+    and match a GEMM on the true weight, on two launches in a row."""
+    from drivedit_b200.ops._ext import check_device_status
+    from drivedit_b200.ops.gemm import gemm
+
+    torch.manual_seed(world * 10 + rank)
+    M = 1024
+    elem0 = 512
+    total = elem0 + N * K + 1024
+    shard = -(-total // (world * 256)) * 256
+    truth = (torch.randn(world * shard, device="cuda") * 0.05).bfloat16()
+    bufs = []
+    for r in range(world):
+        b = torch.full_like(truth, float("nan"))
+        b[r * shard:(r + 1) * shard] = truth[r * shard:(r + 1) * shard]
+        bufs.append(b)
+    W_true = truth[elem0:elem0 + N * K].view(N, K)
+    W_local = bufs[rank][elem0:elem0 + N * K].view(N, K)
+    g = _Gather(bufs, rank, elem0, shard, N)
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    kw = {}
+    if epi == "rope":
+        from drivedit_b200.layers.rope import rope_angles_3d, rope_table
+
+        kw = dict(rope_tab=rope_table(rope_angles_3d(64, 4, 8, 32)).cuda(), rope_cols=1024,
+                  rope_rows_per_seq=M, rope_head_dim=64)
+    for call in range(2):
+        if call == 1:  # the peers' shards changed (an optimizer step) and are gathered again
+            truth.mul_(1.5)
+            for r in range(world):
+                if r != rank:
+                    bufs[r][r * shard:(r + 1) * shard] = truth[r * shard:(r + 1) * shard]
+            bufs[rank][rank * shard:(rank + 1) * shard] = truth[rank * shard:(rank + 1) * shard]
+        if epi == "swiglu":
+            out = gemm(x, W_local, epi="swiglu", gather=g)
+            ref = gemm(x, W_true.contiguous(), epi="swiglu")
+        else:
+            out = gemm(x, W_local, epi=epi, gather=g, **kw)
+            ref = gemm(x, W_true.contiguous(), epi=epi, **kw)
+        torch.cuda.synchronize()
+        check_device_status()
+        assert torch.equal(W_local, W_true), f"call {call}: local copy not restored"
+        assert torch.equal(out, ref), f"call {call}: differs from the GEMM on the gathered weight"
