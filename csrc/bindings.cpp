@@ -147,10 +147,18 @@ int64_t read_status() {
                   "read status");
   return v;
 }
+int64_t read_status_index() {
+  int dev = 0;
+  ddb::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  int v[2] = {0, 0};
+  ddb::check_cuda(cudaMemcpy(v, ddb::device_status(dev), sizeof(v), cudaMemcpyDeviceToHost),
+                  "read status");
+  return v[1];
+}
 void reset_status() {
   int dev = 0;
   ddb::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  ddb::check_cuda(cudaMemset(ddb::device_status(dev), 0, sizeof(int)), "reset status");
+  ddb::check_cuda(cudaMemset(ddb::device_status(dev), 0, 2 * sizeof(int)), "reset status");
 }
 
 // ------------------------------------------------------------------ fused norm
@@ -846,7 +854,8 @@ torch::Tensor moe_dispatch(torch::Tensor x, torch::Tensor topk_idx, torch::Tenso
   ddb::moe_dispatch(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), N, x.size(1), k,
                     ns, E, topk_idx.data_ptr<int>(), seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
                     cursor.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()),
-                    xp.stride(0), slot_of.data_ptr<int>(), stream(), p2, ld2, zero_routed_pad);
+                    xp.stride(0), slot_of.data_ptr<int>(), stream(), p2, ld2, zero_routed_pad,
+                    xp.size(0), xp2 ? xp2->size(0) : 0);
   return slot_of;
 }
 
@@ -869,12 +878,14 @@ ddb::MoeCombineArgs combine_args(torch::Tensor topk_w, torch::Tensor shared_w, t
   a.topk_w = topk_w.data_ptr<float>(); a.shared_w = shared_w.data_ptr<float>();
   a.slot_of = slot_of.data_ptr<int>();
   a.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()); a.ld_y = y.stride(0);
+  a.y_rows = y.size(0);
   if (y2) {
     check_bf16(*y2, "y2");
     check_rows(*y2, "y2");
     TORCH_CHECK(y2->size(1) == y.size(1), "y2 width");
     a.y2 = reinterpret_cast<const __nv_bfloat16*>(y2->data_ptr());
     a.ld_y2 = y2->stride(0);
+    a.y2_rows = y2->size(0);
   }
   return a;
 }
@@ -937,7 +948,8 @@ torch::Tensor moe_unpermute(torch::Tensor dxp, torch::Tensor slot_of, int64_t N,
   auto dx = torch::empty({N, dxp.size(1)}, dxp.options());
   ddb::moe_unpermute(reinterpret_cast<const __nv_bfloat16*>(dxp.data_ptr()), dxp.stride(0),
                      slot_of.data_ptr<int>(), N, slot_of.size(1), dxp.size(1),
-                     reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), stream(), k, p2, ld2);
+                     reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), stream(), k, p2, ld2,
+                     dxp.size(0), dxp2 ? dxp2->size(0) : 0);
   return dx;
 }
 
@@ -1366,6 +1378,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("shared_w") = py::none(), py::arg("slot_s") = py::none(), py::arg("ys") = py::none());
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
   m.def("read_status", &read_status, "device status word (0 = ok)");
+  m.def("read_status_index", &read_status_index, "index recorded with a bad-index status");
+  m.def("set_deterministic", &ddb::set_deterministic, "fixed-order MoE permutation on/off");
+  m.def("deterministic", &ddb::deterministic, "fixed-order MoE permutation enabled");
+  m.def("set_check_bounds", &ddb::set_check_bounds, "bounds-checked index kernels on/off");
+  m.def("check_bounds", &ddb::check_bounds, "bounds-checked index kernels enabled");
   m.def("launch_count", &ddb::launch_count, "kernels launched by this extension so far");
   m.def("reset_status", &reset_status, "clear the device status word");
   m.def("adaln_fwd", &adaln_fwd, "fused AdaLN-RMSNorm forward -> (h, rstd)");

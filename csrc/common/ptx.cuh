@@ -25,7 +25,13 @@ enum DeviceStatus : int {
   kStatusTimeoutEpilogue = 3,
   kStatusTimeoutPeer = 4,
   kStatusBadArgument = 5,
+  kStatusBadIndex = 6,  // bounds-checking mode: a table index out of range (skipped)
 };
+
+// Bounds-checking mode: record the first bad index (code in word 0, index in word 1).
+__device__ __forceinline__ void record_bad_index(int* status, long index) {
+  if (status && atomicCAS(status, 0, kStatusBadIndex) == 0) status[1] = static_cast<int>(index);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

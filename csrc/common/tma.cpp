@@ -110,7 +110,13 @@ CUtensorMap make_tmap_nd(const void* base, CUtensorMapDataType dtype, int elem_b
 
 namespace {
 std::atomic<long> g_launches{0};
+std::atomic<bool> g_deterministic{false};
+std::atomic<bool> g_check_bounds{false};
 }
+void set_deterministic(bool on) { g_deterministic.store(on); }
+bool deterministic() { return g_deterministic.load(); }
+void set_check_bounds(bool on) { g_check_bounds.store(on); }
+bool check_bounds() { return g_check_bounds.load(); }
 void count_launch(long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 

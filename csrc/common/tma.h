@@ -34,8 +34,22 @@ int num_sms(int device);
 void count_launch(long n = 1);
 long launch_count();
 
-// Per-device status word written by kernels whose bounded waits ran out.
+// Per-device status word written by kernels whose bounded waits ran out (and, in the
+// bounds-checking mode, by kernels that met an out-of-range index).
 int* device_status(int device);
+
+// Process-wide debug switches (off by default; read by the kernels' host launchers).
+//  deterministic: index-driven permutations (the MoE dispatch) assign rows in a fixed
+//                 order instead of by atomic arrival, so every reduction over them is
+//                 bit-reproducible run to run;
+//  check_bounds:  index-driven kernels check every table-derived index against the
+//                 extent of the buffer it addresses; an index out of range is recorded
+//                 in the status word (kStatusBadIndex, and the index in word 1) and the
+//                 access is skipped instead of faulting.
+void set_deterministic(bool on);
+bool deterministic();
+void set_check_bounds(bool on);
+bool check_bounds();
 
 inline void check_cuda(cudaError_t e, const char* what) {
   if (e != cudaSuccess)

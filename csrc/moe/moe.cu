@@ -150,12 +150,45 @@ __global__ void moe_plan_kernel(const int* __restrict__ counts, int E, int ns, i
   *total_mtiles = nt;
 }
 
+// Deterministic slot assignment (one block per routed expert): the routes to expert e
+// get the rows of e's segment in (token, route) order, a stable counting sort, so the
+// permuted layout and every reduction over it repeat bit for bit.
+__global__ void __launch_bounds__(1024) moe_slots_stable_kernel(const int* __restrict__ topk_idx,
+                                                                long NK, int k, int R,
+                                                                const int* __restrict__ seg_start,
+                                                                int* __restrict__ slot_of) {
+  __shared__ int warp_cnt[32];
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int base = seg_start[e];
+  for (long c0 = 0; c0 < NK; c0 += blockDim.x) {
+    const long i = c0 + threadIdx.x;
+    const bool mine = i < NK && topk_idx[i] == e;
+    const unsigned m = __ballot_sync(0xffffffffu, mine);
+    if (lane == 0) warp_cnt[w] = __popc(m);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int q = 0; q < nw; ++q) {
+      const int c = warp_cnt[q];
+      before += q < w ? c : 0;
+      total += c;
+    }
+    if (mine) {
+      const long t = i / k, j = i % k;
+      slot_of[t * R + j] = base + before + __popc(m & ((1u << lane) - 1u));
+    }
+    base += total;
+    __syncthreads();
+  }
+}
+
 // One warp per (token, route). Routes j < k are the top-k experts, j >= k the shared ones.
+// fixed_slots: routed slots already assigned (deterministic mode); check: bounds mode.
 __global__ void __launch_bounds__(256) moe_dispatch_kernel(
     const __nv_bfloat16* __restrict__ x, long ldx, int N, int d, int k, int ns, int E,
     const int* __restrict__ topk_idx, const int* __restrict__ seg_start, int* __restrict__ cursor,
     __nv_bfloat16* __restrict__ xp, long ldp, int* __restrict__ slot_of, __nv_bfloat16* __restrict__ xp2,
-    long ldp2) {
+    long ldp2, int fixed_slots, long xp_rows, long xp2_rows, int check, int* status) {
   const int lane = threadIdx.x & 31;
   const long wi = blockIdx.x * 8L + (threadIdx.x >> 5);
   const int R = k + ns;
@@ -165,13 +198,24 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(
   if (lane == 0) {
     if (j < k) {
       const int e = topk_idx[static_cast<long>(t) * k + j];
-      slot = seg_start[e] + atomicAdd(cursor + e, 1);
+      if (check && (e < 0 || e >= E)) {
+        record_bad_index(status, e);
+        slot = -1;
+      } else {
+        slot = fixed_slots ? slot_of[wi] : seg_start[e] + atomicAdd(cursor + e, 1);
+      }
     } else {
       slot = seg_start[E + (j - k)] + t;
+    }
+    const bool second = xp2 != nullptr && j >= k;
+    if (check && slot >= 0 && slot >= (second ? xp2_rows : xp_rows)) {
+      record_bad_index(status, slot);
+      slot = -1;
     }
     slot_of[wi] = slot;
   }
   slot = __shfl_sync(0xffffffffu, slot, 0);
+  if (slot < 0) return;  // bounds mode: the bad route is skipped
   const __nv_bfloat16* src = x + static_cast<long>(t) * ldx;
   __nv_bfloat16* dst = (xp2 != nullptr && j >= k) ? xp2 + static_cast<long>(slot) * ldp2
                                                   : xp + static_cast<long>(slot) * ldp;
@@ -197,6 +241,14 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ seg_start,
 __device__ __forceinline__ float route_w(const MoeCombineArgs& a, int t, int j) {
   return j < a.k ? a.topk_w[static_cast<long>(t) * a.k + j]
                  : a.shared_w[static_cast<long>(t) * a.ns + (j - a.k)];
+}
+
+// bounds mode: slot inside the buffer its route reads (a bad one is recorded and skipped)
+__device__ __forceinline__ bool slot_ok(const MoeCombineArgs& a, int j, int slot) {
+  const long rows = (a.y2 != nullptr && j >= a.k) ? a.y2_rows : a.y_rows;
+  if (slot >= 0 && slot < rows) return true;
+  record_bad_index(a.status, slot);
+  return false;
 }
 
 __device__ __forceinline__ const __nv_bfloat16* y_row(const MoeCombineArgs& a, int j, int slot) {
@@ -228,6 +280,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
     for (int j = 0; j < R; ++j) {
       const float w = route_w(a, t, j);
       const int slot = a.slot_of[static_cast<long>(t) * R + j];
+      if (a.check && !slot_ok(a, j, slot)) continue;
       const uint4 y = ld_global_v4(y_row(a, j, slot) + c);
       const uint32_t yw[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
@@ -256,6 +309,10 @@ __global__ void __launch_bounds__(256) moe_combine_bwd_kernel(MoeCombineArgs a,
   const int t = static_cast<int>(wi / R), j = static_cast<int>(wi % R);
   const float w = route_w(a, t, j);
   const int slot = a.slot_of[wi];
+  if (a.check && !slot_ok(a, j, slot)) {
+    if (lane == 0) dw[wi] = 0.f;
+    return;
+  }
   const bool second = a.y2 != nullptr && j >= a.k;
   __nv_bfloat16* dst = second ? dy2 + static_cast<long>(slot) * a.ld_y2 : dy + static_cast<long>(slot) * a.ld_y;
   const __nv_bfloat16* yr = y_row(a, j, slot);
@@ -284,7 +341,8 @@ __global__ void __launch_bounds__(256) moe_unpermute_kernel(const __nv_bfloat16*
                                                             int N, int R, int d,
                                                             __nv_bfloat16* __restrict__ dx, long ldx,
                                                             int k, const __nv_bfloat16* __restrict__ dxp2,
-                                                            long ldp2) {
+                                                            long ldp2, long rows, long rows2, int check,
+                                                            int* status) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= N) return;
@@ -292,6 +350,10 @@ __global__ void __launch_bounds__(256) moe_unpermute_kernel(const __nv_bfloat16*
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = 0; j < R; ++j) {
       const int slot = slot_of[static_cast<long>(t) * R + j];
+      if (check && (slot < 0 || slot >= ((dxp2 != nullptr && j >= k) ? rows2 : rows))) {
+        record_bad_index(status, slot);
+        continue;
+      }
       const __nv_bfloat16* row = (dxp2 != nullptr && j >= k) ? dxp2 + static_cast<long>(slot) * ldp2
                                                              : dxp + static_cast<long>(slot) * ldp;
       const uint4 v = ld_global_v4(row + c);
@@ -327,11 +389,23 @@ void moe_plan(const int* counts, int E, int ns, int N, int* seg_start, int* seg_
 void moe_dispatch(const __nv_bfloat16* x, long ldx, int N, int d, int k, int ns, int E,
                   const int* topk_idx, const int* seg_start, const int* seg_count, int* cursor,
                   __nv_bfloat16* xp, long ldp, int* slot_of, cudaStream_t s, __nv_bfloat16* xp2,
-                  long ldp2, bool zero_routed_pad) {
+                  long ldp2, bool zero_routed_pad, long xp_rows, long xp2_rows) {
   if (d % 8 != 0) throw std::runtime_error("moe_dispatch: d % 8");
   const long rows = static_cast<long>(N) * (k + ns);
+  const bool det = deterministic() && k > 0 && E > 0;
+  const bool check = check_bounds();
+  if (check && (xp_rows <= 0 || (xp2 != nullptr && xp2_rows <= 0)))
+    throw std::runtime_error("moe_dispatch: bounds checking needs the buffer extents");
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (det) {  // routed slots by a stable counting sort, then the copies
+    moe_slots_stable_kernel<<<E, 1024, 0, s>>>(topk_idx, static_cast<long>(N) * k, k, k + ns,
+                                               seg_start, slot_of);
+    count_launch();
+  }
   moe_dispatch_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, s>>>(
-      x, ldx, N, d, k, ns, E, topk_idx, seg_start, cursor, xp, ldp, slot_of, xp2, ldp2);
+      x, ldx, N, d, k, ns, E, topk_idx, seg_start, cursor, xp, ldp, slot_of, xp2, ldp2, det ? 1 : 0,
+      xp_rows, xp2_rows, check ? 1 : 0, check ? device_status(dev) : nullptr);
   count_launch();
   if (xp2 == nullptr && zero_routed_pad) {
     moe_zero_pad(seg_start, seg_count, E + ns, xp, ldp, d, s);
@@ -349,13 +423,30 @@ void moe_zero_pad(const int* seg_start, const int* seg_count, int nseg, __nv_bfl
   count_launch();
 }
 
-void moe_combine(const MoeCombineArgs& a, cudaStream_t s) {
+namespace {
+MoeCombineArgs with_checks(const MoeCombineArgs& in) {
+  MoeCombineArgs a = in;
+  a.check = check_bounds() ? 1 : 0;
+  if (a.check) {
+    if (a.y_rows <= 0 || (a.y2 != nullptr && a.y2_rows <= 0))
+      throw std::runtime_error("moe_combine: bounds checking needs the buffer extents");
+    int dev = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    a.status = device_status(dev);
+  }
+  return a;
+}
+}  // namespace
+
+void moe_combine(const MoeCombineArgs& a_in, cudaStream_t s) {
+  const MoeCombineArgs a = with_checks(a_in);
   moe_combine_kernel<<<(a.N + 7) / 8, 256, 0, s>>>(a);
   count_launch();
 }
 
-void moe_combine_bwd(const MoeCombineArgs& a, const __nv_bfloat16* dout, long ld_dout,
+void moe_combine_bwd(const MoeCombineArgs& a_in, const __nv_bfloat16* dout, long ld_dout,
                      __nv_bfloat16* dy, float* dw, cudaStream_t s, __nv_bfloat16* dy2) {
+  const MoeCombineArgs a = with_checks(a_in);
   const long rows = static_cast<long>(a.N) * (a.k + a.ns);
   if ((a.y2 == nullptr) != (dy2 == nullptr)) throw std::runtime_error("moe_combine_bwd: y2 / dy2");
   moe_combine_bwd_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, s>>>(a, dout, ld_dout, dy, dw, dy2);
@@ -364,8 +455,15 @@ void moe_combine_bwd(const MoeCombineArgs& a, const __nv_bfloat16* dout, long ld
 
 void moe_unpermute(const __nv_bfloat16* dxp, long ldp, const int* slot_of, int N, int R, int d,
                    __nv_bfloat16* dx, long ldx, cudaStream_t s, int k, const __nv_bfloat16* dxp2,
-                   long ldp2) {
-  moe_unpermute_kernel<<<(N + 7) / 8, 256, 0, s>>>(dxp, ldp, slot_of, N, R, d, dx, ldx, k, dxp2, ldp2);
+                   long ldp2, long rows, long rows2) {
+  const bool check = check_bounds();
+  if (check && (rows <= 0 || (dxp2 != nullptr && rows2 <= 0)))
+    throw std::runtime_error("moe_unpermute: bounds checking needs the buffer extents");
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  moe_unpermute_kernel<<<(N + 7) / 8, 256, 0, s>>>(dxp, ldp, slot_of, N, R, d, dx, ldx, k, dxp2, ldp2,
+                                                   rows, rows2, check ? 1 : 0,
+                                                   check ? device_status(dev) : nullptr);
   count_launch();
 }
 

@@ -31,6 +31,9 @@ struct MoeCombineArgs {
   long ld_res = 0;
   __nv_bfloat16* out = nullptr;
   long ld_out = 0;
+  long y_rows = 0, y2_rows = 0;        // extents of y / y2 (bounds-checking mode)
+  int check = 0;                       // bounds-checking mode
+  int* status = nullptr;
 };
 
 void moe_route(const MoeRouteArgs& a, cudaStream_t s);
@@ -40,7 +43,8 @@ void moe_plan(const int* counts, int E, int ns, int N, int* seg_start, int* seg_
 void moe_dispatch(const __nv_bfloat16* x, long ldx, int N, int d, int k, int ns, int E,
                   const int* topk_idx, const int* seg_start, const int* seg_count, int* cursor,
                   __nv_bfloat16* xp, long ldp, int* slot_of, cudaStream_t s,
-                  __nv_bfloat16* xp2 = nullptr, long ldp2 = 0, bool zero_routed_pad = true);
+                  __nv_bfloat16* xp2 = nullptr, long ldp2 = 0, bool zero_routed_pad = true,
+                  long xp_rows = 0, long xp2_rows = 0);
 void moe_zero_pad(const int* seg_start, const int* seg_count, int nseg, __nv_bfloat16* xp, long ldp,
                   int d, cudaStream_t s);
 void moe_combine(const MoeCombineArgs& a, cudaStream_t s);
@@ -49,7 +53,8 @@ void moe_combine_bwd(const MoeCombineArgs& a, const __nv_bfloat16* dout, long ld
 // routes j >= k read dxp2 (when non-null) instead of dxp
 void moe_unpermute(const __nv_bfloat16* dxp, long ldp, const int* slot_of, int N, int R, int d,
                    __nv_bfloat16* dx, long ldx, cudaStream_t s, int k = 0,
-                   const __nv_bfloat16* dxp2 = nullptr, long ldp2 = 0);
+                   const __nv_bfloat16* dxp2 = nullptr, long ldp2 = 0, long rows = 0,
+                   long rows2 = 0);
 
 // ---- expert parallelism: row-block copies between local and peer (IPC) buffers
 struct EpCopyArgs {
@@ -155,6 +160,9 @@ struct EpSourceArgs {
   long ld_ys = 0;
   __nv_bfloat16* out = nullptr;
   long ld_out = 0;
+  long y_rows = 0, y2_rows = 0;        // extents of y / y2 (bounds-checking mode)
+  int check = 0;                       // bounds-checking mode
+  int* status = nullptr;
 };
 void ep_source_reduce(const EpSourceArgs& a, cudaStream_t s);
 

@@ -126,6 +126,8 @@ class TrainConfig:
     # FULL_SHARD for the block GEMM weights: each forward GEMM all-gathers its weight's
     # peer-owned pieces itself (fused transport); the optimizer keeps them rank-local
     shard_weights: bool = False
+    # fixed-order MoE permutation: bit-reproducible expert gradients (drivedit_b200.ops.debug)
+    deterministic: bool = False
 
 
 @dataclass

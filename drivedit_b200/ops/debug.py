@@ -1,0 +1,66 @@
+"""Debug switches of the sm_100a kernels (substitutes for a race detector and a memory
+checker, which this framework does not rely on):
+
+``deterministic``
+    Index-driven permutations assign rows in a fixed order: the MoE dispatch places the
+    routes to each expert in (token, route) order with a stable counting sort instead of
+    by atomic arrival, so the expert weight-gradient reductions and every later sum repeat
+    bit for bit from run to run. The default (atomic) order is correct but its rounding
+    varies with thread timing.
+``check_bounds``
+    The MoE dispatch / combine / un-permute kernels check every table-derived index
+    (expert ids, row slots) against the extent of the buffer it addresses; the first bad
+    index is recorded in the device status word (code 6, the index in word 1) and the
+    access is skipped, so a corrupt routing table shows up as an error instead of a
+    memory fault. :func:`drivedit_b200.ops._ext.check_device_status` raises on it.
+
+Both are process-wide and off by default.
+"""
+from __future__ import annotations
+
+from contextlib import contextmanager
+
+from ._ext import ext
+
+BAD_INDEX_STATUS = 6
+
+
+def set_deterministic(on: bool = True) -> None:
+    ext().set_deterministic(bool(on))
+
+
+def is_deterministic() -> bool:
+    return bool(ext().deterministic())
+
+
+def set_check_bounds(on: bool = True) -> None:
+    ext().set_check_bounds(bool(on))
+
+
+def is_checking_bounds() -> bool:
+    return bool(ext().check_bounds())
+
+
+def bad_index() -> int:
+    """The index recorded with the last bad-index status."""
+    return int(ext().read_status_index())
+
+
+@contextmanager
+def deterministic(on: bool = True):
+    prev = is_deterministic()
+    set_deterministic(on)
+    try:
+        yield
+    finally:
+        set_deterministic(prev)
+
+
+@contextmanager
+def check_bounds(on: bool = True):
+    prev = is_checking_bounds()
+    set_check_bounds(on)
+    try:
+        yield
+    finally:
+        set_check_bounds(prev)

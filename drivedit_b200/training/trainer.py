@@ -38,6 +38,10 @@ class WorldModelTrainer:
         self.cuda = self.device.type == "cuda"
         self.compute_dtype = torch.bfloat16 if (self.cuda and cfg.dtype == "bf16") else torch.float32
         self.pg = process_group
+        if self.cuda and getattr(cfg, "deterministic", False):
+            from ..ops.debug import set_deterministic
+
+            set_deterministic(True)
         self.engine = None
         self.ep = None
         world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
