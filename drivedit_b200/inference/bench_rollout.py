@@ -30,7 +30,7 @@ def run(batch: int, frames: int, warm_chunks: int = 2, overrides=None, tp_transp
     cfg = get_config("rollout_dit_b", overrides)
     torch.manual_seed(0)
     model = WorldDiT(cfg.model).cuda().eval()
-    group = FlatParamGroup(model.named_parameters(), "cuda")
+    group = FlatParamGroup(model.flat_layout(model.named_parameters()), "cuda")
     model.enable_fused(group=group)
     tp = None
     world = 1

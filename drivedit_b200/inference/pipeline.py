@@ -73,7 +73,7 @@ class InferencePipeline:
         if self.device.type == "cuda":
             from ..parallel.flat import FlatParamGroup
 
-            m.enable_fused(group=FlatParamGroup(m.named_parameters(), self.device))
+            m.enable_fused(group=FlatParamGroup(m.flat_layout(m.named_parameters()), self.device))
         return m
 
     @staticmethod

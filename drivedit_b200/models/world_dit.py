@@ -26,6 +26,7 @@ on CPU the same math runs in PyTorch (the numerical oracle and the CPU baseline)
 from __future__ import annotations
 
 import math
+import re
 from typing import Dict, List, Optional, Tuple
 
 import torch
@@ -238,6 +239,19 @@ class WorldDiT(nn.Module):
     def no_decay_names(self) -> List[str]:
         return [n for n, p in self.named_parameters()
                 if p.dim() < 2 or n.endswith(".bias") or "norm" in n.split(".")[-2]]
+
+    MOD_PARAM = re.compile(r"^(blocks\.\d+\.ada|final_ada)\.(weight|bias)$")
+
+    def flat_layout(self, named):
+        """Parameter order for flat buffers: every block's AdaLN modulation projection
+        and the final one, weights and biases each as one contiguous run (block order,
+        then final), so the fused path computes all modulations with one GEMM."""
+        named = list(named)
+        mods = [(n, p) for n, p in named if self.MOD_PARAM.match(n)]
+        rest = [(n, p) for n, p in named if not self.MOD_PARAM.match(n)]
+        key = lambda np_: (np_[0].endswith(".bias"), np_[0].startswith("final"),
+                           int(np_[0].split(".")[1]) if np_[0].startswith("blocks") else 0)
+        return rest + sorted(mods, key=key)
 
     # ---------------------------------------------------------------- forward
     def forward(self, x_t: torch.Tensor, t: torch.Tensor, actions: torch.Tensor,

@@ -133,10 +133,16 @@ def _moe_backward(dx2, d_aux, sv, blk, W, bc, mod, dmod):
 
 class _BlockFn(torch.autograd.Function):
     """One dense (attention + SwiGLU) or MoE (attention + experts) block; returns
-    ``(x_out, aux_loss)`` where ``aux_loss`` is the unweighted MoE load-balance term."""
+    ``(x_out, aux_loss)`` where ``aux_loss`` is the unweighted MoE load-balance term.
+
+    With ``dmod_out`` (batched modulations, :class:`_AllMods`) ``mod`` is a detached view
+    of the shared modulation matrix; the backward accumulates the modulation gradient
+    into ``dmod_out`` (this block's columns of the shared gradient buffer) and returns a
+    zero gradient for ``token``, the scalar that ties every block to the one GEMM
+    backward of all modulations."""
 
     @staticmethod
-    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx):
+    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx, token=None, dmod_out=None):
         W = group.compute_view
         x1, sa = _attn_forward(x, mod, blk, W, bc)
         if blk.moe is None:
@@ -146,6 +152,7 @@ class _BlockFn(torch.autograd.Function):
             x2, aux, sm = _moe_forward(x1, mod, blk, W, bc)
         ctx.sa, ctx.sm, ctx.mod = sa, sm, mod
         ctx.blk, ctx.group, ctx.bc = blk, group, bc
+        ctx.dmod_out = dmod_out
         return x2, aux
 
     @staticmethod
@@ -153,15 +160,76 @@ class _BlockFn(torch.autograd.Function):
         blk, bc, mod = ctx.blk, ctx.bc, ctx.mod
         W = ctx.group.compute_view
         dx2 = dx2.contiguous()
-        dmod = torch.zeros(mod.shape, device=mod.device, dtype=torch.float32)
+        batched = ctx.dmod_out is not None
+        dmod = ctx.dmod_out if batched else torch.zeros(mod.shape, device=mod.device,
+                                                        dtype=torch.float32)
         if blk.moe is None:
             dx1 = _mlp_backward(dx2, ctx.sm, blk, W, bc, mod, dmod)
         else:
             # d_aux already carries the aux-loss weight (the caller scales the output)
             dx1 = _moe_backward(dx2, d_aux, ctx.sm, blk, W, bc, mod, dmod)
         dx = _attn_backward(dx1, ctx.sa, blk, W, bc, mod, dmod)
-        ctx.sa = ctx.sm = None
-        return dx, dmod, None, None, None
+        ctx.sa = ctx.sm = ctx.dmod_out = None
+        if batched:
+            return dx, None, None, None, None, torch.zeros((), device=dx.device), None
+        return dx, dmod, None, None, None, None, None
+
+
+def _mod_runs(model, group: FlatParamGroup):
+    """(weight offset, bias offset) of the contiguous runs that hold every block's
+    modulation projection followed by the final one, or ``None`` when the group's
+    layout keeps them apart."""
+    mods = [blk.ada for blk in model.blocks] + [model.final_ada]
+    if not all(group.owns(m.weight) and group.owns(m.bias) for m in mods):
+        return None
+    w_off = [group.offsets[group.names[group.index(m.weight)]][0] for m in mods]
+    b_off = [group.offsets[group.names[group.index(m.bias)]][0] for m in mods]
+    w_len = [m.weight.numel() for m in mods]
+    b_len = [m.bias.numel() for m in mods]
+    for i in range(len(mods) - 1):
+        if w_off[i] + w_len[i] != w_off[i + 1] or b_off[i] + b_len[i] != b_off[i + 1]:
+            return None
+    return w_off[0], b_off[0], sum(w_len), sum(b_len)
+
+
+class _AllMods(torch.autograd.Function):
+    """Every block's AdaLN modulation (and the final layer's) from the per-frame
+    conditioning in one tcgen05 GEMM: ``mods [B*F, sum n_mod d] = c W_all^T + b_all``,
+    where ``W_all`` is the contiguous run of all modulation weights in the flat buffer.
+    Backward (after every block has written its columns of the shared gradient):
+    one split-K GEMM for ``dc = dmods W_all``, one weight-gradient GEMM
+    ``dW_all += dmods^T c`` into the flat gradient run, and one column sum for the
+    biases. Outputs: the modulation matrix (no autograd edge), its gradient buffer and
+    ``token``, the scalar each block returns a zero gradient for."""
+
+    @staticmethod
+    def forward(ctx, c2, group: FlatParamGroup, runs):
+        w0, b0, wn, bn = runs
+        d = c2.shape[1]
+        W_all = group.compute[w0:w0 + wn].view(-1, d)
+        b_all = group.master[b0:b0 + bn]
+        cb = c2.detach().to(torch.bfloat16).contiguous()
+        mods = gemm(cb, W_all, epi="f32", bias=b_all)
+        dmods = torch.zeros_like(mods)
+        ctx.save_for_backward(cb)
+        ctx.group, ctx.runs, ctx.dmods = group, runs, dmods
+        ctx.mark_non_differentiable(mods, dmods)
+        return mods, dmods, torch.zeros((), device=c2.device)
+
+    @staticmethod
+    def backward(ctx, _dm, _dd, _dtoken):
+        (cb,) = ctx.saved_tensors
+        g = ctx.group
+        w0, b0, wn, bn = ctx.runs
+        d = cb.shape[1]
+        dm = ctx.dmods.to(torch.bfloat16)
+        W_all = g.compute[w0:w0 + wn].view(-1, d)
+        dW = g.grad[w0:w0 + wn].view(-1, d)
+        gemm(dm, cb, dW, epi="f32_acc", a_t=True, b_t=True)          # dW_all += dm^T c
+        g.grad[b0:b0 + bn].add_(ctx.dmods.sum(0))
+        dc = gemm(dm, W_all, epi="f32_acc", b_t=True)                 # dc = dm W_all
+        ctx.dmods = None
+        return dc, None, None
 
 
 class FusedWorldDiT:
@@ -169,7 +237,13 @@ class FusedWorldDiT:
 
     def __init__(self, model, group: Optional[FlatParamGroup] = None):
         self.model = model
-        self.group = group if group is not None else FlatParamGroup(model.named_parameters())
+        if group is None:
+            named = model.named_parameters()
+            if hasattr(model, "flat_layout"):
+                named = model.flat_layout(named)
+            group = FlatParamGroup(named)
+        self.group = group
+        self._runs = False  # modulation weight runs of the group, looked up on first use
 
     def forward(self, model, x_t, t, actions, frame_offset=0, return_aux=False,
                 return_features=None, extra_cond=None):
@@ -190,14 +264,29 @@ class FusedWorldDiT:
                       cfg.sla, cfg.causal)
         feats = None
         aux = torch.zeros((), device=x.device)
+        if self._runs is False:
+            self._runs = _mod_runs(model, g)
+        if self._runs is not None:  # all modulations in one GEMM (+ one backward pair)
+            mods, dmods, token = _AllMods.apply(c2, g, self._runs)
+            widths = [blk.ada.weight.shape[0] for blk in model.blocks]
+        col = 0
         for i, blk in enumerate(model.blocks):
-            mod = blk.ada(c2)                                      # [B*F, 4d] fp32
-            x, a = _BlockFn.apply(x, mod, blk, g, bc)
+            if self._runs is not None:
+                n = widths[i]
+                x, a = _BlockFn.apply(x, mods[:, col:col + n], blk, g, bc, token,
+                                      dmods[:, col:col + n])
+                col += n
+            else:
+                mod = blk.ada(c2)                                  # [B*F, 4d] fp32
+                x, a = _BlockFn.apply(x, mod, blk, g, bc)
             if blk.moe is not None:
                 aux = aux + a * blk.moe.aux_loss_weight
             if return_features is not None and i + 1 == return_features:
                 feats = x
-        fm = model.final_ada(c2)
+        if self._runs is not None:
+            fm = _FinalMod.apply(mods[:, col:], dmods[:, col:], token)
+        else:
+            fm = model.final_ada(c2)
         h, _ = _FinalNorm.apply(x, fm, model.final_norm.weight, bc.tpf, cfg.norm_eps)
         out = linear(h, g.compute_view(model.out_proj.weight), model.out_proj.bias,
                      model.out_proj.weight, model.out_proj.bias)
@@ -205,6 +294,23 @@ class FusedWorldDiT:
         if return_features is not None:
             return v, aux, feats
         return (v, aux) if return_aux else v
+
+
+class _FinalMod(torch.autograd.Function):
+    """The final layer's columns of the batched modulations as a differentiable input of
+    the final norm: its gradient lands in the shared buffer, and ``token`` orders the
+    batched backward after it."""
+
+    @staticmethod
+    def forward(ctx, fm, dfm, token):
+        ctx.dfm = dfm
+        return fm.clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        ctx.dfm.add_(g)
+        ctx.dfm = None
+        return None, None, torch.zeros((), device=g.device)
 
 
 class _FinalNorm(torch.autograd.Function):
@@ -247,8 +353,21 @@ def _forward_cached_fused(self, model, x_t, t, actions, cache, commit, extra_con
     c2 = model.condition(t, actions, extra_cond).reshape(B * Fc, d)
     tab = model.rope.table(Fc, cache.frames).to(x.device)
     row = cache.reserve(T)
+    if self._runs is False:
+        self._runs = _mod_runs(model, g)
+    mods = None
+    if self._runs is not None:  # every modulation of this forward in one GEMM
+        w0, b0, wn, bn = self._runs
+        mods = gemm(c2.to(torch.bfloat16).contiguous(), g.compute[w0:w0 + wn].view(-1, d),
+                    epi="f32", bias=g.master[b0:b0 + bn])
+    col = 0
     for blk, lc in zip(model.blocks, cache.layers):
-        mod = blk.ada(c2)
+        if mods is not None:
+            n = blk.ada.weight.shape[0]
+            mod = mods[:, col:col + n]
+            col += n
+        else:
+            mod = blk.ada(c2)
         h1, _ = adaln_rmsnorm(x, blk.norm1.weight, mod, 0, d, tpf)
         qkv = gemm(h1, W(blk.attn.qkv.weight), epi="rope", rope_tab=tab, rope_cols=2 * d,
                    rope_rows_per_seq=T, rope_head_dim=cfg.d_head)
@@ -272,7 +391,7 @@ def _forward_cached_fused(self, model, x_t, t, actions, cache, commit, extra_con
         x = gemm(a, W(blk.mlp.w3.weight), residual=x1)
     if commit:
         cache.commit(Fc)
-    fm = model.final_ada(c2)
+    fm = mods[:, col:] if mods is not None else model.final_ada(c2)
     h, _ = adaln_rmsnorm(x, model.final_norm.weight, fm, 0, d, tpf, cfg.norm_eps)
     out = gemm(h, W(model.out_proj.weight), bias=model.out_proj.bias)
     return unpatchify(out.view(B, T, cfg.patch_dim), Fc, C, H, W_, cfg.patch)

@@ -129,6 +129,8 @@ class ShardedDataParallel:
         named_all = list(model.named_parameters())
         local = set(local_params or [])
         named = [(n, p) for n, p in named_all if n not in local]
+        if hasattr(model, "flat_layout"):
+            named = model.flat_layout(named)
         self.weight_gather = bool(weight_gather) and self.transport == "fused" and self.world > 1
         if self.weight_gather:  # gathered weights first: a contiguous prefix of the flat buffer
             named = ([(n, p) for n, p in named if GATHERED_WEIGHT.match(n)]

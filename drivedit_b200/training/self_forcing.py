@@ -472,7 +472,7 @@ class SelfForcingPlusTrainer:
             self.aux["future_anchor_encoder"] = self.future_anchor_encoder
         self.model.to(self.device)
         self.aux.to(self.device)
-        named = list(model.named_parameters()) + [("aux." + n, p) for n, p in self.aux.named_parameters()]
+        named = list(model.flat_layout(model.named_parameters())) + [("aux." + n, p) for n, p in self.aux.named_parameters()]
         nd = set(model.no_decay_names()) | {"aux." + n for n, p in self.aux.named_parameters()
                                             if p.dim() < 2}
         self.group = FlatParamGroup(named, self.device, no_decay=nd)

@@ -64,8 +64,10 @@ class WorldModelTrainer:
             self.group = self.engine.flat
             self.opt = None
         else:
-            self.group = FlatParamGroup(model.named_parameters(), self.device,
-                                        no_decay=model.no_decay_names())
+            named = model.named_parameters()
+            if hasattr(model, "flat_layout"):
+                named = model.flat_layout(named)
+            self.group = FlatParamGroup(named, self.device, no_decay=model.no_decay_names())
             self.opt = FlatAdamW(self.group, cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
                                  cfg.grad_clip)
         self.fused = self.cuda if fused is None else fused

@@ -402,7 +402,7 @@ class UnifiedTrainer:
         if config.cjepa.enabled:
             self.heads["cjepa"] = CJEPAPredictor(config.cjepa, d)
         self.heads.to(self.device)
-        named = list(model.named_parameters()) + [("heads." + n, p) for n, p in self.heads.named_parameters()]
+        named = list(model.flat_layout(model.named_parameters())) + [("heads." + n, p) for n, p in self.heads.named_parameters()]
         nd = set(model.no_decay_names()) | {"heads." + n for n, p in self.heads.named_parameters() if p.dim() < 2}
         self.group = FlatParamGroup(named, self.device, no_decay=nd)
         self.optimizer = FlatAdamW(self.group, config.learning_rate, (0.9, 0.95), 1e-8, config.weight_decay,

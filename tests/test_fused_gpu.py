@@ -98,7 +98,11 @@ def _small_cfg(attention="dense"):
     return cfg
 
 
-def test_fused_model_matches_torch_path():
+@pytest.mark.parametrize("batched_mods", [False, True])
+def test_fused_model_matches_torch_path(batched_mods):
+    """Fused CUDA path vs the PyTorch path, forward and every parameter gradient; with
+    ``batched_mods`` the flat layout groups the AdaLN modulation projections so all of
+    them run as one GEMM (forward) and one GEMM pair (backward)."""
     from drivedit_b200.models.world_dit import WorldDiT
     from drivedit_b200.parallel.flat import FlatParamGroup
     torch.manual_seed(0)
@@ -111,7 +115,8 @@ def test_fused_model_matches_torch_path():
                 p.normal_(0, 0.02)
     m = WorldDiT(cfg.model).cuda()
     m.load_state_dict(m_ref.state_dict())
-    group = FlatParamGroup(m.named_parameters(), "cuda")
+    named = m.flat_layout(m.named_parameters()) if batched_mods else m.named_parameters()
+    group = FlatParamGroup(named, "cuda")
     m.enable_fused(group=group)
     B, Fr = 2, 2
     x = torch.randn(B, Fr, 16, 32, 32, device="cuda")
@@ -134,6 +139,7 @@ def test_fused_model_matches_torch_path():
         worst[n] = _rel(p.grad, g_ref)
     bad = {k: v for k, v in worst.items() if v > 6e-2}
     assert not bad, bad
+    assert (m.fused._runs is not None) == batched_mods
 
 
 def test_video_augment_kernel():
