@@ -117,6 +117,66 @@ def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int
         _attn_trace(fwd, qkv, o, do, lse, delta, dq_acc, dqkv, B, H, T, tpf, sc)
 
 
+def bench_sla_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512):
+    """SLA block-sparse softmax attention (top 12.5 % of 64x64 blocks, frame-causal) at
+    the DiT-B training shape: routing, sparse forward and sparse backward timed
+    separately. Effective TFLOP/s count only the selected (query block, key block) pairs
+    (4 * 64 * 64 * 64 flops per pair forward, 10x backward), so the figure shows how
+    much of the work the kernels spend on selected pairs."""
+    import math
+
+    from ..layers.sla import SLAConfig
+    from ._ext import ext
+    from .attention_kernels import sla_plan_kernel
+
+    d = H * 64
+    torch.manual_seed(0)
+    qkv = (torch.randn(B * T, 3 * d, device="cuda") * 0.5).bfloat16()
+    o = torch.empty(B * T, d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H * T, device="cuda")
+    do = torch.randn(B * T, d, device="cuda").bfloat16()
+    delta = torch.empty(B * H * T, device="cuda")
+    dq_acc = torch.zeros(B * T, d, device="cuda")
+    dqkv = torch.empty(B * T, 3 * d, device="cuda", dtype=torch.bfloat16)
+    cfg = SLAConfig(block_size=64, topk_frac=0.125, causal="frame", tokens_per_frame=tpf)
+    sc = 1.0 / math.sqrt(64)
+    plan = sla_plan_kernel(qkv, B, T, H, cfg, tpf, "frame", sel_bits=True)
+    lists = (plan.pair_blocks, plan.pair_mask, plan.pair_count)
+    tlists = (plan.kv_qtiles, plan.kv_qmask, plan.kv_count)
+    # selected pairs: popcount of the 4-bit quadrant masks of the listed pairs
+    counts = plan.pair_count.long()
+    mask = plan.pair_mask.long()
+    live = torch.arange(mask.shape[1], device="cuda")[None, :] < counts[:, None]
+    bits = sum(((mask >> i) & 1) for i in range(4)) * live
+    selected = float(bits.sum())
+    computed = float(counts.sum()) * 4  # 128 x 128 tiles = 4 block pairs each
+
+    def route():
+        sla_plan_kernel(qkv, B, T, H, cfg, tpf, "frame")
+
+    def fwd():
+        ext().attn_fwd(qkv, qkv, qkv, o, lse, 0, d, 2 * d, 0, B, H, T, T, T, T, 1, tpf, 0, 0, sc,
+                       *lists)
+
+    def bwd():
+        ext().attn_delta(o, do, delta, 0, 0, B, H, T, T)
+        dq_acc.zero_()
+        ext().attn_bwd(qkv, qkv, qkv, o, do, lse, delta, dq_acc, dqkv, dqkv, 0, d, 2 * d, 0, 0, d,
+                       2 * d, B, H, T, T, T, T, 1, tpf, 0, 0, sc, *tlists, 0)
+        ext().attn_dq_finalize(dq_acc, dqkv, 0, H, None, T, 0)
+
+    fwd()
+    f_pair = 64.0 * 64 * 64
+    ms_r, ms_f, ms_b = _timeit(route, iters), _timeit(fwd, iters), _timeit(bwd, iters)
+    print(json.dumps({"kernel": "sla_route", "B": B, "H": H, "T": T, "ms": round(ms_r, 3)}), flush=True)
+    for name, ms, mult in (("sla_attn_fwd", ms_f, 4.0), ("sla_attn_bwd", ms_b, 10.0)):
+        print(json.dumps({"kernel": name, "B": B, "H": H, "T": T, "ms": round(ms, 3),
+                          "selected_pairs": int(selected), "computed_pairs": int(computed),
+                          "tflops_selected": round(mult * f_pair * selected / ms / 1e9, 1),
+                          "tflops_computed": round(mult * f_pair * computed / ms / 1e9, 1)}),
+              flush=True)
+
+
 def _attn_trace(fwd, qkv, o, do, lse, delta, dq_acc, dqkv, B, H, T, tpf, sc):
     """clock64 events of one heavy CTA per kernel (cycles from the CTA's first event):
     forward roles producer / MMA / softmax, backward producer / MMA / softmax / dQ."""
@@ -379,7 +439,7 @@ def bench_optim(iters: int = 10, numel: int = 130_000_000, transport: str = "fus
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", nargs="*", default=["gemm"])
+    p.add_argument("what", nargs="*", default=["gemm"], help="gemm attn sla_attn sla norm conv3d ep optim")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--small", action="store_true", help="small attention case (for ncu)")
     p.add_argument("--B", type=int, default=8, help="attention batch")

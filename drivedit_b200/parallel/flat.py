@@ -58,7 +58,9 @@ class FlatParamGroup:
             allocator = lambda kind, n, dt: torch.zeros(n, dtype=dt, device=self.device)
         self.master = allocator("master", self.numel, torch.float32)
         self.grad = allocator("grad", self.numel, torch.float32)
-        self.compute = allocator("compute", self.numel, compute_dtype)
+        # an fp32 compute copy would equal the master: alias it instead of copying
+        self.compute = (self.master if compute_dtype == torch.float32
+                        else allocator("compute", self.numel, compute_dtype))
         # groups whose parameters this one resolves views for too (rank-local expert
         # parameters under expert parallelism live in their own group)
         self.linked: List["FlatParamGroup"] = []
@@ -99,7 +101,8 @@ class FlatParamGroup:
 
     # ------------------------------------------------------------------ updates
     def refresh_compute(self):
-        self.compute.copy_(self.master)
+        if self.compute.data_ptr() != self.master.data_ptr():
+            self.compute.copy_(self.master)
         for g in self.linked:
             g.refresh_compute()
 

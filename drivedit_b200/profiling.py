@@ -5,6 +5,11 @@ a static dead-code report of the package.
     times ``--steps`` training steps with CUDA events (after ``--warmup``) and then records
     one more step with the PyTorch profiler (CUPTI kernel records) to list the kernels by
     total device time, grouped by name, with their share of the step.
+``python -m drivedit_b200.profiling cpu-step [--config tiny] [--steps 30]``
+    the fp32 CPU training step (forward, backward, AdamW) of a preset, median wall time
+    over ``--steps`` after ``--warmup``; the ``tiny`` preset is the 4-layer d256 workload
+    on which the reference's own modules run at 6,902 latent tok/s (74.2 ms/step) on this
+    machine class (an 8-thread 2.7 GHz Xeon).
 ``python -m drivedit_b200.profiling deadcode [package_dir]``
     functions and classes defined in the package that no other module names.
 
@@ -100,6 +105,45 @@ class ThroughputProfiler:
         return StepProfile(self.name, ms, self.tokens / (ms / 1000.0), self.kernel_breakdown())
 
 
+# ----------------------------------------------------------------------------- CPU step
+REFERENCE_TINY_CPU_TOK_S = 6902.0  # reference modules, same workload, measured on this CPU class
+
+
+def cpu_step(config: str = "tiny", steps: int = 30, warmup: int = 5, overrides=None) -> Dict:
+    """Median wall time of the fp32 CPU training step of a preset."""
+    import statistics
+    import time
+
+    import torch
+
+    from .config import get_config
+    from .data.synthetic import make_batch
+    from .models.world_dit import WorldDiT
+    from .training.trainer import WorldModelTrainer
+
+    cfg = get_config(config, overrides)
+    cfg.train.dtype = "fp32"
+    torch.manual_seed(cfg.train.seed)
+    tr = WorldModelTrainer(WorldDiT(cfg.model), cfg.train, "cpu")
+    batch = make_batch(cfg, generator=torch.Generator().manual_seed(0))
+    tokens = cfg.train.batch_per_gpu * cfg.train.frames * cfg.model.tokens_per_frame
+    for _ in range(warmup):
+        tr.train_step(batch)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        tr.train_step(batch)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    out = {"config": config, "device": "cpu", "dtype": "fp32", "threads": torch.get_num_threads(),
+           "tokens_per_step": tokens, "ms_per_step": round(med * 1000, 2),
+           "tokens_per_s": round(tokens / med, 1)}
+    if config == "tiny" and not overrides:
+        out["reference_tokens_per_s"] = REFERENCE_TINY_CPU_TOK_S
+        out["vs_reference"] = round(out["tokens_per_s"] / REFERENCE_TINY_CPU_TOK_S, 3)
+    return out
+
+
 # ----------------------------------------------------------------------------- dead code
 def dead_code(package_dir: str) -> List[str]:
     """``module:line name`` of top-level functions / classes (and methods not starting
@@ -140,9 +184,17 @@ def main(argv=None):
     st.add_argument("--top", type=int, default=30)
     st.add_argument("--json", default=None, help="write the breakdown as JSON here")
     st.add_argument("override", nargs="*")
+    cs = sub.add_parser("cpu-step")
+    cs.add_argument("--config", default="tiny")
+    cs.add_argument("--steps", type=int, default=30)
+    cs.add_argument("--warmup", type=int, default=5)
+    cs.add_argument("override", nargs="*")
     dc = sub.add_parser("deadcode")
     dc.add_argument("package", nargs="?", default=os.path.dirname(os.path.abspath(__file__)))
     a = ap.parse_args(argv)
+    if a.cmd == "cpu-step":
+        print(json.dumps(cpu_step(a.config, a.steps, a.warmup, a.override or None)))
+        return 0
     if a.cmd == "deadcode":
         for line in dead_code(a.package):
             print(line)

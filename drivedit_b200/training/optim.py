@@ -43,7 +43,7 @@ class FlatAdamW:
             from ..ops.fused import sq_norm
 
             return sq_norm(self.grad)
-        return self.grad.double().pow(2).sum().float()
+        return torch.dot(self.grad, self.grad)   # one BLAS pass on the CPU
 
     def step(self, grad_scale: float = 1.0, sq_norm: Optional[torch.Tensor] = None):
         """Apply one update. ``grad_scale`` multiplies the gradient (e.g. 1/world for a
@@ -67,14 +67,27 @@ class FlatAdamW:
                        lr=self.lr, b1=b1, b2=b2, eps=self.eps, wd=self.wd,
                        bc1=bc1, bc2=bc2, grad_scale=grad_scale, decay_end=self.decay_end)
             return
-        g = self.grad * (grad_scale * clip)
-        self.m.mul_(b1).add_(g, alpha=1 - b1)
-        self.v.mul_(b2).addcmul_(g, g, value=1 - b2)
-        upd = (self.m / bc1) / ((self.v / bc2).sqrt() + self.eps)
-        if self.wd:
-            self.master[: self.decay_end].mul_(1 - self.lr * self.wd)
-        self.master.add_(upd, alpha=-self.lr)
-        self.compute.copy_(self.master)
+        if hasattr(torch, "_fused_adamw_"):
+            # PyTorch's fused CPU AdamW: one pass per segment (decay, no-decay); it divides
+            # the gradient by its grad_scale argument, so pass the reciprocal of ours
+            inv = (1.0 / (grad_scale * clip)).reshape(1).float()
+            step = torch.tensor(float(self.step_count))
+            for lo, hi, wd in ((0, self.decay_end, self.wd), (self.decay_end, self.master.numel(), 0.0)):
+                if hi > lo:
+                    torch._fused_adamw_([self.master[lo:hi]], [self.grad[lo:hi]], [self.m[lo:hi]],
+                                        [self.v[lo:hi]], [], [step], lr=self.lr, beta1=b1,
+                                        beta2=b2, weight_decay=wd, eps=self.eps, amsgrad=False,
+                                        maximize=False, grad_scale=inv, found_inf=None)
+        else:
+            g = self.grad * (grad_scale * clip)
+            self.m.mul_(b1).add_(g, alpha=1 - b1)
+            self.v.mul_(b2).addcmul_(g, g, value=1 - b2)
+            upd = (self.m / bc1) / ((self.v / bc2).sqrt() + self.eps)
+            if self.wd:
+                self.master[: self.decay_end].mul_(1 - self.lr * self.wd)
+            self.master.add_(upd, alpha=-self.lr)
+        if self.compute.data_ptr() != self.master.data_ptr():
+            self.compute.copy_(self.master)
 
     def state_dict(self):
         return {"m": self.m, "v": self.v, "step": self.step_count, "lr": self.lr,

@@ -67,7 +67,9 @@ class WorldModelTrainer:
             named = model.named_parameters()
             if hasattr(model, "flat_layout"):
                 named = model.flat_layout(named)
-            self.group = FlatParamGroup(named, self.device, no_decay=model.no_decay_names())
+            # on the CPU every op reads the fp32 master: no separate compute copy
+            self.group = FlatParamGroup(named, self.device, no_decay=model.no_decay_names(),
+                                        compute_dtype=torch.bfloat16 if self.cuda else torch.float32)
             self.opt = FlatAdamW(self.group, cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
                                  cfg.grad_clip)
         self.fused = self.cuda if fused is None else fused
