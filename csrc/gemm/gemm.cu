@@ -964,6 +964,9 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   auto best_splits = [&](int bn_c) {
     int sp = 1;
     if (epi == kEpiF32Atomic) {
+      // deterministic mode: one writer per output element, so the fp32 accumulation
+      // does not depend on the arrival order of split-K partial sums
+      if (deterministic()) return 1;
       if (a.splits > 0) return a.splits;
       while (kblocks / (sp * 2) >= 8 && est(bn_c, sp * 2) < est(bn_c, sp)) sp *= 2;
     }

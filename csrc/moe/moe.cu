@@ -125,6 +125,24 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a) {
   }
 }
 
+// Deterministic mode: psum[e] = sum over tokens of probs[t, e] in a fixed order (each
+// thread a fixed stride of rows, then a fixed-shape tree), replacing the route kernel's
+// float atomics whose rounding depends on arrival order.
+__global__ void __launch_bounds__(256) moe_psum_fixed_kernel(const float* __restrict__ probs, int N,
+                                                             int E, float* __restrict__ psum) {
+  __shared__ float part[256];
+  const int e = blockIdx.x;
+  float acc = 0.f;
+  for (int t = threadIdx.x; t < N; t += 256) acc += probs[static_cast<long>(t) * E + e];
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) psum[e] = part[0];
+}
+
 // One block: segment layout for E routed + ns shared experts.
 __global__ void moe_plan_kernel(const int* __restrict__ counts, int E, int ns, int N,
                                 int* __restrict__ seg_start, int* __restrict__ seg_count,
@@ -376,6 +394,10 @@ void moe_route(const MoeRouteArgs& a, cudaStream_t s) {
   if (a.E > kMaxE || a.k > 32 || a.k > a.E) throw std::runtime_error("moe_route: E <= 256, k <= 32");
   moe_route_kernel<<<(a.N + 7) / 8, 256, 0, s>>>(a);
   count_launch();
+  if (deterministic() && a.probs != nullptr && a.psum != nullptr) {
+    moe_psum_fixed_kernel<<<a.E, 256, 0, s>>>(a.probs, a.N, a.E, a.psum);
+    count_launch();
+  }
 }
 
 void moe_plan(const int* counts, int E, int ns, int N, int* seg_start, int* seg_count,

@@ -291,6 +291,119 @@ def bench_conv3d(iters: int = 10):
                           "cudnn_tflops": round(flops / ms_ref / 1e9, 1)}), flush=True)
 
 
+def bench_groupnorm(iters: int = 10, small: bool = False):
+    """VAE GroupNorm(32) + SiLU forward and backward (channels-last) at the encoder's
+    level-0 activation (8 frames x 128 ch x 256x512, 268 MB bf16), vs PyTorch's GroupNorm
+    + SiLU. Roofline: the forward reads x once for statistics and once to normalise and
+    writes y; the backward reads dy and x and writes dx."""
+    import torch.nn.functional as F
+
+    from .conv3d import group_norm_silu
+
+    B, C, T, H, W = (1, 128, 2, 128, 256) if small else (1, 128, 8, 256, 512)
+    x = torch.randn(B, C, T, H, W, device="cuda").bfloat16().contiguous(
+        memory_format=torch.channels_last_3d).requires_grad_(True)
+    w = torch.ones(C, device="cuda", requires_grad=True)
+    b = torch.zeros(C, device="cuda", requires_grad=True)
+    dy = torch.randn(B, C, T, H, W, device="cuda").bfloat16().contiguous(
+        memory_format=torch.channels_last_3d)
+    nbytes = x.numel() * 2
+    y = group_norm_silu(x, 32, w, b)
+    ms_f = _timeit(lambda: group_norm_silu(x, 32, w, b), iters)
+    ms_b = _timeit(lambda: torch.autograd.grad(group_norm_silu(x, 32, w, b), (x,), dy), iters)
+    ms_rf = _timeit(lambda: F.silu(F.group_norm(x, 32, w, b)), iters)
+    print(json.dumps({"kernel": "groupnorm_silu_fwd", "shape": [B, C, T, H, W], "ms": round(ms_f, 4),
+                      "gbs": round(3 * nbytes / ms_f / 1e6, 1), "torch_ms": round(ms_rf, 4)}), flush=True)
+    print(json.dumps({"kernel": "groupnorm_silu_fwd+bwd", "ms": round(ms_b, 4),
+                      "gbs_bwd_only": round(6 * nbytes / max(ms_b - ms_f, 1e-6) / 1e6, 1)}), flush=True)
+    del y
+
+
+def bench_kv_attn(iters: int = 20, small: bool = False):
+    """Rollout chunk attention over the rolling KV cache at the DiT-B rollout shape:
+    a 4-frame chunk (2048 queries) against the 32-frame window plus the chunk
+    (18432 keys), frame-causal with absolute offsets, 12 heads, batch 1 and 16. Roofline:
+    the K/V window bytes read (the FLOPs are small at batch 1)."""
+    import math
+
+    from ._ext import ext
+
+    H, tpf = 12, 512
+    d = H * 64
+    Tq, S = 4 * tpf, 36 * tpf
+    for B in ((1,) if small else (1, 16)):
+        q = (torch.randn(B * Tq, d, device="cuda") * 0.5).bfloat16()
+        kv = (torch.randn(B * S, 2 * d, device="cuda") * 0.5).bfloat16()
+        o = torch.empty(B * Tq, d, device="cuda", dtype=torch.bfloat16)
+        pos = S - Tq  # the chunk is the newest 4 frames of the window
+
+        def fwd():
+            ext().attn_fwd(q, kv, kv, o, None, 0, 0, d, 0, B, H, Tq, S, Tq, S, 1, tpf, pos, 0,
+                           1.0 / math.sqrt(64), None, None, None)
+
+        fwd()
+        ms = _timeit(fwd, iters)
+        kv_bytes = 2 * B * S * d * 2
+        flops = 4.0 * B * H * Tq * S * 64
+        print(json.dumps({"kernel": "attn_fwd_kvcache", "B": B, "Tq": Tq, "S": S, "ms": round(ms, 4),
+                          "tflops": round(flops / ms / 1e9, 1),
+                          "kv_gbs": round(kv_bytes / ms / 1e6, 1)}), flush=True)
+
+
+def bench_moe_gemm(iters: int = 10, N: int = 32768, d: int = 1024, E: int = 64, k: int = 6,
+                   F: int = 512, ns: int = 2, small: bool = False):
+    """Grouped (MoE) SwiGLU and down GEMMs of one MoE-DiT-L layer on one GPU (random
+    router, skewed counts), vs one cuBLAS matmul per expert over the same rows."""
+    from ..layers.mlp import pack_swiglu
+    from ._ext import ext
+    from .gemm import EPI
+
+    if small:
+        N = 8192
+    torch.manual_seed(0)
+    h = (torch.randn(N, d, device="cuda") * 0.5).bfloat16()
+    logits = torch.randn(N, E, device="cuda") * 2.0
+    idx, w, sw, probs, counts, psum = ext().moe_route(logits, torch.zeros(E, device="cuda"), E, k, ns, True)
+    mt = (N * k + 127) // 128 + E + ns * ((N + 127) // 128)
+    plan = ext().moe_plan(counts, E, ns, N, mt)
+    rows = mt * 128
+    xp = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+    ext().moe_dispatch(h, idx, plan[0], plan[1], plan[7], xp, E, ns)
+    Ep = E + ns
+    w13 = (torch.randn(Ep, 2 * F, d, device="cuda") * 0.02).bfloat16()
+    w2 = (torch.randn(Ep, d, F, device="cuda") * 0.02).bfloat16()
+    gu = torch.empty(rows, 2 * F, device="cuda", dtype=torch.bfloat16)
+    act = torch.empty(rows, F, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+    tables = (plan[2], plan[3], plan[4], plan[5], plan[6], mt)
+
+    def ours():
+        ext().gemm_grouped(xp, w13, gu, EPI["swiglu"], False, 1, *tables, None, act)
+        ext().gemm_grouped(act, w2, y, EPI["bf16"], False, 1, *tables, None, None)
+
+    seg = plan[0].cpu().tolist()
+    cnt = plan[1].cpu().tolist()
+
+    def per_expert():
+        for e in range(Ep):
+            if cnt[e]:
+                xs = xp[seg[e]:seg[e] + cnt[e]]
+                g = xs @ w13[e].t()
+                a = torch.nn.functional.silu(g[:, :F]) * g[:, F:]
+                y[seg[e]:seg[e] + cnt[e]] = a @ w2[e].t()
+
+    ours()
+    ms = _timeit(ours, iters)
+    ms_ref = _timeit(per_expert, max(3, iters // 2))
+    routed_rows = float(sum(cnt))
+    flops = 2.0 * routed_rows * d * (2 * F) + 2.0 * routed_rows * F * d
+    print(json.dumps({"kernel": "gemm_grouped (swiglu + down)", "tokens": N, "experts": E, "top_k": k,
+                      "shared": ns, "rows": int(routed_rows), "max_rows_per_expert": int(max(cnt[:E])),
+                      "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                      "cublas_loop_ms": round(ms_ref, 4),
+                      "cublas_loop_tflops": round(flops / ms_ref / 1e9, 1)}), flush=True)
+
+
 def bench_ep(iters: int = 5, d: int = 1024, E: int = 64, k: int = 6, F: int = 512, ns: int = 2,
              N: int = 32768, transport: str = "fused"):
     """Expert-parallel MoE layer on all ranks of a torchrun job (one per GPU): device time
@@ -462,6 +575,8 @@ def main():
             bench_ep(args.iters, transport=args.transport)
         elif w == "optim":
             bench_optim(args.iters, transport=args.transport)
+        elif w in ("groupnorm", "kv_attn", "moe_gemm"):
+            globals()[f"bench_{w}"](args.iters, small=args.small)
         else:
             globals()[f"bench_{w}"](args.iters)
     from ._ext import check_device_status

@@ -2,11 +2,14 @@
 checker, which this framework does not rely on):
 
 ``deterministic``
-    Index-driven permutations assign rows in a fixed order: the MoE dispatch places the
-    routes to each expert in (token, route) order with a stable counting sort instead of
-    by atomic arrival, so the expert weight-gradient reductions and every later sum repeat
-    bit for bit from run to run. The default (atomic) order is correct but its rounding
-    varies with thread timing.
+    Reductions whose rounding would depend on thread timing run in a fixed order: the
+    MoE dispatch places the routes to each expert in (token, route) order with a stable
+    counting sort instead of by atomic arrival, the router's per-expert probability sums
+    use a fixed-order reduction instead of float atomics, and fp32-accumulating GEMMs
+    (weight gradients) run without split-K, so each output element has one writer. The
+    MoE layer's forward and all its gradients then repeat bit for bit from run to run.
+    Not covered: the attention backward's dQ, which CTAs of different key tiles add with
+    TMA reductions (correct, but its last bits vary between runs).
 ``check_bounds``
     The MoE dispatch / combine / un-permute kernels check every table-derived index
     (expert ids, row slots) against the extent of the buffer it addresses; the first bad

@@ -23,7 +23,7 @@ def test_deterministic_dispatch_is_a_stable_sort():
     torch.manual_seed(1)
     N, E, k, ns, d = 3000, 16, 4, 1, 256
     h = torch.randn(N, d, device="cuda").bfloat16()
-    logits = torch.randn(N, E, device="cuda")
+    logits = torch.randn(N, E + ns, device="cuda")  # routed, then shared-gate logits
     idx, w, sw, probs, counts, psum = ext().moe_route(logits, torch.zeros(E, device="cuda"), E, k, ns, True)
     mt = (N * k + 127) // 128 + E + ns * ((N + 127) // 128)
     plan = ext().moe_plan(counts, E, ns, N, mt)
@@ -72,7 +72,7 @@ def test_bounds_mode_reports_a_bad_expert_id_and_a_bad_slot():
     reset_device_status()
     N, E, k, ns, d = 512, 8, 2, 1, 128
     h = torch.randn(N, d, device="cuda").bfloat16()
-    logits = torch.randn(N, E, device="cuda")
+    logits = torch.randn(N, E + ns, device="cuda")
     idx, w, sw, probs, counts, psum = ext().moe_route(logits, torch.zeros(E, device="cuda"), E, k, ns, True)
     mt = (N * k + 127) // 128 + E + ns * ((N + 127) // 128)
     plan = ext().moe_plan(counts, E, ns, N, mt)
