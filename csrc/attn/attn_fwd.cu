@@ -74,9 +74,6 @@ __device__ __forceinline__ int row_limit(const AttnArgs& a, int q_local) {
 }
 
 
-// SPARSE: SLA block-pair lists (the softmax skips the exponentials of masked key halves);
-// otherwise dense / causal masks. Two instantiations keep the dense softmax unchanged.
-template <bool SPARSE>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
@@ -112,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = bh / a.H;
   const int h = bh % a.H;
   const int q0 = qt * 128;
-  constexpr bool sparse = SPARSE;
+  const bool sparse = a.pair_count != nullptr;
   const long list_idx = static_cast<long>(bh) * n_qtiles + qt;
   int ntiles;
   if (sparse) {
@@ -301,21 +298,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
       if (tw) fwd_trace(tr, 2, 1, j);
-      // key halves of this tile that carry no selected block for this row's query half
-      // (warp-uniform: a warp's 32 rows share their query half); their exponentials are
-      // skipped below, which matters because the forward is bound by the exp unit
-      bool live0 = true, live1 = true;
       if (sparse) {
         const int bits = a.pair_mask[list_idx * a.max_pairs + j];
-        live0 = row_ok && ((bits >> (qhalf * 2)) & 1);
-        live1 = row_ok && ((bits >> (qhalf * 2 + 1)) & 1);
-        if (!live0) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) sf[c] = -INFINITY;
+        for (int kh = 0; kh < 2; ++kh) {
+          if (!((bits >> (qhalf * 2 + kh)) & 1)) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) sf[kh * 64 + c] = -INFINITY;
+          }
         }
-        if (!live1) {
+        if (!row_ok) {
 #pragma unroll
-          for (int c = 64; c < 128; ++c) sf[c] = -INFINITY;
+          for (int c = 0; c < 128; ++c) sf[c] = -INFINITY;
         }
       } else if (j * 128 + 128 > lim) {
         const int base = j * 128;
@@ -344,41 +338,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       // exponentials packed to bf16 pairs as they are made (P lives in 64 registers)
       float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[64];
-      if constexpr (!sparse) {
 #pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const float p0 = exp2f(sf[c] * sl2 - m_use);
-          const float p1 = exp2f(sf[c + 1] * sl2 - m_use);
-          sp[c & 7] += p0;
-          sp[(c + 1) & 7] += p1;
-          pk[c >> 1] = pack_bf16(p0, p1);
-        }
-      } else if (live0) {
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          const float p0 = exp2f(sf[c] * sl2 - m_use);
-          const float p1 = exp2f(sf[c + 1] * sl2 - m_use);
-          sp[c & 7] += p0;
-          sp[(c + 1) & 7] += p1;
-          pk[c >> 1] = pack_bf16(p0, p1);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = 0u;
-      }
-      if constexpr (!sparse) {
-      } else if (live1) {
-#pragma unroll
-        for (int c = 64; c < 128; c += 2) {
-          const float p0 = exp2f(sf[c] * sl2 - m_use);
-          const float p1 = exp2f(sf[c + 1] * sl2 - m_use);
-          sp[c & 7] += p0;
-          sp[(c + 1) & 7] += p1;
-          pk[c >> 1] = pack_bf16(p0, p1);
-        }
-      } else {
-#pragma unroll
-        for (int c = 32; c < 64; ++c) pk[c] = 0u;
+      for (int c = 0; c < 128; c += 2) {
+        const float p0 = exp2f(sf[c] * sl2 - m_use);
+        const float p1 = exp2f(sf[c + 1] * sl2 - m_use);
+        sp[c & 7] += p0;
+        sp[(c + 1) & 7] += p1;
+        pk[c >> 1] = pack_bf16(p0, p1);
       }
       const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
@@ -469,12 +435,9 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (a.B <= 0 || a.H <= 0 || a.Tq <= 0) return;
   static bool attr = false;
   if (!attr) {
-    check_cuda(cudaFuncSetAttribute(attn_fwd_kernel<false>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+    check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES),
                "cudaFuncSetAttribute(attn_fwd)");
-    check_cuda(cudaFuncSetAttribute(attn_fwd_kernel<true>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
-               "cudaFuncSetAttribute(attn_fwd sparse)");
     attr = true;
   }
   const long q_rows = a.q_rows_total > 0 ? a.q_rows_total : a.B * a.q_rows_per_b;
@@ -489,12 +452,8 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   const int grid = a.B * a.H * n_qtiles;
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  if (a.pair_count != nullptr)
-    attn_fwd_kernel<true><<<grid, kThreads, SMEM_BYTES, stream>>>(tQ, tK, tV, a, n_qtiles,
-                                                                  device_status(dev), g_fwd_trace);
-  else
-    attn_fwd_kernel<false><<<grid, kThreads, SMEM_BYTES, stream>>>(tQ, tK, tV, a, n_qtiles,
-                                                                   device_status(dev), g_fwd_trace);
+  attn_fwd_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tQ, tK, tV, a, n_qtiles,
+                                                          device_status(dev), g_fwd_trace);
   count_launch();
   check_cuda(cudaGetLastError(), "attn_fwd_kernel launch");
 }

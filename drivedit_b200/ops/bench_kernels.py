@@ -362,7 +362,7 @@ def bench_moe_gemm(iters: int = 10, N: int = 32768, d: int = 1024, E: int = 64, 
         N = 8192
     torch.manual_seed(0)
     h = (torch.randn(N, d, device="cuda") * 0.5).bfloat16()
-    logits = torch.randn(N, E, device="cuda") * 2.0
+    logits = torch.randn(N, E + ns, device="cuda") * 2.0  # routed, then shared-gate logits
     idx, w, sw, probs, counts, psum = ext().moe_route(logits, torch.zeros(E, device="cuda"), E, k, ns, True)
     mt = (N * k + 127) // 128 + E + ns * ((N + 127) // 128)
     plan = ext().moe_plan(counts, E, ns, N, mt)

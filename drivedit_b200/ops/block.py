@@ -227,7 +227,8 @@ class _AllMods(torch.autograd.Function):
         dW = g.grad[w0:w0 + wn].view(-1, d)
         gemm(dm, cb, dW, epi="f32_acc", a_t=True, b_t=True)          # dW_all += dm^T c
         g.grad[b0:b0 + bn].add_(ctx.dmods.sum(0))
-        dc = gemm(dm, W_all, epi="f32_acc", b_t=True)                 # dc = dm W_all
+        # dc = dm W_all, read as dm^T [K, M] and W_all [K, N] (both MN-major, split-K)
+        dc = gemm(dm.t().contiguous(), W_all, epi="f32_acc", a_t=True, b_t=True)
         ctx.dmods = None
         return dc, None, None
 
