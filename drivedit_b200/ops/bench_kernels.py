@@ -117,7 +117,8 @@ def bench_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int
         _attn_trace(fwd, qkv, o, do, lse, delta, dq_acc, dqkv, B, H, T, tpf, sc)
 
 
-def bench_sla_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512):
+def bench_sla_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf: int = 512,
+                   small: bool = False):
     """SLA block-sparse softmax attention (top 12.5 % of 64x64 blocks, frame-causal) at
     the DiT-B training shape: routing, sparse forward and sparse backward timed
     separately. Effective TFLOP/s count only the selected (query block, key block) pairs
@@ -129,6 +130,8 @@ def bench_sla_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf:
     from ._ext import ext
     from .attention_kernels import sla_plan_kernel
 
+    if small:
+        B = 2
     d = H * 64
     torch.manual_seed(0)
     qkv = (torch.randn(B * T, 3 * d, device="cuda") * 0.5).bfloat16()
@@ -311,7 +314,8 @@ def bench_groupnorm(iters: int = 10, small: bool = False):
     y = group_norm_silu(x, 32, w, b)
     ms_f = _timeit(lambda: group_norm_silu(x, 32, w, b), iters)
     ms_b = _timeit(lambda: torch.autograd.grad(group_norm_silu(x, 32, w, b), (x,), dy), iters)
-    ms_rf = _timeit(lambda: F.silu(F.group_norm(x, 32, w, b)), iters)
+    wb, bb = w.detach().bfloat16(), b.detach().bfloat16()
+    ms_rf = _timeit(lambda: F.silu(F.group_norm(x, 32, wb, bb)), iters)
     print(json.dumps({"kernel": "groupnorm_silu_fwd", "shape": [B, C, T, H, W], "ms": round(ms_f, 4),
                       "gbs": round(3 * nbytes / ms_f / 1e6, 1), "torch_ms": round(ms_rf, 4)}), flush=True)
     print(json.dumps({"kernel": "groupnorm_silu_fwd+bwd", "ms": round(ms_b, 4),
@@ -575,7 +579,7 @@ def main():
             bench_ep(args.iters, transport=args.transport)
         elif w == "optim":
             bench_optim(args.iters, transport=args.transport)
-        elif w in ("groupnorm", "kv_attn", "moe_gemm"):
+        elif w in ("groupnorm", "kv_attn", "moe_gemm", "sla_attn"):
             globals()[f"bench_{w}"](args.iters, small=args.small)
         else:
             globals()[f"bench_{w}"](args.iters)
