@@ -57,15 +57,25 @@ def init_dist(ws, local, timeout_s=300):
                                 device_id=torch.device("cuda", local))
 
 
-def check_device_free(rank, local, min_free_frac=0.5):
-    """Print this rank's free / total device memory; refuse to start on a GPU that
-    another process already fills (a leftover job would make the run fail later)."""
-    free, total = torch.cuda.mem_get_info(local)
+def check_device_free(rank, local, min_free_frac=0.5, wait_s=120.0):
+    """Print this rank's free / total device memory. A GPU that another process still
+    fills (a job that is being torn down) is polled every 2 s for up to ``wait_s``
+    seconds; the run refuses to start if the memory is not released by then."""
+    t0 = time.time()
+    while True:
+        free, total = torch.cuda.mem_get_info(local)
+        if free >= min_free_frac * total or time.time() - t0 >= wait_s:
+            break
+        if time.time() - t0 < 2.5:
+            print(f"[rank {rank}] cuda:{local} free {free / 2**30:.1f} GiB: waiting for "
+                  f"another process to release the GPU", file=sys.stderr, flush=True)
+        time.sleep(2.0)
     print(f"[rank {rank}] cuda:{local} free {free / 2**30:.1f} / {total / 2**30:.1f} GiB",
           file=sys.stderr, flush=True)
     if free < min_free_frac * total:
         raise RuntimeError(f"rank {rank}: cuda:{local} has only {free / 2**30:.1f} GiB of "
-                           f"{total / 2**30:.1f} GiB free; another process holds the GPU")
+                           f"{total / 2**30:.1f} GiB free after {wait_s:.0f} s; another "
+                           f"process holds the GPU")
 
 
 def max_over_ranks(x: float) -> float:

@@ -60,7 +60,9 @@ struct AttnBwdArgs {
   void* dv = nullptr;
   long lddv = 0;
   int dv_col = 0;
-  // block-sparse transpose lists: per (b, h, kv-tile of 128) the q-tiles that see it
+  // block-sparse transpose lists: per (b, h, kv-tile of 128) the 64-query blocks that see
+  // it, two per 128-query unit: qa | qb << 16 (rows 0-63 of the unit are block qa, rows
+  // 64-127 block qb; qb == qa with its half masked off for an odd last block)
   const int* kv_qtiles = nullptr;    // [B*H*n_kvtiles, max_q]
   const uint8_t* kv_qmask = nullptr; // 4 bits: (q half)*2 + (key half)
   const int* kv_count = nullptr;

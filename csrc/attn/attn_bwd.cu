@@ -1,8 +1,11 @@
 // tcgen05 flash-attention backward, d_head = 64, for sm_100a (KV-stationary).
 //
 // One CTA = one (batch, head, 128-key tile = two adjacent 64-key blocks); it walks the
-// 128-query tiles that can see its keys (all later frames for frame-causal, or the SLA
-// transpose list). Per query tile, with the key tile's K and V resident in shared memory:
+// 128-query units that can see its keys: the 128-query tiles of all later frames
+// (frame-causal), or for SLA the query blocks that selected one of its two key blocks,
+// two 64-query blocks per unit in any combination (routing lists `kv_qtiles`), so a unit
+// carries no query block that selected neither key block. Per query unit, with the key
+// tile's K and V resident in shared memory:
 //
 //   S^T  = K Q^T      (M=128 keys, N=128 queries, K=64)        TMEM cols [  0,128)
 //   dP^T = V dO^T     (M=128, N=128, K=64)                      TMEM cols [128,256)
@@ -134,8 +137,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     nq = fq < a.Tq ? n_qtiles - qt_first : 0;
     if (k0 >= a.S) nq = 0;
   }
-  auto qtile_of = [&](int j) -> int {
-    return sparse ? g.kv_qtiles[list_idx * g.max_q + j] : qt_first + j;
+  // the unit's two 64-query blocks, qa | qb << 16
+  auto qpair_of = [&](int j) -> int {
+    if (sparse) return g.kv_qtiles[list_idx * g.max_q + j];
+    const int qt = qt_first + j;
+    return (2 * qt) | ((2 * qt + 1) << 16);
   };
 
   if (threadIdx.x == 0) {
@@ -191,19 +197,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         DDB_TRACE(0, 0, j);
-        const int qt = qtile_of(j);
-        const int qrow = static_cast<int>(b * a.q_rows_per_b) + qt * 128;
+        const int qp = qpair_of(j);
+        const int qa = qp & 0xffff, qb = (qp >> 16) & 0xffff;
+        const int rowb = static_cast<int>(b * a.q_rows_per_b);
         uint8_t* sq = smem + OFF_Q + s * TILE;
         uint8_t* sd = smem + OFF_DO + s * TILE;
         uint8_t* sv = smem + OFF_VEC + s * 1024;
-        const long vi = static_cast<long>(bh) * a.Tq + qt * 128;  // Tq % 128 == 0
+        // lse / delta of the two blocks: 64 floats (256 bytes, 16-byte aligned) each
+        const long va = static_cast<long>(bh) * a.Tq + qa * 64;
+        const long vb = static_cast<long>(bh) * a.Tq + qb * 64;
         mbar_arrive_expect_tx(&qd_full[s], 2 * TILE + 1024);
-        tma_load_2d(sq, &tmQ, &qd_full[s], a.q_col + h * 64, qrow);
-        tma_load_2d(sq + 8192, &tmQ, &qd_full[s], a.q_col + h * 64, qrow + 64);
-        tma_load_2d(sd, &tmDO, &qd_full[s], g.do_col + h * 64, qrow);
-        tma_load_2d(sd + 8192, &tmDO, &qd_full[s], g.do_col + h * 64, qrow + 64);
-        bulk_load(sv, a.lse + vi, 512, &qd_full[s]);
-        bulk_load(sv + 512, g.delta + vi, 512, &qd_full[s]);
+        tma_load_2d(sq, &tmQ, &qd_full[s], a.q_col + h * 64, rowb + qa * 64);
+        tma_load_2d(sq + 8192, &tmQ, &qd_full[s], a.q_col + h * 64, rowb + qb * 64);
+        tma_load_2d(sd, &tmDO, &qd_full[s], g.do_col + h * 64, rowb + qa * 64);
+        tma_load_2d(sd + 8192, &tmDO, &qd_full[s], g.do_col + h * 64, rowb + qb * 64);
+        bulk_load(sv, a.lse + va, 256, &qd_full[s]);
+        bulk_load(sv + 256, a.lse + vb, 256, &qd_full[s]);
+        bulk_load(sv + 512, g.delta + va, 256, &qd_full[s]);
+        bulk_load(sv + 768, g.delta + vb, 256, &qd_full[s]);
         ++issued;
       }
       if (!ok) {
@@ -323,7 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < nq; ++j) {
       const int s = j % NS;
       const int pb = j & 1;
-      const int q0 = qtile_of(j) * 128;
+      // first query of the unit; only the dense (adjacent-block) masks read it
+      const int q0 = (qpair_of(j) & 0xffff) * 64;
       const float* s_lse = reinterpret_cast<const float*>(smem + OFF_VEC + s * 1024);
       const float* s_delta = s_lse + 128;
       const int bits = sparse ? g.kv_qmask[list_idx * g.max_q + j] : 0xF;
@@ -508,9 +520,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (issuer) {
         staged = mbar_wait(dq_staged, j & 1, abort_flag);
         if (staged && !(g.debug_flags & 1)) {
-          const int row0 = static_cast<int>(b * a.q_rows_per_b) + qtile_of(j) * 128;
-          tma_reduce_add_2d(&tmDQ, stage, h * 64, row0);
-          tma_reduce_add_2d(&tmDQ, stage + TILE, h * 64 + 32, row0);
+          // rows 0-63 of the staged boxes belong to block qa, rows 64-127 to block qb;
+          // a half whose mask is empty (odd last block) adds nothing
+          const int qp = qpair_of(j);
+          const int bits = sparse ? g.kv_qmask[list_idx * g.max_q + j] : 0xF;
+          const int rowb = static_cast<int>(b * a.q_rows_per_b);
+#pragma unroll
+          for (int qh = 0; qh < 2; ++qh) {
+            if (!((bits >> (2 * qh)) & 3)) continue;
+            const int row0 = rowb + ((qp >> (16 * qh)) & 0xffff) * 64;
+            tma_reduce_add_2d(&tmDQ, stage + qh * 8192, h * 64, row0);
+            tma_reduce_add_2d(&tmDQ, stage + TILE + qh * 8192, h * 64 + 32, row0);
+          }
           tma_store_commit();
           tma_store_wait_read();
         }
@@ -619,8 +640,9 @@ void launch_bwd(const AttnBwdArgs& g, int* status, cudaStream_t stream) {
                                 a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tDO = make_tmap_2d(g.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.lddo, q_rows,
                                  g.lddo * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  // dQ reduce-add boxes: 32 fp32 columns x 64 rows (one query block)
   CUtensorMap tDQ = make_tmap_2d(g.dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.ld_dqacc, a.B * a.q_rows_per_b,
-                                 g.ld_dqacc * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+                                 g.ld_dqacc * 4, 32, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   const int n_kvtiles = (a.S + 127) / 128;
   const int n_qtiles = (a.Tq + 127) / 128;
   attn_bwd_kernel<<<a.B * a.H * n_kvtiles, kThreads, SMEM_BYTES, stream>>>(

@@ -8,7 +8,8 @@
 //                     matrix W = valid & ~selected (bf16, for the batched GEMM), the
 //                     forward pair lists (per 128-query tile, the union of its two blocks'
 //                     selections paired into 128-key tiles, 4-bit half masks) and the
-//                     backward lists (per 128-key tile, the query tiles that selected it).
+//                     backward lists (per 128-key tile, the query blocks that selected
+//                     it, paired into 128-query units).
 // Linear branch (phi = elu + 1; reference layers/sla.py:333-357 per block pair, here over
 // all allowed-but-unselected blocks at once), per-block products on the tensor cores in
 // sla_tc.cu:
@@ -175,18 +176,31 @@ __global__ void __launch_bounds__(kRouteThreads) sla_route_kernel(SlaRouteArgs a
     }
     a.pair_count[li] = min(n, a.max_pairs);
   }
-  // backward lists: per key tile t (blocks 2t, 2t+1), the query tiles that selected it
+  // backward lists: per key tile t (blocks 2t, 2t+1), the query blocks that selected
+  // either key block, ascending and paired two at a time into 128-query units (any two
+  // blocks, not only neighbours, so a unit wastes at most its key-half masking); an odd
+  // last block is paired with itself with its second half masked off
   for (int t = threadIdx.x; t < nt; t += kRouteThreads) {
     const long li = static_cast<long>(bh) * nt + t;
-    int n = 0;
-    for (int i = 0; i < nt; ++i) {
-      const uint32_t m = bit(2 * i, 2 * t) | (bit(2 * i, 2 * t + 1) << 1) |
-                         (bit(2 * i + 1, 2 * t) << 2) | (bit(2 * i + 1, 2 * t + 1) << 3);
-      if (m) {
-        a.kv_qtiles[li * nt + n] = i;
-        a.kv_qmask[li * nt + n] = static_cast<uint8_t>(m);
+    int n = 0, pending = -1;
+    uint32_t pending_m = 0;
+    for (int i = 0; i < nb; ++i) {
+      const uint32_t m = bit(i, 2 * t) | (bit(i, 2 * t + 1) << 1);
+      if (!m) continue;
+      if (pending < 0) {
+        pending = i;
+        pending_m = m;
+      } else {
+        a.kv_qtiles[li * nt + n] = pending | (i << 16);
+        a.kv_qmask[li * nt + n] = static_cast<uint8_t>(pending_m | (m << 2));
         ++n;
+        pending = -1;
       }
+    }
+    if (pending >= 0) {
+      a.kv_qtiles[li * nt + n] = pending | (pending << 16);
+      a.kv_qmask[li * nt + n] = static_cast<uint8_t>(pending_m);
+      ++n;
     }
     a.kv_count[li] = n;
   }

@@ -20,7 +20,7 @@ struct SlaRouteArgs {
   uint8_t* pair_mask = nullptr;
   int* pair_count = nullptr;      // [B*H*nb/2]
   int max_pairs = 0;
-  int* kv_qtiles = nullptr;       // [B*H*nb/2, nb/2]
+  int* kv_qtiles = nullptr;       // [B*H*nb/2, nb/2]: query-block pairs qa | qb << 16
   uint8_t* kv_qmask = nullptr;
   int* kv_count = nullptr;
 };

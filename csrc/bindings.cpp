@@ -1377,6 +1377,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("idx"), py::arg("ret"), py::arg("El"), py::arg("residual") = py::none(),
         py::arg("shared_w") = py::none(), py::arg("slot_s") = py::none(), py::arg("ys") = py::none());
   m.def("gemm", &gemm, "tcgen05 GEMM D = A B^T with fused epilogue");
+  m.def("gemm_set_pair_mode", [](int64_t mode) { return static_cast<int64_t>(ddb::gemm_set_pair_mode(static_cast<int>(mode))); },
+        "CTA-pair GEMM tiles: -1 auto, 0 off, 1 whenever eligible; returns the previous mode");
   m.def("read_status", &read_status, "device status word (0 = ok)");
   m.def("read_status_index", &read_status_index, "index recorded with a bad-index status");
   m.def("set_deterministic", &ddb::set_deterministic, "fixed-order MoE permutation on/off");

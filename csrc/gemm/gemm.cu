@@ -16,12 +16,23 @@
 // Tiles are walked persistently (n fastest, so concurrent CTAs share the A panel in L2);
 // the epilogue of tile i overlaps the MMAs of tile i+1.
 //
+// CTA-pair mode (PAIR, clusters of 2 on two SMs, cta_group::2): a tile is 256 x BN; each
+// CTA loads its own 128 rows of A and half (BN/2 rows) of B into its own shared memory
+// with plain TMA loads that count on the even CTA's `full` barrier; the even CTA issues
+// one M=256 MMA per K step, which reads A and B from both CTAs, and each CTA's TMEM
+// receives its 128 rows of D. Per FLOP a CTA then stages and reads a third less
+// operand data than in 128 x 256 single-CTA tiles (the B half instead of all of B).
+// The even CTA's MMA commits free the ring slots and hand accumulators to the epilogue
+// of both CTAs; the odd CTA's epilogue warps release the accumulator on the even CTA's
+// barrier. No load is multicast.
+//
 // Replaces every nn.Linear of the reference (layers/mha.py:307-308, layers/mlp.py:112-114,
 // layers/moe.py:54-56) and carries the SwiGLU (layers/mlp.py:131-155), rotary
 // (layers/rope_v2.py:95-148) and residual epilogues.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -51,15 +62,17 @@ constexpr int kOutStage = kOffC + 4 * 2 * kOutBoxD;
 // bf16 outputs with a second output or a C operand (all boxes, one operand stage fewer).
 enum GemmLayout : int { kLayF32 = 0, kLayOut = 1, kLayOutC = 2 };
 
-template <int BN, int LAY>
+template <int BN, int LAY, bool PAIR = false>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // a pair CTA holds half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = LAY == kLayOutC ? ((BN == 256) ? 3 : 4) : ((BN == 256) ? 4 : 6);
+  static constexpr int OUT_BYTES = LAY == kLayOutC ? kOutStage : (LAY == kLayOut ? kOffD2 : 0);
+  static constexpr int PAIR_STAGES = (232448 - 1280 - OUT_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = PAIR ? (PAIR_STAGES > 8 ? 8 : PAIR_STAGES)
+                                     : (LAY == kLayOutC ? ((BN == 256) ? 3 : 4) : ((BN == 256) ? 4 : 6));
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int OFF_OUT = STAGES * STAGE_BYTES;   // epilogue boxes
-  static constexpr int OUT_BYTES = LAY == kLayOutC ? kOutStage : (LAY == kLayOut ? kOffD2 : 0);
   static constexpr int OFF_BAR = OFF_OUT + OUT_BYTES;    // mbarriers, TMEM slot, abort flag
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
@@ -145,6 +158,7 @@ __device__ __forceinline__ uint4 box_chunk(uint32_t box, int lane, int chunk) {
 
 struct Sched {
   int tiles_m, tiles_n, kblocks, kb_per_split, splits, total, M;
+  int bm;  // rows per tile: 128, or 256 for CTA pairs
   int grouped;
   const int* g_tile_expert;
   const int* g_tile_row;
@@ -170,7 +184,7 @@ struct Sched {
     t /= tiles_m;
     int split = t % splits;
     bt = t / splits;
-    m0 = m_idx * BM;
+    m0 = m_idx * bm;
     if (grouped == 2) {
       kb0 = __ldg(g_kstart + bt);
       kb1 = __ldg(g_kend + bt);
@@ -453,16 +467,21 @@ struct PeerMaps {
 };
 
 // ---------------------------------------------------------------- kernel
-template <int BN, bool A_MN, bool B_MN, int EPI, int LAY>
+template <int BN, bool A_MN, bool B_MN, int EPI, int LAY, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args,
                    const Sched sched, int* status, const __grid_constant__ PeerMaps pmA,
                    const __grid_constant__ OutMaps om) {
   constexpr bool kBf16Out = LAY != kLayF32;
-  using Cfg = GemmCfg<BN, LAY>;
+  using Cfg = GemmCfg<BN, LAY, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC = make_idesc_bf16(BM, BN, A_MN, B_MN);
+  constexpr uint32_t IDESC = make_idesc_bf16(PAIR ? 2 * BM : BM, BN, A_MN, B_MN);
+  // CTA pairs: rank in the pair, tiles walked per cluster, this CTA's rows of a tile
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int t_begin = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int t_step = PAIR ? static_cast<int>(nclusters_x()) : static_cast<int>(gridDim.x);
+  const int m_off = static_cast<int>(crank) * BM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -486,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], PAIR ? 8 : 4);  // pairs: both CTAs' epilogue warps
     }
     mbar_init(drain_bar, 1);
     for (int i = 0; i < 8; ++i) mbar_init(&cin_bar[i], 1);
@@ -497,11 +516,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int p = 0; p < args.a_npeers; ++p) tma_prefetch_desc(&pmA.m[p]);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // pairs: both CTAs' barriers are initialised before either CTA signals the other's
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -513,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool ok = true;
       uint64_t ready = 0;  // row groups (< 64) whose gathered B this CTA has acquired
-      for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
+      for (int t = t_begin; t < sched.total && ok; t += t_step) {
         int m0, nt, kb0, kb1, bt;
         if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
         const int n0 = nt * BN;
@@ -545,6 +571,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
+          if constexpr (PAIR) {
+            // both CTAs' bytes count on the even CTA's barrier (its MMA reads both)
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            const int ma = m0 + m_off;
+            const int nb0 = n0 + static_cast<int>(crank) * (BN / 2);
+            if constexpr (A_MN) {
+              tma_load_3d_pair(sa, &tmA, fb, ma, kb * BK, ab);
+              tma_load_3d_pair(sa + 8192, &tmA, fb, ma + 64, kb * BK, ab);
+            } else {
+              tma_load_3d_pair(sa, &tmA, fb, kb * BK, ma, ab);
+            }
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / 128; ++c)
+                tma_load_3d_pair(sb + c * 8192, &tmB, fb, nb0 + c * 64, kb * BK, bb);
+            } else {
+              tma_load_3d_pair(sb, &tmB, fb, kb * BK, nb0, bb);
+            }
+            ++issued;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           if constexpr (A_MN) {
             tma_load_3d(sa, &tmA, &full[stage], m0, kb * BK, ab);
@@ -572,9 +624,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         record_status(status, kStatusTimeoutProducer);
         *abort_flag = 1;
-        // let copies already in flight land before the CTA exits (bounded)
+        // let copies already in flight land before the CTA exits (bounded); a pair's
+        // copies all count on the even CTA's barriers
         int s = stage, ph = phase;
-        for (int i = 0; i < min(issued, STAGES); ++i) {
+        for (int i = 0; i < ((PAIR && crank != 0) ? 0 : min(issued, STAGES)); ++i) {
           if (--s < 0) {
             s = STAGES - 1;
             ph ^= 1;
@@ -587,14 +640,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // (pairs: the even CTA issues for both; the odd CTA's MMA warp only owns its TMEM)
+    if (lane == 0 && crank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       bool any = false;
-      for (int t = blockIdx.x; t < sched.total && ok; t += gridDim.x) {
+      // signal an mbarrier of this CTA (and, for pairs, the same one of the odd CTA)
+      auto commit_both = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          mma_commit_pair(smem_u32(bar));
+          mma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
+      for (int t = t_begin; t < sched.total && ok; t += t_step) {
         int m0, nt, kb0, kb1, bt;
         if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort_flag)) {
@@ -617,17 +680,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                                : make_sw128_desc(sa + kk * 32, 16, 1024);
             uint64_t db = B_MN ? make_sw128_desc(sb + kk * 2048, 8192, 1024)
                                : make_sw128_desc(sb + kk * 32, 16, 1024);
-            mma_bf16_ss(d_tmem, da, db, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              mma_bf16_ss_pair(d_tmem, da, db, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else
+              mma_bf16_ss(d_tmem, da, db, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           any = true;
-          mma_commit(&empty[stage]);
+          commit_both(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        mma_commit(&acc_full[buf]);
+        commit_both(&acc_full[buf]);
         if (++buf == 2) {
           buf = 0;
           acc_phase ^= 1;
@@ -639,7 +705,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (any) {
         // all MMAs of this thread complete before TMEM is released
-        mma_commit(drain_bar);
+        if constexpr (PAIR)
+          mma_commit_pair(smem_u32(drain_bar));
+        else
+          mma_commit(drain_bar);
         long long t0 = clock64();
         while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < kSpinLimitCycles / 8) {
         }
@@ -668,6 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (args.C == nullptr || tp >= sched.total) return;
         int pm0, pnt, pk0, pk1, pbt;
         if (!sched.decode(tp, pm0, pnt, pk0, pk1, pbt)) return;
+        pm0 += m_off;
         if (pm0 + row_in_tile >= args.M) return;
         const long prow = (sched.grouped == 1 ? 0 : static_cast<long>(pbt) * args.M) + pm0 + row_in_tile;
         const int c0 = (EPI == kEpiDSwiGLU ? 2 : 1) * pnt * BN;
@@ -679,12 +749,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     if (args.gb_world > 1) gather_weight_pieces(args, threadIdx.x - 64);
-    prefetch_c(blockIdx.x);
-    for (int t = blockIdx.x; t < sched.total; t += gridDim.x) {
+    prefetch_c(t_begin);
+    for (int t = t_begin; t < sched.total; t += t_step) {
       int m0, nt, kb0, kb1, bt;
       if (!sched.decode(t, m0, nt, kb0, kb1, bt)) continue;
+      m0 += m_off;  // this CTA's rows of a pair tile
       const int n0 = nt * BN;
-      prefetch_c(t + gridDim.x);
+      prefetch_c(t + t_step);
       // TMA loads of this tile's C boxes (two in flight), issued before the accumulator
       // is ready: DSwiGLU reads one 64-column gu box per 32 accumulator columns, the
       // residual epilogues one box per 64 columns
@@ -783,7 +854,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!c_ok) break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) {
+        if (PAIR && crank != 0)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+        else
+          mbar_arrive(&acc_empty[buf]);
+      }
       if (++buf == 2) {
         buf = 0;
         acc_phase ^= 1;
@@ -800,18 +876,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // pairs: the even CTA's MMAs (which write the odd CTA's TMEM and read its shared
+  // memory) are drained before either CTA releases TMEM or exits
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
 // ---------------------------------------------------------------- host launch
-template <int BN, bool A_MN, bool B_MN, int EPI, int LAY>
+template <int BN, bool A_MN, bool B_MN, int EPI, int LAY, bool PAIR>
 void launch_lay(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
-  using Cfg = GemmCfg<BN, LAY>;
+  using Cfg = GemmCfg<BN, LAY, PAIR>;
   static bool attr_set = false;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, LAY>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, LAY, PAIR>;
   if (!attr_set) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     Cfg::SMEM_BYTES),
@@ -836,7 +918,7 @@ void launch_lay(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream
                       sb * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   else
     tB = make_tmap_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, nbb, a.ldb * 2,
-                      sb * 2, 64, BN, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+                      sb * 2, 64, PAIR ? BN / 2 : BN, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   PeerMaps pm;
   std::memset(&pm, 0, sizeof(pm));
   if (a.a_npeers > 0) {
@@ -873,27 +955,84 @@ void launch_lay(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream
       om.use_c = 1;
     }
   }
-  kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status, pm, om);
+  if constexpr (PAIR) {
+    // clusters of two CTAs (grid = 2 x clusters)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, kern, tA, tB, a, s, status, pm, om),
+               "gemm_tc_kernel (CTA pairs) launch");
+  } else {
+    kern<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tA, tB, a, s, status, pm, om);
+  }
   count_launch();
   check_cuda(cudaGetLastError(), "gemm_tc_kernel launch");
 }
 
+// Clusters of two 1-CTA-per-SM GEMM CTAs that can be resident at once on this device
+// (SMs pair up inside a GPC, so this can be below half the SM count).
+int pair_clusters(int dev) {
+  static int cached[64] = {0};
+  if (dev < 0 || dev >= 64) return 0;
+  if (cached[dev] == 0) {
+    using Cfg = GemmCfg<256, kLayOut, true>;
+    auto kern = gemm_tc_kernel<256, false, false, kEpiBf16, kLayOut, true>;
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES),
+               "cudaFuncSetAttribute(gemm pair smem)");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms(dev), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = -1;  // pairs unavailable
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
 // layout by epilogue: fp32 outputs need no boxes; SwiGLU (second output), dSwiGLU and
 // residual epilogues with a C operand take all boxes; other bf16 outputs the D boxes only
-template <int BN, bool A_MN, bool B_MN, int EPI>
-void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
+void launch_p(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
   if constexpr (EPI == kEpiF32 || EPI == kEpiF32Atomic) {
-    launch_lay<BN, A_MN, B_MN, EPI, kLayF32>(a, s, grid, stream, status);
+    launch_lay<BN, A_MN, B_MN, EPI, kLayF32, PAIR>(a, s, grid, stream, status);
   } else if constexpr (EPI == kEpiSwiGLU || EPI == kEpiDSwiGLU) {
-    launch_lay<BN, A_MN, B_MN, EPI, kLayOutC>(a, s, grid, stream, status);
+    launch_lay<BN, A_MN, B_MN, EPI, kLayOutC, PAIR>(a, s, grid, stream, status);
   } else if constexpr (EPI == kEpiBf16 || EPI == kEpiGateResidual) {
     if (a.C != nullptr)
-      launch_lay<BN, A_MN, B_MN, EPI, kLayOutC>(a, s, grid, stream, status);
+      launch_lay<BN, A_MN, B_MN, EPI, kLayOutC, PAIR>(a, s, grid, stream, status);
     else
-      launch_lay<BN, A_MN, B_MN, EPI, kLayOut>(a, s, grid, stream, status);
+      launch_lay<BN, A_MN, B_MN, EPI, kLayOut, PAIR>(a, s, grid, stream, status);
   } else {
-    launch_lay<BN, A_MN, B_MN, EPI, kLayOut>(a, s, grid, stream, status);
+    launch_lay<BN, A_MN, B_MN, EPI, kLayOut, PAIR>(a, s, grid, stream, status);
   }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch(const GemmArgs& a, const Sched& s, int grid, cudaStream_t stream, int* status) {
+  if (s.bm == 2 * BM)
+    launch_p<BN, A_MN, B_MN, EPI, true>(a, s, grid, stream, status);
+  else
+    launch_p<BN, A_MN, B_MN, EPI, false>(a, s, grid, stream, status);
 }
 
 template <int BN>
@@ -937,7 +1076,15 @@ void dispatch_bn(const GemmArgs& a, int epi, const Sched& s, int grid, cudaStrea
                            std::to_string(epi) + ", mode=" + std::to_string(mode) + ")");
 }
 
+int g_pair_mode = -1;
+
 }  // namespace
+
+int gemm_set_pair_mode(int mode) {
+  const int prev = g_pair_mode;
+  g_pair_mode = mode < 0 ? -1 : (mode > 0 ? 1 : 0);
+  return prev;
+}
 
 void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   GemmArgs a = a_in;
@@ -949,41 +1096,68 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   const int sms = num_sms(dev);
   const int kblocks = (a.K + BK - 1) / BK;
-  const long tiles_m = (a.M + BM - 1) / BM;
   const long nbatch = (a.grouped == 0 && a.batch > 1) ? a.batch : 1;
-  // Estimated time of a (BN, split-K) choice: waves of persistent tiles x tile work. A
-  // 128-wide tile re-reads its A tile from shared memory twice as often per FLOP and runs
-  // at ~0.8 of a 256-wide one.
-  auto est = [&](int bn_c, int sp) -> double {
-    const long items = tiles_m * ((a.N + bn_c - 1) / bn_c) * sp * nbatch;
-    const long waves = (items + sms - 1) / sms;
+  // CTA pairs (256-row tiles over two SMs) for plain GEMMs: not for grouped tables, the
+  // peer-memory operand forms, or problems of one 128-row tile
+  static const bool no_pairs = std::getenv("DDB_GEMM_NO_PAIRS") != nullptr;
+  const int clusters = (!no_pairs && g_pair_mode != 0 && a.grouped == 0 && a.a_npeers == 0 && a.d_peers == nullptr &&
+                        a.gb_world <= 1 && a.M > BM) ? pair_clusters(dev) : 0;
+  // Estimated time of a (pair, BN, split-K) choice: waves of persistent tiles x tile work
+  // at a relative efficiency. Operand bytes staged and read from shared memory per FLOP
+  // set it: a 128-wide single-CTA tile reads A twice as often per FLOP as a 256-wide one
+  // (~0.8 of it); a 256 x 256 CTA-pair tile stages a third less than a 128 x 256
+  // single-CTA tile (taken as ~1.15 of it). The SwiGLU epilogues are bound by their own
+  // memory traffic, where pairs gain nothing (measured), so they stay single-CTA.
+  const bool epi_bound = (epi == kEpiSwiGLU || epi == kEpiDSwiGLU) && g_pair_mode != 1;
+  auto est = [&](bool pr, int bn_c, int sp) -> double {
+    const long tm = (a.M + (pr ? 2 * BM : BM) - 1) / (pr ? 2 * BM : BM);
+    const long units = pr ? clusters : sms;
+    const long items = tm * ((a.N + bn_c - 1) / bn_c) * sp * nbatch;
+    const long waves = (items + units - 1) / units;
     const long kb = (kblocks + sp - 1) / sp;
-    return static_cast<double>(waves) * bn_c * kb / (bn_c == 256 ? 1.0 : 0.8);
+    const double eff = pr ? (epi_bound ? 0.0 : (bn_c == 256 ? 1.15 : 0.95))
+                          : (bn_c == 256 ? 1.0 : 0.8);
+    if (eff == 0.0) return 1e300;
+    return static_cast<double>(waves) * bn_c * kb / eff;
   };
   // split K (fp32-accumulating epilogue only) while it strictly shortens the estimate
-  auto best_splits = [&](int bn_c) {
+  auto best_splits = [&](bool pr, int bn_c) {
     int sp = 1;
     if (epi == kEpiF32Atomic) {
       // deterministic mode: one writer per output element, so the fp32 accumulation
       // does not depend on the arrival order of split-K partial sums
       if (deterministic()) return 1;
       if (a.splits > 0) return a.splits;
-      while (kblocks / (sp * 2) >= 8 && est(bn_c, sp * 2) < est(bn_c, sp)) sp *= 2;
+      while (kblocks / (sp * 2) >= 8 && est(pr, bn_c, sp * 2) < est(pr, bn_c, sp)) sp *= 2;
     }
     return sp;
   };
+  // tile shape (pair or not, width) and split-K chosen together
+  bool pair = false;
   int bn = a.bn;
-  if (bn == 0) {  // tile width and split-K chosen together
-    bn = 128;
-    if (a.N >= 256 && !(a.N % 256 != 0 && a.N < 512) &&
-        est(256, best_splits(256)) <= est(128, best_splits(128)))
-      bn = 256;
+  {
+    double best = 1e300;
+    const bool wide_ok = a.N >= 256 && !(a.N % 256 != 0 && a.N < 512);
+    for (int pr = (clusters > 0 && g_pair_mode == 1) ? 1 : 0; pr < (clusters > 0 ? 2 : 1); ++pr)
+      for (int bn_c : {128, 256}) {
+        if (a.bn != 0 && bn_c != a.bn) continue;
+        if (a.bn == 0 && bn_c == 256 && !wide_ok) continue;
+        const double e = est(pr != 0, bn_c, best_splits(pr != 0, bn_c));
+        // ties: the wider tile of the same kind; a pair only when strictly faster
+        if (e < best || (e == best && bn_c == 256 && bn != 256 && (pr != 0) == pair)) {
+          best = e;
+          pair = pr != 0;
+          bn = bn_c;
+        }
+      }
+    if (bn == 0) bn = 128;
   }
   Sched s;
-  s.tiles_m = static_cast<int>(tiles_m);
+  s.bm = pair ? 2 * BM : BM;
+  s.tiles_m = static_cast<int>((a.M + s.bm - 1) / s.bm);
   s.tiles_n = (a.N + bn - 1) / bn;
   s.kblocks = kblocks;
-  const int splits = best_splits(bn);
+  const int splits = best_splits(pair, bn);
   s.kb_per_split = (s.kblocks + splits - 1) / splits;
   s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
   s.M = a.M;
@@ -1019,6 +1193,11 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
     throw std::runtime_error("gemm: batch strides must be multiples of 8 elements");
   int grid = s.total < sms ? s.total : sms;
   if (a.max_ctas > 0 && grid > a.max_ctas) grid = a.max_ctas;
+  if (pair) {  // two CTAs per cluster, one cluster per pair tile at most
+    int nc = s.total < clusters ? s.total : clusters;
+    if (a.max_ctas > 0 && nc > a.max_ctas / 2) nc = a.max_ctas / 2 > 0 ? a.max_ctas / 2 : 1;
+    grid = 2 * nc;
+  }
   int* status = device_status(dev);
   if (bn == 256)
     dispatch_bn<256>(a, epi, s, grid, stream, status);

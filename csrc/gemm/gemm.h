@@ -95,5 +95,8 @@ struct GemmArgs {
 };
 
 void gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
+// CTA-pair (256-row, cta_group::2) tiles for plain GEMMs: -1 chosen by the cost estimate
+// (default), 0 never, 1 whenever the GEMM is eligible. Returns the previous mode.
+int gemm_set_pair_mode(int mode);
 
 }  // namespace ddb

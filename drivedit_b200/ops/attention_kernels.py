@@ -8,7 +8,8 @@ SLA (``attn_mode == "sla"``):
      frame-causal validity, top-k selection with the diagonal forced; then the
      forward pair lists (per 128-query tile, the union of its two query blocks'
      selections paired two 64-key blocks at a time, with 4-bit half masks) and the
-     backward transpose lists (per 128-key tile, the query tiles that selected it);
+     backward transpose lists (per 128-key tile, the query blocks that selected it,
+     paired two at a time into 128-query units);
   2. block-sparse softmax: the same forward/backward kernels in list mode;
   3. linear branch over the allowed-but-unselected blocks (elu+1 feature map),
      computed as block KV states combined by the (valid & ~selected) block matrix.
@@ -85,19 +86,24 @@ def sla_plan(q, k, B, T, H, cfg, tpf: Optional[int], causal: str) -> SLAPlan:
     pair_blocks = (b0 | (b1 << 16)).to(torch.int32).reshape(B * H * nt, max_pairs).contiguous()
     pair_mask = bits.reshape(B * H * nt, max_pairs).contiguous()
     pair_count = ((cnt + 1) // 2).to(torch.int32).reshape(-1).contiguous()
-    # ---- backward lists: per key tile (blocks 2t, 2t+1), the query tiles that see it
-    s4 = sel.view(B, H, nt, 2, nt, 2)
-    bits_b = (s4[:, :, :, 0, :, 0].to(torch.uint8)
-              | (s4[:, :, :, 0, :, 1].to(torch.uint8) << 1)
-              | (s4[:, :, :, 1, :, 0].to(torch.uint8) << 2)
-              | (s4[:, :, :, 1, :, 1].to(torch.uint8) << 3))      # [B,H,qt,kt]
-    bits_t = bits_b.transpose(-1, -2)                                 # [B,H,kt,qt]
-    any_t = bits_t != 0
-    art = torch.arange(nt, device=dev)
-    order_t = torch.argsort(torch.where(any_t, art, art + nt), dim=-1)
-    kv_count = any_t.sum(-1).to(torch.int32).reshape(-1).contiguous()
-    kv_qtiles = order_t.to(torch.int32).reshape(B * H * nt, nt).contiguous()
-    kv_qmask = torch.gather(bits_t, -1, order_t).reshape(B * H * nt, nt).contiguous()
+    # ---- backward lists: per key tile (blocks 2t, 2t+1), the query blocks that selected
+    # either key block, ascending, paired two at a time (qa | qb << 16; an odd last
+    # block is paired with itself and its second half masked off)
+    sk = sel.view(B, H, nb, nt, 2)                                  # [B,H,q,kt,khalf]
+    kb = (sk[..., 0].to(torch.uint8) | (sk[..., 1].to(torch.uint8) << 1)).transpose(-1, -2)
+    any_t = kb != 0                                                 # [B,H,kt,q]
+    order_t = torch.argsort(torch.where(any_t, ar, ar + nb), dim=-1)
+    cnt_t = any_t.sum(-1)                                           # [B,H,kt]
+    qa, qb = order_t[..., 0::2], order_t[..., 1::2]                 # [B,H,kt,nt]
+    pt = torch.arange(nt, device=dev)
+    va = (2 * pt) < cnt_t[..., None]
+    vb = (2 * pt + 1) < cnt_t[..., None]
+    qb = torch.where(vb, qb, qa)
+    ma = torch.where(va, torch.gather(kb, -1, qa), torch.zeros_like(qa, dtype=torch.uint8))
+    mb = torch.where(vb, torch.gather(kb, -1, qb), torch.zeros_like(qb, dtype=torch.uint8))
+    kv_count = ((cnt_t + 1) // 2).to(torch.int32).reshape(-1).contiguous()
+    kv_qtiles = (qa | (qb << 16)).to(torch.int32).reshape(B * H * nt, nt).contiguous()
+    kv_qmask = (ma | (mb << 2)).to(torch.uint8).reshape(B * H * nt, nt).contiguous()
     return SLAPlan(sel, valid, pair_blocks, pair_mask, pair_count, kv_qtiles, kv_qmask, kv_count)
 
 

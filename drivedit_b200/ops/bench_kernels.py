@@ -153,6 +153,7 @@ def bench_sla_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf:
     bits = sum(((mask >> i) & 1) for i in range(4)) * live
     selected = float(bits.sum())
     computed = float(counts.sum()) * 4  # 128 x 128 tiles = 4 block pairs each
+    computed_bwd = float(plan.kv_count.long().sum()) * 4  # 128-key x 128-query units
 
     def route():
         sla_plan_kernel(qkv, B, T, H, cfg, tpf, "frame")
@@ -172,11 +173,12 @@ def bench_sla_attn(iters: int = 10, B: int = 8, H: int = 12, T: int = 8192, tpf:
     f_pair = 64.0 * 64 * 64
     ms_r, ms_f, ms_b = _timeit(route, iters), _timeit(fwd, iters), _timeit(bwd, iters)
     print(json.dumps({"kernel": "sla_route", "B": B, "H": H, "T": T, "ms": round(ms_r, 3)}), flush=True)
-    for name, ms, mult in (("sla_attn_fwd", ms_f, 4.0), ("sla_attn_bwd", ms_b, 10.0)):
+    for name, ms, mult, comp in (("sla_attn_fwd", ms_f, 4.0, computed),
+                                 ("sla_attn_bwd", ms_b, 10.0, computed_bwd)):
         print(json.dumps({"kernel": name, "B": B, "H": H, "T": T, "ms": round(ms, 3),
-                          "selected_pairs": int(selected), "computed_pairs": int(computed),
+                          "selected_pairs": int(selected), "computed_pairs": int(comp),
                           "tflops_selected": round(mult * f_pair * selected / ms / 1e9, 1),
-                          "tflops_computed": round(mult * f_pair * computed / ms / 1e9, 1)}),
+                          "tflops_computed": round(mult * f_pair * comp / ms / 1e9, 1)}),
               flush=True)
 
 

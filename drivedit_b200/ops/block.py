@@ -227,8 +227,17 @@ class _AllMods(torch.autograd.Function):
         dW = g.grad[w0:w0 + wn].view(-1, d)
         gemm(dm, cb, dW, epi="f32_acc", a_t=True, b_t=True)          # dW_all += dm^T c
         g.grad[b0:b0 + bn].add_(ctx.dmods.sum(0))
-        # dc = dm W_all, read as dm^T [K, M] and W_all [K, N] (both MN-major, split-K)
-        dc = gemm(dm.t().contiguous(), W_all, epi="f32_acc", a_t=True, b_t=True)
+        # dc = dm W_all, read as dm^T [K, M] and W_all [K, N] (both MN-major, split-K);
+        # dm^T rows are padded to a multiple of 8 elements (16 bytes, the TMA row rule)
+        M = dm.shape[0]
+        Mp = (M + 7) // 8 * 8
+        if Mp == M:
+            dmT = dm.t().contiguous()
+        else:
+            dmT = torch.zeros(dm.shape[1], Mp, device=dm.device, dtype=dm.dtype)
+            dmT[:, :M] = dm.t()
+            dmT = dmT[:, :M]
+        dc = gemm(dmT, W_all, epi="f32_acc", a_t=True, b_t=True)
         ctx.dmods = None
         return dc, None, None
 

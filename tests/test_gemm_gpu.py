@@ -5,6 +5,16 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["single", "pairs"])
+def pair_mode(request):
+    """Every test runs with single-CTA tiles only and with CTA-pair (cta_group::2, 256-row)
+    tiles wherever a GEMM is eligible for them."""
+    from drivedit_b200.ops._ext import ext
+    prev = ext().gemm_set_pair_mode(0 if request.param == "single" else 1)
+    yield request.param
+    ext().gemm_set_pair_mode(prev)
+
+
 def _ref(a, b, a_t=False, b_t=False):
     A = (a.t() if a_t else a).float()
     B = (b.t() if b_t else b).float()

@@ -53,6 +53,9 @@ def test_route_kernel_matches_torch(T, tpf):
                             if (m >> (qh * 2 + kh)) & 1:
                                 rebuilt[b, h, 2 * t + qh, blk] = True
     assert torch.equal(rebuilt, sel.cpu())
+    from test_sla_lists_cpu import rebuild_from_kv_lists
+    assert torch.equal(rebuild_from_kv_lists(plan.kv_qtiles.cpu(), plan.kv_qmask.cpu(),
+                                             plan.kv_count.cpu(), B, H, nb), sel.cpu())
 
 
 def test_linear_branch_kernels_match_reference():
