@@ -40,9 +40,21 @@ struct AttnArgs {
   const uint8_t* pair_mask = nullptr;  // 4 bits: (q half)*2 + (key half)
   const int* pair_count = nullptr;     // [B*H*n_qtiles]
   int max_pairs = 0;
+  // split-KV (dense / causal modes): kv_splits CTAs share a query tile's key range; each
+  // writes its normalised fp32 O rows to o_part [kv_splits][B*Tq][H*64] and its log2-domain
+  // lse to lse_part [kv_splits][B*H*Tq], and attn_fwd merges them into o (and lse).
+  // attn_fwd chooses kv_splits (> 1 only when the grid would leave SMs idle) and needs
+  // the two scratch buffers then (attn_fwd_split_scratch gives their sizes).
+  int kv_splits = 1;
+  float* o_part = nullptr;
+  float* lse_part = nullptr;
 };
 
 void attn_fwd(const AttnArgs& a, cudaStream_t s);
+// key-range splits attn_fwd would use for `a` on this device (1: no scratch needed) and
+// the fp32 element counts of the two scratch buffers for that many splits
+int attn_fwd_kv_splits(const AttnArgs& a);
+void attn_fwd_split_scratch(const AttnArgs& a, int splits, long* o_part_elems, long* lse_part_elems);
 // pipeline-study hook: record clock64 events of CTA `cta` into buf[3 * 8 * 64] (nullptr: off)
 void attn_fwd_set_trace(long long* buf, int cta);
 

@@ -17,11 +17,17 @@
 // Masks: frame-causal (all keys of frames <= the query's frame), token-causal, none;
 // KV-cache attention via absolute query/key position offsets; block-sparse SLA via a
 // per-tile list of 64-key block pairs with a 4-bit (query half x key half) mask.
+//
+// Split-KV: when batch x heads x query tiles would leave SMs idle (rollout at batch 1:
+// 12 heads x 16 tiles of a 4-frame chunk against a 36-frame window), `kv_splits` CTAs
+// share each query tile's key tiles; each writes its normalised fp32 O and its lse, and
+// attn_split_merge_kernel combines them (O = sum 2^(lse_i - lse) O_i).
 // Semantics oracle: layers/attention.py attention_reference (reference layers/mha.py:88-116
 // with fp32 softmax), layers/sla.py sla_sparse_reference.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <stdexcept>
 
 #include "../common/ptx.cuh"
@@ -103,7 +109,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int item = blockIdx.x;
+  const int splits = a.kv_splits > 1 ? a.kv_splits : 1;
+  const int split = blockIdx.x % splits;
+  const int item = blockIdx.x / splits;
   const int qt = n_qtiles - 1 - (item % n_qtiles);  // heavy (late) tiles first
   const int bh = item / n_qtiles;
   const int b = bh / a.H;
@@ -112,11 +120,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   const bool sparse = a.pair_count != nullptr;
   const long list_idx = static_cast<long>(bh) * n_qtiles + qt;
   int ntiles;
+  int j0 = 0;  // first key tile of this CTA (split-KV: its share of the tile's key range)
   if (sparse) {
     ntiles = a.pair_count[list_idx];
   } else {
     const int lim = row_limit(a, min(q0 + 127, a.Tq - 1));
     ntiles = (lim + 127) / 128;
+    if (splits > 1) {
+      const int per = (ntiles + splits - 1) / splits;
+      j0 = min(ntiles, split * per);
+      ntiles = min(ntiles, j0 + per) - j0;
+    }
   }
 
   if (threadIdx.x == 0) {
@@ -164,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint64_t* full = is_v ? &v_full[s] : &k_full[s];
         if (!mbar_wait(empty, ((j / NS) & 1) ^ 1, abort_flag)) return false;
         fwd_trace(tr, 0, is_v ? 1 : 0, j);
-        int b0 = 2 * j, b1 = 2 * j + 1;
+        int b0 = 2 * (j0 + j), b1 = 2 * (j0 + j) + 1;
         if (sparse) {
           const int packed = a.pair_blocks[list_idx * a.max_pairs + j];
           b0 = packed & 0xffff;
@@ -311,8 +325,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int c = 0; c < 128; ++c) sf[c] = -INFINITY;
         }
-      } else if (j * 128 + 128 > lim) {
-        const int base = j * 128;
+      } else if ((j0 + j) * 128 + 128 > lim) {
+        const int base = (j0 + j) * 128;
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (base + c >= lim) sf[c] = -INFINITY;
@@ -403,7 +417,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int c = 0; c < 64; ++c) ov[c] = 0.f;
     }
-    if (row_ok) {
+    if (row_ok && splits > 1) {
+      // this split's normalised O (fp32) and lse; attn_split_merge_kernel combines them
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const long prow = static_cast<long>(split) * a.B * a.Tq + static_cast<long>(b) * a.Tq + q_local;
+      float* op = a.o_part + prow * (a.H * 64) + h * 64;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4)
+        st_global_v4(op + c, __float_as_uint(ov[c] * inv), __float_as_uint(ov[c + 1] * inv),
+                     __float_as_uint(ov[c + 2] * inv), __float_as_uint(ov[c + 3] * inv));
+      a.lse_part[(static_cast<long>(split) * a.B * a.H + bh) * a.Tq + q_local] =
+          l > 0.f ? m + __log2f(l) : -INFINITY;
+    } else if (row_ok) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o) +
                             (b * a.q_rows_per_b + q_local) * a.ldo + a.o_col + h * 64;
@@ -427,7 +452,72 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 FwdTrace g_fwd_trace{nullptr, 0};
 
+// Split-KV merge: one warp per (query row, head); lane i holds columns 2i, 2i+1.
+__global__ void __launch_bounds__(256) attn_split_merge_kernel(const AttnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long item = blockIdx.x * 8L + (threadIdx.x >> 5);
+  const long rows = static_cast<long>(a.B) * a.Tq;
+  if (item >= rows * a.H) return;
+  const int h = static_cast<int>(item % a.H);
+  const long r = item / a.H;  // b * Tq + q
+  const int b = static_cast<int>(r / a.Tq);
+  const int q = static_cast<int>(r % a.Tq);
+  const long bh = static_cast<long>(b) * a.H + h;
+  const int splits = a.kv_splits;
+  float mx = -INFINITY;
+  for (int i = 0; i < splits; ++i)
+    mx = fmaxf(mx, a.lse_part[(static_cast<long>(i) * a.B * a.H + bh) * a.Tq + q]);
+  float o0 = 0.f, o1 = 0.f, wsum = 0.f;
+  if (mx != -INFINITY) {
+    for (int i = 0; i < splits; ++i) {
+      const float li = a.lse_part[(static_cast<long>(i) * a.B * a.H + bh) * a.Tq + q];
+      const float wi = exp2f(li - mx);  // 0 for an empty split (lse = -inf)
+      const float2 v = *reinterpret_cast<const float2*>(
+          a.o_part + (static_cast<long>(i) * rows + r) * (a.H * 64) + h * 64 + 2 * lane);
+      o0 += wi * v.x;
+      o1 += wi * v.y;
+      wsum += wi;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o) +
+                        (b * a.q_rows_per_b + q) * a.ldo + a.o_col + h * 64;
+  *reinterpret_cast<uint32_t*>(orow + 2 * lane) = pack_bf16(o0 * inv, o1 * inv);
+  if (a.lse && lane == 0) a.lse[bh * a.Tq + q] = wsum > 0.f ? mx + __log2f(wsum) : -INFINITY;
+}
+
 }  // namespace
+
+int attn_fwd_kv_splits(const AttnArgs& a) {
+  if (a.pair_count != nullptr || a.B <= 0 || a.H <= 0 || a.Tq <= 0) return 1;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  const long slots = 2L * num_sms(dev);  // two forward CTAs per SM
+  const long ctas = static_cast<long>(a.B) * a.H * ((a.Tq + 127) / 128);
+  if (ctas >= slots) return 1;
+  // key tiles of the last (longest) query tile; a split keeps at least 4 of them
+  int lim = a.S;
+  const int qa = a.q_pos_offset + a.Tq - 1;
+  if (a.causal == kCausalFrame) lim = std::min(lim, (qa / a.tpf + 1) * a.tpf - a.kv_pos_offset);
+  else if (a.causal == kCausalToken) lim = std::min(lim, qa + 1 - a.kv_pos_offset);
+  const int tiles = (std::max(lim, 0) + 127) / 128;
+  // time ~ waves x key tiles per split: the fewest splits with the smallest estimate
+  int best = 1;
+  double best_t = 1.0;
+  for (int s = 2; s <= 8 && tiles / s >= 4; ++s) {
+    const double t = static_cast<double>((ctas * s + slots - 1) / slots) / s;
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
+void attn_fwd_split_scratch(const AttnArgs& a, int splits, long* o_part_elems, long* lse_part_elems) {
+  *o_part_elems = static_cast<long>(splits) * a.B * a.Tq * a.H * 64;
+  *lse_part_elems = static_cast<long>(splits) * a.B * a.H * a.Tq;
+}
 
 void attn_fwd_set_trace(long long* buf, int cta) { g_fwd_trace = FwdTrace{buf, cta}; }
 
@@ -449,13 +539,22 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tV = make_tmap_2d(a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.ldv, kv_rows,
                                 a.ldv * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   const int n_qtiles = (a.Tq + 127) / 128;
-  const int grid = a.B * a.H * n_qtiles;
+  const int splits = a.kv_splits > 1 ? a.kv_splits : 1;
+  if (splits > 1 && (a.pair_count != nullptr || a.o_part == nullptr || a.lse_part == nullptr))
+    throw std::runtime_error("attn_fwd: split-KV needs dense/causal mode and both scratch buffers");
+  const int grid = a.B * a.H * n_qtiles * splits;
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   attn_fwd_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tQ, tK, tV, a, n_qtiles,
                                                           device_status(dev), g_fwd_trace);
   count_launch();
   check_cuda(cudaGetLastError(), "attn_fwd_kernel launch");
+  if (splits > 1) {
+    const long items = static_cast<long>(a.B) * a.Tq * a.H;
+    attn_split_merge_kernel<<<static_cast<int>((items + 7) / 8), 256, 0, stream>>>(a);
+    count_launch();
+    check_cuda(cudaGetLastError(), "attn_split_merge_kernel launch");
+  }
 }
 
 }  // namespace ddb

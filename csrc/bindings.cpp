@@ -319,6 +319,9 @@ ddb::AttnArgs make_attn_args(const torch::Tensor& q, const torch::Tensor& k, con
   return a;
 }
 
+// split-KV override for tests: 0 = chosen per launch, n >= 1 = always n splits
+int64_t g_attn_kv_splits = 0;
+
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               c10::optional<torch::Tensor> lse, int64_t q_col, int64_t k_col, int64_t v_col,
               int64_t o_col, int64_t B, int64_t H, int64_t Tq, int64_t S, int64_t q_rows_per_b,
@@ -351,6 +354,19 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
     a.pair_mask = pair_mask->data_ptr<uint8_t>();
     a.pair_count = pair_count->data_ptr<int>();
     a.max_pairs = pair_blocks->size(1);
+  }
+  // split-KV when the grid would leave SMs idle (scratch from the caching allocator)
+  const int splits = g_attn_kv_splits > 0 ? (a.pair_count ? 1 : static_cast<int>(g_attn_kv_splits))
+                                          : ddb::attn_fwd_kv_splits(a);
+  torch::Tensor o_part, lse_part;
+  if (splits > 1) {
+    long oe = 0, le = 0;
+    ddb::attn_fwd_split_scratch(a, splits, &oe, &le);
+    o_part = torch::empty({oe}, q.options().dtype(torch::kFloat32));
+    lse_part = torch::empty({le}, q.options().dtype(torch::kFloat32));
+    a.kv_splits = splits;
+    a.o_part = o_part.data_ptr<float>();
+    a.lse_part = lse_part.data_ptr<float>();
   }
   ddb::attn_fwd(a, stream());
 }
@@ -1395,6 +1411,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_rotate", &rope_rotate, "in-place rotary rotation of leading columns");
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention forward (dense / frame-causal / sparse)");
   m.def("attn_fwd_set_trace", &attn_fwd_set_trace, "clock64 trace of one forward CTA (None: off)");
+  m.def("attn_fwd_set_kv_splits", [](int64_t n) { const int64_t prev = g_attn_kv_splits; g_attn_kv_splits = n < 0 ? 0 : n; return prev; },
+        "split-KV of the attention forward: 0 = chosen per launch, n >= 1 = n splits; returns the previous setting");
   m.def("attn_bwd", &attn_bwd, "tcgen05 flash attention backward (KV-stationary)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"), py::arg("lse"),
         py::arg("delta"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("q_col"),

@@ -73,6 +73,7 @@ def run(batch: int, frames: int, warm_chunks: int = 2, overrides=None, tp_transp
         "chunks": len(res.chunk_ms),
         "p50_chunk_ms": round(res.percentile_ms(50), 3),
         "p99_chunk_ms": round(res.percentile_ms(99), 3),
+        "chunk_ms": [round(x, 3) for x in res.chunk_ms],
         "dtype": "bf16",
         "data": "synthetic context latents/actions, random-init weights",
         "model": cfg.model.name,

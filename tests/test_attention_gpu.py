@@ -76,6 +76,30 @@ def test_flash_kv_cache_offsets():
     assert _rel(o, ro) < 2e-2
 
 
+@pytest.mark.parametrize("splits", [1, 2, 3, 0])
+def test_flash_kv_cache_split_kv(splits):
+    """Rollout-shaped KV-cache attention (a 4-frame chunk over a longer window, few
+    heads) with the key range split over 1, 2 or 3 CTAs per query tile (0: the launch's
+    own choice) and merged by log-sum-exp: output and lse match the fp32 reference."""
+    from drivedit_b200.ops._ext import ext
+    from drivedit_b200.ops.attention_kernels import flash_attention
+    B, H, D, tpf = 1, 2, 64, 256
+    Tq, S = 4 * tpf, 12 * tpf          # chunk = the newest 4 of 12 frames
+    q = torch.randn(B, Tq, H, D, device="cuda").bfloat16()
+    k = torch.randn(B, S, H, D, device="cuda").bfloat16()
+    v = torch.randn(B, S, H, D, device="cuda").bfloat16()
+    prev = ext().attn_fwd_set_kv_splits(splits)
+    try:
+        o, lse = flash_attention(q, k, v, "frame", tpf, q_pos_offset=S - Tq, kv_pos_offset=0)
+    finally:
+        ext().attn_fwd_set_kv_splits(prev)
+    mask = _mask(Tq, S, "frame", tpf, S - Tq, 0)
+    ro, rlse = _ref(q, k, v, mask)
+    assert _rel(o, ro) < 2e-2
+    # the kernels' lse is in the log2 domain of the scaled scores
+    assert (lse.float() - rlse * 1.4426950408889634).abs().max().item() < 2e-2
+
+
 def test_sla_sparse_fwd_bwd_matches_masked_reference():
     from drivedit_b200.config import SLAParams
     from drivedit_b200.layers.sla import expand_block_mask

@@ -9,7 +9,7 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
 
 
-@pytest.mark.parametrize("D", [256, 768, 1024])
+@pytest.mark.parametrize("D", [256, 768, 1024, 1536, 2048])
 def test_adaln_fwd_bwd(D):
     from drivedit_b200.ops.fused import adaln_rmsnorm, adaln_rmsnorm_bwd
     M, tpf = 1024, 128
