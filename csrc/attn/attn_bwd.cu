@@ -130,16 +130,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long list_idx = static_cast<long>(bh) * n_kvtiles + kt;
   int nq, qt_first = 0;
   if (sparse) {
-    nq = g.kv_count[list_idx];
+    nq = min(g.kv_count[list_idx], g.max_q);
   } else {
     const int fq = max(0, first_query_seeing(a, k0));
     qt_first = fq / 128;
     nq = fq < a.Tq ? n_qtiles - qt_first : 0;
     if (k0 >= a.S) nq = 0;
   }
-  // the unit's two 64-query blocks, qa | qb << 16
+  // the unit's two 64-query blocks, qa | qb << 16; a list entry naming a block past the
+  // queries is recorded in the status word and clamped (no access leaves the tensors)
+  const int n_qblocks = (a.Tq + 63) / 64;
   auto qpair_of = [&](int j) -> int {
-    if (sparse) return g.kv_qtiles[list_idx * g.max_q + j];
+    if (sparse) {
+      const int qp = g.kv_qtiles[list_idx * g.max_q + j];
+      int qa = qp & 0xffff, qb = (qp >> 16) & 0xffff;
+      if (qa >= n_qblocks || qb >= n_qblocks) {
+        if (threadIdx.x == 0) record_bad_index(status, list_idx);
+        qa = min(qa, n_qblocks - 1);
+        qb = min(qb, n_qblocks - 1);
+      }
+      return qa | (qb << 16);
+    }
     const int qt = qt_first + j;
     return (2 * qt) | ((2 * qt + 1) << 16);
   };

@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   int ntiles;
   int j0 = 0;  // first key tile of this CTA (split-KV: its share of the tile's key range)
   if (sparse) {
-    ntiles = a.pair_count[list_idx];
+    ntiles = min(a.pair_count[list_idx], a.max_pairs);
   } else {
     const int lim = row_limit(a, min(q0 + 127, a.Tq - 1));
     ntiles = (lim + 127) / 128;
@@ -183,6 +183,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int packed = a.pair_blocks[list_idx * a.max_pairs + j];
           b0 = packed & 0xffff;
           b1 = (packed >> 16) & 0xffff;
+          const int nkb = (a.S + 63) / 64;  // a block past the keys: recorded, clamped
+          if (b0 >= nkb || b1 >= nkb) {
+            record_bad_index(status, list_idx);
+            b0 = min(b0, nkb - 1);
+            b1 = min(b1, nkb - 1);
+          }
         }
         uint8_t* dst = smem + (is_v ? OFF_V : OFF_K) + s * TILE_BYTES;
         const CUtensorMap* tm = is_v ? &tmV : &tmK;

@@ -2,6 +2,9 @@
 // contiguity and alignment and raises on anything its kernel does not handle, so a
 // kernel never receives arguments it was not written for.
 #include <torch/extension.h>
+
+#include <map>
+#include <utility>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -175,7 +178,8 @@ std::vector<torch::Tensor> adaln_fwd(torch::Tensor x, torch::Tensor w, torch::Te
   TORCH_CHECK(mod.stride(0) % 4 == 0 && scale_off % 4 == 0 && shift_off % 4 == 0,
               "mod columns must be 16-byte aligned");
   const int64_t M = x.size(0), D = x.size(1);
-  TORCH_CHECK(D % 256 == 0 && D <= 2048, "adaln: D must be a multiple of 256, <= 2048");
+  TORCH_CHECK(D % 256 == 0 && D <= 2048 && D != 1280 && D != 1792,
+              "adaln: D must be 256, 512, 768, 1024, 1536 or 2048");
   TORCH_CHECK((M + rows_per_group - 1) / rows_per_group <= mod.size(0), "mod has too few rows");
   TORCH_CHECK(std::max(scale_off, shift_off) + D <= mod.size(1), "mod too narrow");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -199,7 +203,8 @@ torch::Tensor adaln_bwd(torch::Tensor dh, torch::Tensor x, torch::Tensor rstd, t
   check_bf16(x, "x");
   TORCH_CHECK(dh.is_contiguous() && x.is_contiguous() && dh.sizes() == x.sizes(), "dh/x shape");
   const int64_t M = x.size(0), D = x.size(1);
-  TORCH_CHECK(D % 256 == 0 && D <= 1024, "adaln bwd: D must be a multiple of 256, <= 1024");
+  TORCH_CHECK(D % 256 == 0 && D <= 2048 && D != 1280 && D != 1792,
+              "adaln bwd: D must be 256, 512, 768, 1024, 1536 or 2048");
   TORCH_CHECK(rstd.scalar_type() == torch::kFloat32 && rstd.numel() == M, "rstd");
   TORCH_CHECK(dmod.scalar_type() == torch::kFloat32 && dmod.dim() == 2 && dmod.stride(1) == 1 &&
                   dmod.size(0) >= (M + rows_per_group - 1) / rows_per_group,
@@ -358,15 +363,21 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   // split-KV when the grid would leave SMs idle (scratch from the caching allocator)
   const int splits = g_attn_kv_splits > 0 ? (a.pair_count ? 1 : static_cast<int>(g_attn_kv_splits))
                                           : ddb::attn_fwd_kv_splits(a);
-  torch::Tensor o_part, lse_part;
   if (splits > 1) {
     long oe = 0, le = 0;
     ddb::attn_fwd_split_scratch(a, splits, &oe, &le);
-    o_part = torch::empty({oe}, q.options().dtype(torch::kFloat32));
-    lse_part = torch::empty({le}, q.options().dtype(torch::kFloat32));
+    // one persistent scratch per (device, stream), grown on demand: launches on one
+    // stream run in order, so reusing it needs no allocation per call
+    // (never destroyed: tensors released after the CUDA context at exit would fault)
+    static auto* scratch = new std::map<std::pair<int, cudaStream_t>, torch::Tensor>();
+    const auto key = std::make_pair(static_cast<int>(q.get_device()), stream());
+    torch::Tensor& buf = (*scratch)[key];
+    const long need = (oe + 63) / 64 * 64 + le;
+    if (!buf.defined() || buf.numel() < need)
+      buf = torch::empty({need}, q.options().dtype(torch::kFloat32));
     a.kv_splits = splits;
-    a.o_part = o_part.data_ptr<float>();
-    a.lse_part = lse_part.data_ptr<float>();
+    a.o_part = buf.data_ptr<float>();
+    a.lse_part = a.o_part + (oe + 63) / 64 * 64;
   }
   ddb::attn_fwd(a, stream());
 }

@@ -87,6 +87,8 @@ def main():
     p.add_argument("--batch", type=int, nargs="+", default=[1, 16])
     p.add_argument("--frames", type=int, default=120)
     p.add_argument("--tp-transport", default="fused")
+    p.add_argument("--kv-splits", type=int, default=0,
+                   help="attention split-KV: 0 = chosen per launch, n >= 1 = n splits")
     p.add_argument("override", nargs="*")
     a = p.parse_args()
     if not torch.cuda.is_available():
@@ -103,6 +105,10 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+    if a.kv_splits:
+        from ..ops._ext import ext
+
+        ext().attn_fwd_set_kv_splits(a.kv_splits)
     for b in a.batch:
         out = run(b, a.frames, overrides=a.override, tp_transport=a.tp_transport)
         if int(os.environ.get("RANK", "0")) == 0:
