@@ -213,9 +213,10 @@ def _train_throughput(cfg_name, overrides, steps, warmup, ws, rank, local, e2e_s
     n_launch = launch_count() - n0  # this extension's kernels only (the L2 flush is not one)
     ms = max_over_ranks(start.elapsed_time(end) / steps)
     check_device_status()
+    peak = max_over_ranks(torch.cuda.max_memory_allocated(dev) / 2**30)
     out = {"ms_per_step": ms, "value": ws * tokens_per_step / (ms / 1000.0),
            "gpu_launches": n_launch, "tokens_per_step_per_gpu": tokens_per_step,
-           "final_loss": float(loss.item())}
+           "final_loss": float(loss.item()), "peak_mem_gib": round(peak, 1)}
     if clk is not None:
         out["clocks"] = clk.summary()
 
@@ -306,6 +307,7 @@ def run_ours(args, ws, rank, local):
         "e2e": res["e2e"],
         "gpu_launches": res["gpu_launches"],
         "final_loss": res["final_loss"],
+        "peak_mem_gib_per_gpu": res["peak_mem_gib"],
     }
     if not args.no_extras:
         extras = {}

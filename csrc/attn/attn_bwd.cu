@@ -59,17 +59,6 @@ constexpr uint32_t IDESC_SS = make_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_GRAD = make_idesc_bf16(128, 64, false, true);  // A K-major, B MN-major
 constexpr uint32_t IDESC_DQ = make_idesc_bf16(128, 64, true, true);     // both MN-major
 
-__device__ __forceinline__ int row_limit(const AttnArgs& a, int q_local) {
-  int lim = a.S;
-  const int qa = a.q_pos_offset + q_local;
-  if (a.causal == kCausalFrame) {
-    lim = min(lim, (qa / a.tpf + 1) * a.tpf - a.kv_pos_offset);
-  } else if (a.causal == kCausalToken) {
-    lim = min(lim, qa + 1 - a.kv_pos_offset);
-  }
-  return max(lim, 0);
-}
-
 // first query (within the sample) whose key limit exceeds key index k
 __device__ __forceinline__ int first_query_seeing(const AttnArgs& a, int k) {
   if (a.causal == kCausalFrame) {

@@ -548,6 +548,25 @@ void gemm_tp(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> D, i
 }
 
 // out[r] = residual[r] + sum_s recv[s * rows + r] (bf16, fp32 accumulation)
+// out [n] = residual + sum over ranks of their bf16 partial buffers (peer pointer table)
+torch::Tensor tp_allreduce_sum(torch::Tensor peer_table, int64_t world, int64_t n, torch::Tensor like,
+                               c10::optional<torch::Tensor> residual) {
+  TORCH_CHECK(peer_table.is_cuda() && peer_table.scalar_type() == torch::kInt64 && peer_table.numel() >= world,
+              "tp_allreduce_sum: peer table must be int64 CUDA [world]");
+  check_bf16(like, "like");
+  TORCH_CHECK(like.numel() == n && like.is_contiguous(), "tp_allreduce_sum: like must be contiguous with n elements");
+  auto out = torch::empty_like(like);
+  const __nv_bfloat16* res = nullptr;
+  if (residual) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->numel() == n && residual->is_contiguous(), "tp_allreduce_sum: residual shape");
+    res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  ddb::tp_allreduce_sum(reinterpret_cast<const __nv_bfloat16* const*>(peer_table.data_ptr<int64_t>()), world, n,
+                        res, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), stream());
+  return out;
+}
+
 torch::Tensor tp_sum_rows(torch::Tensor recv, int64_t world, int64_t rows, c10::optional<torch::Tensor> residual) {
   check_bf16(recv, "recv");
   TORCH_CHECK(recv.is_contiguous() && recv.size(0) >= world * rows, "recv [world * rows, d]");
@@ -1442,6 +1461,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("xrank_barrier", &xrank_barrier, "bounded cross-rank flag barrier over peer memory");
   m.def("gemm_tp", &gemm_tp, "tcgen05 GEMM with the all-gather of A and/or the reduce-scatter of D fused");
   m.def("tp_sum_rows", &tp_sum_rows, "sum of the per-rank partial rows (+ residual)");
+  m.def("tp_allreduce_sum", &tp_allreduce_sum, "all-reduce by peer loads: residual + sum of every rank's partial");
   m.def("rs_sum_sqnorm", &rs_sum_sqnorm, "reduce-scatter by peer loads + squared norm");
   m.def("shard_adamw_allgather", &shard_adamw_allgather, "sharded AdamW + all-gather by peer stores");
   m.def("gemm_grouped", &gemm_grouped, "grouped (MoE) tcgen05 GEMM with device tile tables");

@@ -215,7 +215,51 @@ __global__ void __launch_bounds__(256) tp_sum_rows_kernel(const __nv_bfloat16* _
     *reinterpret_cast<uint4*>(out + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
+
+// All-reduce by peer loads: out = residual + sum over ranks p of peer p's partial
+// (peer_parts[p] is rank p's buffer, this rank's own entry included), 16 bytes per
+// thread per rank, fp32 sums in a fixed rank order (every rank computes bit-identical
+// rows).
+__global__ void __launch_bounds__(256) tp_allreduce_sum_kernel(const __nv_bfloat16* const* __restrict__ peer_parts,
+                                                               long world, long n8,
+                                                               const __nv_bfloat16* __restrict__ res,
+                                                               __nv_bfloat16* __restrict__ out) {
+  for (long i = blockIdx.x * 256L + threadIdx.x; i < n8; i += static_cast<long>(gridDim.x) * 256) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    auto add = [&](const __nv_bfloat16* p) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p + i * 8);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[q]));
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    };
+    for (long s = 0; s < world; ++s) add(peer_parts[s]);
+    if (res) add(res);
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+      o[q] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(out + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
 }  // namespace
+
+void tp_allreduce_sum(const __nv_bfloat16* const* peer_parts, long world, long n, const __nv_bfloat16* residual,
+                      __nv_bfloat16* out, cudaStream_t s) {
+  if (n % 8 != 0) throw std::runtime_error("tp_allreduce_sum: element count % 8");
+  const long n8 = n / 8;
+  if (n8 == 0) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = static_cast<int>(std::min<long>((n8 + 255) / 256, 4L * num_sms(dev)));
+  tp_allreduce_sum_kernel<<<grid, 256, 0, s>>>(peer_parts, world, n8, residual, out);
+  count_launch();
+}
 
 void tp_sum_rows(const __nv_bfloat16* recv, long world, long rows, long d, const __nv_bfloat16* residual,
                  __nv_bfloat16* out, cudaStream_t s) {

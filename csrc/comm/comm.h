@@ -24,6 +24,10 @@ void ipc_free(void* ptr);
 // slot r of every peer's flag array, then waits (bounded) until every slot of its own array
 // holds >= epoch. flags layout per rank: [world] uint32 flags, then [world] float payloads.
 // out[r] = residual[r] + sum_s recv[s * rows + r] over d bf16 columns (d % 8 == 0).
+// out = residual + sum of the n-element bf16 partials of every rank (peer_parts: device
+// array of the ranks' buffer pointers, P2P mappings for the peers), read by peer loads
+void tp_allreduce_sum(const __nv_bfloat16* const* peer_parts, long world, long n, const __nv_bfloat16* residual,
+                      __nv_bfloat16* out, cudaStream_t s);
 void tp_sum_rows(const __nv_bfloat16* recv, long world, long rows, long d, const __nv_bfloat16* residual,
                  __nv_bfloat16* out, cudaStream_t s);
 void xrank_barrier(void* const* peer_flag_bufs, void* local_flag_buf, int rank, int world,

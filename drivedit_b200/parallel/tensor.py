@@ -14,6 +14,17 @@ ranks); the KV cache holds only the rank's heads. Per block::
     a = swiglu(all_gather(h2) @ W13_r^T)                  AG -> GEMM
     x2 = x1 + reduce_scatter(a @ W3_r^T)                  GEMM -> RS
 
+Small chunks (at most ``replicate_rows_max`` token rows, e.g. a 4-frame chunk at batch 1)
+use plain tensor parallelism instead: every rank holds all rows of the residual stream
+(AdaLN and the head run on all rows on every rank), the QKV and SwiGLU GEMMs read the
+local rows with the rank's column shard of the weights (no all-gather), and the output and
+down projections end in an all-reduce: each rank's GEMM writes its partial into its own
+peer-readable buffer, one barrier, and ``tp_allreduce_sum`` adds every rank's partial
+(P2P loads, fixed rank order, so all ranks hold identical rows) and the residual. That is
+two barriers per block instead of four, no gather copies, and every AdaLN modulation of
+the forward comes from one GEMM; the bytes crossing NVLink per all-reduce are a few MB at
+batch 1, so latency, not bandwidth, sets the cost.
+
 Transports:
 
 ``fused``
@@ -105,9 +116,11 @@ class TensorParallelWorldDiT:
     through ``make_kv_cache`` / ``forward_cached_chunk``."""
 
     def __init__(self, model, group=None, transport: Optional[str] = None, dtype=torch.bfloat16,
-                 ag_tma_max_n: int = 256):
+                 ag_tma_max_n: int = 256, replicate_rows_max: int = 4096):
         """``ag_tma_max_n``: widest per-rank GEMM (columns) whose all-gather runs inside the
-        GEMM as peer TMA loads; wider ones pull the rows once and overlap."""
+        GEMM as peer TMA loads; wider ones pull the rows once and overlap.
+        ``replicate_rows_max``: chunks of at most this many token rows run with the
+        residual stream replicated on every rank and all-reduces (see the module notes)."""
         self.model = model
         self.cfg = model.cfg
         self.group = group if group is not None else dist.group.WORLD
@@ -117,6 +130,9 @@ class TensorParallelWorldDiT:
         self.transport = transport or ("fused" if self.device.type == "cuda" else "nccl")
         self.dtype = dtype
         self.ag_tma_max_n = ag_tma_max_n
+        self.replicate_rows_max = replicate_rows_max
+        self._ping = 0
+        self._mods_w = None
         self.layers = [TPLayerWeights(b, self.rank, self.world, self.cfg, dtype) for b in model.blocks]
         self.heads_local = self.layers[0].heads
         self.d_local = self.heads_local * self.cfg.d_head
@@ -164,7 +180,94 @@ class TensorParallelWorldDiT:
     def forward_cached_chunk(self, x_t, t, actions, cache: TPKVCache, commit: bool, extra_cond=None):
         if self.device.type != "cuda":
             raise RuntimeError("tensor-parallel rollout runs on the CUDA kernels")
+        rows = x_t.shape[0] * x_t.shape[1] * self.cfg.tokens_per_frame
+        if rows <= self.replicate_rows_max:
+            return self._forward_replicated(x_t, t, actions, cache, commit, extra_cond)
         return self._forward(x_t, t, actions, cache, commit, extra_cond)
+
+    # ---------------------------------------------------------------- replicated rows
+    def _all_mods(self, c2):
+        """Every block's AdaLN modulation and the head's for the chunk's frames in one
+        GEMM (bf16 operands, fp32 accumulation and bias): per-block views of
+        ``[frames, n_mod x d]`` and the head's ``[frames, 2 d]``."""
+        from ..ops.gemm import gemm
+
+        if self._mods_w is None:
+            lins = [lw.ada for lw in self.layers] + [self.model.final_ada]
+            ws = [lin.weight.detach() for lin in lins]
+            bs = [lin.bias.detach() for lin in lins]
+            self._mods_w = (torch.cat(ws).to(torch.bfloat16).contiguous(), torch.cat(bs).float().contiguous(),
+                            ws[0].shape[0])
+        w, b, per = self._mods_w
+        mods = gemm(c2.to(torch.bfloat16).contiguous(), w, epi="f32", bias=b)
+        L = len(self.layers)
+        return [mods[:, i * per:(i + 1) * per] for i in range(L)], mods[:, L * per:]
+
+    def _allreduce_gemm(self, a, w, residual):
+        """``residual + all_reduce(a @ w^T)``: the GEMM writes this rank's partial into its
+        peer-readable buffer (two buffers used in turn: a rank writes a buffer again only
+        after the next collective's barrier, which every peer reaches after its sum of the
+        buffer's previous contents), one barrier, then the peer-load sum."""
+        from ..ops._ext import ext
+        from ..ops.gemm import gemm
+
+        M, N = a.shape[0], w.shape[0]
+        if self.transport == "fused":
+            self._ping ^= 1
+            buf = self._buf(f"part{self._ping}", M * N * 2)
+            part = buf.tensor(M * N, torch.bfloat16).view(M, N)
+            gemm(a, w, part)
+            self._barrier()                              # every rank's partial is complete
+            return ext().tp_allreduce_sum(buf.table, self.world, M * N, part, residual)
+        part = gemm(a, w)
+        dist.all_reduce(part, group=self.group)
+        return part + residual
+
+    def _forward_replicated(self, x_t, t, actions, cache, commit, extra_cond):
+        from ..models.world_dit import patchify, unpatchify
+        from ..ops._ext import ext
+        from ..ops.fused import adaln_rmsnorm
+        from ..ops.gemm import gemm
+
+        m, cfg = self.model, self.cfg
+        B, Fc, C, H, W_ = x_t.shape
+        d, Dh = cfg.d_model, cfg.d_head
+        dl, Hl = self.d_local, self.heads_local
+        tok = patchify(x_t, cfg.patch).reshape(-1, cfg.patch_dim).to(torch.bfloat16).contiguous()
+        M = tok.shape[0]
+        T = M // B
+        tpf = T // Fc
+        x = gemm(tok, m.patch_embed.weight.detach().to(torch.bfloat16), bias=m.patch_embed.bias.detach().float())
+        c2 = m.condition(t, actions, extra_cond).reshape(B * Fc, d)
+        mods, fm = self._all_mods(c2)
+        tab = m.rope.table(Fc, cache.frames).to(x.device)
+        row = cache.reserve(T)
+        scale = 1.0 / math.sqrt(Dh)
+        for lw, lc, mod in zip(self.layers, cache.layers, mods):
+            h1, _ = adaln_rmsnorm(x, lw.norm1, mod, 0, d, tpf)
+            qkv = gemm(h1, lw.wqkv, epi="rope", rope_tab=tab, rope_cols=2 * dl, rope_rows_per_seq=T,
+                       rope_head_dim=Dh)
+            q3 = qkv.view(B, T, 3 * dl)
+            lc.k[:, row:row + T].copy_(q3[:, :, dl:2 * dl])
+            lc.v[:, row:row + T].copy_(q3[:, :, 2 * dl:])
+            cap = lc.k.shape[1]
+            k2 = lc.k.view(B * cap, dl)[lc.start:]
+            v2 = lc.v.view(B * cap, dl)[lc.start:]
+            S = row + T - lc.start
+            o = torch.empty(M, dl, device=x.device, dtype=torch.bfloat16)
+            ext().attn_fwd(qkv, k2, v2, o, None, 0, 0, 0, 0, B, Hl, T, S, T, cap, 1, tpf,
+                           lc.pos0 + row, lc.pos0 + lc.start, scale, None, None, None)
+            x1 = self._allreduce_gemm(o, lw.wproj, x)
+            h2, _ = adaln_rmsnorm(x1, lw.norm2, mod, 2 * d, 3 * d, tpf)
+            gu = torch.empty(M, lw.w13.shape[0], device=x.device, dtype=torch.bfloat16)
+            a = torch.empty(M, lw.w13.shape[0] // 2, device=x.device, dtype=torch.bfloat16)
+            gemm(h2, lw.w13, gu, epi="swiglu", out2=a)
+            x = self._allreduce_gemm(a, lw.w3, x1)
+        if commit:
+            cache.commit(Fc)
+        h, _ = adaln_rmsnorm(x, m.final_norm.weight.detach(), fm, 0, d, tpf, cfg.norm_eps)
+        out = gemm(h, m.out_proj.weight.detach().to(torch.bfloat16), bias=m.out_proj.bias.detach().float())
+        return unpatchify(out.view(B, T, cfg.patch_dim), Fc, C, H, W_, cfg.patch)
 
     # ---------------------------------------------------------------- collectives
     def _gather_gemm(self, h_shard, h_sym, w, rows, M, epi="bf16", **kw):

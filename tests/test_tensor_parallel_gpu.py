@@ -3,7 +3,9 @@
 * one rank: the tensor-parallel path (peer-shard A loads and peer-store reduce-scatter in
   the GEMM, row sums, bounded barriers) reproduces the single-GPU fused rollout;
 * two ranks: the peer-memory transport and the NCCL transport both reproduce it, and every
-  rank ends with the same frames.
+  rank ends with the same frames;
+* both layouts: row-sharded activations (all-gather / reduce-scatter) and, for small
+  chunks, replicated rows with all-reduces by peer loads.
 """
 import datetime
 import os
@@ -28,7 +30,7 @@ def _port():
     return p
 
 
-def _rollout(model, tp_transport=None, ag_tma_max_n=256):
+def _rollout(model, tp_transport=None, ag_tma_max_n=256, replicate_rows_max=0):
     from drivedit_b200.config import RolloutConfig
     from drivedit_b200.inference.rollout import StreamingRollout
 
@@ -42,7 +44,8 @@ def _rollout(model, tp_transport=None, ag_tma_max_n=256):
     if tp_transport is not None:
         from drivedit_b200.parallel.tensor import TensorParallelWorldDiT
 
-        tp = TensorParallelWorldDiT(model, transport=tp_transport, ag_tma_max_n=ag_tma_max_n)
+        tp = TensorParallelWorldDiT(model, transport=tp_transport, ag_tma_max_n=ag_tma_max_n,
+                                    replicate_rows_max=replicate_rows_max)
         target = tp
     res = StreamingRollout(target, cfg).run(ctx, act, 8, generator=g)
     torch.cuda.synchronize()
@@ -77,6 +80,7 @@ def _worker(rank, world, port, q, transports):
     out = {"single": _rollout(model)}
     for t in transports:
         out[t] = _rollout(model, t)
+        out[t + "_rep"] = _rollout(model, t, replicate_rows_max=1 << 30)
     if "fused" in transports:      # every all-gather inside the GEMM as peer TMA loads
         out["fused_tma"] = _rollout(model, "fused", ag_tma_max_n=1 << 20)
     check_device_status()
@@ -119,6 +123,7 @@ def _close(a, b, tol):
 def test_tensor_parallel_rollout_one_rank_matches_single_gpu():
     res = _run(1, ["fused"])[0]
     _close(res["fused"], res["single"], 2e-2)
+    _close(res["fused_rep"], res["single"], 2e-2)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -128,4 +133,8 @@ def test_tensor_parallel_rollout_two_ranks():
         _close(res[r]["fused"], res[r]["single"], 2e-2)
         _close(res[r]["nccl"], res[r]["single"], 2e-2)
         _close(res[r]["fused_tma"], res[r]["single"], 2e-2)
+        _close(res[r]["fused_rep"], res[r]["single"], 2e-2)
+        _close(res[r]["nccl_rep"], res[r]["single"], 2e-2)
+    # replicated rows: both ranks hold bit-identical frames
+    assert np.array_equal(res[0]["fused_rep"], res[1]["fused_rep"])
     np.testing.assert_array_equal(res[0]["fused"], res[1]["fused"])
