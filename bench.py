@@ -178,7 +178,8 @@ def _train_throughput(cfg_name, overrides, steps, warmup, ws, rank, local, e2e_s
     cfg = get_config(cfg_name, overrides)
     torch.manual_seed(cfg.train.seed + rank)
     dev = torch.device("cuda", local)
-    model = WorldDiT(cfg.model)
+    with torch.device(dev):  # random init on the device (the 2B-active MoE has 9.4B params)
+        model = WorldDiT(cfg.model)
     trainer = WorldModelTrainer(model, cfg.train, dev,
                                 process_group=dist.group.WORLD if ws > 1 else None)
     B, Fr = cfg.train.batch_per_gpu, cfg.train.frames

@@ -128,6 +128,9 @@ class TrainConfig:
     shard_weights: bool = False
     # fixed-order MoE permutation: bit-reproducible expert gradients (drivedit_b200.ops.debug)
     deterministic: bool = False
+    # activation checkpointing (the reference's gradient_checkpointing): each block keeps
+    # only its input and recomputes its forward in the backward
+    checkpoint_blocks: bool = False
 
 
 @dataclass

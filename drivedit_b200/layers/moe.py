@@ -263,7 +263,7 @@ class MoEFFN(nn.Module):
         """Aux-loss-free balancing (reference layers/moe.py:164-181). The step's
         per-expert counts stay on the device in ``last_counts`` for monitoring."""
         self.last_counts = counts.detach()
-        if not self.training:
+        if not self.training or getattr(self, "frozen_bias", False):
             return
         s = self.bias_update_speed
         load = counts.float() / (n_tokens * self.top_k + 1e-8)

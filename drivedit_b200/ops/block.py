@@ -46,6 +46,7 @@ class BlockCtx:
         self.sla_cfg = sla_cfg
         self.causal = causal
         self.rope_pos_offset = rope_pos_offset
+        self.recompute = False  # activation checkpointing: blocks rerun their forward in backward
 
 
 def _gather_of(W):
@@ -142,14 +143,25 @@ class _BlockFn(torch.autograd.Function):
     backward of all modulations."""
 
     @staticmethod
-    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx, token=None, dmod_out=None):
-        W = group.compute_view
+    def _run(x, mod, blk, W, bc):
         x1, sa = _attn_forward(x, mod, blk, W, bc)
         if blk.moe is None:
             x2, sm = _mlp_forward(x1, mod, blk, W, bc)
             aux = torch.zeros((), device=x.device)
         else:
             x2, aux, sm = _moe_forward(x1, mod, blk, W, bc)
+        return x2, aux, sa, sm
+
+    @staticmethod
+    def forward(ctx, x, mod, blk, group: FlatParamGroup, bc: BlockCtx, token=None, dmod_out=None):
+        W = group.compute_view
+        # with recomputation the routing bias this forward used is kept, so the backward's
+        # rerun routes every token exactly as this forward did
+        bias = blk.moe.expert_bias.clone() if (bc.recompute and blk.moe is not None) else None
+        x2, aux, sa, sm = _BlockFn._run(x, mod, blk, W, bc)
+        if bc.recompute:  # keep only the block input; the activations are rebuilt in backward
+            sa = sm = None
+            ctx.x_in, ctx.bias = x, bias
         ctx.sa, ctx.sm, ctx.mod = sa, sm, mod
         ctx.blk, ctx.group, ctx.bc = blk, group, bc
         ctx.dmod_out = dmod_out
@@ -159,6 +171,20 @@ class _BlockFn(torch.autograd.Function):
     def backward(ctx, dx2, d_aux):
         blk, bc, mod = ctx.blk, ctx.bc, ctx.mod
         W = ctx.group.compute_view
+        if ctx.sa is None:  # recompute the forward (no MoE bias update, the forward's bias)
+            moe = blk.moe
+            cur = None
+            if moe is not None:
+                cur = moe.expert_bias.clone()
+                moe.expert_bias.copy_(ctx.bias)
+                moe.frozen_bias = True
+            try:
+                _, _, ctx.sa, ctx.sm = _BlockFn._run(ctx.x_in, mod, blk, W, bc)
+            finally:
+                if moe is not None:
+                    moe.expert_bias.copy_(cur)
+                    moe.frozen_bias = False
+            ctx.x_in = ctx.bias = None
         dx2 = dx2.contiguous()
         batched = ctx.dmod_out is not None
         dmod = ctx.dmod_out if batched else torch.zeros(mod.shape, device=mod.device,
@@ -254,6 +280,7 @@ class FusedWorldDiT:
             group = FlatParamGroup(named)
         self.group = group
         self._runs = False  # modulation weight runs of the group, looked up on first use
+        self.recompute = False  # activation checkpointing (TrainConfig.checkpoint_blocks)
 
     def forward(self, model, x_t, t, actions, frame_offset=0, return_aux=False,
                 return_features=None, extra_cond=None):
@@ -272,6 +299,7 @@ class FusedWorldDiT:
         tab = model.rope.table(Fr, frame_offset).to(x.device)
         bc = BlockCtx(B, T, Fr, T // Fr, d, cfg.n_heads, cfg.d_head, tab, cfg.attention,
                       cfg.sla, cfg.causal)
+        bc.recompute = self.recompute and torch.is_grad_enabled()
         feats = None
         aux = torch.zeros((), device=x.device)
         if self._runs is False:

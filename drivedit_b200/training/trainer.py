@@ -75,6 +75,7 @@ class WorldModelTrainer:
         self.fused = self.cuda if fused is None else fused
         if self.fused:
             model.enable_fused(group=self.group)
+            model.fused.recompute = bool(getattr(cfg, "checkpoint_blocks", False))
         self.gen = torch.Generator(device=self.device)
         self.gen.manual_seed(cfg.seed + 1)
         self.step_idx = 0

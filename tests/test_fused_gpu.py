@@ -157,3 +157,50 @@ def test_video_augment_kernel():
     y2 = AugmentationPipeline.fused_clip_augment(u8, flip, br, ct, mean, std, out_bf16=True, input_u8_hwc=True)
     ref2 = clip_augment_reference(u8.permute(0, 1, 4, 2, 3).float() / 255, flip, br, ct, mean, std)
     assert (y2.float() - ref2).abs().max() < 3e-2
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_block_recompute_matches_saved_activations(moe):
+    """Activation checkpointing in the fused engine (each block keeps only its input and
+    reruns its forward in the backward): the same output, the same parameter gradients
+    and the same MoE routing-bias state as keeping the activations."""
+    from drivedit_b200.config import MoEParams
+    from drivedit_b200.models.world_dit import WorldDiT
+    from drivedit_b200.ops.debug import deterministic
+    from drivedit_b200.parallel.flat import FlatParamGroup
+    torch.manual_seed(0)
+    cfg = _small_cfg()
+    if moe:
+        cfg.model.mlp_hidden = 0
+        cfg.model.moe = MoEParams(num_experts=8, top_k=2, expert_dim=128, num_shared=2,
+                                  aux_loss_weight=0.01)
+    m = WorldDiT(cfg.model).cuda().train()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.abs().sum() == 0:
+                p.normal_(0, 0.02)
+    group = FlatParamGroup(m.flat_layout(m.named_parameters()), "cuda")
+    m.enable_fused(group=group)
+    x = torch.randn(2, 2, 16, 32, 32, device="cuda").bfloat16()
+    t = torch.rand(2, device="cuda")
+    a = torch.rand(2, 2, 2, device="cuda")
+    dv = torch.randn(2, 2, 16, 32, 32, device="cuda")
+    moes = [b.moe for b in m.blocks if b.moe is not None]
+    state0 = [(mo.expert_bias.clone(), mo.expert_load_ema.clone()) for mo in moes]
+    out = {}
+    with deterministic():
+        for rec in (False, True):
+            for mo, (b0, e0) in zip(moes, state0):  # both runs start from the same balancing state
+                mo.expert_bias.copy_(b0)
+                mo.expert_load_ema.copy_(e0)
+            m.fused.recompute = rec
+            group.zero_grad()
+            v, aux = m(x, t, a, return_aux=True)
+            (v.float() * dv).sum().add(aux).backward()
+            torch.cuda.synchronize()
+            out[rec] = (v.float().clone(), group.grad.clone(),
+                        [b.moe.expert_bias.clone() for b in m.blocks if b.moe is not None])
+    assert _rel(out[True][0], out[False][0]) < 1e-6
+    assert _rel(out[True][1], out[False][1]) < 1e-3
+    for b1, b2 in zip(out[True][2], out[False][2]):
+        assert torch.equal(b1, b2)
