@@ -47,6 +47,7 @@ class BlockCtx:
         self.causal = causal
         self.rope_pos_offset = rope_pos_offset
         self.recompute = False  # activation checkpointing: blocks rerun their forward in backward
+        self.grad_ready = None  # callback(block index) once a block's backward is enqueued
 
 
 def _gather_of(W):
@@ -196,6 +197,8 @@ class _BlockFn(torch.autograd.Function):
             dx1 = _moe_backward(dx2, d_aux, ctx.sm, blk, W, bc, mod, dmod)
         dx = _attn_backward(dx1, ctx.sa, blk, W, bc, mod, dmod)
         ctx.sa = ctx.sm = ctx.dmod_out = None
+        if bc.grad_ready is not None:  # the block's weight gradients are final
+            bc.grad_ready(getattr(blk, "block_index", -1))
         if batched:
             return dx, None, None, None, None, torch.zeros((), device=dx.device), None
         return dx, dmod, None, None, None, None, None
@@ -281,6 +284,9 @@ class FusedWorldDiT:
         self.group = group
         self._runs = False  # modulation weight runs of the group, looked up on first use
         self.recompute = False  # activation checkpointing (TrainConfig.checkpoint_blocks)
+        # set by a sharded engine: called with a block's index after its backward, so that
+        # block's gradient bucket can be reduced while the rest of the backward runs
+        self.grad_ready = None
 
     def forward(self, model, x_t, t, actions, frame_offset=0, return_aux=False,
                 return_features=None, extra_cond=None):
@@ -300,6 +306,7 @@ class FusedWorldDiT:
         bc = BlockCtx(B, T, Fr, T // Fr, d, cfg.n_heads, cfg.d_head, tab, cfg.attention,
                       cfg.sla, cfg.causal)
         bc.recompute = self.recompute and torch.is_grad_enabled()
+        bc.grad_ready = self.grad_ready
         feats = None
         aux = torch.zeros((), device=x.device)
         if self._runs is False:
@@ -309,6 +316,7 @@ class FusedWorldDiT:
             widths = [blk.ada.weight.shape[0] for blk in model.blocks]
         col = 0
         for i, blk in enumerate(model.blocks):
+            blk.block_index = i
             if self._runs is not None:
                 n = widths[i]
                 x, a = _BlockFn.apply(x, mods[:, col:col + n], blk, g, bc, token,

@@ -115,7 +115,8 @@ class ShardedDataParallel:
 
     def __init__(self, model: nn.Module, group=None, device=None, transport: Optional[str] = None,
                  lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, grad_clip=1.0,
-                 local_params: Optional[Sequence[str]] = None, weight_gather: bool = False):
+                 local_params: Optional[Sequence[str]] = None, weight_gather: bool = False,
+                 overlap: bool = True):
         """``local_params``: names of rank-local parameters (expert-parallel experts).
         They are neither reduced nor sharded: a local flat group with a full AdamW holds
         them, their squared gradient norm joins the global clipping norm, and the main
@@ -174,9 +175,22 @@ class ShardedDataParallel:
                     self.gathers[id(p)] = WeightGather(self, n, p)
             self.local_end = (self.local_end + 3) // 4 * 4
             self.flat.gather_for = lambda p: self.gathers.get(id(p))
-        self.m = torch.zeros(self.shard_len, device=self.device)
-        self.v = torch.zeros(self.shard_len, device=self.device)
-        self.red = torch.zeros(self.shard_len, device=self.device)
+        # Reduce-scatter overlapped with the backward (fused transport): the flat buffer is
+        # cut into buckets (each block's contiguous GEMM weights, plus the remaining
+        # ranges) and every rank owns 1/W of every bucket, so each bucket's reduce can run
+        # on a side stream as soon as the backward has finished that block on all ranks.
+        self.pieces = None
+        self._armed = False
+        self._done = set()
+        self._side = None
+        if overlap and self.transport == "fused" and self.world > 1 and not self.weight_gather:
+            self.pieces = self._plan_pieces()
+            if self.pieces is not None:
+                self.shard_len = sum(hi - lo for lo, hi, _, _ in self.pieces)
+                self.shard_off = -1  # the shard is the pieces' union, not one range
+        self.m = torch.zeros(max(self.shard_len, 4), device=self.device)
+        self.v = torch.zeros(max(self.shard_len, 4), device=self.device)
+        self.red = torch.zeros(max(self.shard_len, 4), device=self.device)
         self.sumsq = torch.zeros(1, device=self.device)
         self.step_count = 0
         self.epoch = 0
@@ -187,6 +201,81 @@ class ShardedDataParallel:
         if self.transport == "fused":
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
+
+    # ------------------------------------------------------------------ overlap
+    def _plan_pieces(self):
+        """This rank's pieces ``(global lo, global hi, local offset, bucket)``: bucket ``i``
+        is the contiguous flat run of block ``i``'s weights (its AdaLN projection, which
+        the batched modulation backward writes last, excluded), bucket ``None`` every
+        remaining range. Each bucket is cut into ``W`` pieces of a multiple of 4 elements
+        (16 bytes); rank ``r`` owns piece ``r`` of every bucket. ``None`` when no block has
+        a contiguous run."""
+        W, r = self.world, self.rank
+        spans: Dict[int, list] = {}
+        for name in self.flat.names:
+            mm = re.match(r"^blocks\.(\d+)\.", name)
+            if mm is None or ".ada." in name or name.endswith("norm1.weight") or name.endswith("norm2.weight"):
+                continue
+            o, k = self.flat.offsets[name]
+            spans.setdefault(int(mm.group(1)), []).append((o, o + k))
+        starts = sorted(o for o, _ in self.flat.offsets.values())
+        runs = {}
+        for i, v in spans.items():
+            lo, hi = min(a for a, _ in v), max(b for _, b in v)
+            mine = {a for a, _ in v}
+            if any(lo <= a < hi and a not in mine for a in starts):  # not contiguous
+                continue
+            lo, hi = lo // 4 * 4, (hi + 3) // 4 * 4
+            runs[i] = (lo, hi)
+        if not runs:
+            return None
+        self.bucket_ids = set(runs)  # identical on every rank (the layout is)
+        # the remaining ranges of [0, numel)
+        rest, cur = [], 0
+        for lo, hi in sorted(runs.values()):
+            if lo > cur:
+                rest.append((cur, lo))
+            cur = max(cur, hi)
+        if cur < self.flat.numel:
+            rest.append((cur, self.flat.numel))
+        buckets = [(i, lo, hi) for i, (lo, hi) in sorted(runs.items())] + [(None, lo, hi) for lo, hi in rest]
+        pieces, off = [], 0
+        for b, lo, hi in buckets:
+            q = ((hi - lo + W - 1) // W + 3) // 4 * 4
+            plo, phi = min(hi, lo + r * q), min(hi, lo + (r + 1) * q)
+            if phi > plo:
+                pieces.append((plo, phi, off, b))
+                off += phi - plo
+        return pieces
+
+    def arm_overlap(self):
+        """Before one backward whose gradients the next ``step`` consumes: each block's
+        bucket is reduced as soon as that block's backward is done (``bucket_ready``)."""
+        self._armed = self.pieces is not None
+        self._done = set()
+
+    def bucket_ready(self, block: int):
+        """Called (by the fused engine) right after block ``block``'s backward has been
+        enqueued: after every rank got there (bounded barrier on a side stream), reduce
+        this rank's piece of the block's bucket by peer loads into the local shard."""
+        if not self._armed or block in self._done:
+            return
+        from ..ops._ext import ext
+
+        if block not in self.bucket_ids:
+            return
+        mine = [p for p in self.pieces if p[3] == block]  # may be empty: still in the barrier
+        main = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            if not self._done:
+                self.sumsq.zero_()
+            self._barrier()                               # block `block` is final on every rank
+            for lo, hi, off, _ in mine:
+                ext().rs_sum_sqnorm(self.sym["grad"].table, self.world, lo, hi - lo, self.red[off:], self.sumsq)
+        self._done.add(block)
 
     # ------------------------------------------------------------------ step
     def zero_grad(self):
@@ -212,23 +301,42 @@ class ShardedDataParallel:
     def _step_fused(self, bc1, bc2, scale):
         from ..ops._ext import ext
 
+        pieces = self.pieces
+        if pieces is None:  # one contiguous shard
+            pieces = [(self.shard_off, self.shard_off + self.shard_len, 0, None)]
+        armed = self._armed and self.pieces is not None
+        if armed and self._side is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._side)
+        # buckets reduced during the backward are done; the rest now
+        done = self._done if armed else set()
+        if armed:  # every planned bucket took its barrier, in the same order on all ranks
+            for b in sorted(self.bucket_ids - done):
+                self.bucket_ready(b)
+            torch.cuda.current_stream(self.device).wait_stream(self._side)
+            done = self._done
+        if not done:
+            self.sumsq.zero_()
         self._barrier()                                   # every rank's gradients are final
-        self.sumsq.zero_()
-        ext().rs_sum_sqnorm(self.sym["grad"].table, self.world, self.shard_off, self.shard_len,
-                            self.red, self.sumsq)
+        for lo, hi, off, b in pieces:
+            if b is None or b not in done:
+                ext().rs_sum_sqnorm(self.sym["grad"].table, self.world, lo, hi - lo, self.red[off:],
+                                    self.sumsq)
         if self.local_opt is not None and self.grad_clip > 0:
             self.sumsq += self.local_opt.grad_sq_norm()
         self._barrier(self.sumsq)                         # squared-norm partials exchanged
         pay = self.flags.tensor(self.world, torch.float32, 4 * self.world)
-        ext().shard_adamw_allgather(
-            self.red, self.flat.master, self.m, self.v, self.sym["master"].table,
-            self.sym["compute"].table, self.world, self.shard_off, self.shard_len,
-            self.flat.decay_end, pay if self.grad_clip > 0 else None, float(self.grad_clip),
-            self.lr, self.betas[0], self.betas[1], self.eps, self.wd, bc1, bc2, scale,
-            self.rank, self.local_end)
+        for lo, hi, off, _ in pieces:
+            ext().shard_adamw_allgather(
+                self.red[off:], self.flat.master, self.m[off:], self.v[off:], self.sym["master"].table,
+                self.sym["compute"].table, self.world, lo, hi - lo,
+                self.flat.decay_end, pay if self.grad_clip > 0 else None, float(self.grad_clip),
+                self.lr, self.betas[0], self.betas[1], self.eps, self.wd, bc1, bc2, scale,
+                self.rank, self.local_end)
         if self.local_opt is not None:
             self._local_step(scale, pay.sum() if self.grad_clip > 0 else None)
         self._barrier()                                   # all peers' stores have landed
+        self._armed = False
+        self._done = set()
 
     def _step_collective(self, bc1, bc2, scale):
         g = self.flat.grad

@@ -60,7 +60,8 @@ class WorldModelTrainer:
             self.engine = ShardedDataParallel(model, process_group, self.device, transport,
                                               cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
                                               cfg.grad_clip, local_params=local,
-                                              weight_gather=getattr(cfg, "shard_weights", False))
+                                              weight_gather=getattr(cfg, "shard_weights", False),
+                                              overlap=getattr(cfg, "overlap_grad_reduce", True))
             self.group = self.engine.flat
             self.opt = None
         else:
@@ -76,6 +77,8 @@ class WorldModelTrainer:
         if self.fused:
             model.enable_fused(group=self.group)
             model.fused.recompute = bool(getattr(cfg, "checkpoint_blocks", False))
+            if self.engine is not None and self.engine.pieces is not None:
+                model.fused.grad_ready = self.engine.bucket_ready
         self.gen = torch.Generator(device=self.device)
         self.gen.manual_seed(cfg.seed + 1)
         self.step_idx = 0
@@ -135,6 +138,8 @@ class WorldModelTrainer:
     def train_step(self, batch: LatentBatch) -> torch.Tensor:
         self.group.zero_grad()
         loss = self.loss(batch)
+        if self.engine is not None:
+            self.engine.arm_overlap()  # one backward, then the step: buckets reduce as they finish
         loss.backward()
         if self.engine is not None:
             self.engine.step()

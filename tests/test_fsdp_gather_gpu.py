@@ -2,7 +2,9 @@
 weight's peer-owned pieces itself (the all-gather fused with the consuming GEMM). Three
 training steps must match the weight-replicated fused engine (to the rounding of the
 atomically accumulated gradients, which differs between any two runs), and every rank
-must end with identical full weights after ``gather_weights``."""
+must end with identical full weights after ``gather_weights``. The same holds for the
+replicated-weight engine whose gradient reduce-scatter runs per block during the backward
+(``train.overlap_grad_reduce``) against the one that reduces after the backward."""
 import os
 import socket
 
@@ -37,15 +39,17 @@ def _worker(rank, world, port, q):
     from drivedit_b200.training.trainer import WorldModelTrainer
 
     out = {}
-    for shard in (False, True):
+    for key, shard, overlap in (("plain", False, False), ("overlap", False, True), ("shard", True, False)):
         cfg = get_config("tiny", ["train.dtype=bf16", "model.attention=sla", "model.latent_h=32",
                                   "model.latent_w=32", "train.grad_clip=0",
-                                  f"train.shard_weights={shard}"])
+                                  f"train.shard_weights={shard}",
+                                  f"train.overlap_grad_reduce={overlap}"])
         torch.manual_seed(0)
         model = WorldDiT(cfg.model)
         tr = WorldModelTrainer(model, cfg.train, torch.device("cuda", rank),
                                process_group=dist.group.WORLD)
         assert tr.engine.weight_gather == shard
+        assert (tr.engine.pieces is not None) == overlap
         if shard:
             assert tr.engine.local_end > tr.engine.shard_len  # the gathered prefix spans ranks
         gen = torch.Generator().manual_seed(7 + rank)
@@ -56,7 +60,7 @@ def _worker(rank, world, port, q):
         sd = tr.state_dict()["model"]
         torch.cuda.synchronize()
         check_device_status()
-        out[shard] = (losses, {k: v.detach().cpu().clone() for k, v in sd.items()},
+        out[key] = (losses, {k: v.detach().cpu().clone() for k, v in sd.items()},
                       tr.engine.flat.compute.float().cpu().clone())
         tr.close()
     q.put((rank, out))
@@ -77,14 +81,16 @@ def test_fused_weight_gather_training_matches_replicated_weights():
         p.join(timeout=120)
         assert p.exitcode == 0
     for r in range(2):
-        for a, b in zip(res[r][True][0], res[r][False][0]):
-            assert abs(a - b) <= 1e-3 * abs(b), (r, res[r][True][0], res[r][False][0])
-        for k, v in res[r][False][1].items():
-            got = res[r][True][1][k]
-            # AdamW's early steps are sign-like: a gradient whose rounding differs can move
-            # an element by up to 2 lr per step (lr 1e-4, 3 steps)
-            assert torch.allclose(got, v, rtol=0, atol=1e-3), (r, k, (got - v).abs().max())
-    for k in res[0][True][1]:
-        assert torch.equal(res[0][True][1][k], res[1][True][1][k]), k
-    # after gather_weights both ranks hold the same full bf16 weights
-    assert torch.equal(res[0][True][2], res[1][True][2])
+        for other in ("shard", "overlap"):
+            for a, b in zip(res[r][other][0], res[r]["plain"][0]):
+                assert abs(a - b) <= 1e-3 * abs(b), (r, other, res[r][other][0], res[r]["plain"][0])
+            for k, v in res[r]["plain"][1].items():
+                got = res[r][other][1][k]
+                # AdamW's early steps are sign-like: a gradient whose rounding differs can move
+                # an element by up to 2 lr per step (lr 1e-4, 3 steps)
+                assert torch.allclose(got, v, rtol=0, atol=1e-3), (r, other, k, (got - v).abs().max())
+    for other in ("shard", "overlap"):
+        for k in res[0][other][1]:
+            assert torch.equal(res[0][other][1][k], res[1][other][1][k]), (other, k)
+        # both ranks hold the same full bf16 weights
+        assert torch.equal(res[0][other][2], res[1][other][2])
