@@ -24,7 +24,8 @@
 // operand data than in 128 x 256 single-CTA tiles (the B half instead of all of B).
 // The even CTA's MMA commits free the ring slots and hand accumulators to the epilogue
 // of both CTAs; the odd CTA's epilogue warps release the accumulator on the even CTA's
-// barrier. No load is multicast.
+// barrier. No load is multicast. Before a CTA of a pair exits it waits for the last
+// arrive its peer sends to each of its barriers. Pairs are opt-in (see gemm()).
 //
 // Replaces every nn.Linear of the reference (layers/mha.py:307-308, layers/mlp.py:112-114,
 // layers/moe.py:54-56) and carries the SwiGLU (layers/mlp.py:131-155), rotary
@@ -621,6 +622,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if constexpr (PAIR) {
+        // the even CTA's MMA commits release this CTA's stages through the cluster; wait
+        // for the last release of every stage used, so that no arrive from the peer can
+        // land in this CTA's shared memory after it exits (where the next kernel's CTA
+        // may already own it)
+        if (ok) {
+          int s = stage, ph = phase;
+          for (int i = 0; i < min(issued, STAGES); ++i) {
+            if (--s < 0) {
+              s = STAGES - 1;
+              ph ^= 1;
+            }
+            long long t0 = clock64();
+            while (!mbar_try_wait(&empty[s], ph) && clock64() - t0 < kSpinLimitCycles / 8) {
+            }
+          }
+        }
+      }
       if (!ok) {
         record_status(status, kStatusTimeoutProducer);
         *abort_flag = 1;
@@ -648,6 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       bool any = false;
+      int tiles = 0;
       // signal an mbarrier of this CTA (and, for pairs, the same one of the odd CTA)
       auto commit_both = [&](uint64_t* bar) {
         if constexpr (PAIR) {
@@ -694,6 +714,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         commit_both(&acc_full[buf]);
+        ++tiles;
         if (++buf == 2) {
           buf = 0;
           acc_phase ^= 1;
@@ -702,6 +723,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         record_status(status, kStatusTimeoutMma);
         *abort_flag = 1;
+      } else if (PAIR) {
+        // the odd CTA's epilogue releases the accumulators with remote arrives: take the
+        // last release of each buffer used before this CTA can exit
+        int b = buf, ph = acc_phase;
+        for (int i = 0; i < min(tiles, 2); ++i) {
+          if (--b < 0) {
+            b = 1;
+            ph ^= 1;
+          }
+          long long t0 = clock64();
+          while (!mbar_try_wait(&acc_empty[b], ph) && clock64() - t0 < kSpinLimitCycles / 8) {
+          }
+        }
       }
       if (any) {
         // all MMAs of this thread complete before TMEM is released
@@ -1099,8 +1133,13 @@ void gemm(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   const long nbatch = (a.grouped == 0 && a.batch > 1) ? a.batch : 1;
   // CTA pairs (256-row tiles over two SMs) for plain GEMMs: not for grouped tables, the
   // peer-memory operand forms, or problems of one 128-row tile
-  static const bool no_pairs = std::getenv("DDB_GEMM_NO_PAIRS") != nullptr;
-  const int clusters = (!no_pairs && g_pair_mode != 0 && a.grouped == 0 && a.a_npeers == 0 && a.d_peers == nullptr &&
+  // Pairs are opt-in (DDB_GEMM_PAIRS=1 lets the cost model choose them, gemm_set_pair_mode(1)
+  // forces them): intermittent launch failures and TMEM-leak errors appeared in long
+  // training runs once pairs were on by default; the cause is not pinned down.
+  static const bool pairs_env = std::getenv("DDB_GEMM_PAIRS") != nullptr &&
+                                std::getenv("DDB_GEMM_NO_PAIRS") == nullptr;
+  const bool pairs_on = g_pair_mode == 1 || (g_pair_mode == -1 && pairs_env);
+  const int clusters = (pairs_on && a.grouped == 0 && a.a_npeers == 0 && a.d_peers == nullptr &&
                         a.gb_world <= 1 && a.M > BM) ? pair_clusters(dev) : 0;
   // Estimated time of a (pair, BN, split-K) choice: waves of persistent tiles x tile work
   // at a relative efficiency. Operand bytes staged and read from shared memory per FLOP
