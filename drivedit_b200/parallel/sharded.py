@@ -116,7 +116,7 @@ class ShardedDataParallel:
     def __init__(self, model: nn.Module, group=None, device=None, transport: Optional[str] = None,
                  lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, grad_clip=1.0,
                  local_params: Optional[Sequence[str]] = None, weight_gather: bool = False,
-                 overlap: bool = True):
+                 overlap: bool = False):
         """``local_params``: names of rank-local parameters (expert-parallel experts).
         They are neither reduced nor sharded: a local flat group with a full AdamW holds
         them, their squared gradient norm joins the global clipping norm, and the main

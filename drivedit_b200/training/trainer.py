@@ -61,7 +61,7 @@ class WorldModelTrainer:
                                               cfg.lr, cfg.betas, cfg.eps, cfg.weight_decay,
                                               cfg.grad_clip, local_params=local,
                                               weight_gather=getattr(cfg, "shard_weights", False),
-                                              overlap=getattr(cfg, "overlap_grad_reduce", True))
+                                              overlap=getattr(cfg, "overlap_grad_reduce", False))
             self.group = self.engine.flat
             self.opt = None
         else:
