@@ -17,13 +17,22 @@ checker, which this framework does not rely on):
     access is skipped, so a corrupt routing table shows up as an error instead of a
     memory fault. :func:`drivedit_b200.ops._ext.check_device_status` raises on it.
 
-Both are process-wide and off by default.
+``sync_check``
+    Every extension entry point is bracketed by a device synchronize and a read of the
+    status word, so an asynchronous kernel fault (or an expired bounded wait) is raised
+    as a :class:`~drivedit_b200.ops._ext.KernelFault` naming the entry point that launched
+    it (or, when raised before it, the work in between), with the entry points called
+    just before. ``DDB_SYNC_CHECK=1`` turns it on for a whole run (``bench.py``, the
+    tests), ``DDB_SYNC_CHECK_LOG=<file>`` also appends every call to a file before it
+    runs. For locating a fault, not for timing; not usable inside CUDA-graph capture.
+
+All are process-wide and off by default.
 """
 from __future__ import annotations
 
 from contextlib import contextmanager
 
-from ._ext import ext
+from ._ext import KernelFault, ext, set_sync_check, sync_check  # noqa: F401
 
 BAD_INDEX_STATUS = 6
 
