@@ -12,6 +12,7 @@ applied in the GEMM epilogue. :func:`pack_swiglu` / :func:`unpack_swiglu` conver
 """
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import torch
@@ -49,19 +50,38 @@ def swiglu_hidden(d_model: int, d_ff: Optional[int] = None, multiple_of: int = 8
     return multiple_of * ((h + multiple_of - 1) // multiple_of)
 
 
+_ACTIVATIONS = {"silu": F.silu, "swish": F.silu, "gelu": F.gelu, "relu": F.relu}
+
+
+def _init_in_out(w_in, w_out, biases=()):
+    """Input projections N(0, 0.02); the projection back into the residual stream
+    N(0, 0.02 / sqrt(24)) (depth-scaled); biases zero."""
+    for w in w_in:
+        nn.init.normal_(w.weight, std=0.02)
+    nn.init.normal_(w_out.weight, std=0.02 / math.sqrt(24.0))
+    for lin in list(w_in) + [w_out]:
+        if lin.bias is not None:
+            nn.init.zeros_(lin.bias)
+
+
 class MLP(nn.Module):
-    def __init__(self, d_model: int, d_ff: Optional[int] = None, activation: str = "gelu",
-                 dropout: float = 0.0, bias: bool = True):
+    """``w2(act(w1 x))``; ``activation`` one of silu (default), swish, gelu (exact), relu."""
+
+    def __init__(self, d_model: int, d_ff: Optional[int] = None, activation: str = "silu",
+                 dropout: float = 0.0, bias: bool = False):
         super().__init__()
-        d_ff = d_ff or 4 * d_model
-        self.fc1 = nn.Linear(d_model, d_ff, bias=bias)
-        self.fc2 = nn.Linear(d_ff, d_model, bias=bias)
-        self.act = {"gelu": nn.GELU(approximate="tanh"), "relu": nn.ReLU(),
-                    "silu": nn.SiLU()}[activation]
-        self.dropout = nn.Dropout(dropout) if dropout > 0 else nn.Identity()
+        if activation not in _ACTIVATIONS:
+            raise ValueError(f"Unsupported activation: {activation}")
+        self.d_model, self.d_ff = d_model, d_ff or 4 * d_model
+        self.activation_name = activation
+        self.activation = _ACTIVATIONS[activation]
+        self.w1 = nn.Linear(d_model, self.d_ff, bias=bias)
+        self.w2 = nn.Linear(self.d_ff, d_model, bias=bias)
+        self.drop = nn.Dropout(dropout) if dropout > 0 else nn.Identity()
+        _init_in_out([self.w1], self.w2)
 
     def forward(self, x):
-        return self.fc2(self.dropout(self.act(self.fc1(x))))
+        return self.w2(self.drop(self.activation(self.w1(x))))
 
 
 class SwiGLU(nn.Module):
@@ -81,47 +101,59 @@ class SwiGLU(nn.Module):
 
 
 class GeGLU(nn.Module):
+    """``w3(gelu(w1 x) * w2 x)`` (exact GELU), hidden ``8d/3`` rounded up to 8 by default."""
+
     def __init__(self, d_model: int, d_ff: Optional[int] = None, dropout: float = 0.0,
                  bias: bool = False):
         super().__init__()
+        self.d_model = d_model
         self.d_ff = swiglu_hidden(d_model, d_ff)
         self.w1 = nn.Linear(d_model, self.d_ff, bias=bias)
         self.w2 = nn.Linear(d_model, self.d_ff, bias=bias)
         self.w3 = nn.Linear(self.d_ff, d_model, bias=bias)
         self.dropout = nn.Dropout(dropout) if dropout > 0 else nn.Identity()
+        _init_in_out([self.w1, self.w2], self.w3)
 
     def forward(self, x):
-        return self.w3(self.dropout(F.gelu(self.w1(x), approximate="tanh") * self.w2(x)))
+        return self.w3(self.dropout(F.gelu(self.w1(x)) * self.w2(x)))
 
 
 class ConditionalMLP(nn.Module):
-    """SwiGLU whose hidden activations are FiLM-modulated by a conditioning vector."""
+    """A standard :class:`MLP` applied to ``x + cond_proj(cond)``; ``cond`` is per token
+    ``[B, T, d_cond]`` or per sample ``[B, d_cond]`` (broadcast over the tokens)."""
 
-    def __init__(self, d_model: int, cond_dim: int, d_ff: Optional[int] = None,
-                 dropout: float = 0.0, bias: bool = False):
+    def __init__(self, d_model: int, d_cond: int, d_ff: Optional[int] = None,
+                 activation: str = "silu", dropout: float = 0.0, bias: bool = False):
         super().__init__()
-        self.mlp = SwiGLU(d_model, d_ff, dropout, bias)
-        self.film = nn.Linear(cond_dim, 2 * self.mlp.d_ff)
-        nn.init.zeros_(self.film.weight)
-        nn.init.zeros_(self.film.bias)
+        self.d_model, self.d_cond = d_model, d_cond
+        self.mlp = MLP(d_model, d_ff or 4 * d_model, activation, dropout, bias)
+        self.d_ff = self.mlp.d_ff
+        self.cond_proj = nn.Linear(d_cond, d_model, bias=bias)
+        nn.init.normal_(self.cond_proj.weight, std=0.02)
+        if bias:
+            nn.init.zeros_(self.cond_proj.bias)
 
     def forward(self, x, cond):
-        gamma, beta = self.film(cond).chunk(2, -1)
-        if gamma.dim() == 2:
-            gamma, beta = gamma[:, None], beta[:, None]
-        h = F.silu(self.mlp.w1(x)) * self.mlp.w2(x)
-        h = h * (1 + gamma) + beta
-        return self.mlp.w3(self.mlp.dropout(h))
+        c = self.cond_proj(cond)
+        return self.mlp(x + (c[:, None] if c.dim() == 2 else c))
 
 
-def create_mlp(d_model: int, mlp_type: str = "swiglu", d_ff: Optional[int] = None,
-               dropout: float = 0.0, bias: bool = False, **kw) -> nn.Module:
+def create_mlp(d_model: int, mlp_type: str = "standard", d_ff: Optional[int] = None,
+               activation: str = "silu", dropout: float = 0.0, bias: bool = False,
+               d_cond: Optional[int] = None) -> nn.Module:
+    """``standard`` (an :class:`MLP` with ``activation``), ``swiglu``, ``geglu``; also
+    ``gelu`` / ``relu`` / ``silu`` (a standard MLP with that activation) and
+    ``conditional`` (needs ``d_cond``)."""
+    if mlp_type == "standard":
+        return MLP(d_model, d_ff, activation, dropout, bias)
     if mlp_type == "swiglu":
         return SwiGLU(d_model, d_ff, dropout, bias)
     if mlp_type == "geglu":
         return GeGLU(d_model, d_ff, dropout, bias)
-    if mlp_type in ("gelu", "relu", "silu", "mlp"):
-        return MLP(d_model, d_ff, "gelu" if mlp_type == "mlp" else mlp_type, dropout, bias)
+    if mlp_type in ("gelu", "relu", "silu"):
+        return MLP(d_model, d_ff, mlp_type, dropout, bias)
     if mlp_type == "conditional":
-        return ConditionalMLP(d_model, kw["cond_dim"], d_ff, dropout, bias)
-    raise ValueError(f"unknown mlp_type {mlp_type!r}")
+        if d_cond is None:
+            raise ValueError("the conditional MLP needs d_cond")
+        return ConditionalMLP(d_model, d_cond, d_ff, activation, dropout, bias)
+    raise ValueError(f"Unsupported MLP type: {mlp_type}")

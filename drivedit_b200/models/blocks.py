@@ -10,11 +10,13 @@
   projected context.
 * :class:`MemoryEfficientDiTBlock` (:249-307): activation checkpointing wrapper.
 * :class:`MoEDiTBlock` (``layers/moe.py:427-547``): the same block with the MoE FFN.
-* :class:`FlowMatchingBlock` / :class:`FlowPredictor` (flow_matching.py:94-218): 6-way
-  AdaLN-Zero modulation from the time embedding, zero-initialised output.
+* :class:`FlowMatchingConfig`, :class:`FlowMatchingBlock`, :class:`FlowPredictor`
+  (flow_matching.py:35-218): the reference's module names and call signatures, so its
+  weights and configs load; the predictor can also map a token width other than ``dim``.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -40,7 +42,7 @@ class DiTBlock(nn.Module):
         cls = CausalMultiHeadAttention if causal else BidirectionalMultiHeadAttention
         self.attn = cls(d_model, n_heads, dropout=dropout, bias=bias, rope_layer=self.rope_layer,
                         tokens_per_frame=tokens_per_frame)
-        self.mlp = create_mlp(d_model, mlp_type, d_ff, dropout, bias)
+        self.mlp = create_mlp(d_model, mlp_type=mlp_type, d_ff=d_ff, dropout=dropout, bias=bias)
         if cond_dim is not None:
             self.norm_attn = AdaLN(d_model, cond_dim)
             self.norm_mlp = AdaLN(d_model, cond_dim)
@@ -166,47 +168,83 @@ class FlowTimestepEmbedding(nn.Module):
         return self.linear2(F.silu(self.linear1(torch.cat([ang.sin(), ang.cos()], -1))))
 
 
+@dataclass
+class FlowMatchingConfig:
+    """Settings of the flow-matching predictor, sampler and trainer (the reference's
+    schema, blocks/flow_matching.py:35-59, kept field for field so its configs load).
+    ``latent_dim`` and ``context_dim`` are additions: the token width when it differs
+    from ``dim`` (an input and an output projection then map between them), and the
+    width of a context that is projected to ``dim`` instead of added as it is."""
+    dim: int = 512
+    num_layers: int = 6
+    num_heads: int = 8
+    mlp_ratio: int = 4
+    num_steps: int = 4
+    sigma_min: float = 1e-4
+    sigma_max: float = 80.0
+    use_cfg: bool = True
+    cfg_scale: float = 7.5
+    teacher_steps: int = 4
+    student_steps: int = 1
+    distillation_weight: float = 1.0
+    time_embed_dim: int = 128
+    fourier_features: int = 256
+    latent_dim: Optional[int] = None
+    context_dim: Optional[int] = None
+
+
 class FlowMatchingBlock(nn.Module):
-    """Bidirectional block with AdaLN-Zero (shift, scale, gate) x 2 from the time embedding."""
+    """Bidirectional transformer block modulated by the time embedding: ``time_mlp`` maps
+    it to (scale, shift, gate) for the attention and for the MLP, in that order, and each
+    branch computes ``x + gate * f(norm(x) * (1 + scale) + shift)``
+    (blocks/flow_matching.py:94-146; same module names, so its weights load)."""
 
-    def __init__(self, d_model: int, n_heads: int, d_ff: Optional[int] = None, dropout: float = 0.0):
+    def __init__(self, dim: int, num_heads: int, mlp_ratio: int = 4):
         super().__init__()
-        self.norm1 = RMSNorm(d_model)
-        self.attn = BidirectionalMultiHeadAttention(d_model, n_heads, dropout=dropout)
-        self.norm2 = RMSNorm(d_model)
-        self.mlp = MLP(d_model, d_ff or 4 * d_model, "gelu", dropout)
-        self.modulation = nn.Sequential(nn.SiLU(), nn.Linear(d_model, 6 * d_model))
-        nn.init.zeros_(self.modulation[1].weight)
-        nn.init.zeros_(self.modulation[1].bias)
+        self.dim, self.num_heads = dim, num_heads
+        self.norm1 = RMSNorm(dim)
+        self.norm2 = RMSNorm(dim)
+        self.time_mlp = nn.Sequential(nn.SiLU(), nn.Linear(dim, 6 * dim))
+        self.attention = MultiHeadAttention(dim, num_heads)
+        self.mlp = MLP(dim, dim * mlp_ratio)
 
-    def forward(self, x: torch.Tensor, t_emb: torch.Tensor) -> torch.Tensor:
-        sh1, sc1, g1, sh2, sc2, g2 = self.modulation(t_emb)[:, None].chunk(6, -1)
-        x = x + g1 * self.attn(self.norm1(x) * (1 + sc1) + sh1)[0]
-        return x + g2 * self.mlp(self.norm2(x) * (1 + sc2) + sh2)
+    def forward(self, x: torch.Tensor, time_emb: torch.Tensor,
+                mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        mods = self.time_mlp(time_emb)[:, None]
+        sc1, sh1, g1, sc2, sh2, g2 = mods.chunk(6, dim=-1)
+        a, _ = self.attention(torch.addcmul(sh1, self.norm1(x), 1 + sc1), mask=mask)
+        x = torch.addcmul(x, g1, a)
+        return torch.addcmul(x, g2, self.mlp(torch.addcmul(sh2, self.norm2(x), 1 + sc2)))
 
 
 class FlowPredictor(nn.Module):
-    """Velocity network ``v(z_t, t[, context])`` over token sequences ``[B, T, latent_dim]``."""
+    """Velocity network ``v(z_t, t)`` over token sequences: time embedding, input
+    projection, :class:`FlowMatchingBlock` stack, RMSNorm + zero-initialised output
+    projection (blocks/flow_matching.py:149-218; same module names). A context
+    ``[B, C, D]`` enters as its token mean added to every token."""
 
-    def __init__(self, latent_dim: int, d_model: int = 512, n_layers: int = 6, n_heads: int = 8,
-                 d_ff: Optional[int] = None, context_dim: Optional[int] = None):
+    def __init__(self, config: FlowMatchingConfig):
         super().__init__()
-        self.time_embed = FlowTimestepEmbedding(d_model)
-        self.input_proj = nn.Linear(latent_dim, d_model)
-        self.context_proj = nn.Linear(context_dim, d_model) if context_dim else None
-        self.blocks = nn.ModuleList([FlowMatchingBlock(d_model, n_heads, d_ff) for _ in range(n_layers)])
-        self.norm = RMSNorm(d_model)
-        self.output_proj = nn.Linear(d_model, latent_dim)
-        nn.init.zeros_(self.output_proj.weight)
-        nn.init.zeros_(self.output_proj.bias)
+        self.config = config
+        d, ld = config.dim, config.latent_dim or config.dim
+        self.time_embed = FlowTimestepEmbedding(d, config.fourier_features, time_scale=1.0)
+        self.input_proj = nn.Linear(ld, d)
+        self.context_proj = nn.Linear(config.context_dim, d) if config.context_dim else None
+        self.blocks = nn.ModuleList([FlowMatchingBlock(d, config.num_heads, config.mlp_ratio)
+                                     for _ in range(config.num_layers)])
+        self.output_proj = nn.Sequential(RMSNorm(d), nn.Linear(d, ld))
+        nn.init.zeros_(self.output_proj[1].weight)
+        nn.init.zeros_(self.output_proj[1].bias)
 
-    def forward(self, z_t: torch.Tensor, t: torch.Tensor, context: Optional[torch.Tensor] = None):
+    def forward(self, z: torch.Tensor, t: torch.Tensor, mask: Optional[torch.Tensor] = None,
+                context: Optional[torch.Tensor] = None) -> torch.Tensor:
         if t.dim() == 0:
-            t = t.expand(z_t.shape[0])
+            t = t.expand(z.shape[0])
         te = self.time_embed(t)
-        x = self.input_proj(z_t)
-        if context is not None and self.context_proj is not None:
-            x = x + self.context_proj(context).mean(1, keepdim=True)
+        h = self.input_proj(z)
+        if context is not None:
+            c = self.context_proj(context) if self.context_proj is not None else context
+            h = h + c.mean(dim=1, keepdim=True)
         for blk in self.blocks:
-            x = blk(x, te)
-        return self.output_proj(self.norm(x))
+            h = blk(h, te, mask)
+        return self.output_proj(h)

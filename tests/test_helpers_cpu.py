@@ -57,18 +57,22 @@ def test_fused_add_norm_and_rotary_and_positions():
 
 
 def test_ddim_sample_equals_euler_at_eta_zero_and_is_exact_on_straight_paths():
-    from drivedit_b200.training.flow_matching import RectifiedFlowSampler
+    from drivedit_b200.training.flow_matching import RectifiedFlowSampler, ddim_sample, euler_sample
 
     torch.manual_seed(3)
     x0, x1 = torch.randn(4, 8), torch.randn(4, 8)
     # the exact velocity field of the straight path through (x0, x1)
     vel = lambda x, t: x1 - x0
-    s = RectifiedFlowSampler(num_steps=5)
-    fwd = s.ddim_sample(vel, x0, t_start=0.0, t_end=1.0)
+    fwd = ddim_sample(vel, x0, 5, t_start=0.0, t_end=1.0)
     assert torch.allclose(fwd, x1, atol=1e-5)
-    assert torch.allclose(fwd, s.sample(vel, x0), atol=1e-5)
-    back = s.ddim_sample(vel, x1)  # reference schedule: t from 1 to 0
+    assert torch.allclose(fwd, euler_sample(vel, x0, 5), atol=1e-5)
+    back = ddim_sample(vel, x1, 5)  # reference schedule: t from 1 to 0
     assert torch.allclose(back, x0, atol=1e-5)
     g = torch.Generator().manual_seed(0)
-    noisy = s.ddim_sample(vel, x1, eta=0.5, generator=g)
+    noisy = ddim_sample(vel, x1, 5, eta=0.5, generator=g)
     assert noisy.shape == x0.shape and not torch.allclose(noisy, x0)
+    # the predictor form: v(z, t, mask, context), trajectory and final sample
+    s = RectifiedFlowSampler(lambda z, t, mask, ctx: x1 - x0)
+    out = s.sample(x0, 5)
+    assert out["trajectory"].shape == (6, 4, 8) and torch.allclose(out["final_sample"], x1, atol=1e-5)
+    assert torch.allclose(s.ddim_sample(x1, 5), x0, atol=1e-5)

@@ -51,6 +51,9 @@ def test_block_variants():
 
 
 def test_flow_predictor_zero_init():
-    fp = FlowPredictor(latent_dim=8, d_model=32, n_layers=2, n_heads=4)
-    v = fp(torch.randn(2, 6, 8), torch.rand(2))
-    assert torch.count_nonzero(v) == 0
+    from drivedit_b200.models.blocks import FlowMatchingConfig
+
+    cfg = FlowMatchingConfig(dim=32, num_layers=2, num_heads=4, latent_dim=8, context_dim=12)
+    fp = FlowPredictor(cfg)
+    v = fp(torch.randn(2, 6, 8), torch.rand(2), None, torch.randn(2, 3, 12))
+    assert v.shape == (2, 6, 8) and torch.count_nonzero(v) == 0

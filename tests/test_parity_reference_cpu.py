@@ -196,3 +196,113 @@ def test_sla_reference_semantics(ref, causal):
     r = ref["layers.sla"].sla(q, k, v, config=rcfg, training=False)
     o = sla_reference(q, k, v, ocfg)
     _close(o, r, 1e-4)
+
+
+@pytest.mark.parametrize("activation", ["silu", "gelu", "relu"])
+def test_mlp_family(ref, activation):
+    """Standard MLP, GeGLU and the conditional MLP load the reference's weights by name
+    and match its outputs (exact GELU)."""
+    from drivedit_b200.layers.mlp import GeGLU, ConditionalMLP, MLP, create_mlp
+    torch.manual_seed(0)
+    rm = ref["layers.mlp"]
+    x = torch.randn(2, 16, 64)
+    r, o = rm.MLP(64, 128, activation), MLP(64, 128, activation)
+    o.load_state_dict(r.state_dict())
+    _close(o(x), r(x))
+    r, o = rm.GeGLU(64), GeGLU(64)
+    o.load_state_dict(r.state_dict())
+    _close(o(x), r(x))
+    c = torch.randn(2, 24)
+    r, o = rm.ConditionalMLP(64, 24, activation=activation), ConditionalMLP(64, 24, activation=activation)
+    o.load_state_dict(r.state_dict())
+    _close(o(x, c), r(x, c))
+    for kind in ("standard", "swiglu", "geglu"):
+        r, o = rm.create_mlp(64, kind, 96, activation), create_mlp(64, kind, 96, activation)
+        o.load_state_dict(r.state_dict())
+        _close(o(x), r(x))
+
+
+def test_dit_block_standard_mlp(ref):
+    from drivedit_b200.models.blocks import DiTBlock
+    torch.manual_seed(0)
+    kw = dict(d_ff=256, mlp_type="standard", causal=True, use_rope=True, max_seq_len=64)
+    r = ref["blocks.dit_block"].DiTBlock(128, 4, **kw)
+    o = DiTBlock(128, 4, **kw)
+    o.load_state_dict(r.state_dict())
+    x = torch.randn(2, 16, 128)
+    _close(o(x)[0], r(x)[0], 1e-4)
+
+
+def _flow_pair(ref, **kw):
+    fm = ref["blocks.flow_matching"]
+    from drivedit_b200.models.blocks import FlowMatchingConfig, FlowPredictor
+    torch.manual_seed(0)
+    rc = fm.FlowMatchingConfig(**kw)
+    r = fm.FlowPredictor(rc)
+    with torch.no_grad():  # the zero-initialised output would hide every difference
+        r.output_proj[1].weight.normal_(0, 0.02)
+        r.output_proj[1].bias.normal_(0, 0.02)
+    o = FlowPredictor(FlowMatchingConfig(**kw))
+    o.load_state_dict(r.state_dict())
+    return fm, rc, r, o
+
+
+def test_flow_matching_block_and_predictor(ref):
+    fm = ref["blocks.flow_matching"]
+    from drivedit_b200.models.blocks import FlowMatchingBlock
+    torch.manual_seed(0)
+    rb, ob = fm.FlowMatchingBlock(64, 4), FlowMatchingBlock(64, 4)
+    ob.load_state_dict(rb.state_dict())
+    x, te = torch.randn(2, 12, 64), torch.randn(2, 64)
+    _close(ob(x, te), rb(x, te), 1e-5)
+    _, _, r, o = _flow_pair(ref, dim=64, num_layers=2, num_heads=4)
+    z, t, ctx = torch.randn(2, 12, 64), torch.rand(2), torch.randn(2, 5, 64)
+    _close(o(z, t), r(z, t), 1e-5)
+    _close(o(z, t, None, ctx), r(z, t, None, ctx), 1e-5)
+
+
+def test_flow_sampler_and_losses(ref):
+    from drivedit_b200.training.flow_matching import FlowMatchingLoss, RectifiedFlowSampler
+    fm, rc, r, o = _flow_pair(ref, dim=64, num_layers=2, num_heads=4)
+    z, ctx = torch.randn(2, 12, 64), torch.randn(2, 5, 64)
+    rs = fm.RectifiedFlowSampler(r, rc).sample(z, 4, ctx, guidance_scale=2.0)
+    os_ = RectifiedFlowSampler(o, o.config).sample(z, 4, ctx, guidance_scale=2.0)
+    _close(os_["trajectory"], rs["trajectory"], 1e-5)
+    _close(RectifiedFlowSampler(o).ddim_sample(z, 4), fm.RectifiedFlowSampler(r, rc).ddim_sample(z, 4), 1e-5)
+    rl, ol = fm.FlowMatchingLoss(rc), FlowMatchingLoss(o.config)
+    z0, z1, pred = torch.randn(3, 2, 12, 64).unbind(0)
+    mask = (torch.rand(2, 12) > 0.3).float()
+    t = torch.rand(2)
+    _close(ol.flow_matching_loss(pred, z0, z1, t, mask), rl.flow_matching_loss(pred, z0, z1, t, mask))
+    traj = rs["trajectory"]
+    _close(ol.distillation_loss(pred, traj, 0.25, mask), rl.distillation_loss(pred, traj, 0.25, mask))
+
+
+def test_flow_trainer_steps(ref):
+    """Same seed, same batch, same optimizer: the reference trainer and this one draw
+    the same noise and times, report the same losses and leave the same weights."""
+    from drivedit_b200.training.flow_matching import FlowMatchingTrainer
+    fm, rc, r, o = _flow_pair(ref, dim=64, num_layers=2, num_heads=4, teacher_steps=2)
+    batch = {"latents": torch.randn(2, 12, 64), "context": torch.randn(2, 5, 64)}
+    rt, ot = fm.FlowMatchingTrainer(r, rc), FlowMatchingTrainer(o, o.config)
+    ropt = torch.optim.AdamW(r.parameters(), lr=1e-3)
+    oopt = torch.optim.AdamW(o.parameters(), lr=1e-3)
+    for step in (0, 1):  # step 0 adds the consistency term
+        torch.manual_seed(10 + step)
+        lr_ = rt.train_step(batch, ropt, step)
+        torch.manual_seed(10 + step)
+        lo_ = ot.train_step(batch, oopt, step)
+        assert lr_.keys() == lo_.keys()
+        for k in lr_:
+            assert abs(lr_[k] - lo_[k]) <= 1e-5 * max(1.0, abs(lr_[k])), (k, lr_[k], lo_[k])
+    rp = dict(r.named_parameters())
+    for n, p in o.named_parameters():
+        _close(p.detach(), rp[n].detach(), 1e-4)
+    teacher_r = fm.FlowPredictor(rc)
+    teacher_o = type(o)(o.config)
+    teacher_o.load_state_dict(teacher_r.state_dict())
+    torch.manual_seed(20)
+    dr = rt.distillation_step(teacher_r, batch, ropt)
+    torch.manual_seed(20)
+    do = ot.distillation_step(teacher_o, batch, oopt)
+    assert abs(dr["distillation"] - do["distillation"]) <= 1e-5 * max(1.0, dr["distillation"])
