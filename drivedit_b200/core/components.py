@@ -218,3 +218,14 @@ class FlowMatchingPredictor(nn.Module):
         for i in range(n):
             z = z + self.forward(z, torch.full((z.shape[0],), i / n, device=z.device)) / n
         return z
+
+
+def create_attention_mask(seq_len: int, causal: bool = True, device=None) -> torch.Tensor:
+    """Additive mask ``[seq_len, seq_len]`` (core/components.py:496-502): 0 where a query
+    may attend, ``-inf`` above the diagonal when ``causal``; all zeros otherwise."""
+    if not causal:
+        return torch.zeros(seq_len, seq_len, device=device)
+    return torch.full((seq_len, seq_len), float("-inf"), device=device).triu(1)
+
+
+from ..utils.model_utils import count_parameters  # noqa: E402,F401  (the reference exports it here too)

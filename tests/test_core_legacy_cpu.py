@@ -49,3 +49,45 @@ def test_system_trains_and_generates():
     assert torch.isfinite(out["loss"]) and out["latents"].shape[1] == 4
     gen = sysm(frames, controls, mode="inference", horizon=2)
     assert gen["frames"].shape == (1, 2, 3, 32, 32) and gen["latents"].shape[1] == 2
+
+
+def test_core_encoders_memory_and_causal_dit():
+    """The working counterparts of the reference's core sketch: encoders into the token
+    space, the memory bank, and the causal DiT whose cached generation equals the
+    full-sequence forward."""
+    from drivedit_b200.core.base import (BaseEncoder, CausalDiT, ControlEncoder, DepthEncoder,
+                                         MemoryBank, VAEEncoder)
+    from drivedit_b200.core.components import create_attention_mask
+    torch.manual_seed(0)
+    cfg = DriveDiTConfig(latent_channels=4, latent_spatial_size=2, model_dim=32, n_heads=4,
+                         n_layers=2, max_memory_frames=2, max_memory_objects=3, device="cpu",
+                         dtype=torch.float32)
+    vae = VAEEncoder(cfg)
+    frames = torch.rand(1, 2, 3, 32, 32)
+    tok = vae.encode(frames)
+    assert isinstance(vae, BaseEncoder) and tok.shape == (1, 2, 4, 32) and vae.get_token_dim() == 32
+    assert vae.decode(tok, (32, 32)).shape == (1, 2, 3, 32, 32)
+    assert DepthEncoder(cfg).encode(torch.rand(1, 2, 1, 16, 16)).shape == (1, 2, 4, 32)
+    assert ControlEncoder(cfg).encode(torch.randn(3, 6)).shape == (3, 1, 32)
+
+    mem = MemoryBank(cfg)
+    sp, ob = mem.get_memory_tokens()
+    assert sp.shape == (1, 1, 32) and not sp.any()          # not full yet: one zero token
+    for i in range(2):
+        mem.update(torch.rand(1, 3, 16, 16), i)
+    mem.add_objects(torch.randn(1, 32))
+    sp, ob = mem.get_memory_tokens()
+    assert sp.shape == (1, 2, 32) and ob.shape == (1, 1, 32)
+
+    dit = CausalDiT(cfg).eval()
+    x = torch.randn(1, 6, 32)
+    with torch.no_grad():
+        full, _ = dit(x, (sp, ob))
+        dit.reset_cache()
+        dit(x[:, :4], (sp, ob), use_cache=True)
+        step, cache = dit(x[:, 4:], (sp, ob), use_cache=True)
+    assert full.shape == (1, 4, 2, 2) and cache["layer_1"]["k"].shape[1] == 6
+    torch.testing.assert_close(step, full, rtol=1e-4, atol=1e-5)
+
+    m = create_attention_mask(3)
+    assert m[0, 1] == float("-inf") and m[1, 0] == 0 and not create_attention_mask(2, False).any()
