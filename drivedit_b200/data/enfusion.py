@@ -61,8 +61,8 @@ class EnfusionDatasetConfig:
 class AnchorDetector:
     """Anchor (key) frames: ENFCAP anchor flags when present, else frames where the
     normalised controls change sharply (steering / acceleration jumps) or every
-    ``max_interval`` frames (the reference's EnfusionAnchorDetector,
-    data/enfusion_preprocessing.py:840-900)."""
+    ``max_interval`` frames. The reference's detector, with its own thresholds and API, is
+    :class:`drivedit_b200.data.enfusion_preprocessing.EnfusionAnchorDetector`."""
 
     def __init__(self, steering_threshold: float = 0.3, accel_threshold: float = 0.5,
                  min_interval: int = 4, max_interval: int = 32):
@@ -85,7 +85,6 @@ class AnchorDetector:
         return mask
 
 
-EnfusionAnchorDetector = AnchorDetector
 
 
 class EnfusionSession:
@@ -308,17 +307,60 @@ class EnfusionDataset(Dataset):
 
 
 class EnfusionCollator:
-    """Stacks tensors, keeps lists (scene entities) and metadata as lists."""
+    """Stacks tensors, keeps lists (scene entities) and metadata as lists; scene entities
+    are dropped unless ``include_scene_entities`` (the reference's collator options,
+    data/enfusion_loader.py:616-663; ``pad_to_max`` / ``max_sequence_length`` are
+    accepted for its call sites: samples of one dataset already share their length)."""
+
+    def __init__(self, pad_to_max: bool = True, max_sequence_length: Optional[int] = None,
+                 include_scene_entities: bool = True):
+        self.pad_to_max, self.max_sequence_length = pad_to_max, max_sequence_length
+        self.include_scene_entities = include_scene_entities
 
     def __call__(self, batch: List[Dict[str, Any]]) -> Dict[str, Any]:
         out: Dict[str, Any] = {}
+        if not batch:
+            return out
         for k in batch[0]:
+            if k == "scene_entities" and not self.include_scene_entities:
+                continue
             vals = [b[k] for b in batch if k in b]
             if torch.is_tensor(vals[0]) and len(vals) == len(batch):
                 out[k] = torch.stack(vals)
             else:
                 out[k] = vals
         return out
+
+
+class EnfusionDataLoader:
+    """Batches of an :class:`EnfusionDataset` delivered on ``device`` (CUDA when
+    available): worker processes decode, the collator stacks into pinned memory, and
+    every tensor moves with a non-blocking copy (data/enfusion_loader.py:666-722)."""
+
+    def __init__(self, dataset: "EnfusionDataset", batch_size: int = 8, shuffle: bool = True,
+                 num_workers: int = 4, pin_memory: bool = True, drop_last: bool = True,
+                 prefetch_factor: int = 2, include_scene_entities: bool = False,
+                 device: Optional[Union[str, torch.device]] = None):
+        self.dataset = dataset
+        self.device = torch.device(device) if device is not None else (
+            torch.device("cuda") if torch.cuda.is_available() else None)
+        kw = dict(prefetch_factor=prefetch_factor, persistent_workers=True) if num_workers > 0 else {}
+        pin = pin_memory and self.device is not None and self.device.type == "cuda"
+        self.dataloader = DataLoader(dataset, batch_size=batch_size, shuffle=shuffle,
+                                     num_workers=num_workers, pin_memory=pin, drop_last=drop_last,
+                                     collate_fn=EnfusionCollator(include_scene_entities=include_scene_entities),
+                                     **kw)
+
+    def __iter__(self):
+        for batch in self.dataloader:
+            if self.device is None:
+                yield batch
+                continue
+            yield {k: v.to(self.device, non_blocking=True) if torch.is_tensor(v) else v
+                   for k, v in batch.items()}
+
+    def __len__(self) -> int:
+        return len(self.dataloader)
 
 
 def create_enfusion_dataloaders(data_root, config: Optional[EnfusionDatasetConfig] = None,

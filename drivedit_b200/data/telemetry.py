@@ -20,11 +20,32 @@ from .native import native
 
 @dataclass
 class TelemetryConfig:
+    """Normalisation ranges, the reference's column names and rates, and the session
+    quality thresholds (the reference's ``EnfusionTelemetryConfig`` fields and defaults,
+    data/enfusion_preprocessing.py:20-56, so its configs load). The native parser finds
+    columns by its alias lists; the ``*_col`` names are kept for the reference's code."""
     steering_range: Tuple[float, float] = (-1.0, 1.0)
     throttle_range: Tuple[float, float] = (0.0, 1.0)
     brake_range: Tuple[float, float] = (0.0, 1.0)
     speed_range: Tuple[float, float] = (0.0, 50.0)  # m/s
     speed_unit_kmh: bool = True                      # the `speed` column is km/h
+    timestamp_col: str = "timestamp"
+    position_cols: Tuple[str, str, str] = ("pos_x", "pos_y", "pos_z")
+    rotation_cols: Tuple[str, str, str] = ("rot_pitch", "rot_yaw", "rot_roll")
+    velocity_cols: Tuple[str, str, str] = ("vel_x", "vel_y", "vel_z")
+    throttle_col: str = "throttle"
+    brake_col: str = "brake"
+    steering_col: str = "steering"
+    gear_col: str = "gear"
+    rpm_col: str = "rpm"
+    speed_col: str = "speed"
+    telemetry_rate: float = 5.0       # Hz
+    frame_rate: float = 30.0          # Hz
+    min_speed_variation: float = 0.1  # speed std (m/s) of a "dynamic" session
+    max_stationary_ratio: float = 0.8
+    min_steering_variation: float = 0.01
+    max_position_jump: float = 10.0   # m between rows
+    max_rotation_jump: float = 90.0   # degrees between rows
 
 
 EnfusionTelemetryConfig = TelemetryConfig

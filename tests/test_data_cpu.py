@@ -119,6 +119,14 @@ def test_enfusion_dataset(tmp_path):
     assert b["frames"].shape == (2, 4, 3, 16, 32)
     tr, va = create_enfusion_dataloaders(tmp_path, cfg, batch_size=2, num_workers=0, pin_memory=False)
     assert len(tr.dataset) + len(va.dataset) == len(ds)
+    from drivedit_b200.data.enfusion import EnfusionDataLoader
+    dl = EnfusionDataLoader(ds, batch_size=3, num_workers=0, device="cpu")
+    batches = list(dl)
+    assert len(dl) == len(batches) == len(ds) // 3
+    assert batches[0]["frames"].shape == (3, 4, 3, 16, 32) and "scene_entities" not in batches[0]
+    from drivedit_b200.data.enfusion_preprocessing import EnfusionQualityFilter
+    ranked = EnfusionQualityFilter().filter_sessions(sorted(tmp_path.iterdir()), min_quality=0.0)
+    assert len(ranked) == 2 and ranked[0][1] >= ranked[1][1]
 
 
 def test_transforms_collate_samplers(tmp_path):

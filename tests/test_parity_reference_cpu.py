@@ -306,3 +306,54 @@ def test_flow_trainer_steps(ref):
     torch.manual_seed(20)
     do = ot.distillation_step(teacher_o, batch, oopt)
     assert abs(dr["distillation"] - do["distillation"]) <= 1e-5 * max(1.0, dr["distillation"])
+
+
+def test_enfusion_preprocessing(ref, tmp_path):
+    """Frame, depth, scene, quality and anchor processors against the reference's own
+    (data/enfusion_preprocessing.py) on the same files and telemetry."""
+    import importlib
+    import json
+
+    import cv2
+    import numpy as np
+
+    rp = importlib.import_module("data.enfusion_preprocessing")
+    from drivedit_b200.data import enfusion_preprocessing as op
+
+    rng = np.random.default_rng(0)
+    # frames: PNG files at the target size (no resampling differences between decoders)
+    paths = []
+    for i in range(3):
+        p = tmp_path / f"f{i}.png"
+        cv2.imwrite(str(p), rng.integers(0, 256, (32, 48, 3), dtype=np.uint8))
+        paths.append(p)
+    rf, of = rp.EnfusionFrameProcessor((32, 48)), op.EnfusionFrameProcessor((32, 48))
+    _close(of.load_frames(paths), rf.load_frames(paths), 1e-6)
+    _close(of.load_frame(paths[1]), rf.load_frame(paths[1]), 1e-6)
+    x = of.load_frames(paths)
+    _close(of.denormalize(x), rf.denormalize(x), 1e-6)
+    # depth: an npz in metres, same size
+    d = (rng.random((32, 48)) * 150).astype(np.float32)
+    np.savez(tmp_path / "d.npz", depth=d)
+    rd, od = rp.EnfusionDepthProcessor((32, 48)), op.EnfusionDepthProcessor((32, 48))
+    _close(od.load_depth(tmp_path / "d.npz"), rd.load_depth(tmp_path / "d.npz"))
+    # scene graph
+    scene = {"timestamp": 1.5, "weather": "rain",
+             "entities": [{"id": "a", "class": "car", "position": [1, 2, 3]}, {"id": "b"}]}
+    (tmp_path / "s.json").write_text(json.dumps(scene))
+    assert op.EnfusionSceneParser(1).parse_scene(tmp_path / "s.json") == \
+        rp.EnfusionSceneParser(1).parse_scene(tmp_path / "s.json")
+    # quality score and anchors on synthetic telemetry
+    n = 60
+    tel = {"timestamp": np.linspace(0, 4, n).astype(np.float32),
+           "speed": np.abs(np.sin(np.linspace(0, 3, n)) * 8).astype(np.float32),
+           "steering": np.sin(np.linspace(0, 6, n)).astype(np.float32) * 0.3,
+           "position": np.cumsum(rng.normal(0, 3, (n, 3)), 0).astype(np.float32)}
+    frames = [f"{i}.png" for i in range(70)]
+    q_ref = rp.EnfusionQualityFilter().compute_quality_score(tel, frames)
+    q_our = op.EnfusionQualityFilter().compute_quality_score(tel, frames)
+    assert abs(q_ref - q_our) < 1e-6
+    ctrl = torch.randn(80, 6)
+    assert torch.equal(op.EnfusionAnchorDetector().detect_anchors(ctrl),
+                       rp.EnfusionAnchorDetector().detect_anchors(ctrl))
+    assert set(op.create_enfusion_preprocessors()) == set(rp.create_enfusion_preprocessors())
