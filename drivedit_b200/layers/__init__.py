@@ -1,7 +1,9 @@
 """PyTorch layer library (CPU path and numerical oracle for the sm_100a kernels)."""
-from .attention import (BidirectionalMultiHeadAttention, CausalMultiHeadAttention,
+from .attention import (AttentionBackend, BidirectionalMultiHeadAttention, CausalMultiHeadAttention,
                         CrossAttention, KVCache, MultiHeadAttention, attention_reference,
-                        create_block_causal_mask, create_causal_mask, frame_causal_mask, mha)
+                        create_block_causal_mask, create_causal_mask, frame_causal_mask,
+                        get_attention_backend, get_available_backends, mha,
+                        set_attention_backend)
 from .helpers import (FusedMLP, PositionalEncoding, ScaledDotProductAttention,
                       apply_rotary_pos_emb, fused_add_norm, gelu_tanh, silu)
 from .mlp import GeGLU, MLP, ConditionalMLP, SwiGLU, create_mlp, pack_swiglu, unpack_swiglu

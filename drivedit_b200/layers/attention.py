@@ -9,8 +9,9 @@ output-projection std 0.02/sqrt(24) (:284-378), causal / bidirectional variants
 Differences, chosen on purpose:
   * the reference has several global "backends" (flash_attn / SDPA / einsum) selected at
     import time (:24-81) and crashes when flash_attn is importable but tensors are on
-    the CPU. Here there is one CPU/oracle path (PyTorch SDPA or einsum) and one CUDA
-    path (the sm_100a kernels in ``drivedit_b200.ops.attention``), chosen by device.
+    the CPU. Here there is one path per device (PyTorch SDPA in modules, the sm_100a
+    kernels in ``drivedit_b200.ops.attention`` in the fused engine); the backend API is
+    kept, and its one real choice is the fp32 einsum oracle (``AttentionBackend.EINSUM``).
   * the reference drops the causal mask whenever a KV cache is passed (:406-408), so a
     multi-token step attends to its own future; here the mask always covers the new
     tokens (offset by the cache length).
@@ -22,6 +23,8 @@ Differences, chosen on purpose:
 from __future__ import annotations
 
 import math
+import warnings
+from enum import Enum
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -67,6 +70,40 @@ def attention_reference(q, k, v, mask: Optional[torch.Tensor] = None,
     return (o, lse) if return_lse else o
 
 
+class AttentionBackend(Enum):
+    """The reference's backend names (layers/mha.py:24-28) plus this framework's own.
+    There is no dispatch between libraries: ``SM100`` (the default) is PyTorch SDPA for
+    module-level attention and this framework's tcgen05 kernels in the fused engine;
+    ``EINSUM`` makes :func:`mha` compute the fp32 einsum oracle instead (for numerical
+    comparisons). The flash-attention names are never available."""
+    SM100 = "sm100"
+    FLASH_ATTN_3 = "flash_attn_3"
+    FLASH_ATTN_2 = "flash_attn_2"
+    EINSUM = "einsum"
+
+
+_BACKEND = AttentionBackend.SM100
+
+
+def get_available_backends() -> list:
+    return [AttentionBackend.SM100, AttentionBackend.EINSUM]
+
+
+def get_attention_backend() -> AttentionBackend:
+    return _BACKEND
+
+
+def set_attention_backend(backend: AttentionBackend) -> bool:
+    """Select the backend; an unavailable one warns and returns False (the reference's
+    behaviour, layers/mha.py:73-81)."""
+    global _BACKEND
+    if backend not in get_available_backends():
+        warnings.warn(f"Backend {backend} not available. Available: {get_available_backends()}")
+        return False
+    _BACKEND = backend
+    return True
+
+
 def mha(q, k, v, mask: Optional[torch.Tensor] = None, dropout_p: float = 0.0,
         training: bool = False, causal: bool = False) -> torch.Tensor:
     """Reference-compatible scaled dot-product attention on ``[B, T, H, D]``.
@@ -74,6 +111,13 @@ def mha(q, k, v, mask: Optional[torch.Tensor] = None, dropout_p: float = 0.0,
     ``mask`` follows the reference: 0 = blocked (any dtype) or a bool tensor."""
     if mask is not None and mask.dtype != torch.bool:
         mask = mask != 0
+    if _BACKEND is AttentionBackend.EINSUM:
+        if causal and mask is None:
+            mask = create_causal_mask(q.shape[1], q.device, k.shape[1])
+        o = attention_reference(q, k, v, mask)
+        if training and dropout_p > 0:
+            o = F.dropout(o, dropout_p)
+        return o.to(q.dtype)
     qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
     o = F.scaled_dot_product_attention(
         qt, kt, vt, attn_mask=mask, dropout_p=dropout_p if training else 0.0,

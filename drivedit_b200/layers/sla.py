@@ -166,6 +166,33 @@ def classify_blocks_reference(q, k, cfg: SLAConfig):
     return crit, marg, negl
 
 
+def classify_blocks(q, k, config: SLAConfig, mask: Optional[torch.Tensor] = None):
+    """The reference's name and signature for :func:`classify_blocks_reference`
+    (its ``mask`` argument is accepted and, as there, unused)."""
+    return classify_blocks_reference(q, k, config)
+
+
+@dataclass
+class SLAStats:
+    """Block counts of one classification (layers/sla.py:36-43): ``critical_ratio`` =
+    critical / total, ``compute_savings`` = 1 - (critical + marginal / block_size) /
+    total, the share of exact-softmax work a classification avoids when a marginal block
+    costs 1/block_size of a critical one (linear attention against quadratic)."""
+    critical_blocks: int
+    marginal_blocks: int
+    negligible_blocks: int
+    total_blocks: int
+    critical_ratio: float
+    compute_savings: float
+
+    @classmethod
+    def from_masks(cls, critical: torch.Tensor, marginal: torch.Tensor, negligible: torch.Tensor,
+                   block_size: int = 64) -> "SLAStats":
+        c, m, n = int(critical.sum()), int(marginal.sum()), int(negligible.sum())
+        tot = max(c + m + n, 1)
+        return cls(c, m, n, c + m + n, c / tot, 1.0 - (c + m / block_size) / tot)
+
+
 def sla_reference(q, k, v, cfg: SLAConfig) -> torch.Tensor:
     """The reference's SLA output (layers/sla.py:140-247), vectorised over block pairs."""
     B, T, H, D = q.shape

@@ -76,3 +76,30 @@ def test_ddim_sample_equals_euler_at_eta_zero_and_is_exact_on_straight_paths():
     out = s.sample(x0, 5)
     assert out["trajectory"].shape == (6, 4, 8) and torch.allclose(out["final_sample"], x1, atol=1e-5)
     assert torch.allclose(s.ddim_sample(x1, 5), x0, atol=1e-5)
+
+
+def test_attention_backend_api_and_sla_stats():
+    import warnings
+
+    from drivedit_b200.layers.attention import (AttentionBackend, attention_reference,
+                                                get_attention_backend, mha, set_attention_backend)
+    from drivedit_b200.layers.sla import SLAConfig, SLAStats, classify_blocks
+
+    torch.manual_seed(0)
+    q, k, v = (torch.randn(2, 12, 2, 8) for _ in range(3))
+    assert get_attention_backend() is AttentionBackend.SM100
+    with warnings.catch_warnings(record=True) as w:
+        warnings.simplefilter("always")
+        assert set_attention_backend(AttentionBackend.FLASH_ATTN_3) is False and w
+    try:
+        assert set_attention_backend(AttentionBackend.EINSUM)
+        torch.testing.assert_close(mha(q, k, v, causal=True),
+                                   attention_reference(q, k, v, torch.ones(12, 12).tril().bool()))
+    finally:
+        set_attention_backend(AttentionBackend.SM100)
+    torch.testing.assert_close(mha(q, k, v), attention_reference(q, k, v), rtol=1e-4, atol=1e-5)
+    c, m, n = classify_blocks(torch.randn(1, 256, 2, 32), torch.randn(1, 256, 2, 32),
+                              SLAConfig(block_size=64, causal=True))
+    st = SLAStats.from_masks(c, m, n, 64)
+    assert st.total_blocks == 2 * 16 and st.critical_blocks + st.marginal_blocks + st.negligible_blocks == 32
+    assert 0.0 <= st.compute_savings <= 1.0
