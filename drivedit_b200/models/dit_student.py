@@ -206,15 +206,21 @@ class DiTTeacher(nn.Module):
 
     def __init__(self, latent_dim: int = 8, d_model: int = 1024, n_layers: int = 24,
                  n_heads: int = 16, d_ff: Optional[int] = None, mlp_type: str = "swiglu",
-                 max_seq_len: int = 2048, num_steps: int = 4, time_scale: float = 1000.0):
+                 dropout: float = 0.0, max_seq_len: int = 2048, time_embed_dim: int = 256,
+                 use_rope: bool = True, bias: bool = False, num_diffusion_steps: int = 1000,
+                 num_steps: int = 4, time_scale: float = 1000.0):
+        """The reference's constructor arguments (models/dit_teacher.py:126-140);
+        ``time_embed_dim`` is the number of Fourier features of the time embedding,
+        ``num_diffusion_steps`` the scale of integer timesteps (``t / steps`` in [0, 1])."""
         super().__init__()
         self.latent_dim, self.num_steps = latent_dim, num_steps
+        self.num_diffusion_steps = num_diffusion_steps
         self.input_proj = nn.Linear(latent_dim, d_model)
         self.pos_embed = PositionalEncoding(d_model, max_seq_len)
-        self.time_embed = FlowTimestepEmbedding(d_model, time_scale=time_scale)
+        self.time_embed = FlowTimestepEmbedding(d_model, time_embed_dim, time_scale=time_scale)
         self.blocks = nn.ModuleList([
-            DiTBlock(d_model, n_heads, d_ff, mlp_type, causal=False, max_seq_len=max_seq_len,
-                     cond_dim=d_model) for _ in range(n_layers)])
+            DiTBlock(d_model, n_heads, d_ff, mlp_type, dropout, causal=False, use_rope=use_rope,
+                     max_seq_len=max_seq_len, cond_dim=d_model, bias=bias) for _ in range(n_layers)])
         self.norm = RMSNorm(d_model)
         self.out_proj = nn.Linear(d_model, latent_dim)
         nn.init.zeros_(self.out_proj.weight)
@@ -223,6 +229,8 @@ class DiTTeacher(nn.Module):
     def forward(self, z_t: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
         if t.dim() == 0:
             t = t.expand(z_t.shape[0])
+        if not t.is_floating_point():  # integer diffusion timesteps
+            t = t.float() / self.num_diffusion_steps
         cond = F.silu(self.time_embed(t))
         x = self.pos_embed(self.input_proj(z_t))
         for blk in self.blocks:

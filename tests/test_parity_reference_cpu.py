@@ -357,3 +357,20 @@ def test_enfusion_preprocessing(ref, tmp_path):
     assert torch.equal(op.EnfusionAnchorDetector().detect_anchors(ctrl),
                        rp.EnfusionAnchorDetector().detect_anchors(ctrl))
     assert set(op.create_enfusion_preprocessors()) == set(rp.create_enfusion_preprocessors())
+
+
+@pytest.mark.parametrize("use_memory", [False, True])
+def test_dit_student_forward(ref, use_memory):
+    """The reference's causal student loads by name and gives the same outputs, also on
+    a second call (after the memory bank has been written)."""
+    import importlib
+    from drivedit_b200.models.dit_student import DiTStudent
+    rs = importlib.import_module("models.dit_student")
+    torch.manual_seed(0)
+    kw = dict(latent_dim=8, d_model=64, n_layers=2, n_heads=4, max_seq_len=64,
+              use_memory=use_memory, memory_size=32)
+    r, o = rs.DiTStudent(**kw).eval(), DiTStudent(**kw).eval()
+    o.load_state_dict(r.state_dict(), strict=False)
+    x = torch.randn(2, 16, 8)
+    for _ in range(2):
+        _close(o(x)[0], r(x)[0], 1e-5)
