@@ -374,3 +374,51 @@ def test_dit_student_forward(ref, use_memory):
     x = torch.randn(2, 16, 8)
     for _ in range(2):
         _close(o(x)[0], r(x)[0], 1e-5)
+
+
+def test_fused_ops_api(ref, monkeypatch):
+    """The reference's fused-op functions and modules (their PyTorch statements, which
+    define the semantics) against this framework's on the same inputs and weights."""
+    import importlib
+    fo = importlib.import_module("layers.kernels.fused_ops")
+    fn = importlib.import_module("training.kernels.fused_normalize")
+    fa = importlib.import_module("training.kernels.fused_augment")
+    monkeypatch.setattr(fo, "FUSED_OPS_AVAILABLE", False)   # no Triton on CPU tensors
+    from drivedit_b200.layers import fused_ops as ofo
+    from drivedit_b200.training import fused_kernels as ofk
+    torch.manual_seed(0)
+    x, r, g = torch.randn(3, 2, 10, 64).unbind(0)
+    w = torch.rand(64) + 0.5
+    _close(ofo.fused_rmsnorm(x, w), fo.fused_rmsnorm(x, w))
+    _close(ofo.fused_silu_multiply(x, g), fo.fused_silu_multiply(x, g))
+    _close(ofo.fused_add_rmsnorm(x, r, w), fo.fused_add_rmsnorm(x, r, w))
+    q, k = torch.randn(2, 2, 10, 4, 16).unbind(0)
+    ang = torch.rand(10, 8) * 6
+    for a, b in zip(ofo.fused_rotary_embedding(q, k, ang.cos(), ang.sin()),
+                    fo.fused_rotary_embedding(q, k, ang.cos(), ang.sin())):
+        _close(a, b)
+    rm, om = fo.FusedSiLUMLP(64, 96), ofo.FusedSiLUMLP(64, 96)
+    om.load_state_dict(rm.state_dict())
+    _close(om(x), rm(x))
+    rn, on = fo.FusedRMSNorm(64), ofo.FusedRMSNorm(64)
+    on.load_state_dict(rn.state_dict())
+    _close(on(x), rn(x))
+    for affine in (True, False):
+        rn, on = fn.FusedNormalize(64, affine=affine), ofk.FusedNormalize(64, affine=affine)
+        if affine:
+            with torch.no_grad():
+                rn.weight.normal_(1, 0.1), rn.bias.normal_(0, 0.1)
+        on.load_state_dict(rn.state_dict())
+        _close(on(x), rn(x))
+    _close(ofk.fused_normalize_kernel(x), fn.fused_normalize_kernel(x))
+    img = torch.rand(4, 3, 8, 12)
+    flip = torch.tensor([True, False, True, False])
+    bright, contr = torch.rand(4) * 0.2 - 0.1, torch.rand(4) * 0.2 + 0.9
+    _close(ofk.fused_augment_kernel(img, flip, bright, contr), fa._torch_augment(img, flip, bright, contr))
+    ra, oa = fa.FusedAugmentation(normalize=True), ofk.FusedAugmentation(normalize=True)
+    _close(oa(img, deterministic=True), ra(img, deterministic=True))
+    vid = torch.rand(2, 3, 3, 8, 12)
+    y = ofk.FusedAugmentation()(vid, deterministic=True, flip_override=torch.tensor([True, False]))
+    _close(y[0], vid[0].flip(-1))      # one flip decision per clip, every frame
+    _close(y[1], vid[1])
+    assert ofk.VideoAugmentation()(vid).shape == vid.shape
