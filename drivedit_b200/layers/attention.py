@@ -40,10 +40,13 @@ def create_causal_mask(T: int, device=None, S: Optional[int] = None) -> torch.Te
     return (k <= q)[None, None]
 
 
-def create_block_causal_mask(T: int, block_size: int, device=None) -> torch.Tensor:
-    """Block-causal: token i sees token j when ``j // block <= i // block``."""
-    idx = torch.arange(T, device=device) // block_size
-    return (idx[None, :] <= idx[:, None])[None, None]
+def create_block_causal_mask(block_size: int, num_blocks: int, device=None) -> torch.Tensor:
+    """``[1, 1, L, L]`` float mask (1 = attend) over ``L = block_size * num_blocks``
+    tokens, the reference's block-causal mask (layers/mha.py:249-281): every earlier
+    block in full and the current block causally, which is token-causal attention. The
+    block-bidirectional mask (a whole block sees itself) is :func:`frame_causal_mask`."""
+    L = block_size * num_blocks
+    return create_causal_mask(L, device).float()
 
 
 def frame_causal_mask(T: int, tokens_per_frame: int, S: Optional[int] = None,
@@ -257,10 +260,17 @@ class CrossAttention(nn.Module):
         self.proj = nn.Linear(d_model, d_model, bias=bias)
         nn.init.zeros_(self.proj.weight)
 
-    def forward(self, x, context, context_mask: Optional[torch.Tensor] = None):
-        B, T, D = x.shape
-        S = context.shape[1]
-        q = self.q(x).view(B, T, self.n_heads, self.d_head)
+    def project_context(self, context: torch.Tensor) -> Dict[str, torch.Tensor]:
+        """The context's keys and values ``{"k", "v"}`` ``[B, S, H, d_head]``."""
+        B, S = context.shape[:2]
         k, v = self.kv(context).view(B, S, 2, self.n_heads, self.d_head).unbind(2)
+        return {"k": k, "v": v}
+
+    def attend(self, x, kv: Dict[str, torch.Tensor], context_mask: Optional[torch.Tensor] = None):
+        B, T, D = x.shape
+        q = self.q(x).view(B, T, self.n_heads, self.d_head)
         m = None if context_mask is None else context_mask[:, None, None, :].bool()
-        return self.proj(mha(q, k, v, mask=m).reshape(B, T, D))
+        return self.proj(mha(q, kv["k"], kv["v"], mask=m).reshape(B, T, D))
+
+    def forward(self, x, context, context_mask: Optional[torch.Tensor] = None):
+        return self.attend(x, self.project_context(context), context_mask)

@@ -125,17 +125,18 @@ def routing_metrics(probs, weights, experts, counts, num_experts) -> MoEMetrics:
 class ExpertFFN(nn.Module):
     """One SwiGLU expert (reference names ``w_gate``, ``w_value``, ``w_out``)."""
 
-    def __init__(self, d_model: int, d_expert: int, bias: bool = False):
+    def __init__(self, d_model: int, d_expert: int, dropout: float = 0.0, bias: bool = False):
         super().__init__()
         self.w_gate = nn.Linear(d_model, d_expert, bias=bias)
         self.w_value = nn.Linear(d_model, d_expert, bias=bias)
         self.w_out = nn.Linear(d_expert, d_model, bias=bias)
+        self.dropout = nn.Dropout(dropout) if dropout > 0 else nn.Identity()
         nn.init.normal_(self.w_gate.weight, std=0.02)
         nn.init.normal_(self.w_value.weight, std=0.02)
         nn.init.normal_(self.w_out.weight, std=0.02 / math.sqrt(2))
 
     def forward(self, x):
-        return self.w_out(F.silu(self.w_gate(x)) * self.w_value(x))
+        return self.w_out(self.dropout(F.silu(self.w_gate(x)) * self.w_value(x)))
 
 
 class MoEFFN(nn.Module):

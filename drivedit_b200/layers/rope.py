@@ -36,10 +36,12 @@ def rope_angles_1d(dim: int, positions: torch.Tensor, base: float = 10000.0) -> 
     return torch.outer(positions.to(torch.float64), inv_freqs(dim, base, positions.device))
 
 
-def compute_rope_freqs(dim: int, max_seq_len: int, base: float = 10000.0, device=None):
-    """(sin, cos) ``[max_seq_len, dim/2]`` — the reference's return order."""
+def compute_rope_freqs(dim: int, max_seq_len: int, base: float = 10000.0, device=None,
+                       dtype: torch.dtype = torch.float32):
+    """(sin, cos) ``[max_seq_len, dim/2]`` — the reference's return order; angles in
+    float64, tables in ``dtype``."""
     ang = rope_angles_1d(dim, torch.arange(max_seq_len, device=device), base)
-    return ang.sin().float(), ang.cos().float()
+    return ang.sin().to(dtype), ang.cos().to(dtype)
 
 
 def ntk_base(base: float, dim: int, alpha: float) -> float:
@@ -47,17 +49,18 @@ def ntk_base(base: float, dim: int, alpha: float) -> float:
     return base * alpha ** (dim / (dim - 2)) if alpha != 1.0 else base
 
 
-def compute_ntk_rope_freqs(dim, max_seq_len, base=10000.0, alpha=1.0, device=None):
-    return compute_rope_freqs(dim, max_seq_len, ntk_base(base, dim, alpha), device)
+def compute_ntk_rope_freqs(dim, max_seq_len, base=10000.0, alpha=1.0, device=None,
+                           dtype: torch.dtype = torch.float32):
+    return compute_rope_freqs(dim, max_seq_len, ntk_base(base, dim, alpha), device, dtype)
 
 
 def compute_dynamic_ntk_rope_freqs(dim, seq_len, original_max_len, base=10000.0,
-                                   ntk_factor=1.0, device=None):
+                                   ntk_factor=1.0, device=None, dtype: torch.dtype = torch.float32):
     """Standard RoPE up to the training length; past it, alpha grows with the ratio."""
     if seq_len <= original_max_len:
-        return compute_rope_freqs(dim, seq_len, base, device)
+        return compute_rope_freqs(dim, seq_len, base, device, dtype)
     alpha = ntk_factor * seq_len / original_max_len - (ntk_factor - 1)
-    return compute_ntk_rope_freqs(dim, seq_len, base, alpha, device)
+    return compute_ntk_rope_freqs(dim, seq_len, base, alpha, device, dtype)
 
 
 def yarn_inv_freqs(dim, max_seq_len, original_max_len, base=10000.0, beta_fast=32.0,
@@ -78,11 +81,14 @@ def yarn_inv_freqs(dim, max_seq_len, original_max_len, base=10000.0, beta_fast=3
 
 
 def compute_yarn_rope_freqs(dim, max_seq_len, original_max_len, base=10000.0,
-                            beta_fast=32.0, beta_slow=1.0, device=None):
-    inv, mscale = yarn_inv_freqs(dim, max_seq_len, original_max_len, base, beta_fast,
-                                 beta_slow, device)
+                            beta_fast=32.0, beta_slow=1.0, mscale: float = 0.0, device=None,
+                            dtype: torch.dtype = torch.float32):
+    """(sin, cos, attention scale); ``mscale > 0`` overrides the automatic scale
+    ``0.1 ln(s) + 1``."""
+    inv, auto = yarn_inv_freqs(dim, max_seq_len, original_max_len, base, beta_fast,
+                               beta_slow, device)
     ang = torch.outer(torch.arange(max_seq_len, dtype=torch.float64, device=device), inv)
-    return ang.sin().float(), ang.cos().float(), mscale
+    return ang.sin().to(dtype), ang.cos().to(dtype), (mscale if mscale > 0 else auto)
 
 
 def interpolate_positions(seq_len: int, train_len: int, device=None) -> torch.Tensor:

@@ -37,16 +37,24 @@ from .attention import attention_reference
 
 @dataclass
 class SLAConfig:
+    """The reference's fields in its order (layers/sla.py:23-32; ``flash_attention`` and
+    ``linear_feature_dim`` are accepted, the exact branch always runs on this framework's
+    attention kernels and the feature map is elu + 1), then this framework's: the
+    routing ``mode`` (``topk``: a fixed share of key blocks per query block, or
+    ``reference``: the threshold classification), its share and diagonal rule, the
+    frame size of frame-causal routing and the linear branch's epsilon."""
     block_size: int = 64
-    mode: str = "topk"               # "topk" | "reference"
-    topk_frac: float = 0.125
-    always_diag: bool = True
     critical_threshold: float = 0.5  # reference mode
     negligible_threshold: float = 0.01
     causal: bool = False             # token-causal (reference mode) / block-causal
-    tokens_per_frame: Optional[int] = None  # frame-causal when set (topk mode)
+    flash_attention: bool = True
     use_elu_feature: bool = True
+    linear_feature_dim: int = 64
     temperature: float = 1.0
+    mode: str = "topk"               # "topk" | "reference"
+    topk_frac: float = 0.125
+    always_diag: bool = True
+    tokens_per_frame: Optional[int] = None  # frame-causal when set (topk mode)
     eps: float = 1e-6
 
 

@@ -67,20 +67,39 @@ class DiTBlock(nn.Module):
 
 
 class DiTBlockWithCrossAttention(DiTBlock):
-    def __init__(self, d_model: int, n_heads: int, context_dim: Optional[int] = None, **kw):
-        super().__init__(d_model, n_heads, **kw)
-        self.norm_cross = RMSNorm(d_model)
-        self.cross_attn = CrossAttention(d_model, n_heads, context_dim)
+    """:class:`DiTBlock` plus attention from the tokens to a projected ``context``
+    between the self-attention and the MLP, normalised by ``norm_cross`` (AdaLN when
+    ``cond_dim`` is set). The reference's constructor and call (blocks/dit_block.py:
+    143-246); its forward returns ``(x, kv_cache, cross_kv_cache)``, where the cross cache
+    holds the context's projected keys and values, so a streaming caller projects a
+    fixed context once."""
 
-    def forward(self, x, context: Optional[torch.Tensor] = None, kv_cache=None, pos=None,
-                cond=None, causal_mask=None, start_pos=None, context_mask=None):
+    def __init__(self, d_model: int, n_heads: int, d_ff: Optional[int] = None,
+                 mlp_type: str = "swiglu", dropout: float = 0.0, causal: bool = True,
+                 use_rope: bool = True, max_seq_len: int = 2048, cond_dim: Optional[int] = None,
+                 bias: bool = False, context_dim: Optional[int] = None,
+                 tokens_per_frame: Optional[int] = None):
+        super().__init__(d_model, n_heads, d_ff, mlp_type, dropout, causal, use_rope, max_seq_len,
+                         cond_dim, bias, tokens_per_frame)
+        self.norm_cross = AdaLN(d_model, cond_dim) if cond_dim is not None else RMSNorm(d_model)
+        self.cross_attn = CrossAttention(d_model, n_heads, context_dim, bias=bias)
+
+    def forward(self, x, context: Optional[torch.Tensor] = None, kv_cache=None,
+                cross_kv_cache: Optional[Dict[str, torch.Tensor]] = None, pos=None, cond=None,
+                causal_mask=None, start_pos=None, context_mask=None):
         h = self._norm(self.norm_attn, x, cond)
-        a, new_cache = self.attn(h, kv_cache=kv_cache, start_pos=start_pos)
+        if causal_mask is not None:
+            a, new_cache = MultiHeadAttention.forward(self.attn, h, kv_cache, causal_mask, start_pos)
+        else:
+            a, new_cache = self.attn(h, kv_cache=kv_cache, start_pos=start_pos)
         x = x + a
-        if context is not None:
-            x = x + self.cross_attn(self.norm_cross(x), context, context_mask)
+        new_cross = cross_kv_cache
+        if context is not None or cross_kv_cache is not None:
+            if new_cross is None:
+                new_cross = self.cross_attn.project_context(context)
+            x = x + self.cross_attn.attend(self._norm(self.norm_cross, x, cond), new_cross, context_mask)
         x = x + self.mlp(self._norm(self.norm_mlp, x, cond))
-        return x, new_cache
+        return x, new_cache, new_cross
 
 
 class MemoryEfficientDiTBlock(DiTBlock):
@@ -145,9 +164,15 @@ def create_moe_dit_block(d_model: int, n_heads: int, num_experts: int = 8, top_k
     return MoEDiTBlock(d_model, n_heads, num_experts=num_experts, top_k=top_k, **kw)
 
 
-def create_dit_block(block_type: str = "standard", **kw) -> nn.Module:
-    return {"standard": DiTBlock, "cross_attention": DiTBlockWithCrossAttention,
-            "memory_efficient": MemoryEfficientDiTBlock, "moe": MoEDiTBlock}[block_type](**kw)
+def create_dit_block(d_model: int, n_heads: int, block_type: str = "standard", **kwargs) -> nn.Module:
+    """``standard``, ``cross_attn`` (also ``cross_attention``), ``memory_efficient`` or
+    ``moe`` (blocks/dit_block.py:310-335)."""
+    kinds = {"standard": DiTBlock, "cross_attn": DiTBlockWithCrossAttention,
+             "cross_attention": DiTBlockWithCrossAttention,
+             "memory_efficient": MemoryEfficientDiTBlock, "moe": MoEDiTBlock}
+    if block_type not in kinds:
+        raise ValueError(f"Unsupported block type: {block_type}")
+    return kinds[block_type](d_model, n_heads, **kwargs)
 
 
 # ----------------------------------------------------------------------------- flow matching

@@ -65,8 +65,22 @@ def smoothing_kernel(size: int, smoothing_type: str = "gaussian") -> torch.Tenso
     return k / k.sum()
 
 
-def finite_difference_gradient(x: torch.Tensor, dim: int = -1, spacing: float = 1.0, order: int = 1) -> torch.Tensor:
-    """Central differences inside, one-sided at the ends (``torch.gradient``)."""
+def finite_difference_gradient(x: torch.Tensor, spacing: float = 1.0,
+                               edge_order: int = 1) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Spatial gradients ``(d/dy, d/dx)`` over the last two dims of ``x [..., H, W]``
+    (utils/math_utils.py:194-231): central differences inside and one-sided ones at the
+    borders with ``edge_order=1``; periodic central differences (wrapping at the
+    borders) otherwise."""
+    if edge_order == 1:
+        gy, gx = torch.gradient(x, spacing=spacing, dim=(-2, -1), edge_order=1)
+        return gy, gx
+    return ((x.roll(-1, -2) - x.roll(1, -2)) / (2 * spacing),
+            (x.roll(-1, -1) - x.roll(1, -1)) / (2 * spacing))
+
+
+def gradient_along(x: torch.Tensor, dim: int = -1, spacing: float = 1.0, order: int = 1) -> torch.Tensor:
+    """``order``-th derivative along one dim: central differences inside, one-sided at
+    the ends (``torch.gradient`` applied ``order`` times)."""
     g = x
     for _ in range(order):
         g = torch.gradient(g, spacing=spacing, dim=dim)[0]

@@ -100,7 +100,9 @@ def load_checkpoint(filepath: str, model: nn.Module, optimizer=None, scheduler=N
 
 
 @torch.no_grad()
-def exponential_moving_average(ema_model: nn.Module, model: nn.Module, decay: float = 0.999) -> None:
+def exponential_moving_average(model: nn.Module, ema_model: nn.Module, decay: float = 0.999) -> None:
+    """``ema <- decay * ema + (1 - decay) * model`` for every parameter (the reference's
+    argument order, utils/model_utils.py:241-258: the live model first)."""
     ep, mp = list(ema_model.parameters()), list(model.parameters())
     torch._foreach_lerp_(ep, [p.detach() for p in mp], 1 - decay)
 

@@ -42,8 +42,13 @@ def test_block_variants():
     y, _ = b(x, cond=torch.randn(2, 16))
     assert y.shape == x.shape
     c = DiTBlockWithCrossAttention(32, 4, context_dim=24)
-    y, _ = c(x, context=torch.randn(2, 5, 24))
-    assert y.shape == x.shape
+    ctx = torch.randn(2, 5, 24)
+    y, _, cross = c(x, context=ctx)
+    assert y.shape == x.shape and cross["k"].shape == (2, 5, 4, 8)
+    y2, _, _ = c(x, cross_kv_cache=cross)          # projected context reused
+    torch.testing.assert_close(y2, y)
+    from drivedit_b200.models.blocks import create_dit_block
+    assert isinstance(create_dit_block(32, 4, "cross_attn", context_dim=24), DiTBlockWithCrossAttention)
     m = MemoryEfficientDiTBlock(32, 4).train()
     xr = x.clone().requires_grad_(True)
     m(xr)[0].sum().backward()

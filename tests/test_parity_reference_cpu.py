@@ -422,3 +422,36 @@ def test_fused_ops_api(ref, monkeypatch):
     _close(y[0], vid[0].flip(-1))      # one flip decision per clip, every frame
     _close(y[1], vid[1])
     assert ofk.VideoAugmentation()(vid).shape == vid.shape
+
+
+def test_utility_signatures_and_semantics(ref):
+    """Helpers whose argument order or meaning a caller relies on: EMA (live model
+    first), spatial finite differences, the block-causal mask, the expert FFN and the
+    block factory, called positionally as the reference's callers do."""
+    import copy
+    import importlib
+    mu = importlib.import_module("utils.model_utils")
+    ma = importlib.import_module("utils.math_utils")
+    from drivedit_b200.layers.attention import create_block_causal_mask
+    from drivedit_b200.layers.moe import ExpertFFN
+    from drivedit_b200.models.blocks import DiTBlock, create_dit_block
+    from drivedit_b200.utils.math_utils import finite_difference_gradient
+    from drivedit_b200.utils.model_utils import exponential_moving_average
+    torch.manual_seed(0)
+    model = torch.nn.Linear(4, 4)
+    ema_r, ema_o = copy.deepcopy(model), copy.deepcopy(model)
+    with torch.no_grad():
+        model.weight.add_(1.0)
+    mu.exponential_moving_average(model, ema_r, 0.9)
+    exponential_moving_average(model, ema_o, 0.9)
+    _close(ema_o.weight, ema_r.weight)
+    x = torch.randn(2, 3, 7, 9)
+    for edge in (1, 2):
+        for a, b in zip(finite_difference_gradient(x, 0.5, edge), ma.finite_difference_gradient(x, 0.5, edge)):
+            _close(a, b)
+    assert torch.equal(create_block_causal_mask(4, 3, None), ref["layers.mha"].create_block_causal_mask(4, 3, "cpu"))
+    r, o = ref["layers.moe"].ExpertFFN(32, 48, 0.0, False), ExpertFFN(32, 48, 0.0, False)
+    o.load_state_dict(r.state_dict())
+    h = torch.randn(5, 32)
+    _close(o(h), r(h))
+    assert isinstance(create_dit_block(64, 4, "standard", d_ff=128), DiTBlock)
