@@ -149,10 +149,23 @@ class GraphedModule(nn.Module):
 
 
 class ModelCompiler:
-    """Captures models / sub-modules into CUDA graphs (see :class:`GraphedModule`)."""
+    """Captures models / sub-modules into CUDA graphs (see :class:`GraphedModule`).
 
-    def __init__(self, config: Optional[OptimizationConfig] = None):
-        self.config = config or OptimizationConfig()
+    Takes the reference's arguments (``mode, dynamic, fullgraph, backend,
+    disable_cudagraphs``, inference/optimization.py:210-235) or an
+    :class:`OptimizationConfig` as its first argument. ``dynamic``, ``fullgraph`` and
+    ``backend`` are recorded only (there is no tracing compiler); ``disable_cudagraphs``
+    makes :meth:`compile` return the model unchanged."""
+
+    def __init__(self, mode=CompileMode.REDUCE_OVERHEAD, dynamic: bool = False, fullgraph: bool = False,
+                 backend: str = "inductor", disable_cudagraphs: bool = False,
+                 config: Optional[OptimizationConfig] = None):
+        if isinstance(mode, OptimizationConfig):
+            config, mode = mode, mode.compile_mode
+        self.config = config or OptimizationConfig(compile_mode=mode, compile_dynamic=dynamic,
+                                                   compile_fullgraph=fullgraph)
+        self.mode, self.dynamic, self.fullgraph = self.config.compile_mode, dynamic, fullgraph
+        self.backend, self.disable_cudagraphs = backend, disable_cudagraphs
         self._compiled: Dict[int, nn.Module] = {}
         self._warm: set = set()
         self._errors: Dict[int, Exception] = {}
@@ -160,7 +173,8 @@ class ModelCompiler:
     def compile(self, model: nn.Module, example_inputs: Optional[Sequence[torch.Tensor]] = None,
                 mode: Optional[CompileMode] = None) -> nn.Module:
         mode = mode or self.config.compile_mode
-        if mode == CompileMode.NONE or example_inputs is None or not torch.cuda.is_available():
+        if (mode == CompileMode.NONE or self.disable_cudagraphs or example_inputs is None
+                or not torch.cuda.is_available()):
             return model
         if isinstance(example_inputs, torch.Tensor):
             example_inputs = (example_inputs,)
@@ -318,11 +332,14 @@ class InferenceOptimizer:
 
 @dataclass
 class FrameMetrics:
+    """Per generated frame (the reference's fields, inference/optimization.py:821-827,
+    plus whether the frame met the latency budget)."""
     frame_idx: int
     generation_time_ms: float
     total_latency_ms: float
     memory_mb: float
-    meets_deadline: bool
+    kv_cache_length: int = 0
+    meets_deadline: bool = True
 
 
 class StreamingInference:
@@ -367,14 +384,16 @@ class StreamingInference:
         self._is_streaming = True
         Fc = context.shape[1]
         t0 = time.perf_counter()
-        res = self._rollout(Fc + num_frames).run(context.to(self.device), controls.to(self.device), Fc + num_frames)
+        ro = self._rollout(Fc + num_frames)
+        res = ro.run(context.to(self.device), controls.to(self.device), Fc + num_frames)
         per_frame = [ms / self.config.chunk_size for ms in res.chunk_ms for _ in range(self.config.chunk_size)]
         for i in range(num_frames):
             gen_ms = per_frame[i] if i < len(per_frame) else 0.0
             self._latency_history.append(gen_ms)
             m = FrameMetrics(Fc + i, gen_ms, (time.perf_counter() - t0) * 1000,
                              torch.cuda.memory_allocated(self.device) / 1e6 if self.device.type == "cuda" else 0.0,
-                             gen_ms <= self._frame_deadline_ms)
+                             kv_cache_length=min(Fc + i, ro.cfg.window_frames),  # frames in the KV window
+                             meets_deadline=gen_ms <= self._frame_deadline_ms)
             self.frame_metrics.append(m)
             frame = res.frames[:, Fc + i]
             self.frame_buffer.append(frame)

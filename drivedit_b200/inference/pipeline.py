@@ -29,12 +29,21 @@ from .rollout import StreamingRollout
 
 @dataclass
 class PipelineConfig:
+    """The reference's fields in its order (inference/pipeline.py:23-34), then this
+    framework's settings. Of the reference's, ``max_sequence_length``, ``context_window``,
+    ``temperature`` and ``cache_models`` are accepted and recorded only: the number of
+    frames is the ``num_frames`` of each call, the KV window is ``window_frames``,
+    sampling is the deterministic flow ODE and the models stay resident."""
     model_path: Optional[str] = None
     vae_path: Optional[str] = None
     device: str = "cuda"
     batch_size: int = 1
-    use_torch_compile: bool = False       # accepted for API parity; kernels are fused already
+    max_sequence_length: int = 64
+    context_window: int = 8
+    temperature: float = 0.8
     use_mixed_precision: bool = True
+    use_torch_compile: bool = False       # accepted for API parity; kernels are fused already
+    cache_models: bool = True
     model_preset: str = "rollout_dit_b"
     model_overrides: List[str] = field(default_factory=list)
     use_vae: bool = True
@@ -266,8 +275,13 @@ class MultiModelPipeline:
                 "performance": {"total_ms": sum(o["performance"]["total_ms"] for o in outs)}}
 
 
-def create_pipeline(pipeline_type: str = "standard", **kwargs):
-    cfg = PipelineConfig(**{k: v for k, v in kwargs.items() if k in PipelineConfig.__dataclass_fields__})
+def create_pipeline(model_path: Optional[str] = None, vae_path: Optional[str] = None,
+                    pipeline_type: str = "standard", device: str = "cuda", **kwargs):
+    """``standard``, ``batch`` or ``realtime`` pipeline (inference/pipeline.py:541-575)."""
+    if pipeline_type not in ("standard", "batch", "realtime"):
+        raise ValueError(f"Unsupported pipeline type: {pipeline_type}")
+    cfg = PipelineConfig(model_path=model_path, vae_path=vae_path, device=device,
+                         **{k: v for k, v in kwargs.items() if k in PipelineConfig.__dataclass_fields__})
     if pipeline_type == "batch":
         return BatchInferencePipeline(cfg)
     if pipeline_type == "realtime":

@@ -145,12 +145,27 @@ class RolloutEvaluator:
 
 
 class StreamingRollout:
-    def __init__(self, model: WorldDiT, cfg, dtype: Optional[torch.dtype] = None):
-        if isinstance(cfg, InferenceConfig):
-            cfg = cfg.to_rollout_config()
-        self.model = model
-        self.cfg = cfg
-        dev = next(model.parameters()).device
+    """Chunked flow-matching rollout of a :class:`WorldDiT` over a sliding KV window.
+
+    Constructed as the reference's (``world_model, vae_model, config, device``,
+    inference/rollout.py:158-197); ``StreamingRollout(model, config[, dtype])`` also
+    works. ``config`` is a :class:`RolloutConfig` or an :class:`InferenceConfig`. With a
+    VAE, :meth:`generate_sequence` takes and returns RGB frames (encoded to the model's
+    latent grid, rolled out, decoded); :meth:`run` always works on latents."""
+
+    def __init__(self, world_model: WorldDiT, vae_model=None, config=None, device=None,
+                 dtype: Optional[torch.dtype] = None):
+        if vae_model is not None and not isinstance(vae_model, torch.nn.Module):
+            # (model, config[, dtype])
+            vae_model, config, dtype = None, vae_model, (config if isinstance(config, torch.dtype) else dtype)
+        if config is None:
+            config = RolloutConfig()
+        if isinstance(config, InferenceConfig):
+            config = config.to_rollout_config()
+        self.model = self.world_model = world_model
+        self.vae_model = vae_model.eval() if vae_model is not None else None
+        self.cfg = self.config = config
+        dev = next(world_model.parameters()).device
         self.device = dev
         self.dtype = dtype or (torch.bfloat16 if dev.type == "cuda" else torch.float32)
 
@@ -233,16 +248,54 @@ class StreamingRollout:
     def reset_state(self):
         """Rollouts keep no state between ``run`` calls (each builds its own KV window)."""
 
-    def generate_sequence(self, context_frames: torch.Tensor, controls: Optional[torch.Tensor] = None,
-                          num_frames: Optional[int] = None, return_intermediates: bool = False):
-        """``context_frames [B, Fc, C, H, W]`` latents, ``controls [B, F_total, A]`` ->
-        ``{"frames": generated frames only, "chunk_ms": [...]}``."""
-        B, Fc = context_frames.shape[:2]
-        total = Fc + (num_frames if num_frames is not None else self.cfg.total_frames - Fc)
+    def _encode_rgb(self, frames: torch.Tensor) -> torch.Tensor:
+        """RGB ``[B, T, 3, H, W]`` in [0, 1] -> posterior-mean latents on the model's grid."""
+        with torch.no_grad():
+            mean, _ = self.vae_model.encode((frames.float() * 2 - 1).transpose(1, 2))
+        lat = mean.transpose(1, 2).float()
+        Hm, Wm = self.model.cfg.latent_h, self.model.cfg.latent_w
+        lat = lat[..., :Hm, :Wm]
+        return F.pad(lat, (0, Wm - lat.shape[-1], 0, Hm - lat.shape[-2]))
+
+    def _decode_rgb(self, lat: torch.Tensor, hw) -> torch.Tensor:
+        tc = getattr(self.vae_model.config, "temporal_compression", 1)
+        z = lat.float().transpose(1, 2)
+        with torch.no_grad():
+            x = self.vae_model.decode(z, output_shape=(z.shape[2] * tc,) + tuple(hw))
+        return ((x.float() + 1) / 2).clamp(0, 1).transpose(1, 2)
+
+    def generate_sequence(self, context_frames: torch.Tensor, control_sequence: Optional[torch.Tensor] = None,
+                          max_new_frames: Optional[int] = None, return_intermediates: bool = False, *,
+                          controls: Optional[torch.Tensor] = None, num_frames: Optional[int] = None):
+        """``context_frames [B, Fc, C, H, W]`` (latents, or RGB in [0, 1] with a VAE),
+        per-frame controls ``[B, F_total, A]`` (zeros when omitted), ``max_new_frames``
+        frames to generate. Returns the reference's keys (``context_frames``,
+        ``generated_frames``, ``full_sequence``, ``metadata``, ``performance``) and
+        ``frames`` (the generated latents), ``chunk_ms``, ``total_ms``."""
+        controls = control_sequence if control_sequence is not None else controls
+        n_new = max_new_frames if max_new_frames is not None else num_frames
+        rgb = self.vae_model is not None and context_frames.shape[2] == 3
+        lat = self._encode_rgb(context_frames.to(self.device)) if rgb else context_frames
+        B, Fc = lat.shape[:2]
+        total = Fc + (n_new if n_new is not None else self.cfg.total_frames - Fc)
+        A = self.model.cfg.action_dim
         if controls is None:
-            controls = torch.zeros(B, total, self.model.cfg.action_dim, device=self.device)
-        res = self.run(context_frames, controls, total)
-        out = {"frames": res.frames[:, Fc:], "chunk_ms": res.chunk_ms, "total_ms": res.total_ms}
+            controls = torch.zeros(B, total, A, device=self.device)
+        controls = controls.to(self.device).float()[..., :A]
+        if controls.shape[1] < total:  # hold the last control
+            controls = torch.cat([controls, controls[:, -1:].expand(-1, total - controls.shape[1], -1)], 1)
+        res = self.run(lat, controls[:, :total], total)
+        gen_lat = res.frames[:, Fc:]
+        gen = self._decode_rgb(gen_lat, context_frames.shape[-2:]) if rgb else gen_lat
+        n = max(gen_lat.shape[1], 1)
+        mem = torch.cuda.max_memory_allocated(self.device) / 1e6 if self.device.type == "cuda" else 0.0
+        out = {"context_frames": context_frames, "generated_frames": gen,
+               "full_sequence": torch.cat([context_frames.to(gen.device, gen.dtype), gen], 1),
+               "metadata": {"frame_times": [ms / 1e3 * len(res.chunk_ms) / n for ms in res.chunk_ms],
+                            "chunk_ms": res.chunk_ms},
+               "performance": {"avg_fps": 1e3 * n / res.total_ms if res.total_ms > 0 else 0.0,
+                               "peak_memory_mb": mem, "avg_memory_mb": mem},
+               "frames": gen_lat, "chunk_ms": res.chunk_ms, "total_ms": res.total_ms}
         if return_intermediates:
             out["all_frames"] = res.frames
         return out

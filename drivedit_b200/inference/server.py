@@ -227,14 +227,13 @@ class MultiModalServer(InferenceServer):
         uvicorn.run(self.app, host=host, port=port)
 
 
-def create_server(server_type: str = "http", **kwargs) -> InferenceServer:
-    if server_type == "http":
-        return HTTPServer(**kwargs)
-    if server_type == "websocket":
-        return WebSocketServer(**kwargs)
-    if server_type == "multimodal":
-        return MultiModalServer(**kwargs)
-    raise ValueError(f"unknown server type {server_type!r}")
+def create_server(server_type: str = "http", model_path: Optional[str] = None,
+                  vae_path: Optional[str] = None, **kwargs) -> InferenceServer:
+    """``http``, ``websocket`` or ``multimodal`` (inference/server.py:502-527)."""
+    kinds = {"http": HTTPServer, "websocket": WebSocketServer, "multimodal": MultiModalServer}
+    if server_type not in kinds:
+        raise ValueError(f"Unknown server type: {server_type}")
+    return kinds[server_type](model_path, vae_path, **kwargs)
 
 
 def main():

@@ -36,6 +36,17 @@ def test_rollout_evaluator_and_generate_sequence():
                                                  flow_steps=2))
     out = ro.generate_sequence(torch.randn(1, 2, 4, 8, 8), None, num_frames=4)
     assert out["frames"].shape == (1, 4, 4, 8, 8) and len(out["chunk_ms"]) == 2
+    # the reference's construction: (world_model, vae_model, config, device), RGB in and out
+    from drivedit_b200.models.vae3d import VAE3DConfig, VAE3Dv2
+    vae = VAE3Dv2(VAE3DConfig(latent_dim=4, hidden_dims=[16, 16, 16, 16], num_res_blocks=1,
+                              use_attention=False, temporal_compression=1, spatial_compression=8,
+                              use_perceptual_loss=False))
+    ro = StreamingRollout(model, vae, InferenceConfig(max_sequence_length=8, context_window=4,
+                                                      chunk_size=2, flow_steps=2), "cpu")
+    rgb = torch.rand(1, 2, 3, 64, 64)
+    out = ro.generate_sequence(rgb, torch.zeros(1, 6, 6), 4)
+    assert out["generated_frames"].shape == (1, 4, 3, 64, 64)
+    assert out["full_sequence"].shape == (1, 6, 3, 64, 64) and out["performance"]["avg_fps"] > 0
     si = StreamingInference(model, OptimizationConfig(chunk_size=2, target_fps=1.0), device="cpu")
     si.initialize(num_layers=2)
     frames = [f for f, _ in si.generate_stream(torch.randn(1, 2, 4, 8, 8), torch.zeros(1, 6, 2), 4)]
@@ -62,3 +73,19 @@ def test_benchmark_profile_and_deployment_cpu():
     mt = MemoryTracker()
     mt.record("x")
     assert mt.get_report()["samples"] == 1
+
+
+def test_reference_factories_and_signatures():
+    """The inference factories and configs take the reference's positional arguments."""
+    from drivedit_b200.inference.optimization import CompileMode, FrameMetrics, ModelCompiler
+    from drivedit_b200.inference.pipeline import InferencePipeline, PipelineConfig, create_pipeline
+    from drivedit_b200.inference.server import InferenceServer, create_server
+
+    cfg = PipelineConfig(None, None, "cpu", 1, 16, 4, 0.8, False)
+    assert cfg.device == "cpu" and cfg.max_sequence_length == 16 and not cfg.use_mixed_precision
+    assert ModelCompiler(CompileMode.REDUCE_OVERHEAD, False, False, "inductor", True).disable_cudagraphs
+    assert FrameMetrics(0, 1.0, 2.0, 3.0, 5).kv_cache_length == 5
+    p = create_pipeline(None, None, "standard", "cpu", model_preset="tiny", use_vae=False)
+    assert isinstance(p, InferencePipeline) and p.device.type == "cpu"
+    srv = create_server("http", None, None, device="cpu", model_preset="tiny", use_vae=False)
+    assert isinstance(srv, InferenceServer)
