@@ -174,9 +174,16 @@ class WorldModelBenchmark:
     """Quality / temporal / control / long-sequence suite over a test batch
     ``{'latents': [B, T, C, H, W], 'actions': [B, T, A]}``."""
 
-    def __init__(self, model, device: str = "cuda", output_dir: Optional[str] = None):
+    def __init__(self, model, vae_model=None, device: str = "cuda", save_path: Optional[str] = None,
+                 output_dir: Optional[str] = None):
+        """The reference's arguments (``model, vae_model, device, save_path``,
+        evaluation/benchmarks.py); ``WorldModelBenchmark(model, device)`` also works."""
+        if isinstance(vae_model, (str, torch.device)):   # (model, device, ...)
+            vae_model, device = None, vae_model
+        self.vae_model = vae_model
         self.model, self.device = model, torch.device(device)
-        self.output_dir = Path(output_dir) if output_dir else None
+        out = save_path or output_dir
+        self.output_dir = Path(out) if out else None
         self.results: Dict[str, Any] = {}
 
     def run_full_benchmark(self, test_data: Dict[str, torch.Tensor]) -> Dict[str, Any]:

@@ -447,17 +447,28 @@ class ClosedLoopEvaluator:
             actions_taken=torch.stack(self.actions_history) if self.actions_history else None)
 
 
-def create_lane_following_task(duration_steps: int = 100, target_speed: float = 10.0) -> TaskDefinition:
-    return TaskDefinition(TaskType.LANE_FOLLOWING, "lane_following", "keep the lane at constant speed",
-                          max_duration_steps=duration_steps, goal_speed=target_speed)
+def create_lane_following_task(name: str = "lane_following", max_duration: int = 300,
+                               target_speed: float = 10.0) -> TaskDefinition:
+    """Keep the lane at ``target_speed`` for up to ``max_duration`` steps
+    (evaluation/closed_loop.py:1199-1211)."""
+    return TaskDefinition(TaskType.LANE_FOLLOWING, name, "keep the lane at a safe constant speed",
+                          max_duration_steps=max_duration, max_lateral_deviation=0.5,
+                          goal_speed=target_speed)
 
 
-def create_obstacle_avoidance_task(obstacle_position=(20.0, 0.0), duration_steps: int = 150) -> TaskDefinition:
-    return TaskDefinition(TaskType.OBSTACLE_AVOIDANCE, "obstacle_avoidance", "pass the obstacle",
-                          max_duration_steps=duration_steps,
+def create_obstacle_avoidance_task(obstacle_position=(20.0, 0.0), name: str = "obstacle_avoidance",
+                                   max_duration: int = 200) -> TaskDefinition:
+    """Pass an obstacle at ``obstacle_position`` (metres ahead, lateral) keeping a
+    time-to-collision of at least 2 s; the goal is 10 m past it
+    (evaluation/closed_loop.py:1214-1225)."""
+    return TaskDefinition(TaskType.OBSTACLE_AVOIDANCE, name, "avoid the obstacle while making progress",
+                          max_duration_steps=max_duration, min_ttc=2.0,
                           goal_position=(obstacle_position[0] + 10.0, obstacle_position[1]))
 
 
-def create_emergency_stop_task(initial_speed: float = 15.0) -> TaskDefinition:
-    return TaskDefinition(TaskType.EMERGENCY_STOP, "emergency_stop", "stop as fast as allowed",
-                          max_duration_steps=100, goal_speed=0.0)
+def create_emergency_stop_task(name: str = "emergency_stop", max_duration: int = 50) -> TaskDefinition:
+    """Stop completely as fast as the deceleration limit allows
+    (evaluation/closed_loop.py:1228-1240)."""
+    return TaskDefinition(TaskType.EMERGENCY_STOP, name, "come to a complete stop quickly and safely",
+                          max_duration_steps=max_duration, min_duration_steps=5,
+                          max_deceleration=10.0, goal_speed=0.0)

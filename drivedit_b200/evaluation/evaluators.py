@@ -13,8 +13,18 @@ from .metrics import LatentMetrics, TemporalConsistencyMetrics, VideoMetrics
 
 
 class SequenceEvaluator:
-    def __init__(self, model, device: str = "cuda", context_frames: int = 2, flow_steps: int = 2,
-                 chunk_frames: int = 1):
+    """Rolls a world model out from the first ``context_frames`` latent frames of each
+    sequence and scores the generated frames. Takes the reference's arguments
+    (``model, vae_model, device, compute_expensive_metrics``, evaluation/evaluators.py);
+    ``SequenceEvaluator(model, device)`` also works. Evaluation is in latent space, so
+    ``vae_model`` is kept for callers that decode."""
+
+    def __init__(self, model, vae_model=None, device: str = "cuda",
+                 compute_expensive_metrics: bool = True, context_frames: int = 2,
+                 flow_steps: int = 2, chunk_frames: int = 1):
+        if isinstance(vae_model, (str, torch.device)):   # (model, device, ...)
+            vae_model, device = None, vae_model
+        self.vae_model, self.compute_expensive_metrics = vae_model, compute_expensive_metrics
         self.model, self.device = model, torch.device(device)
         self.context_frames, self.flow_steps, self.chunk_frames = context_frames, flow_steps, chunk_frames
 
@@ -202,12 +212,12 @@ class AblationEvaluator:
 
     def evaluate_component_ablation(self, batches: Sequence[Dict[str, torch.Tensor]],
                                     ablation_configs: List[Dict[str, Any]]) -> Dict[str, Any]:
-        results = {"base_model": SequenceEvaluator(self.base_model, self.device,
+        results = {"base_model": SequenceEvaluator(self.base_model, device=self.device,
                                                    **self.seq_kwargs).evaluate_batch(batches)}
         for i, c in enumerate(ablation_configs):
             model = self._create_ablated_model(c)
             results[c.get("name", f"ablation_{i}")] = SequenceEvaluator(
-                model, self.device, **self.seq_kwargs).evaluate_batch(batches)
+                model, device=self.device, **self.seq_kwargs).evaluate_batch(batches)
         return {"results": results, "analysis": self._analyze_ablation_results(results)}
 
     @staticmethod

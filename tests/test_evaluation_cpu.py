@@ -67,3 +67,18 @@ def test_closed_loop_benchmarks_evaluators():
     rt = RealTimeEvaluator(m, "cpu").evaluate_real_time_performance(target_fps=1.0, frames=4, chunk_frames=2,
                                                                     flow_steps=1)
     assert rt["fps"] > 0
+
+
+def test_reference_constructor_forms():
+    from drivedit_b200.evaluation.benchmarks import WorldModelBenchmark
+    from drivedit_b200.evaluation.closed_loop import (create_emergency_stop_task, create_lane_following_task,
+                                                      create_obstacle_avoidance_task)
+    from drivedit_b200.evaluation.evaluators import SequenceEvaluator
+    m = torch.nn.Linear(2, 2)
+    b = WorldModelBenchmark(m, None, "cpu", None)
+    assert b.device.type == "cpu" and b.vae_model is None
+    assert SequenceEvaluator(m, None, "cpu", False).device.type == "cpu"
+    assert create_lane_following_task("lf", 120).max_duration_steps == 120
+    assert create_obstacle_avoidance_task((5.0, 1.0), "oa").goal_position == (15.0, 1.0)
+    t = create_emergency_stop_task("es")
+    assert t.name == "es" and t.goal_speed == 0.0 and t.max_duration_steps == 50
