@@ -65,9 +65,9 @@ class SlotAttention(nn.Module):
     slots), weighted-mean updates, GRU + residual MLP, ``num_iterations`` rounds."""
 
     def __init__(self, num_slots: int, slot_dim: int, input_dim: int, num_iterations: int = 3,
-                 hidden_dim: int = 512, eps: float = 1e-8):
+                 epsilon: float = 1e-8, hidden_dim: int = 512):
         super().__init__()
-        self.num_slots, self.slot_dim, self.num_iterations, self.eps = num_slots, slot_dim, num_iterations, eps
+        self.num_slots, self.slot_dim, self.num_iterations, self.eps = num_slots, slot_dim, num_iterations, epsilon
         self.scale = slot_dim ** -0.5
         self.slots_mu = nn.Parameter(torch.randn(1, 1, slot_dim) * 0.02)
         self.slots_log_sigma = nn.Parameter(torch.zeros(1, 1, slot_dim))
@@ -107,7 +107,8 @@ class ObjectSlotEncoder(nn.Module):
                  hidden_dim: int = 512, num_heads: int = 8, dropout: float = 0.1):
         super().__init__()
         self.input_dim, self.slot_dim, self.max_objects = input_dim, slot_dim, max_objects
-        self.slot_attention = SlotAttention(max_objects, slot_dim, input_dim, num_iterations, hidden_dim)
+        self.slot_attention = SlotAttention(max_objects, slot_dim, input_dim, num_iterations,
+                                            hidden_dim=hidden_dim)
         self.position_head = nn.Linear(slot_dim, 4)
         self.existence_head = nn.Linear(slot_dim, 1)
 

@@ -307,8 +307,12 @@ def setup_distributed_model(model: torch.nn.Module, local_rank: int, find_unused
     return DDP(model, find_unused_parameters=find_unused_parameters)
 
 
-def create_distributed_dataloader(dataset, batch_size: int, num_workers: int = 2, shuffle: bool = True,
+def create_distributed_dataloader(dataset, batch_size: int, shuffle: bool = True, num_workers: int = 4,
+                                  pin_memory: bool = True, drop_last: bool = True,
                                   rank: Optional[int] = None, world_size: Optional[int] = None, **kw):
+    """A loader over this rank's share of ``dataset`` (the reference's arguments,
+    training/distributed.py:256-274); without a process group (or with one rank) it
+    shuffles the whole dataset itself. Pinned memory only when CUDA is present."""
     from torch.utils.data import DataLoader, DistributedSampler
 
     if world_size is None:
@@ -316,7 +320,8 @@ def create_distributed_dataloader(dataset, batch_size: int, num_workers: int = 2
         rank = dist.get_rank() if dist.is_initialized() else 0
     sampler = DistributedSampler(dataset, world_size, rank, shuffle=shuffle) if world_size > 1 else None
     return DataLoader(dataset, batch_size=batch_size, shuffle=shuffle and sampler is None, sampler=sampler,
-                      num_workers=num_workers, pin_memory=torch.cuda.is_available(), **kw)
+                      num_workers=num_workers, pin_memory=pin_memory and torch.cuda.is_available(),
+                      drop_last=drop_last, **kw)
 
 
 def reduce_dict(input_dict: Dict[str, torch.Tensor], world_size: int, average: bool = True) -> Dict[str, float]:

@@ -206,20 +206,36 @@ def _info_nce(a: torch.Tensor, b: torch.Tensor, temperature: float) -> torch.Ten
 
 
 class InfoNCELoss(BaseLoss):
-    """Positives: the same sequence's representation ``k`` steps later; negatives: the
-    rest of the batch (symmetric InfoNCE)."""
+    """Positives: the same sequence's representation ``delta`` steps later; negatives:
+    the rest of the batch (symmetric InfoNCE). With ``use_hard_negatives`` the state one
+    step past the positive (same sequence, when it exists) joins each anchor's negatives:
+    close in time, but not the target."""
 
-    def __init__(self, weight: float = 1.0, temperature: float = 0.1, offset: int = 1):
+    def __init__(self, weight: float = 1.0, temperature: float = 0.1, delta: int = 1,
+                 use_hard_negatives: bool = True):
         super().__init__(weight)
-        self.temperature, self.offset = temperature, offset
+        self.temperature, self.delta, self.use_hard_negatives = temperature, delta, use_hard_negatives
 
     def forward(self, predictions, targets, **kw):
         h = predictions.get("hidden_states")
-        if h is None or h.dim() != 3 or h.shape[1] <= self.offset:
+        d = self.delta
+        if h is None or h.dim() != 3 or h.shape[1] <= d:
             return self._zero(predictions, targets)
-        a = h[:, :-self.offset].reshape(-1, h.shape[-1])
-        b = h[:, self.offset:].reshape(-1, h.shape[-1])
-        return self._out(_info_nce(a, b, self.temperature))
+        B, T, D = h.shape
+        if not self.use_hard_negatives or T <= d + 1:
+            a = h[:, :-d].reshape(-1, D)
+            b = h[:, d:].reshape(-1, D)
+            return self._out(_info_nce(a, b, self.temperature))
+        za = F.normalize(h[:, :-d].float(), dim=-1)                     # [B, T-d, D]
+        zp = F.normalize(h[:, d:].float(), dim=-1)
+        zh = F.normalize(h[:, d + 1:].float(), dim=-1)                  # [B, T-d-1, D]
+        a, p = za.reshape(-1, D), zp.reshape(-1, D)
+        logits = a @ p.t() / self.temperature                           # in-batch
+        hard = torch.full((B, T - d), float("-inf"), device=h.device)
+        hard[:, :T - d - 1] = (za[:, :T - d - 1] * zh).sum(-1) / self.temperature
+        logits = torch.cat([logits, hard.reshape(-1, 1)], 1)
+        lab = torch.arange(a.shape[0], device=h.device)
+        return self._out(F.cross_entropy(logits, lab))
 
 
 class CrossModalContrastiveLoss(BaseLoss):
@@ -249,12 +265,15 @@ class CrossModalContrastiveLoss(BaseLoss):
 
 
 class TemporalContrastiveLoss(BaseLoss):
-    """Frames within ``window`` steps of an anchor are positives; other sequences'
-    frames are negatives (multi-positive InfoNCE over the time axis)."""
+    """Frames within ``positive_window`` steps of an anchor are positives; negatives are
+    other sequences' frames and the anchor's own frames at least ``negative_margin``
+    steps away; own frames in between are neither (multi-positive InfoNCE over time)."""
 
-    def __init__(self, weight: float = 1.0, temperature: float = 0.1, window: int = 2):
+    def __init__(self, weight: float = 1.0, temperature: float = 0.1, positive_window: int = 2,
+                 negative_margin: int = 5):
         super().__init__(weight)
-        self.temperature, self.window = temperature, window
+        self.temperature, self.window = temperature, positive_window
+        self.negative_margin = max(negative_margin, positive_window + 1)
 
     def forward(self, predictions, targets, **kw):
         h = predictions.get("hidden_states")
@@ -266,10 +285,12 @@ class TemporalContrastiveLoss(BaseLoss):
         seq = torch.arange(B, device=h.device).repeat_interleave(T)
         tt = torch.arange(T, device=h.device).repeat(B)
         same = seq[:, None] == seq[None]
-        near = (tt[:, None] - tt[None]).abs() <= self.window
+        dt = (tt[:, None] - tt[None]).abs()
+        near = dt <= self.window
         eye = torch.eye(B * T, dtype=torch.bool, device=h.device)
         pos = same & near & ~eye
-        sim = sim.masked_fill(eye, -1e9)
+        ignore = eye | (same & ~near & (dt < self.negative_margin))
+        sim = sim.masked_fill(ignore, -1e9)
         logp = sim - torch.logsumexp(sim, 1, keepdim=True)
         loss = -(logp * pos).sum(1) / pos.sum(1).clamp_min(1)
         return self._out(loss.mean())
@@ -279,15 +300,15 @@ class VICRegLoss(BaseLoss):
     """Variance-invariance-covariance regularisation (Bardes et al. 2022)."""
 
     def __init__(self, weight: float = 1.0, sim_weight: float = 25.0, var_weight: float = 25.0,
-                 cov_weight: float = 1.0):
+                 cov_weight: float = 1.0, variance_target: float = 1.0):
         super().__init__(weight)
         self.sim_weight, self.var_weight, self.cov_weight = sim_weight, var_weight, cov_weight
+        self.variance_target = variance_target
 
-    @staticmethod
-    def _var_cov(z):
+    def _var_cov(self, z):
         z = z - z.mean(0)
         std = torch.sqrt(z.var(0) + 1e-4)
-        var = F.relu(1 - std).mean()
+        var = F.relu(self.variance_target - std).mean()
         n, d = z.shape
         cov = (z.t() @ z) / max(n - 1, 1)
         off = cov - torch.diag(torch.diag(cov))
@@ -375,18 +396,20 @@ def _grad_xy(x):
 
 
 class ScaleInvariantDepthLoss(BaseLoss):
-    """Eigen et al. 2014: ``mean(d^2) - lam * mean(d)^2`` with ``d = log p - log t``."""
+    """Eigen et al. 2014: ``mean(d^2) - lambda_scale * mean(d)^2`` with
+    ``d = log p - log t`` over target depths in ``(eps, max_depth)``."""
 
-    def __init__(self, weight: float = 1.0, lam: float = 0.5, max_depth: float = 100.0):
+    def __init__(self, weight: float = 1.0, lambda_scale: float = 0.5, max_depth: float = 100.0,
+                 eps: float = 1e-3):
         super().__init__(weight)
-        self.lam, self.max_depth = lam, max_depth
+        self.lam, self.max_depth, self.eps = lambda_scale, max_depth, eps
 
     def forward(self, predictions, targets, **kw):
         p, t = predictions.get("depth_predictions"), targets.get("depth")
         if p is None or t is None:
             return self._zero(predictions, targets)
-        valid = (t > 1e-3) & (t < self.max_depth)
-        d = torch.log(p.float().clamp_min(1e-3)) - torch.log(t.float().clamp_min(1e-3))
+        valid = (t > self.eps) & (t < self.max_depth)
+        d = torch.log(p.float().clamp_min(self.eps)) - torch.log(t.float().clamp_min(self.eps))
         d = d[valid]
         if d.numel() == 0:
             return self._zero(predictions, targets)
@@ -429,9 +452,13 @@ class EdgeAwareDepthLoss(BaseLoss):
 
 
 class MultiScaleDepthLoss(BaseLoss):
-    def __init__(self, weight: float = 1.0, scales: Tuple[int, ...] = (1, 2, 4, 8)):
+    """Depth error at several average-pooled resolutions, each weighted 1/scale: L1, or
+    with ``use_si`` the scale-invariant log error."""
+
+    def __init__(self, weight: float = 1.0, scales: Tuple[int, ...] = (1, 2, 4, 8), use_si: bool = False):
         super().__init__(weight)
         self.scales = scales
+        self.si = ScaleInvariantDepthLoss(1.0) if use_si else None
 
     def forward(self, predictions, targets, **kw):
         p, t = predictions.get("depth_predictions"), targets.get("depth")
@@ -444,7 +471,10 @@ class MultiScaleDepthLoss(BaseLoss):
             if min(p.shape[-2:]) // s < 1:
                 continue
             ps, ts = (F.avg_pool2d(p, s), F.avg_pool2d(t, s)) if s > 1 else (p, t)
-            terms.append(F.l1_loss(ps, ts) / s)
+            if self.si is not None:
+                terms.append(self.si({"depth_predictions": ps}, {"depth": ts}).reshape(()) / s)
+            else:
+                terms.append(F.l1_loss(ps, ts) / s)
         return self._out(torch.stack(terms).sum())
 
 
@@ -476,17 +506,21 @@ class ActionSmoothnessLoss(BaseLoss):
 
 
 class BoundaryActionClippingLoss(BaseLoss):
-    """Penalises actions beyond ``margin`` of the valid [-1, 1] range (quadratic)."""
+    """Penalises actions beyond ``margin`` of the valid range ``action_bounds``
+    (quadratic in the excess over the shrunken bounds)."""
 
-    def __init__(self, weight: float = 1.0, margin: float = 0.95):
+    def __init__(self, weight: float = 1.0, margin: float = 0.95,
+                 action_bounds: Tuple[float, float] = (-1.0, 1.0)):
         super().__init__(weight)
         self.margin = margin
+        self.lower, self.upper = action_bounds
 
     def forward(self, predictions, targets, **kw):
         a = predictions.get("predicted_actions")
         if a is None:
             return self._zero(predictions, targets)
-        return self._out(F.relu(a.float().abs() - self.margin).pow(2).mean())
+        mid, half = 0.5 * (self.upper + self.lower), 0.5 * (self.upper - self.lower)
+        return self._out(F.relu((a.float() - mid).abs() - self.margin * half).pow(2).mean())
 
 
 class GoalConditionedActionLoss(BaseLoss):
@@ -588,9 +622,9 @@ class _PatchViT(nn.Module):
 class DINOFeatureLoss(BaseLoss):
     """Cosine distance between patch tokens of a frozen ViT encoder."""
 
-    def __init__(self, weight: float = 1.0, dim: int = 256):
+    def __init__(self, weight: float = 1.0, embed_dim: int = 256):
         super().__init__(weight)
-        self.encoder = _PatchViT(dim, seed=4)
+        self.encoder = _PatchViT(embed_dim, seed=4)
 
     def forward(self, predictions, targets, **kw):
         p, t = predictions.get("predictions"), targets.get("frames")
@@ -604,9 +638,9 @@ class DINOFeatureLoss(BaseLoss):
 class CLIPSimilarityLoss(BaseLoss):
     """``1 - cos`` between pooled embeddings of a frozen image encoder."""
 
-    def __init__(self, weight: float = 1.0, dim: int = 256):
+    def __init__(self, weight: float = 1.0, embed_dim: int = 256):
         super().__init__(weight)
-        self.encoder = _PatchViT(dim, seed=5)
+        self.encoder = _PatchViT(embed_dim, seed=5)
 
     def forward(self, predictions, targets, **kw):
         p, t = predictions.get("predictions"), targets.get("frames")
@@ -665,11 +699,13 @@ class MotionMagnitudeLoss(BaseLoss):
 
 
 class SceneStabilityLoss(BaseLoss):
-    """Low-frequency content (heavily pooled frames) should change like the target's."""
+    """Low-frequency content (heavily pooled frames) should change like the target's;
+    with ``motion_threshold > 0`` instead, the prediction should stay still wherever the
+    target's pooled change is at most the threshold (static scene content)."""
 
-    def __init__(self, weight: float = 1.0, pool: int = 8):
+    def __init__(self, weight: float = 1.0, motion_threshold: float = 0.0, pool: int = 8):
         super().__init__(weight)
-        self.pool = pool
+        self.motion_threshold, self.pool = motion_threshold, pool
 
     def forward(self, predictions, targets, **kw):
         p, t = predictions.get("predictions"), targets.get("frames")
@@ -679,7 +715,12 @@ class SceneStabilityLoss(BaseLoss):
         k = max(1, min(self.pool, p.shape[-1], p.shape[-2]))
         lp = F.avg_pool2d(_frames(p), k).view(p.shape[0], p.shape[1], -1)
         lt = F.avg_pool2d(_frames(t), k).view(t.shape[0], t.shape[1], -1)
-        return self._out(F.mse_loss(lp[:, 1:] - lp[:, :-1], lt[:, 1:] - lt[:, :-1]))
+        dp, dtg = lp[:, 1:] - lp[:, :-1], lt[:, 1:] - lt[:, :-1]
+        if self.motion_threshold > 0:
+            # the prediction should not change where the target scene is static
+            static = (dtg.abs() <= self.motion_threshold).float()
+            return self._out((dp * static).pow(2).mean())
+        return self._out(F.mse_loss(dp, dtg))
 
 
 # ----------------------------------------------------------------------------- balancing

@@ -158,15 +158,11 @@ class TrainingConfig:
     gradient_clip_norm: float = 1.0
     mixed_precision: bool = True
     checkpoint_every: int = 1000
-    checkpoint_dir: Optional[str] = None
-    log_dir: Optional[str] = None
-    log_every: int = 100
     distributed: bool = False
     local_rank: int = 0
     world_size: int = 1
     max_memory_gb: float = 16.0
     memory_cleanup_threshold: float = 0.8
-    seed: int = 0
     repa: REPAConfig = field(default_factory=REPAConfig)
     cjepa: CJEPAConfig = field(default_factory=CJEPAConfig)
     moe: MoEConfig = field(default_factory=MoEConfig)
@@ -174,6 +170,12 @@ class TrainingConfig:
     loss_weights: Dict[str, float] = field(default_factory=lambda: {
         "reconstruction": 1.0, "flow_matching": 1.0, "temporal_consistency": 0.2, "jepa": 0.1,
         "repa": 0.5, "cjepa": 0.3, "moe_balance": 0.01})
+    # this framework's additions, after the reference's fields
+    # (training/unified_trainer.py TrainingConfig) so positional construction matches
+    checkpoint_dir: Optional[str] = None
+    log_dir: Optional[str] = None
+    log_every: int = 100
+    seed: int = 0
 
     def is_component_enabled(self, name: str) -> bool:
         sub = getattr(self, name, None)
@@ -308,7 +310,8 @@ class CJEPAPredictor(nn.Module):
     predict the slots of the next ``prediction_horizon`` frames; InfoNCE between
     predicted and actual (stop-gradient) slots."""
 
-    def __init__(self, config: CJEPAConfig, input_dim: int):
+    def __init__(self, config: CJEPAConfig, model_dim: int):
+        input_dim = model_dim
         super().__init__()
         self.config = config
         self.slots = SlotAttention(config.num_object_queries, config.object_dim, input_dim,
@@ -632,5 +635,16 @@ def create_training_config(preset: str = "default", **overrides) -> TrainingConf
     return cfg
 
 
-def create_unified_trainer(model: nn.Module, config: Optional[TrainingConfig] = None, **kw) -> UnifiedTrainer:
-    return UnifiedTrainer(model, config or TrainingConfig(), **kw)
+def create_unified_trainer(model_config, training_config: Optional[TrainingConfig] = None,
+                           device=None, **kw) -> UnifiedTrainer:
+    """A trainer over a new :class:`~drivedit_b200.models.world_model.WorldModel` built
+    from ``model_config`` (a ``DriveDiTConfig``), as the reference's factory
+    (training/unified_trainer.py:1830-1851); an ``nn.Module`` as the first argument is
+    trained as it is."""
+    if isinstance(model_config, nn.Module):
+        model = model_config
+    else:
+        from ..models.world_model import WorldModel
+
+        model = WorldModel(model_config)
+    return UnifiedTrainer(model, training_config or TrainingConfig(), device, **kw)

@@ -57,7 +57,7 @@ def test_loss_aggregator_all_types():
 
 def test_individual_losses():
     d = torch.rand(2, 1, 8, 8) + 0.5
-    assert float(ScaleInvariantDepthLoss(lam=1.0)({"depth_predictions": d * 3}, {"depth": d})) < 1e-6  # lam=1: scale invariant
+    assert float(ScaleInvariantDepthLoss(lambda_scale=1.0)({"depth_predictions": d * 3}, {"depth": d})) < 1e-6  # lam=1: scale invariant
     a = torch.randn(64, 16)
     v = VICRegLoss()({"hidden_states": a, "hidden_states_aug": a}, {})
     assert torch.isfinite(v)
@@ -71,3 +71,27 @@ def test_individual_losses():
     out = agg(pr, {"latents": torch.zeros(4), "noise": torch.zeros(4)})
     agg.apply_gradient_surgery(out, [w])
     assert w.grad is not None and w.grad.shape == (4,)
+
+
+def test_reference_loss_parameters():
+    """The reference's constructor parameters carry their meaning."""
+    from drivedit_b200.training.losses_v2 import (BoundaryActionClippingLoss, InfoNCELoss,
+                                                  MultiScaleDepthLoss, SceneStabilityLoss,
+                                                  TemporalContrastiveLoss, VICRegLoss)
+    torch.manual_seed(0)
+    h = torch.randn(4, 6, 16)
+    for hard in (False, True):
+        assert float(InfoNCELoss(1.0, 0.1, 2, hard)({"hidden_states": h}, {})) > 0
+    assert float(TemporalContrastiveLoss(1.0, 0.1, 1, 3)({"hidden_states": h}, {})) > 0
+    a = torch.tensor([[[1.5, 0.0]]])
+    assert float(BoundaryActionClippingLoss(1.0, 1.0, (0.0, 2.0))({"predicted_actions": a}, {})) == 0.0
+    assert float(BoundaryActionClippingLoss(1.0, 1.0, (-1.0, 1.0))({"predicted_actions": a}, {})) > 0.0
+    d = torch.rand(2, 1, 16, 16) + 0.5
+    # a constant log offset c costs (1 - lambda) c^2 per scale, weighted 1/scale
+    import math
+    expect = 0.5 * math.log(2.0) ** 2 * (1 + 1 / 2)
+    assert abs(float(MultiScaleDepthLoss(1.0, (1, 2), True)({"depth_predictions": d * 2}, {"depth": d})) - expect) < 1e-4
+    v = torch.rand(1, 3, 3, 16, 16)
+    still = v[:, :1].expand(-1, 3, -1, -1, -1)
+    assert float(SceneStabilityLoss(1.0, 0.1)({"predictions": still}, {"frames": still})) == 0.0
+    assert float(VICRegLoss(1.0, variance_target=0.0)({"hidden_states": h, "hidden_states_aug": h}, {})) >= 0
