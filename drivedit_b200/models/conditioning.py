@@ -63,7 +63,6 @@ class ConditioningConfig:
     cond_dim: int = 256
     num_cameras: int = 6
     camera_embed_dim: int = 128
-    image_size: Tuple[int, int] = (256, 512)
     max_waypoints: int = 50
     max_lanes: int = 8
     road_embed_dim: int = 128
@@ -77,6 +76,7 @@ class ConditioningConfig:
     num_adaln_modulation_outputs: int = 6
     dropout: float = 0.1
     cfg_dropout_prob: float = 0.1
+    image_size: Tuple[int, int] = (256, 512)  # addition: normalises the camera intrinsics
 
 
 def normalize_intrinsics(K: torch.Tensor, image_size: Tuple[int, int]) -> torch.Tensor:
@@ -109,12 +109,12 @@ class CameraEncoder(nn.Module):
     """Intrinsics (fx, fy, cx, cy, skew) + extrinsics (6-D rotation, translation) + a
     camera-id embedding -> per-camera tokens, mean-pooled to one vector."""
 
-    def __init__(self, num_cameras: int = 6, embed_dim: int = 128, output_dim: int = 256,
-                 image_size: Tuple[int, int] = (256, 512)):
+    def __init__(self, embed_dim: int = 128, output_dim: int = 256, num_cameras: int = 6,
+                 image_size: Tuple[int, int] = (256, 512), dropout: float = 0.0):
         super().__init__()
         self.image_size = image_size
         self.camera_embed = nn.Embedding(num_cameras, embed_dim)
-        self.proj = _mlp(5 + 9 + embed_dim, embed_dim * 2, output_dim)
+        self.proj = _mlp(5 + 9 + embed_dim, embed_dim * 2, output_dim, dropout)
 
     def forward(self, intrinsics, extrinsics, camera_ids=None, return_per_camera: bool = False):
         B, N = intrinsics.shape[:2]
@@ -130,10 +130,11 @@ class RoadTopologyEncoder(nn.Module):
     """Waypoints (x, y, z, heading, curvature, speed limit) -> tokens; road type, lane and
     turn features -> a global vector; returns (global [B, D], context tokens [B, N, D])."""
 
-    def __init__(self, max_waypoints: int = 50, embed_dim: int = 128, output_dim: int = 256,
-                 num_heads: int = 4, num_road_types: int = 8):
+    def __init__(self, embed_dim: int = 128, output_dim: int = 256, max_waypoints: int = 50,
+                 max_lanes: int = 8, num_road_types: int = 8, num_heads: int = 4, dropout: float = 0.0):
         super().__init__()
-        self.wp_proj = _mlp(6 + 32, embed_dim, output_dim)
+        self.max_waypoints, self.max_lanes = max_waypoints, max_lanes
+        self.wp_proj = _mlp(6 + 32, embed_dim, output_dim, dropout)
         self.road_type = nn.Embedding(num_road_types, output_dim)
         self.lane_proj = nn.Linear(3, output_dim)
         self.turn_proj = nn.Linear(5, output_dim)
@@ -168,11 +169,12 @@ class BoundingBox3DEncoder(nn.Module):
     """Per-object (position, size, heading sin/cos, velocity, confidence, class) tokens,
     distance-weighted pooling (closer objects count more); returns (global, tokens)."""
 
-    def __init__(self, max_objects: int = 64, embed_dim: int = 128, output_dim: int = 256,
-                 num_classes: int = 11, num_heads: int = 4):
+    def __init__(self, embed_dim: int = 128, output_dim: int = 256, max_objects: int = 64,
+                 num_object_classes: int = 11, num_heads: int = 4, dropout: float = 0.0):
         super().__init__()
-        self.class_embed = nn.Embedding(num_classes, embed_dim)
-        self.proj = _mlp(3 + 3 + 2 + 3 + 1 + embed_dim, embed_dim * 2, output_dim)
+        self.max_objects = max_objects
+        self.class_embed = nn.Embedding(num_object_classes, embed_dim)
+        self.proj = _mlp(3 + 3 + 2 + 3 + 1 + embed_dim, embed_dim * 2, output_dim, dropout)
         self.attn = nn.MultiheadAttention(output_dim, num_heads, batch_first=True)
         self.norm = nn.LayerNorm(output_dim)
         self.out = nn.Linear(output_dim, output_dim)
@@ -201,20 +203,21 @@ class BoundingBox3DEncoder(nn.Module):
 class EgoStateEncoder(nn.Module):
     """Position, velocity, acceleration, heading (sin/cos), heading rate, optional GPS/IMU."""
 
-    def __init__(self, state_dim: int = 64, output_dim: int = 256, gps_dim: int = 3, imu_dim: int = 6):
+    def __init__(self, embed_dim: int = 64, output_dim: int = 256, use_gps: bool = True,
+                 use_imu: bool = True, dropout: float = 0.0, gps_dim: int = 3, imu_dim: int = 6):
         super().__init__()
-        self.base = _mlp(3 + 3 + 3 + 2 + 1, state_dim, output_dim)
-        self.gps = nn.Linear(gps_dim, output_dim)
-        self.imu = nn.Linear(imu_dim, output_dim)
+        self.base = _mlp(3 + 3 + 3 + 2 + 1, embed_dim, output_dim, dropout)
+        self.gps = nn.Linear(gps_dim, output_dim) if use_gps else None
+        self.imu = nn.Linear(imu_dim, output_dim) if use_imu else None
 
     def forward(self, position, velocity, acceleration, heading, heading_rate, gps=None, imu=None):
         x = torch.cat([position.float(), velocity.float(), acceleration.float(),
                        heading.sin()[..., None].float(), heading.cos()[..., None].float(),
                        heading_rate.float()[..., None]], -1)
         out = self.base(x)
-        if gps is not None:
+        if gps is not None and self.gps is not None:
             out = out + self.gps(gps.float())
-        if imu is not None:
+        if imu is not None and self.imu is not None:
             out = out + self.imu(imu.float())
         return out
 
@@ -222,13 +225,13 @@ class EgoStateEncoder(nn.Module):
 class TemporalEnvironmentalEncoder(nn.Module):
     """Time of day (cyclic), weather (+ intensity), season, sun angles, lighting."""
 
-    def __init__(self, time_dim: int = 64, weather_dim: int = 32, output_dim: int = 256,
-                 num_weather: int = 8, num_seasons: int = 4):
+    def __init__(self, time_embed_dim: int = 64, weather_embed_dim: int = 32, output_dim: int = 256,
+                 num_weather_conditions: int = 8, num_seasons: int = 4, dropout: float = 0.0):
         super().__init__()
-        self.weather = nn.Embedding(num_weather, weather_dim)
-        self.season = nn.Embedding(num_seasons, weather_dim)
-        self.proj = _mlp(time_dim + 2 * weather_dim + 1 + 4 + 1, output_dim, output_dim)
-        self.time_dim = time_dim
+        self.weather = nn.Embedding(num_weather_conditions, weather_embed_dim)
+        self.season = nn.Embedding(num_seasons, weather_embed_dim)
+        self.proj = _mlp(time_embed_dim + 2 * weather_embed_dim + 1 + 4 + 1, output_dim, output_dim, dropout)
+        self.time_dim = time_embed_dim
 
     def forward(self, time_of_day, weather, weather_intensity=None, season=None, sun_azimuth=None,
                 sun_elevation=None, lighting=None):
@@ -267,11 +270,14 @@ class ConditioningIntegration(nn.Module):
         super().__init__()
         c = self.config = config or ConditioningConfig()
         D = c.cond_dim
-        self.camera_encoder = CameraEncoder(c.num_cameras, c.camera_embed_dim, D, c.image_size)
-        self.road_encoder = RoadTopologyEncoder(c.max_waypoints, c.road_embed_dim, D, c.road_cross_attn_heads)
-        self.bbox_encoder = BoundingBox3DEncoder(c.max_objects, c.bbox_embed_dim, D, c.num_object_classes)
-        self.ego_encoder = EgoStateEncoder(c.ego_state_dim, D)
-        self.temporal_encoder = TemporalEnvironmentalEncoder(c.time_embed_dim, c.weather_embed_dim, D)
+        self.camera_encoder = CameraEncoder(c.camera_embed_dim, D, c.num_cameras, c.image_size, c.dropout)
+        self.road_encoder = RoadTopologyEncoder(c.road_embed_dim, D, c.max_waypoints, c.max_lanes,
+                                                num_heads=c.road_cross_attn_heads, dropout=c.dropout)
+        self.bbox_encoder = BoundingBox3DEncoder(c.bbox_embed_dim, D, c.max_objects, c.num_object_classes,
+                                                 dropout=c.dropout)
+        self.ego_encoder = EgoStateEncoder(c.ego_state_dim, D, dropout=c.dropout)
+        self.temporal_encoder = TemporalEnvironmentalEncoder(c.time_embed_dim, c.weather_embed_dim, D,
+                                                             dropout=c.dropout)
         self.null_tokens = nn.Parameter(torch.zeros(len(self.MODALITIES), D))
         self.fusion = nn.Sequential(nn.Linear(len(self.MODALITIES) * D, 2 * D), nn.SiLU(),
                                     nn.Dropout(c.dropout), nn.Linear(2 * D, D))
@@ -346,5 +352,11 @@ class ConditioningIntegration(nn.Module):
         return uncond_out + cfg_scale * (cond_out - uncond_out)
 
 
-def create_conditioning_module(model_dim: int = 512, cond_dim: int = 256, **kw) -> ConditioningIntegration:
-    return ConditioningIntegration(ConditioningConfig(model_dim=model_dim, cond_dim=cond_dim, **kw))
+def create_conditioning_module(model_dim: int = 512, cond_dim: int = 256, num_cameras: int = 6,
+                               max_waypoints: int = 50, max_objects: int = 64,
+                               cfg_dropout_prob: float = 0.1, dropout: float = 0.1,
+                               **kw) -> ConditioningIntegration:
+    """(models/conditioning.py:1447-1475); other :class:`ConditioningConfig` fields by keyword."""
+    return ConditioningIntegration(ConditioningConfig(
+        model_dim=model_dim, cond_dim=cond_dim, num_cameras=num_cameras, max_waypoints=max_waypoints,
+        max_objects=max_objects, cfg_dropout_prob=cfg_dropout_prob, dropout=dropout, **kw))
