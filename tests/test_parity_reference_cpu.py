@@ -455,3 +455,34 @@ def test_utility_signatures_and_semantics(ref):
     h = torch.randn(5, 32)
     _close(o(h), r(h))
     assert isinstance(create_dit_block(64, 4, "standard", d_ff=128), DiTBlock)
+
+
+def test_video_dataset(ref, tmp_path):
+    """The reference's image-folder dataset and this one read the same directory into the
+    same samples (start indices, frames, controls, depth)."""
+    import importlib
+    import json
+
+    import cv2
+    import numpy as np
+    rv = importlib.import_module("data.video_loader")
+    from drivedit_b200.data.video_loader import VideoDataset
+    rng = np.random.default_rng(0)
+    for s in range(2):
+        d = tmp_path / "train" / f"seq{s}"
+        (d / "depth").mkdir(parents=True)
+        for i in range(9 + s):
+            cv2.imwrite(str(d / f"{i:04d}.png"), rng.integers(0, 256, (12, 20, 3), dtype=np.uint8))
+            cv2.imwrite(str(d / "depth" / f"{i:04d}.png"), rng.integers(0, 65535, (12, 20), dtype=np.uint16))
+        (d / "controls.json").write_text(json.dumps({"controls": [
+            {"steering": float(rng.random()), "acceleration": 0.5, "goal_x": 1.0, "goal_y": -1.0}
+            for _ in range(9 + s)]}))
+    kw = dict(sequence_length=4, frame_skip=2, image_size=(12, 20), load_depth=True)
+    r, o = rv.VideoDataset(tmp_path, **kw), VideoDataset(tmp_path, **kw)
+    key = lambda sq: sq["sequence_id"]
+    assert sorted(map(key, r.sequences)) == sorted(map(key, o.sequences)) and len(r) == len(o)
+    rs = {(r.sequences[i]["sequence_id"], s): n for n, (i, s) in enumerate(r.sequence_indices)}
+    for n, (i, s) in enumerate(o.sequence_indices):
+        a, b = o[n], r[rs[(o.sequences[i]["sequence_id"], s)]]
+        for k in ("frames", "controls", "depth"):
+            _close(a[k], b[k], 1e-6)
