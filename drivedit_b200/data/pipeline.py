@@ -15,7 +15,7 @@ import queue
 import random
 import threading
 from pathlib import Path
-from typing import Any, Dict, Iterator, List, Optional, Sequence, Tuple
+from typing import Any, Dict, Iterator, List, Optional, Sequence, Tuple, Union
 
 import numpy as np
 import torch
@@ -78,36 +78,74 @@ class VideoMemoryMap:
 
 
 class DrivingDataset(Dataset):
-    """Windows of ``sequence_length`` frames (+ per-frame controls) over memory-mapped
-    videos; ``controls[i]`` is an ``[N_i, A]`` array for video ``i``."""
+    """Windows of ``sequence_length`` frames ``stride`` frames apart over memory-mapped
+    videos (the reference's arguments, data/pipeline.py:134-226): ``video_paths`` are
+    video files (cached on first use under ``cache_dir``) or :class:`VideoMemoryMap`
+    objects; a window may start at any frame that leaves room for it. Frames are resized
+    to ``image_size``; with ``augment``, half of the windows get one brightness /
+    contrast change and one horizontal flip decision for all their frames.
+    ``controls[i]`` (``[N_i, A]``) adds per-frame controls. Returns ``frames``,
+    ``video_idx``, ``start_frame`` (and ``controls``)."""
 
-    def __init__(self, videos: List[VideoMemoryMap], controls: Optional[List[np.ndarray]] = None,
-                 sequence_length: int = 16, stride: int = 1):
-        self.videos, self.controls = videos, controls
-        self.sequence_length, self.stride = sequence_length, stride
-        self.index = [(vi, s) for vi, v in enumerate(videos)
-                      for s in range(0, len(v) - sequence_length + 1, stride)]
+    def __init__(self, video_paths: Sequence, sequence_length: int = 16,
+                 image_size: Tuple[int, int] = (256, 256), cache_dir: Optional[str] = None,
+                 stride: int = 1, augment: bool = True, controls: Optional[List[np.ndarray]] = None):
+        self.videos = [v if isinstance(v, VideoMemoryMap) else VideoMemoryMap(str(v), cache_dir)
+                       for v in video_paths]
+        self.video_paths = [str(v.video_path) for v in self.videos]
+        self.sequence_length, self.stride = sequence_length, max(1, stride)
+        self.image_size = tuple(image_size) if image_size is not None else None
+        self.augment, self.controls = augment, controls
+        span = (sequence_length - 1) * self.stride + 1
+        self.index = [(vi, s) for vi, v in enumerate(self.videos) for s in range(0, len(v) - span + 1)]
 
     def __len__(self):
         return len(self.index)
 
+    def _augment_sequence(self, frames: torch.Tensor) -> torch.Tensor:
+        if random.random() < 0.3:
+            gain = 0.8 + 0.4 * random.random()       # contrast
+            shift = 0.8 + 0.4 * random.random() - 1  # brightness
+            frames = (frames * gain + shift).clamp(0, 1)
+        if random.random() < 0.5:
+            frames = frames.flip(-1)
+        return frames
+
     def __getitem__(self, i):
         vi, s = self.index[i]
-        idx = list(range(s, s + self.sequence_length))
-        out = {"frames": self.videos[vi].get_batch(idx)}
+        idx = list(range(s, s + self.sequence_length * self.stride, self.stride))
+        frames = self.videos[vi].get_batch(idx)
+        if self.image_size is not None and tuple(frames.shape[-2:]) != self.image_size:
+            frames = torch.nn.functional.interpolate(frames, size=self.image_size, mode="bilinear",
+                                                     align_corners=False)
+        if self.augment and random.random() < 0.5:
+            frames = self._augment_sequence(frames)
+        out = {"frames": frames, "video_idx": vi, "start_frame": s}
         if self.controls is not None:
-            out["controls"] = torch.from_numpy(np.asarray(self.controls[vi][s:s + self.sequence_length],
-                                                          dtype=np.float32))
+            out["controls"] = torch.from_numpy(np.asarray(self.controls[vi][idx], dtype=np.float32))
         return out
 
 
 class StreamingDataLoader:
-    """Iterates a DataLoader and stages each batch on the device ahead of use: a
-    background thread pins host tensors, copies run on a side stream, and the consumer
-    waits on that stream's event only when it takes the batch."""
+    """Batches of a dataset staged on the device ahead of use: a background thread pins
+    host tensors, copies run on a side stream, and the consumer waits on that stream's
+    event only when it takes the batch. Built as the reference's (``dataset, batch_size,
+    num_workers, prefetch_factor, pin_memory``, data/pipeline.py:229-265: shuffled, last
+    partial batch dropped) or around an existing ``DataLoader`` (``device``, ``prefetch``)."""
 
-    def __init__(self, loader: DataLoader, device="cuda", prefetch: int = 2):
-        self.loader, self.device, self.prefetch = loader, torch.device(device), prefetch
+    def __init__(self, dataset, batch_size: int = 8, num_workers: int = 4, prefetch_factor: int = 2,
+                 pin_memory: bool = True, device="cuda", prefetch: Optional[int] = None):
+        if isinstance(dataset, DataLoader):
+            loader = dataset
+        else:
+            kw = dict(prefetch_factor=prefetch_factor, persistent_workers=True) if num_workers > 0 else {}
+            loader = DataLoader(dataset, batch_size=batch_size, shuffle=True, num_workers=num_workers,
+                                drop_last=True, **kw)
+        self.dataset = getattr(loader, "dataset", dataset)
+        self.batch_size, self.pin_memory = batch_size, pin_memory
+        self.loader = self.dataloader = loader
+        self.device = torch.device(device if (str(device) != "cuda" or torch.cuda.is_available()) else "cpu")
+        self.prefetch = prefetch if prefetch is not None else max(1, prefetch_factor)
 
     def __len__(self):
         return len(self.loader)
@@ -115,7 +153,8 @@ class StreamingDataLoader:
     def _to_device(self, batch, stream):
         def mv(x):
             if torch.is_tensor(x):
-                x = x.pin_memory() if not x.is_pinned() else x
+                if self.device.type == "cuda" and not x.is_pinned():
+                    x = x.pin_memory()
                 return x.to(self.device, non_blocking=True)
             if isinstance(x, dict):
                 return {k: mv(v) for k, v in x.items()}
@@ -158,7 +197,27 @@ class StreamingDataLoader:
 
 class DatasetSplitter:
     @staticmethod
+    def split_by_video(video_paths: Sequence[str], train_ratio: float = 0.8, val_ratio: float = 0.1,
+                       seed: Optional[int] = None) -> Tuple[List[str], List[str], List[str]]:
+        """Whole videos to train / val / test (no window of one video in two splits)."""
+        paths = list(video_paths)
+        random.Random(seed).shuffle(paths)
+        n_tr, n_va = int(len(paths) * train_ratio), int(len(paths) * val_ratio)
+        return paths[:n_tr], paths[n_tr:n_tr + n_va], paths[n_tr + n_va:]
+
+    @staticmethod
+    def create_datasets(video_paths: Sequence[str], sequence_length: int = 16,
+                        image_size: Tuple[int, int] = (256, 256), cache_dir: Optional[str] = None,
+                        seed: Optional[int] = None, **kwargs):
+        """(train, val, test) :class:`DrivingDataset` of a video-level split; augmentation
+        on the training set only."""
+        tr, va, te = DatasetSplitter.split_by_video(video_paths, seed=seed)
+        return tuple(DrivingDataset(p, sequence_length, image_size, cache_dir, augment=(i == 0), **kwargs)
+                     for i, p in enumerate((tr, va, te)))
+
+    @staticmethod
     def split(dataset: Dataset, ratios: Sequence[float] = (0.8, 0.1, 0.1), seed: int = 0) -> List[Subset]:
+        """Random subsets of a dataset's items in the given proportions."""
         n = len(dataset)
         perm = torch.randperm(n, generator=torch.Generator().manual_seed(seed)).tolist()
         out, s = [], 0
@@ -169,11 +228,17 @@ class DatasetSplitter:
         return out
 
 
-def create_efficient_pipeline(videos: List[VideoMemoryMap], controls=None, sequence_length: int = 16,
-                              batch_size: int = 4, num_workers: int = 2, device="cuda",
-                              split=(0.9, 0.1), seed: int = 0):
-    ds = DrivingDataset(videos, controls, sequence_length)
-    parts = DatasetSplitter.split(ds, split, seed)
-    mk = lambda d, sh: StreamingDataLoader(DataLoader(d, batch_size=batch_size, shuffle=sh,
-                                                      num_workers=num_workers, drop_last=sh), device)
-    return [mk(p, i == 0) for i, p in enumerate(parts)]
+def create_efficient_pipeline(video_dir: Union[str, Path, Sequence], batch_size: int = 8,
+                              sequence_length: int = 16, image_size: Tuple[int, int] = (256, 256),
+                              cache_dir: Optional[str] = None, num_workers: int = 4, device="cuda",
+                              seed: Optional[int] = None):
+    """(train, val, test) :class:`StreamingDataLoader` over the ``*.mp4`` / ``*.avi`` /
+    ``*.mov`` videos of ``video_dir`` (or a list of paths / :class:`VideoMemoryMap`),
+    split by video (data/pipeline.py:341-381)."""
+    if isinstance(video_dir, (str, Path)):
+        d = Path(video_dir)
+        videos = sorted(str(p) for ext in ("*.mp4", "*.avi", "*.mov") for p in d.glob(ext))
+    else:
+        videos = list(video_dir)
+    splits = DatasetSplitter.create_datasets(videos, sequence_length, image_size, cache_dir, seed=seed)
+    return tuple(StreamingDataLoader(ds, batch_size, num_workers, device=device) for ds in splits)

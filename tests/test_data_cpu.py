@@ -166,7 +166,16 @@ def test_transforms_collate_samplers(tmp_path):
     vm = VideoMemoryMap(str(tmp_path / "clip.mp4"), frames=frames)
     vm2 = VideoMemoryMap(str(tmp_path / "clip.mp4"))  # reopens the cache
     assert torch.allclose(vm2.get_batch([3])[0], torch.from_numpy(frames[3]).permute(2, 0, 1).float() / 255)
-    ds = DrivingDataset([vm], [np.zeros((12, 6))], sequence_length=4)
+    ds = DrivingDataset([vm], sequence_length=4, image_size=(8, 10), augment=False,
+                        controls=[np.arange(72, dtype=np.float32).reshape(12, 6)])
     assert len(ds) == 9 and ds[0]["controls"].shape == (4, 6)
     parts = DatasetSplitter.split(ds, (0.5, 0.5))
     assert len(parts[0]) + len(parts[1]) == 9
+    ds2 = DrivingDataset([vm], 4, (4, 5), None, 3, False, [np.arange(12, dtype=np.float32)[:, None]])
+    x = ds2[1]                     # frames 1, 4, 7, 10 resized to 4 x 5
+    assert len(ds2) == 12 - 9 and x["frames"].shape == (4, 3, 4, 5) and x["controls"][:, 0].tolist() == [1, 4, 7, 10]
+    tr, va, te = DatasetSplitter.split_by_video([f"v{i}" for i in range(10)], 0.6, 0.2, seed=0)
+    assert (len(tr), len(va), len(te)) == (6, 2, 2) and not set(tr) & set(te)
+    from drivedit_b200.data.pipeline import StreamingDataLoader
+    sl = StreamingDataLoader(ds, batch_size=2, num_workers=0, device="cpu")
+    assert len(sl) == 4 and next(iter(sl))["frames"].shape == (2, 4, 3, 8, 10)
