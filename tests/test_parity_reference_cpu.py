@@ -486,3 +486,41 @@ def test_video_dataset(ref, tmp_path):
         a, b = o[n], r[rs[(o.sequences[i]["sequence_id"], s)]]
         for k in ("frames", "controls", "depth"):
             _close(a[k], b[k], 1e-6)
+
+
+def test_preprocessing_stages(ref):
+    """The reference's video / latent / control preprocessors and this framework's give
+    the same outputs on the same batch."""
+    import importlib
+    rp = importlib.import_module("data.preprocessing")
+    from drivedit_b200.data import preprocessing as op
+    torch.manual_seed(0)
+    frames = torch.rand(2, 3, 3, 20, 24) * 255
+    for norm in (True, False):
+        rv, ov = rp.VideoPreprocessor((16, 16), norm), op.VideoPreprocessor((16, 16), norm)
+        _close(ov.preprocess_batch(frames), rv.preprocess_batch(frames))
+        x = ov.preprocess_batch(frames)
+        _close(ov.denormalize(x), rv.denormalize(x))
+    lat = torch.randn(2, 3, 4, 6, 6)
+    rl, ol = rp.LatentPreprocessor(4, (8, 8), True, (-2.0, 2.0)), op.LatentPreprocessor(4, (8, 8), True, (-2.0, 2.0))
+    _close(ol.preprocess_latents(lat), rl.preprocess_latents(lat))
+    t = ol.tokenize_latents(ol.preprocess_latents(lat))
+    _close(ol.detokenize_latents(t), rl.detokenize_latents(t))
+    ctl = torch.randn(2, 9, 4) * 3
+    for smooth in (True, False):
+        rc, oc = rp.ControlPreprocessor(4, True, None, smooth, 3), op.ControlPreprocessor(4, True, None, smooth, 3)
+        _close(oc.preprocess_controls(ctl), rc.preprocess_controls(ctl))
+        _close(oc.preprocess_controls(ctl[0]), rc.preprocess_controls(ctl[0]))
+        y = oc.preprocess_controls(ctl)
+        _close(oc.denormalize_controls(y), rc.denormalize_controls(y))
+    _close(oc.interpolate_controls(ctl, 15), rc.interpolate_controls(ctl, 15))
+    batch = {"frames": frames, "latents": lat, "controls": ctl, "id": 3}
+    rpipe = rp.DataPreprocessingPipeline(rp.VideoPreprocessor(), rp.LatentPreprocessor(4, (6, 6)),
+                                         rp.ControlPreprocessor())
+    opipe = op.DataPreprocessingPipeline(op.VideoPreprocessor(), op.LatentPreprocessor(4, (6, 6)),
+                                         op.ControlPreprocessor())
+    a, b = opipe(batch), rpipe(batch)
+    assert a["id"] == 3
+    for k in ("frames", "latents", "controls"):
+        _close(a[k], b[k])
+    assert opipe.get_preprocessor_configs() == rpipe.get_preprocessor_configs()
