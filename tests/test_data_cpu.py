@@ -151,7 +151,8 @@ def test_transforms_collate_samplers(tmp_path):
     b = VideoCollator()(batch)
     assert b["frames"].shape == (2, 5, 3, 4, 4) and b["sequence_mask"].sum() == 8 and b["id"] == [3, 5]
     assert ChunkedBatchCollator(chunk_size=2, overlap=1)(batch)["frames"].shape[1] == 2
-    assert len(MemoryEfficientCollator(max_memory_mb=1e-4)(batch)["id"]) == 1
+    assert len(MemoryEfficientCollator(frame_memory_limit_mb=1e-4)(batch)["id"]) == 1
+    assert len(MemoryEfficientCollator(max_batch_frames=10 ** 6)(batch)["id"]) == len(batch)
     ts = TemporalSampler([10, 3, 20], window=4, stride=4)
     assert len(ts) == 2 + 0 + 5 and sorted(ts) == list(range(7))
     bs = BalancedSampler(["a"] * 9 + ["b"], num_samples=2000)

@@ -524,3 +524,26 @@ def test_preprocessing_stages(ref):
     for k in ("frames", "latents", "controls"):
         _close(a[k], b[k])
     assert opipe.get_preprocessor_configs() == rpipe.get_preprocessor_configs()
+
+
+def test_collators(ref):
+    import importlib
+    rc = importlib.import_module("data.collate")
+    from drivedit_b200.data import collate as oc
+    torch.manual_seed(0)
+    batch = [{"frames": torch.rand(n, 3, 4, 4), "controls": torch.rand(n, 4), "sequence_id": f"s{n}"}
+             for n in (3, 6, 5)]
+    for kw in (dict(), dict(max_sequence_length=4), dict(max_sequence_length=5, drop_incomplete=True),
+               dict(padding_value=-1.0)):
+        a, b = oc.VideoCollator(**kw)(batch), rc.VideoCollator(**kw)(batch)
+        for k in ("frames", "controls"):
+            _close(a[k], b[k])
+        assert a["sequence_id"] == b["sequence_id"]
+    for tok, lens in ((True, (4, 4)), (False, (2, 4))):  # the reference re-stacks raw latents when tokenising
+        lat = [{"latents": torch.randn(t, 2, 3, 3)} for t in lens]
+        a, b = oc.LatentCollator(tok, 3)(lat), rc.LatentCollator(tok, 3)(lat)
+        k = "latent_tokens" if tok else "latents"
+        _close(a[k], b[k])
+    for kw in (dict(max_batch_frames=9), dict(frame_memory_limit_mb=1e-4), dict(adaptive_batching=False)):
+        a, b = oc.MemoryEfficientCollator(**kw)(batch), rc.MemoryEfficientCollator(**kw)(batch)
+        _close(a["frames"], b["frames"])
