@@ -153,16 +153,30 @@ def test_transforms_collate_samplers(tmp_path):
     assert ChunkedBatchCollator(chunk_size=2, overlap=1)(batch)["frames"].shape[1] == 2
     assert len(MemoryEfficientCollator(frame_memory_limit_mb=1e-4)(batch)["id"]) == 1
     assert len(MemoryEfficientCollator(max_batch_frames=10 ** 6)(batch)["id"]) == len(batch)
-    ts = TemporalSampler([10, 3, 20], window=4, stride=4)
-    assert len(ts) == 2 + 0 + 5 and sorted(ts) == list(range(7))
-    bs = BalancedSampler(["a"] * 9 + ["b"], num_samples=2000)
-    assert 0.3 < sum(1 for i in bs if i == 9) / 2000 < 0.7
-    assert sorted(ChunkedSampler(10, 3)) == list(range(10))
-    sc = list(SequentialChunkSampler([5, 3], chunk_size=2, shuffle=False))
-    assert sc == list(range(8))
-    ad = AdaptiveSampler(4, warmup_updates=1)
-    ad.update_difficulty_scores([0, 1, 2, 3], [1e-6, 1e-6, 1e-6, 1.0])
-    assert ad.get_current_strategy() == "difficulty" and sum(1 for i in ad if i == 3) >= 3
+    class _Seqs(torch.utils.data.Dataset):      # sequence structure as VideoDataset exposes it
+        sequences = [{"num_frames": 10}, {"num_frames": 3}, {"num_frames": 20}]
+        sequence_indices = [(0, 0), (0, 4), (2, 0), (2, 4), (2, 8), (2, 12)]
+
+        def __len__(self):
+            return len(self.sequence_indices)
+
+        def __getitem__(self, i):
+            return {"class_label": "a" if i < 5 else "b"}
+    ds_s = _Seqs()
+    ts = TemporalSampler(ds_s, "sparse", sequence_length=4, seed=0)
+    assert ts.temporal_indices == [(0, 0), (0, 4), (2, 0), (2, 4), (2, 8), (2, 12), (2, 16)]
+    assert sorted(ts) == list(range(7)) and list(ts) == list(ts)        # seeded: repeatable
+    assert len(TemporalSampler(ds_s, "dense", sequence_length=4)) == 7 + 17
+    bs = BalancedSampler(ds_s, seed=0)
+    assert {k: len(v) for k, v in bs.class_indices.items()} == {"a": 5, "b": 1}
+    assert bs.get_class_distribution() == {"a": 5, "b": 5} and len(bs) == 10
+    assert sorted(ChunkedSampler(ds_s, chunk_size=3, overlap=1, shuffle_chunks=False)) == [0, 1, 2, 2, 3, 4, 4, 5]
+    sc = list(SequentialChunkSampler(ds_s, sequences_per_chunk=2))
+    assert sc == [0, 1, 2, 3, 4, 5]
+    ad = AdaptiveSampler(ds_s, adaptation_frequency=1, seed=0)
+    ad.update_difficulty_scores(list(range(100)), [0.0, 1.0] * 50)
+    list(ad)
+    assert ad.get_current_strategy() == "balanced"
     frames = np.random.default_rng(0).integers(0, 256, (12, 8, 10, 3), dtype=np.uint8)
     vm = VideoMemoryMap(str(tmp_path / "clip.mp4"), frames=frames)
     vm2 = VideoMemoryMap(str(tmp_path / "clip.mp4"))  # reopens the cache

@@ -547,3 +547,36 @@ def test_collators(ref):
     for kw in (dict(max_batch_frames=9), dict(frame_memory_limit_mb=1e-4), dict(adaptive_batching=False)):
         a, b = oc.MemoryEfficientCollator(**kw)(batch), rc.MemoryEfficientCollator(**kw)(batch)
         _close(a["frames"], b["frames"])
+
+
+def test_samplers(ref):
+    """Window starts, class balancing and chunk structure as the reference's samplers
+    (orders are random in both, so the index sets are compared)."""
+    import importlib
+    rs = importlib.import_module("data.sampler")
+    from drivedit_b200.data import sampler as os_
+
+    class Seqs(torch.utils.data.Dataset):
+        sequences = [{"num_frames": n} for n in (10, 3, 40, 17)]
+        sequence_indices = [(q, s) for q, n in enumerate((10, 3, 40, 17)) for s in range(0, n - 3, 3)]
+
+        def __len__(self):
+            return len(self.sequence_indices)
+
+        def __getitem__(self, i):
+            return {"class_label": "a" if i % 4 else "b"}
+    ds = Seqs()
+    for strat in ("uniform", "dense", "sparse", "adaptive"):
+        for stride in (1, 2):
+            kw = dict(sampling_strategy=strat, sequence_length=4, temporal_stride=stride, seed=0)
+            assert os_.TemporalSampler(ds, **kw).temporal_indices == rs.TemporalSampler(ds, **kw).temporal_indices
+    for over, under in ((True, False), (False, True), (True, True)):
+        a = os_.BalancedSampler(ds, oversample_minority=over, undersample_majority=under, seed=0)
+        b = rs.BalancedSampler(ds, oversample_minority=over, undersample_majority=under, seed=0)
+        assert a.get_class_distribution() == b.get_class_distribution() and len(a) == len(b)
+    for drop in (False, True):
+        a = os_.ChunkedSampler(ds, 5, 2, drop_incomplete=drop, seed=0)
+        b = rs.ChunkedSampler(ds, 5, 2, drop_incomplete=drop, seed=0)
+        assert a.chunks == b.chunks and sorted(a) == sorted(b)
+    a, b = os_.SequentialChunkSampler(ds, 4, seed=0), rs.SequentialChunkSampler(ds, 4, seed=0)
+    assert a.sequence_chunks == b.sequence_chunks and list(a) == list(b)
