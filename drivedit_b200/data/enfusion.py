@@ -364,30 +364,55 @@ class EnfusionDataLoader:
 
 
 def create_enfusion_dataloaders(data_root, config: Optional[EnfusionDatasetConfig] = None,
-                                batch_size: int = 4, num_workers: int = 2, val_fraction: float = 0.1,
-                                seed: int = 0, pin_memory: bool = True):
-    """Session-level train/val split -> (train_loader, val_loader)."""
+                                batch_size: int = 8, num_workers: int = 4, train_ratio: float = 0.8,
+                                val_ratio: float = 0.1, seed: Optional[int] = None, pin_memory: bool = True,
+                                device=None):
+    """(train, val, test) :class:`EnfusionDataLoader` (data/enfusion_loader.py:725-819):
+    ``train/`` and ``val/`` (and ``test/``, else ``val/`` again) folders when the root has
+    them, otherwise a session-level split of ``session_*`` by ``train_ratio`` /
+    ``val_ratio``. Training batches are shuffled (last partial batch dropped) and
+    augmented when the config asks; validation and test are not augmented."""
+    from dataclasses import replace
+
+    root = Path(data_root)
     config = config or EnfusionDatasetConfig()
-    full = EnfusionDataset(data_root, config)
-    names = [s.session_dir.name for s in full.sessions]
-    rng = random.Random(seed)
-    rng.shuffle(names)
-    nv = max(1, int(round(len(names) * val_fraction))) if len(names) > 1 else 0
-    val_ids, train_ids = names[:nv], names[nv:]
-    tr = EnfusionDataset(data_root, config, "train", train_ids, seed)
-    va = EnfusionDataset(data_root, config, "val", val_ids, seed) if val_ids else None
-    mk = lambda ds, sh: DataLoader(ds, batch_size=batch_size, shuffle=sh, num_workers=num_workers,
-                                   collate_fn=EnfusionCollator(), pin_memory=pin_memory, drop_last=sh)
-    return mk(tr, True), (mk(va, False) if va is not None else None)
+    evalc = replace(config, augment=False)
+    if (root / "train").is_dir() and (root / "val").is_dir():
+        tr = EnfusionDataset(root / "train", config, "train")
+        va = EnfusionDataset(root / "val", evalc, "val")
+        te = EnfusionDataset(root / "test" if (root / "test").is_dir() else root / "val", evalc, "test")
+    else:
+        names = sorted(p.name for p in root.glob("session_*") if p.is_dir())
+        random.Random(seed).shuffle(names)
+        n_tr, n_va = int(len(names) * train_ratio), int(len(names) * val_ratio)
+        tr = EnfusionDataset(root, config, "train", names[:n_tr])
+        va = EnfusionDataset(root, evalc, "val", names[n_tr:n_tr + n_va])
+        te = EnfusionDataset(root, evalc, "test", names[n_tr + n_va:])
+    mk = lambda ds, train: EnfusionDataLoader(ds, batch_size, shuffle=train and len(ds) > 0,
+                                              num_workers=num_workers, pin_memory=pin_memory,
+                                              drop_last=train, device=device)
+    return mk(tr, True), mk(va, False), mk(te, False)
 
 
 class EnfusionToDriveDiTAdapter:
-    """Dataset sample -> world-model inputs: frames scaled to [-1, 1] and the first
-    ``action_dim`` control channels as per-frame actions."""
+    """Loader batch -> training inputs (data/enfusion_loader.py:822-890): ``frames`` as
+    they are, ``controls`` zero-padded or cut to ``target_control_dim`` channels, depth,
+    ego transforms (when included and present) and anchor masks."""
 
-    def __init__(self, action_dim: int = 3):
-        self.action_dim = action_dim
+    def __init__(self, target_control_dim: int = 6, include_depth: bool = True,
+                 include_ego_transform: bool = True):
+        self.target_control_dim = target_control_dim
+        self.include_depth, self.include_ego_transform = include_depth, include_ego_transform
 
     def __call__(self, batch: Dict[str, Any]) -> Dict[str, torch.Tensor]:
-        return {"frames": batch["frames"] * 2 - 1, "actions": batch["controls"][..., :self.action_dim],
-                "controls": batch["controls"], "ego_transform": batch["ego_transform"]}
+        c = batch["controls"]
+        d = self.target_control_dim
+        c = F.pad(c, (0, d - c.shape[-1])) if c.shape[-1] < d else c[..., :d]
+        out = {"frames": batch["frames"], "controls": c}
+        if self.include_depth and batch.get("depth") is not None:
+            out["depth"] = batch["depth"]
+        if self.include_ego_transform and batch.get("ego_transform") is not None:
+            out["ego_transform"] = batch["ego_transform"]
+        if batch.get("anchor_mask") is not None:
+            out["anchor_mask"] = batch["anchor_mask"]
+        return out

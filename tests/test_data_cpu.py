@@ -117,8 +117,12 @@ def test_enfusion_dataset(tmp_path):
     assert x["metadata"]["map"] == "everon"
     b = EnfusionCollator()([ds[0], ds[1]])
     assert b["frames"].shape == (2, 4, 3, 16, 32)
-    tr, va = create_enfusion_dataloaders(tmp_path, cfg, batch_size=2, num_workers=0, pin_memory=False)
-    assert len(tr.dataset) + len(va.dataset) == len(ds)
+    tr, va, te = create_enfusion_dataloaders(tmp_path, cfg, batch_size=2, num_workers=0, pin_memory=False,
+                                             train_ratio=0.5, val_ratio=0.0, seed=0, device="cpu")
+    assert len(tr.dataset) + len(va.dataset) + len(te.dataset) == len(ds) and len(va.dataset) == 0
+    from drivedit_b200.data.enfusion import EnfusionToDriveDiTAdapter
+    ad = EnfusionToDriveDiTAdapter(8)(next(iter(tr)))
+    assert ad["controls"].shape[-1] == 8 and "anchor_mask" in ad
     from drivedit_b200.data.enfusion import EnfusionDataLoader
     dl = EnfusionDataLoader(ds, batch_size=3, num_workers=0, device="cpu")
     batches = list(dl)
