@@ -15,6 +15,7 @@ its role is taken by that service.
 """
 from __future__ import annotations
 
+import logging
 import random
 import time
 from collections import defaultdict, deque
@@ -81,6 +82,7 @@ class NativeEnfusionDataset(EnfusionDataset):
 
 class NativeCollator(EnfusionCollator):
     def __init__(self, include_depth: bool = True):
+        super().__init__()
         self.include_depth = include_depth
 
     def __call__(self, batch):
@@ -217,68 +219,180 @@ def benchmark_native_vs_python(data_root, config: Optional[NativeDatasetConfig] 
 # ----------------------------------------------------------------------------- hybrid
 @dataclass
 class HybridLoaderConfig:
-    prefer_native: bool = True
+    """The reference's loader settings (data/hybrid_loader.py:63-125). ``prefer_rust``
+    selects the native (C++) runtime when it is built; ``use_batch_loader`` its batch
+    loader (one native call decodes a whole batch). The Go prefetch-service fields are
+    accepted and unused: there is no such service; the native loader prefetches."""
+    sequence_length: int = 16
+    frame_skip: int = 1
+    image_size: Tuple[int, int] = (256, 256)
+    load_depth: bool = True
+    load_controls: bool = True
+    control_dim: int = 6
     batch_size: int = 8
-    num_workers: int = 0
+    num_workers: int = 4
+    shuffle: bool = True
+    drop_last: bool = True
+    pin_memory: bool = True
+    prefetch_factor: int = 2
+    cache_frames: bool = True
+    max_cache_mb: float = 1000.0
+    prefer_rust: bool = True
+    use_batch_loader: bool = True
+    go_prefetch_enabled: bool = False
+    go_prefetch_address: str = "localhost:50051"
+    go_prefetch_buffer_size: int = 16
     track_performance: bool = True
+    log_interval: int = 100
+
+    @property
+    def prefer_native(self) -> bool:
+        return self.prefer_rust
+
+    def to_rust_config(self) -> NativeDatasetConfig:
+        return NativeDatasetConfig(sequence_length=self.sequence_length, frame_skip=self.frame_skip,
+                                   image_height=self.image_size[0], image_width=self.image_size[1],
+                                   load_depth=self.load_depth, load_controls=self.load_controls,
+                                   control_dim=self.control_dim, cache_frames=self.cache_frames,
+                                   max_cache_mb=self.max_cache_mb, num_workers=self.num_workers)
+
+    to_native_config = to_rust_config
+
+    def to_python_config(self) -> EnfusionDatasetConfig:
+        return self.to_rust_config().to_enfusion_config()
 
 
 class PerformanceTracker:
-    """Per-source batch timing (seconds between yielded batches)."""
+    """Batch load times and throughput; a summary is logged every ``log_interval``
+    batches."""
 
-    def __init__(self, window: int = 100):
-        self.times: Dict[str, deque] = defaultdict(lambda: deque(maxlen=window))
+    def __init__(self, log_interval: int = 100):
+        self.log_interval = log_interval
+        self.reset()
 
-    def record(self, source: str, seconds: float):
-        self.times[source].append(seconds)
+    def reset(self):
+        self.load_times: List[float] = []
+        self.batch_count = self.total_samples = 0
+        self.start_time = time.time()
 
-    def summary(self) -> Dict[str, Dict[str, float]]:
-        return {k: {"batches": len(v), "mean_s": float(np.mean(v)) if v else 0.0,
-                    "batches_per_s": float(1 / np.mean(v)) if v and np.mean(v) > 0 else 0.0}
-                for k, v in self.times.items()}
+    def record_batch(self, load_time: float, batch_size: int):
+        self.load_times.append(load_time)
+        self.batch_count += 1
+        self.total_samples += batch_size
+        if self.log_interval and self.batch_count % self.log_interval == 0:
+            st = self.get_stats()
+            logging.getLogger(__name__).info("batch %d: %.1f ms per batch, %.1f samples/s", self.batch_count,
+                                             st["avg_load_time_ms"], st["samples_per_sec"])
+
+    def get_stats(self) -> Dict[str, float]:
+        if not self.load_times:
+            return {}
+        dt = time.time() - self.start_time
+        return {"batch_count": self.batch_count, "total_samples": self.total_samples, "total_time_sec": dt,
+                "avg_load_time_ms": float(np.mean(self.load_times)) * 1000.0,
+                "samples_per_sec": self.total_samples / dt if dt > 0 else 0.0}
 
 
 class HybridDataLoader:
-    """The native batch loader when the runtime is built, else a torch DataLoader over the
-    Python dataset; records per-batch timing either way."""
+    """The native batch loader when the runtime is built (and preferred), else a torch
+    DataLoader over the Python dataset (data/hybrid_loader.py:255-427); records the time
+    each batch took to arrive."""
 
-    def __init__(self, data_root, dataset_config: Optional[NativeDatasetConfig] = None,
-                 config: Optional[HybridLoaderConfig] = None):
-        self.config = config or HybridLoaderConfig()
-        cfg = dataset_config or NativeDatasetConfig()
-        self.tracker = PerformanceTracker()
-        if self.config.prefer_native and available():
-            self.source = "native"
-            self.loader = NativeBatchLoader(NativeEnfusionDataset(data_root, cfg), self.config.batch_size)
-        else:
-            self.source = "python"
-            self.loader = DataLoader(EnfusionDataset(data_root, cfg.to_enfusion_config()),
-                                     batch_size=self.config.batch_size, shuffle=True, drop_last=True,
-                                     num_workers=self.config.num_workers, collate_fn=EnfusionCollator())
+    def __init__(self, data_root, config: Optional[HybridLoaderConfig] = None, split: str = "train",
+                 session_ids: Optional[List[str]] = None):
+        self.data_root = Path(data_root)
+        self.config = c = config or HybridLoaderConfig()
+        self.split, self.session_ids = split, session_ids
+        self._use_native = c.prefer_rust and available()
+        self._backend_name = "rust" if self._use_native else "python"
+        self._performance_tracker = PerformanceTracker(c.log_interval) if c.track_performance else None
+        self._loader = self._create_loader()
+
+    def _create_loader(self):
+        c = self.config
+        if self._use_native:
+            ds = NativeEnfusionDataset(self.data_root, c.to_rust_config(), self.split, session_ids=self.session_ids)
+            if c.use_batch_loader:
+                return NativeBatchLoader(ds, c.batch_size, shuffle=c.shuffle and len(ds) > 0)
+            return NativeDataLoader(ds, c.batch_size, shuffle=c.shuffle and len(ds) > 0, num_workers=c.num_workers)
+        ds = EnfusionDataset(self.data_root, c.to_python_config(), self.split, self.session_ids)
+        kw = dict(prefetch_factor=c.prefetch_factor) if c.num_workers > 0 else {}
+        return DataLoader(ds, batch_size=c.batch_size, shuffle=c.shuffle and len(ds) > 0,
+                          drop_last=c.drop_last, num_workers=c.num_workers,
+                          pin_memory=c.pin_memory and torch.cuda.is_available(),
+                          collate_fn=EnfusionCollator(), **kw)
+
+    @property
+    def backend(self) -> str:
+        return self._backend_name
+
+    @property
+    def is_rust(self) -> bool:
+        return self._use_native
 
     def __iter__(self):
         t = time.perf_counter()
-        for b in self.loader:
+        for b in self._loader:
             now = time.perf_counter()
-            if self.config.track_performance:
-                self.tracker.record(self.source, now - t)
+            if self._performance_tracker is not None:
+                x = b.get("frames", b.get("controls")) if isinstance(b, dict) else None
+                self._performance_tracker.record_batch(now - t, int(x.shape[0]) if x is not None else 0)
             t = now
             yield b
 
     def __len__(self):
-        return len(self.loader)
+        return len(self._loader)
 
-    def get_performance_stats(self):
-        return self.tracker.summary()
+    def get_performance_stats(self) -> Dict[str, float]:
+        return self._performance_tracker.get_stats() if self._performance_tracker is not None else {}
+
+    def reset_performance_stats(self):
+        if self._performance_tracker is not None:
+            self._performance_tracker.reset()
+
+    def cache_stats(self) -> Dict[str, float]:
+        for obj in (self._loader, getattr(self._loader, "dataset", None)):
+            if obj is not None and hasattr(obj, "cache_stats"):
+                return obj.cache_stats()
+        return {}
+
+    def clear_cache(self):
+        for obj in (self._loader, getattr(self._loader, "dataset", None)):
+            if obj is not None and hasattr(obj, "clear_cache"):
+                obj.clear_cache()
+                return
+
+    def close(self):
+        pass
 
 
-def create_hybrid_dataloaders(data_root, dataset_config: Optional[NativeDatasetConfig] = None,
-                              config: Optional[HybridLoaderConfig] = None):
-    return HybridDataLoader(data_root, dataset_config, config)
+def create_hybrid_dataloaders(data_root, config: Optional[HybridLoaderConfig] = None,
+                              train_ratio: float = 0.8, val_ratio: float = 0.1, seed: Optional[int] = None):
+    """(train, val, test) loaders from ``train/`` / ``val/`` (/ ``test/``) folders or a
+    session-level split of ``session_*``; validation and test are not shuffled."""
+    from dataclasses import replace
+
+    root = Path(data_root)
+    config = config or HybridLoaderConfig()
+    evalc = replace(config, shuffle=False)
+    if (root / "train").is_dir() and (root / "val").is_dir():
+        return (HybridDataLoader(root / "train", config, "train"),
+                HybridDataLoader(root / "val", evalc, "val"),
+                HybridDataLoader(root / "test" if (root / "test").is_dir() else root / "val", evalc, "test"))
+    names = sorted(p.name for p in root.glob("session_*") if p.is_dir())
+    random.Random(seed).shuffle(names)
+    n_tr, n_va = int(len(names) * train_ratio), int(len(names) * val_ratio)
+    return (HybridDataLoader(root, config, "train", names[:n_tr]),
+            HybridDataLoader(root, evalc, "val", names[n_tr:n_tr + n_va]),
+            HybridDataLoader(root, evalc, "test", names[n_tr + n_va:]))
 
 
-def get_best_loader(data_root, dataset_config: Optional[NativeDatasetConfig] = None, batch_size: int = 8):
-    return HybridDataLoader(data_root, dataset_config, HybridLoaderConfig(batch_size=batch_size))
+def get_best_loader(data_root, batch_size: int = 8, sequence_length: int = 16,
+                    image_size: Tuple[int, int] = (256, 256), **kwargs) -> HybridDataLoader:
+    """One loader on the fastest available backend (other :class:`HybridLoaderConfig`
+    fields by keyword)."""
+    return HybridDataLoader(data_root, HybridLoaderConfig(batch_size=batch_size, sequence_length=sequence_length,
+                                                          image_size=tuple(image_size), **kwargs))
 
 
 # names of the reference's compiled-loader API

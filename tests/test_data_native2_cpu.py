@@ -167,12 +167,17 @@ def test_native_batch_loader_matches_dataset(tmp_path):
         assert b0["anchor_mask"][j].tolist() == ref["anchor_mask"].tolist()
     tr, va = nl.create_rust_dataloaders(tmp_path, cfg, batch_size=2, val_fraction=0.34)
     assert len(tr.dataset) + len(va.dataset) == len(ds)
-    hy = nl.get_best_loader(tmp_path, cfg, batch_size=2)
-    assert hy.source == "native"
+    hcfg = dict(sequence_length=3, frame_skip=2, image_size=(16, 24), load_depth=False, num_workers=0)
+    hy = nl.get_best_loader(tmp_path, 2, **{k: v for k, v in hcfg.items() if k != "sequence_length"},
+                            sequence_length=3)
+    assert hy.backend == "rust" and hy.is_rust
     n = sum(1 for _ in hy)
-    assert n == len(hy) and hy.get_performance_stats()["native"]["batches"] == n
-    py = nl.HybridDataLoader(tmp_path, cfg, nl.HybridLoaderConfig(prefer_native=False, batch_size=2))
-    assert py.source == "python" and next(iter(py))["frames"].shape == (2, 3, 3, 16, 24)
+    assert n == len(hy) and hy.get_performance_stats()["batch_count"] == n
+    py = nl.HybridDataLoader(tmp_path, nl.HybridLoaderConfig(prefer_rust=False, batch_size=2, **hcfg))
+    assert py.backend == "python" and next(iter(py))["frames"].shape == (2, 3, 3, 16, 24)
+    tr, va, te = nl.create_hybrid_dataloaders(tmp_path, nl.HybridLoaderConfig(batch_size=2, **hcfg),
+                                              train_ratio=0.34, val_ratio=0.34, seed=0)
+    assert sum(len(l._loader.dataset) for l in (tr, va, te)) == len(ds)
     r = nl.benchmark_rust_vs_python(tmp_path, cfg, batch_size=2, num_batches=2)
     assert r["native_batches_per_s"] > 0 and r["python_batches_per_s"] > 0
     assert nl.get_rust_version()
