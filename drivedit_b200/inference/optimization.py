@@ -499,12 +499,15 @@ def benchmark_inference(model: nn.Module, input_shape: Tuple[int, ...], device: 
     return r
 
 
-def profile_bottlenecks(model: nn.Module, example_input, device: str = "cuda", top_k: int = 20,
-                        num_iterations: int = 3) -> Dict[str, Any]:
-    """Device time per kernel (PyTorch profiler) over a few forward calls."""
+def profile_bottlenecks(model: nn.Module, example_input, num_iterations: int = 10, verbose: bool = False,
+                        device: Optional[str] = None, top_k: int = 20) -> Dict[str, Any]:
+    """Device time per kernel (PyTorch profiler) over ``num_iterations`` forward calls
+    (the reference's arguments, inference/optimization.py); the device is the input's
+    unless given; ``verbose`` prints the top operations."""
     from torch.profiler import ProfilerActivity, profile
 
-    dev = torch.device(device)
+    first = example_input[0] if isinstance(example_input, (tuple, list)) else example_input
+    dev = torch.device(device) if device is not None else first.device
     xs = example_input if isinstance(example_input, (tuple, list)) else (example_input,)
     acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if dev.type == "cuda" else [])
     with torch.no_grad():
@@ -522,6 +525,9 @@ def profile_bottlenecks(model: nn.Module, example_input, device: str = "cuda", t
     total = sum(r["total_ms"] for r in rows) or 1.0
     for r in rows:
         r["share"] = r["total_ms"] / total
+    if verbose:
+        for r in rows[:top_k]:
+            print(f"{r['total_ms']:10.3f} ms {100 * r['share']:5.1f}%  {r['name']}")
     return {"top_operations": rows[:top_k], "total_ms": total / num_iterations}
 
 

@@ -108,10 +108,19 @@ def set_attention_backend(backend: AttentionBackend) -> bool:
 
 
 def mha(q, k, v, mask: Optional[torch.Tensor] = None, dropout_p: float = 0.0,
-        training: bool = False, causal: bool = False) -> torch.Tensor:
+        training: bool = False, is_causal: bool = False, backend: Optional[AttentionBackend] = None,
+        causal: bool = False) -> torch.Tensor:
     """Reference-compatible scaled dot-product attention on ``[B, T, H, D]``.
 
-    ``mask`` follows the reference: 0 = blocked (any dtype) or a bool tensor."""
+    ``mask`` follows the reference: 0 = blocked (any dtype) or a bool tensor. ``backend``
+    ``EINSUM`` selects the fp32 oracle for this call (see :class:`AttentionBackend`)."""
+    causal = causal or is_causal
+    if backend is AttentionBackend.EINSUM and _BACKEND is not AttentionBackend.EINSUM:
+        if mask is not None and mask.dtype != torch.bool:
+            mask = mask != 0
+        if causal and mask is None:
+            mask = create_causal_mask(q.shape[1], q.device, k.shape[1])
+        return attention_reference(q, k, v, mask).to(q.dtype)
     if mask is not None and mask.dtype != torch.bool:
         mask = mask != 0
     if _BACKEND is AttentionBackend.EINSUM:

@@ -345,13 +345,16 @@ def get_available_port() -> int:
         return s.getsockname()[1]
 
 
-def launch_distributed(fn, world_size: int, backend: str = "nccl", *args) -> None:
-    """Spawns ``world_size`` processes running ``fn(rank, world_size, *args)`` inside a
-    ``distributed_context`` (rendezvous on 127.0.0.1, a free port)."""
+def launch_distributed(train_func, world_size: int, backend: str = "nccl", master_addr: str = "127.0.0.1",
+                       master_port: Optional[str] = None, *args) -> None:
+    """Spawns ``world_size`` processes running ``train_func(rank, world_size, *args)``
+    inside a ``distributed_context`` (rendezvous at ``master_addr``, a free port unless
+    ``master_port`` is given)."""
     import torch.multiprocessing as mp
 
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(get_available_port())
+    fn = train_func
+    os.environ["MASTER_ADDR"] = master_addr
+    os.environ["MASTER_PORT"] = str(master_port or get_available_port())
     mp.spawn(_launch_entry, args=(world_size, backend, fn, args), nprocs=world_size, join=True)
 
 

@@ -2,7 +2,7 @@
 from __future__ import annotations
 
 import math
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 import torch.nn.functional as F
@@ -95,12 +95,19 @@ def laplacian(x: torch.Tensor, spacing: float = 1.0) -> torch.Tensor:
     return y.view(s)
 
 
-def spectral_norm_power_iteration(W: torch.Tensor, iterations: int = 10) -> torch.Tensor:
-    v = torch.randn(W.shape[1], device=W.device, dtype=W.dtype)
-    for _ in range(iterations):
-        u = F.normalize(W @ v, dim=0)
-        v = F.normalize(W.t() @ u, dim=0)
-    return u @ W @ v
+def spectral_norm_power_iteration(weight: torch.Tensor, u: Optional[torch.Tensor] = None,
+                                  num_iterations: int = 1) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Power iteration for the largest singular value of ``weight [out, in]`` from the
+    left-vector estimate ``u`` (random when None): returns ``(u, sigma)`` with ``u``
+    updated, to be passed back in on the next call (utils/math_utils.py)."""
+    with torch.no_grad():
+        if u is None:
+            u = F.normalize(torch.randn(weight.shape[0], device=weight.device, dtype=weight.dtype), dim=0)
+        v = F.normalize(weight.t() @ u, dim=0, eps=1e-12)
+        for _ in range(num_iterations):
+            v = F.normalize(weight.t() @ u, dim=0, eps=1e-12)
+            u = F.normalize(weight @ v, dim=0, eps=1e-12)
+        return u, u @ weight @ v
 
 
 def batch_trace(x: torch.Tensor) -> torch.Tensor:
@@ -130,16 +137,16 @@ def wasserstein_distance_1d(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     return (x.flatten().sort().values - y.flatten().sort().values).abs().mean()
 
 
-def sinkhorn_divergence(x: torch.Tensor, y: torch.Tensor, epsilon: float = 0.1, iterations: int = 100) -> torch.Tensor:
+def sinkhorn_divergence(x: torch.Tensor, y: torch.Tensor, reg: float = 0.1, num_iters: int = 100) -> torch.Tensor:
     """Entropic OT cost (log-domain Sinkhorn) debiased: ``OT(x,y) - (OT(x,x)+OT(y,y))/2``."""
     def ot(a, b):
         C = torch.cdist(a, b) ** 2
         n, m = C.shape
         la, lb = torch.full((n,), -math.log(n), device=a.device), torch.full((m,), -math.log(m), device=a.device)
         f, g = torch.zeros(n, device=a.device), torch.zeros(m, device=a.device)
-        for _ in range(iterations):
-            f = -epsilon * torch.logsumexp((g[None] - C) / epsilon + lb[None], 1)
-            g = -epsilon * torch.logsumexp((f[:, None] - C) / epsilon + la[:, None], 0)
-        P = torch.exp((f[:, None] + g[None] - C) / epsilon + la[:, None] + lb[None])
+        for _ in range(num_iters):
+            f = -reg * torch.logsumexp((g[None] - C) / reg + lb[None], 1)
+            g = -reg * torch.logsumexp((f[:, None] - C) / reg + la[:, None], 0)
+        P = torch.exp((f[:, None] + g[None] - C) / reg + la[:, None] + lb[None])
         return (P * C).sum()
     return ot(x, y) - 0.5 * (ot(x, x) + ot(y, y))

@@ -17,9 +17,13 @@ def safe_stack(tensors: List[torch.Tensor], dim: int = 0) -> torch.Tensor:
     return torch.stack(tensors, dim) if tensors else torch.empty(0)
 
 
-def pad_sequence(sequences: Sequence[torch.Tensor], max_length: Optional[int] = None, pad_value: float = 0.0,
-                 batch_first: bool = True) -> torch.Tensor:
-    """Pad / truncate along dim 0 and stack (``[B, L, ...]`` or ``[L, B, ...]``)."""
+def pad_sequence(sequences: Sequence[torch.Tensor], batch_first: bool = True, padding_value: float = 0.0,
+                 max_length: Optional[int] = None) -> torch.Tensor:
+    """Pad / truncate along dim 0 and stack (``[B, L, ...]`` or ``[L, B, ...]``); the
+    reference's argument order (utils/tensor_utils.py)."""
+    if not sequences:
+        return torch.empty(0)
+    pad_value = padding_value
     L = max_length or max(s.shape[0] for s in sequences)
     out = []
     for s in sequences:
@@ -93,7 +97,12 @@ def interpolate_tensors(a: torch.Tensor, b: torch.Tensor, alpha: Union[float, to
     return torch.lerp(a, b, alpha if torch.is_tensor(alpha) else float(alpha))
 
 
-def normalize_tensor(x: torch.Tensor, mode: str = "minmax", dim=None, eps: float = 1e-8) -> torch.Tensor:
+def normalize_tensor(x: torch.Tensor, dim=None, eps: float = 1e-8, mode: str = "l2") -> torch.Tensor:
+    """``x / (||x|| + eps)`` over ``dim`` (all elements when None), the reference's
+    default; ``mode`` ``minmax`` or ``zscore`` rescale instead."""
+    if mode == "l2":
+        n = x.norm() if dim is None else x.norm(dim=dim, keepdim=True)
+        return x / (n + eps)
     if mode == "minmax":
         lo = x.amin(dim=dim, keepdim=True) if dim is not None else x.min()
         hi = x.amax(dim=dim, keepdim=True) if dim is not None else x.max()
@@ -102,6 +111,4 @@ def normalize_tensor(x: torch.Tensor, mode: str = "minmax", dim=None, eps: float
         m = x.mean(dim=dim, keepdim=True) if dim is not None else x.mean()
         s = x.std(dim=dim, keepdim=True) if dim is not None else x.std()
         return (x - m) / (s + eps)
-    if mode == "l2":
-        return F.normalize(x, dim=-1 if dim is None else dim, eps=eps)
     raise ValueError(mode)
