@@ -580,3 +580,30 @@ def test_samplers(ref):
         assert a.chunks == b.chunks and sorted(a) == sorted(b)
     a, b = os_.SequentialChunkSampler(ds, 4, seed=0), rs.SequentialChunkSampler(ds, 4, seed=0)
     assert a.sequence_chunks == b.sequence_chunks and list(a) == list(b)
+
+
+@pytest.mark.parametrize("attention", [False, True])
+def test_vae3d_forward_and_gradients(ref, attention):
+    """The reference's causal video VAE weights load by name; the forward (encoder,
+    posterior, decoder with skips, losses) and the parameter gradients of the total loss
+    match."""
+    import importlib
+    rv = importlib.import_module("models.vae3d")
+    from drivedit_b200.models import vae3d as ov
+    kw = dict(in_channels=3, latent_dim=4, hidden_dims=[16, 32], num_res_blocks=1, use_attention=attention,
+              attention_resolution=[8], temporal_compression=2, spatial_compression=4,
+              use_perceptual_loss=False)
+    torch.manual_seed(0)
+    r = rv.VAE3Dv2(rv.VAE3DConfig(**kw)).eval()
+    o = ov.VAE3Dv2(ov.VAE3DConfig(**kw)).eval()
+    o.load_state_dict(r.state_dict())
+    x = torch.randn(1, 3, 4, 16, 16)
+    fr, fo = r(x, return_loss=True, deterministic=True), o(x, return_loss=True, deterministic=True)
+    for k in ("recon", "mean", "logvar", "recon_loss", "kl_loss", "total_loss"):
+        _close(fo[k], fr[k], 1e-5)
+    fr["total_loss"].backward()
+    fo["total_loss"].backward()
+    rg = dict(r.named_parameters())
+    for n, p in o.named_parameters():
+        if rg[n].grad is not None:
+            _close(p.grad, rg[n].grad, 1e-4)
