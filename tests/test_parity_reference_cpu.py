@@ -607,3 +607,24 @@ def test_vae3d_forward_and_gradients(ref, attention):
     for n, p in o.named_parameters():
         if rg[n].grad is not None:
             _close(p.grad, rg[n].grad, 1e-4)
+
+
+def test_vjepa_backbone(ref):
+    """The reference's V-JEPA backbone weights load by name; on ``[B, T, C, H, W]`` clips
+    every output matches. (On ``[B, C, T, H, W]`` input the reference reads the channel
+    count as the frame count and resamples frames; this backbone takes either layout.)"""
+    import importlib
+    rv = importlib.import_module("core.vjepa_backbone")
+    from drivedit_b200.models import vjepa as ov
+    kw = dict(embed_dim=64, num_layers=2, num_heads=4, patch_size=8, tubelet_size=2, num_frames=4,
+              image_size=32, extract_layers=[0, 1], use_fp16=False)
+    torch.manual_seed(0)
+    r, o = rv.VJEPABackbone(rv.VJEPAConfig(**kw)).eval(), ov.VJEPABackbone(ov.VJEPAConfig(**kw)).eval()
+    o.load_state_dict(r.state_dict())
+    clip = torch.rand(2, 4, 3, 40, 40)          # resized to 32 x 32 by both
+    a, b = r(clip), o(clip)
+    for k in ("final", "pooled", "patch_features"):
+        _close(b[k], a[k], 1e-5)
+    for k in a["intermediate"]:
+        _close(b["intermediate"][k], a["intermediate"][k], 1e-5)
+    _close(o(clip.transpose(1, 2))["final"], a["final"], 1e-5)   # channel-first layout, same result
