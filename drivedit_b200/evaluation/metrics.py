@@ -244,8 +244,12 @@ class PerceptualMetrics:
         return kl.mean().exp()
 
 
-def compute_all_metrics(pred: torch.Tensor, target: torch.Tensor, pred_controls=None, target_controls=None,
-                        pred_depth=None, target_depth=None, positions=None) -> Dict[str, torch.Tensor]:
+def compute_all_metrics(pred_frames: torch.Tensor, target_frames: torch.Tensor, pred_controls=None,
+                        target_controls=None, pred_depth=None, target_depth=None,
+                        positions=None) -> Dict[str, torch.Tensor]:
+    """Frame, temporal, control, depth and trajectory metrics (the reference's argument
+    names, evaluation/metrics.py)."""
+    pred, target = pred_frames, target_frames
     m: Dict[str, torch.Tensor] = {
         "mse": VideoMetrics.mse(pred, target), "mae": VideoMetrics.mae(pred, target),
         "psnr": VideoMetrics.psnr(pred, target), "ssim": VideoMetrics.ssim(pred, target),

@@ -35,11 +35,11 @@ def pad_sequence(sequences: Sequence[torch.Tensor], batch_first: bool = True, pa
     return y if batch_first else y.transpose(0, 1)
 
 
-def chunk_tensor(x: torch.Tensor, chunk_size: int, dim: int = 1, overlap: int = 0) -> List[torch.Tensor]:
+def chunk_tensor(tensor: torch.Tensor, chunk_size: int, dim: int = 1, overlap: int = 0) -> List[torch.Tensor]:
     step = chunk_size - overlap
     assert step > 0
-    n = x.shape[dim]
-    return [x.narrow(dim, s, min(chunk_size, n - s)) for s in range(0, max(n - overlap, 1), step)]
+    n = tensor.shape[dim]
+    return [tensor.narrow(dim, s, min(chunk_size, n - s)) for s in range(0, max(n - overlap, 1), step)]
 
 
 def flatten_dict_tensors(tensor_dict: dict, prefix: str = "") -> dict:
@@ -93,8 +93,8 @@ def detach_tensors(obj: Any) -> Any:
     return obj
 
 
-def interpolate_tensors(a: torch.Tensor, b: torch.Tensor, alpha: Union[float, torch.Tensor]) -> torch.Tensor:
-    return torch.lerp(a, b, alpha if torch.is_tensor(alpha) else float(alpha))
+def interpolate_tensors(tensor1: torch.Tensor, tensor2: torch.Tensor, alpha: Union[float, torch.Tensor]) -> torch.Tensor:
+    return torch.lerp(tensor1, tensor2, alpha if torch.is_tensor(alpha) else float(alpha))
 
 
 def normalize_tensor(x: torch.Tensor, dim=None, eps: float = 1e-8, mode: str = "l2") -> torch.Tensor:
